@@ -1,0 +1,443 @@
+#!/usr/bin/env python3
+"""Benchmark of the k-mamba hot path on B200 (one JSON line on rank 0).
+
+Workload ("config 2"): 1D selective scan forward
++ backward in fp32, batch 8, L 4096, D 1536, N 16, B/C shared across
+channels, synthetic inputs with the config's distributions.  One step =
+kmb_scan1d_fwd (y + checkpoints) then kmb_scan1d_bwd (dx, ddt, dA, dB, dC).
+
+metric: algorithmic HBM GB/s of the step (bytes a perfect kernel must
+move: fwd 4(3E + 2BLN + DN), bwd 4(5E + 4BLN + 2DN), E = B*L*D) divided by
+the device time.  Every [B,L,D] tensor is 201 MB, larger than the 126 MB
+L2, so no flush is needed between steps.
+
+--impl reference times the reference's own CPU implementation of the path
+(oracle/_ref: src/scan_nd.c scannd_ref for the forward states and
+cpu/scan1d_backward.c for the backward) on the host cores, on bounded
+samples of the same workload, with the same metric.
+
+Multi-GPU (torchrun): every rank runs a full config-2 batch of its own
+(weak scaling); the only exchange is the sum of the parameter gradient dA
+over ranks (NCCL all-reduce), as data-parallel training needs.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "k-mamba_b200"))
+
+BATCH, L, D, N = 8, 4096, 1536, 16
+E = BATCH * L * D
+FWD_BYTES = 4 * (3 * E + 2 * BATCH * L * N + D * N)
+BWD_BYTES = 4 * (5 * E + 4 * BATCH * L * N + 2 * D * N)
+STEP_BYTES = FWD_BYTES + BWD_BYTES
+
+
+def set_batch(b):
+    global BATCH, E, FWD_BYTES, BWD_BYTES, STEP_BYTES
+    BATCH = b
+    E = BATCH * L * D
+    FWD_BYTES = 4 * (3 * E + 2 * BATCH * L * N + D * N)
+    BWD_BYTES = 4 * (5 * E + 4 * BATCH * L * N + 2 * D * N)
+    STEP_BYTES = FWD_BYTES + BWD_BYTES
+
+
+WORKLOAD = ("config2: 1D selective scan fwd+bwd, fp32, batch 8, L 4096, D 1536, N 16, "
+            "B/C shared across D")
+METRIC = "scan HBM GB/s (algorithmic bytes / device time), 1D selective scan fwd+bwd"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
+    except OSError:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+def make_inputs(seed, batch=None, d=D):
+    """Config-2 distributions: x, dy ~ N(0,1); dt = softplus(N(0,1) - 2);
+    A = -exp(U[ln 1, ln 16]); B, C ~ N(0,1) of shape (B, L, N)."""
+    batch = BATCH if batch is None else batch
+    rng = np.random.default_rng(seed)
+    f = np.float32
+    x = rng.standard_normal((batch, L, d), dtype=f)
+    dt = np.log1p(np.exp(rng.standard_normal((batch, L, d), dtype=f) - 2)).astype(f)
+    A = (-np.exp(rng.uniform(0, np.log(16), (d, N)))).astype(f)
+    B = rng.standard_normal((batch, L, N), dtype=f)
+    Cm = rng.standard_normal((batch, L, N), dtype=f)
+    dy = rng.standard_normal((batch, L, d), dtype=f)
+    return x, dt, A, B, Cm, dy
+
+
+class Clocks:
+    """Samples nvidia-smi during the timed region."""
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        os.makedirs(os.path.join(ROOT, "gpurun_out"), exist_ok=True)
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{self.index}.csv")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.index)],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            self.proc.wait()
+
+    def summary(self):
+        if not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                rows.append((float(parts[0]), float(parts[1]), float(parts[2]), parts[3:]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[3])
+                          if v.lower().startswith("active")})
+        loaded = [r for r in rows if r[2] > 250] or rows
+        return {"sm_mhz": statistics.median(r[0] for r in loaded),
+                "sm_max_mhz": max(r[1] for r in rows),
+                "power_w_max": max(r[2] for r in rows),
+                "samples": len(rows), "reasons": reasons}
+
+
+def traffic_from_profile():
+    """DRAM bytes per launch of the dominant kernel from the committed ncu
+    summary (profiles/scan1d_config2_traffic.json), if present."""
+    p = os.path.join(ROOT, "profiles", "scan1d_config2_traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return None
+
+
+# --------------------------------------------------------------------------
+# reference CPU arm / CPU baseline
+# --------------------------------------------------------------------------
+
+def cpu_reference_sample(nthreads, chans_per_thread, seed=1):
+    """Times the reference's CPU path on nthreads independent channel
+    slices (one batch item each): scannd_ref (1D) for y and the state
+    history, then scan1d_backward.  Returns (seconds, channel_sequences)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle  # noqa: WPS433  (CPU baseline leg only)
+    import kmamba_b200 as kb
+    ref = oracle.ref_lib()
+    kind = "reference"
+    if ref is None:
+        ref = None
+        kind = "port"
+    rng = np.random.default_rng(seed)
+    f = np.float32
+    jobs = []
+    for t in range(nthreads):
+        dch = chans_per_thread
+        x = rng.standard_normal((L, dch), dtype=f)
+        dt = np.log1p(np.exp(rng.standard_normal((L, dch), dtype=f) - 2)).astype(f)
+        A = (-np.exp(rng.uniform(0, np.log(16), (dch, N)))).astype(f)
+        Bs = rng.standard_normal((L, N), dtype=f)
+        Cs = rng.standard_normal((L, N), dtype=f)
+        dy = rng.standard_normal((L, dch), dtype=f)
+        Bx = np.ascontiguousarray(np.broadcast_to(Bs[:, None, :], (L, dch, N)))
+        Cx = np.ascontiguousarray(np.broadcast_to(Cs[:, None, :], (L, dch, N)))
+        jobs.append(dict(x=x, dt=dt, A=A, B=Bx, C=Cx, dy=dy, dch=dch,
+                         h=np.zeros((L, dch, N), f), y=np.zeros((L, dch), f),
+                         dx=np.zeros((L, dch), f), ddt=np.zeros((L, dch), f),
+                         dA=np.zeros((dch, N), f), dB=np.zeros((L, dch, N), f),
+                         dC=np.zeros((L, dch, N), f)))
+
+    P = lambda a: a.ctypes.data  # noqa: E731
+
+    def run(j):
+        if ref is not None:
+            dims = np.array([L], np.int64)
+            j["dims"] = dims
+            p = kb.ScanNDParams(P(dims), 1, j["dch"], N, P(j["x"]), P(j["A"]), P(j["B"]),
+                                P(j["C"]), P(j["dt"]), P(j["h"]), P(j["y"]), None, None)
+            ref.scannd_ref(C.byref(p))
+            bp = kb.ScanBackwardParams(P(j["x"]), P(j["A"]), P(j["B"]), P(j["C"]), P(j["dt"]),
+                                       None, P(j["h"]), P(j["dy"]), P(j["dx"]), P(j["dA"]),
+                                       P(j["dB"]), P(j["dC"]), P(j["ddt"]), L, j["dch"], N)
+            ref.scan1d_backward(C.byref(bp))
+        else:
+            y, _, h = oracle.scan1d_fwd(j["x"], j["dt"], j["A"], j["B"], j["C"], clamp=False,
+                                        want_h_all=True)
+            oracle.scan1d_bwd(j["x"], j["dt"], j["A"], j["B"], j["C"], h, j["dy"])
+
+    if ref is not None:
+        ref.scannd_ref.argtypes = [C.POINTER(kb.ScanNDParams)]
+        ref.scannd_ref.restype = C.c_int
+        ref.scan1d_backward.argtypes = [C.POINTER(kb.ScanBackwardParams)]
+    threads = [threading.Thread(target=run, args=(j,)) for j in jobs]
+    t0 = time.perf_counter()
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join()
+    return time.perf_counter() - t0, nthreads * chans_per_thread, kind
+
+
+def cpu_threads():
+    try:
+        n = len(os.sched_getaffinity(0))
+    except AttributeError:
+        n = os.cpu_count() or 1
+    return max(1, min(n, 32))
+
+
+def bytes_for_channels(nch):
+    return STEP_BYTES * nch / (BATCH * D)
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    os.environ["OMP_NUM_THREADS"] = "1"  # scannd_ref's inner OpenMP loop races
+    nth = cpu_threads()
+    per = 32
+    times = []
+    kind = "reference"
+    for i in range(args.warmup + args.steps):
+        dt, nch, kind = cpu_reference_sample(nth, per, seed=100 + i)
+        if i >= args.warmup:
+            times.append(dt)
+    t = sum(times) / len(times)
+    v = bytes_for_channels(nth * per) / t / 1e9
+    sample = (f"{nth} threads x {per} channels of one batch item, full L={L}, N={N} "
+              f"(B/C expanded to [L,D,N] for the reference API): {nth * per} of "
+              f"{BATCH * D} channel-sequences per step")
+    line = {"metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": WORKLOAD, "batch": BATCH, "L": L, "D": D, "N": N},
+            "cpu_baseline": {"value": v, "unit": "GB/s", "cores": nth, "kind": kind,
+                             "sample": sample},
+            "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------
+# GPU arm
+# --------------------------------------------------------------------------
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=BATCH,
+                    help="batch items per GPU (profiling of small cases only)")
+    args = ap.parse_args()
+    set_batch(args.batch)
+    if args.impl == "reference":
+        run_reference_arm(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+    import kmamba_b200 as kb
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    lib = kb.load()
+    stream = torch.cuda.current_stream()
+    lib.kmb_set_stream(C.c_void_p(stream.cuda_stream))
+    lib.kmb_set_sync(0)
+
+    x, dt, A, B, Cm, dy = make_inputs(seed=1000 + rank)
+    dev = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
+    tx, tdt, tA, tB, tC, tdy = map(dev, (x, dt, A, B, Cm, dy))
+    ty = torch.empty_like(tx)
+    nck = lib.kmb_scan1d_ckpt_elems(BATCH, L, D, N)
+    tck = torch.empty(nck, dtype=torch.float32, device="cuda")
+    g = {k: torch.empty(s, dtype=torch.float32, device="cuda") for k, s in
+         (("dx", (BATCH, L, D)), ("ddt", (BATCH, L, D)), ("dA", (D, N)),
+          ("dB", (BATCH, L, N)), ("dC", (BATCH, L, N)))}
+
+    fa = kb.KmbScan1D()
+    fa.x, fa.dt, fa.A, fa.B, fa.C = (t.data_ptr() for t in (tx, tdt, tA, tB, tC))
+    fa.y, fa.ckpt = ty.data_ptr(), tck.data_ptr()
+    fa.batch, fa.L, fa.D, fa.N, fa.bc_shared, fa.clamp = BATCH, L, D, N, 1, 1
+    ba = kb.KmbScan1D()
+    C.memmove(C.byref(ba), C.byref(fa), C.sizeof(fa))
+    ba.y = None
+    ba.dy = tdy.data_ptr()
+    ba.dx, ba.ddt, ba.dA, ba.dB, ba.dC = (g[k].data_ptr() for k in ("dx", "ddt", "dA", "dB", "dC"))
+
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+
+    def step(marks=None):
+        if marks:
+            marks[0].record(stream)
+        kb.check(lib, lib.kmb_scan1d_fwd(C.byref(fa)))
+        if marks:
+            marks[1].record(stream)
+        kb.check(lib, lib.kmb_scan1d_bwd(C.byref(ba)))
+        if marks:
+            marks[2].record(stream)
+        if world > 1:
+            dist.all_reduce(g["dA"])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+    marks = [[ev(), ev(), ev()] for _ in range(args.steps)]
+    start, stop = ev(), ev()
+    with Clocks(local) as clk:
+        start.record(stream)
+        for i in range(args.steps):
+            step(marks[i])
+        stop.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    elapsed = start.elapsed_time(stop) / 1e3
+    fwd_ms = sum(m[0].elapsed_time(m[1]) for m in marks) / args.steps
+    bwd_ms = sum(m[1].elapsed_time(m[2]) for m in marks) / args.steps
+    t_max = torch.tensor([elapsed], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    elapsed = float(t_max.item())
+    value = STEP_BYTES * world * args.steps / elapsed / 1e9
+
+    # ---------------- e2e through the public C ABI with host buffers ----------
+    h2d = d2h = 0
+    e2e_val = None
+    if args.e2e_steps > 0:
+        pin = lambda a: torch.from_numpy(a).pin_memory()  # noqa: E731
+        hx, hdt, hA, hB, hC, hdy = map(pin, (x, dt, A, B, Cm, dy))
+        hy = torch.empty(x.shape, dtype=torch.float32).pin_memory()
+        hg = {k: torch.empty(tuple(v.shape), dtype=torch.float32).pin_memory()
+              for k, v in g.items()}
+        ef = kb.KmbScan1D()
+        ef.x, ef.dt, ef.A, ef.B, ef.C = (t.data_ptr() for t in (hx, hdt, hA, hB, hC))
+        ef.y = hy.data_ptr()
+        ef.batch, ef.L, ef.D, ef.N, ef.bc_shared, ef.clamp = BATCH, L, D, N, 1, 1
+        eb = kb.KmbScan1D()
+        C.memmove(C.byref(eb), C.byref(ef), C.sizeof(ef))
+        eb.y = None
+        eb.dy = hdy.data_ptr()
+        eb.dx, eb.ddt, eb.dA, eb.dB, eb.dC = (hg[k].data_ptr()
+                                              for k in ("dx", "ddt", "dA", "dB", "dC"))
+        lib.kmb_set_sync(1)
+        fin = [hx, hdt, hA, hB, hC]
+        h2d = sum(t.numel() * 4 for t in fin) * 2 + hdy.numel() * 4
+        d2h = hy.numel() * 4 + sum(t.numel() * 4 for t in hg.values())
+        kb.check(lib, lib.kmb_scan1d_fwd(C.byref(ef)))  # warm the staging pool
+        kb.check(lib, lib.kmb_scan1d_bwd(C.byref(eb)))
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(args.e2e_steps):
+            kb.check(lib, lib.kmb_scan1d_fwd(C.byref(ef)))
+            kb.check(lib, lib.kmb_scan1d_bwd(C.byref(eb)))
+        torch.cuda.synchronize()
+        te = (time.perf_counter() - t0) / args.e2e_steps
+        te_t = torch.tensor([te], dtype=torch.float64, device="cuda")
+        if world > 1:
+            dist.all_reduce(te_t, op=dist.ReduceOp.MAX)
+        e2e_val = STEP_BYTES * world / float(te_t.item()) / 1e9
+        lib.kmb_set_sync(0)
+
+    pk, pk_kind = peaks()
+    dom_ms, dom_bytes, dom_name = ((bwd_ms, BWD_BYTES, "k_scan1d_bwd") if bwd_ms >= fwd_ms
+                                   else (fwd_ms, FWD_BYTES, "k_scan1d_fwd"))
+    achieved = dom_bytes / (dom_ms / 1e3) / 1e9
+    tr = traffic_from_profile()
+    traffic = None
+    if tr and dom_name in tr:
+        traffic = tr[dom_name]
+
+    line = None
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline:
+            nth = cpu_threads()
+            per = 64
+            secs, nch, kind = cpu_reference_sample(nth, per)
+            cpu = {"value": bytes_for_channels(nch) / secs / 1e9, "unit": "GB/s", "cores": nth,
+                   "kind": kind,
+                   "sample": (f"{nth} host threads x {per} channel-sequences (L={L}, N={N}) "
+                              f"of one batch item: reference scannd_ref (1D) forward + "
+                              f"scan1d_backward, {nch} of {BATCH * D} sequences, "
+                              f"{secs:.1f} s")}
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (config-2 distributions, seeded per rank)",
+            "config": {"workload": WORKLOAD, "batch_per_gpu": BATCH, "L": L, "D": D, "N": N,
+                       "parallelism": f"dp{world} (independent batch per rank, dA all-reduce)",
+                       "l2": "inputs larger than L2 (each [B,L,D] tensor is 201 MB)",
+                       "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
+                       "fwd_GBps": FWD_BYTES / fwd_ms / 1e6, "bwd_GBps": BWD_BYTES / bwd_ms / 1e6},
+            "roofline": {"bound": "hbm", "kernel": dom_name, "achieved": achieved,
+                         "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                         "peak_source": f"{pk_kind} hbm_gbs (MEASURED_PEAKS.json)",
+                         "algorithmic_bytes_per_launch": dom_bytes, "traffic": traffic},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_val, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h,
+                    "path": "kmb_scan1d_fwd + kmb_scan1d_bwd on pinned host buffers "
+                            "(staged through the library's device pool)"},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

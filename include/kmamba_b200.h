@@ -1,0 +1,107 @@
+#ifndef KMAMBA_B200_H
+#define KMAMBA_B200_H
+
+/*
+ * B200 extensions of the k-mamba C API: status-returning, batched entry
+ * points for the hot path, and the runtime controls they share.  All
+ * entry points run on the GPU; pointers may be device memory (used in
+ * place) or host memory (staged through pooled device buffers inside the
+ * call).  Nothing here falls back to the CPU.
+ */
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes returned by every kmb_* entry point. */
+#define KMB_OK            0
+#define KMB_EINVAL       -1   /* bad pointer, size or layout */
+#define KMB_ECUDA        -2   /* CUDA runtime / launch failure */
+#define KMB_ENOMEM       -3   /* device or host allocation failed */
+#define KMB_ETIMEOUT     -4   /* a bounded device-side wait gave up */
+#define KMB_EUNSUPPORTED -5   /* shape outside what the kernels support */
+
+/* Message and status of the last failure on the calling thread. */
+const char *kmb_last_error(void);
+int kmb_last_status(void);
+void kmb_clear_error(void);
+
+/* Stream used by every entry point of the library (a cudaStream_t; NULL
+ * = legacy default stream).  Per calling thread. */
+void kmb_set_stream(void *cuda_stream);
+void *kmb_get_stream(void);
+
+/* When on (default), entry points synchronize the stream before they
+ * return, which the reference API requires.  With it off, kmb_* calls on
+ * device pointers are asynchronous on the library stream. */
+void kmb_set_sync(int on);
+int kmb_get_sync(void);
+
+/* Device buffer pool (replaces the reference's host km_memory_pool for
+ * device scratch).  Blocks are cached per device and reused by size. */
+void *kmb_pool_alloc(size_t bytes);
+void kmb_pool_free(void *dptr);
+/* Frees every cached, unused block; returns the bytes released. */
+size_t kmb_pool_trim(void);
+/* Bytes currently held from cudaMalloc (in use + cached). */
+size_t kmb_pool_bytes_held(void);
+
+/* ------------------------------------------------------------------ */
+/* Batched 1D selective scan                                           */
+/* ------------------------------------------------------------------ */
+/*
+ * For every batch item b, channel d and state n:
+ *   h_t = exp(dt_t*A[d,n]) * h_{t-1} + dt_t*B_t[n]*x_t      (h_{-1} = h0)
+ *   y_t = sum_n C_t[n] * h_t
+ * with x, dt, y [batch, L, D] and A [D, N].  B and C are [batch, L, N]
+ * (shared by all channels) when bc_shared, else [batch, L, D, N].
+ *
+ * Forward outputs: y (may be NULL), h_last [batch, D, N], h_all
+ * [batch, L, D, N] and ckpt (states every KMB_SCAN1D_CHUNK steps, size
+ * kmb_scan1d_ckpt_elems()); each optional output may be NULL.
+ *
+ * Backward: reads dy and either h_all (stored states, the reference
+ * contract) or ckpt (written by the forward); when both are NULL the
+ * checkpoints are computed into pooled scratch.  Writes dx, ddt
+ * [batch, L, D], dA [D, N] (summed over the batch) and dB, dC (same layout
+ * as B, C; summed over D when bc_shared).  Every gradient is overwritten.
+ * The backward treats the clamp as the identity, like the reference.
+ */
+typedef struct {
+    const float *x;
+    const float *dt;
+    const float *A;
+    const float *B;
+    const float *C;
+    const float *h0;
+    float *y;
+    float *h_last;
+    float *h_all;
+    float *ckpt;
+    const float *dy;
+    float *dx;
+    float *ddt;
+    float *dA;
+    float *dB;
+    float *dC;
+    long batch;
+    long L;
+    long D;
+    long N;
+    int bc_shared;
+    int clamp;       /* 1: clamp states to [-1000, 1000] after every step */
+    int flags;       /* reserved, must be 0 */
+    int pad_;
+} KmbScan1D;
+
+long kmb_scan1d_ckpt_elems(long batch, long L, long D, long N);
+int kmb_scan1d_fwd(const KmbScan1D *args);
+int kmb_scan1d_bwd(const KmbScan1D *args);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KMAMBA_B200_H */

@@ -1,0 +1,673 @@
+/*
+ * 1D selective scan, forward and backward, for sm_100a.
+ *
+ * Recurrence (reference cpu/scan1d.asm:88-152, cuda/scan1d.cu:57-89):
+ *   h_t[d,n] = exp(dt_t[d]*A[d,n]) * h_{t-1}[d,n] + dt_t[d]*B_t[n]*x_t[d]
+ *   y_t[d]   = sum_n C_t[n] * h_t[d,n]
+ * Backward = the reverse adjoint of cpu/scan1d_backward.c:248-295.
+ *
+ * Work decomposition.  The recurrence is sequential in t and independent
+ * per (batch, channel, state): every (b, d) owns P lanes, every lane owns
+ * G = 4 consecutive states, so one lane runs 4 independent chains over the
+ * whole sequence.  A CTA of 128 threads covers DT = 128/P channels of one
+ * batch item.  Per step and state the work is one MUFU ex2 plus four FMA-
+ * pipe operations; exp(dt*A) is fused (A is pre-scaled by log2 e) and no
+ * [L,D,N] temporary ever reaches memory unless the caller asks for h_all.
+ *
+ * Inputs are staged through shared memory with a 3-stage cp.async
+ * pipeline (x, dt as [TT][DT] tiles, B, C as [TT][N] rows when they are
+ * shared across channels).  y is reduced across the P lanes of a channel
+ * with xor shuffles.
+ *
+ * The backward walks the sequence in reverse in chunks of
+ * KMB_SCAN1D_CHUNK steps.  For each chunk it re-runs the forward from the
+ * checkpoint the forward stored at the chunk start (or reads h from h_all),
+ * keeps the chunk's states in registers, and sweeps the chunk backwards
+ * carrying the adjoint g = dL/dh.  When B and C are shared across channels
+ * dB/dC are sums over channels: a shuffle reduce-scatter folds the warp's
+ * channels, shared memory folds the CTA's warps and one atomic per
+ * (step, state, CTA) folds the CTAs.
+ */
+#include "kmb_common.cuh"
+#include "../kmb_internal.h"
+
+namespace {
+
+constexpr int kNT = 128;      /* threads per CTA */
+constexpr int kG = 4;         /* states per lane */
+constexpr int kChunk = KMB_SCAN1D_CHUNK;
+constexpr unsigned kFull = 0xffffffffu;
+
+struct Scan1DDev {
+    const float *x, *dt, *A, *B, *C, *h0;
+    float *y, *h_last, *h_all, *ckpt;
+    const float *dy;
+    float *dx, *ddt, *dA, *dB, *dC;
+    const float *ckpt_in;
+    long L, D, N, nslots;
+    int clamp;
+    int vec_xd;
+    int vec_bc;
+};
+
+__device__ __forceinline__ float clamp1000(float v) {
+    /* min first, then max: NaN becomes +1000 as with SSE minss/maxss. */
+    return fmaxf(fminf(v, 1000.f), -1000.f);
+}
+
+/* Loads the G state-values of row `row` for lane group g (zero past N). */
+template <bool VEC>
+__device__ __forceinline__ void load_states(const float *row, int g, int N,
+                                            float (&v)[kG]) {
+    if (VEC) {
+        if (g * kG < N) {
+            float4 t = *reinterpret_cast<const float4 *>(row);
+            v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+        } else {
+            v[0] = v[1] = v[2] = v[3] = 0.f;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < kG; ++j) v[j] = (g * kG + j < N) ? row[j] : 0.f;
+    }
+}
+
+template <bool VEC>
+__device__ __forceinline__ void store_states(float *dst, int g, int N,
+                                             const float (&v)[kG]) {
+    if (VEC) {
+        if (g * kG < N)
+            *reinterpret_cast<float4 *>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+#pragma unroll
+        for (int j = 0; j < kG; ++j)
+            if (g * kG + j < N) dst[j] = v[j];
+    }
+}
+
+template <bool VEC>
+__device__ __forceinline__ void load_states_g(const float *src, int g, int N,
+                                              float (&v)[kG]) {
+    if (VEC) {
+        if (g * kG < N) {
+            float4 t = __ldg(reinterpret_cast<const float4 *>(src));
+            v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+        } else {
+            v[0] = v[1] = v[2] = v[3] = 0.f;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < kG; ++j) v[j] = (g * kG + j < N) ? __ldg(src + j) : 0.f;
+    }
+}
+
+/* ------------------------------------------------------------------ */
+/* forward                                                             */
+/* ------------------------------------------------------------------ */
+
+template <int P, bool SHARED>
+struct FwdCfg {
+    static constexpr int DT = kNT / P;
+    static constexpr int TT = SHARED ? 32 : 8;
+    static constexpr int ST = 3;
+};
+
+__host__ __device__ inline int bc_row_stride(bool shared, int dt_ch, int N) {
+    /* shared-memory floats per step row of B (or C), padded to 16 bytes */
+    return shared ? ((N + 3) & ~3) : ((dt_ch * N + 3) & ~3);
+}
+
+template <int P, bool SHARED, bool VEC>
+__global__ void __launch_bounds__(kNT) k_scan1d_fwd(Scan1DDev p) {
+    using Cfg = FwdCfg<P, SHARED>;
+    constexpr int DT = Cfg::DT, TT = Cfg::TT, ST = Cfg::ST;
+    extern __shared__ __align__(16) float smem[];
+
+    const int tid = threadIdx.x;
+    const int g = tid % P;
+    const int dl = tid / P;
+    const long b = blockIdx.y;
+    const long D = p.D, L = p.L;
+    const int N = (int)p.N;
+    const long d0 = (long)blockIdx.x * DT;
+    const long d = d0 + dl;
+    const bool dok = d < D;
+    const int dvalid = (int)min((long)DT, D - d0);
+
+    const int BWr = bc_row_stride(SHARED, DT, N);
+    const int xs_sz = TT * DT;
+    const int bs_sz = TT * BWr;
+    const int stage_sz = 2 * xs_sz + 2 * bs_sz;
+
+    float A2[kG], h[kG];
+#pragma unroll
+    for (int j = 0; j < kG; ++j) {
+        const int n = g * kG + j;
+        const bool ok = dok && n < N;
+        A2[j] = ok ? __ldg(p.A + d * N + n) * KMB_LOG2E : 0.f;
+        h[j] = (ok && p.h0) ? p.h0[(b * D + d) * N + n] : 0.f;
+    }
+
+    const float *xg = p.x + b * L * D + d0;
+    const float *dg = p.dt + b * L * D + d0;
+    const long bld = SHARED ? (long)N : D * N;
+    const float *Bg = p.B + (SHARED ? b * L * N : (b * L * D + d0) * N);
+    const float *Cg = p.C + (SHARED ? b * L * N : (b * L * D + d0) * N);
+    const int bcols = SHARED ? N : DT * N;
+    const int bvalid = SHARED ? N : dvalid * N;
+    const bool vxd = p.vec_xd, vbc = p.vec_bc;
+
+    const int ntiles = (int)((L + TT - 1) / TT);
+    auto load = [&](int k) {
+        float *st = smem + (k % ST) * stage_sz;
+        const long t0 = (long)k * TT;
+        const int rv = (int)min((long)TT, L - t0);
+        kmb_load_tile<kNT>(st, DT, xg + t0 * D, D, TT, DT, rv, dvalid, vxd, tid);
+        kmb_load_tile<kNT>(st + xs_sz, DT, dg + t0 * D, D, TT, DT, rv, dvalid, vxd, tid);
+        kmb_load_tile<kNT>(st + 2 * xs_sz, BWr, Bg + t0 * bld, bld, TT, bcols, rv,
+                           bvalid, vbc, tid);
+        kmb_load_tile<kNT>(st + 2 * xs_sz + bs_sz, BWr, Cg + t0 * bld, bld, TT,
+                           bcols, rv, bvalid, vbc, tid);
+    };
+
+#pragma unroll
+    for (int k = 0; k < ST - 1; ++k) {
+        if (k < ntiles) load(k);
+        kmb_cp_async_commit();
+    }
+
+    const int boff = (SHARED ? 0 : dl * N) + g * kG;
+    const bool clampit = p.clamp != 0;
+    for (int k = 0; k < ntiles; ++k) {
+        kmb_cp_async_wait<ST - 2>();
+        __syncthreads();
+        if (k + ST - 1 < ntiles) load(k + ST - 1);
+        kmb_cp_async_commit();
+
+        const float *st = smem + (k % ST) * stage_sz;
+        const float *xs = st;
+        const float *ds = st + xs_sz;
+        const float *bs = st + 2 * xs_sz;
+        const float *cs = bs + bs_sz;
+        const long t0 = (long)k * TT;
+        const int rv = (int)min((long)TT, L - t0);
+
+#pragma unroll 2
+        for (int i = 0; i < rv; ++i) {
+            const float xv = xs[i * DT + dl];
+            const float dv = ds[i * DT + dl];
+            const float u = dv * xv;
+            float bv[kG], cv[kG];
+            load_states<VEC>(bs + i * BWr + boff, g, N, bv);
+            load_states<VEC>(cs + i * BWr + boff, g, N, cv);
+            float yp = 0.f;
+#pragma unroll
+            for (int j = 0; j < kG; ++j) {
+                const float a = kmb_ex2(dv * A2[j]);
+                float hn = fmaf(a, h[j], bv[j] * u);
+                if (clampit) hn = clamp1000(hn);
+                h[j] = hn;
+                yp = fmaf(cv[j], hn, yp);
+            }
+#pragma unroll
+            for (int o = P / 2; o > 0; o >>= 1) yp += __shfl_xor_sync(kFull, yp, o);
+
+            const long t = t0 + i;
+            if (dok) {
+                if (g == 0 && p.y) p.y[(b * L + t) * D + d] = yp;
+                if (p.h_all) store_states<VEC>(p.h_all + ((b * L + t) * D + d) * N + g * kG, g, N, h);
+                if (p.ckpt && ((t + 1) % kChunk) == 0)
+                    store_states<VEC>(p.ckpt + ((b * p.nslots + t / kChunk) * D + d) * N + g * kG,
+                                      g, N, h);
+            }
+        }
+    }
+    kmb_cp_async_wait<0>();
+    if (p.h_last && dok) store_states<VEC>(p.h_last + (b * D + d) * N + g * kG, g, N, h);
+}
+
+/* ------------------------------------------------------------------ */
+/* backward                                                            */
+/* ------------------------------------------------------------------ */
+
+/*
+ * Reduce-scatter of 8 values across the lanes of a warp that share the
+ * same lane-group index g (lanes differing in bits >= log2(P)).  After the
+ * call lane holds `cnt` sums starting at index `base`; lanes with
+ * (lane & dup) != 0 hold duplicates of another lane's sums.
+ */
+template <int P>
+__device__ __forceinline__ void reduce_scatter8(float (&v)[8], int lane, int &base,
+                                                int &cnt, int &dup) {
+    cnt = 8;
+    base = 0;
+    dup = 0;
+#pragma unroll
+    for (int o = 16; o >= P; o >>= 1) {
+        if (cnt > 1) {
+            const int half = cnt >> 1;
+            const bool up = (lane & o) != 0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                if (k < half) {
+                    const float send = up ? v[k] : v[k + half];
+                    const float keep = up ? v[k + half] : v[k];
+                    v[k] = keep + __shfl_xor_sync(kFull, send, o);
+                }
+            }
+            if (up) base += half;
+            cnt = half;
+        } else {
+            v[0] += __shfl_xor_sync(kFull, v[0], o);
+            dup |= o;
+        }
+    }
+}
+
+template <int P, bool SHARED, bool VEC, bool HALL>
+__global__ void __launch_bounds__(kNT) k_scan1d_bwd(Scan1DDev p) {
+    constexpr int DT = kNT / P;
+    constexpr int T = kChunk;
+    constexpr int NW = kNT / 32;
+    constexpr int NP = kG * P;
+    extern __shared__ __align__(16) float smem[];
+
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    const int g = tid % P;
+    const int dl = tid / P;
+    const long b = blockIdx.y;
+    const long D = p.D, L = p.L;
+    const int N = (int)p.N;
+    const long d0 = (long)blockIdx.x * DT;
+    const long d = d0 + dl;
+    const bool dok = d < D;
+    const int dvalid = (int)min((long)DT, D - d0);
+
+    const int BWr = bc_row_stride(SHARED, DT, N);
+    const int xs_sz = T * DT;
+    const int bs_sz = T * BWr;
+    const int stage_sz = 3 * xs_sz + 2 * bs_sz;
+    float *part = smem + 2 * stage_sz; /* [T][NW][2*NP], SHARED only */
+
+    float A2[kG], Ar[kG], gc[kG], dAacc[kG];
+#pragma unroll
+    for (int j = 0; j < kG; ++j) {
+        const int n = g * kG + j;
+        const bool ok = dok && n < N;
+        Ar[j] = ok ? __ldg(p.A + d * N + n) : 0.f;
+        A2[j] = Ar[j] * KMB_LOG2E;
+        gc[j] = 0.f;
+        dAacc[j] = 0.f;
+    }
+
+    const float *xg = p.x + b * L * D + d0;
+    const float *dg = p.dt + b * L * D + d0;
+    const float *yg = p.dy + b * L * D + d0;
+    const long bld = SHARED ? (long)N : D * N;
+    const float *Bg = p.B + (SHARED ? b * L * N : (b * L * D + d0) * N);
+    const float *Cg = p.C + (SHARED ? b * L * N : (b * L * D + d0) * N);
+    const int bcols = SHARED ? N : DT * N;
+    const int bvalid = SHARED ? N : dvalid * N;
+    const bool vxd = p.vec_xd, vbc = p.vec_bc;
+
+    const int nch = (int)((L + T - 1) / T);
+    auto load = [&](int c, int stage) {
+        float *st = smem + stage * stage_sz;
+        const long t0 = (long)c * T;
+        const int rv = (int)min((long)T, L - t0);
+        kmb_load_tile<kNT>(st, DT, xg + t0 * D, D, T, DT, rv, dvalid, vxd, tid);
+        kmb_load_tile<kNT>(st + xs_sz, DT, dg + t0 * D, D, T, DT, rv, dvalid, vxd, tid);
+        kmb_load_tile<kNT>(st + 2 * xs_sz, DT, yg + t0 * D, D, T, DT, rv, dvalid, vxd, tid);
+        kmb_load_tile<kNT>(st + 3 * xs_sz, BWr, Bg + t0 * bld, bld, T, bcols, rv, bvalid,
+                           vbc, tid);
+        kmb_load_tile<kNT>(st + 3 * xs_sz + bs_sz, BWr, Cg + t0 * bld, bld, T, bcols, rv,
+                           bvalid, vbc, tid);
+    };
+
+    load(nch - 1, 0);
+    kmb_cp_async_commit();
+
+    const int boff = (SHARED ? 0 : dl * N) + g * kG;
+    const bool clampit = p.clamp != 0;
+
+    for (int c = nch - 1, it = 0; c >= 0; --c, ++it) {
+        kmb_cp_async_wait<0>();
+        __syncthreads();
+        if (c > 0) load(c - 1, (it + 1) & 1);
+        kmb_cp_async_commit();
+
+        const float *st = smem + (it & 1) * stage_sz;
+        const float *xs = st;
+        const float *ds = st + xs_sz;
+        const float *dys = st + 2 * xs_sz;
+        const float *bs = st + 3 * xs_sz;
+        const float *cs = bs + bs_sz;
+        const long t0 = (long)c * T;
+        const int len = (int)min((long)T, L - t0);
+
+        /* state before the chunk's first step */
+        float hs[kG];
+        if (c > 0) {
+            const float *src = HALL ? p.h_all + ((b * L + t0 - 1) * D + d) * N + g * kG
+                                    : p.ckpt_in + ((b * p.nslots + c - 1) * D + d) * N + g * kG;
+            if (dok) load_states_g<VEC>(src, g, N, hs);
+            else hs[0] = hs[1] = hs[2] = hs[3] = 0.f;
+        } else {
+#pragma unroll
+            for (int j = 0; j < kG; ++j) {
+                const int n = g * kG + j;
+                hs[j] = (dok && n < N && p.h0) ? p.h0[(b * D + d) * N + n] : 0.f;
+            }
+        }
+
+        /* forward recompute of the chunk's states (kept in registers) */
+        float hr[HALL ? 1 : T][kG];
+        if (!HALL) {
+            float hh[kG] = {hs[0], hs[1], hs[2], hs[3]};
+#pragma unroll
+            for (int i = 0; i < T; ++i) {
+                if (i < len) {
+                    const float xv = xs[i * DT + dl];
+                    const float dv = ds[i * DT + dl];
+                    const float u = dv * xv;
+                    float bv[kG];
+                    load_states<VEC>(bs + i * BWr + boff, g, N, bv);
+#pragma unroll
+                    for (int j = 0; j < kG; ++j) {
+                        const float a = kmb_ex2(dv * A2[j]);
+                        float hn = fmaf(a, hh[j], bv[j] * u);
+                        if (clampit) hn = clamp1000(hn);
+                        hh[j] = hn;
+                        hr[i][j] = hn;
+                    }
+                }
+            }
+        }
+
+        /* reverse sweep */
+#pragma unroll
+        for (int i = T - 1; i >= 0; --i) {
+            if (i < len) {
+                const long t = t0 + i;
+                const float xv = xs[i * DT + dl];
+                const float dv = ds[i * DT + dl];
+                const float dyv = dys[i * DT + dl];
+                float bv[kG], cv[kG], hp[kG], ht[kG];
+                load_states<VEC>(bs + i * BWr + boff, g, N, bv);
+                load_states<VEC>(cs + i * BWr + boff, g, N, cv);
+                if (HALL) {
+                    if (dok) {
+                        load_states_g<VEC>(p.h_all + ((b * L + t) * D + d) * N + g * kG, g, N, ht);
+                        if (i > 0)
+                            load_states_g<VEC>(p.h_all + ((b * L + t - 1) * D + d) * N + g * kG,
+                                               g, N, hp);
+                        else
+                            for (int j = 0; j < kG; ++j) hp[j] = hs[j];
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < kG; ++j) ht[j] = hp[j] = 0.f;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < kG; ++j) {
+                        ht[j] = hr[HALL ? 0 : i][j];
+                        hp[j] = (i > 0) ? hr[HALL ? 0 : (i > 0 ? i - 1 : 0)][j] : hs[j];
+                    }
+                }
+
+                float dxp = 0.f, ddtp = 0.f;
+                float v[8];
+#pragma unroll
+                for (int j = 0; j < kG; ++j) {
+                    const float a = kmb_ex2(dv * A2[j]);
+                    const float ah = fmaf(dyv, cv[j], gc[j]);
+                    const float gdt = ah * dv;
+                    v[j] = gdt * xv;          /* dB contribution */
+                    v[4 + j] = dyv * ht[j];   /* dC contribution */
+                    dAacc[j] = fmaf(gdt * a, hp[j], dAacc[j]);
+                    dxp = fmaf(gdt, bv[j], dxp);
+                    ddtp = fmaf(ah, fmaf(Ar[j] * a, hp[j], bv[j] * xv), ddtp);
+                    gc[j] = ah * a;
+                }
+#pragma unroll
+                for (int o = P / 2; o > 0; o >>= 1) {
+                    dxp += __shfl_xor_sync(kFull, dxp, o);
+                    ddtp += __shfl_xor_sync(kFull, ddtp, o);
+                }
+                if (dok && g == 0) {
+                    p.dx[(b * L + t) * D + d] = dxp;
+                    p.ddt[(b * L + t) * D + d] = ddtp;
+                }
+                if (SHARED) {
+                    int base, cnt, dup;
+                    reduce_scatter8<P>(v, lane, base, cnt, dup);
+                    if ((lane & dup) == 0) {
+                        float *prow = part + (i * NW + warp) * (2 * NP);
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) {
+                            if (k < cnt) {
+                                const int idx = base + k;
+                                prow[(idx >> 2) * NP + g * kG + (idx & 3)] = v[k];
+                            }
+                        }
+                    }
+                } else if (dok) {
+                    float vb[kG] = {v[0], v[1], v[2], v[3]};
+                    float vc[kG] = {v[4], v[5], v[6], v[7]};
+                    const long o = ((b * L + t) * D + d) * N + g * kG;
+                    store_states<VEC>(p.dB + o, g, N, vb);
+                    store_states<VEC>(p.dC + o, g, N, vc);
+                }
+            }
+        }
+
+        if (SHARED) {
+            __syncthreads();
+            const int tot = len * 2 * NP;
+            for (int e = tid; e < tot; e += kNT) {
+                const int i = e / (2 * NP);
+                const int r = e - i * (2 * NP);
+                const int n = r % NP;
+                if (n < N) {
+                    float s = 0.f;
+#pragma unroll
+                    for (int w = 0; w < NW; ++w) s += part[(i * NW + w) * (2 * NP) + r];
+                    float *dst = (r < NP) ? p.dB : p.dC;
+                    atomicAdd(dst + (b * L + t0 + i) * N + n, s);
+                }
+            }
+        }
+    }
+    kmb_cp_async_wait<0>();
+
+#pragma unroll
+    for (int j = 0; j < kG; ++j) {
+        const int n = g * kG + j;
+        if (dok && n < N) atomicAdd(p.dA + d * N + n, dAacc[j]);
+    }
+}
+
+/* M = 1 backward with per-channel A/B/C and a per-step delta shared by all
+ * channels (reference cpu/scan1d_backward.c:23-191).  One thread per
+ * channel walks t downwards; ddelta[t] is a sum over channels. */
+__global__ void __launch_bounds__(128)
+k_scan1d_bwd_m1_shared(const float *x, const float *A, const float *A_diag,
+                       const float *B, const float *C, const float *delta,
+                       const float *h0, const float *h, const float *dy,
+                       float *dx, float *dA, float *dB, float *dC,
+                       float *ddelta, long L, long D) {
+    const long d = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    const bool ok = d < D;
+    const float a = ok ? A[d] : 0.f, bb = ok ? B[d] : 0.f, cc = ok ? C[d] : 0.f;
+    float adj = 0.f, sA = 0.f, sB = 0.f, sC = 0.f;
+    for (long t = L - 1; t >= 0; --t) {
+        float ddt = 0.f;
+        if (ok) {
+            const long td = t * D + d;
+            const float dt = delta[t];
+            const float xt = x[td];
+            const float g = dy[td];
+            const float da = A_diag ? A_diag[td] : kmb_ex2(dt * a * KMB_LOG2E);
+            const float hprev = t > 0 ? h[(t - 1) * D + d] : (h0 ? h0[d] : 0.f);
+            const float ah = fmaf(g, cc, adj);
+            sC = fmaf(g, h[td], sC);
+            sB = fmaf(ah * dt, xt, sB);
+            sA = fmaf(ah * dt * da, hprev, sA);
+            dx[td] = ah * dt * bb;
+            ddt = ah * fmaf(a * da, hprev, bb * xt);
+            adj = ah * da;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ddt += __shfl_xor_sync(kFull, ddt, o);
+        if ((threadIdx.x & 31) == 0) atomicAdd(ddelta + t, ddt);
+    }
+    if (ok) {
+        dA[d] = sA;
+        dB[d] = sB;
+        dC[d] = sC;
+    }
+}
+
+int pick_p(long N) {
+    long q = (N + kG - 1) / kG;
+    int p = 1;
+    while (p < q) p <<= 1;
+    return p;
+}
+
+Scan1DDev make_dev(const KmbScan1D *a) {
+    Scan1DDev p;
+    p.x = a->x; p.dt = a->dt; p.A = a->A; p.B = a->B; p.C = a->C; p.h0 = a->h0;
+    p.y = a->y; p.h_last = a->h_last; p.h_all = a->h_all; p.ckpt = a->ckpt;
+    p.dy = a->dy; p.dx = a->dx; p.ddt = a->ddt; p.dA = a->dA; p.dB = a->dB; p.dC = a->dC;
+    p.ckpt_in = nullptr;
+    p.L = a->L; p.D = a->D; p.N = a->N;
+    p.nslots = (a->L + kChunk - 1) / kChunk;
+    p.clamp = a->clamp;
+    auto al = [](const void *q) { return ((uintptr_t)q & 15u) == 0; };
+    p.vec_xd = (a->D % 4 == 0) && al(a->x) && al(a->dt) && (!a->dy || al(a->dy));
+    p.vec_bc = (a->N % 4 == 0) && al(a->B) && al(a->C);
+    return p;
+}
+
+template <int P, bool SHARED, bool VEC>
+cudaError_t launch_fwd_t(const Scan1DDev &p, long batch, cudaStream_t s) {
+    using Cfg = FwdCfg<P, SHARED>;
+    const int BWr = bc_row_stride(SHARED, Cfg::DT, (int)p.N);
+    const size_t smem = sizeof(float) * Cfg::ST * (2 * Cfg::TT * Cfg::DT + 2 * Cfg::TT * BWr);
+    auto kern = k_scan1d_fwd<P, SHARED, VEC>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    dim3 grid((unsigned)((p.D + Cfg::DT - 1) / Cfg::DT), (unsigned)batch);
+    kern<<<grid, kNT, smem, s>>>(p);
+    return cudaGetLastError();
+}
+
+template <int P, bool SHARED, bool VEC, bool HALL>
+cudaError_t launch_bwd_t(const Scan1DDev &p, long batch, cudaStream_t s) {
+    constexpr int DT = kNT / P;
+    const int BWr = bc_row_stride(SHARED, DT, (int)p.N);
+    size_t smem = sizeof(float) * 2 * (3 * kChunk * DT + 2 * kChunk * BWr);
+    if (SHARED) smem += sizeof(float) * kChunk * (kNT / 32) * 2 * (kG * P);
+    auto kern = k_scan1d_bwd<P, SHARED, VEC, HALL>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    dim3 grid((unsigned)((p.D + DT - 1) / DT), (unsigned)batch);
+    kern<<<grid, kNT, smem, s>>>(p);
+    return cudaGetLastError();
+}
+
+template <int P>
+cudaError_t fwd_p(const Scan1DDev &p, long batch, bool shared, bool vec, cudaStream_t s) {
+    if (shared) return vec ? launch_fwd_t<P, true, true>(p, batch, s)
+                           : launch_fwd_t<P, true, false>(p, batch, s);
+    return vec ? launch_fwd_t<P, false, true>(p, batch, s)
+               : launch_fwd_t<P, false, false>(p, batch, s);
+}
+
+template <int P>
+cudaError_t bwd_p(const Scan1DDev &p, long batch, bool shared, bool vec, bool hall,
+                  cudaStream_t s) {
+    if (shared) {
+        if (vec) return hall ? launch_bwd_t<P, true, true, true>(p, batch, s)
+                             : launch_bwd_t<P, true, true, false>(p, batch, s);
+        return hall ? launch_bwd_t<P, true, false, true>(p, batch, s)
+                    : launch_bwd_t<P, true, false, false>(p, batch, s);
+    }
+    if (vec) return hall ? launch_bwd_t<P, false, true, true>(p, batch, s)
+                         : launch_bwd_t<P, false, true, false>(p, batch, s);
+    return hall ? launch_bwd_t<P, false, false, true>(p, batch, s)
+                : launch_bwd_t<P, false, false, false>(p, batch, s);
+}
+
+} // namespace
+
+extern "C" int kmb_launch_scan1d_fwd(const KmbScan1D *a, cudaStream_t s) {
+    Scan1DDev p = make_dev(a);
+    const bool vec = (a->N % 4) == 0;
+    const bool shared = a->bc_shared != 0;
+    cudaError_t e;
+    switch (pick_p(a->N)) {
+    case 1: e = fwd_p<1>(p, a->batch, shared, vec, s); break;
+    case 2: e = fwd_p<2>(p, a->batch, shared, vec, s); break;
+    case 4: e = fwd_p<4>(p, a->batch, shared, vec, s); break;
+    case 8: e = fwd_p<8>(p, a->batch, shared, vec, s); break;
+    case 16: e = fwd_p<16>(p, a->batch, shared, vec, s); break;
+    case 32: e = fwd_p<32>(p, a->batch, shared, vec, s); break;
+    default: return kmb_fail(KMB_EUNSUPPORTED, "scan1d: N=%ld exceeds 128 states", a->N);
+    }
+    if (e != cudaSuccess) return kmb_cuda_fail(e, "scan1d forward launch");
+    return KMB_OK;
+}
+
+extern "C" int kmb_launch_scan1d_bwd(const KmbScan1D *a, const float *ckpt_in,
+                                     cudaStream_t s) {
+    Scan1DDev p = make_dev(a);
+    p.ckpt_in = ckpt_in;
+    const bool vec = (a->N % 4) == 0;
+    const bool shared = a->bc_shared != 0;
+    const bool hall = a->h_all != nullptr;
+    cudaError_t e = cudaMemsetAsync(a->dA, 0, sizeof(float) * a->D * a->N, s);
+    if (e == cudaSuccess && shared) {
+        const size_t nb = sizeof(float) * a->batch * a->L * a->N;
+        e = cudaMemsetAsync(a->dB, 0, nb, s);
+        if (e == cudaSuccess) e = cudaMemsetAsync(a->dC, 0, nb, s);
+    }
+    if (e != cudaSuccess) return kmb_cuda_fail(e, "scan1d backward memset");
+    switch (pick_p(a->N)) {
+    case 1: e = bwd_p<1>(p, a->batch, shared, vec, hall, s); break;
+    case 2: e = bwd_p<2>(p, a->batch, shared, vec, hall, s); break;
+    case 4: e = bwd_p<4>(p, a->batch, shared, vec, hall, s); break;
+    case 8: e = bwd_p<8>(p, a->batch, shared, vec, hall, s); break;
+    case 16: e = bwd_p<16>(p, a->batch, shared, vec, hall, s); break;
+    case 32: e = bwd_p<32>(p, a->batch, shared, vec, hall, s); break;
+    default: return kmb_fail(KMB_EUNSUPPORTED, "scan1d: N=%ld exceeds 128 states", a->N);
+    }
+    if (e != cudaSuccess) return kmb_cuda_fail(e, "scan1d backward launch");
+    return KMB_OK;
+}
+
+extern "C" int kmb_launch_scan1d_bwd_m1_shared(const float *x, const float *A,
+                                               const float *A_diag, const float *B,
+                                               const float *C, const float *delta,
+                                               const float *h0, const float *h,
+                                               const float *dy, float *dx, float *dA,
+                                               float *dB, float *dC, float *ddelta,
+                                               long L, long D, cudaStream_t s) {
+    cudaError_t e = cudaMemsetAsync(ddelta, 0, sizeof(float) * L, s);
+    if (e != cudaSuccess) return kmb_cuda_fail(e, "scan1d m1 backward memset");
+    const unsigned blocks = (unsigned)((D + 127) / 128);
+    k_scan1d_bwd_m1_shared<<<blocks, 128, 0, s>>>(x, A, A_diag, B, C, delta, h0, h, dy, dx,
+                                                  dA, dB, dC, ddelta, L, D);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return kmb_cuda_fail(e, "scan1d m1 backward launch");
+    return KMB_OK;
+}

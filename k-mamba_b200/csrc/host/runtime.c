@@ -1,0 +1,309 @@
+/*
+ * Host runtime of the B200 k-mamba library: error reporting, the library
+ * stream, the device buffer pool and host<->device staging of caller
+ * buffers.
+ *
+ * The reference keeps a thread-local first-fit pool of host chunks
+ * (src/km_memory_pool.c:54-117).  Here the scratch lives on the device, so
+ * the pool caches cudaMalloc blocks per device and hands them out by size
+ * under a mutex.  Every call that staged buffers or used pooled scratch
+ * synchronizes its stream before the blocks go back to the pool, so a
+ * block is never reused while a kernel may still read it.
+ */
+#define _GNU_SOURCE
+#include <pthread.h>
+#include <stdarg.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "../kmb_internal.h"
+
+/* ------------------------------------------------------------------ */
+/* errors                                                              */
+/* ------------------------------------------------------------------ */
+
+static __thread char t_err[512];
+static __thread int t_status;
+
+int kmb_fail(int status, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(t_err, sizeof t_err, fmt, ap);
+    va_end(ap);
+    t_status = status;
+    return status;
+}
+
+int kmb_cuda_fail(cudaError_t e, const char *where) {
+    return kmb_fail(KMB_ECUDA, "%s: %s (%s)", where, cudaGetErrorString(e),
+                    cudaGetErrorName(e));
+}
+
+const char *kmb_last_error(void) { return t_err; }
+int kmb_last_status(void) { return t_status; }
+void kmb_clear_error(void) {
+    t_err[0] = 0;
+    t_status = 0;
+}
+
+/* ------------------------------------------------------------------ */
+/* stream and synchronisation mode                                     */
+/* ------------------------------------------------------------------ */
+
+static __thread cudaStream_t t_stream;
+static int g_sync = 1;
+
+void kmb_set_stream(void *s) { t_stream = (cudaStream_t)s; }
+void *kmb_get_stream(void) { return (void *)t_stream; }
+cudaStream_t kmb_stream(void) { return t_stream; }
+void kmb_set_sync(int on) { __atomic_store_n(&g_sync, on ? 1 : 0, __ATOMIC_RELAXED); }
+int kmb_get_sync(void) { return __atomic_load_n(&g_sync, __ATOMIC_RELAXED); }
+int kmb_sync_enabled(void) { return kmb_get_sync(); }
+
+int kmb_is_device_ptr(const void *p) {
+    struct cudaPointerAttributes at;
+    cudaError_t e;
+    if (!p) return 0;
+    e = cudaPointerGetAttributes(&at, p);
+    if (e != cudaSuccess) {
+        (void)cudaGetLastError();
+        return 0;
+    }
+    return at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged;
+}
+
+/* ------------------------------------------------------------------ */
+/* device pool                                                         */
+/* ------------------------------------------------------------------ */
+
+typedef struct PoolBlock {
+    void *p;
+    size_t bytes;
+    int device;
+    int used;
+    struct PoolBlock *next;
+} PoolBlock;
+
+static pthread_mutex_t g_pool_mu = PTHREAD_MUTEX_INITIALIZER;
+static PoolBlock *g_pool;
+static size_t g_pool_held;
+
+static size_t pool_round(size_t n) {
+    const size_t q = 512;
+    if (n == 0) n = 1;
+    return (n + q - 1) / q * q;
+}
+
+static size_t pool_trim_locked(void) {
+    size_t freed = 0;
+    PoolBlock **pp = &g_pool;
+    while (*pp) {
+        PoolBlock *b = *pp;
+        if (!b->used) {
+            int cur = 0;
+            cudaGetDevice(&cur);
+            if (cur != b->device) cudaSetDevice(b->device);
+            cudaFree(b->p);
+            if (cur != b->device) cudaSetDevice(cur);
+            freed += b->bytes;
+            g_pool_held -= b->bytes;
+            *pp = b->next;
+            free(b);
+        } else {
+            pp = &b->next;
+        }
+    }
+    return freed;
+}
+
+void *kmb_pool_alloc(size_t bytes) {
+    int dev = 0;
+    PoolBlock *best = NULL;
+    void *p = NULL;
+    cudaError_t e;
+
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        (void)cudaGetLastError();
+        kmb_fail(KMB_ECUDA, "kmb_pool_alloc: no CUDA device");
+        return NULL;
+    }
+    bytes = pool_round(bytes);
+    pthread_mutex_lock(&g_pool_mu);
+    for (PoolBlock *b = g_pool; b; b = b->next) {
+        if (b->used || b->device != dev || b->bytes < bytes || b->bytes > 2 * bytes)
+            continue;
+        if (!best || b->bytes < best->bytes) best = b;
+    }
+    if (best) {
+        best->used = 1;
+        p = best->p;
+        pthread_mutex_unlock(&g_pool_mu);
+        return p;
+    }
+    e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) {
+        (void)cudaGetLastError();
+        pool_trim_locked();
+        e = cudaMalloc(&p, bytes);
+    }
+    if (e != cudaSuccess) {
+        (void)cudaGetLastError();
+        pthread_mutex_unlock(&g_pool_mu);
+        kmb_cuda_fail(e, "kmb_pool_alloc cudaMalloc");
+        return NULL;
+    }
+    best = (PoolBlock *)calloc(1, sizeof *best);
+    if (!best) {
+        cudaFree(p);
+        pthread_mutex_unlock(&g_pool_mu);
+        kmb_fail(KMB_ENOMEM, "kmb_pool_alloc: host allocation failed");
+        return NULL;
+    }
+    best->p = p;
+    best->bytes = bytes;
+    best->device = dev;
+    best->used = 1;
+    best->next = g_pool;
+    g_pool = best;
+    g_pool_held += bytes;
+    pthread_mutex_unlock(&g_pool_mu);
+    return p;
+}
+
+void kmb_pool_free(void *p) {
+    if (!p) return;
+    pthread_mutex_lock(&g_pool_mu);
+    for (PoolBlock *b = g_pool; b; b = b->next) {
+        if (b->p == p) {
+            b->used = 0;
+            break;
+        }
+    }
+    pthread_mutex_unlock(&g_pool_mu);
+}
+
+size_t kmb_pool_trim(void) {
+    size_t f;
+    pthread_mutex_lock(&g_pool_mu);
+    f = pool_trim_locked();
+    pthread_mutex_unlock(&g_pool_mu);
+    return f;
+}
+
+size_t kmb_pool_bytes_held(void) {
+    size_t h;
+    pthread_mutex_lock(&g_pool_mu);
+    h = g_pool_held;
+    pthread_mutex_unlock(&g_pool_mu);
+    return h;
+}
+
+/* ------------------------------------------------------------------ */
+/* staging                                                             */
+/* ------------------------------------------------------------------ */
+
+void kmb_stage_begin(KmbStage *st) {
+    memset(st, 0, sizeof *st);
+    st->s = kmb_stream();
+}
+
+static KmbStageBuf *stage_find(KmbStage *st, const void *p) {
+    for (int i = 0; i < st->n; ++i)
+        if (st->b[i].user == p) return &st->b[i];
+    return NULL;
+}
+
+static void *stage_add(KmbStage *st, const void *p, size_t bytes, int out, int copy_in) {
+    KmbStageBuf *b;
+    cudaError_t e;
+    if (st->status) return NULL;
+    if (!p) return NULL;
+    b = stage_find(st, p);
+    if (b) {
+        if (bytes > b->bytes && b->owned) {
+            st->status = kmb_fail(KMB_EINVAL, "staging: buffer %p reused with a larger size", p);
+            return NULL;
+        }
+        b->out |= out;
+        return b->dev;
+    }
+    if (st->n >= KMB_STAGE_MAX) {
+        st->status = kmb_fail(KMB_EINVAL, "staging: too many buffers");
+        return NULL;
+    }
+    b = &st->b[st->n++];
+    b->user = p;
+    b->bytes = bytes;
+    b->out = out;
+    if (kmb_is_device_ptr(p)) {
+        b->dev = (void *)p;
+        b->owned = 0;
+        return b->dev;
+    }
+    b->owned = 1;
+    b->dev = kmb_pool_alloc(bytes);
+    if (!b->dev) {
+        st->status = kmb_last_status() ? kmb_last_status() : KMB_ENOMEM;
+        return NULL;
+    }
+    if (copy_in && bytes) {
+        e = cudaMemcpyAsync(b->dev, p, bytes, cudaMemcpyHostToDevice, st->s);
+        if (e != cudaSuccess) {
+            st->status = kmb_cuda_fail(e, "staging host->device copy");
+            return NULL;
+        }
+    }
+    return b->dev;
+}
+
+void *kmb_stage_in(KmbStage *st, const void *p, size_t bytes) {
+    return stage_add(st, p, bytes, 0, 1);
+}
+
+void *kmb_stage_out(KmbStage *st, void *p, size_t bytes, int copy_in) {
+    return stage_add(st, p, bytes, 1, copy_in);
+}
+
+void *kmb_scratch(KmbStage *st, size_t bytes) {
+    KmbStageBuf *b;
+    if (st->status) return NULL;
+    if (st->n >= KMB_STAGE_MAX) {
+        st->status = kmb_fail(KMB_EINVAL, "staging: too many buffers");
+        return NULL;
+    }
+    b = &st->b[st->n++];
+    memset(b, 0, sizeof *b);
+    b->owned = 1;
+    b->bytes = bytes;
+    b->dev = kmb_pool_alloc(bytes);
+    if (!b->dev) {
+        st->status = kmb_last_status() ? kmb_last_status() : KMB_ENOMEM;
+        return NULL;
+    }
+    return b->dev;
+}
+
+int kmb_stage_finish(KmbStage *st, int status) {
+    int any_owned = 0;
+    cudaError_t e;
+    if (!status) status = st->status;
+    for (int i = 0; i < st->n; ++i) {
+        KmbStageBuf *b = &st->b[i];
+        if (!b->owned) continue;
+        any_owned = 1;
+        if (status == KMB_OK && b->out && b->user && b->bytes) {
+            e = cudaMemcpyAsync((void *)b->user, b->dev, b->bytes, cudaMemcpyDeviceToHost, st->s);
+            if (e != cudaSuccess) status = kmb_cuda_fail(e, "staging device->host copy");
+        }
+    }
+    if (any_owned || kmb_sync_enabled()) {
+        e = cudaStreamSynchronize(st->s);
+        if (e != cudaSuccess && status == KMB_OK) status = kmb_cuda_fail(e, "stream synchronize");
+    }
+    for (int i = 0; i < st->n; ++i)
+        if (st->b[i].owned) kmb_pool_free(st->b[i].dev);
+    st->n = 0;
+    return status;
+}

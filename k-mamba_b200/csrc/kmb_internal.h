@@ -1,0 +1,78 @@
+/*
+ * Internal ABI between the C host layer (csrc/host) and the CUDA
+ * launchers (csrc/cuda).  Plain C types only; every launcher takes
+ * device pointers and a cudaStream_t and returns a KMB_* status.
+ */
+#ifndef KMB_INTERNAL_H
+#define KMB_INTERNAL_H
+
+#include <stddef.h>
+#include <cuda_runtime_api.h>
+#include "kmamba_b200.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Steps between forward checkpoints; also the backward chunk length. */
+#define KMB_SCAN1D_CHUNK 16
+
+/* Records a status and a message for kmb_last_error(); returns status. */
+int kmb_fail(int status, const char *fmt, ...);
+int kmb_cuda_fail(cudaError_t e, const char *where);
+
+/* 1D selective scan launchers (csrc/cuda/scan1d.cu). */
+int kmb_launch_scan1d_fwd(const KmbScan1D *a, cudaStream_t s);
+int kmb_launch_scan1d_bwd(const KmbScan1D *a, const float *ckpt_in,
+                          cudaStream_t s);
+int kmb_launch_scan1d_bwd_m1_shared(const float *x, const float *A,
+                                    const float *A_diag, const float *B,
+                                    const float *C, const float *delta,
+                                    const float *h0, const float *h,
+                                    const float *dy, float *dx, float *dA,
+                                    float *dB, float *dC, float *ddelta,
+                                    long L, long D, cudaStream_t s);
+
+/* ------------------------------------------------------------------ */
+/* host runtime (csrc/host/runtime.c)                                   */
+/* ------------------------------------------------------------------ */
+cudaStream_t kmb_stream(void);
+int kmb_sync_enabled(void);
+/* 1 when p is device-accessible memory (device or managed). */
+int kmb_is_device_ptr(const void *p);
+
+/*
+ * Staging of caller buffers.  kmb_stage_in/out return a device pointer:
+ * the caller's own pointer when it is device memory, else a pooled device
+ * buffer (inputs are copied host->device on the library stream; outputs
+ * are copied back by kmb_stage_finish).  Passing the same host pointer
+ * twice returns the same device buffer.
+ */
+#define KMB_STAGE_MAX 48
+typedef struct {
+    const void *user;
+    void *dev;
+    size_t bytes;
+    int out;     /* copy back on finish */
+    int owned;   /* dev is a pool block */
+} KmbStageBuf;
+typedef struct {
+    KmbStageBuf b[KMB_STAGE_MAX];
+    int n;
+    int status;
+    cudaStream_t s;
+} KmbStage;
+
+void kmb_stage_begin(KmbStage *st);
+void *kmb_stage_in(KmbStage *st, const void *p, size_t bytes);
+void *kmb_stage_out(KmbStage *st, void *p, size_t bytes, int copy_in);
+void *kmb_scratch(KmbStage *st, size_t bytes);
+/* Copies outputs back (when status is OK), synchronizes when needed and
+ * releases pooled buffers.  Returns the first error seen. */
+int kmb_stage_finish(KmbStage *st, int status);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif
