@@ -100,6 +100,72 @@ long kmb_scan1d_ckpt_elems(long batch, long L, long D, long N);
 int kmb_scan1d_fwd(const KmbScan1D *args);
 int kmb_scan1d_bwd(const KmbScan1D *args);
 
+/* ------------------------------------------------------------------ */
+/* Batched causal depthwise ConvND                                     */
+/* ------------------------------------------------------------------ */
+/*
+ * Per batch item the semantics of convnd() (convnd.h): input, output, dy,
+ * dinput [batch, prod(dims), D]; kernel, dkernel [K^ndims, D]; bias,
+ * dbias [D] (bias / dbias may be NULL).  The backward overwrites dinput
+ * and writes dkernel / dbias summed over the batch.
+ */
+typedef struct {
+    const float *input;
+    const float *kernel;
+    const float *bias;
+    float *output;
+    const float *dy;
+    float *dinput;
+    float *dkernel;
+    float *dbias;
+    long dims[8];
+    long ndims;
+    long batch;
+    long D;
+    long K;
+} KmbConvND;
+
+int kmb_convnd_fwd(const KmbConvND *args);
+int kmb_convnd_bwd(const KmbConvND *args);
+
+/* ------------------------------------------------------------------ */
+/* Batched ND selective scan with stored states                        */
+/* ------------------------------------------------------------------ */
+/*
+ * Per batch item the recurrence of scannd() (scan_nd.h).  x, y, dx
+ * [batch, P, D]; delta, ddelta [batch, ndims, P, D]; A, dA [ndims, D, M];
+ * B, C, dB, dC [batch, P, D, M] or, when bc_shared, [batch, P, M] (shared
+ * by all channels; dB / dC are then channel sums); h [batch, P, D, M] is
+ * written by the forward and read by the backward.  dA is summed over the
+ * batch.  The backward has no reference implementation: it is the adjoint
+ * of the forward recurrence.
+ */
+typedef struct {
+    const float *x;
+    const float *delta;
+    const float *A;
+    const float *B;
+    const float *C;
+    float *h;
+    float *y;
+    const float *dy;
+    float *dx;
+    float *ddelta;
+    float *dA;
+    float *dB;
+    float *dC;
+    long dims[8];
+    long ndims;
+    long batch;
+    long D;
+    long M;
+    int bc_shared;
+    int flags;     /* reserved, must be 0 */
+} KmbScanND;
+
+int kmb_scannd_fwd(const KmbScanND *args);
+int kmb_scannd_bwd(const KmbScanND *args);
+
 #ifdef __cplusplus
 }
 #endif

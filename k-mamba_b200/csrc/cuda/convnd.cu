@@ -1,0 +1,472 @@
+/*
+ * Causal depthwise ND convolution (dense K^ndims kernel), forward and
+ * backward, for sm_100a.  Semantics of the reference src/convnd.c:67-202:
+ *
+ *   out(p,d)  = bias[d] + sum_k in(p - (K-1-k_axis)_axis, d) * ker[k,d]
+ *   din(s,d)  = sum_k dy(s + (K-1-k_axis)_axis, d) * ker[k,d]      (gather)
+ *   dker[k,d] = sum_p dy(p,d) * in(p - (K-1-k_axis)_axis, d)
+ *   dbias[d]  = sum_p dy(p,d)
+ *
+ * with k the row-major tap index (last axis fastest) and out-of-grid
+ * neighbours counting as zero.  The convolution has no dependency between
+ * outputs, so the reference's wavefront levels do not constrain the GPU:
+ * every kernel is a single pass over the grid.
+ *
+ * 2D fast path (the config-3 shape).  A thread owns one column j, a
+ * strip of TI rows and 4 consecutive channels (float4).  A K x K window
+ * of float4 slides down the strip, so each output row costs K 128-bit
+ * loads (the column neighbours come from L1) and K*K float4 FMAs; the
+ * kernel taps stay in registers.  The backward slides two windows (dy
+ * rows r..r+K-1 for the gather-form dinput, input rows r-K+1..r for
+ * dkernel) downwards through the strip; dkernel/dbias partials are folded
+ * in shared memory and added to global memory with one atomic per CTA
+ * and (tap, channel).
+ *
+ * Any other rank uses the generic kernels (thread per point and channel).
+ */
+#include <string.h>
+
+#include "kmb_common.cuh"
+#include "../kmb_internal.h"
+
+namespace {
+
+constexpr int kMaxNd = 8;
+
+struct ConvDev {
+    const float *in, *ker, *bias, *dy;
+    float *out, *din, *dker, *dbias;
+    long batch, P, D, K, KV;
+    int nd;
+    long dims[kMaxNd];
+    long strides[kMaxNd];
+};
+
+/* ------------------------------------------------------------------ */
+/* 2D fast path                                                        */
+/* ------------------------------------------------------------------ */
+
+constexpr int kThreads2d = 256;
+
+template <int CW>
+struct Vec;
+template <>
+struct Vec<4> {
+    using T = float4;
+    __device__ static T zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
+    __device__ static T load(const float *p) { return __ldg(reinterpret_cast<const float4 *>(p)); }
+    __device__ static void store(float *p, T v) { *reinterpret_cast<float4 *>(p) = v; }
+    __device__ static T fma(T a, T b, T c) {
+        return make_float4(fmaf(a.x, b.x, c.x), fmaf(a.y, b.y, c.y), fmaf(a.z, b.z, c.z),
+                           fmaf(a.w, b.w, c.w));
+    }
+    __device__ static T add(T a, T b) { return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w); }
+    __device__ static float get(T v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
+};
+template <>
+struct Vec<1> {
+    using T = float;
+    __device__ static T zero() { return 0.f; }
+    __device__ static T load(const float *p) { return __ldg(p); }
+    __device__ static void store(float *p, T v) { *p = v; }
+    __device__ static T fma(T a, T b, T c) { return fmaf(a, b, c); }
+    __device__ static T add(T a, T b) { return a + b; }
+    __device__ static float get(T v, int) { return v; }
+};
+
+/* Launch geometry of the 2D kernels: CGT channel groups x TJ columns per
+ * CTA, TI rows per strip. */
+struct Geo2d {
+    int cgt, tj, ti;
+    long ctiles, jtiles, strips;
+};
+
+
+
+template <int K, int CW>
+__global__ void __launch_bounds__(kThreads2d) k_conv2d_fwd(ConvDev p, Geo2d g) {
+    using V = Vec<CW>;
+    using T = typename V::T;
+    const int tid = threadIdx.x;
+    const int cg = tid % g.cgt;
+    const int jj = tid / g.cgt;
+    const long H = p.dims[0], W = p.dims[1], D = p.D;
+    const long ct = blockIdx.x % g.ctiles;
+    const long jt = blockIdx.x / g.ctiles;
+    const long j = jt * g.tj + jj;
+    const long c = (ct * g.cgt + cg) * CW;
+    const long b = blockIdx.z;
+    const long r0 = (long)blockIdx.y * g.ti;
+    if (j >= W || c >= D) return;
+
+    T wk[K * K];
+#pragma unroll
+    for (int k = 0; k < K * K; ++k) wk[k] = V::load(p.ker + k * D + c);
+    const T bias = p.bias ? V::load(p.bias + c) : V::zero();
+
+    const float *base = p.in + b * H * W * D + c;
+    float *obase = p.out + b * H * W * D + c;
+    T win[K][K];
+    /* rows r0-K+1 .. r0-1 */
+#pragma unroll
+    for (int a = 0; a < K - 1; ++a) {
+        const long rr = r0 - (K - 1) + a;
+#pragma unroll
+        for (int q = 0; q < K; ++q) {
+            const long cc = j - (K - 1) + q;
+            win[a + 1][q] = (rr >= 0 && cc >= 0) ? V::load(base + (rr * W + cc) * D) : V::zero();
+        }
+    }
+    const long rend = min(H, r0 + g.ti);
+    for (long r = r0; r < rend; ++r) {
+#pragma unroll
+        for (int a = 0; a < K - 1; ++a)
+#pragma unroll
+            for (int q = 0; q < K; ++q) win[a][q] = win[a + 1][q];
+#pragma unroll
+        for (int q = 0; q < K; ++q) {
+            const long cc = j - (K - 1) + q;
+            win[K - 1][q] = cc >= 0 ? V::load(base + (r * W + cc) * D) : V::zero();
+        }
+        T s = bias;
+#pragma unroll
+        for (int a = 0; a < K; ++a)
+#pragma unroll
+            for (int q = 0; q < K; ++q) s = V::fma(win[a][q], wk[a * K + q], s);
+        V::store(obase + (r * W + j) * D, s);
+    }
+}
+
+template <int K, int CW>
+__global__ void __launch_bounds__(kThreads2d) k_conv2d_bwd(ConvDev p, Geo2d g) {
+    using V = Vec<CW>;
+    using T = typename V::T;
+    constexpr int NACC = K * K + 1; /* dkernel taps + dbias */
+    extern __shared__ __align__(16) float red[]; /* [kThreads2d][NACC][CW] */
+    const int tid = threadIdx.x;
+    const int cg = tid % g.cgt;
+    const int jj = tid / g.cgt;
+    const long H = p.dims[0], W = p.dims[1], D = p.D;
+    const long ct = blockIdx.x % g.ctiles;
+    const long jt = blockIdx.x / g.ctiles;
+    const long j = jt * g.tj + jj;
+    const long c = (ct * g.cgt + cg) * CW;
+    const long b = blockIdx.z;
+    const long r0 = (long)blockIdx.y * g.ti;
+    const bool act = j < W && c < D;
+
+    T acc[NACC];
+#pragma unroll
+    for (int k = 0; k < NACC; ++k) acc[k] = V::zero();
+
+    if (act) {
+        T wk[K * K];
+#pragma unroll
+        for (int k = 0; k < K * K; ++k) wk[k] = V::load(p.ker + k * D + c);
+        const float *ib = p.in + b * H * W * D + c;
+        const float *gb = p.dy + b * H * W * D + c;
+        float *db = p.din + b * H * W * D + c;
+        const long rend = min(H, r0 + g.ti);
+        /* walk rows downwards: r = rend-1 .. r0.
+         * gwin[a][q] = dy(r + a, j + q)       a, q in [0, K)
+         * iwin[a][q] = in(r - (K-1) + a, j - (K-1) + q) */
+        T gwin[K][K], iwin[K][K];
+        /* pre-shift state for r = rend-1: gwin[a] = dy(rend + a),
+         * iwin[a] = in(rend - (K-1) + a), a in [0, K-1) */
+#pragma unroll
+        for (int a = 0; a < K - 1; ++a) {
+            const long rg = rend + a;
+            const long ri = rend - (K - 1) + a;
+#pragma unroll
+            for (int q = 0; q < K; ++q) {
+                const long cg2 = j + q;
+                const long ci = j - (K - 1) + q;
+                gwin[a][q] = (rg < H && cg2 < W) ? V::load(gb + (rg * W + cg2) * D) : V::zero();
+                iwin[a][q] = (ri >= 0 && ci >= 0) ? V::load(ib + (ri * W + ci) * D) : V::zero();
+            }
+        }
+        for (long r = rend - 1; r >= r0; --r) {
+            /* dy window: shift up (towards larger a), load row r at a = 0 */
+#pragma unroll
+            for (int a = K - 1; a > 0; --a)
+#pragma unroll
+                for (int q = 0; q < K; ++q) gwin[a][q] = gwin[a - 1][q];
+#pragma unroll
+            for (int q = 0; q < K; ++q) {
+                const long cc = j + q;
+                gwin[0][q] = cc < W ? V::load(gb + (r * W + cc) * D) : V::zero();
+            }
+            /* input window: rows r-(K-1) .. r; shift down, load row r-(K-1) */
+#pragma unroll
+            for (int a = K - 1; a > 0; --a)
+#pragma unroll
+                for (int q = 0; q < K; ++q) iwin[a][q] = iwin[a - 1][q];
+            {
+                const long rr = r - (K - 1);
+#pragma unroll
+                for (int q = 0; q < K; ++q) {
+                    const long cc = j - (K - 1) + q;
+                    iwin[0][q] = (rr >= 0 && cc >= 0) ? V::load(ib + (rr * W + cc) * D)
+                                                      : V::zero();
+                }
+            }
+            /* dinput(r, j): tap (k0, k1) reads dy(r + K-1-k0, j + K-1-k1) */
+            T s = V::zero();
+#pragma unroll
+            for (int k0 = 0; k0 < K; ++k0)
+#pragma unroll
+                for (int k1 = 0; k1 < K; ++k1)
+                    s = V::fma(gwin[K - 1 - k0][K - 1 - k1], wk[k0 * K + k1], s);
+            V::store(db + (r * W + j) * D, s);
+            /* dkernel / dbias at output (r, j) */
+            const T gy = gwin[0][0];
+#pragma unroll
+            for (int k0 = 0; k0 < K; ++k0)
+#pragma unroll
+                for (int k1 = 0; k1 < K; ++k1)
+                    acc[k0 * K + k1] = V::fma(gy, iwin[k0][k1], acc[k0 * K + k1]);
+            acc[K * K] = V::add(acc[K * K], gy);
+        }
+    }
+
+    /* fold the CTA's partials per (tap, channel) and add them to global */
+#pragma unroll
+    for (int k = 0; k < NACC; ++k)
+#pragma unroll
+        for (int i = 0; i < CW; ++i) red[(tid * NACC + k) * CW + i] = V::get(acc[k], i);
+    __syncthreads();
+    const int tj = g.tj;
+    const int nout = g.cgt * NACC * CW;
+    for (int o = tid; o < nout; o += kThreads2d) {
+        const int i = o % CW;
+        const int k = (o / CW) % NACC;
+        const int cgo = o / (CW * NACC);
+        const long cc = (ct * g.cgt + cgo) * CW + i;
+        if (cc >= D) continue;
+        float s = 0.f;
+        for (int q = 0; q < tj; ++q) s += red[((q * g.cgt + cgo) * NACC + k) * CW + i];
+        if (k < K * K) atomicAdd(p.dker + (long)k * D + cc, s);
+        else if (p.dbias) atomicAdd(p.dbias + cc, s);
+    }
+}
+
+/* ------------------------------------------------------------------ */
+/* generic ND                                                          */
+/* ------------------------------------------------------------------ */
+
+__device__ __forceinline__ void unravel(const ConvDev &p, long lin, long *co) {
+#pragma unroll
+    for (int a = 0; a < kMaxNd; ++a)
+        if (a < p.nd) co[a] = (lin / p.strides[a]) % p.dims[a];
+}
+
+/* Offset of the tap kl neighbour of `co` in direction sgn (-1: causal
+ * source for forward / dkernel, +1: output for the dinput gather), or -1. */
+__device__ __forceinline__ long tap_neighbor(const ConvDev &p, const long *co, long kl, int sgn) {
+    long off = 0;
+    for (int a = p.nd - 1; a >= 0; --a) {
+        const long ka = kl % p.K;
+        kl /= p.K;
+        const long v = co[a] + sgn * (p.K - 1 - ka);
+        if (v < 0 || v >= p.dims[a]) return -1;
+        off += v * p.strides[a];
+    }
+    return off;
+}
+
+__global__ void k_convnd_fwd_generic(ConvDev p) {
+    const long total = p.batch * p.P * p.D;
+    for (long e = (long)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+         e += (long)gridDim.x * blockDim.x) {
+        const long d = e % p.D;
+        const long pt = (e / p.D) % p.P;
+        const long b = e / (p.D * p.P);
+        long co[kMaxNd];
+        unravel(p, pt, co);
+        const float *ib = p.in + b * p.P * p.D;
+        float s = p.bias ? p.bias[d] : 0.f;
+        for (long kl = 0; kl < p.KV; ++kl) {
+            const long src = tap_neighbor(p, co, kl, -1);
+            if (src >= 0) s = fmaf(ib[src * p.D + d], p.ker[kl * p.D + d], s);
+        }
+        p.out[e] = s;
+    }
+}
+
+__global__ void k_convnd_bwd_input_generic(ConvDev p) {
+    const long total = p.batch * p.P * p.D;
+    for (long e = (long)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+         e += (long)gridDim.x * blockDim.x) {
+        const long d = e % p.D;
+        const long pt = (e / p.D) % p.P;
+        const long b = e / (p.D * p.P);
+        long co[kMaxNd];
+        unravel(p, pt, co);
+        const float *gb = p.dy + b * p.P * p.D;
+        float s = 0.f;
+        for (long kl = 0; kl < p.KV; ++kl) {
+            const long o = tap_neighbor(p, co, kl, +1);
+            if (o >= 0) s = fmaf(gb[o * p.D + d], p.ker[kl * p.D + d], s);
+        }
+        p.din[e] = s;
+    }
+}
+
+/* blockIdx.y = channel d, blockIdx.z = tap kl (KV) or KV for dbias;
+ * blockIdx.x strides over the batch x points. */
+__global__ void __launch_bounds__(256) k_convnd_bwd_param_generic(ConvDev p) {
+    __shared__ float wsum[8];
+    const long d = blockIdx.y;
+    const long kl = blockIdx.z;
+    const long total = p.batch * p.P;
+    float s = 0.f;
+    for (long e = (long)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+         e += (long)gridDim.x * blockDim.x) {
+        const long pt = e % p.P;
+        const long b = e / p.P;
+        const float gy = p.dy[(b * p.P + pt) * p.D + d];
+        if (kl == p.KV) {
+            s += gy;
+        } else {
+            long co[kMaxNd];
+            unravel(p, pt, co);
+            const long src = tap_neighbor(p, co, kl, -1);
+            if (src >= 0) s = fmaf(gy, p.in[(b * p.P + src) * p.D + d], s);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) wsum[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += wsum[w];
+        if (kl == p.KV) {
+            if (p.dbias) atomicAdd(p.dbias + d, t);
+        } else {
+            atomicAdd(p.dker + kl * p.D + d, t);
+        }
+    }
+}
+
+/* ------------------------------------------------------------------ */
+/* launch                                                              */
+/* ------------------------------------------------------------------ */
+
+bool make_dev(const KmbConvND *a, ConvDev *p) {
+    memset(p, 0, sizeof *p);
+    p->in = a->input; p->ker = a->kernel; p->bias = a->bias; p->dy = a->dy;
+    p->out = a->output; p->din = a->dinput; p->dker = a->dkernel; p->dbias = a->dbias;
+    p->batch = a->batch; p->D = a->D; p->K = a->K; p->nd = (int)a->ndims;
+    long s = 1;
+    for (int ax = p->nd - 1; ax >= 0; --ax) {
+        p->dims[ax] = a->dims[ax];
+        p->strides[ax] = s;
+        s *= a->dims[ax];
+    }
+    p->P = s;
+    long kv = 1;
+    for (int ax = 0; ax < p->nd; ++ax) kv *= a->K;
+    p->KV = kv;
+    return true;
+}
+
+Geo2d geo2d(const ConvDev &p, int cw, int ti) {
+    Geo2d g;
+    const long groups = (p.D + cw - 1) / cw;
+    g.cgt = (int)(groups < 16 ? groups : 16);
+    g.tj = kThreads2d / g.cgt;
+    g.ti = ti;
+    g.ctiles = (groups + g.cgt - 1) / g.cgt;
+    g.jtiles = (p.dims[1] + g.tj - 1) / g.tj;
+    g.strips = (p.dims[0] + ti - 1) / ti;
+    return g;
+}
+
+template <int K, int CW>
+cudaError_t launch2d(const ConvDev &p, bool bwd, cudaStream_t s) {
+    const Geo2d g = geo2d(p, CW, bwd ? 64 : 32);
+    dim3 grid((unsigned)(g.ctiles * g.jtiles), (unsigned)g.strips, (unsigned)p.batch);
+    if (!bwd) {
+        k_conv2d_fwd<K, CW><<<grid, kThreads2d, 0, s>>>(p, g);
+    } else {
+        const size_t smem = sizeof(float) * kThreads2d * (K * K + 1) * CW;
+        auto kern = k_conv2d_bwd<K, CW>;
+        if (smem > 48 * 1024) {
+            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)smem);
+            if (e != cudaSuccess) return e;
+        }
+        kern<<<grid, kThreads2d, smem, s>>>(p, g);
+    }
+    return cudaGetLastError();
+}
+
+template <int CW>
+cudaError_t dispatch2d(const ConvDev &p, bool bwd, cudaStream_t s) {
+    switch (p.K) {
+    case 1: return launch2d<1, CW>(p, bwd, s);
+    case 2: return launch2d<2, CW>(p, bwd, s);
+    case 3: return launch2d<3, CW>(p, bwd, s);
+    case 4: return launch2d<4, CW>(p, bwd, s);
+    case 5: return launch2d<5, CW>(p, bwd, s);
+    default: return cudaErrorNotSupported;
+    }
+}
+
+bool use_2d(const ConvDev &p) { return p.nd == 2 && p.K >= 1 && p.K <= 5; }
+
+bool aligned4(const KmbConvND *a, bool bwd) {
+    auto al = [](const void *q) { return q == nullptr || ((uintptr_t)q & 15u) == 0; };
+    if (a->D % 4) return false;
+    if (!al(a->input) || !al(a->kernel) || !al(a->bias)) return false;
+    if (!bwd) return al(a->output);
+    return al(a->dy) && al(a->dinput);
+}
+
+unsigned grid_for(long total, int threads) {
+    long blocks = (total + threads - 1) / threads;
+    if (blocks > 148L * 64) blocks = 148L * 64;
+    if (blocks < 1) blocks = 1;
+    return (unsigned)blocks;
+}
+
+} // namespace
+
+extern "C" int kmb_launch_convnd_fwd(const KmbConvND *a, cudaStream_t s) {
+    ConvDev p;
+    make_dev(a, &p);
+    cudaError_t e;
+    if (use_2d(p)) {
+        e = aligned4(a, false) ? dispatch2d<4>(p, false, s) : dispatch2d<1>(p, false, s);
+    } else {
+        k_convnd_fwd_generic<<<grid_for(p.batch * p.P * p.D, 256), 256, 0, s>>>(p);
+        e = cudaGetLastError();
+    }
+    if (e != cudaSuccess) return kmb_cuda_fail(e, "convnd forward launch");
+    return KMB_OK;
+}
+
+extern "C" int kmb_launch_convnd_bwd(const KmbConvND *a, cudaStream_t s) {
+    ConvDev p;
+    make_dev(a, &p);
+    cudaError_t e = cudaMemsetAsync(a->dkernel, 0, sizeof(float) * p.KV * p.D, s);
+    if (e == cudaSuccess && a->dbias) e = cudaMemsetAsync(a->dbias, 0, sizeof(float) * p.D, s);
+    if (e != cudaSuccess) return kmb_cuda_fail(e, "convnd backward memset");
+    if (use_2d(p)) {
+        e = aligned4(a, true) ? dispatch2d<4>(p, true, s) : dispatch2d<1>(p, true, s);
+    } else {
+        k_convnd_bwd_input_generic<<<grid_for(p.batch * p.P * p.D, 256), 256, 0, s>>>(p);
+        e = cudaGetLastError();
+        if (e == cudaSuccess) {
+            long per = p.batch * p.P;
+            unsigned bx = (unsigned)((per + 255) / 256);
+            if (bx > 64) bx = 64;
+            dim3 grid(bx, (unsigned)p.D, (unsigned)(p.KV + 1));
+            k_convnd_bwd_param_generic<<<grid, 256, 0, s>>>(p);
+            e = cudaGetLastError();
+        }
+    }
+    if (e != cudaSuccess) return kmb_cuda_fail(e, "convnd backward launch");
+    return KMB_OK;
+}

@@ -7,34 +7,39 @@
  * Backward = the reverse adjoint of cpu/scan1d_backward.c:248-295.
  *
  * Work decomposition.  The recurrence is sequential in t and independent
- * per (batch, channel, state): every (b, d) owns P lanes, every lane owns
- * G = 4 consecutive states, so one lane runs 4 independent chains over the
- * whole sequence.  A CTA of 128 threads covers DT = 128/P channels of one
- * batch item.  Per step and state the work is one MUFU ex2 plus four FMA-
- * pipe operations; exp(dt*A) is fused (A is pre-scaled by log2 e) and no
- * [L,D,N] temporary ever reaches memory unless the caller asks for h_all.
+ * per (batch, channel, state): every (b, d) owns P lanes and every lane
+ * owns G = 4 consecutive states, i.e. 4 independent chains over the whole
+ * sequence.  A CTA of 128 threads covers DT = 128/P channels of one batch
+ * item.  Per step and state the forward costs one MUFU ex2 plus four
+ * FMA-pipe operations: exp(dt*A) is fused (A is pre-scaled by log2 e) and
+ * no [L,D,N] temporary reaches memory unless the caller asks for h_all.
  *
- * Inputs are staged through shared memory with a 3-stage cp.async
- * pipeline (x, dt as [TT][DT] tiles, B, C as [TT][N] rows when they are
- * shared across channels).  y is reduced across the P lanes of a channel
- * with xor shuffles.
+ * Inputs are staged through shared memory by a 3-stage cp.async pipeline
+ * (x, dt as [TT][DT] tiles; B, C as [TT][N] rows when shared across
+ * channels).  Full tiles run fully unrolled: every P steps the P lanes of
+ * a channel fold their partial y values with a reduce-scatter (P-1
+ * shuffles for P outputs), the result goes to a shared [TT][DT] tile that
+ * is written to global memory with coalesced 128-bit stores.
  *
  * The backward walks the sequence in reverse in chunks of
- * KMB_SCAN1D_CHUNK steps.  For each chunk it re-runs the forward from the
- * checkpoint the forward stored at the chunk start (or reads h from h_all),
- * keeps the chunk's states in registers, and sweeps the chunk backwards
- * carrying the adjoint g = dL/dh.  When B and C are shared across channels
- * dB/dC are sums over channels: a shuffle reduce-scatter folds the warp's
- * channels, shared memory folds the CTA's warps and one atomic per
- * (step, state, CTA) folds the CTAs.
+ * KMB_SCAN1D_CHUNK steps.  Each chunk re-runs the forward from the state
+ * the forward checkpointed at the chunk start (or reads h from h_all),
+ * keeps the chunk's states in registers and sweeps it backwards carrying
+ * the adjoint g = dL/dh.  With q = (g + dy C) a and qh = q h_{t-1}:
+ *   dA += dt qh,  ddt = sum_n A qh + x sum_n (g + dy C) B,
+ *   dx = dt sum_n (g + dy C) B,  dB = (g + dy C) dt x,  dC = dy h.
+ * dx / ddt fold across the P lanes with a batched reduce-scatter; when
+ * B and C are shared across channels dB / dC are channel sums: a shuffle
+ * reduce-scatter folds the warp's channels, shared memory folds the CTA's
+ * warps and one 128-bit atomic per (step, 4 states, CTA) folds the CTAs.
  */
 #include "kmb_common.cuh"
 #include "../kmb_internal.h"
 
 namespace {
 
-constexpr int kNT = 128;      /* threads per CTA */
-constexpr int kG = 4;         /* states per lane */
+constexpr int kNT = 128;   /* threads per CTA */
+constexpr int kG = 4;      /* states per lane */
 constexpr int kChunk = KMB_SCAN1D_CHUNK;
 constexpr unsigned kFull = 0xffffffffu;
 
@@ -45,9 +50,8 @@ struct Scan1DDev {
     float *dx, *ddt, *dA, *dB, *dC;
     const float *ckpt_in;
     long L, D, N, nslots;
-    int clamp;
-    int vec_xd;
-    int vec_bc;
+    int vec_xd;   /* x / dt / dy / y rows can use 16-byte accesses */
+    int vec_bc;   /* B / C rows can use 16-byte accesses */
 };
 
 __device__ __forceinline__ float clamp1000(float v) {
@@ -55,50 +59,69 @@ __device__ __forceinline__ float clamp1000(float v) {
     return fmaxf(fminf(v, 1000.f), -1000.f);
 }
 
-/* Loads the G state-values of row `row` for lane group g (zero past N). */
 template <bool VEC>
-__device__ __forceinline__ void load_states(const float *row, int g, int N,
-                                            float (&v)[kG]) {
+__device__ __forceinline__ void lds4(const float *row, bool gok, int N, int n0,
+                                     float (&v)[kG]) {
     if (VEC) {
-        if (g * kG < N) {
-            float4 t = *reinterpret_cast<const float4 *>(row);
+        if (gok) {
+            const float4 t = *reinterpret_cast<const float4 *>(row);
             v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
         } else {
             v[0] = v[1] = v[2] = v[3] = 0.f;
         }
     } else {
 #pragma unroll
-        for (int j = 0; j < kG; ++j) v[j] = (g * kG + j < N) ? row[j] : 0.f;
+        for (int j = 0; j < kG; ++j) v[j] = (n0 + j < N) ? row[j] : 0.f;
     }
 }
 
 template <bool VEC>
-__device__ __forceinline__ void store_states(float *dst, int g, int N,
-                                             const float (&v)[kG]) {
+__device__ __forceinline__ void stg4(float *dst, bool gok, int N, int n0, const float (&v)[kG]) {
     if (VEC) {
-        if (g * kG < N)
-            *reinterpret_cast<float4 *>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+        if (gok) *reinterpret_cast<float4 *>(dst) = make_float4(v[0], v[1], v[2], v[3]);
     } else {
 #pragma unroll
         for (int j = 0; j < kG; ++j)
-            if (g * kG + j < N) dst[j] = v[j];
+            if (n0 + j < N) dst[j] = v[j];
     }
 }
 
 template <bool VEC>
-__device__ __forceinline__ void load_states_g(const float *src, int g, int N,
-                                              float (&v)[kG]) {
+__device__ __forceinline__ void ldg4(const float *src, bool gok, int N, int n0, float (&v)[kG]) {
     if (VEC) {
-        if (g * kG < N) {
-            float4 t = __ldg(reinterpret_cast<const float4 *>(src));
+        if (gok) {
+            const float4 t = __ldg(reinterpret_cast<const float4 *>(src));
             v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
         } else {
             v[0] = v[1] = v[2] = v[3] = 0.f;
         }
     } else {
 #pragma unroll
-        for (int j = 0; j < kG; ++j) v[j] = (g * kG + j < N) ? __ldg(src + j) : 0.f;
+        for (int j = 0; j < kG; ++j) v[j] = (n0 + j < N) ? __ldg(src + j) : 0.f;
     }
+}
+
+/* Reduce-scatter of P values across P consecutive lanes: on return lane
+ * (lane % P) holds the group sum of value index (lane % P).  P - 1
+ * shuffles in total. */
+template <int P>
+__device__ __forceinline__ float rs_sum(float (&v)[P], int lane) {
+#pragma unroll
+    for (int h = P / 2; h > 0; h >>= 1) {
+        const bool up = (lane & h) != 0;
+#pragma unroll
+        for (int k = 0; k < h; ++k) {
+            const float send = up ? v[k] : v[k + h];
+            const float keep = up ? v[k + h] : v[k];
+            v[k] = keep + __shfl_xor_sync(kFull, send, h);
+        }
+    }
+    return v[0];
+}
+
+__host__ __device__ inline int bc_row_stride(bool shared, int dt_ch, int N) {
+    /* shared-memory floats per step row of B (or C), padded to 16 bytes */
+    return shared ? ((N + 3) & ~3) : ((dt_ch * N + 3) & ~3);
 }
 
 /* ------------------------------------------------------------------ */
@@ -108,54 +131,57 @@ __device__ __forceinline__ void load_states_g(const float *src, int g, int N,
 template <int P, bool SHARED>
 struct FwdCfg {
     static constexpr int DT = kNT / P;
-    static constexpr int TT = SHARED ? 32 : 8;
+    static constexpr int TT = SHARED ? 32 : 16;
     static constexpr int ST = 3;
 };
 
-__host__ __device__ inline int bc_row_stride(bool shared, int dt_ch, int N) {
-    /* shared-memory floats per step row of B (or C), padded to 16 bytes */
-    return shared ? ((N + 3) & ~3) : ((dt_ch * N + 3) & ~3);
-}
-
-template <int P, bool SHARED, bool VEC>
-__global__ void __launch_bounds__(kNT) k_scan1d_fwd(Scan1DDev p) {
+template <int P, bool SHARED, bool VEC, bool CLAMP>
+__global__ void __launch_bounds__(kNT, 3) k_scan1d_fwd(Scan1DDev p) {
     using Cfg = FwdCfg<P, SHARED>;
     constexpr int DT = Cfg::DT, TT = Cfg::TT, ST = Cfg::ST;
+    static_assert(TT % P == 0 && TT % kChunk == 0, "tile must hold whole groups");
     extern __shared__ __align__(16) float smem[];
 
     const int tid = threadIdx.x;
+    const int lane = tid & 31;
     const int g = tid % P;
     const int dl = tid / P;
+    const int n0 = g * kG;
     const long b = blockIdx.y;
     const long D = p.D, L = p.L;
     const int N = (int)p.N;
     const long d0 = (long)blockIdx.x * DT;
     const long d = d0 + dl;
     const bool dok = d < D;
+    const bool gok = n0 < N;
     const int dvalid = (int)min((long)DT, D - d0);
 
     const int BWr = bc_row_stride(SHARED, DT, N);
     const int xs_sz = TT * DT;
     const int bs_sz = TT * BWr;
-    const int stage_sz = 2 * xs_sz + 2 * bs_sz;
+    const int stage_sz = 3 * xs_sz + 2 * bs_sz; /* x, dt, y, B, C */
 
     float A2[kG], h[kG];
 #pragma unroll
     for (int j = 0; j < kG; ++j) {
-        const int n = g * kG + j;
-        const bool ok = dok && n < N;
-        A2[j] = ok ? __ldg(p.A + d * N + n) * KMB_LOG2E : 0.f;
-        h[j] = (ok && p.h0) ? p.h0[(b * D + d) * N + n] : 0.f;
+        const bool ok = dok && n0 + j < N;
+        A2[j] = ok ? __ldg(p.A + d * N + n0 + j) * KMB_LOG2E : 0.f;
+        h[j] = (ok && p.h0) ? p.h0[(b * D + d) * N + n0 + j] : 0.f;
     }
 
-    const float *xg = p.x + b * L * D + d0;
-    const float *dg = p.dt + b * L * D + d0;
+    const long xoff = b * L * D + d0;
+    const float *xg = p.x + xoff;
+    const float *dg = p.dt + xoff;
     const long bld = SHARED ? (long)N : D * N;
-    const float *Bg = p.B + (SHARED ? b * L * N : (b * L * D + d0) * N);
-    const float *Cg = p.C + (SHARED ? b * L * N : (b * L * D + d0) * N);
+    const long boff = SHARED ? b * L * N : (b * L * D + d0) * N;
+    const float *Bg = p.B + boff;
+    const float *Cg = p.C + boff;
     const int bcols = SHARED ? N : DT * N;
     const int bvalid = SHARED ? N : dvalid * N;
     const bool vxd = p.vec_xd, vbc = p.vec_bc;
+    float *const hall = p.h_all ? p.h_all + (b * L * D + d) * N + n0 : nullptr;
+    float *const ckpt = p.ckpt ? p.ckpt + (b * p.nslots * D + d) * N + n0 : nullptr;
+    const long hstride = D * N; /* one step in h_all, one slot in ckpt */
 
     const int ntiles = (int)((L + TT - 1) / TT);
     auto load = [&](int k) {
@@ -164,10 +190,31 @@ __global__ void __launch_bounds__(kNT) k_scan1d_fwd(Scan1DDev p) {
         const int rv = (int)min((long)TT, L - t0);
         kmb_load_tile<kNT>(st, DT, xg + t0 * D, D, TT, DT, rv, dvalid, vxd, tid);
         kmb_load_tile<kNT>(st + xs_sz, DT, dg + t0 * D, D, TT, DT, rv, dvalid, vxd, tid);
-        kmb_load_tile<kNT>(st + 2 * xs_sz, BWr, Bg + t0 * bld, bld, TT, bcols, rv,
+        kmb_load_tile<kNT>(st + 3 * xs_sz, BWr, Bg + t0 * bld, bld, TT, bcols, rv, bvalid,
+                           vbc, tid);
+        kmb_load_tile<kNT>(st + 3 * xs_sz + bs_sz, BWr, Cg + t0 * bld, bld, TT, bcols, rv,
                            bvalid, vbc, tid);
-        kmb_load_tile<kNT>(st + 2 * xs_sz + bs_sz, BWr, Cg + t0 * bld, bld, TT,
-                           bcols, rv, bvalid, vbc, tid);
+    };
+    /* coalesced store of the y tile of tile k (rows rv, channels dvalid) */
+    auto flush_y = [&](int k) {
+        const float *ys = smem + (k % ST) * stage_sz + 2 * xs_sz;
+        const long t0 = (long)k * TT;
+        const int rv = (int)min((long)TT, L - t0);
+        float *yg = p.y + b * L * D + t0 * D + d0;
+        if (vxd) {
+            constexpr int C4 = DT / 4;
+            for (int e = tid; e < rv * C4; e += kNT) {
+                const int r = e / C4, c = (e - r * C4) * 4;
+                if (c < dvalid)
+                    *reinterpret_cast<float4 *>(yg + (long)r * D + c) =
+                        *reinterpret_cast<const float4 *>(ys + r * DT + c);
+            }
+        } else {
+            for (int e = tid; e < rv * DT; e += kNT) {
+                const int r = e / DT, c = e - r * DT;
+                if (c < dvalid) yg[(long)r * D + c] = ys[r * DT + c];
+            }
+        }
     };
 
 #pragma unroll
@@ -176,54 +223,81 @@ __global__ void __launch_bounds__(kNT) k_scan1d_fwd(Scan1DDev p) {
         kmb_cp_async_commit();
     }
 
-    const int boff = (SHARED ? 0 : dl * N) + g * kG;
-    const bool clampit = p.clamp != 0;
+    const int brow = (SHARED ? 0 : dl * N) + n0;
     for (int k = 0; k < ntiles; ++k) {
         kmb_cp_async_wait<ST - 2>();
         __syncthreads();
+        if (k > 0 && p.y) flush_y(k - 1);
         if (k + ST - 1 < ntiles) load(k + ST - 1);
         kmb_cp_async_commit();
 
         const float *st = smem + (k % ST) * stage_sz;
-        const float *xs = st;
-        const float *ds = st + xs_sz;
-        const float *bs = st + 2 * xs_sz;
+        const float *xs = st + dl;
+        const float *ds = st + xs_sz + dl;
+        float *ys = const_cast<float *>(st) + 2 * xs_sz + dl;
+        const float *bs = st + 3 * xs_sz + brow;
         const float *cs = bs + bs_sz;
         const long t0 = (long)k * TT;
         const int rv = (int)min((long)TT, L - t0);
 
-#pragma unroll 2
-        for (int i = 0; i < rv; ++i) {
-            const float xv = xs[i * DT + dl];
-            const float dv = ds[i * DT + dl];
-            const float u = dv * xv;
-            float bv[kG], cv[kG];
-            load_states<VEC>(bs + i * BWr + boff, g, N, bv);
-            load_states<VEC>(cs + i * BWr + boff, g, N, cv);
-            float yp = 0.f;
+        if (rv == TT) {
 #pragma unroll
-            for (int j = 0; j < kG; ++j) {
-                const float a = kmb_ex2(dv * A2[j]);
-                float hn = fmaf(a, h[j], bv[j] * u);
-                if (clampit) hn = clamp1000(hn);
-                h[j] = hn;
-                yp = fmaf(cv[j], hn, yp);
+            for (int i0 = 0; i0 < TT; i0 += P) {
+                float yq[P];
+#pragma unroll
+                for (int s = 0; s < P; ++s) {
+                    const int i = i0 + s;
+                    const float dv = ds[i * DT];
+                    const float u = dv * xs[i * DT];
+                    float bv[kG], cv[kG];
+                    lds4<VEC>(bs + i * BWr, gok, N, n0, bv);
+                    lds4<VEC>(cs + i * BWr, gok, N, n0, cv);
+                    float yp = 0.f;
+#pragma unroll
+                    for (int j = 0; j < kG; ++j) {
+                        const float a = kmb_ex2(dv * A2[j]);
+                        float hn = fmaf(a, h[j], bv[j] * u);
+                        if (CLAMP) hn = clamp1000(hn);
+                        h[j] = hn;
+                        yp = fmaf(cv[j], hn, yp);
+                    }
+                    yq[s] = yp;
+                    if (hall && dok) stg4<VEC>(hall + (t0 + i) * hstride, gok, N, n0, h);
+                    if ((i + 1) % kChunk == 0 && ckpt && dok)
+                        stg4<VEC>(ckpt + ((t0 + i) / kChunk) * hstride, gok, N, n0, h);
+                }
+                ys[(i0 + g) * DT] = rs_sum<P>(yq, lane);
             }
+        } else {
+            /* last, partial tile */
+            for (int i = 0; i < rv; ++i) {
+                const float dv = ds[i * DT];
+                const float u = dv * xs[i * DT];
+                float bv[kG], cv[kG];
+                lds4<VEC>(bs + i * BWr, gok, N, n0, bv);
+                lds4<VEC>(cs + i * BWr, gok, N, n0, cv);
+                float yp = 0.f;
 #pragma unroll
-            for (int o = P / 2; o > 0; o >>= 1) yp += __shfl_xor_sync(kFull, yp, o);
-
-            const long t = t0 + i;
-            if (dok) {
-                if (g == 0 && p.y) p.y[(b * L + t) * D + d] = yp;
-                if (p.h_all) store_states<VEC>(p.h_all + ((b * L + t) * D + d) * N + g * kG, g, N, h);
-                if (p.ckpt && ((t + 1) % kChunk) == 0)
-                    store_states<VEC>(p.ckpt + ((b * p.nslots + t / kChunk) * D + d) * N + g * kG,
-                                      g, N, h);
+                for (int j = 0; j < kG; ++j) {
+                    const float a = kmb_ex2(dv * A2[j]);
+                    float hn = fmaf(a, h[j], bv[j] * u);
+                    if (CLAMP) hn = clamp1000(hn);
+                    h[j] = hn;
+                    yp = fmaf(cv[j], hn, yp);
+                }
+#pragma unroll
+                for (int o = P / 2; o > 0; o >>= 1) yp += __shfl_xor_sync(kFull, yp, o);
+                if (g == 0) ys[i * DT] = yp;
+                if (hall && dok) stg4<VEC>(hall + (t0 + i) * hstride, gok, N, n0, h);
+                if ((i + 1) % kChunk == 0 && ckpt && dok)
+                    stg4<VEC>(ckpt + ((t0 + i) / kChunk) * hstride, gok, N, n0, h);
             }
         }
     }
     kmb_cp_async_wait<0>();
-    if (p.h_last && dok) store_states<VEC>(p.h_last + (b * D + d) * N + g * kG, g, N, h);
+    __syncthreads();
+    if (p.y) flush_y(ntiles - 1);
+    if (p.h_last && dok) stg4<VEC>(p.h_last + (b * D + d) * N + n0, gok, N, n0, h);
 }
 
 /* ------------------------------------------------------------------ */
@@ -264,12 +338,15 @@ __device__ __forceinline__ void reduce_scatter8(float (&v)[8], int lane, int &ba
     }
 }
 
-template <int P, bool SHARED, bool VEC, bool HALL>
-__global__ void __launch_bounds__(kNT) k_scan1d_bwd(Scan1DDev p) {
+template <int P, bool SHARED, bool VEC, bool HALL, bool CLAMP>
+__global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
     constexpr int DT = kNT / P;
     constexpr int T = kChunk;
     constexpr int NW = kNT / 32;
     constexpr int NP = kG * P;
+    constexpr int S = P >= 2 ? P / 2 : 1;   /* steps per dx/ddt reduce-scatter */
+    constexpr int NV = P >= 2 ? P : 2;      /* values per reduce-scatter */
+    static_assert(T % S == 0, "chunk must hold whole groups");
     extern __shared__ __align__(16) float smem[];
 
     const int tid = threadIdx.x;
@@ -277,12 +354,14 @@ __global__ void __launch_bounds__(kNT) k_scan1d_bwd(Scan1DDev p) {
     const int warp = tid >> 5;
     const int g = tid % P;
     const int dl = tid / P;
+    const int n0 = g * kG;
     const long b = blockIdx.y;
     const long D = p.D, L = p.L;
     const int N = (int)p.N;
     const long d0 = (long)blockIdx.x * DT;
     const long d = d0 + dl;
     const bool dok = d < D;
+    const bool gok = n0 < N;
     const int dvalid = (int)min((long)DT, D - d0);
 
     const int BWr = bc_row_stride(SHARED, DT, N);
@@ -294,23 +373,26 @@ __global__ void __launch_bounds__(kNT) k_scan1d_bwd(Scan1DDev p) {
     float A2[kG], Ar[kG], gc[kG], dAacc[kG];
 #pragma unroll
     for (int j = 0; j < kG; ++j) {
-        const int n = g * kG + j;
-        const bool ok = dok && n < N;
-        Ar[j] = ok ? __ldg(p.A + d * N + n) : 0.f;
+        const bool ok = dok && n0 + j < N;
+        Ar[j] = ok ? __ldg(p.A + d * N + n0 + j) : 0.f;
         A2[j] = Ar[j] * KMB_LOG2E;
         gc[j] = 0.f;
         dAacc[j] = 0.f;
     }
 
-    const float *xg = p.x + b * L * D + d0;
-    const float *dg = p.dt + b * L * D + d0;
-    const float *yg = p.dy + b * L * D + d0;
+    const long xoff = b * L * D + d0;
+    const float *xg = p.x + xoff;
+    const float *dg = p.dt + xoff;
+    const float *yg = p.dy + xoff;
     const long bld = SHARED ? (long)N : D * N;
-    const float *Bg = p.B + (SHARED ? b * L * N : (b * L * D + d0) * N);
-    const float *Cg = p.C + (SHARED ? b * L * N : (b * L * D + d0) * N);
+    const long boff = SHARED ? b * L * N : (b * L * D + d0) * N;
+    const float *Bg = p.B + boff;
+    const float *Cg = p.C + boff;
     const int bcols = SHARED ? N : DT * N;
     const int bvalid = SHARED ? N : dvalid * N;
     const bool vxd = p.vec_xd, vbc = p.vec_bc;
+    const long hstride = D * N;
+    const float *hall = HALL ? p.h_all + (b * L * D + d) * N + n0 : nullptr;
 
     const int nch = (int)((L + T - 1) / T);
     auto load = [&](int c, int stage) {
@@ -329,8 +411,9 @@ __global__ void __launch_bounds__(kNT) k_scan1d_bwd(Scan1DDev p) {
     load(nch - 1, 0);
     kmb_cp_async_commit();
 
-    const int boff = (SHARED ? 0 : dl * N) + g * kG;
-    const bool clampit = p.clamp != 0;
+    const int brow = (SHARED ? 0 : dl * N) + n0;
+    float *dxg = p.dx + b * L * D + d;
+    float *dtg = p.ddt + b * L * D + d;
 
     for (int c = nch - 1, it = 0; c >= 0; --c, ++it) {
         kmb_cp_async_wait<0>();
@@ -339,10 +422,10 @@ __global__ void __launch_bounds__(kNT) k_scan1d_bwd(Scan1DDev p) {
         kmb_cp_async_commit();
 
         const float *st = smem + (it & 1) * stage_sz;
-        const float *xs = st;
-        const float *ds = st + xs_sz;
-        const float *dys = st + 2 * xs_sz;
-        const float *bs = st + 3 * xs_sz;
+        const float *xs = st + dl;
+        const float *ds = st + xs_sz + dl;
+        const float *dys = st + 2 * xs_sz + dl;
+        const float *bs = st + 3 * xs_sz + brow;
         const float *cs = bs + bs_sz;
         const long t0 = (long)c * T;
         const int len = (int)min((long)T, L - t0);
@@ -350,35 +433,32 @@ __global__ void __launch_bounds__(kNT) k_scan1d_bwd(Scan1DDev p) {
         /* state before the chunk's first step */
         float hs[kG];
         if (c > 0) {
-            const float *src = HALL ? p.h_all + ((b * L + t0 - 1) * D + d) * N + g * kG
-                                    : p.ckpt_in + ((b * p.nslots + c - 1) * D + d) * N + g * kG;
-            if (dok) load_states_g<VEC>(src, g, N, hs);
+            const float *src = HALL ? hall + (t0 - 1) * hstride
+                                    : p.ckpt_in + ((b * p.nslots + c - 1) * D + d) * N + n0;
+            if (dok) ldg4<VEC>(src, gok, N, n0, hs);
             else hs[0] = hs[1] = hs[2] = hs[3] = 0.f;
         } else {
 #pragma unroll
-            for (int j = 0; j < kG; ++j) {
-                const int n = g * kG + j;
-                hs[j] = (dok && n < N && p.h0) ? p.h0[(b * D + d) * N + n] : 0.f;
-            }
+            for (int j = 0; j < kG; ++j)
+                hs[j] = (dok && n0 + j < N && p.h0) ? p.h0[(b * D + d) * N + n0 + j] : 0.f;
         }
 
-        /* forward recompute of the chunk's states (kept in registers) */
+        /* forward recompute of the chunk's states (registers) */
         float hr[HALL ? 1 : T][kG];
         if (!HALL) {
             float hh[kG] = {hs[0], hs[1], hs[2], hs[3]};
 #pragma unroll
             for (int i = 0; i < T; ++i) {
                 if (i < len) {
-                    const float xv = xs[i * DT + dl];
-                    const float dv = ds[i * DT + dl];
-                    const float u = dv * xv;
+                    const float dv = ds[i * DT];
+                    const float u = dv * xs[i * DT];
                     float bv[kG];
-                    load_states<VEC>(bs + i * BWr + boff, g, N, bv);
+                    lds4<VEC>(bs + i * BWr, gok, N, n0, bv);
 #pragma unroll
                     for (int j = 0; j < kG; ++j) {
                         const float a = kmb_ex2(dv * A2[j]);
                         float hn = fmaf(a, hh[j], bv[j] * u);
-                        if (clampit) hn = clamp1000(hn);
+                        if (CLAMP) hn = clamp1000(hn);
                         hh[j] = hn;
                         hr[i][j] = hn;
                     }
@@ -386,96 +466,124 @@ __global__ void __launch_bounds__(kNT) k_scan1d_bwd(Scan1DDev p) {
             }
         }
 
-        /* reverse sweep */
+        /* reverse sweep, S steps per dx/ddt reduce-scatter group */
 #pragma unroll
-        for (int i = T - 1; i >= 0; --i) {
-            if (i < len) {
-                const long t = t0 + i;
-                const float xv = xs[i * DT + dl];
-                const float dv = ds[i * DT + dl];
-                const float dyv = dys[i * DT + dl];
-                float bv[kG], cv[kG], hp[kG], ht[kG];
-                load_states<VEC>(bs + i * BWr + boff, g, N, bv);
-                load_states<VEC>(cs + i * BWr + boff, g, N, cv);
-                if (HALL) {
-                    if (dok) {
-                        load_states_g<VEC>(p.h_all + ((b * L + t) * D + d) * N + g * kG, g, N, ht);
-                        if (i > 0)
-                            load_states_g<VEC>(p.h_all + ((b * L + t - 1) * D + d) * N + g * kG,
-                                               g, N, hp);
-                        else
-                            for (int j = 0; j < kG; ++j) hp[j] = hs[j];
+        for (int i0 = T - 1; i0 >= 0; i0 -= S) {
+            float rv[NV];
+#pragma unroll
+            for (int s = 0; s < S; ++s) {
+                const int i = i0 - s;
+                rv[2 * s] = 0.f;
+                rv[2 * s + 1] = 0.f;
+                if (i < len) {
+                    const float xv = xs[i * DT];
+                    const float dv = ds[i * DT];
+                    const float dyv = dys[i * DT];
+                    const float u = dv * xv;
+                    float bv[kG], cv[kG], hp[kG], ht[kG];
+                    lds4<VEC>(bs + i * BWr, gok, N, n0, bv);
+                    lds4<VEC>(cs + i * BWr, gok, N, n0, cv);
+                    if (HALL) {
+                        if (dok) {
+                            ldg4<VEC>(hall + (t0 + i) * hstride, gok, N, n0, ht);
+                            if (i > 0) ldg4<VEC>(hall + (t0 + i - 1) * hstride, gok, N, n0, hp);
+                            else for (int j = 0; j < kG; ++j) hp[j] = hs[j];
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < kG; ++j) ht[j] = hp[j] = 0.f;
+                        }
                     } else {
 #pragma unroll
-                        for (int j = 0; j < kG; ++j) ht[j] = hp[j] = 0.f;
-                    }
-                } else {
-#pragma unroll
-                    for (int j = 0; j < kG; ++j) {
-                        ht[j] = hr[HALL ? 0 : i][j];
-                        hp[j] = (i > 0) ? hr[HALL ? 0 : (i > 0 ? i - 1 : 0)][j] : hs[j];
-                    }
-                }
-
-                float dxp = 0.f, ddtp = 0.f;
-                float v[8];
-#pragma unroll
-                for (int j = 0; j < kG; ++j) {
-                    const float a = kmb_ex2(dv * A2[j]);
-                    const float ah = fmaf(dyv, cv[j], gc[j]);
-                    const float gdt = ah * dv;
-                    v[j] = gdt * xv;          /* dB contribution */
-                    v[4 + j] = dyv * ht[j];   /* dC contribution */
-                    dAacc[j] = fmaf(gdt * a, hp[j], dAacc[j]);
-                    dxp = fmaf(gdt, bv[j], dxp);
-                    ddtp = fmaf(ah, fmaf(Ar[j] * a, hp[j], bv[j] * xv), ddtp);
-                    gc[j] = ah * a;
-                }
-#pragma unroll
-                for (int o = P / 2; o > 0; o >>= 1) {
-                    dxp += __shfl_xor_sync(kFull, dxp, o);
-                    ddtp += __shfl_xor_sync(kFull, ddtp, o);
-                }
-                if (dok && g == 0) {
-                    p.dx[(b * L + t) * D + d] = dxp;
-                    p.ddt[(b * L + t) * D + d] = ddtp;
-                }
-                if (SHARED) {
-                    int base, cnt, dup;
-                    reduce_scatter8<P>(v, lane, base, cnt, dup);
-                    if ((lane & dup) == 0) {
-                        float *prow = part + (i * NW + warp) * (2 * NP);
-#pragma unroll
-                        for (int k = 0; k < 8; ++k) {
-                            if (k < cnt) {
-                                const int idx = base + k;
-                                prow[(idx >> 2) * NP + g * kG + (idx & 3)] = v[k];
-                            }
+                        for (int j = 0; j < kG; ++j) {
+                            ht[j] = hr[HALL ? 0 : i][j];
+                            hp[j] = i > 0 ? hr[HALL ? 0 : (i > 0 ? i - 1 : 0)][j] : hs[j];
                         }
                     }
-                } else if (dok) {
-                    float vb[kG] = {v[0], v[1], v[2], v[3]};
-                    float vc[kG] = {v[4], v[5], v[6], v[7]};
-                    const long o = ((b * L + t) * D + d) * N + g * kG;
-                    store_states<VEC>(p.dB + o, g, N, vb);
-                    store_states<VEC>(p.dC + o, g, N, vc);
+                    float dxs = 0.f, dts = 0.f;
+                    float v[8];
+#pragma unroll
+                    for (int j = 0; j < kG; ++j) {
+                        const float a = kmb_ex2(dv * A2[j]);
+                        const float ah = fmaf(dyv, cv[j], gc[j]);
+                        const float q = ah * a;
+                        const float qh = q * hp[j];
+                        dAacc[j] = fmaf(dv, qh, dAacc[j]);
+                        dts = fmaf(Ar[j], qh, dts);
+                        dxs = fmaf(ah, bv[j], dxs);
+                        v[j] = ah * u;           /* dB contribution */
+                        v[4 + j] = dyv * ht[j];  /* dC contribution */
+                        gc[j] = q;
+                    }
+                    rv[2 * s] = dxs;
+                    rv[2 * s + 1] = fmaf(xv, dxs, dts);
+                    if (SHARED) {
+                        int base, cnt, dup;
+                        reduce_scatter8<P>(v, lane, base, cnt, dup);
+                        if ((lane & dup) == 0) {
+                            float *prow = part + (i * NW + warp) * (2 * NP);
+#pragma unroll
+                            for (int k = 0; k < 8; ++k) {
+                                if (k < cnt) {
+                                    const int idx = base + k;
+                                    prow[(idx >> 2) * NP + n0 + (idx & 3)] = v[k];
+                                }
+                            }
+                        }
+                    } else if (dok) {
+                        float vb[kG] = {v[0], v[1], v[2], v[3]};
+                        float vc[kG] = {v[4], v[5], v[6], v[7]};
+                        const long o = ((b * L + t0 + i) * D + d) * N + n0;
+                        stg4<VEC>(p.dB + o, gok, N, n0, vb);
+                        stg4<VEC>(p.dC + o, gok, N, n0, vc);
+                    }
+                }
+            }
+            /* fold dx / ddt over the P lanes of the channel */
+            if (P >= 2) {
+                const float r = rs_sum<NV>(rv, lane);
+                const int s = g >> 1;
+                const int i = i0 - s;
+                if (dok && i >= 0 && i < len) {
+                    const long t = t0 + i;
+                    if (g & 1) dtg[t * D] = r;
+                    else dxg[t * D] = r * ds[i * DT];
+                }
+            } else {
+                const int i = i0;
+                if (dok && i < len) {
+                    const long t = t0 + i;
+                    dxg[t * D] = rv[0] * ds[i * DT];
+                    dtg[t * D] = rv[1];
                 }
             }
         }
 
         if (SHARED) {
             __syncthreads();
-            const int tot = len * 2 * NP;
+            /* 4 consecutive states per thread: one 128-bit atomic each */
+            constexpr int Q = 2 * NP / 4;
+            const int tot = len * Q;
             for (int e = tid; e < tot; e += kNT) {
-                const int i = e / (2 * NP);
-                const int r = e - i * (2 * NP);
+                const int i = e / Q;
+                const int r = (e - i * Q) * 4;   /* index in [0, 2*NP) */
                 const int n = r % NP;
                 if (n < N) {
-                    float s = 0.f;
+                    float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                    for (int w = 0; w < NW; ++w) s += part[(i * NW + w) * (2 * NP) + r];
-                    float *dst = (r < NP) ? p.dB : p.dC;
-                    atomicAdd(dst + (b * L + t0 + i) * N + n, s);
+                    for (int w = 0; w < NW; ++w) {
+                        const float *src = part + (i * NW + w) * (2 * NP) + r;
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) s4[k] += src[k];
+                    }
+                    float *dst = ((r < NP) ? p.dB : p.dC) + (b * L + t0 + i) * N + n;
+                    if (VEC && vbc) {
+                        atomicAdd(reinterpret_cast<float4 *>(dst),
+                                  make_float4(s4[0], s4[1], s4[2], s4[3]));
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < 4; ++k)
+                            if (n + k < N) atomicAdd(dst + k, s4[k]);
+                    }
                 }
             }
         }
@@ -483,10 +591,8 @@ __global__ void __launch_bounds__(kNT) k_scan1d_bwd(Scan1DDev p) {
     kmb_cp_async_wait<0>();
 
 #pragma unroll
-    for (int j = 0; j < kG; ++j) {
-        const int n = g * kG + j;
-        if (dok && n < N) atomicAdd(p.dA + d * N + n, dAacc[j]);
-    }
+    for (int j = 0; j < kG; ++j)
+        if (dok && n0 + j < N) atomicAdd(p.dA + d * N + n0 + j, dAacc[j]);
 }
 
 /* M = 1 backward with per-channel A/B/C and a per-step delta shared by all
@@ -508,11 +614,11 @@ k_scan1d_bwd_m1_shared(const float *x, const float *A, const float *A_diag,
             const long td = t * D + d;
             const float dt = delta[t];
             const float xt = x[td];
-            const float g = dy[td];
+            const float gy = dy[td];
             const float da = A_diag ? A_diag[td] : kmb_ex2(dt * a * KMB_LOG2E);
             const float hprev = t > 0 ? h[(t - 1) * D + d] : (h0 ? h0[d] : 0.f);
-            const float ah = fmaf(g, cc, adj);
-            sC = fmaf(g, h[td], sC);
+            const float ah = fmaf(gy, cc, adj);
+            sC = fmaf(gy, h[td], sC);
             sB = fmaf(ah * dt, xt, sB);
             sA = fmaf(ah * dt * da, hprev, sA);
             dx[td] = ah * dt * bb;
@@ -545,19 +651,20 @@ Scan1DDev make_dev(const KmbScan1D *a) {
     p.ckpt_in = nullptr;
     p.L = a->L; p.D = a->D; p.N = a->N;
     p.nslots = (a->L + kChunk - 1) / kChunk;
-    p.clamp = a->clamp;
     auto al = [](const void *q) { return ((uintptr_t)q & 15u) == 0; };
-    p.vec_xd = (a->D % 4 == 0) && al(a->x) && al(a->dt) && (!a->dy || al(a->dy));
-    p.vec_bc = (a->N % 4 == 0) && al(a->B) && al(a->C);
+    p.vec_xd = (a->D % 4 == 0) && al(a->x) && al(a->dt) && (!a->dy || al(a->dy)) &&
+               (!a->y || al(a->y));
+    p.vec_bc = (a->N % 4 == 0) && al(a->B) && al(a->C) && (!a->dB || al(a->dB)) &&
+               (!a->dC || al(a->dC));
     return p;
 }
 
-template <int P, bool SHARED, bool VEC>
+template <int P, bool SHARED, bool VEC, bool CLAMP>
 cudaError_t launch_fwd_t(const Scan1DDev &p, long batch, cudaStream_t s) {
     using Cfg = FwdCfg<P, SHARED>;
     const int BWr = bc_row_stride(SHARED, Cfg::DT, (int)p.N);
-    const size_t smem = sizeof(float) * Cfg::ST * (2 * Cfg::TT * Cfg::DT + 2 * Cfg::TT * BWr);
-    auto kern = k_scan1d_fwd<P, SHARED, VEC>;
+    const size_t smem = sizeof(float) * Cfg::ST * (3 * Cfg::TT * Cfg::DT + 2 * Cfg::TT * BWr);
+    auto kern = k_scan1d_fwd<P, SHARED, VEC, CLAMP>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)smem);
@@ -568,13 +675,13 @@ cudaError_t launch_fwd_t(const Scan1DDev &p, long batch, cudaStream_t s) {
     return cudaGetLastError();
 }
 
-template <int P, bool SHARED, bool VEC, bool HALL>
+template <int P, bool SHARED, bool VEC, bool HALL, bool CLAMP>
 cudaError_t launch_bwd_t(const Scan1DDev &p, long batch, cudaStream_t s) {
     constexpr int DT = kNT / P;
     const int BWr = bc_row_stride(SHARED, DT, (int)p.N);
     size_t smem = sizeof(float) * 2 * (3 * kChunk * DT + 2 * kChunk * BWr);
     if (SHARED) smem += sizeof(float) * kChunk * (kNT / 32) * 2 * (kG * P);
-    auto kern = k_scan1d_bwd<P, SHARED, VEC, HALL>;
+    auto kern = k_scan1d_bwd<P, SHARED, VEC, HALL, CLAMP>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)smem);
@@ -585,27 +692,35 @@ cudaError_t launch_bwd_t(const Scan1DDev &p, long batch, cudaStream_t s) {
     return cudaGetLastError();
 }
 
+template <int P, bool SHARED>
+cudaError_t fwd_ps(const Scan1DDev &p, long batch, bool vec, bool clamp, cudaStream_t s) {
+    if (vec) return clamp ? launch_fwd_t<P, SHARED, true, true>(p, batch, s)
+                          : launch_fwd_t<P, SHARED, true, false>(p, batch, s);
+    return clamp ? launch_fwd_t<P, SHARED, false, true>(p, batch, s)
+                 : launch_fwd_t<P, SHARED, false, false>(p, batch, s);
+}
+
 template <int P>
-cudaError_t fwd_p(const Scan1DDev &p, long batch, bool shared, bool vec, cudaStream_t s) {
-    if (shared) return vec ? launch_fwd_t<P, true, true>(p, batch, s)
-                           : launch_fwd_t<P, true, false>(p, batch, s);
-    return vec ? launch_fwd_t<P, false, true>(p, batch, s)
-               : launch_fwd_t<P, false, false>(p, batch, s);
+cudaError_t fwd_p(const Scan1DDev &p, long batch, bool shared, bool vec, bool clamp,
+                  cudaStream_t s) {
+    return shared ? fwd_ps<P, true>(p, batch, vec, clamp, s)
+                  : fwd_ps<P, false>(p, batch, vec, clamp, s);
+}
+
+template <int P, bool SHARED, bool VEC>
+cudaError_t bwd_psv(const Scan1DDev &p, long batch, bool hall, bool clamp, cudaStream_t s) {
+    if (hall) return launch_bwd_t<P, SHARED, VEC, true, false>(p, batch, s);
+    return clamp ? launch_bwd_t<P, SHARED, VEC, false, true>(p, batch, s)
+                 : launch_bwd_t<P, SHARED, VEC, false, false>(p, batch, s);
 }
 
 template <int P>
 cudaError_t bwd_p(const Scan1DDev &p, long batch, bool shared, bool vec, bool hall,
-                  cudaStream_t s) {
-    if (shared) {
-        if (vec) return hall ? launch_bwd_t<P, true, true, true>(p, batch, s)
-                             : launch_bwd_t<P, true, true, false>(p, batch, s);
-        return hall ? launch_bwd_t<P, true, false, true>(p, batch, s)
-                    : launch_bwd_t<P, true, false, false>(p, batch, s);
-    }
-    if (vec) return hall ? launch_bwd_t<P, false, true, true>(p, batch, s)
-                         : launch_bwd_t<P, false, true, false>(p, batch, s);
-    return hall ? launch_bwd_t<P, false, false, true>(p, batch, s)
-                : launch_bwd_t<P, false, false, false>(p, batch, s);
+                  bool clamp, cudaStream_t s) {
+    if (shared) return vec ? bwd_psv<P, true, true>(p, batch, hall, clamp, s)
+                           : bwd_psv<P, true, false>(p, batch, hall, clamp, s);
+    return vec ? bwd_psv<P, false, true>(p, batch, hall, clamp, s)
+               : bwd_psv<P, false, false>(p, batch, hall, clamp, s);
 }
 
 } // namespace
@@ -614,14 +729,18 @@ extern "C" int kmb_launch_scan1d_fwd(const KmbScan1D *a, cudaStream_t s) {
     Scan1DDev p = make_dev(a);
     const bool vec = (a->N % 4) == 0;
     const bool shared = a->bc_shared != 0;
+    const bool clamp = a->clamp != 0;
+    const int P = pick_p(a->N);
     cudaError_t e;
-    switch (pick_p(a->N)) {
-    case 1: e = fwd_p<1>(p, a->batch, shared, vec, s); break;
-    case 2: e = fwd_p<2>(p, a->batch, shared, vec, s); break;
-    case 4: e = fwd_p<4>(p, a->batch, shared, vec, s); break;
-    case 8: e = fwd_p<8>(p, a->batch, shared, vec, s); break;
-    case 16: e = fwd_p<16>(p, a->batch, shared, vec, s); break;
-    case 32: e = fwd_p<32>(p, a->batch, shared, vec, s); break;
+    if (!shared && P > 16)
+        return kmb_fail(KMB_EUNSUPPORTED, "scan1d: per-channel B/C support N <= 64 (N=%ld)", a->N);
+    switch (P) {
+    case 1: e = fwd_p<1>(p, a->batch, shared, vec, clamp, s); break;
+    case 2: e = fwd_p<2>(p, a->batch, shared, vec, clamp, s); break;
+    case 4: e = fwd_p<4>(p, a->batch, shared, vec, clamp, s); break;
+    case 8: e = fwd_p<8>(p, a->batch, shared, vec, clamp, s); break;
+    case 16: e = fwd_p<16>(p, a->batch, shared, vec, clamp, s); break;
+    case 32: e = fwd_ps<32, true>(p, a->batch, vec, clamp, s); break;
     default: return kmb_fail(KMB_EUNSUPPORTED, "scan1d: N=%ld exceeds 128 states", a->N);
     }
     if (e != cudaSuccess) return kmb_cuda_fail(e, "scan1d forward launch");
@@ -635,6 +754,10 @@ extern "C" int kmb_launch_scan1d_bwd(const KmbScan1D *a, const float *ckpt_in,
     const bool vec = (a->N % 4) == 0;
     const bool shared = a->bc_shared != 0;
     const bool hall = a->h_all != nullptr;
+    const bool clamp = a->clamp != 0;
+    const int P = pick_p(a->N);
+    if (!shared && P > 16)
+        return kmb_fail(KMB_EUNSUPPORTED, "scan1d: per-channel B/C support N <= 64 (N=%ld)", a->N);
     cudaError_t e = cudaMemsetAsync(a->dA, 0, sizeof(float) * a->D * a->N, s);
     if (e == cudaSuccess && shared) {
         const size_t nb = sizeof(float) * a->batch * a->L * a->N;
@@ -642,13 +765,16 @@ extern "C" int kmb_launch_scan1d_bwd(const KmbScan1D *a, const float *ckpt_in,
         if (e == cudaSuccess) e = cudaMemsetAsync(a->dC, 0, nb, s);
     }
     if (e != cudaSuccess) return kmb_cuda_fail(e, "scan1d backward memset");
-    switch (pick_p(a->N)) {
-    case 1: e = bwd_p<1>(p, a->batch, shared, vec, hall, s); break;
-    case 2: e = bwd_p<2>(p, a->batch, shared, vec, hall, s); break;
-    case 4: e = bwd_p<4>(p, a->batch, shared, vec, hall, s); break;
-    case 8: e = bwd_p<8>(p, a->batch, shared, vec, hall, s); break;
-    case 16: e = bwd_p<16>(p, a->batch, shared, vec, hall, s); break;
-    case 32: e = bwd_p<32>(p, a->batch, shared, vec, hall, s); break;
+    switch (P) {
+    case 1: e = bwd_p<1>(p, a->batch, shared, vec, hall, clamp, s); break;
+    case 2: e = bwd_p<2>(p, a->batch, shared, vec, hall, clamp, s); break;
+    case 4: e = bwd_p<4>(p, a->batch, shared, vec, hall, clamp, s); break;
+    case 8: e = bwd_p<8>(p, a->batch, shared, vec, hall, clamp, s); break;
+    case 16: e = bwd_p<16>(p, a->batch, shared, vec, hall, clamp, s); break;
+    case 32:
+        e = vec ? bwd_psv<32, true, true>(p, a->batch, hall, clamp, s)
+                : bwd_psv<32, true, false>(p, a->batch, hall, clamp, s);
+        break;
     default: return kmb_fail(KMB_EUNSUPPORTED, "scan1d: N=%ld exceeds 128 states", a->N);
     }
     if (e != cudaSuccess) return kmb_cuda_fail(e, "scan1d backward launch");

