@@ -33,6 +33,8 @@
  * reduce-scatter folds the warp's channels, shared memory folds the CTA's
  * warps and one 128-bit atomic per (step, 4 states, CTA) folds the CTAs.
  */
+#include <type_traits>
+
 #include "kmb_common.cuh"
 #include "../kmb_internal.h"
 
@@ -119,9 +121,28 @@ __device__ __forceinline__ float rs_sum(float (&v)[P], int lane) {
     return v[0];
 }
 
-__host__ __device__ inline int bc_row_stride(bool shared, int dt_ch, int N) {
-    /* shared-memory floats per step row of B (or C), padded to 16 bytes */
-    return shared ? ((N + 3) & ~3) : ((dt_ch * N + 3) & ~3);
+__host__ __device__ inline int bc_row_stride(bool shared, int np, int N) {
+    /* Shared-memory floats per step row of channel-shared B (or C): at
+     * least the np = 4*P states the lanes cover, zero-filled past N, so
+     * every lane reads its 4 states with one unconditional 128-bit load.
+     * Per-channel B/C ([.., L, D, N]) are read straight from global memory:
+     * the lanes of a warp cover consecutive channels, so each step's rows
+     * are contiguous and the loads coalesce without staging. */
+    const int n4 = (N + 3) & ~3;
+    return shared ? (n4 > np ? n4 : np) : 0;
+}
+
+/* 4 consecutive states of a padded shared-memory row (16-byte aligned). */
+__device__ __forceinline__ void lds4u(const float *row, float (&v)[kG]) {
+    const float4 t = *reinterpret_cast<const float4 *>(row);
+    v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+}
+
+/* max(m, |h|) for the clamp detector: a state whose magnitude reaches the
+ * reference's 1000 bound (or any NaN, which the final state carries on)
+ * sends the tile through the exact clamping path again. */
+__device__ __forceinline__ bool clamp_hit(float hmax, const float (&h)[kG]) {
+    return !(hmax < 1000.f) || h[0] != h[0] || h[1] != h[1] || h[2] != h[2] || h[3] != h[3];
 }
 
 /* ------------------------------------------------------------------ */
@@ -156,7 +177,7 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_fwd(Scan1DDev p) {
     const bool gok = n0 < N;
     const int dvalid = (int)min((long)DT, D - d0);
 
-    const int BWr = bc_row_stride(SHARED, DT, N);
+    const int BWr = bc_row_stride(SHARED, kG * P, N);
     const int xs_sz = TT * DT;
     const int bs_sz = TT * BWr;
     const int stage_sz = 3 * xs_sz + 2 * bs_sz; /* x, dt, y, B, C */
@@ -176,7 +197,7 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_fwd(Scan1DDev p) {
     const long boff = SHARED ? b * L * N : (b * L * D + d0) * N;
     const float *Bg = p.B + boff;
     const float *Cg = p.C + boff;
-    const int bcols = SHARED ? N : DT * N;
+    const int bcols = SHARED ? BWr : DT * N; /* padded columns are zero-filled */
     const int bvalid = SHARED ? N : dvalid * N;
     const bool vxd = p.vec_xd, vbc = p.vec_bc;
     float *const hall = p.h_all ? p.h_all + (b * L * D + d) * N + n0 : nullptr;
@@ -190,10 +211,12 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_fwd(Scan1DDev p) {
         const int rv = (int)min((long)TT, L - t0);
         kmb_load_tile<kNT>(st, DT, xg + t0 * D, D, TT, DT, rv, dvalid, vxd, tid);
         kmb_load_tile<kNT>(st + xs_sz, DT, dg + t0 * D, D, TT, DT, rv, dvalid, vxd, tid);
-        kmb_load_tile<kNT>(st + 3 * xs_sz, BWr, Bg + t0 * bld, bld, TT, bcols, rv, bvalid,
-                           vbc, tid);
-        kmb_load_tile<kNT>(st + 3 * xs_sz + bs_sz, BWr, Cg + t0 * bld, bld, TT, bcols, rv,
-                           bvalid, vbc, tid);
+        if (SHARED) {
+            kmb_load_tile<kNT>(st + 3 * xs_sz, BWr, Bg + t0 * bld, bld, TT, bcols, rv, bvalid,
+                               vbc, tid);
+            kmb_load_tile<kNT>(st + 3 * xs_sz + bs_sz, BWr, Cg + t0 * bld, bld, TT, bcols, rv,
+                               bvalid, vbc, tid);
+        }
     };
     /* coalesced store of the y tile of tile k (rows rv, channels dvalid) */
     auto flush_y = [&](int k) {
@@ -223,7 +246,10 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_fwd(Scan1DDev p) {
         kmb_cp_async_commit();
     }
 
-    const int brow = (SHARED ? 0 : dl * N) + n0;
+    const int brow = n0;
+    /* per-channel B/C row of this lane at step 0 (SHARED == false) */
+    const float *bgl = SHARED ? nullptr : p.B + (b * L * D + d) * N + n0;
+    const float *cgl = SHARED ? nullptr : p.C + (b * L * D + d) * N + n0;
     for (int k = 0; k < ntiles; ++k) {
         kmb_cp_async_wait<ST - 2>();
         __syncthreads();
@@ -240,42 +266,19 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_fwd(Scan1DDev p) {
         const long t0 = (long)k * TT;
         const int rv = (int)min((long)TT, L - t0);
 
-        if (rv == TT) {
-#pragma unroll
-            for (int i0 = 0; i0 < TT; i0 += P) {
-                float yq[P];
-#pragma unroll
-                for (int s = 0; s < P; ++s) {
-                    const int i = i0 + s;
-                    const float dv = ds[i * DT];
-                    const float u = dv * xs[i * DT];
-                    float bv[kG], cv[kG];
-                    lds4<VEC>(bs + i * BWr, gok, N, n0, bv);
-                    lds4<VEC>(cs + i * BWr, gok, N, n0, cv);
-                    float yp = 0.f;
-#pragma unroll
-                    for (int j = 0; j < kG; ++j) {
-                        const float a = kmb_ex2(dv * A2[j]);
-                        float hn = fmaf(a, h[j], bv[j] * u);
-                        if (CLAMP) hn = clamp1000(hn);
-                        h[j] = hn;
-                        yp = fmaf(cv[j], hn, yp);
-                    }
-                    yq[s] = yp;
-                    if (hall && dok) stg4<VEC>(hall + (t0 + i) * hstride, gok, N, n0, h);
-                    if ((i + 1) % kChunk == 0 && ckpt && dok)
-                        stg4<VEC>(ckpt + ((t0 + i) / kChunk) * hstride, gok, N, n0, h);
-                }
-                ys[(i0 + g) * DT] = rs_sum<P>(yq, lane);
-            }
-        } else {
-            /* last, partial tile */
-            for (int i = 0; i < rv; ++i) {
+        /* exact path: partial last tile, or a tile the clamp detector flagged */
+        auto slow_tile = [&](int rows) {
+            for (int i = 0; i < rows; ++i) {
                 const float dv = ds[i * DT];
                 const float u = dv * xs[i * DT];
                 float bv[kG], cv[kG];
-                lds4<VEC>(bs + i * BWr, gok, N, n0, bv);
-                lds4<VEC>(cs + i * BWr, gok, N, n0, cv);
+                if (SHARED) {
+                    lds4u(bs + i * BWr, bv);
+                    lds4u(cs + i * BWr, cv);
+                } else {
+                    ldg4<VEC>(bgl + (t0 + i) * hstride, gok && dok, N, dok ? n0 : N, bv);
+                    ldg4<VEC>(cgl + (t0 + i) * hstride, gok && dok, N, dok ? n0 : N, cv);
+                }
                 float yp = 0.f;
 #pragma unroll
                 for (int j = 0; j < kG; ++j) {
@@ -289,9 +292,55 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_fwd(Scan1DDev p) {
                 for (int o = P / 2; o > 0; o >>= 1) yp += __shfl_xor_sync(kFull, yp, o);
                 if (g == 0) ys[i * DT] = yp;
                 if (hall && dok) stg4<VEC>(hall + (t0 + i) * hstride, gok, N, n0, h);
-                if ((i + 1) % kChunk == 0 && ckpt && dok)
+                if (((i + 1) & (kChunk - 1)) == 0 && ckpt && dok)
                     stg4<VEC>(ckpt + ((t0 + i) / kChunk) * hstride, gok, N, n0, h);
             }
+        };
+
+        if (rv == TT) {
+            /* fast path: no clamp on the critical path; the detector tracks
+             * max|h| and a flagged tile is replayed exactly from its start */
+            const float hst[kG] = {h[0], h[1], h[2], h[3]};
+            float hmax = 0.f;
+#pragma unroll
+            for (int i0 = 0; i0 < TT; i0 += P) {
+                float yq[P];
+#pragma unroll
+                for (int s = 0; s < P; ++s) {
+                    const int i = i0 + s;
+                    const float dv = ds[i * DT];
+                    const float u = dv * xs[i * DT];
+                    float bv[kG], cv[kG];
+                    if (SHARED) {
+                        lds4u(bs + i * BWr, bv);
+                        lds4u(cs + i * BWr, cv);
+                    } else {
+                        ldg4<VEC>(bgl + (t0 + i) * hstride, gok && dok, N, dok ? n0 : N, bv);
+                        ldg4<VEC>(cgl + (t0 + i) * hstride, gok && dok, N, dok ? n0 : N, cv);
+                    }
+                    float yp = 0.f;
+#pragma unroll
+                    for (int j = 0; j < kG; ++j) {
+                        const float a = kmb_ex2(dv * A2[j]);
+                        const float hn = fmaf(a, h[j], bv[j] * u);
+                        if (CLAMP) hmax = fmaxf(hmax, fabsf(hn));
+                        h[j] = hn;
+                        yp = fmaf(cv[j], hn, yp);
+                    }
+                    yq[s] = yp;
+                    if (hall && dok) stg4<VEC>(hall + (t0 + i) * hstride, gok, N, n0, h);
+                    if ((i + 1) % kChunk == 0 && ckpt && dok)
+                        stg4<VEC>(ckpt + ((t0 + i) / kChunk) * hstride, gok, N, n0, h);
+                }
+                ys[(i0 + g) * DT] = rs_sum<P>(yq, lane);
+            }
+            if (CLAMP && __any_sync(kFull, clamp_hit(hmax, h))) {
+#pragma unroll
+                for (int j = 0; j < kG; ++j) h[j] = hst[j];
+                slow_tile(TT);
+            }
+        } else {
+            slow_tile(rv);
         }
     }
     kmb_cp_async_wait<0>();
@@ -364,7 +413,7 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
     const bool gok = n0 < N;
     const int dvalid = (int)min((long)DT, D - d0);
 
-    const int BWr = bc_row_stride(SHARED, DT, N);
+    const int BWr = bc_row_stride(SHARED, NP, N);
     const int xs_sz = T * DT;
     const int bs_sz = T * BWr;
     const int stage_sz = 3 * xs_sz + 2 * bs_sz;
@@ -388,7 +437,7 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
     const long boff = SHARED ? b * L * N : (b * L * D + d0) * N;
     const float *Bg = p.B + boff;
     const float *Cg = p.C + boff;
-    const int bcols = SHARED ? N : DT * N;
+    const int bcols = SHARED ? BWr : DT * N; /* padded columns are zero-filled */
     const int bvalid = SHARED ? N : dvalid * N;
     const bool vxd = p.vec_xd, vbc = p.vec_bc;
     const long hstride = D * N;
@@ -402,16 +451,20 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
         kmb_load_tile<kNT>(st, DT, xg + t0 * D, D, T, DT, rv, dvalid, vxd, tid);
         kmb_load_tile<kNT>(st + xs_sz, DT, dg + t0 * D, D, T, DT, rv, dvalid, vxd, tid);
         kmb_load_tile<kNT>(st + 2 * xs_sz, DT, yg + t0 * D, D, T, DT, rv, dvalid, vxd, tid);
-        kmb_load_tile<kNT>(st + 3 * xs_sz, BWr, Bg + t0 * bld, bld, T, bcols, rv, bvalid,
-                           vbc, tid);
-        kmb_load_tile<kNT>(st + 3 * xs_sz + bs_sz, BWr, Cg + t0 * bld, bld, T, bcols, rv,
-                           bvalid, vbc, tid);
+        if (SHARED) {
+            kmb_load_tile<kNT>(st + 3 * xs_sz, BWr, Bg + t0 * bld, bld, T, bcols, rv, bvalid,
+                               vbc, tid);
+            kmb_load_tile<kNT>(st + 3 * xs_sz + bs_sz, BWr, Cg + t0 * bld, bld, T, bcols, rv,
+                               bvalid, vbc, tid);
+        }
     };
 
     load(nch - 1, 0);
     kmb_cp_async_commit();
 
-    const int brow = (SHARED ? 0 : dl * N) + n0;
+    const int brow = n0;
+    const float *bgl = SHARED ? nullptr : p.B + (b * L * D + d) * N + n0;
+    const float *cgl = SHARED ? nullptr : p.C + (b * L * D + d) * N + n0;
     float *dxg = p.dx + b * L * D + d;
     float *dtg = p.ddt + b * L * D + d;
 
@@ -443,27 +496,39 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
                 hs[j] = (dok && n0 + j < N && p.h0) ? p.h0[(b * D + d) * N + n0 + j] : 0.f;
         }
 
-        /* forward recompute of the chunk's states (registers) */
+        /* forward recompute of the chunk's states (registers).  Without the
+         * clamp on the critical path; when a state reaches the clamp bound
+         * (or NaN) the chunk is recomputed with the exact clamp, so the
+         * states match the forward's bit for bit either way. */
         float hr[HALL ? 1 : T][kG];
         if (!HALL) {
-            float hh[kG] = {hs[0], hs[1], hs[2], hs[3]};
+            auto recompute = [&](auto exact_tag) {
+                constexpr bool EXACT = decltype(exact_tag)::value;
+                float hh[kG] = {hs[0], hs[1], hs[2], hs[3]};
+                float hmax = 0.f;
 #pragma unroll
-            for (int i = 0; i < T; ++i) {
-                if (i < len) {
-                    const float dv = ds[i * DT];
-                    const float u = dv * xs[i * DT];
-                    float bv[kG];
-                    lds4<VEC>(bs + i * BWr, gok, N, n0, bv);
+                for (int i = 0; i < T; ++i) {
+                    if (i < len) {
+                        const float dv = ds[i * DT];
+                        const float u = dv * xs[i * DT];
+                        float bv[kG];
+                        if (SHARED) lds4u(bs + i * BWr, bv);
+                        else ldg4<VEC>(bgl + (t0 + i) * hstride, gok && dok, N, dok ? n0 : N, bv);
 #pragma unroll
-                    for (int j = 0; j < kG; ++j) {
-                        const float a = kmb_ex2(dv * A2[j]);
-                        float hn = fmaf(a, hh[j], bv[j] * u);
-                        if (CLAMP) hn = clamp1000(hn);
-                        hh[j] = hn;
-                        hr[i][j] = hn;
+                        for (int j = 0; j < kG; ++j) {
+                            const float a = kmb_ex2(dv * A2[j]);
+                            float hn = fmaf(a, hh[j], bv[j] * u);
+                            if (EXACT) hn = clamp1000(hn);
+                            else if (CLAMP) hmax = fmaxf(hmax, fabsf(hn));
+                            hh[j] = hn;
+                            hr[i][j] = hn;
+                        }
                     }
                 }
-            }
+                return CLAMP && !EXACT && clamp_hit(hmax, hh);
+            };
+            if (__any_sync(kFull, recompute(std::false_type{})))
+                recompute(std::true_type{});
         }
 
         /* reverse sweep, S steps per dx/ddt reduce-scatter group */
@@ -481,8 +546,13 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
                     const float dyv = dys[i * DT];
                     const float u = dv * xv;
                     float bv[kG], cv[kG], hp[kG], ht[kG];
-                    lds4<VEC>(bs + i * BWr, gok, N, n0, bv);
-                    lds4<VEC>(cs + i * BWr, gok, N, n0, cv);
+                    if (SHARED) {
+                        lds4u(bs + i * BWr, bv);
+                        lds4u(cs + i * BWr, cv);
+                    } else {
+                        ldg4<VEC>(bgl + (t0 + i) * hstride, gok && dok, N, dok ? n0 : N, bv);
+                        ldg4<VEC>(cgl + (t0 + i) * hstride, gok && dok, N, dok ? n0 : N, cv);
+                    }
                     if (HALL) {
                         if (dok) {
                             ldg4<VEC>(hall + (t0 + i) * hstride, gok, N, n0, ht);
@@ -662,7 +732,7 @@ Scan1DDev make_dev(const KmbScan1D *a) {
 template <int P, bool SHARED, bool VEC, bool CLAMP>
 cudaError_t launch_fwd_t(const Scan1DDev &p, long batch, cudaStream_t s) {
     using Cfg = FwdCfg<P, SHARED>;
-    const int BWr = bc_row_stride(SHARED, Cfg::DT, (int)p.N);
+    const int BWr = bc_row_stride(SHARED, kG * P, (int)p.N);
     const size_t smem = sizeof(float) * Cfg::ST * (3 * Cfg::TT * Cfg::DT + 2 * Cfg::TT * BWr);
     auto kern = k_scan1d_fwd<P, SHARED, VEC, CLAMP>;
     if (smem > 48 * 1024) {
@@ -678,7 +748,7 @@ cudaError_t launch_fwd_t(const Scan1DDev &p, long batch, cudaStream_t s) {
 template <int P, bool SHARED, bool VEC, bool HALL, bool CLAMP>
 cudaError_t launch_bwd_t(const Scan1DDev &p, long batch, cudaStream_t s) {
     constexpr int DT = kNT / P;
-    const int BWr = bc_row_stride(SHARED, DT, (int)p.N);
+    const int BWr = bc_row_stride(SHARED, kG * P, (int)p.N);
     size_t smem = sizeof(float) * 2 * (3 * kChunk * DT + 2 * kChunk * BWr);
     if (SHARED) smem += sizeof(float) * kChunk * (kNT / 32) * 2 * (kG * P);
     auto kern = k_scan1d_bwd<P, SHARED, VEC, HALL, CLAMP>;

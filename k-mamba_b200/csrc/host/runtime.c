@@ -37,6 +37,7 @@ int kmb_fail(int status, const char *fmt, ...) {
 }
 
 int kmb_cuda_fail(cudaError_t e, const char *where) {
+    (void)cudaGetLastError(); /* do not leave the error for the next caller */
     return kmb_fail(KMB_ECUDA, "%s: %s (%s)", where, cudaGetErrorString(e),
                     cudaGetErrorName(e));
 }
@@ -205,6 +206,9 @@ size_t kmb_pool_bytes_held(void) {
 /* ------------------------------------------------------------------ */
 
 void kmb_stage_begin(KmbStage *st) {
+    /* a call that passed validation starts with a clean error state, so
+     * kmb_last_status() always describes the latest call */
+    kmb_clear_error();
     memset(st, 0, sizeof *st);
     st->s = kmb_stream();
 }
