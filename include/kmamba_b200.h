@@ -100,6 +100,28 @@ long kmb_scan1d_ckpt_elems(long batch, long L, long D, long N);
 int kmb_scan1d_fwd(const KmbScan1D *args);
 int kmb_scan1d_bwd(const KmbScan1D *args);
 
+/*
+ * kmb_scan1d_bwd_noalloc -- no counterpart in the reference.
+ *
+ * The same backward as kmb_scan1d_bwd with h_all = ckpt = NULL, for
+ * callers that cannot allocate device memory while it runs: a host whose
+ * device memory is owned by another allocator (a framework's caching
+ * allocator that has reserved it, so cudaMalloc would fail or fragment
+ * its pool), a latency-bound loop that cannot absorb the device-wide
+ * synchronisation cudaMalloc / cudaFree may impose, or a plugin host that
+ * forbids allocations outside its own set-up phase.  It allocates nothing
+ * and stages nothing: every pointer must be device memory, h_all and ckpt
+ * must be NULL.  The forward checkpoints live in a static device array of
+ * KMB_NOALLOC_CKPT_ELEMS floats (8 MiB, held by every GPU that loads the
+ * library until exit); a call needing more -- batch * ceil(L /
+ * KMB_SCAN1D_CHUNK) * D * N floats -- is rejected with KMB_EUNSUPPORTED.
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress), so make it before any stream capture.  All
+ * calls share the array: calls that overlap on the GPU race on it.
+ */
+#define KMB_NOALLOC_CKPT_ELEMS (2L * 1024 * 1024)
+int kmb_scan1d_bwd_noalloc(const KmbScan1D *args);
+
 /* ------------------------------------------------------------------ */
 /* Batched causal depthwise ConvND                                     */
 /* ------------------------------------------------------------------ */
