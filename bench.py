@@ -254,6 +254,115 @@ def run_reference_arm(args):
 
 
 # --------------------------------------------------------------------------
+# secondary workloads (configs 3 and 4), single GPU, device-resident
+# --------------------------------------------------------------------------
+
+def run_secondary(args):
+    """Times one forward + backward of BASELINE config 3 (ConvND 512x512,
+    D 64, K 3, batch 16) or config 4 (2D scan 256x256, batch 8, D 256,
+    N 16, B/C shared, same dt on both axes) and prints one JSON line with
+    the per-kernel roofline.  Algorithmic bytes follow SURVEY 8(d)."""
+    import torch
+    import kmamba_b200 as kb
+    lib = kb.load()
+    stream = torch.cuda.current_stream()
+    lib.kmb_set_stream(C.c_void_p(stream.cuda_stream))
+    lib.kmb_set_sync(0)
+    f = np.float32
+    rng = np.random.default_rng(7)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=f)).cuda()  # noqa: E731
+    if args.workload == "conv3":
+        bsz, H, W, Dc, K = (args.batch if args.batch != BATCH else 16), 512, 512, 64, 3
+        Pn = H * W
+        E3 = bsz * Pn * Dc
+        fwd_b, bwd_b = 4 * (2 * E3 + 640), 4 * (3 * E3 + 1280)
+        inp = dev(rng.standard_normal((bsz, Pn, Dc), dtype=f))
+        ker = dev(rng.standard_normal((9, Dc), dtype=f) / 3)
+        bias = dev(rng.standard_normal((Dc,), dtype=f) * 0.1)
+        dy = dev(rng.standard_normal((bsz, Pn, Dc), dtype=f))
+        out, din = torch.empty_like(inp), torch.empty_like(inp)
+        dk, db = torch.empty_like(ker), torch.empty_like(bias)
+        a = kb.KmbConvND()
+        a.input, a.kernel, a.bias, a.output = (t.data_ptr() for t in (inp, ker, bias, out))
+        a.dy, a.dinput, a.dkernel, a.dbias = (t.data_ptr() for t in (dy, din, dk, db))
+        a.dims[0], a.dims[1] = H, W
+        a.ndims, a.batch, a.D, a.K = 2, bsz, Dc, K
+        fwd = lambda: kb.check(lib, lib.kmb_convnd_fwd(C.byref(a)))  # noqa: E731
+        bwd = lambda: kb.check(lib, lib.kmb_convnd_bwd(C.byref(a)))  # noqa: E731
+        names = ("k_conv2d_fwd", "k_conv2d_bwd")
+        workload = f"config3: ConvND 2D 512x512, D 64, K 3, batch {bsz}, fp32, fwd+bwd"
+        metric = "ConvND HBM GB/s (algorithmic bytes / device time)"
+    else:
+        bsz, H, W, Dc, Nn = (args.batch if args.batch != BATCH else 8), 256, 256, 256, 16
+        Pn = H * W
+        E4 = bsz * Pn * Dc
+        fwd_b = 4 * (3 * E4 + 2 * bsz * Pn * Nn + 2 * Dc * Nn)
+        bwd_b = 4 * (5 * E4 + 4 * bsz * Pn * Nn + 4 * Dc * Nn)
+        x = dev(rng.standard_normal((bsz, Pn, Dc), dtype=f))
+        dt1 = (np.log1p(np.exp(rng.standard_normal((bsz, 1, Pn, Dc), dtype=f) - 2)) +
+               np.log(2)).astype(f)
+        delta = dev(np.concatenate([dt1, dt1], axis=1))  # same dt on both axes
+        A = dev(-np.exp(rng.uniform(0, np.log(16), (2, Dc, Nn))))
+        B = dev(rng.standard_normal((bsz, Pn, Nn), dtype=f))
+        Cm = dev(rng.standard_normal((bsz, Pn, Nn), dtype=f))
+        dy = dev(rng.standard_normal((bsz, Pn, Dc), dtype=f))
+        h = torch.empty((bsz, Pn, Dc, Nn), device="cuda")
+        y, dx = torch.empty_like(x), torch.empty_like(x)
+        ddl, dA = torch.empty_like(delta), torch.empty_like(A)
+        dB, dC = torch.empty_like(B), torch.empty_like(Cm)
+
+        class KmbScanND(C.Structure):
+            _fields_ = [(n, C.c_void_p) for n in ("x", "delta", "A", "B", "C", "h", "y", "dy",
+                                                  "dx", "ddelta", "dA", "dB", "dC")] + [
+                ("dims", C.c_long * 8), ("ndims", C.c_long), ("batch", C.c_long),
+                ("D", C.c_long), ("M", C.c_long), ("bc_shared", C.c_int), ("flags", C.c_int)]
+        a = KmbScanND()
+        a.x, a.delta, a.A, a.B, a.C, a.h, a.y = (t.data_ptr() for t in (x, delta, A, B, Cm, h, y))
+        a.dy, a.dx, a.ddelta, a.dA, a.dB, a.dC = (t.data_ptr() for t in (dy, dx, ddl, dA, dB, dC))
+        a.dims[0], a.dims[1] = H, W
+        a.ndims, a.batch, a.D, a.M, a.bc_shared = 2, bsz, Dc, Nn, 1
+        lib.kmb_scannd_fwd.argtypes = [C.c_void_p]
+        lib.kmb_scannd_bwd.argtypes = [C.c_void_p]
+        fwd = lambda: kb.check(lib, lib.kmb_scannd_fwd(C.byref(a)))  # noqa: E731
+        bwd = lambda: kb.check(lib, lib.kmb_scannd_bwd(C.byref(a)))  # noqa: E731
+        names = ("k_scannd_fwd", "k_scannd_bwd")
+        workload = (f"config4: 2D selective scan 256x256, batch {bsz}, D 256, N 16, fp32, "
+                    "B/C shared, dt = softplus(N(0,1)-2) + ln 2 on both axes, fwd+bwd "
+                    "(stored-state kernels of the reference API)")
+        metric = "scan HBM GB/s (algorithmic bytes / device time), 2D selective scan fwd+bwd"
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+    for _ in range(args.warmup):
+        fwd()
+        bwd()
+    torch.cuda.synchronize()
+    marks = [[ev(), ev(), ev()] for _ in range(args.steps)]
+    with Clocks(0) as clk:
+        for m in marks:
+            m[0].record(stream)
+            fwd()
+            m[1].record(stream)
+            bwd()
+            m[2].record(stream)
+        torch.cuda.synchronize()
+    fms = sum(m[0].elapsed_time(m[1]) for m in marks) / args.steps
+    bms = sum(m[1].elapsed_time(m[2]) for m in marks) / args.steps
+    pk, pk_kind = peaks()
+    dom = (bms, bwd_b, names[1]) if bms >= fms else (fms, fwd_b, names[0])
+    ach = dom[1] / (dom[0] / 1e3) / 1e9
+    print(json.dumps({
+        "metric": metric, "value": (fwd_b + bwd_b) / ((fms + bms) / 1e3) / 1e9, "unit": "GB/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": fms + bms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": workload, "fwd_ms": fms, "bwd_ms": bms,
+                                        "fwd_GBps": fwd_b / fms / 1e6,
+                                        "bwd_GBps": bwd_b / bms / 1e6},
+        "roofline": {"bound": "hbm", "kernel": dom[2], "achieved": ach, "peak": pk["hbm_gbs"],
+                     "unit": "GB/s", "frac": ach / pk["hbm_gbs"],
+                     "peak_source": f"{pk_kind} hbm_gbs", "traffic": None},
+        "gpu_launches": 2 * args.steps, "clocks": clk.summary()}), flush=True)
+
+
+# --------------------------------------------------------------------------
 # GPU arm
 # --------------------------------------------------------------------------
 
@@ -267,10 +376,16 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="batch items per GPU (profiling of small cases only)")
+    ap.add_argument("--workload", default="scan1d", choices=["scan1d", "conv3", "scan2d4"],
+                    help="scan1d = BASELINE config 2 (the headline); conv3 / scan2d4 time "
+                         "configs 3 and 4 for their roofline evidence")
     args = ap.parse_args()
     set_batch(args.batch)
     if args.impl == "reference":
         run_reference_arm(args)
+        return
+    if args.workload != "scan1d":
+        run_secondary(args)
         return
 
     import torch

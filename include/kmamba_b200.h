@@ -69,6 +69,9 @@ size_t kmb_pool_bytes_held(void);
  * as B, C; summed over D when bc_shared).  Every gradient is overwritten.
  * The backward treats the clamp as the identity, like the reference.
  */
+/* Steps between two forward checkpoints (the backward's chunk length). */
+#define KMB_SCAN1D_CHUNK 8
+
 typedef struct {
     const float *x;
     const float *dt;

@@ -33,6 +33,8 @@
  * reduce-scatter folds the warp's channels, shared memory folds the CTA's
  * warps and one 128-bit atomic per (step, 4 states, CTA) folds the CTAs.
  */
+#include <stdlib.h>
+
 #include <type_traits>
 
 #include "kmb_common.cuh"
@@ -145,6 +147,62 @@ __device__ __forceinline__ bool clamp_hit(float hmax, const float (&h)[kG]) {
     return !(hmax < 1000.f) || h[0] != h[0] || h[1] != h[1] || h[2] != h[2] || h[3] != h[3];
 }
 
+/* G-state versions of the helpers above, for the forward kernel that runs
+ * with 2 or 4 states per lane. */
+template <int G>
+__device__ __forceinline__ void ldsv(const float *row, float (&v)[G]) {
+    if constexpr (G == 4) {
+        const float4 t = *reinterpret_cast<const float4 *>(row);
+        v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+    } else {
+        static_assert(G == 2, "2 or 4 states per lane");
+        const float2 t = *reinterpret_cast<const float2 *>(row);
+        v[0] = t.x; v[1] = t.y;
+    }
+}
+
+template <int G, bool VEC>
+__device__ __forceinline__ void ldgv(const float *src, bool gok, int N, int n0, float (&v)[G]) {
+    if constexpr (G == 4) {
+        ldg4<VEC>(src, gok, N, n0, v);
+    } else {
+        if (VEC) {
+            if (gok) {
+                const float2 t = __ldg(reinterpret_cast<const float2 *>(src));
+                v[0] = t.x; v[1] = t.y;
+            } else {
+                v[0] = v[1] = 0.f;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < G; ++j) v[j] = (n0 + j < N) ? __ldg(src + j) : 0.f;
+        }
+    }
+}
+
+template <int G, bool VEC>
+__device__ __forceinline__ void stgv(float *dst, bool gok, int N, int n0, const float (&v)[G]) {
+    if constexpr (G == 4) {
+        stg4<VEC>(dst, gok, N, n0, v);
+    } else {
+        if (VEC) {
+            if (gok) *reinterpret_cast<float2 *>(dst) = make_float2(v[0], v[1]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < G; ++j)
+                if (n0 + j < N) dst[j] = v[j];
+        }
+    }
+}
+
+template <int G>
+__device__ __forceinline__ bool clamp_hitv(float hmax, const float (&h)[G]) {
+    bool nan = false;
+#pragma unroll
+    for (int j = 0; j < G; ++j) nan |= h[j] != h[j];
+    return !(hmax < 1000.f) || nan;
+}
+
 /* ------------------------------------------------------------------ */
 /* forward                                                             */
 /* ------------------------------------------------------------------ */
@@ -156,7 +214,7 @@ struct FwdCfg {
     static constexpr int ST = 3;
 };
 
-template <int P, bool SHARED, bool VEC, bool CLAMP>
+template <int P, int G, bool SHARED, bool VEC, bool CLAMP>
 __global__ void __launch_bounds__(kNT, 3) k_scan1d_fwd(Scan1DDev p) {
     using Cfg = FwdCfg<P, SHARED>;
     constexpr int DT = Cfg::DT, TT = Cfg::TT, ST = Cfg::ST;
@@ -167,7 +225,7 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_fwd(Scan1DDev p) {
     const int lane = tid & 31;
     const int g = tid % P;
     const int dl = tid / P;
-    const int n0 = g * kG;
+    const int n0 = g * G;
     const long b = blockIdx.y;
     const long D = p.D, L = p.L;
     const int N = (int)p.N;
@@ -177,14 +235,14 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_fwd(Scan1DDev p) {
     const bool gok = n0 < N;
     const int dvalid = (int)min((long)DT, D - d0);
 
-    const int BWr = bc_row_stride(SHARED, kG * P, N);
+    const int BWr = bc_row_stride(SHARED, G * P, N);
     const int xs_sz = TT * DT;
     const int bs_sz = TT * BWr;
     const int stage_sz = 3 * xs_sz + 2 * bs_sz; /* x, dt, y, B, C */
 
-    float A2[kG], h[kG];
+    float A2[G], h[G];
 #pragma unroll
-    for (int j = 0; j < kG; ++j) {
+    for (int j = 0; j < G; ++j) {
         const bool ok = dok && n0 + j < N;
         A2[j] = ok ? __ldg(p.A + d * N + n0 + j) * KMB_LOG2E : 0.f;
         h[j] = (ok && p.h0) ? p.h0[(b * D + d) * N + n0 + j] : 0.f;
@@ -271,18 +329,18 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_fwd(Scan1DDev p) {
             for (int i = 0; i < rows; ++i) {
                 const float dv = ds[i * DT];
                 const float u = dv * xs[i * DT];
-                float bv[kG], cv[kG];
+                float bv[G], cv[G];
                 if (SHARED) {
-                    lds4u(bs + i * BWr, bv);
-                    lds4u(cs + i * BWr, cv);
+                    ldsv<G>(bs + i * BWr, bv);
+                    ldsv<G>(cs + i * BWr, cv);
                 } else {
-                    ldg4<VEC>(bgl + (t0 + i) * hstride, gok && dok, N, dok ? n0 : N, bv);
-                    ldg4<VEC>(cgl + (t0 + i) * hstride, gok && dok, N, dok ? n0 : N, cv);
+                    ldgv<G, VEC>(bgl + (t0 + i) * hstride, gok && dok, N, dok ? n0 : N, bv);
+                    ldgv<G, VEC>(cgl + (t0 + i) * hstride, gok && dok, N, dok ? n0 : N, cv);
                 }
                 float yp = 0.f;
 #pragma unroll
-                for (int j = 0; j < kG; ++j) {
-                    const float a = kmb_ex2(dv * A2[j]);
+                for (int j = 0; j < G; ++j) {
+                    const float a = kmb_exp2_decay(dv * A2[j]);
                     float hn = fmaf(a, h[j], bv[j] * u);
                     if (CLAMP) hn = clamp1000(hn);
                     h[j] = hn;
@@ -291,16 +349,20 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_fwd(Scan1DDev p) {
 #pragma unroll
                 for (int o = P / 2; o > 0; o >>= 1) yp += __shfl_xor_sync(kFull, yp, o);
                 if (g == 0) ys[i * DT] = yp;
-                if (hall && dok) stg4<VEC>(hall + (t0 + i) * hstride, gok, N, n0, h);
+                if (hall && dok) stgv<G, VEC>(hall + (t0 + i) * hstride, gok, N, n0, h);
                 if (((i + 1) & (kChunk - 1)) == 0 && ckpt && dok)
-                    stg4<VEC>(ckpt + ((t0 + i) / kChunk) * hstride, gok, N, n0, h);
+                    stgv<G, VEC>(ckpt + ((t0 + i) / kChunk) * hstride, gok, N, n0, h);
             }
         };
 
-        if (rv == TT) {
+        if (rv == TT && !hall) {
             /* fast path: no clamp on the critical path; the detector tracks
-             * max|h| and a flagged tile is replayed exactly from its start */
-            const float hst[kG] = {h[0], h[1], h[2], h[3]};
+             * max|h| and a flagged tile is replayed exactly from its start.
+             * Callers asking for the state history (h_all) take the exact
+             * per-step path below instead. */
+            float hst[G];
+#pragma unroll
+            for (int j = 0; j < G; ++j) hst[j] = h[j];
             float hmax = 0.f;
 #pragma unroll
             for (int i0 = 0; i0 < TT; i0 += P) {
@@ -310,33 +372,32 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_fwd(Scan1DDev p) {
                     const int i = i0 + s;
                     const float dv = ds[i * DT];
                     const float u = dv * xs[i * DT];
-                    float bv[kG], cv[kG];
+                    float bv[G], cv[G];
                     if (SHARED) {
-                        lds4u(bs + i * BWr, bv);
-                        lds4u(cs + i * BWr, cv);
+                        ldsv<G>(bs + i * BWr, bv);
+                        ldsv<G>(cs + i * BWr, cv);
                     } else {
-                        ldg4<VEC>(bgl + (t0 + i) * hstride, gok && dok, N, dok ? n0 : N, bv);
-                        ldg4<VEC>(cgl + (t0 + i) * hstride, gok && dok, N, dok ? n0 : N, cv);
+                        ldgv<G, VEC>(bgl + (t0 + i) * hstride, gok && dok, N, dok ? n0 : N, bv);
+                        ldgv<G, VEC>(cgl + (t0 + i) * hstride, gok && dok, N, dok ? n0 : N, cv);
                     }
                     float yp = 0.f;
 #pragma unroll
-                    for (int j = 0; j < kG; ++j) {
-                        const float a = kmb_ex2(dv * A2[j]);
+                    for (int j = 0; j < G; ++j) {
+                        const float a = kmb_exp2_decay(dv * A2[j]);
                         const float hn = fmaf(a, h[j], bv[j] * u);
                         if (CLAMP) hmax = fmaxf(hmax, fabsf(hn));
                         h[j] = hn;
                         yp = fmaf(cv[j], hn, yp);
                     }
                     yq[s] = yp;
-                    if (hall && dok) stg4<VEC>(hall + (t0 + i) * hstride, gok, N, n0, h);
                     if ((i + 1) % kChunk == 0 && ckpt && dok)
-                        stg4<VEC>(ckpt + ((t0 + i) / kChunk) * hstride, gok, N, n0, h);
+                        stgv<G, VEC>(ckpt + ((t0 + i) / kChunk) * hstride, gok, N, n0, h);
                 }
                 ys[(i0 + g) * DT] = rs_sum<P>(yq, lane);
             }
-            if (CLAMP && __any_sync(kFull, clamp_hit(hmax, h))) {
+            if (CLAMP && __any_sync(kFull, clamp_hitv<G>(hmax, h))) {
 #pragma unroll
-                for (int j = 0; j < kG; ++j) h[j] = hst[j];
+                for (int j = 0; j < G; ++j) h[j] = hst[j];
                 slow_tile(TT);
             }
         } else {
@@ -346,7 +407,7 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_fwd(Scan1DDev p) {
     kmb_cp_async_wait<0>();
     __syncthreads();
     if (p.y) flush_y(ntiles - 1);
-    if (p.h_last && dok) stg4<VEC>(p.h_last + (b * D + d) * N + n0, gok, N, n0, h);
+    if (p.h_last && dok) stgv<G, VEC>(p.h_last + (b * D + d) * N + n0, gok, N, n0, h);
 }
 
 /* ------------------------------------------------------------------ */
@@ -393,7 +454,9 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
     constexpr int T = kChunk;
     constexpr int NW = kNT / 32;
     constexpr int NP = kG * P;
-    constexpr int S = P >= 2 ? P / 2 : 1;   /* steps per dx/ddt reduce-scatter */
+    /* steps per dx/ddt reduce-scatter group (2 values per step, one value
+     * per lane of the channel; slots past 2*S are zero when P > 2*T) */
+    constexpr int S = P >= 2 ? (P / 2 < T ? P / 2 : T) : 1;
     constexpr int NV = P >= 2 ? P : 2;      /* values per reduce-scatter */
     static_assert(T % S == 0, "chunk must hold whole groups");
     extern __shared__ __align__(16) float smem[];
@@ -500,7 +563,8 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
          * clamp on the critical path; when a state reaches the clamp bound
          * (or NaN) the chunk is recomputed with the exact clamp, so the
          * states match the forward's bit for bit either way. */
-        float hr[HALL ? 1 : T][kG];
+        float hr[HALL ? 1 : T][kG]; /* states h_t of the chunk */
+        float ar[HALL ? 1 : T][kG]; /* decays a_t, reused by the reverse sweep */
         if (!HALL) {
             auto recompute = [&](auto exact_tag) {
                 constexpr bool EXACT = decltype(exact_tag)::value;
@@ -516,12 +580,13 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
                         else ldg4<VEC>(bgl + (t0 + i) * hstride, gok && dok, N, dok ? n0 : N, bv);
 #pragma unroll
                         for (int j = 0; j < kG; ++j) {
-                            const float a = kmb_ex2(dv * A2[j]);
+                            const float a = kmb_exp2_decay(dv * A2[j]);
                             float hn = fmaf(a, hh[j], bv[j] * u);
                             if (EXACT) hn = clamp1000(hn);
                             else if (CLAMP) hmax = fmaxf(hmax, fabsf(hn));
                             hh[j] = hn;
                             hr[i][j] = hn;
+                            ar[i][j] = a;
                         }
                     }
                 }
@@ -535,6 +600,8 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
 #pragma unroll
         for (int i0 = T - 1; i0 >= 0; i0 -= S) {
             float rv[NV];
+#pragma unroll
+            for (int k = 0; k < NV; ++k) rv[k] = 0.f;
 #pragma unroll
             for (int s = 0; s < S; ++s) {
                 const int i = i0 - s;
@@ -573,7 +640,7 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
                     float v[8];
 #pragma unroll
                     for (int j = 0; j < kG; ++j) {
-                        const float a = kmb_ex2(dv * A2[j]);
+                        const float a = HALL ? kmb_exp2_decay(dv * A2[j]) : ar[HALL ? 0 : i][j];
                         const float ah = fmaf(dyv, cv[j], gc[j]);
                         const float q = ah * a;
                         const float qh = q * hp[j];
@@ -613,7 +680,7 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
                 const float r = rs_sum<NV>(rv, lane);
                 const int s = g >> 1;
                 const int i = i0 - s;
-                if (dok && i >= 0 && i < len) {
+                if (dok && g < 2 * S && i >= 0 && i < len) {
                     const long t = t0 + i;
                     if (g & 1) dtg[t * D] = r;
                     else dxg[t * D] = r * ds[i * DT];
@@ -685,7 +752,7 @@ k_scan1d_bwd_m1_shared(const float *x, const float *A, const float *A_diag,
             const float dt = delta[t];
             const float xt = x[td];
             const float gy = dy[td];
-            const float da = A_diag ? A_diag[td] : kmb_ex2(dt * a * KMB_LOG2E);
+            const float da = A_diag ? A_diag[td] : kmb_exp2_decay(dt * a * KMB_LOG2E);
             const float hprev = t > 0 ? h[(t - 1) * D + d] : (h0 ? h0[d] : 0.f);
             const float ah = fmaf(gy, cc, adj);
             sC = fmaf(gy, h[td], sC);
@@ -729,12 +796,12 @@ Scan1DDev make_dev(const KmbScan1D *a) {
     return p;
 }
 
-template <int P, bool SHARED, bool VEC, bool CLAMP>
+template <int P, int G, bool SHARED, bool VEC, bool CLAMP>
 cudaError_t launch_fwd_t(const Scan1DDev &p, long batch, cudaStream_t s) {
     using Cfg = FwdCfg<P, SHARED>;
-    const int BWr = bc_row_stride(SHARED, kG * P, (int)p.N);
+    const int BWr = bc_row_stride(SHARED, G * P, (int)p.N);
     const size_t smem = sizeof(float) * Cfg::ST * (3 * Cfg::TT * Cfg::DT + 2 * Cfg::TT * BWr);
-    auto kern = k_scan1d_fwd<P, SHARED, VEC, CLAMP>;
+    auto kern = k_scan1d_fwd<P, G, SHARED, VEC, CLAMP>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)smem);
@@ -764,10 +831,18 @@ cudaError_t launch_bwd_t(const Scan1DDev &p, long batch, cudaStream_t s) {
 
 template <int P, bool SHARED>
 cudaError_t fwd_ps(const Scan1DDev &p, long batch, bool vec, bool clamp, cudaStream_t s) {
-    if (vec) return clamp ? launch_fwd_t<P, SHARED, true, true>(p, batch, s)
-                          : launch_fwd_t<P, SHARED, true, false>(p, batch, s);
-    return clamp ? launch_fwd_t<P, SHARED, false, true>(p, batch, s)
-                 : launch_fwd_t<P, SHARED, false, false>(p, batch, s);
+    if (vec) return clamp ? launch_fwd_t<P, 4, SHARED, true, true>(p, batch, s)
+                          : launch_fwd_t<P, 4, SHARED, true, false>(p, batch, s);
+    return clamp ? launch_fwd_t<P, 4, SHARED, false, true>(p, batch, s)
+                 : launch_fwd_t<P, 4, SHARED, false, false>(p, batch, s);
+}
+
+/* 2 states per lane: twice the lanes (and warps) per channel, for
+ * channel-shared B/C with 16-byte aligned rows. */
+template <int P>
+cudaError_t fwd_g2(const Scan1DDev &p, long batch, bool clamp, cudaStream_t s) {
+    return clamp ? launch_fwd_t<P, 2, true, true, true>(p, batch, s)
+                 : launch_fwd_t<P, 2, true, true, false>(p, batch, s);
 }
 
 template <int P>
@@ -795,6 +870,18 @@ cudaError_t bwd_p(const Scan1DDev &p, long batch, bool shared, bool vec, bool ha
 
 } // namespace
 
+/* States per lane of the forward on channel-shared B/C: 4 (default) or 2
+ * (twice the warps, more cross-lane folding).  KMB_SCAN1D_LANE_STATES=2
+ * selects the latter; any other value keeps 4. */
+static int lane_states() {
+    static int g = 0;
+    if (!g) {
+        const char *e = getenv("KMB_SCAN1D_LANE_STATES");
+        g = (e && e[0] == '2' && e[1] == 0) ? 2 : 4;
+    }
+    return g;
+}
+
 extern "C" int kmb_launch_scan1d_fwd(const KmbScan1D *a, cudaStream_t s) {
     Scan1DDev p = make_dev(a);
     const bool vec = (a->N % 4) == 0;
@@ -804,6 +891,19 @@ extern "C" int kmb_launch_scan1d_fwd(const KmbScan1D *a, cudaStream_t s) {
     cudaError_t e;
     if (!shared && P > 16)
         return kmb_fail(KMB_EUNSUPPORTED, "scan1d: per-channel B/C support N <= 64 (N=%ld)", a->N);
+    if (shared && vec && p.vec_bc && a->N <= 64 && lane_states() == 2) {
+        int p2 = 1;
+        while (p2 < (a->N + 1) / 2) p2 <<= 1;
+        switch (p2) {
+        case 2: e = fwd_g2<2>(p, a->batch, clamp, s); break;
+        case 4: e = fwd_g2<4>(p, a->batch, clamp, s); break;
+        case 8: e = fwd_g2<8>(p, a->batch, clamp, s); break;
+        case 16: e = fwd_g2<16>(p, a->batch, clamp, s); break;
+        default: e = fwd_g2<32>(p, a->batch, clamp, s); break;
+        }
+        if (e != cudaSuccess) return kmb_cuda_fail(e, "scan1d forward launch");
+        return KMB_OK;
+    }
     switch (P) {
     case 1: e = fwd_p<1>(p, a->batch, shared, vec, clamp, s); break;
     case 2: e = fwd_p<2>(p, a->batch, shared, vec, clamp, s); break;

@@ -89,7 +89,7 @@ __global__ void __launch_bounds__(kThreads) k_scannd_fwd(NDDev p) {
                     float hn = dt_bar * (Bb[bcb + m] * xv);
                     for (int a = 0; a < nd; ++a) {
                         if (pv[a] >= 0) {
-                            const float e = kmb_ex2(dta[a] * (p.A[a][d * M + m] * KMB_LOG2E));
+                            const float e = kmb_exp2_decay(dta[a] * (p.A[a][d * M + m] * KMB_LOG2E));
                             hn = fmaf(e, h[((long)pv[a] * D + d) * M + m], hn);
                         }
                     }
@@ -156,7 +156,7 @@ __global__ void __launch_bounds__(kThreads) k_scannd_bwd(NDDev p) {
                     float gg = Cb[bcb + m] * gy;
                     for (int a = 0; a < nd; ++a) {
                         if (nx[a] >= 0) {
-                            const float e = kmb_ex2(dtn[a] * (p.A[a][d * M + m] * KMB_LOG2E));
+                            const float e = kmb_exp2_decay(dtn[a] * (p.A[a][d * M + m] * KMB_LOG2E));
                             gg = fmaf(e, G[((long)nx[a] * D + d) * M + m], gg);
                         }
                     }
@@ -174,7 +174,7 @@ __global__ void __launch_bounds__(kThreads) k_scannd_bwd(NDDev p) {
                     for (int a = 0; a < nd; ++a) {
                         if (pv[a] >= 0) {
                             const float aa = p.A[a][d * M + m];
-                            const float e = kmb_ex2(dta[a] * (aa * KMB_LOG2E));
+                            const float e = kmb_exp2_decay(dta[a] * (aa * KMB_LOG2E));
                             const float gh = gg * h[((long)pv[a] * D + d) * M + m] * e;
                             atomicAdd(&sdA[(a * p.dtile + dd) * M + m], gh * dta[a]);
                             sdt[a] = fmaf(gh, aa, sdt[a]);
@@ -197,9 +197,14 @@ __global__ void __launch_bounds__(kThreads) k_scannd_bwd(NDDev p) {
     }
 }
 
-int pick_dtile(long D, int nd, long M, bool bwd) {
+/* Channel tile of a CTA: a power of two dividing 256, small enough that
+ * the grid has >= 2 CTAs per SM (every CTA walks all levels, so CTAs are
+ * the only parallelism across chains), and within the backward's shared
+ * dA budget. */
+int pick_dtile(long D, int nd, long M, bool bwd, long batch) {
     int t = 64;
     while (t > 1 && t / 2 >= D) t >>= 1;
+    while (t > 4 && batch * ((D + t - 1) / t) < 2 * 148) t >>= 1;
     if (bwd)
         while (t > 1 && (long)nd * t * M * 4 > 96 * 1024) t >>= 1;
     return t;
@@ -231,7 +236,7 @@ void fill_dev(const KmbNDLaunch *a, NDDev *p) {
 extern "C" int kmb_launch_scannd_fwd(const KmbNDLaunch *a, cudaStream_t s) {
     NDDev p;
     fill_dev(a, &p);
-    p.dtile = pick_dtile(a->D, a->nd, a->M, false);
+    p.dtile = pick_dtile(a->D, a->nd, a->M, false, a->batch);
     dim3 grid((unsigned)((a->D + p.dtile - 1) / p.dtile), (unsigned)a->batch);
     k_scannd_fwd<<<grid, kThreads, 0, s>>>(p);
     cudaError_t e = cudaGetLastError();
@@ -242,7 +247,7 @@ extern "C" int kmb_launch_scannd_fwd(const KmbNDLaunch *a, cudaStream_t s) {
 extern "C" int kmb_launch_scannd_bwd(const KmbNDLaunch *a, cudaStream_t s) {
     NDDev p;
     fill_dev(a, &p);
-    p.dtile = pick_dtile(a->D, a->nd, a->M, true);
+    p.dtile = pick_dtile(a->D, a->nd, a->M, true, a->batch);
     if ((long)a->nd * p.dtile * a->M * 4 > 96 * 1024)
         return kmb_fail(KMB_EUNSUPPORTED, "scannd backward: ndims*M too large (M=%ld)", a->M);
     cudaError_t e = cudaSuccess;

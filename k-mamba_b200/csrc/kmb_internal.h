@@ -14,9 +14,6 @@
 extern "C" {
 #endif
 
-/* Steps between forward checkpoints; also the backward chunk length. */
-#define KMB_SCAN1D_CHUNK 16
-
 /* Records a status and a message for kmb_last_error(); returns status. */
 int kmb_fail(int status, const char *fmt, ...);
 int kmb_cuda_fail(cudaError_t e, const char *where);

@@ -23,7 +23,7 @@ KMB_ENOMEM = -3
 KMB_ETIMEOUT = -4
 KMB_EUNSUPPORTED = -5
 
-KMB_SCAN1D_CHUNK = 16
+KMB_SCAN1D_CHUNK = 8
 
 fp = C.c_void_p  # float* / long* passed as raw addresses
 lg = C.c_long

@@ -52,8 +52,8 @@ def test_invalid_arguments_rejected_without_gpu(lib):
 
 
 def test_ckpt_size(lib):
-    assert lib.kmb_scan1d_ckpt_elems(8, 4096, 1536, 16) == 8 * 256 * 1536 * 16
-    assert lib.kmb_scan1d_ckpt_elems(1, 17, 2, 3) == 2 * 2 * 3
+    assert lib.kmb_scan1d_ckpt_elems(8, 4096, 1536, 16) == 8 * (4096 // kb.KMB_SCAN1D_CHUNK) * 1536 * 16
+    assert lib.kmb_scan1d_ckpt_elems(1, 17, 2, 3) == 3 * 2 * 3
     assert lib.kmb_scan1d_ckpt_elems(0, 17, 2, 3) == 0
 
 
