@@ -30,6 +30,7 @@ import statistics
 import subprocess
 import sys
 import threading
+import tempfile
 import time
 
 import numpy as np
@@ -93,8 +94,9 @@ class Clocks:
         q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
              "clocks_event_reasons.sw_power_cap")
-        os.makedirs(os.path.join(ROOT, "gpurun_out"), exist_ok=True)
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{self.index}.csv")
+        d = os.environ.get("KMB_CLOCKS_DIR") or tempfile.gettempdir()
+        os.makedirs(d, exist_ok=True)
+        self.path = os.path.join(d, f"clocks_gpu{self.index}.csv")
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
@@ -261,7 +263,8 @@ def run_secondary(args):
     """Times one forward + backward of BASELINE config 3 (ConvND 512x512,
     D 64, K 3, batch 16) or config 4 (2D scan 256x256, batch 8, D 256,
     N 16, B/C shared, same dt on both axes) and prints one JSON line with
-    the per-kernel roofline.  Algorithmic bytes follow SURVEY 8(d)."""
+    the per-kernel roofline.  Algorithmic bytes: inputs read once plus
+    outputs written once."""
     import torch
     import kmamba_b200 as kb
     lib = kb.load()

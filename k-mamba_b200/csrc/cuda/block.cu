@@ -1,0 +1,650 @@
+/*
+ * Mamba-3 block and LM-model kernels (sm_100a), fp32.
+ *
+ * Semantics of the reference CPU block (src/mamba_block.c:89-120 for the
+ * controller projections, :413-465 for the scan, :471-502 for the block)
+ * and model step (src/kmamba.c:344-466):
+ *
+ *   u_t = silu(W_in x_t)                        [R]
+ *   dt_t = clamp(softplus(delta_proj . x_t), dt_min, dt_max)
+ *   lam_t = sigmoid(lambda_proj . x_t)
+ *   B_t = W_B x_t + b_B,  C_t = W_C x_t + b_C   [R*N], index r*N + n
+ *   Bu_t[n] = sum_r B_t[r*N+n] u_t[r]
+ *   h_t = exp(dt_t A) * R(theta) h_{t-1} + (1-lam_t) dt_t exp(dt_t A) Bu_{t-1}
+ *         + lam_t dt_t Bu_t                     (R rotates state pairs)
+ *   y_t[r] = sum_n C_t[r*N+n] h_t[n],   out_t = x_t + W_out y_t
+ *
+ * The projections of all tokens are one GEMM against the concatenated
+ * weight [W_in; delta_proj; lambda_proj; W_B; W_C] (fp32 SIMT GEMM: fp32
+ * parity with the reference excludes tf32/bf16 tensor-core GEMMs here),
+ * followed by one elementwise activation pass.  The scan runs one CTA per
+ * sequence with one thread per state pair, sequential in t; y is folded
+ * across the CTA each step.  The backward is the adjoint of the scan (the
+ * reference's CPU backward is an empty stub), walked in reverse with the
+ * adjoint carried through the transposed rotation.
+ */
+#include "kmb_common.cuh"
+#include "../kmb_internal.h"
+
+namespace {
+
+/* ------------------------------------------------------------------ */
+/* strided fp32 GEMM                                                    */
+/* ------------------------------------------------------------------ */
+
+constexpr int kTM = 64, kTN = 64, kTK = 16;
+
+/* C[m*ldc + n] (+)= sum_k A[m*am + k*ak] * B[k*bk + n*bn] */
+__global__ void __launch_bounds__(256)
+k_gemm(int M, int N, int K, const float *A, long am, long ak, const float *B, long bk,
+       long bn, float *C, long ldc, int accumulate) {
+    __shared__ float As[kTK][kTM + 4];
+    __shared__ float Bs[kTK][kTN + 4];
+    const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+    const int m0 = blockIdx.y * kTM, n0 = blockIdx.x * kTN;
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+    const bool a_kfast = ak == 1, b_nfast = bn == 1;
+    for (int k0 = 0; k0 < K; k0 += kTK) {
+        for (int e = threadIdx.x; e < kTM * kTK; e += 256) {
+            int mm, kk;
+            if (a_kfast) { mm = e / kTK; kk = e % kTK; } else { kk = e / kTM; mm = e % kTM; }
+            const int gm = m0 + mm, gk = k0 + kk;
+            As[kk][mm] = (gm < M && gk < K) ? A[gm * am + gk * ak] : 0.f;
+        }
+        for (int e = threadIdx.x; e < kTK * kTN; e += 256) {
+            int nn, kk;
+            if (b_nfast) { kk = e / kTN; nn = e % kTN; } else { nn = e / kTK; kk = e % kTK; }
+            const int gn = n0 + nn, gk = k0 + kk;
+            Bs[kk][nn] = (gn < N && gk < K) ? B[gk * bk + gn * bn] : 0.f;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < kTK; ++kk) {
+            float a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) a[i] = As[kk][ty * 4 + i];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int gm = m0 + ty * 4 + i;
+        if (gm >= M) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int gn = n0 + tx * 4 + j;
+            if (gn >= N) continue;
+            float *c = C + (long)gm * ldc + gn;
+            *c = accumulate ? *c + acc[i][j] : acc[i][j];
+        }
+    }
+}
+
+/* ------------------------------------------------------------------ */
+/* projection activations                                               */
+/* ------------------------------------------------------------------ */
+
+struct ActArgs {
+    const float *zraw;   /* [rows, W] GEMM output */
+    float *zact;         /* [rows, W] activated */
+    const float *bB, *bC;
+    long rows;
+    int W, R, NR;
+    float dt_min, dt_max;
+    int has_dp, has_lp;  /* 0: dt = dt_scale, lambda = 0.5 (no projection) */
+    float dt_scale;
+};
+
+__global__ void k_block_act(ActArgs a) {
+    const long total = a.rows * a.W;
+    for (long e = (long)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+         e += (long)gridDim.x * blockDim.x) {
+        const int c = (int)(e % a.W);
+        const float z = a.zraw[e];
+        float v;
+        if (c < a.R) {
+            v = z / (1.0f + expf(-z));                 /* silu */
+        } else if (c == a.R) {
+            if (a.has_dp) {
+                v = logf(1.0f + expf(z));              /* softplus, then clamp */
+                if (v < a.dt_min) v = a.dt_min;
+                if (v > a.dt_max) v = a.dt_max;
+            } else {
+                v = a.dt_scale;
+            }
+        } else if (c == a.R + 1) {
+            v = a.has_lp ? 1.0f / (1.0f + expf(-z)) : 0.5f; /* sigmoid */
+        } else if (c < a.R + 2 + a.NR) {
+            v = z + a.bB[c - a.R - 2];
+        } else {
+            v = z + a.bC[c - a.R - 2 - a.NR];
+        }
+        a.zact[e] = v;
+    }
+}
+
+/* dZ (in place) from the gradients of the activated values */
+__global__ void k_block_act_bwd(ActArgs a, float *dz) {
+    const long total = a.rows * a.W;
+    for (long e = (long)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+         e += (long)gridDim.x * blockDim.x) {
+        const int c = (int)(e % a.W);
+        if (c > a.R + 1) continue; /* B / C columns: identity (+bias) */
+        const float z = a.zraw[e];
+        const float g = dz[e];
+        float d;
+        if (c < a.R) {
+            const float s = 1.0f / (1.0f + expf(-z));
+            d = g * s * (1.0f + z * (1.0f - s));
+        } else if (c == a.R) {
+            const float sp = logf(1.0f + expf(z));
+            d = (a.has_dp && sp > a.dt_min && sp < a.dt_max) ? g / (1.0f + expf(-z)) : 0.f;
+        } else {
+            const float l = a.zact[e];
+            d = a.has_lp ? g * l * (1.0f - l) : 0.f;
+        }
+        dz[e] = d;
+    }
+}
+
+/* column sums of dZ over the rows for the B / C bias gradients */
+__global__ void k_colsum_acc(const float *dz, long rows, int W, int c0, int ncols, float *out) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= ncols) return;
+    float s = 0.f;
+    for (long r = 0; r < rows; ++r) s += dz[r * W + c0 + c];
+    out[c] += s;
+}
+
+/* ------------------------------------------------------------------ */
+/* Mamba-3 scan                                                         */
+/* ------------------------------------------------------------------ */
+
+constexpr int kMaxR = 8;
+
+struct ScanArgs {
+    const float *zact;   /* [batch, L, W] */
+    const float *A;      /* [N] (A_log used as A) */
+    const float *theta;  /* [N/2] */
+    float *h_hist;       /* [batch, L, N] or NULL */
+    float *h_last;       /* [batch, N] final state, or NULL */
+    float *y;            /* [batch, L, R] */
+    /* backward */
+    const float *dy;     /* [batch, L, R] */
+    float *dz;           /* [batch, L, W] (u, dt, lam, B, C columns) */
+    float *dA;           /* [N], accumulated */
+    float *dtheta;       /* [N/2], accumulated */
+    int L, N, R, W;
+};
+
+/* block-wide sum of `cnt` values (cnt <= kMaxR + 2); result in red[0..cnt) */
+__device__ __forceinline__ void block_sum(float *v, int cnt, float *red, int nwarps) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    for (int k = 0; k < cnt; ++k) {
+        float x = v[k];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+        if (lane == 0) red[k * 32 + w] = x;
+    }
+    __syncthreads();
+    if (threadIdx.x < cnt) {
+        float s = 0.f;
+        for (int i = 0; i < nwarps; ++i) s += red[threadIdx.x * 32 + i];
+        red[kMaxR * 32 + 64 + threadIdx.x] = s;
+    }
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(1024) k_m3_scan_fwd(ScanArgs a) {
+    __shared__ float red[(kMaxR + 2) * 32 + 64 + 16];
+    const int b = blockIdx.x;
+    const int N = a.N, R = a.R, W = a.W, L = a.L;
+    const int npairs = (N + 1) / 2;
+    const int i = threadIdx.x; /* pair index */
+    const bool act = i < npairs;
+    const int n0 = 2 * i, n1 = 2 * i + 1;
+    const bool has1 = act && n1 < N;
+    const bool rot = has1; /* an odd N leaves its last state unrotated */
+    float cv = 1.f, sv = 0.f, A0 = 0.f, A1 = 0.f;
+    if (act) {
+        A0 = a.A[n0];
+        if (has1) A1 = a.A[n1];
+        if (rot) {
+            const float th = a.theta[i];
+            cv = cosf(th);
+            sv = sinf(th);
+        }
+    }
+    float h0 = 0.f, h1 = 0.f, pb0 = 0.f, pb1 = 0.f;
+    const int nw = (blockDim.x + 31) / 32;
+    const float *zb = a.zact + (long)b * L * W;
+    for (int t = 0; t < L; ++t) {
+        const float *row = zb + (long)t * W;
+        const float dt = row[R], lam = row[R + 1];
+        const float *Bt = row + R + 2;
+        const float *Ct = Bt + R * N;
+        float yp[kMaxR];
+        for (int r = 0; r < R; ++r) yp[r] = 0.f;
+        if (act) {
+            float bu0 = 0.f, bu1 = 0.f;
+            for (int r = 0; r < R; ++r) {
+                const float ur = row[r];
+                bu0 += Bt[r * N + n0] * ur;
+                if (has1) bu1 += Bt[r * N + n1] * ur;
+            }
+            const float hr0 = rot ? cv * h0 - sv * h1 : h0;
+            const float hr1 = rot ? sv * h0 + cv * h1 : h1;
+            const float al0 = expf(dt * A0), al1 = expf(dt * A1);
+            const float be0 = (1.0f - lam) * dt * al0, be1 = (1.0f - lam) * dt * al1;
+            const float ga = lam * dt;
+            h0 = al0 * hr0 + be0 * pb0 + ga * bu0;
+            h1 = has1 ? al1 * hr1 + be1 * pb1 + ga * bu1 : 0.f;
+            pb0 = bu0;
+            pb1 = bu1;
+            if (a.h_hist) {
+                float *hh = a.h_hist + ((long)b * L + t) * N;
+                hh[n0] = h0;
+                if (has1) hh[n1] = h1;
+            }
+            for (int r = 0; r < R; ++r)
+                yp[r] = Ct[r * N + n0] * h0 + (has1 ? Ct[r * N + n1] * h1 : 0.f);
+        }
+        block_sum(yp, R, red, nw);
+        if (threadIdx.x < R) a.y[((long)b * L + t) * R + threadIdx.x] = red[kMaxR * 32 + 64 + threadIdx.x];
+    }
+    if (a.h_last && act) {
+        a.h_last[(long)b * N + n0] = h0;
+        if (has1) a.h_last[(long)b * N + n1] = h1;
+    }
+}
+
+__global__ void __launch_bounds__(1024) k_m3_scan_bwd(ScanArgs a) {
+    __shared__ float red[(kMaxR + 2) * 32 + 64 + 16];
+    const int b = blockIdx.x;
+    const int N = a.N, R = a.R, W = a.W, L = a.L;
+    const int npairs = (N + 1) / 2;
+    const int i = threadIdx.x;
+    const bool act = i < npairs;
+    const int n0 = 2 * i, n1 = 2 * i + 1;
+    const bool has1 = act && n1 < N;
+    const bool rot = has1;
+    float cv = 1.f, sv = 0.f, A0 = 0.f, A1 = 0.f;
+    if (act) {
+        A0 = a.A[n0];
+        if (has1) A1 = a.A[n1];
+        if (rot) {
+            const float th = a.theta[i];
+            cv = cosf(th);
+            sv = sinf(th);
+        }
+    }
+    const int nw = (blockDim.x + 31) / 32;
+    const float *zb = a.zact + (long)b * L * W;
+    float *dzb = a.dz + (long)b * L * W;
+    const float *hb = a.h_hist + (long)b * L * N;
+    /* carry = R^T(alpha_{t+1} * G_{t+1});  bgn = beta_{t+1} * G_{t+1} */
+    float c0 = 0.f, c1 = 0.f, bg0 = 0.f, bg1 = 0.f, sA0 = 0.f, sA1 = 0.f, sth = 0.f;
+    for (int t = L - 1; t >= 0; --t) {
+        const float *row = zb + (long)t * W;
+        const float dt = row[R], lam = row[R + 1];
+        const float *Bt = row + R + 2;
+        const float *Ct = Bt + R * N;
+        const float *dyt = a.dy + ((long)b * L + t) * R;
+        float part[kMaxR + 2];
+        for (int k = 0; k < R + 2; ++k) part[k] = 0.f;
+        if (act) {
+            float bu0 = 0.f, bu1 = 0.f, pb0 = 0.f, pb1 = 0.f;
+            for (int r = 0; r < R; ++r) {
+                const float ur = row[r];
+                bu0 += Bt[r * N + n0] * ur;
+                if (has1) bu1 += Bt[r * N + n1] * ur;
+            }
+            if (t > 0) {
+                const float *prow = row - W;
+                const float *Bp = prow + R + 2;
+                for (int r = 0; r < R; ++r) {
+                    const float ur = prow[r];
+                    pb0 += Bp[r * N + n0] * ur;
+                    if (has1) pb1 += Bp[r * N + n1] * ur;
+                }
+            }
+            const float hp0 = t > 0 ? hb[(long)(t - 1) * N + n0] : 0.f;
+            const float hp1 = (t > 0 && has1) ? hb[(long)(t - 1) * N + n1] : 0.f;
+            const float ht0 = hb[(long)t * N + n0];
+            const float ht1 = has1 ? hb[(long)t * N + n1] : 0.f;
+            float G0 = c0, G1 = c1;
+            for (int r = 0; r < R; ++r) {
+                G0 = fmaf(Ct[r * N + n0], dyt[r], G0);
+                if (has1) G1 = fmaf(Ct[r * N + n1], dyt[r], G1);
+            }
+            const float hr0 = rot ? cv * hp0 - sv * hp1 : hp0;
+            const float hr1 = rot ? sv * hp0 + cv * hp1 : hp1;
+            const float al0 = expf(dt * A0), al1 = has1 ? expf(dt * A1) : 0.f;
+            const float oml = 1.0f - lam;
+            const float ga0 = G0 * (hr0 + oml * dt * pb0);
+            const float ga1 = G1 * (hr1 + oml * dt * pb1);
+            /* ddt, dlam */
+            part[R] = ga0 * A0 * al0 + G0 * (oml * al0 * pb0 + lam * bu0) +
+                      ga1 * A1 * al1 + G1 * (oml * al1 * pb1 + lam * bu1);
+            part[R + 1] = G0 * dt * (bu0 - al0 * pb0) + G1 * dt * (bu1 - al1 * pb1);
+            sA0 = fmaf(ga0 * dt, al0, sA0);
+            sA1 = fmaf(ga1 * dt, al1, sA1);
+            /* Bu_t feeds h_t (gamma) and h_{t+1} (beta_{t+1}) */
+            const float dbu0 = lam * dt * G0 + bg0;
+            const float dbu1 = lam * dt * G1 + bg1;
+            bg0 = oml * dt * al0 * G0;
+            bg1 = oml * dt * al1 * G1;
+            float *dzr = dzb + (long)t * W;
+            for (int r = 0; r < R; ++r) {
+                const float ur = row[r];
+                dzr[R + 2 + r * N + n0] = dbu0 * ur;
+                dzr[R + 2 + R * N + r * N + n0] = dyt[r] * ht0;
+                part[r] = dbu0 * Bt[r * N + n0];
+                if (has1) {
+                    dzr[R + 2 + r * N + n1] = dbu1 * ur;
+                    dzr[R + 2 + R * N + r * N + n1] = dyt[r] * ht1;
+                    part[r] += dbu1 * Bt[r * N + n1];
+                }
+            }
+            /* rotation: h_rot = R h_{t-1};  d h_rot = alpha * G */
+            const float dr0 = al0 * G0, dr1 = al1 * G1;
+            if (rot) {
+                sth += dr0 * (-sv * hp0 - cv * hp1) + dr1 * (cv * hp0 - sv * hp1);
+                c0 = cv * dr0 + sv * dr1;
+                c1 = -sv * dr0 + cv * dr1;
+            } else {
+                c0 = dr0;
+                c1 = dr1;
+            }
+        }
+        block_sum(part, R + 2, red, nw);
+        if (threadIdx.x < R + 2) dzb[(long)t * W + threadIdx.x] = red[kMaxR * 32 + 64 + threadIdx.x];
+    }
+    if (act) {
+        atomicAdd(a.dA + n0, sA0);
+        if (has1) atomicAdd(a.dA + n1, sA1);
+        if (rot) atomicAdd(a.dtheta + i, sth);
+    }
+}
+
+/* ------------------------------------------------------------------ */
+/* model pieces                                                         */
+/* ------------------------------------------------------------------ */
+
+__global__ void k_embed_gather(const float *emb, const unsigned *tok, long L, long D, long V,
+                               float *out) {
+    for (long e = (long)blockIdx.x * blockDim.x + threadIdx.x; e < L * D;
+         e += (long)gridDim.x * blockDim.x) {
+        const long t = e / D, d = e % D;
+        const unsigned id = tok[t];
+        out[e] = id < V ? emb[(long)id * D + d] : 0.f;
+    }
+}
+
+__global__ void k_embed_scatter(const float *dx, const unsigned *tok, long L, long D, long V,
+                                float *gemb) {
+    for (long e = (long)blockIdx.x * blockDim.x + threadIdx.x; e < L * D;
+         e += (long)gridDim.x * blockDim.x) {
+        const long t = e / D, d = e % D;
+        const unsigned id = tok[t];
+        if (id < V) atomicAdd(gemb + (long)id * D + d, dx[e]);
+    }
+}
+
+/* One CTA per row: reference softmax (src/kmamba.c:29-52) and CE terms. */
+__global__ void __launch_bounds__(256)
+k_softmax_ce(const float *logits, const unsigned *tgt, long V, float invL, float *dlogits,
+             float *row_loss) {
+    __shared__ float red[32];
+    __shared__ float bmax, bsum;
+    const long t = blockIdx.x;
+    const float *x = logits + t * V;
+    float m = -INFINITY;
+    for (long i = threadIdx.x; i < V; i += blockDim.x) {
+        const float v = x[i];
+        if (!isnan(v) && !isinf(v)) m = fmaxf(m, v);
+    }
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float mm = -INFINITY;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) mm = fmaxf(mm, red[w]);
+        bmax = (isinf(mm) || isnan(mm)) ? 0.f : mm;
+    }
+    __syncthreads();
+    const float mx = bmax;
+    float s = 0.f;
+    for (long i = threadIdx.x; i < V; i += blockDim.x) s += expf(fmaxf(x[i] - mx, -80.0f));
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float ss = 0.f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) ss += red[w];
+        bsum = ss < 1e-20f ? 1e-20f : ss;
+    }
+    __syncthreads();
+    const float inv = 1.0f / bsum;
+    const unsigned tg = tgt[t];
+    if (tg >= (unsigned)V && threadIdx.x == 0) row_loss[t] = NAN; /* host rejects these */
+    for (long i = threadIdx.x; i < V; i += blockDim.x) {
+        const float p = expf(fmaxf(x[i] - mx, -80.0f)) * inv;
+        float d = p * invL;
+        if (i == (long)tg) {
+            d -= invL;
+            row_loss[t] = -logf(p < 1e-20f ? 1e-20f : p);
+        }
+        dlogits[t * V + i] = d;
+    }
+}
+
+__global__ void k_adamw(float *p, const float *g, float *m, float *v, long n, float lr,
+                        float b1, float b2, float eps, float wd, float bc1, float bc2) {
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (long)gridDim.x * blockDim.x) {
+        const float gi = g[i];
+        const float mi = b1 * m[i] + (1.0f - b1) * gi;
+        const float vi = b2 * v[i] + (1.0f - b2) * gi * gi;
+        m[i] = mi;
+        v[i] = vi;
+        const float mh = mi / bc1, vh = vi / bc2;
+        p[i] = p[i] * (1.0f - lr * wd) - lr * mh / (sqrtf(vh) + eps);
+    }
+}
+
+__global__ void k_sumsq(const float *x, long n, double *out) {
+    double s = 0.0;
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (long)gridDim.x * blockDim.x)
+        s += (double)x[i] * x[i];
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) atomicAdd(out, s);
+}
+
+/* y = a*y + b*x */
+__global__ void k_axpby(float *y, const float *x, long n, float a, float b) {
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (long)gridDim.x * blockDim.x)
+        y[i] = x ? a * y[i] + b * x[i] : a * y[i];
+}
+
+/* dt = clamp(softplus(z), dt_min, dt_max) */
+__global__ void k_dt_act(const float *z, float *out, long n, float dt_min, float dt_max) {
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (long)gridDim.x * blockDim.x) {
+        float v = logf(1.0f + expf(z[i]));
+        if (v < dt_min) v = dt_min;
+        if (v > dt_max) v = dt_max;
+        out[i] = v;
+    }
+}
+
+/* m = mu*m + g (momentum of the MUON optimizer) */
+__global__ void k_momentum(float *m, const float *g, long n, float mu) {
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (long)gridDim.x * blockDim.x)
+        m[i] = mu * m[i] + g[i];
+}
+
+/* G = 1.5 G - 0.5 T (one Newton-Schulz step after T = G G^T G) */
+__global__ void k_ns_combine(float *G, const float *T, long n) {
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (long)gridDim.x * blockDim.x)
+        G[i] = 1.5f * G[i] - 0.5f * T[i];
+}
+
+/* p -= lr * x * scale, scale = clip / ||x|| when ||x|| > clip (sumsq from
+ * k_sumsq), else 1; sumsq == NULL gives scale 1 (plain SGD) */
+__global__ void k_scaled_sub(float *p, const float *x, long n, float lr, float clip,
+                             const double *sumsq) {
+    float scale = 1.0f;
+    if (sumsq) {
+        const float norm = sqrtf((float)*sumsq);
+        scale = norm > clip ? clip / norm : 1.0f;
+    }
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (long)gridDim.x * blockDim.x)
+        p[i] -= lr * x[i] * scale;
+}
+
+unsigned grid1d(long n) {
+    long b = (n + 255) / 256;
+    if (b > 148L * 16) b = 148L * 16;
+    return (unsigned)(b < 1 ? 1 : b);
+}
+
+} // namespace
+
+extern "C" int kmb_gemm(int M, int N, int K, const float *A, long am, long ak, const float *B,
+                        long bk, long bn, float *C, long ldc, int accumulate, cudaStream_t s) {
+    if (M <= 0 || N <= 0) return KMB_OK;
+    if (K <= 0) {
+        if (!accumulate) {
+            for (int m = 0; m < M; ++m) {
+                cudaError_t e = cudaMemsetAsync(C + (long)m * ldc, 0, sizeof(float) * N, s);
+                if (e != cudaSuccess) return kmb_cuda_fail(e, "gemm memset");
+            }
+        }
+        return KMB_OK;
+    }
+    dim3 grid((unsigned)((N + kTN - 1) / kTN), (unsigned)((M + kTM - 1) / kTM));
+    k_gemm<<<grid, 256, 0, s>>>(M, N, K, A, am, ak, B, bk, bn, C, ldc, accumulate);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "gemm launch");
+}
+
+extern "C" int kmb_block_act(const float *zraw, float *zact, const float *bB, const float *bC,
+                             long rows, int W, int R, int NR, float dt_min, float dt_max,
+                             int has_dp, int has_lp, float dt_scale, float *dz_inplace,
+                             cudaStream_t s) {
+    ActArgs a{zraw, zact, bB, bC, rows, W, R, NR, dt_min, dt_max, has_dp, has_lp, dt_scale};
+    if (dz_inplace) k_block_act_bwd<<<grid1d(rows * W), 256, 0, s>>>(a, dz_inplace);
+    else k_block_act<<<grid1d(rows * W), 256, 0, s>>>(a);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "block activation launch");
+}
+
+extern "C" int kmb_colsum_acc(const float *dz, long rows, int W, int c0, int ncols, float *out,
+                              cudaStream_t s) {
+    k_colsum_acc<<<(unsigned)((ncols + 127) / 128), 128, 0, s>>>(dz, rows, W, c0, ncols, out);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "colsum launch");
+}
+
+extern "C" int kmb_m3_scan(int batch, int L, int N, int R, int W, const float *zact,
+                           const float *A, const float *theta, float *h_hist, float *h_last,
+                           float *y, const float *dy, float *dz, float *dA, float *dtheta,
+                           cudaStream_t s) {
+    if (R > kMaxR) return kmb_fail(KMB_EUNSUPPORTED, "block: mimo_rank %d exceeds %d", R, kMaxR);
+    const int npairs = (N + 1) / 2;
+    if (npairs > 1024)
+        return kmb_fail(KMB_EUNSUPPORTED, "block: state_size %d exceeds 2048", N);
+    const int threads = ((npairs + 31) / 32) * 32;
+    if (dy && !h_hist) return kmb_fail(KMB_EINVAL, "block scan backward needs the state history");
+    ScanArgs a{zact, A, theta, h_hist, h_last, y, dy, dz, dA, dtheta, L, N, R, W};
+    if (dy) k_m3_scan_bwd<<<batch, threads, 0, s>>>(a);
+    else k_m3_scan_fwd<<<batch, threads, 0, s>>>(a);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "block scan launch");
+}
+
+extern "C" int kmb_embed(const float *emb, const unsigned *tok, long L, long D, long V,
+                         float *out, const float *dx_for_grad, float *gemb, cudaStream_t s) {
+    if (gemb) k_embed_scatter<<<grid1d(L * D), 256, 0, s>>>(dx_for_grad, tok, L, D, V, gemb);
+    else k_embed_gather<<<grid1d(L * D), 256, 0, s>>>(emb, tok, L, D, V, out);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "embedding launch");
+}
+
+extern "C" int kmb_softmax_ce(const float *logits, const unsigned *tgt, long L, long V,
+                              float *dlogits, float *row_loss, cudaStream_t s) {
+    k_softmax_ce<<<(unsigned)L, 256, 0, s>>>(logits, tgt, V, 1.0f / (float)L, dlogits, row_loss);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "softmax-ce launch");
+}
+
+extern "C" int kmb_adamw(float *p, const float *g, float *m, float *v, long n, float lr,
+                         float b1, float b2, float eps, float wd, float bc1, float bc2,
+                         cudaStream_t s) {
+    if (n <= 0) return KMB_OK;
+    k_adamw<<<grid1d(n), 256, 0, s>>>(p, g, m, v, n, lr, b1, b2, eps, wd, bc1, bc2);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "adamw launch");
+}
+
+extern "C" int kmb_sumsq(const float *x, long n, double *out, cudaStream_t s) {
+    if (n <= 0) return KMB_OK;
+    k_sumsq<<<grid1d(n), 256, 0, s>>>(x, n, out);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "sumsq launch");
+}
+
+#define KMB_ELEMWISE_RET(what)                                                       \
+    do {                                                                             \
+        cudaError_t e_ = cudaGetLastError();                                         \
+        return e_ == cudaSuccess ? KMB_OK : kmb_cuda_fail(e_, what);                 \
+    } while (0)
+
+extern "C" int kmb_axpby(float *y, const float *x, long n, float a, float b, cudaStream_t s) {
+    if (n <= 0) return KMB_OK;
+    k_axpby<<<grid1d(n), 256, 0, s>>>(y, x, n, a, b);
+    KMB_ELEMWISE_RET("axpby launch");
+}
+
+extern "C" int kmb_dt_act(const float *z, float *out, long n, float dt_min, float dt_max,
+                          cudaStream_t s) {
+    if (n <= 0) return KMB_OK;
+    k_dt_act<<<grid1d(n), 256, 0, s>>>(z, out, n, dt_min, dt_max);
+    KMB_ELEMWISE_RET("dt activation launch");
+}
+
+extern "C" int kmb_momentum(float *m, const float *g, long n, float mu, cudaStream_t s) {
+    if (n <= 0) return KMB_OK;
+    k_momentum<<<grid1d(n), 256, 0, s>>>(m, g, n, mu);
+    KMB_ELEMWISE_RET("momentum launch");
+}
+
+extern "C" int kmb_ns_combine(float *G, const float *T, long n, cudaStream_t s) {
+    if (n <= 0) return KMB_OK;
+    k_ns_combine<<<grid1d(n), 256, 0, s>>>(G, T, n);
+    KMB_ELEMWISE_RET("newton-schulz launch");
+}
+
+extern "C" int kmb_scaled_sub(float *p, const float *x, long n, float lr, float clip,
+                              const double *sumsq, cudaStream_t s) {
+    if (n <= 0) return KMB_OK;
+    k_scaled_sub<<<grid1d(n), 256, 0, s>>>(p, x, n, lr, clip, sumsq);
+    KMB_ELEMWISE_RET("scaled update launch");
+}

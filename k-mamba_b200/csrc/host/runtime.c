@@ -210,7 +210,21 @@ void kmb_stage_begin(KmbStage *st) {
      * kmb_last_status() always describes the latest call */
     kmb_clear_error();
     memset(st, 0, sizeof *st);
+    st->b = st->inl;
+    st->cap = KMB_STAGE_MAX;
     st->s = kmb_stream();
+}
+
+int kmb_stage_reserve(KmbStage *st, int cap) {
+    KmbStageBuf *t;
+    if (cap <= st->cap) return KMB_OK;
+    t = (KmbStageBuf *)calloc((size_t)cap, sizeof *t);
+    if (!t) return st->status = kmb_fail(KMB_ENOMEM, "staging: host allocation failed");
+    memcpy(t, st->b, sizeof *t * (size_t)st->n);
+    if (st->b != st->inl) free(st->b);
+    st->b = t;
+    st->cap = cap;
+    return KMB_OK;
 }
 
 static KmbStageBuf *stage_find(KmbStage *st, const void *p) {
@@ -233,7 +247,7 @@ static void *stage_add(KmbStage *st, const void *p, size_t bytes, int out, int c
         b->out |= out;
         return b->dev;
     }
-    if (st->n >= KMB_STAGE_MAX) {
+    if (st->n >= st->cap) {
         st->status = kmb_fail(KMB_EINVAL, "staging: too many buffers");
         return NULL;
     }
@@ -273,7 +287,7 @@ void *kmb_stage_out(KmbStage *st, void *p, size_t bytes, int copy_in) {
 void *kmb_scratch(KmbStage *st, size_t bytes) {
     KmbStageBuf *b;
     if (st->status) return NULL;
-    if (st->n >= KMB_STAGE_MAX) {
+    if (st->n >= st->cap) {
         st->status = kmb_fail(KMB_EINVAL, "staging: too many buffers");
         return NULL;
     }
@@ -309,5 +323,8 @@ int kmb_stage_finish(KmbStage *st, int status) {
     for (int i = 0; i < st->n; ++i)
         if (st->b[i].owned) kmb_pool_free(st->b[i].dev);
     st->n = 0;
+    if (st->b != st->inl) free(st->b);
+    st->b = st->inl;
+    st->cap = KMB_STAGE_MAX;
     return status;
 }

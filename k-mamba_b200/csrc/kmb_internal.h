@@ -53,6 +53,38 @@ typedef struct {
 int kmb_launch_scannd_fwd(const KmbNDLaunch *a, cudaStream_t s);
 int kmb_launch_scannd_bwd(const KmbNDLaunch *a, cudaStream_t s);
 
+/* Block / model kernels (csrc/cuda/block.cu). */
+/* C[m*ldc + n] (+)= sum_k A[m*am + k*ak] * B[k*bk + n*bn], fp32 */
+int kmb_gemm(int M, int N, int K, const float *A, long am, long ak, const float *B, long bk,
+             long bn, float *C, long ldc, int accumulate, cudaStream_t s);
+/* projection activations (dz_inplace == NULL) or their backward in place */
+int kmb_block_act(const float *zraw, float *zact, const float *bB, const float *bC, long rows,
+                  int W, int R, int NR, float dt_min, float dt_max, int has_dp, int has_lp,
+                  float dt_scale, float *dz_inplace, cudaStream_t s);
+int kmb_colsum_acc(const float *dz, long rows, int W, int c0, int ncols, float *out,
+                   cudaStream_t s);
+/* Mamba-3 scan forward (dy == NULL) or backward */
+int kmb_m3_scan(int batch, int L, int N, int R, int W, const float *zact, const float *A,
+                const float *theta, float *h_hist, float *h_last, float *y, const float *dy,
+                float *dz, float *dA, float *dtheta, cudaStream_t s);
+/* embedding gather (gemb == NULL) or gradient scatter-add */
+int kmb_embed(const float *emb, const unsigned *tok, long L, long D, long V, float *out,
+              const float *dx_for_grad, float *gemb, cudaStream_t s);
+int kmb_softmax_ce(const float *logits, const unsigned *tgt, long L, long V, float *dlogits,
+                   float *row_loss, cudaStream_t s);
+int kmb_adamw(float *p, const float *g, float *m, float *v, long n, float lr, float b1,
+              float b2, float eps, float wd, float bc1, float bc2, cudaStream_t s);
+int kmb_sumsq(const float *x, long n, double *out, cudaStream_t s);
+/* y = a*y + b*x (x may be NULL: y = a*y) */
+int kmb_axpby(float *y, const float *x, long n, float a, float b, cudaStream_t s);
+/* out = clamp(softplus(z), dt_min, dt_max) */
+int kmb_dt_act(const float *z, float *out, long n, float dt_min, float dt_max, cudaStream_t s);
+/* MUON pieces: m = mu*m + g;  G = 1.5G - 0.5T;  p -= lr*x*clip_scale(sumsq) */
+int kmb_momentum(float *m, const float *g, long n, float mu, cudaStream_t s);
+int kmb_ns_combine(float *G, const float *T, long n, cudaStream_t s);
+int kmb_scaled_sub(float *p, const float *x, long n, float lr, float clip, const double *sumsq,
+                   cudaStream_t s);
+
 /* Device copy of a grid's wavefront schedule (csrc/host/plan_cache.c):
  * level starts / offsets of km_wavefront_plan_create as int32 plus the
  * predecessor (p - e_axis) and successor (p + e_axis) offsets, -1 outside
@@ -83,7 +115,7 @@ int kmb_is_device_ptr(const void *p);
  * are copied back by kmb_stage_finish).  Passing the same host pointer
  * twice returns the same device buffer.
  */
-#define KMB_STAGE_MAX 48
+#define KMB_STAGE_MAX 64
 typedef struct {
     const void *user;
     void *dev;
@@ -92,13 +124,19 @@ typedef struct {
     int owned;   /* dev is a pool block */
 } KmbStageBuf;
 typedef struct {
-    KmbStageBuf b[KMB_STAGE_MAX];
+    KmbStageBuf inl[KMB_STAGE_MAX];
+    KmbStageBuf *b;   /* inl, or a heap table from kmb_stage_reserve */
+    int cap;
     int n;
     int status;
     cudaStream_t s;
 } KmbStage;
 
 void kmb_stage_begin(KmbStage *st);
+/* Grows the table to hold `cap` buffers (model calls that move every
+ * parameter, gradient and moment of every layer).  Call right after
+ * kmb_stage_begin. */
+int kmb_stage_reserve(KmbStage *st, int cap);
 void *kmb_stage_in(KmbStage *st, const void *p, size_t bytes);
 void *kmb_stage_out(KmbStage *st, void *p, size_t bytes, int copy_in);
 void *kmb_scratch(KmbStage *st, size_t bytes);

@@ -83,6 +83,129 @@ class KmbConvND(C.Structure):
 
 VISIT_FN = C.CFUNCTYPE(C.c_int, C.POINTER(lg), lg, lg, lg, C.c_void_p)
 
+# ---------------------------------------------------------------- kmamba.h
+KMAMBA_MAX_NDIMS = 8
+OPTIMIZER_ADAM_CLIP, OPTIMIZER_MUON, OPTIMIZER_SGD, OPTIMIZER_ADAMW = 0, 1, 2, 3
+_fptr = C.POINTER(C.c_float)
+
+
+class MBOptimConfig(C.Structure):
+    _fields_ = [(n, C.c_float) for n in ("lr", "mu", "beta2", "eps", "clip_norm",
+                                         "weight_decay")]
+
+
+class MBMatrix(C.Structure):
+    _fields_ = [("data", _fptr), ("rows", C.c_size_t), ("cols", C.c_size_t)]
+
+
+class MBConfig(C.Structure):
+    _fields_ = [("dim", C.c_size_t), ("state_size", C.c_size_t), ("seq_len", C.c_size_t),
+                ("mimo_rank", C.c_size_t), ("dt_scale", C.c_float), ("dt_min", C.c_float),
+                ("dt_max", C.c_float), ("use_fp16", C.c_int), ("use_bf16", C.c_int),
+                ("loss_scale", C.c_float), ("spatial_ndims", lg),
+                ("spatial_dims", lg * KMAMBA_MAX_NDIMS), ("use_convnd", C.c_int),
+                ("convnd_K", lg), ("convnd_ndims", lg)]
+
+
+# parameter tensors of a block in the order of the MBOptimState g_/m_/v_ fields
+BLOCK_PARAMS = ("W_in", "W_out", "A_log", "W_B", "W_C", "b_B", "b_C", "delta_proj", "theta",
+                "lambda_proj")
+
+
+class MBOptimState(C.Structure):
+    _fields_ = ([("type", C.c_int), ("step", C.c_size_t)]
+                + [("g_" + n, _fptr) for n in BLOCK_PARAMS]
+                + [(f"{k}_{n}", _fptr) for n in BLOCK_PARAMS for k in ("m", "v")])
+
+
+class MambaBlockWorkspace(C.Structure):
+    _fields_ = [(n, _fptr) for n in ("hidden", "delta", "scan_B", "scan_C", "scan_delta",
+                                     "scan_h")]
+
+
+class MambaBlock(C.Structure):
+    _fields_ = [("config", MBConfig), ("W_in", MBMatrix), ("W_out", MBMatrix),
+                ("A_log", MBMatrix), ("W_B", MBMatrix), ("W_C", MBMatrix),
+                ("delta_proj", MBMatrix), ("b_B", _fptr), ("b_C", _fptr), ("theta", _fptr),
+                ("lambda_proj", MBMatrix), ("wavefront_plan", C.c_void_p),
+                ("convnd_kernel", _fptr), ("convnd_bias", _fptr), ("hidden", _fptr),
+                ("delta", _fptr), ("scan_B", _fptr), ("scan_C", _fptr),
+                ("scan_delta", _fptr), ("scan_h", _fptr),
+                ("opt_state", C.POINTER(MBOptimState))]
+
+
+class KMambaConfig(C.Structure):
+    _fields_ = [("vocab_size", C.c_size_t), ("dim", C.c_size_t), ("state_size", C.c_size_t),
+                ("seq_len", C.c_size_t), ("n_layers", C.c_size_t), ("mimo_rank", C.c_size_t),
+                ("dt_scale", C.c_float), ("dt_min", C.c_float), ("dt_max", C.c_float),
+                ("spatial_ndims", lg), ("spatial_dims", lg * KMAMBA_MAX_NDIMS),
+                ("use_convnd", C.c_int), ("convnd_K", lg), ("convnd_ndims", lg),
+                ("weight_tying", C.c_int)]
+
+
+class KMamba(C.Structure):
+    _fields_ = [("cfg", KMambaConfig), ("embedding", _fptr), ("head", _fptr),
+                ("layers", C.POINTER(C.POINTER(MambaBlock))), ("for_training", C.c_int),
+                ("opt_blocks", MBOptimConfig), ("lr_embed_head", C.c_float),
+                ("weight_decay", C.c_float), ("m_embedding", _fptr), ("v_embedding", _fptr),
+                ("m_head", _fptr), ("v_head", _fptr), ("step_embed_head", C.c_size_t),
+                ("last_grad_norm", C.c_float), ("last_grad_over_clip", C.c_float),
+                ("last_grad_would_clip", C.c_int)]
+
+
+_PB = C.POINTER(MambaBlock)
+_PK = C.POINTER(KMamba)
+_PW = C.POINTER(MambaBlockWorkspace)
+_PS = C.POINTER(MBOptimState)
+_PO = C.POINTER(MBOptimConfig)
+_PM = C.POINTER(MBMatrix)
+
+MODEL_PROTOTYPES = {
+    "mamba_block_create": (_PB, [C.POINTER(MBConfig)]),
+    "mamba_block_free": (None, [_PB]),
+    "mamba_block_init": (None, [_PB]),
+    "mamba_block_workspace_create": (_PW, [_PB]),
+    "mamba_block_workspace_free": (None, [_PW]),
+    "mamba_block_forward": (None, [_PB, fp, fp, C.c_size_t]),
+    "mamba_block_forward_ws": (None, [_PB, _PW, fp, fp, C.c_size_t]),
+    "mamba_attach_optimizer": (None, [_PB, C.c_int, _PO]),
+    "mamba_free_optimizer": (None, [_PB]),
+    "mamba_zero_grads": (None, [_PB]),
+    "mamba_optimizer_step": (None, [_PB, _PO]),
+    "mamba_block_grad_sqnorm": (C.c_float, [_PB]),
+    "mamba_backward": (None, [_PB, fp, fp, fp, C.c_size_t]),
+    "mamba_backward_ws": (None, [_PB, _PW, fp, fp, fp, C.c_size_t]),
+    "mamba_backward_ws_local": (None, [_PB, _PW, fp, fp, fp, C.c_size_t, _PS]),
+    "mamba_local_grad_alloc": (_PS, [_PB]),
+    "mamba_local_grad_reduce": (None, [_PB, _PS]),
+    "mamba_local_grad_free": (None, [_PS]),
+    "mb_matrix_create": (_PM, [C.c_size_t, C.c_size_t]),
+    "mb_matrix_free": (None, [_PM]),
+    "mb_matrix_zero": (None, [_PM]),
+    "mb_matrix_copy": (None, [_PM, _PM]),
+    "mb_matrix_vec_mult": (None, [fp, _PM, fp]),
+    "mb_vec_add": (None, [fp, fp, C.c_size_t]),
+    "mb_vec_scale": (None, [fp, C.c_float, C.c_size_t]),
+    "mb_compute_delta": (None, [fp, _PB, fp, C.c_size_t]),
+    "kmamba_create": (_PK, [C.POINTER(KMambaConfig)]),
+    "kmamba_free": (None, [_PK]),
+    "kmamba_init": (C.c_int, [_PK, C.c_uint32]),
+    "kmamba_enable_training": (C.c_int, [_PK, _PO, C.c_float, C.c_float]),
+    "kmamba_enable_training_with_optimizer": (C.c_int, [_PK, C.c_int, _PO, C.c_float,
+                                                        C.c_float]),
+    "kmamba_save": (C.c_int, [_PK, C.c_char_p]),
+    "kmamba_load": (_PK, [C.c_char_p, C.c_int, _PO, C.c_float, C.c_float]),
+    "kmamba_forward": (C.c_int, [_PK, fp, fp]),
+    "kmamba_train_step": (C.c_float, [_PK, fp]),
+    "kmamba_train_batch": (C.c_float, [_PK, fp, C.c_size_t]),
+    "kmamba_train_batch_hybrid": (C.c_float, [_PK, fp, C.c_size_t]),
+    "kmamba_last_grad_norm": (C.c_float, [_PK]),
+    "kmamba_last_grad_over_clip": (C.c_float, [_PK]),
+    "kmamba_last_grad_would_clip": (C.c_int, [_PK]),
+    "kmamba_step_count": (C.c_size_t, [_PK]),
+    "kmamba_update_lr": (None, [_PK, C.c_float, C.c_float]),
+}
+
 # name -> (restype, argtypes)
 PROTOTYPES = {
     # runtime
@@ -149,13 +272,19 @@ def load(path: str = LIB_PATH):
     """Loads the library and declares every prototype.  Raises OSError when
     the library is missing (the product has no fallback)."""
     lib = C.CDLL(path)
-    for name, (res, args) in PROTOTYPES.items():
+    declare(lib)
+    return lib
+
+
+def declare(lib, table=None):
+    """Sets restype/argtypes of every known prototype present in `lib`
+    (also used for the reference library the tests load as the oracle)."""
+    for name, (res, args) in (table or {**PROTOTYPES, **MODEL_PROTOTYPES}).items():
         f = getattr(lib, name, None)
         if f is None:
             continue
         f.restype = res
         f.argtypes = args
-    return lib
 
 
 def last_error(lib) -> str:
@@ -166,3 +295,29 @@ def last_error(lib) -> str:
 def check(lib, status: int) -> None:
     if status != KMB_OK:
         raise RuntimeError(f"kmamba_b200 status {status}: {last_error(lib)}")
+
+
+def as_array(ptr, n):
+    """numpy view of n floats at a float* field (host memory)."""
+    import numpy as np
+    return np.ctypeslib.as_array(ptr, shape=(int(n),))
+
+
+def block_tensor(block, name):
+    """numpy view of one parameter of a MambaBlock (host arrays)."""
+    b = block.contents if hasattr(block, "contents") else block
+    c = b.config
+    R = max(int(c.mimo_rank), 1)
+    N, D = int(c.state_size), int(c.dim)
+    sizes = {"W_in": R * D, "W_out": D * R, "A_log": N, "W_B": N * R * D, "W_C": N * R * D,
+             "b_B": N * R, "b_C": N * R, "delta_proj": D, "lambda_proj": D,
+             "theta": max(N // 2, 1)}
+    f = getattr(b, name)
+    return as_array(f.data if isinstance(f, MBMatrix) else f, sizes[name])
+
+
+def block_state(block, prefix, name):
+    """numpy view of g_/m_/v_<name> of a block's optimizer state."""
+    b = block.contents if hasattr(block, "contents") else block
+    n = block_tensor(b, name).size
+    return as_array(getattr(b.opt_state.contents, f"{prefix}_{name}"), n)

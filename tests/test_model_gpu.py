@@ -1,0 +1,414 @@
+"""GPU parity of the block / model API (kmamba.h) through the C ABI.
+
+- config 1 (README model): logits, first-step loss and the updated head
+  against the reference's own CPU build (oracle/_ref);
+- block forward, block backward (d_input and every parameter gradient) and
+  a full multi-layer train_batch step against torch autograd of the
+  float64 restatement (oracle/block_ref.py, pinned to the reference forward
+  by the CPU tests); the reference has no block backward to compare with.
+
+Tolerance: rel_err (conftest) <= 1e-4 for forward values, <= 2e-4 for
+gradients (fp32 GPU against float64: long fp32 reductions over tokens and
+the reverse-time recurrence), and 1e-4 for optimizer updates.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import kmamba_b200 as kb
+import model_util as mu
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+
+FWD_TOL = 1e-4
+GRAD_TOL = 2e-4
+
+
+def delta_err(a1, a0, b1, b0=None):
+    """Relative error of a parameter update a1 - a0 against b1 - b0, with an
+    allowance of 4 fp32 ulps of the stored parameter per element (an fp32
+    parameter cannot hold its update more exactly)."""
+    a1, a0, b1 = (np.asarray(v, np.float64) for v in (a1, a0, b1))
+    b0 = a0 if b0 is None else np.asarray(b0, np.float64)
+    da, db = a1 - a0, b1 - b0
+    slack = 4 * 2.0 ** -24 * np.maximum(np.abs(a0), np.abs(a1))
+    tau = 1e-2 * float(np.max(np.abs(db))) + 1e-30
+    return float(np.max(np.maximum(np.abs(da - db) - slack, 0) / np.maximum(np.abs(db), tau)))
+
+
+@pytest.fixture(scope="module")
+def ref(oracle):
+    if not oracle.has_ref():
+        pytest.skip("reference library (oracle/_ref) not built")
+    return mu.declare_ref(oracle.ref_lib())
+
+
+@pytest.fixture(scope="module")
+def torch_mod():
+    import torch
+    return torch
+
+
+# ------------------------------------------------------------------ config 1
+
+
+def test_config1_forward_matches_reference(lib, ref, cuda):
+    ours = mu.new_model(lib, **mu.CFG1)
+    theirs = mu.new_model(ref, **mu.CFG1)
+    toks = mu.libc_tokens(mu.CFG1["seq_len"] + 1, seed=0)
+    n = mu.CFG1["seq_len"] * mu.CFG1["vocab_size"]
+    a, b = np.zeros(n, np.float32), np.zeros(n, np.float32)
+    try:
+        assert lib.kmamba_forward(ours, toks.ctypes.data, a.ctypes.data) == 0, kb.last_error(lib)
+        assert ref.kmamba_forward(theirs, toks.ctypes.data, b.ctypes.data) == 0
+        assert rel_err(a, b) <= FWD_TOL
+        assert float(a.astype(np.float64).sum()) == pytest.approx(mu.CFG1_SUM_LOGITS, rel=1e-4)
+    finally:
+        lib.kmamba_free(ours)
+        ref.kmamba_free(theirs)
+
+
+def test_config1_train_step_matches_reference(lib, ref, cuda):
+    """Loss of the first step, and the head after it.  eps = 1 makes the
+    AdamW step linear enough in the gradient for a relative comparison (at
+    step 1 with eps = 0 it is lr * sign(g))."""
+    ours = mu.new_model(lib, **mu.CFG1)
+    theirs = mu.new_model(ref, **mu.CFG1)
+    toks = mu.libc_tokens(mu.CFG1["seq_len"] + 1, seed=0)
+    o = mu.opt(lr=1e-2, clip_norm=1.0, eps=1.0)
+    try:
+        for L_, m in ((lib, ours), (ref, theirs)):
+            assert L_.kmamba_enable_training(m, C.byref(o), 1e-3, 1e-5) == 0
+        h0 = mu.model_arrays(ours)["head"].copy()
+        la = lib.kmamba_train_step(ours, toks.ctypes.data)
+        lb = ref.kmamba_train_step(theirs, toks.ctypes.data)
+        assert np.isfinite(la), kb.last_error(lib)
+        assert la == pytest.approx(lb, rel=1e-5)
+        assert la == pytest.approx(mu.CFG1_LOSS, rel=1e-5)
+        ha, hb = mu.model_arrays(ours)["head"], mu.model_arrays(theirs)["head"]
+        assert delta_err(ha, h0, hb) <= FWD_TOL
+        assert lib.kmamba_step_count(ours) == 1
+        # dt_min = dt_max = 0 in this config: the block is the identity and
+        # its gradients are zero, exactly as in the reference
+        assert lib.kmamba_last_grad_norm(ours) == pytest.approx(
+            ref.kmamba_last_grad_norm(theirs), rel=1e-4)
+    finally:
+        lib.kmamba_free(ours)
+        ref.kmamba_free(theirs)
+
+
+# ------------------------------------------------------------------ block
+
+BLOCK_CASES = [
+    dict(dim=32, state=16, seq_len=24, rank=1, batch=3),
+    dict(dim=24, state=7, seq_len=17, rank=3, batch=2),
+    dict(dim=20, state=1, seq_len=9, rank=2, batch=1),
+    dict(dim=384, state=1024, seq_len=32, rank=1, batch=1),
+]
+
+
+def _block(lib, case, seed=3):
+    cfg = mu.mbconfig(case["dim"], case["state"], case["seq_len"], case["rank"])
+    b = lib.mamba_block_create(C.byref(cfg))
+    assert b
+    mu._libc.srand(seed)
+    lib.mamba_block_init(b)
+    mu.perturb_block(b, np.random.default_rng(seed))
+    return b, cfg
+
+
+def _torch_block(torch, b, cfg, x, requires_grad=False):
+    import block_ref
+    P = mu.block_params_torch(b, torch, requires_grad)
+    xt = torch.tensor(x, dtype=torch.float64, requires_grad=requires_grad)
+    out = block_ref.block_forward(xt, P, cfg.dt_min, cfg.dt_max, int(cfg.state_size),
+                                  max(int(cfg.mimo_rank), 1))
+    return out, xt, P
+
+
+@pytest.mark.parametrize("case", BLOCK_CASES, ids=lambda c: f"D{c['dim']}N{c['state']}R{c['rank']}")
+def test_block_forward(lib, cuda, torch_mod, case):
+    b, cfg = _block(lib, case)
+    try:
+        rng = np.random.default_rng(1)
+        x = rng.standard_normal((case["batch"], case["seq_len"], case["dim"])).astype(np.float32)
+        out = np.zeros_like(x)
+        lib.kmb_clear_error()
+        lib.mamba_block_forward(b, out.ctypes.data, x.ctypes.data, case["batch"])
+        assert lib.kmb_last_status() == 0, kb.last_error(lib)
+        want, _, _ = _torch_block(torch_mod, b, cfg, x)
+        assert rel_err(out - x, want.detach().numpy() - x) <= FWD_TOL
+    finally:
+        lib.mamba_block_free(b)
+
+
+@pytest.mark.parametrize("case", BLOCK_CASES, ids=lambda c: f"D{c['dim']}N{c['state']}R{c['rank']}")
+def test_block_backward(lib, cuda, torch_mod, case):
+    """mamba_backward on one sequence: d_input and the accumulated
+    parameter gradients against torch autograd in float64."""
+    torch = torch_mod
+    b, cfg = _block(lib, case)
+    lib.mamba_attach_optimizer(b, kb.OPTIMIZER_ADAMW, None)
+    try:
+        rng = np.random.default_rng(2)
+        L, D = case["seq_len"], case["dim"]
+        x = rng.standard_normal((L, D)).astype(np.float32)
+        dy = rng.standard_normal((L, D)).astype(np.float32)
+        dx = np.full_like(x, np.nan)
+        lib.kmb_clear_error()
+        lib.mamba_backward(b, dy.ctypes.data, x.ctypes.data, dx.ctypes.data, 0)
+        assert lib.kmb_last_status() == 0, kb.last_error(lib)
+        out, xt, P = _torch_block(torch, b, cfg, x[None], requires_grad=True)
+        (out[0] * torch.tensor(dy, dtype=torch.float64)).sum().backward()
+        assert rel_err(dx, xt.grad[0].numpy()) <= GRAD_TOL
+        g1 = {}
+        for n in kb.BLOCK_PARAMS:
+            got = g1[n] = kb.block_state(b, "g", n).copy()
+            if P[n].grad is None:  # theta with a single state: no pair to rotate
+                assert n == "theta" and case["state"] < 2
+                assert np.all(got == 0)
+                continue
+            assert rel_err(got, P[n].grad.numpy().reshape(-1)) <= GRAD_TOL, n
+        # a second call accumulates onto the gradients already there
+        lib.mamba_backward(b, dy.ctypes.data, x.ctypes.data, dx.ctypes.data, 0)
+        for n in kb.BLOCK_PARAMS:
+            np.testing.assert_allclose(kb.block_state(b, "g", n), 2 * g1[n], rtol=1e-5,
+                                       atol=1e-6 * float(np.max(np.abs(g1[n])) + 1e-30))
+    finally:
+        lib.mamba_block_free(b)
+
+
+def test_block_workspace_and_local_grads(lib, cuda, torch_mod):
+    """forward_ws leaves the last item's controls in the workspace;
+    backward_ws_local + local_grad_reduce equals backward into the block."""
+    torch = torch_mod
+    case = dict(dim=16, state=6, seq_len=11, rank=2, batch=2)
+    b, cfg = _block(lib, case)
+    lib.mamba_attach_optimizer(b, kb.OPTIMIZER_ADAMW, None)
+    ws = lib.mamba_block_workspace_create(b)
+    loc = lib.mamba_local_grad_alloc(b)
+    try:
+        rng = np.random.default_rng(4)
+        x = rng.standard_normal((2, 11, 16)).astype(np.float32)
+        out = np.zeros_like(x)
+        lib.mamba_block_forward_ws(b, ws, out.ctypes.data, x.ctypes.data, 2)
+        assert lib.kmb_last_status() == 0, kb.last_error(lib)
+        xl = torch.tensor(x[1], dtype=torch.float64)
+        P = mu.block_params_torch(b, torch)
+        dt = torch.clamp(torch.nn.functional.softplus(xl @ P["delta_proj"]), cfg.dt_min,
+                         cfg.dt_max)
+        Bw = xl @ P["W_B"].T + P["b_B"]
+        Cw = xl @ P["W_C"].T + P["b_C"]
+        w = ws.contents
+        assert rel_err(kb.as_array(w.delta, 11), dt.numpy()) <= FWD_TOL
+        assert rel_err(kb.as_array(w.scan_B, 11 * 12), Bw.numpy().reshape(-1)) <= FWD_TOL
+        assert rel_err(kb.as_array(w.scan_C, 11 * 12), Cw.numpy().reshape(-1)) <= FWD_TOL
+        assert np.all(np.isfinite(kb.as_array(w.scan_h, 6)))
+        dy = rng.standard_normal((11, 16)).astype(np.float32)
+        dx1, dx2 = np.zeros_like(dy), np.zeros_like(dy)
+        lib.mamba_zero_grads(b)
+        lib.mamba_backward_ws(b, ws, dy.ctypes.data, x[0].ctypes.data, dx1.ctypes.data, 0)
+        direct = {n: kb.block_state(b, "g", n).copy() for n in kb.BLOCK_PARAMS}
+        lib.mamba_zero_grads(b)
+        lib.mamba_backward_ws_local(b, ws, dy.ctypes.data, x[0].ctypes.data, dx2.ctypes.data, 0,
+                                    loc)
+        assert all(np.all(kb.block_state(b, "g", n) == 0) for n in kb.BLOCK_PARAMS)
+        lib.mamba_local_grad_reduce(b, loc)
+        np.testing.assert_array_equal(dx1, dx2)
+        for n in kb.BLOCK_PARAMS:
+            np.testing.assert_allclose(kb.block_state(b, "g", n), direct[n], rtol=1e-6,
+                                       atol=1e-7 * np.max(np.abs(direct[n])))
+        # grad sqnorm is the sum of squares of every gradient
+        sq = sum(float(np.sum(direct[n].astype(np.float64) ** 2)) for n in kb.BLOCK_PARAMS)
+        assert lib.mamba_block_grad_sqnorm(b) == pytest.approx(sq, rel=1e-5)
+    finally:
+        lib.mamba_local_grad_free(loc)
+        lib.mamba_block_workspace_free(ws)
+        lib.mamba_block_free(b)
+
+
+@pytest.mark.parametrize("otype", [kb.OPTIMIZER_ADAMW, kb.OPTIMIZER_MUON, kb.OPTIMIZER_SGD])
+def test_block_optimizer_step(lib, cuda, torch_mod, otype):
+    import block_ref
+    torch = torch_mod
+    case = dict(dim=12, state=6, seq_len=5, rank=2, batch=1)
+    b, cfg = _block(lib, case)
+    conf = mu.opt(lr=1e-2, mu=0.9, eps=1e-3, clip_norm=0.5, weight_decay=0.01)
+    lib.mamba_attach_optimizer(b, otype, C.byref(conf))
+    try:
+        rng = np.random.default_rng(9)
+        st = b.contents.opt_state.contents
+        p0, g, m0, v0 = {}, {}, {}, {}
+        # small gradients: Newton-Schulz without normalisation (the
+        # reference rule) only converges for singular values below sqrt(3)
+        gs = 0.02 if otype == kb.OPTIMIZER_MUON else 1.0
+        for n in kb.BLOCK_PARAMS:
+            p0[n] = kb.block_tensor(b, n).astype(np.float64)
+            g[n] = (gs * rng.standard_normal(p0[n].size)).astype(np.float32)
+            kb.block_state(b, "g", n)[:] = g[n]
+            if otype != kb.OPTIMIZER_SGD:
+                m0[n] = (0.1 * gs * rng.standard_normal(p0[n].size)).astype(np.float32)
+                kb.block_state(b, "m", n)[:] = m0[n]
+            if otype == kb.OPTIMIZER_ADAMW:
+                v0[n] = (0.01 * rng.random(p0[n].size)).astype(np.float32)
+                kb.block_state(b, "v", n)[:] = v0[n]
+        st.step = 2
+        lib.kmb_clear_error()
+        lib.mamba_optimizer_step(b, C.byref(conf))
+        assert lib.kmb_last_status() == 0, kb.last_error(lib)
+        assert st.step == 3
+        D, N, R = 12, 6, 2
+        mats = {"W_in": (R, D), "W_out": (D, R), "W_B": (N * R, D), "W_C": (N * R, D)}
+        for n in kb.BLOCK_PARAMS:
+            T = lambda a: torch.tensor(np.asarray(a, np.float64))  # noqa: E731
+            if otype == kb.OPTIMIZER_ADAMW:
+                p, m, v = block_ref.adamw(T(p0[n]), T(g[n]), T(m0[n]), T(v0[n]), 3, 1e-2, 1e-3,
+                                          0.01)
+                assert rel_err(kb.block_state(b, "v", n), v.numpy()) <= FWD_TOL, n
+            elif otype == kb.OPTIMIZER_MUON:
+                rc = mats.get(n, (None, None))
+                p, m = block_ref.muon(T(p0[n]), T(g[n]), T(m0[n]), 0.9, 1e-2, 0.5, *rc)
+            else:
+                p, m = T(p0[n]) - 1e-2 * T(g[n]), None
+            if m is not None:
+                assert rel_err(kb.block_state(b, "m", n), m.numpy()) <= FWD_TOL, n
+            assert delta_err(kb.block_tensor(b, n), p0[n], p.numpy()) <= 1e-4, n
+    finally:
+        lib.mamba_block_free(b)
+
+
+# ------------------------------------------------------------------ model
+
+
+@pytest.mark.parametrize("batch", [1, 3])
+def test_model_train_matches_autograd(lib, cuda, torch_mod, batch):
+    """One train_step (batch 1) / train_batch (batch 3) of a two-layer
+    model: loss, every block gradient left in opt_state, the grad norm, and
+    the AdamW-updated embedding / head / block weights against float64
+    autograd of the restatement followed by the reference AdamW rule."""
+    import block_ref
+    torch = torch_mod
+    V, D, N, L, NL = 48, 32, 12, 16, 2
+    cfg = dict(vocab_size=V, dim=D, state_size=N, seq_len=L, n_layers=NL, mimo_rank=1,
+               dt_min=1e-3, dt_max=0.3)
+    m = mu.new_model(lib, seed=21, **cfg)
+    conf = mu.opt(lr=1e-2, eps=1.0, clip_norm=1.0, weight_decay=0.01)
+    try:
+        rng = np.random.default_rng(5)
+        for i in range(NL):
+            mu.perturb_block(m.contents.layers[i], rng)
+        assert lib.kmamba_enable_training(m, C.byref(conf), 1e-3, 0.0) == 0
+        toks = rng.integers(0, V, size=(batch, L + 1)).astype(np.uint32)
+        arr0 = {k: v.copy() for k, v in mu.model_arrays(m).items()}
+        emb = torch.tensor(arr0["embedding"].reshape(V, D).astype(np.float64), requires_grad=True)
+        head = torch.tensor(arr0["head"].reshape(D, V).astype(np.float64), requires_grad=True)
+        blocks = [mu.block_params_torch(m.contents.layers[i], torch, True) for i in range(NL)]
+        loss_t, _ = block_ref.model_loss(torch.tensor(toks.astype(np.int64)), emb, head, blocks,
+                                         1e-3, 0.3, N, 1)
+        loss_t.backward()
+        if batch == 1:
+            loss = lib.kmamba_train_step(m, toks.ctypes.data)
+        else:
+            loss = lib.kmamba_train_batch(m, toks.ctypes.data, batch)
+        assert np.isfinite(loss), kb.last_error(lib)
+        assert loss == pytest.approx(float(loss_t), rel=1e-5)
+        gsq = float((emb.grad ** 2).sum() + (head.grad ** 2).sum())
+        for i in range(NL):
+            blk = m.contents.layers[i]
+            for n in kb.BLOCK_PARAMS:
+                want = blocks[i][n].grad.numpy().reshape(-1)
+                gsq += float((want ** 2).sum())
+                assert rel_err(kb.block_state(blk, "g", n), want) <= GRAD_TOL, (i, n)
+        assert lib.kmamba_last_grad_norm(m) == pytest.approx(np.sqrt(gsq), rel=1e-4)
+        # AdamW step 1 with eps = 1: p' = p (1 - lr wd) - lr g / (|g| + 1)
+        # (eps = 1 keeps the update linear enough in g for a relative check)
+        T = lambda a: torch.tensor(np.asarray(a, np.float64))  # noqa: E731
+        checks = [("embedding", emb.grad), ("head", head.grad)]
+        checks += [(f"{i}.{n}", blocks[i][n].grad) for i in range(NL) for n in kb.BLOCK_PARAMS]
+        arr1 = mu.model_arrays(m)
+        for k, gr in checks:
+            p0 = T(arr0[k])
+            z = torch.zeros_like(p0)
+            p1, _, _ = block_ref.adamw(p0, gr.reshape(-1), z, z, 1, 1e-2, 1.0, 0.01)
+            assert delta_err(arr1[k], arr0[k], p1.numpy()) <= GRAD_TOL, k
+        assert lib.kmamba_step_count(m) == 1
+    finally:
+        lib.kmamba_free(m)
+
+
+def test_model_weight_tying_and_save_after_training(lib, cuda, tmp_path):
+    V, D = 40, 40
+    m = mu.new_model(lib, seed=3, vocab_size=V, dim=D, state_size=8, seq_len=12, n_layers=1,
+                     dt_min=1e-3, dt_max=0.2, weight_tying=1)
+    try:
+        assert C.cast(m.contents.head, C.c_void_p).value == \
+            C.cast(m.contents.embedding, C.c_void_p).value
+        assert lib.kmamba_enable_training(m, C.byref(mu.opt(lr=1e-3, eps=1e-6)), 1e-3, 0.0) == 0
+        toks = np.random.default_rng(0).integers(0, V, 13).astype(np.uint32)
+        l0 = lib.kmamba_train_step(m, toks.ctypes.data)
+        for _ in range(5):
+            l1 = lib.kmamba_train_step(m, toks.ctypes.data)
+        assert np.isfinite(l0) and np.isfinite(l1) and l1 < l0
+        p = str(tmp_path / "tied.kmamba")
+        assert lib.kmamba_save(m, p.encode()) == 0
+        m2 = lib.kmamba_load(p.encode(), 0, None, 0.0, 0.0)
+        assert m2
+        la, lb = np.zeros(12 * V, np.float32), np.zeros(12 * V, np.float32)
+        assert lib.kmamba_forward(m, toks.ctypes.data, la.ctypes.data) == 0
+        assert lib.kmamba_forward(m2, toks.ctypes.data, lb.ctypes.data) == 0
+        # the loaded model is untied (the file stores head separately) but
+        # holds the same values
+        np.testing.assert_array_equal(la, lb)
+        lib.kmamba_free(m2)
+    finally:
+        lib.kmamba_free(m)
+
+
+def test_model_rejects_bad_targets(lib, cuda):
+    m = mu.new_model(lib, vocab_size=16, dim=8, state_size=4, seq_len=6, n_layers=1)
+    try:
+        assert lib.kmamba_enable_training(m, C.byref(mu.opt(lr=1e-3)), 1e-3, 0.0) == 0
+        toks = np.array([1, 2, 3, 99, 4, 5, 6], np.uint32)
+        assert np.isnan(lib.kmamba_train_step(m, toks.ctypes.data))
+        assert "vocab" in kb.last_error(lib)
+        assert lib.kmamba_step_count(m) == 0
+    finally:
+        lib.kmamba_free(m)
+
+
+def test_matrix_helpers(lib, cuda):
+    rng = np.random.default_rng(3)
+    M = lib.mb_matrix_create(7, 5)
+    try:
+        a = kb.as_array(M.contents.data, 35)
+        a[:] = rng.standard_normal(35).astype(np.float32)
+        v = rng.standard_normal(5).astype(np.float32)
+        out = np.zeros(7, np.float32)
+        lib.mb_matrix_vec_mult(out.ctypes.data, M, v.ctypes.data)
+        np.testing.assert_allclose(out, a.reshape(7, 5) @ v, rtol=1e-5, atol=1e-6)
+        y = rng.standard_normal(9).astype(np.float32)
+        x = rng.standard_normal(9).astype(np.float32)
+        want = y + x
+        lib.mb_vec_add(y.ctypes.data, x.ctypes.data, 9)
+        np.testing.assert_allclose(y, want, rtol=1e-6)
+        lib.mb_vec_scale(y.ctypes.data, C.c_float(-2.0), 9)
+        np.testing.assert_allclose(y, -2 * want, rtol=1e-6)
+        lib.mb_matrix_zero(M)
+        assert np.all(a == 0)
+    finally:
+        lib.mb_matrix_free(M)
+    cfg = mu.mbconfig(8, 4, 6, dt_min=0.01, dt_max=0.5)
+    b = lib.mamba_block_create(C.byref(cfg))
+    try:
+        lib.mamba_block_init(b)
+        dp = kb.block_tensor(b, "delta_proj")
+        dp[:] = rng.standard_normal(8).astype(np.float32)
+        xin = rng.standard_normal((6, 8)).astype(np.float32)
+        d = np.zeros(6, np.float32)
+        lib.mb_compute_delta(d.ctypes.data, b, xin.ctypes.data, 6)
+        want = np.clip(np.log1p(np.exp(xin.astype(np.float64) @ dp)), 0.01, 0.5)
+        np.testing.assert_allclose(d, want, rtol=1e-5)
+    finally:
+        lib.mamba_block_free(b)
