@@ -275,7 +275,7 @@ def run_secondary(args):
     rng = np.random.default_rng(7)
     dev = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=f)).cuda()  # noqa: E731
     if args.workload == "conv3":
-        bsz, H, W, Dc, K = (args.batch if args.batch != BATCH else 16), 512, 512, 64, 3
+        bsz, H, W, Dc, K = (args.batch or 16), 512, 512, 64, 3
         Pn = H * W
         E3 = bsz * Pn * Dc
         fwd_b, bwd_b = 4 * (2 * E3 + 640), 4 * (3 * E3 + 1280)
@@ -296,7 +296,7 @@ def run_secondary(args):
         workload = f"config3: ConvND 2D 512x512, D 64, K 3, batch {bsz}, fp32, fwd+bwd"
         metric = "ConvND HBM GB/s (algorithmic bytes / device time)"
     else:
-        bsz, H, W, Dc, Nn = (args.batch if args.batch != BATCH else 8), 256, 256, 256, 16
+        bsz, H, W, Dc, Nn = (args.batch or 8), 256, 256, 256, 16
         Pn = H * W
         E4 = bsz * Pn * Dc
         fwd_b = 4 * (3 * E4 + 2 * bsz * Pn * Nn + 2 * Dc * Nn)
@@ -366,6 +366,108 @@ def run_secondary(args):
 
 
 # --------------------------------------------------------------------------
+# config 1: the README KMamba model through kmamba.h
+# --------------------------------------------------------------------------
+
+MODEL1_CFG = dict(vocab_size=256, dim=384, state_size=1024, seq_len=128, n_layers=1)
+MODEL1_WORKLOAD = ("config1: KMamba LM (vocab 256, dim 384, state 1024, seq_len 128, 1 layer, "
+                   "kmamba_init(1234), tokens srand(0) rand()%256), one kmamba_forward + one "
+                   "kmamba_train_step per step, lr 1e-3, clip_norm 1.0, host token/logit "
+                   "buffers through the C API")
+
+
+def _model1(libm):
+    """Builds the config-1 model with `libm` (ours or the reference's)."""
+    import kmamba_b200 as kb
+    cfg = kb.KMambaConfig()
+    for k, v in MODEL1_CFG.items():
+        setattr(cfg, k, v)
+    m = libm.kmamba_create(C.byref(cfg))
+    libm.kmamba_init(m, 1234)
+    o = kb.MBOptimConfig()
+    o.lr, o.clip_norm = 1e-3, 1.0
+    libm.kmamba_enable_training(m, C.byref(o), 1e-3, 1e-5)
+    libc = C.CDLL(None)
+    libc.srand(0)
+    toks = np.array([libc.rand() % 256 for _ in range(129)], dtype=np.uint32)
+    logits = np.zeros(128 * 256, np.float32)
+    return m, toks, logits
+
+
+def _model1_step(libm, m, toks, logits):
+    libm.kmamba_forward(m, toks.ctypes.data, logits.ctypes.data)
+    return libm.kmamba_train_step(m, toks.ctypes.data)
+
+
+def _model1_cpu(steps):
+    """ms per step of the reference's own CPU build (oracle/_ref), all host
+    threads (OpenMP inside its GEMMs)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as o
+    import kmamba_b200 as kb
+    ref = o.ref_lib()
+    if ref is None:
+        return None
+    kb.declare(ref, kb.MODEL_PROTOTYPES)
+    m, toks, logits = _model1(ref)
+    _model1_step(ref, m, toks, logits)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        _model1_step(ref, m, toks, logits)
+    ms = (time.perf_counter() - t0) / steps * 1e3
+    ref.kmamba_free(m)
+    return ms
+
+
+def run_model1(args):
+    """Times config 1: one kmamba_forward + one kmamba_train_step per step
+    through the C API with host buffers (the API's own contract: tokens and
+    logits in host memory, weights and Adam moments in the host structs,
+    staged to the device by every call).  value = ms per step, host wall
+    clock around the synchronous calls; device_ms = CUDA-event time on the
+    library stream over the same steps."""
+    import torch
+    import kmamba_b200 as kb
+    lib = kb.load()
+    stream = torch.cuda.current_stream()
+    lib.kmb_set_stream(C.c_void_p(stream.cuda_stream))
+    lib.kmb_set_sync(1)
+    m, toks, logits = _model1(lib)
+    for _ in range(args.warmup):
+        _model1_step(lib, m, toks, logits)
+    torch.cuda.synchronize()
+    n0 = lib.kmb_block_launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(0) as clk:
+        e0.record(stream)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            _model1_step(lib, m, toks, logits)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        wall = (time.perf_counter() - t0) / args.steps * 1e3
+    dev_ms = e0.elapsed_time(e1) / args.steps
+    launches = lib.kmb_block_launch_count() - n0
+    lib.kmamba_free(m)
+    cpu = None if args.no_cpu_baseline else _model1_cpu(3)
+    V, L = 256, 128
+    h2d = 4 * (129 + 129)  # tokens of forward + train_step (weights: see staged_bytes)
+    print(json.dumps({
+        "metric": "KMamba config-1 step time (kmamba_forward + kmamba_train_step)",
+        "value": wall, "unit": "ms/step", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": wall, "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": MODEL1_WORKLOAD, "device_ms_per_step": dev_ms,
+                   "l2": "working set < L2 (the config is small); weights restaged per call"},
+        "e2e": {"value": wall, "unit": "ms/step", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": 4 * (L * V + L)},
+        "cpu_baseline": None if cpu is None else {
+            "value": cpu, "unit": "ms/step", "cores": os.cpu_count(), "kind": "reference",
+            "sample": "3 steps of the same workload, reference CPU build (OpenMP)"},
+        "gpu_launches": int(launches), "clocks": clk.summary()}), flush=True)
+
+
+# --------------------------------------------------------------------------
 # GPU arm
 # --------------------------------------------------------------------------
 
@@ -377,15 +479,21 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--batch", type=int, default=BATCH,
-                    help="batch items per GPU (profiling of small cases only)")
-    ap.add_argument("--workload", default="scan1d", choices=["scan1d", "conv3", "scan2d4"],
+    ap.add_argument("--batch", type=int, default=None,
+                    help="batch items per GPU (profiling of small cases only; default: "
+                         "the workload's BASELINE batch)")
+    ap.add_argument("--workload", default="scan1d",
+                    choices=["scan1d", "conv3", "scan2d4", "model1"],
                     help="scan1d = BASELINE config 2 (the headline); conv3 / scan2d4 time "
                          "configs 3 and 4 for their roofline evidence")
     args = ap.parse_args()
-    set_batch(args.batch)
+    if args.batch is not None and args.workload == "scan1d":
+        set_batch(args.batch)
     if args.impl == "reference":
         run_reference_arm(args)
+        return
+    if args.workload == "model1":
+        run_model1(args)
         return
     if args.workload != "scan1d":
         run_secondary(args)

@@ -48,6 +48,10 @@ size_t kmb_pool_trim(void);
 /* Bytes currently held from cudaMalloc (in use + cached). */
 size_t kmb_pool_bytes_held(void);
 
+/* Number of kernels the block / model path (kmamba.h) has launched in
+ * this process, for measurement.  No reference counterpart. */
+unsigned long long kmb_block_launch_count(void);
+
 /* ------------------------------------------------------------------ */
 /* Batched 1D selective scan                                           */
 /* ------------------------------------------------------------------ */

@@ -525,7 +525,15 @@ unsigned grid1d(long n) {
     return (unsigned)(b < 1 ? 1 : b);
 }
 
+unsigned long long g_launches = 0; /* kernels launched by this file */
+
+inline void count_launch() { __atomic_fetch_add(&g_launches, 1ULL, __ATOMIC_RELAXED); }
+
 } // namespace
+
+extern "C" unsigned long long kmb_block_launch_count(void) {
+    return __atomic_load_n(&g_launches, __ATOMIC_RELAXED);
+}
 
 extern "C" int kmb_gemm(int M, int N, int K, const float *A, long am, long ak, const float *B,
                         long bk, long bn, float *C, long ldc, int accumulate, cudaStream_t s) {
@@ -540,6 +548,7 @@ extern "C" int kmb_gemm(int M, int N, int K, const float *A, long am, long ak, c
         return KMB_OK;
     }
     dim3 grid((unsigned)((N + kTN - 1) / kTN), (unsigned)((M + kTM - 1) / kTM));
+    count_launch();
     k_gemm<<<grid, 256, 0, s>>>(M, N, K, A, am, ak, B, bk, bn, C, ldc, accumulate);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "gemm launch");
@@ -550,14 +559,20 @@ extern "C" int kmb_block_act(const float *zraw, float *zact, const float *bB, co
                              int has_dp, int has_lp, float dt_scale, float *dz_inplace,
                              cudaStream_t s) {
     ActArgs a{zraw, zact, bB, bC, rows, W, R, NR, dt_min, dt_max, has_dp, has_lp, dt_scale};
-    if (dz_inplace) k_block_act_bwd<<<grid1d(rows * W), 256, 0, s>>>(a, dz_inplace);
-    else k_block_act<<<grid1d(rows * W), 256, 0, s>>>(a);
+    if (dz_inplace) {
+        count_launch();
+        k_block_act_bwd<<<grid1d(rows * W), 256, 0, s>>>(a, dz_inplace);
+    } else {
+        count_launch();
+        k_block_act<<<grid1d(rows * W), 256, 0, s>>>(a);
+    }
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "block activation launch");
 }
 
 extern "C" int kmb_colsum_acc(const float *dz, long rows, int W, int c0, int ncols, float *out,
                               cudaStream_t s) {
+    count_launch();
     k_colsum_acc<<<(unsigned)((ncols + 127) / 128), 128, 0, s>>>(dz, rows, W, c0, ncols, out);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "colsum launch");
@@ -574,22 +589,33 @@ extern "C" int kmb_m3_scan(int batch, int L, int N, int R, int W, const float *z
     const int threads = ((npairs + 31) / 32) * 32;
     if (dy && !h_hist) return kmb_fail(KMB_EINVAL, "block scan backward needs the state history");
     ScanArgs a{zact, A, theta, h_hist, h_last, y, dy, dz, dA, dtheta, L, N, R, W};
-    if (dy) k_m3_scan_bwd<<<batch, threads, 0, s>>>(a);
-    else k_m3_scan_fwd<<<batch, threads, 0, s>>>(a);
+    if (dy) {
+        count_launch();
+        k_m3_scan_bwd<<<batch, threads, 0, s>>>(a);
+    } else {
+        count_launch();
+        k_m3_scan_fwd<<<batch, threads, 0, s>>>(a);
+    }
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "block scan launch");
 }
 
 extern "C" int kmb_embed(const float *emb, const unsigned *tok, long L, long D, long V,
                          float *out, const float *dx_for_grad, float *gemb, cudaStream_t s) {
-    if (gemb) k_embed_scatter<<<grid1d(L * D), 256, 0, s>>>(dx_for_grad, tok, L, D, V, gemb);
-    else k_embed_gather<<<grid1d(L * D), 256, 0, s>>>(emb, tok, L, D, V, out);
+    if (gemb) {
+        count_launch();
+        k_embed_scatter<<<grid1d(L * D), 256, 0, s>>>(dx_for_grad, tok, L, D, V, gemb);
+    } else {
+        count_launch();
+        k_embed_gather<<<grid1d(L * D), 256, 0, s>>>(emb, tok, L, D, V, out);
+    }
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "embedding launch");
 }
 
 extern "C" int kmb_softmax_ce(const float *logits, const unsigned *tgt, long L, long V,
                               float *dlogits, float *row_loss, cudaStream_t s) {
+    count_launch();
     k_softmax_ce<<<(unsigned)L, 256, 0, s>>>(logits, tgt, V, 1.0f / (float)L, dlogits, row_loss);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "softmax-ce launch");
@@ -599,6 +625,7 @@ extern "C" int kmb_adamw(float *p, const float *g, float *m, float *v, long n, f
                          float b1, float b2, float eps, float wd, float bc1, float bc2,
                          cudaStream_t s) {
     if (n <= 0) return KMB_OK;
+    count_launch();
     k_adamw<<<grid1d(n), 256, 0, s>>>(p, g, m, v, n, lr, b1, b2, eps, wd, bc1, bc2);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "adamw launch");
@@ -606,6 +633,7 @@ extern "C" int kmb_adamw(float *p, const float *g, float *m, float *v, long n, f
 
 extern "C" int kmb_sumsq(const float *x, long n, double *out, cudaStream_t s) {
     if (n <= 0) return KMB_OK;
+    count_launch();
     k_sumsq<<<grid1d(n), 256, 0, s>>>(x, n, out);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "sumsq launch");
@@ -619,6 +647,7 @@ extern "C" int kmb_sumsq(const float *x, long n, double *out, cudaStream_t s) {
 
 extern "C" int kmb_axpby(float *y, const float *x, long n, float a, float b, cudaStream_t s) {
     if (n <= 0) return KMB_OK;
+    count_launch();
     k_axpby<<<grid1d(n), 256, 0, s>>>(y, x, n, a, b);
     KMB_ELEMWISE_RET("axpby launch");
 }
@@ -626,18 +655,21 @@ extern "C" int kmb_axpby(float *y, const float *x, long n, float a, float b, cud
 extern "C" int kmb_dt_act(const float *z, float *out, long n, float dt_min, float dt_max,
                           cudaStream_t s) {
     if (n <= 0) return KMB_OK;
+    count_launch();
     k_dt_act<<<grid1d(n), 256, 0, s>>>(z, out, n, dt_min, dt_max);
     KMB_ELEMWISE_RET("dt activation launch");
 }
 
 extern "C" int kmb_momentum(float *m, const float *g, long n, float mu, cudaStream_t s) {
     if (n <= 0) return KMB_OK;
+    count_launch();
     k_momentum<<<grid1d(n), 256, 0, s>>>(m, g, n, mu);
     KMB_ELEMWISE_RET("momentum launch");
 }
 
 extern "C" int kmb_ns_combine(float *G, const float *T, long n, cudaStream_t s) {
     if (n <= 0) return KMB_OK;
+    count_launch();
     k_ns_combine<<<grid1d(n), 256, 0, s>>>(G, T, n);
     KMB_ELEMWISE_RET("newton-schulz launch");
 }
@@ -645,6 +677,7 @@ extern "C" int kmb_ns_combine(float *G, const float *T, long n, cudaStream_t s) 
 extern "C" int kmb_scaled_sub(float *p, const float *x, long n, float lr, float clip,
                               const double *sumsq, cudaStream_t s) {
     if (n <= 0) return KMB_OK;
+    count_launch();
     k_scaled_sub<<<grid1d(n), 256, 0, s>>>(p, x, n, lr, clip, sumsq);
     KMB_ELEMWISE_RET("scaled update launch");
 }

@@ -220,6 +220,7 @@ PROTOTYPES = {
     "kmb_pool_free": (None, [C.c_void_p]),
     "kmb_pool_trim": (C.c_size_t, []),
     "kmb_pool_bytes_held": (C.c_size_t, []),
+    "kmb_block_launch_count": (C.c_ulonglong, []),
     # 1D scan
     "kmb_scan1d_ckpt_elems": (lg, [lg, lg, lg, lg]),
     "kmb_scan1d_fwd": (C.c_int, [C.POINTER(KmbScan1D)]),

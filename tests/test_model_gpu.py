@@ -90,10 +90,42 @@ def test_config1_train_step_matches_reference(lib, ref, cuda):
         ha, hb = mu.model_arrays(ours)["head"], mu.model_arrays(theirs)["head"]
         assert delta_err(ha, h0, hb) <= FWD_TOL
         assert lib.kmamba_step_count(ours) == 1
-        # dt_min = dt_max = 0 in this config: the block is the identity and
-        # its gradients are zero, exactly as in the reference
-        assert lib.kmamba_last_grad_norm(ours) == pytest.approx(
-            ref.kmamba_last_grad_norm(theirs), rel=1e-4)
+    finally:
+        lib.kmamba_free(ours)
+        ref.kmamba_free(theirs)
+
+
+def test_config1_grad_norm(lib, ref, cuda, torch_mod):
+    """dt_min = dt_max = 0 in config 1, so dt is clamped to 0 and the block
+    is the identity with zero parameter gradients.  The residual still
+    carries the loss gradient to the embedding: ours includes it, the
+    reference's empty block backward drops it (its norm is the head
+    gradient alone).  Both against float64 autograd."""
+    import block_ref
+    torch = torch_mod
+    ours = mu.new_model(lib, **mu.CFG1)
+    theirs = mu.new_model(ref, **mu.CFG1)
+    toks = mu.libc_tokens(mu.CFG1["seq_len"] + 1, seed=0)
+    o = mu.opt(lr=1e-3, clip_norm=1.0, eps=1e-8)
+    try:
+        arr = mu.model_arrays(ours)
+        V, D = mu.CFG1["vocab_size"], mu.CFG1["dim"]
+        emb = torch.tensor(arr["embedding"].reshape(V, D).astype(np.float64), requires_grad=True)
+        head = torch.tensor(arr["head"].reshape(D, V).astype(np.float64), requires_grad=True)
+        blk = mu.block_params_torch(ours.contents.layers[0], torch, True)
+        loss, _ = block_ref.model_loss(torch.tensor(toks.astype(np.int64))[None], emb, head,
+                                       [blk], 0.0, 0.0, mu.CFG1["state_size"], 1)
+        loss.backward()
+        gh = float(torch.sqrt((head.grad ** 2).sum()))
+        ge = float(torch.sqrt((emb.grad ** 2).sum()))
+        assert all(blk[n].grad is None or float(blk[n].grad.abs().max()) == 0.0 for n in blk)
+        for L_, m in ((lib, ours), (ref, theirs)):
+            assert L_.kmamba_enable_training(m, C.byref(o), 1e-3, 1e-5) == 0
+            assert np.isfinite(L_.kmamba_train_step(m, toks.ctypes.data))
+        assert ref.kmamba_last_grad_norm(theirs) == pytest.approx(gh, rel=1e-4)
+        assert lib.kmamba_last_grad_norm(ours) == pytest.approx(np.hypot(gh, ge), rel=1e-4)
+        assert lib.kmamba_last_grad_over_clip(ours) == pytest.approx(np.hypot(gh, ge), rel=1e-4)
+        assert lib.kmamba_last_grad_would_clip(ours) == int(np.hypot(gh, ge) > 1.0)
     finally:
         lib.kmamba_free(ours)
         ref.kmamba_free(theirs)
