@@ -452,7 +452,6 @@ template <int P, bool SHARED, bool VEC, bool HALL, bool CLAMP>
 __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
     constexpr int DT = kNT / P;
     constexpr int T = kChunk;
-    constexpr int NW = kNT / 32;
     constexpr int NP = kG * P;
     /* steps per dx/ddt reduce-scatter group (2 values per step, one value
      * per lane of the channel; slots past 2*S are zero when P > 2*T) */
@@ -463,7 +462,6 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
 
     const int tid = threadIdx.x;
     const int lane = tid & 31;
-    const int warp = tid >> 5;
     const int g = tid % P;
     const int dl = tid / P;
     const int n0 = g * kG;
@@ -479,8 +477,13 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
     const int BWr = bc_row_stride(SHARED, NP, N);
     const int xs_sz = T * DT;
     const int bs_sz = T * BWr;
-    const int stage_sz = 3 * xs_sz + 2 * bs_sz;
-    float *part = smem + 2 * stage_sz; /* [T][NW][2*NP], SHARED only */
+    const int ck_sz = HALL ? 0 : DT * NP; /* checkpointed chunk-start states [DT][NP] */
+    const int stage_sz = 3 * xs_sz + 2 * bs_sz + ck_sz;
+    /* per-thread dB / dC contributions of the chunk, [T][DT][NP] each
+     * (SHARED only): thread (dl, g) writes 16 bytes at 16 * tid, so the
+     * 128-bit stores are conflict-free; folded once per chunk */
+    float *partB = smem + 2 * stage_sz;
+    float *partC = partB + T * DT * NP;
 
     float A2[kG], Ar[kG], gc[kG], dAacc[kG];
 #pragma unroll
@@ -520,6 +523,13 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
             kmb_load_tile<kNT>(st + 3 * xs_sz + bs_sz, BWr, Cg + t0 * bld, bld, T, bcols, rv,
                                bvalid, vbc, tid);
         }
+        if (!HALL && c > 0) {
+            /* the forward's checkpoint of the state before this chunk: the
+             * CTA's DT channels x N states are contiguous */
+            const float *src = p.ckpt_in + ((b * p.nslots + c - 1) * D + d0) * N;
+            kmb_load_tile<kNT>(st + 3 * xs_sz + 2 * bs_sz, NP, src, N, DT, NP, dvalid, N,
+                               VEC, tid);
+        }
     };
 
     load(nch - 1, 0);
@@ -549,10 +559,19 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
         /* state before the chunk's first step */
         float hs[kG];
         if (c > 0) {
-            const float *src = HALL ? hall + (t0 - 1) * hstride
-                                    : p.ckpt_in + ((b * p.nslots + c - 1) * D + d) * N + n0;
-            if (dok) ldg4<VEC>(src, gok, N, n0, hs);
-            else hs[0] = hs[1] = hs[2] = hs[3] = 0.f;
+            if (HALL) {
+                if (dok) ldg4<VEC>(hall + (t0 - 1) * hstride, gok, N, n0, hs);
+                else hs[0] = hs[1] = hs[2] = hs[3] = 0.f;
+            } else {
+                /* zero-filled past N and for channels past D */
+                const float *ck = st + 3 * xs_sz + 2 * bs_sz + dl * NP + n0;
+                if (VEC) {
+                    lds4u(ck, hs);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < kG; ++j) hs[j] = ck[j];
+                }
+            }
         } else {
 #pragma unroll
             for (int j = 0; j < kG; ++j)
@@ -654,18 +673,9 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
                     rv[2 * s] = dxs;
                     rv[2 * s + 1] = fmaf(xv, dxs, dts);
                     if (SHARED) {
-                        int base, cnt, dup;
-                        reduce_scatter8<P>(v, lane, base, cnt, dup);
-                        if ((lane & dup) == 0) {
-                            float *prow = part + (i * NW + warp) * (2 * NP);
-#pragma unroll
-                            for (int k = 0; k < 8; ++k) {
-                                if (k < cnt) {
-                                    const int idx = base + k;
-                                    prow[(idx >> 2) * NP + n0 + (idx & 3)] = v[k];
-                                }
-                            }
-                        }
+                        const int o = (i * DT + dl) * NP + n0;
+                        *reinterpret_cast<float4 *>(partB + o) = make_float4(v[0], v[1], v[2], v[3]);
+                        *reinterpret_cast<float4 *>(partC + o) = make_float4(v[4], v[5], v[6], v[7]);
                     } else if (dok) {
                         float vb[kG] = {v[0], v[1], v[2], v[3]};
                         float vc[kG] = {v[4], v[5], v[6], v[7]};
@@ -697,29 +707,51 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
 
         if (SHARED) {
             __syncthreads();
-            /* 4 consecutive states per thread: one 128-bit atomic each */
-            constexpr int Q = 2 * NP / 4;
-            const int tot = len * Q;
-            for (int e = tid; e < tot; e += kNT) {
-                const int i = e / Q;
-                const int r = (e - i * Q) * 4;   /* index in [0, 2*NP) */
-                const int n = r % NP;
-                if (n < N) {
-                    float s4[4] = {0.f, 0.f, 0.f, 0.f};
+            /* channel sums of the chunk's dB / dC: HR threads per 4-state
+             * output, each summing every HR-th channel (interleaved so that
+             * a quarter-warp reads adjacent rows), folded by shuffles; one
+             * 128-bit atomic per output and CTA */
+            constexpr int NQ = NP / 4;
+            constexpr int HR = NP >= 32 ? 1 : 32 / NP;
+            constexpr int OUTS = 2 * T * NQ;
+            constexpr int ITER = (OUTS * HR + kNT - 1) / kNT;
 #pragma unroll
-                    for (int w = 0; w < NW; ++w) {
-                        const float *src = part + (i * NW + w) * (2 * NP) + r;
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) s4[k] += src[k];
+            for (int r = 0; r < ITER; ++r) {
+                const int e = r * kNT + tid;
+                const int o = e / HR, hh = e % HR;
+                const int arr = o / (T * NQ);
+                const int i = (o % (T * NQ)) / NQ;
+                const int q = o % NQ;
+                const bool live = o < OUTS && i < len && q * 4 < N;
+                float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (live) {
+                    const float *src = (arr ? partC : partB) + i * DT * NP + q * 4;
+#pragma unroll 8
+                    for (int k = 0; k < DT / HR; ++k) {
+                        const int dlx = k * HR + hh;
+                        if (dlx < dvalid) {
+                            const float4 t4 = *reinterpret_cast<const float4 *>(src + dlx * NP);
+                            s4.x += t4.x; s4.y += t4.y; s4.z += t4.z; s4.w += t4.w;
+                        }
                     }
-                    float *dst = ((r < NP) ? p.dB : p.dC) + (b * L + t0 + i) * N + n;
+                }
+#pragma unroll
+                for (int m = HR / 2; m > 0; m >>= 1) {
+                    s4.x += __shfl_xor_sync(kFull, s4.x, m);
+                    s4.y += __shfl_xor_sync(kFull, s4.y, m);
+                    s4.z += __shfl_xor_sync(kFull, s4.z, m);
+                    s4.w += __shfl_xor_sync(kFull, s4.w, m);
+                }
+                if (live && hh == 0) {
+                    const int n = q * 4;
+                    float *dst = (arr ? p.dC : p.dB) + (b * L + t0 + i) * N + n;
                     if (VEC && vbc) {
-                        atomicAdd(reinterpret_cast<float4 *>(dst),
-                                  make_float4(s4[0], s4[1], s4[2], s4[3]));
+                        atomicAdd(reinterpret_cast<float4 *>(dst), s4);
                     } else {
+                        const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
                         for (int k = 0; k < 4; ++k)
-                            if (n + k < N) atomicAdd(dst + k, s4[k]);
+                            if (n + k < N) atomicAdd(dst + k, sv[k]);
                     }
                 }
             }
@@ -816,8 +848,9 @@ template <int P, bool SHARED, bool VEC, bool HALL, bool CLAMP>
 cudaError_t launch_bwd_t(const Scan1DDev &p, long batch, cudaStream_t s) {
     constexpr int DT = kNT / P;
     const int BWr = bc_row_stride(SHARED, kG * P, (int)p.N);
-    size_t smem = sizeof(float) * 2 * (3 * kChunk * DT + 2 * kChunk * BWr);
-    if (SHARED) smem += sizeof(float) * kChunk * (kNT / 32) * 2 * (kG * P);
+    const int ck = HALL ? 0 : DT * kG * P;
+    size_t smem = sizeof(float) * 2 * (3 * kChunk * DT + 2 * kChunk * BWr + ck);
+    if (SHARED) smem += sizeof(float) * 2 * kChunk * DT * (kG * P);
     auto kern = k_scan1d_bwd<P, SHARED, VEC, HALL, CLAMP>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
