@@ -40,6 +40,28 @@ __device__ __forceinline__ float kmb_exp2_decay(float w) {
     return fabsf(w) < 0.0625f ? p : m;
 }
 
+/* Packed fp32 pairs (sm_100 FFMA2 / FMUL2 / FADD2): two single-precision
+ * operations per instruction, each element rounded exactly as fmaf / * /
+ * + round it, so pair code gives the scalar code's results bit for bit. */
+__device__ __forceinline__ float2 kmb_f2(float x, float y) { return make_float2(x, y); }
+__device__ __forceinline__ float2 kmb_f2s(float v) { return make_float2(v, v); }
+__device__ __forceinline__ float2 kmb_fma2(float2 a, float2 b, float2 c) {
+    return __ffma2_rn(a, b, c);
+}
+__device__ __forceinline__ float2 kmb_mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 kmb_add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+
+/* kmb_exp2_decay of two values: the polynomial runs on pairs, MUFU ex2
+ * and the selection per element; each element equals kmb_exp2_decay. */
+__device__ __forceinline__ float2 kmb_exp2_decay2(float2 w) {
+    const float mx = kmb_ex2(w.x), my = kmb_ex2(w.y);
+    float2 p = kmb_fma2(kmb_f2s(0.009617380797863007f), w, kmb_f2s(0.055510617792606354f));
+    p = kmb_fma2(p, w, kmb_f2s(0.24022650718688965f));
+    p = kmb_fma2(p, w, kmb_f2s(0.6931471824645996f));
+    p = kmb_fma2(p, w, kmb_f2s(1.0f));
+    return kmb_f2(fabsf(w.x) < 0.0625f ? p.x : mx, fabsf(w.y) < 0.0625f ? p.y : my);
+}
+
 /* Asynchronous global->shared copies (cp.async, sm_80+).  A source size
  * below the copy size zero-fills the remainder of the destination. */
 __device__ __forceinline__ void kmb_cp_async4(void *smem, const void *gmem,

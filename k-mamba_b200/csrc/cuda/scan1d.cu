@@ -140,13 +140,6 @@ __device__ __forceinline__ void lds4u(const float *row, float (&v)[kG]) {
     v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
 }
 
-/* max(m, |h|) for the clamp detector: a state whose magnitude reaches the
- * reference's 1000 bound (or any NaN, which the final state carries on)
- * sends the tile through the exact clamping path again. */
-__device__ __forceinline__ bool clamp_hit(float hmax, const float (&h)[kG]) {
-    return !(hmax < 1000.f) || h[0] != h[0] || h[1] != h[1] || h[2] != h[2] || h[3] != h[3];
-}
-
 /* G-state versions of the helpers above, for the forward kernel that runs
  * with 2 or 4 states per lane. */
 template <int G>
@@ -380,16 +373,21 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_fwd(Scan1DDev p) {
                         ldgv<G, VEC>(bgl + (t0 + i) * hstride, gok && dok, N, dok ? n0 : N, bv);
                         ldgv<G, VEC>(cgl + (t0 + i) * hstride, gok && dok, N, dok ? n0 : N, cv);
                     }
-                    float yp = 0.f;
+                    /* state pairs on FFMA2 / FMUL2 (same per-element rounding) */
+                    const float2 dv2 = kmb_f2s(dv), u2 = kmb_f2s(u);
+                    float2 y2 = kmb_f2s(0.f);
 #pragma unroll
-                    for (int j = 0; j < G; ++j) {
-                        const float a = kmb_exp2_decay(dv * A2[j]);
-                        const float hn = fmaf(a, h[j], bv[j] * u);
-                        if (CLAMP) hmax = fmaxf(hmax, fabsf(hn));
-                        h[j] = hn;
-                        yp = fmaf(cv[j], hn, yp);
+                    for (int jp = 0; jp < G / 2; ++jp) {
+                        const int j = 2 * jp;
+                        const float2 a = kmb_exp2_decay2(kmb_mul2(dv2, kmb_f2(A2[j], A2[j + 1])));
+                        const float2 hn = kmb_fma2(a, kmb_f2(h[j], h[j + 1]),
+                                                   kmb_mul2(kmb_f2(bv[j], bv[j + 1]), u2));
+                        if (CLAMP) hmax = fmaxf(hmax, fmaxf(fabsf(hn.x), fabsf(hn.y)));
+                        h[j] = hn.x;
+                        h[j + 1] = hn.y;
+                        y2 = kmb_fma2(kmb_f2(cv[j], cv[j + 1]), hn, y2);
                     }
-                    yq[s] = yp;
+                    yq[s] = y2.x + y2.y;
                     if ((i + 1) % kChunk == 0 && ckpt && dok)
                         stgv<G, VEC>(ckpt + ((t0 + i) / kChunk) * hstride, gok, N, n0, h);
                 }
@@ -485,14 +483,17 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
     float *partB = smem + 2 * stage_sz;
     float *partC = partB + T * DT * NP;
 
-    float A2[kG], Ar[kG], gc[kG], dAacc[kG];
+    /* per-state values live as pairs: the FFMA2 / FMUL2 operands */
+    float2 A2p[2], Arp[2], gcp[2], dAp[2];
 #pragma unroll
-    for (int j = 0; j < kG; ++j) {
-        const bool ok = dok && n0 + j < N;
-        Ar[j] = ok ? __ldg(p.A + d * N + n0 + j) : 0.f;
-        A2[j] = Ar[j] * KMB_LOG2E;
-        gc[j] = 0.f;
-        dAacc[j] = 0.f;
+    for (int jp = 0; jp < 2; ++jp) {
+        const int j = n0 + 2 * jp;
+        const float a0 = (dok && j < N) ? __ldg(p.A + d * N + j) : 0.f;
+        const float a1 = (dok && j + 1 < N) ? __ldg(p.A + d * N + j + 1) : 0.f;
+        Arp[jp] = kmb_f2(a0, a1);
+        A2p[jp] = kmb_f2(a0 * KMB_LOG2E, a1 * KMB_LOG2E);
+        gcp[jp] = kmb_f2s(0.f);
+        dAp[jp] = kmb_f2s(0.f);
     }
 
     const long xoff = b * L * D + d0;
@@ -541,6 +542,20 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
     float *dxg = p.dx + b * L * D + d;
     float *dtg = p.ddt + b * L * D + d;
 
+    /* 4 states of a B / C row as two pairs (shared tile or global row) */
+    auto row_pairs = [&](const float *srow, const float *grow, long t, float2 (&v)[2]) {
+        float4 t4;
+        if (SHARED) {
+            t4 = *reinterpret_cast<const float4 *>(srow);
+        } else {
+            float f[kG];
+            ldg4<VEC>(grow + t * hstride, gok && dok, N, dok ? n0 : N, f);
+            t4 = make_float4(f[0], f[1], f[2], f[3]);
+        }
+        v[0] = kmb_f2(t4.x, t4.y);
+        v[1] = kmb_f2(t4.z, t4.w);
+    };
+
     for (int c = nch - 1, it = 0; c >= 0; --c, ++it) {
         kmb_cp_async_wait<0>();
         __syncthreads();
@@ -557,150 +572,172 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
         const int len = (int)min((long)T, L - t0);
 
         /* state before the chunk's first step */
-        float hs[kG];
+        float2 hsp[2];
         if (c > 0) {
+            float hs[kG];
             if (HALL) {
                 if (dok) ldg4<VEC>(hall + (t0 - 1) * hstride, gok, N, n0, hs);
                 else hs[0] = hs[1] = hs[2] = hs[3] = 0.f;
             } else {
-                /* zero-filled past N and for channels past D */
-                const float *ck = st + 3 * xs_sz + 2 * bs_sz + dl * NP + n0;
-                if (VEC) {
-                    lds4u(ck, hs);
-                } else {
-#pragma unroll
-                    for (int j = 0; j < kG; ++j) hs[j] = ck[j];
-                }
+                /* 16-byte aligned row of the staged checkpoint, zero-filled
+                 * past N and for channels past D */
+                lds4u(st + 3 * xs_sz + 2 * bs_sz + dl * NP + n0, hs);
             }
+            hsp[0] = kmb_f2(hs[0], hs[1]);
+            hsp[1] = kmb_f2(hs[2], hs[3]);
         } else {
+            float hs[kG];
 #pragma unroll
             for (int j = 0; j < kG; ++j)
                 hs[j] = (dok && n0 + j < N && p.h0) ? p.h0[(b * D + d) * N + n0 + j] : 0.f;
+            hsp[0] = kmb_f2(hs[0], hs[1]);
+            hsp[1] = kmb_f2(hs[2], hs[3]);
         }
 
-        /* forward recompute of the chunk's states (registers).  Without the
-         * clamp on the critical path; when a state reaches the clamp bound
-         * (or NaN) the chunk is recomputed with the exact clamp, so the
-         * states match the forward's bit for bit either way. */
-        float hr[HALL ? 1 : T][kG]; /* states h_t of the chunk */
-        float ar[HALL ? 1 : T][kG]; /* decays a_t, reused by the reverse sweep */
-        if (!HALL) {
-            auto recompute = [&](auto exact_tag) {
-                constexpr bool EXACT = decltype(exact_tag)::value;
-                float hh[kG] = {hs[0], hs[1], hs[2], hs[3]};
-                float hmax = 0.f;
+        /* With channel-shared B/C and no h_all, steps past the end of the
+         * sequence (only in the last chunk, which is processed first) are
+         * exact identity steps: the staged x, dt, dy, B, C rows are
+         * zero-filled there, so dt = 0 gives a decay of exactly 1, u = 0
+         * leaves h unchanged and dy = C = 0 with a zero carry makes every
+         * gradient term 0.  Those steps need no bounds; the other modes
+         * read global memory per step and keep them. */
+        constexpr bool FULL = SHARED && !HALL;
+        {
+            /* forward recompute of the chunk's states (registers).  Without
+             * the clamp on the critical path; when a state reaches the clamp
+             * bound (or NaN) the chunk is recomputed with the exact clamp, so
+             * the states match the forward's bit for bit either way. */
+            float2 hr[HALL ? 1 : T][2]; /* states h_t of the chunk */
+            float2 ar[HALL ? 1 : T][2]; /* decays a_t, reused by the reverse sweep */
+            if (!HALL) {
+                auto recompute = [&](auto exact_tag) {
+                    constexpr bool EXACT = decltype(exact_tag)::value;
+                    float2 hh[2] = {hsp[0], hsp[1]};
+                    float hmax = 0.f;
 #pragma unroll
-                for (int i = 0; i < T; ++i) {
-                    if (i < len) {
-                        const float dv = ds[i * DT];
-                        const float u = dv * xs[i * DT];
-                        float bv[kG];
-                        if (SHARED) lds4u(bs + i * BWr, bv);
-                        else ldg4<VEC>(bgl + (t0 + i) * hstride, gok && dok, N, dok ? n0 : N, bv);
+                    for (int i = 0; i < T; ++i) {
+                        if (FULL || i < len) {
+                            const float dv = ds[i * DT];
+                            const float2 dv2 = kmb_f2s(dv), u2 = kmb_f2s(dv * xs[i * DT]);
+                            float2 bp[2];
+                            row_pairs(bs + i * BWr, bgl, t0 + i, bp);
 #pragma unroll
-                        for (int j = 0; j < kG; ++j) {
-                            const float a = kmb_exp2_decay(dv * A2[j]);
-                            float hn = fmaf(a, hh[j], bv[j] * u);
-                            if (EXACT) hn = clamp1000(hn);
-                            else if (CLAMP) hmax = fmaxf(hmax, fabsf(hn));
-                            hh[j] = hn;
-                            hr[i][j] = hn;
-                            ar[i][j] = a;
+                            for (int jp = 0; jp < 2; ++jp) {
+                                const float2 a = kmb_exp2_decay2(kmb_mul2(dv2, A2p[jp]));
+                                float2 hn = kmb_fma2(a, hh[jp], kmb_mul2(bp[jp], u2));
+                                if (EXACT) {
+                                    hn.x = clamp1000(hn.x);
+                                    hn.y = clamp1000(hn.y);
+                                } else if (CLAMP) {
+                                    hmax = fmaxf(hmax, fmaxf(fabsf(hn.x), fabsf(hn.y)));
+                                }
+                                hh[jp] = hn;
+                                hr[i][jp] = hn;
+                                ar[i][jp] = a;
+                            }
                         }
                     }
-                }
-                return CLAMP && !EXACT && clamp_hit(hmax, hh);
-            };
-            if (__any_sync(kFull, recompute(std::false_type{})))
-                recompute(std::true_type{});
-        }
+                    return CLAMP && !EXACT &&
+                           (!(hmax < 1000.f) || hh[0].x != hh[0].x || hh[0].y != hh[0].y ||
+                            hh[1].x != hh[1].x || hh[1].y != hh[1].y);
+                };
+                if (__any_sync(kFull, recompute(std::false_type{})))
+                    recompute(std::true_type{});
+            }
 
-        /* reverse sweep, S steps per dx/ddt reduce-scatter group */
+            /* reverse sweep, S steps per dx/ddt reduce-scatter group */
 #pragma unroll
-        for (int i0 = T - 1; i0 >= 0; i0 -= S) {
-            float rv[NV];
+            for (int i0 = T - 1; i0 >= 0; i0 -= S) {
+                float rv[NV];
 #pragma unroll
-            for (int k = 0; k < NV; ++k) rv[k] = 0.f;
+                for (int k = 0; k < NV; ++k) rv[k] = 0.f;
 #pragma unroll
-            for (int s = 0; s < S; ++s) {
-                const int i = i0 - s;
-                rv[2 * s] = 0.f;
-                rv[2 * s + 1] = 0.f;
-                if (i < len) {
-                    const float xv = xs[i * DT];
-                    const float dv = ds[i * DT];
-                    const float dyv = dys[i * DT];
-                    const float u = dv * xv;
-                    float bv[kG], cv[kG], hp[kG], ht[kG];
-                    if (SHARED) {
-                        lds4u(bs + i * BWr, bv);
-                        lds4u(cs + i * BWr, cv);
-                    } else {
-                        ldg4<VEC>(bgl + (t0 + i) * hstride, gok && dok, N, dok ? n0 : N, bv);
-                        ldg4<VEC>(cgl + (t0 + i) * hstride, gok && dok, N, dok ? n0 : N, cv);
-                    }
-                    if (HALL) {
-                        if (dok) {
-                            ldg4<VEC>(hall + (t0 + i) * hstride, gok, N, n0, ht);
-                            if (i > 0) ldg4<VEC>(hall + (t0 + i - 1) * hstride, gok, N, n0, hp);
-                            else for (int j = 0; j < kG; ++j) hp[j] = hs[j];
+                for (int s = 0; s < S; ++s) {
+                    const int i = i0 - s;
+                    if (FULL || i < len) {
+                        const float xv = xs[i * DT];
+                        const float dv = ds[i * DT];
+                        const float dyv = dys[i * DT];
+                        const float2 dv2 = kmb_f2s(dv), dyv2 = kmb_f2s(dyv);
+                        const float2 u2 = kmb_f2s(dv * xv);
+                        float2 bp[2], cp[2], hp[2], ht[2];
+                        row_pairs(bs + i * BWr, bgl, t0 + i, bp);
+                        row_pairs(cs + i * BWr, cgl, t0 + i, cp);
+                        if (HALL) {
+                            float f[kG], q[kG];
+                            if (dok) {
+                                ldg4<VEC>(hall + (t0 + i) * hstride, gok, N, n0, f);
+                                if (i > 0) {
+                                    ldg4<VEC>(hall + (t0 + i - 1) * hstride, gok, N, n0, q);
+                                } else {
+                                    q[0] = hsp[0].x; q[1] = hsp[0].y;
+                                    q[2] = hsp[1].x; q[3] = hsp[1].y;
+                                }
+                            } else {
+#pragma unroll
+                                for (int j = 0; j < kG; ++j) f[j] = q[j] = 0.f;
+                            }
+                            ht[0] = kmb_f2(f[0], f[1]);
+                            ht[1] = kmb_f2(f[2], f[3]);
+                            hp[0] = kmb_f2(q[0], q[1]);
+                            hp[1] = kmb_f2(q[2], q[3]);
                         } else {
 #pragma unroll
-                            for (int j = 0; j < kG; ++j) ht[j] = hp[j] = 0.f;
+                            for (int jp = 0; jp < 2; ++jp) {
+                                ht[jp] = hr[HALL ? 0 : i][jp];
+                                hp[jp] = i > 0 ? hr[HALL ? 0 : (i > 0 ? i - 1 : 0)][jp] : hsp[jp];
+                            }
                         }
-                    } else {
+                        float2 dxs2 = kmb_f2s(0.f), dts2 = kmb_f2s(0.f), vb[2], vc[2];
 #pragma unroll
-                        for (int j = 0; j < kG; ++j) {
-                            ht[j] = hr[HALL ? 0 : i][j];
-                            hp[j] = i > 0 ? hr[HALL ? 0 : (i > 0 ? i - 1 : 0)][j] : hs[j];
+                        for (int jp = 0; jp < 2; ++jp) {
+                            const float2 a = HALL ? kmb_exp2_decay2(kmb_mul2(dv2, A2p[jp]))
+                                                  : ar[HALL ? 0 : i][jp];
+                            const float2 ah = kmb_fma2(dyv2, cp[jp], gcp[jp]);
+                            const float2 q = kmb_mul2(ah, a);
+                            const float2 qh = kmb_mul2(q, hp[jp]);
+                            dAp[jp] = kmb_fma2(dv2, qh, dAp[jp]);
+                            dts2 = kmb_fma2(Arp[jp], qh, dts2);
+                            dxs2 = kmb_fma2(ah, bp[jp], dxs2);
+                            vb[jp] = kmb_mul2(ah, u2);      /* dB contribution */
+                            vc[jp] = kmb_mul2(dyv2, ht[jp]); /* dC contribution */
+                            gcp[jp] = q;
                         }
-                    }
-                    float dxs = 0.f, dts = 0.f;
-                    float v[8];
-#pragma unroll
-                    for (int j = 0; j < kG; ++j) {
-                        const float a = HALL ? kmb_exp2_decay(dv * A2[j]) : ar[HALL ? 0 : i][j];
-                        const float ah = fmaf(dyv, cv[j], gc[j]);
-                        const float q = ah * a;
-                        const float qh = q * hp[j];
-                        dAacc[j] = fmaf(dv, qh, dAacc[j]);
-                        dts = fmaf(Ar[j], qh, dts);
-                        dxs = fmaf(ah, bv[j], dxs);
-                        v[j] = ah * u;           /* dB contribution */
-                        v[4 + j] = dyv * ht[j];  /* dC contribution */
-                        gc[j] = q;
-                    }
-                    rv[2 * s] = dxs;
-                    rv[2 * s + 1] = fmaf(xv, dxs, dts);
-                    if (SHARED) {
-                        const int o = (i * DT + dl) * NP + n0;
-                        *reinterpret_cast<float4 *>(partB + o) = make_float4(v[0], v[1], v[2], v[3]);
-                        *reinterpret_cast<float4 *>(partC + o) = make_float4(v[4], v[5], v[6], v[7]);
-                    } else if (dok) {
-                        float vb[kG] = {v[0], v[1], v[2], v[3]};
-                        float vc[kG] = {v[4], v[5], v[6], v[7]};
-                        const long o = ((b * L + t0 + i) * D + d) * N + n0;
-                        stg4<VEC>(p.dB + o, gok, N, n0, vb);
-                        stg4<VEC>(p.dC + o, gok, N, n0, vc);
+                        const float dxs = dxs2.x + dxs2.y;
+                        rv[2 * s] = dxs;
+                        rv[2 * s + 1] = fmaf(xv, dxs, dts2.x + dts2.y);
+                        if (SHARED) {
+                            const int o = (i * DT + dl) * NP + n0;
+                            *reinterpret_cast<float4 *>(partB + o) =
+                                make_float4(vb[0].x, vb[0].y, vb[1].x, vb[1].y);
+                            *reinterpret_cast<float4 *>(partC + o) =
+                                make_float4(vc[0].x, vc[0].y, vc[1].x, vc[1].y);
+                        } else if (dok) {
+                            const float fb[kG] = {vb[0].x, vb[0].y, vb[1].x, vb[1].y};
+                            const float fc[kG] = {vc[0].x, vc[0].y, vc[1].x, vc[1].y};
+                            const long o = ((b * L + t0 + i) * D + d) * N + n0;
+                            stg4<VEC>(p.dB + o, gok, N, n0, fb);
+                            stg4<VEC>(p.dC + o, gok, N, n0, fc);
+                        }
                     }
                 }
-            }
-            /* fold dx / ddt over the P lanes of the channel */
-            if (P >= 2) {
-                const float r = rs_sum<NV>(rv, lane);
-                const int s = g >> 1;
-                const int i = i0 - s;
-                if (dok && g < 2 * S && i >= 0 && i < len) {
-                    const long t = t0 + i;
-                    if (g & 1) dtg[t * D] = r;
-                    else dxg[t * D] = r * ds[i * DT];
-                }
-            } else {
-                const int i = i0;
-                if (dok && i < len) {
-                    const long t = t0 + i;
-                    dxg[t * D] = rv[0] * ds[i * DT];
-                    dtg[t * D] = rv[1];
+                /* fold dx / ddt over the P lanes of the channel */
+                if (P >= 2) {
+                    const float r = rs_sum<NV>(rv, lane);
+                    const int s = g >> 1;
+                    const int i = i0 - s;
+                    if (dok && g < 2 * S && i >= 0 && i < len) {
+                        const long t = t0 + i;
+                        if (g & 1) dtg[t * D] = r;
+                        else dxg[t * D] = r * ds[i * DT];
+                    }
+                } else {
+                    const int i = i0;
+                    if (dok && i < len) {
+                        const long t = t0 + i;
+                        dxg[t * D] = rv[0] * ds[i * DT];
+                        dtg[t * D] = rv[1];
+                    }
                 }
             }
         }
@@ -723,7 +760,7 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
                 const int i = (o % (T * NQ)) / NQ;
                 const int q = o % NQ;
                 const bool live = o < OUTS && i < len && q * 4 < N;
-                float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+                float2 lo = kmb_f2s(0.f), hi = kmb_f2s(0.f);
                 if (live) {
                     const float *src = (arr ? partC : partB) + i * DT * NP + q * 4;
 #pragma unroll 8
@@ -731,24 +768,25 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
                         const int dlx = k * HR + hh;
                         if (dlx < dvalid) {
                             const float4 t4 = *reinterpret_cast<const float4 *>(src + dlx * NP);
-                            s4.x += t4.x; s4.y += t4.y; s4.z += t4.z; s4.w += t4.w;
+                            lo = kmb_add2(lo, kmb_f2(t4.x, t4.y));
+                            hi = kmb_add2(hi, kmb_f2(t4.z, t4.w));
                         }
                     }
                 }
 #pragma unroll
                 for (int m = HR / 2; m > 0; m >>= 1) {
-                    s4.x += __shfl_xor_sync(kFull, s4.x, m);
-                    s4.y += __shfl_xor_sync(kFull, s4.y, m);
-                    s4.z += __shfl_xor_sync(kFull, s4.z, m);
-                    s4.w += __shfl_xor_sync(kFull, s4.w, m);
+                    lo.x += __shfl_xor_sync(kFull, lo.x, m);
+                    lo.y += __shfl_xor_sync(kFull, lo.y, m);
+                    hi.x += __shfl_xor_sync(kFull, hi.x, m);
+                    hi.y += __shfl_xor_sync(kFull, hi.y, m);
                 }
                 if (live && hh == 0) {
                     const int n = q * 4;
                     float *dst = (arr ? p.dC : p.dB) + (b * L + t0 + i) * N + n;
                     if (VEC && vbc) {
-                        atomicAdd(reinterpret_cast<float4 *>(dst), s4);
+                        atomicAdd(reinterpret_cast<float4 *>(dst), make_float4(lo.x, lo.y, hi.x, hi.y));
                     } else {
-                        const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+                        const float sv[4] = {lo.x, lo.y, hi.x, hi.y};
 #pragma unroll
                         for (int k = 0; k < 4; ++k)
                             if (n + k < N) atomicAdd(dst + k, sv[k]);
@@ -759,9 +797,12 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
     }
     kmb_cp_async_wait<0>();
 
+    {
+        const float dAs[kG] = {dAp[0].x, dAp[0].y, dAp[1].x, dAp[1].y};
 #pragma unroll
-    for (int j = 0; j < kG; ++j)
-        if (dok && n0 + j < N) atomicAdd(p.dA + d * N + n0 + j, dAacc[j]);
+        for (int j = 0; j < kG; ++j)
+            if (dok && n0 + j < N) atomicAdd(p.dA + d * N + n0 + j, dAs[j]);
+    }
 }
 
 /* M = 1 backward with per-channel A/B/C and a per-step delta shared by all
