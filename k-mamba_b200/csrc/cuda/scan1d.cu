@@ -1002,7 +1002,11 @@ extern "C" int kmb_launch_scan1d_bwd(const KmbScan1D *a, const float *ckpt_in,
     const int P = pick_p(a->N);
     if (!shared && P > 16)
         return kmb_fail(KMB_EUNSUPPORTED, "scan1d: per-channel B/C support N <= 64 (N=%ld)", a->N);
-    cudaError_t e = cudaMemsetAsync(a->dA, 0, sizeof(float) * a->D * a->N, s);
+    /* KMB_SCAN1D_DA_ACCUM (host layer only): add to dA instead of
+     * overwriting it, for batch slices of one call */
+    cudaError_t e = (a->flags & KMB_SCAN1D_DA_ACCUM)
+                        ? cudaSuccess
+                        : cudaMemsetAsync(a->dA, 0, sizeof(float) * a->D * a->N, s);
     if (e == cudaSuccess && shared) {
         const size_t nb = sizeof(float) * a->batch * a->L * a->N;
         e = cudaMemsetAsync(a->dB, 0, nb, s);

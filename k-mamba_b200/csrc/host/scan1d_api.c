@@ -70,11 +70,215 @@ static void stage_args(KmbStage *st, const KmbScan1D *a, KmbScan1D *d, int bwd) 
     }
 }
 
+/* ------------------------------------------------------------------ */
+/* batch-sliced host <-> device pipeline                               */
+/* ------------------------------------------------------------------ */
+
+/*
+ * A call whose large tensors live in host memory runs one batch item at a
+ * time through a ring of PIPE_SLOTS device slots: host->device copies of
+ * item i+1 (copy stream), the kernels of item i (library stream) and the
+ * device->host copies of item i-1 (second copy stream) overlap, so the
+ * call takes about as long as its larger copy direction instead of the
+ * sum of both directions and the kernels.  Tensors already in device
+ * memory are used in place.  Copies overlap only for page-locked host
+ * buffers; pageable ones are still correct (the driver stages them).
+ */
+#define PIPE_SLOTS 3
+#define PIPE_MAX_DEV 16
+enum { PT_X, PT_DT, PT_B, PT_C, PT_H0, PT_Y, PT_HL, PT_HALL, PT_CK, PT_DY, PT_DX, PT_DDT,
+       PT_DB, PT_DC, PT_N };
+
+typedef struct {
+    const void *user; /* caller pointer, NULL when absent */
+    size_t item;      /* bytes per batch item */
+    int in, out;      /* copied in before / out after the item's kernels */
+    int host;         /* user points to host memory */
+    void *slot[PIPE_SLOTS];
+} PipeTensor;
+
+typedef struct {
+    cudaStream_t in, out;
+    cudaEvent_t start, ev_in[PIPE_SLOTS], ev_comp[PIPE_SLOTS], ev_out[PIPE_SLOTS];
+    int ready;
+} PipeRes;
+
+/* per host thread and device; created on first use, kept for the thread's
+ * lifetime (streams and events are reclaimed with the CUDA context) */
+static __thread PipeRes t_pipe[PIPE_MAX_DEV];
+
+static PipeRes *pipe_res(void) {
+    int dev = 0;
+    PipeRes *r;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= PIPE_MAX_DEV) {
+        (void)cudaGetLastError();
+        return NULL;
+    }
+    r = &t_pipe[dev];
+    if (!r->ready) {
+        int ok = cudaStreamCreateWithFlags(&r->in, cudaStreamNonBlocking) == cudaSuccess &&
+                 cudaStreamCreateWithFlags(&r->out, cudaStreamNonBlocking) == cudaSuccess &&
+                 cudaEventCreateWithFlags(&r->start, cudaEventDisableTiming) == cudaSuccess;
+        for (int k = 0; ok && k < PIPE_SLOTS; ++k)
+            ok = cudaEventCreateWithFlags(&r->ev_in[k], cudaEventDisableTiming) == cudaSuccess &&
+                 cudaEventCreateWithFlags(&r->ev_comp[k], cudaEventDisableTiming) == cudaSuccess &&
+                 cudaEventCreateWithFlags(&r->ev_out[k], cudaEventDisableTiming) == cudaSuccess;
+        if (!ok) {
+            (void)cudaGetLastError();
+            return NULL;
+        }
+        r->ready = 1;
+    }
+    return r;
+}
+
+static void pt_set(PipeTensor *t, const void *user, size_t item, int in, int out) {
+    memset(t, 0, sizeof *t);
+    t->user = user;
+    t->item = item;
+    t->in = in;
+    t->out = out;
+    t->host = user && !kmb_is_device_ptr(user);
+}
+
+/* pointer of batch item i: the slot when staged, else in place */
+static void *pt_ptr(const PipeTensor *t, long i, int k) {
+    if (!t->user) return NULL;
+    return t->host ? t->slot[k] : (void *)((const char *)t->user + (size_t)i * t->item);
+}
+
+/* 1 when the call should take the sliced pipeline */
+static int pipe_wanted(const KmbScan1D *a, int bwd) {
+    const void *big[6] = {a->x, a->dt, bwd ? a->dy : a->y, bwd ? a->dx : NULL,
+                          bwd ? a->ddt : NULL, a->B};
+    if (a->batch < 2) return 0;
+    for (int i = 0; i < 6; ++i)
+        if (big[i] && !kmb_is_device_ptr(big[i])) return 1;
+    return 0;
+}
+
+static int scan1d_pipelined(const KmbScan1D *a, int bwd) {
+    KmbStage st;
+    PipeTensor T[PT_N];
+    PipeRes *r = pipe_res();
+    const size_t f = sizeof(float);
+    const long L = a->L, D = a->D, N = a->N;
+    const size_t e_ld = f * (size_t)(L * D);
+    const size_t e_bc = f * (size_t)(L * (a->bc_shared ? 1 : D) * N);
+    const size_t e_st = f * (size_t)(D * N);
+    const size_t e_all = f * (size_t)(L * D * N);
+    const size_t e_ck = f * (size_t)kmb_scan1d_ckpt_elems(1, L, D, N);
+    const int alias = !bwd && a->h_last && a->h_last == a->h0;
+    const int own_ck = bwd && !a->h_all && !a->ckpt;
+    const float *dA_in;
+    float *dA = NULL;
+    void *ck_slot[PIPE_SLOTS] = {0};
+    cudaStream_t s;
+    int rc = KMB_OK;
+    cudaError_t e;
+
+    if (!r) return 1; /* no pipeline resources: the caller runs the single-shot path */
+    kmb_stage_begin(&st);
+    s = st.s;
+    pt_set(&T[PT_X], a->x, e_ld, 1, 0);
+    pt_set(&T[PT_DT], a->dt, e_ld, 1, 0);
+    pt_set(&T[PT_B], a->B, e_bc, 1, 0);
+    pt_set(&T[PT_C], a->C, e_bc, 1, 0);
+    pt_set(&T[PT_H0], a->h0, e_st, 1, alias);
+    pt_set(&T[PT_Y], bwd ? NULL : a->y, e_ld, 0, 1);
+    pt_set(&T[PT_HL], (bwd || alias) ? NULL : a->h_last, e_st, 0, 1);
+    pt_set(&T[PT_HALL], a->h_all, e_all, bwd, !bwd);
+    pt_set(&T[PT_CK], a->ckpt, e_ck, bwd, !bwd);
+    pt_set(&T[PT_DY], bwd ? a->dy : NULL, e_ld, 1, 0);
+    pt_set(&T[PT_DX], bwd ? a->dx : NULL, e_ld, 0, 1);
+    pt_set(&T[PT_DDT], bwd ? a->ddt : NULL, e_ld, 0, 1);
+    pt_set(&T[PT_DB], bwd ? a->dB : NULL, e_bc, 0, 1);
+    pt_set(&T[PT_DC], bwd ? a->dC : NULL, e_bc, 0, 1);
+    dA_in = (const float *)kmb_stage_in(&st, a->A, e_st);
+    if (bwd) dA = (float *)kmb_stage_out(&st, a->dA, e_st, 0);
+    for (int t = 0; t < PT_N && !st.status; ++t)
+        if (T[t].user && T[t].host)
+            for (int k = 0; k < PIPE_SLOTS; ++k) T[t].slot[k] = kmb_scratch(&st, T[t].item);
+    for (int k = 0; own_ck && k < PIPE_SLOTS && !st.status; ++k) ck_slot[k] = kmb_scratch(&st, e_ck);
+    if (st.status) return kmb_stage_finish(&st, st.status);
+
+    e = cudaEventRecord(r->start, s);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(r->in, r->start, 0);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(r->out, r->start, 0);
+    if (e != cudaSuccess) return kmb_stage_finish(&st, kmb_cuda_fail(e, "scan1d pipeline start"));
+
+    for (long i = 0; i < a->batch && rc == KMB_OK; ++i) {
+        const int k = (int)(i % PIPE_SLOTS);
+        KmbScan1D sl = *a;
+        /* slot k is free once the copies out of item i - PIPE_SLOTS are done */
+        if (i >= PIPE_SLOTS) e = cudaStreamWaitEvent(r->in, r->ev_out[k], 0);
+        for (int t = 0; t < PT_N && e == cudaSuccess; ++t)
+            if (T[t].user && T[t].host && T[t].in)
+                e = cudaMemcpyAsync(T[t].slot[k], (const char *)T[t].user + (size_t)i * T[t].item,
+                                    T[t].item, cudaMemcpyHostToDevice, r->in);
+        if (e == cudaSuccess) e = cudaEventRecord(r->ev_in[k], r->in);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(s, r->ev_in[k], 0);
+        if (e != cudaSuccess) {
+            rc = kmb_cuda_fail(e, "scan1d pipeline copy-in");
+            break;
+        }
+        sl.batch = 1;
+        sl.A = dA_in;
+        sl.x = (const float *)pt_ptr(&T[PT_X], i, k);
+        sl.dt = (const float *)pt_ptr(&T[PT_DT], i, k);
+        sl.B = (const float *)pt_ptr(&T[PT_B], i, k);
+        sl.C = (const float *)pt_ptr(&T[PT_C], i, k);
+        sl.h0 = (const float *)pt_ptr(&T[PT_H0], i, k);
+        sl.h_all = (float *)pt_ptr(&T[PT_HALL], i, k);
+        sl.ckpt = (float *)pt_ptr(&T[PT_CK], i, k);
+        if (!bwd) {
+            sl.y = (float *)pt_ptr(&T[PT_Y], i, k);
+            sl.h_last = alias ? (float *)sl.h0 : (float *)pt_ptr(&T[PT_HL], i, k);
+            rc = kmb_launch_scan1d_fwd(&sl, s);
+        } else {
+            const float *ck = sl.ckpt;
+            sl.dy = (const float *)pt_ptr(&T[PT_DY], i, k);
+            sl.dx = (float *)pt_ptr(&T[PT_DX], i, k);
+            sl.ddt = (float *)pt_ptr(&T[PT_DDT], i, k);
+            sl.dB = (float *)pt_ptr(&T[PT_DB], i, k);
+            sl.dC = (float *)pt_ptr(&T[PT_DC], i, k);
+            sl.dA = dA;
+            sl.y = NULL;
+            sl.h_last = NULL;
+            if (own_ck) {
+                KmbScan1D fw = sl;
+                fw.ckpt = (float *)ck_slot[k];
+                fw.h_all = NULL;
+                rc = kmb_launch_scan1d_fwd(&fw, s);
+                ck = fw.ckpt;
+            }
+            if (i > 0) sl.flags |= KMB_SCAN1D_DA_ACCUM;
+            if (rc == KMB_OK) rc = kmb_launch_scan1d_bwd(&sl, ck, s);
+        }
+        if (rc != KMB_OK) break;
+        e = cudaEventRecord(r->ev_comp[k], s);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(r->out, r->ev_comp[k], 0);
+        for (int t = 0; t < PT_N && e == cudaSuccess; ++t)
+            if (T[t].user && T[t].host && T[t].out)
+                e = cudaMemcpyAsync((char *)T[t].user + (size_t)i * T[t].item, T[t].slot[k],
+                                    T[t].item, cudaMemcpyDeviceToHost, r->out);
+        if (e == cudaSuccess) e = cudaEventRecord(r->ev_out[k], r->out);
+        if (e != cudaSuccess) rc = kmb_cuda_fail(e, "scan1d pipeline copy-out");
+    }
+    /* every slot goes back to the pool only after both copy streams drain */
+    e = cudaStreamSynchronize(r->out);
+    if (e != cudaSuccess && rc == KMB_OK) rc = kmb_cuda_fail(e, "scan1d pipeline drain");
+    e = cudaStreamSynchronize(r->in);
+    if (e != cudaSuccess && rc == KMB_OK) rc = kmb_cuda_fail(e, "scan1d pipeline drain");
+    return kmb_stage_finish(&st, rc);
+}
+
 int kmb_scan1d_fwd(const KmbScan1D *a) {
     KmbStage st;
     KmbScan1D d;
     int rc = validate_common(a);
     if (rc) return rc;
+    if (pipe_wanted(a, 0) && (rc = scan1d_pipelined(a, 0)) != 1) return rc;
     kmb_stage_begin(&st);
     stage_args(&st, a, &d, 0);
     if (st.status) return kmb_stage_finish(&st, st.status);
@@ -90,6 +294,7 @@ int kmb_scan1d_bwd(const KmbScan1D *a) {
     if (rc) return rc;
     if (!a->dy || !a->dx || !a->ddt || !a->dA || !a->dB || !a->dC)
         return kmb_fail(KMB_EINVAL, "scan1d backward: dy and every gradient are required");
+    if (pipe_wanted(a, 1) && (rc = scan1d_pipelined(a, 1)) != 1) return rc;
     kmb_stage_begin(&st);
     stage_args(&st, a, &d, 1);
     if (st.status) return kmb_stage_finish(&st, st.status);

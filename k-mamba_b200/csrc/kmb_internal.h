@@ -18,7 +18,11 @@ extern "C" {
 int kmb_fail(int status, const char *fmt, ...);
 int kmb_cuda_fail(cudaError_t e, const char *where);
 
-/* 1D selective scan launchers (csrc/cuda/scan1d.cu). */
+/* 1D selective scan launchers (csrc/cuda/scan1d.cu).  The host layer sets
+ * KMB_SCAN1D_DA_ACCUM in KmbScan1D.flags (after validating the caller's
+ * zero) when it launches a call's batch in slices: the backward then
+ * accumulates into dA instead of zeroing it first. */
+#define KMB_SCAN1D_DA_ACCUM 0x10000
 int kmb_launch_scan1d_fwd(const KmbScan1D *a, cudaStream_t s);
 int kmb_launch_scan1d_bwd(const KmbScan1D *a, const float *ckpt_in,
                           cudaStream_t s);

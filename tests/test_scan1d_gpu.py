@@ -259,3 +259,84 @@ def test_config2_full_size_channel_slices(lib, cuda, oracle):
     assert rel_err(g["dC"][b], dC) <= TOL
     del hall
     torch.cuda.empty_cache()
+
+
+# --------------------------------------------- host buffers: batch-sliced pipeline
+
+def run_host(lib, x, A, B, Cm, dt, dy, shared, h0, pinned, with_ckpt, alias_state):
+    """kmb_scan1d_fwd / _bwd with every tensor in host memory (numpy,
+    pageable, or torch page-locked), which takes the batch-sliced copy
+    pipeline for batch >= 2."""
+    import torch
+    bsz, L, D = x.shape
+    N = A.shape[1]
+
+    def hbuf(a=None, shape=None):
+        if pinned:
+            t = torch.empty(shape if a is None else a.shape, dtype=torch.float32).pin_memory()
+            if a is not None:
+                t.copy_(torch.from_numpy(np.ascontiguousarray(a, dtype=f32)))
+            else:
+                t.fill_(float("nan"))
+            return t, t.numpy()
+        arr = np.ascontiguousarray(a, dtype=f32).copy() if a is not None else \
+            np.full(shape, np.nan, f32)
+        return arr, arr
+
+    keep = []
+
+    def P(a=None, shape=None):
+        obj, arr = hbuf(a, shape)
+        keep.append(obj)
+        return arr
+
+    hx, hdt, hA, hB, hC, hdy = P(x), P(dt), P(A), P(B), P(Cm), P(dy)
+    hh0 = P(h0)
+    hy = P(shape=(bsz, L, D))
+    hl = hh0 if alias_state else P(shape=(bsz, D, N))
+    ck = P(shape=(lib.kmb_scan1d_ckpt_elems(bsz, L, D, N),)) if with_ckpt else None
+    a = kb.KmbScan1D()
+    a.x, a.dt, a.A, a.B, a.C, a.h0 = (v.ctypes.data for v in (hx, hdt, hA, hB, hC, hh0))
+    a.y, a.h_last = hy.ctypes.data, hl.ctypes.data
+    a.ckpt = None if ck is None else ck.ctypes.data
+    a.batch, a.L, a.D, a.N, a.bc_shared, a.clamp = bsz, L, D, N, int(shared), 1
+    kb.check(lib, lib.kmb_scan1d_fwd(C.byref(a)))
+    h_last = hl.copy()
+    if alias_state:  # the backward needs the initial state again
+        hh0[...] = h0
+    g = {k: P(shape=s) for k, s in (("dx", (bsz, L, D)), ("ddt", (bsz, L, D)), ("dA", (D, N)),
+                                    ("dB", B.shape), ("dC", B.shape))}
+    a.dy = hdy.ctypes.data
+    a.dx, a.ddt, a.dA, a.dB, a.dC = (g[k].ctypes.data for k in ("dx", "ddt", "dA", "dB", "dC"))
+    a.y = a.h_last = None
+    kb.check(lib, lib.kmb_scan1d_bwd(C.byref(a)))
+    return hy.copy(), h_last, {k: v.copy() for k, v in g.items()}
+
+
+@pytest.mark.parametrize("pinned,with_ckpt,alias_state,shared,bsz", [
+    (True, False, False, True, 5), (False, True, False, True, 3),
+    (True, True, True, False, 4), (False, False, True, True, 2)])
+def test_host_pipeline_matches_device(lib, cuda, pinned, with_ckpt, alias_state, shared, bsz):
+    """Host-buffer calls (the sliced copy pipeline) give the device path's
+    results: per-item outputs bit for bit (the same kernels run on each
+    item); dA, dB, dC are sums of CTA partials added by atomics in an
+    unspecified order, so they agree to fp32 rounding (1e-5)."""
+    rng = np.random.default_rng(77 + bsz)
+    L, D, N = 203, 72, 16 if shared else 8
+    x = rng.normal(0, 1, (bsz, L, D)).astype(f32)
+    dt = np.log1p(np.exp(rng.normal(0, 1, (bsz, L, D)) - 2)).astype(f32)
+    A = (-np.exp(rng.uniform(0, np.log(16), (D, N)))).astype(f32)
+    bs = (bsz, L, N) if shared else (bsz, L, D, N)
+    B = rng.normal(0, 1, bs).astype(f32)
+    Cm = rng.normal(0, 1, bs).astype(f32)
+    dy = rng.normal(0, 1, (bsz, L, D)).astype(f32)
+    h0 = rng.normal(0, 0.5, (bsz, D, N)).astype(f32)
+    y_d, hl_d, g_d = run_batched(lib, x, A, B, Cm, dt, dy, shared, h0=h0)
+    y_h, hl_h, g_h = run_host(lib, x, A, B, Cm, dt, dy, shared, h0, pinned, with_ckpt,
+                              alias_state)
+    np.testing.assert_array_equal(y_h, y_d)
+    np.testing.assert_array_equal(hl_h, hl_d)
+    for k in ("dx", "ddt"):
+        np.testing.assert_array_equal(g_h[k], g_d[k])
+    for k in ("dB", "dC", "dA"):
+        assert rel_err(g_h[k], g_d[k]) <= 1e-5, k
