@@ -12,19 +12,28 @@
  * outputs, so the reference's wavefront levels do not constrain the GPU:
  * every kernel is a single pass over the grid.
  *
- * 2D fast path (the config-3 shape).  A thread owns one column j, a
- * strip of TI rows and 4 consecutive channels (float4).  A K x K window
- * of float4 slides down the strip, so each output row costs K 128-bit
- * loads (the column neighbours come from L1) and K*K float4 FMAs; the
- * kernel taps stay in registers.  The backward slides two windows (dy
- * rows r..r+K-1 for the gather-form dinput, input rows r-K+1..r for
- * dkernel) downwards through the strip; dkernel/dbias partials are folded
- * in shared memory and added to global memory with one atomic per CTA
- * and (tap, channel).
+ * 2D paths.  A thread owns one column j, a strip of rows and 4
+ * consecutive channels (float4); a K x K window of float4 slides along the
+ * strip in registers with the kernel taps, so each output row costs K*K
+ * float4 FMAs.  The backward slides two windows (dy rows r..r+K-1 for the
+ * gather-form dinput, input rows r-K+1..r for dkernel); dkernel/dbias
+ * partials are folded in shared memory and added to global memory with
+ * one atomic per CTA and (tap, channel).
+ *
+ *  - streamed rows (D a multiple of 64, K <= 3, 16-byte aligned tensors;
+ *    the config-3 shape): a CTA covers 64 channels x 16 columns of a
+ *    128-row strip; whole rows with their column halo are copied by
+ *    cp.async into a shared ring several rows ahead of the compute (deep
+ *    enough to cover HBM latency at one CTA per SM), and each row reads
+ *    only its new K values per tensor from shared memory;
+ *  - direct (other 2D shapes): the windows load straight from global
+ *    memory, column neighbours from L1.
  *
  * Any other rank uses the generic kernels (thread per point and channel).
  */
 #include <string.h>
+
+#include <type_traits>
 
 #include "kmb_common.cuh"
 #include "../kmb_internal.h"
@@ -62,6 +71,20 @@ struct Vec<4> {
     }
     __device__ static T add(T a, T b) { return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w); }
     __device__ static float get(T v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
+};
+/* float4 math on FFMA2 / FADD2 pairs (each element rounded as fmaf / +
+ * round it), for the streamed backward whose issue rate it relieves */
+struct Vec4p : Vec<4> {
+    __device__ static T fma(T a, T b, T c) {
+        const float2 lo = kmb_fma2(kmb_f2(a.x, a.y), kmb_f2(b.x, b.y), kmb_f2(c.x, c.y));
+        const float2 hi = kmb_fma2(kmb_f2(a.z, a.w), kmb_f2(b.z, b.w), kmb_f2(c.z, c.w));
+        return make_float4(lo.x, lo.y, hi.x, hi.y);
+    }
+    __device__ static T add(T a, T b) {
+        const float2 lo = kmb_add2(kmb_f2(a.x, a.y), kmb_f2(b.x, b.y));
+        const float2 hi = kmb_add2(kmb_f2(a.z, a.w), kmb_f2(b.z, b.w));
+        return make_float4(lo.x, lo.y, hi.x, hi.y);
+    }
 };
 template <>
 struct Vec<1> {
@@ -247,6 +270,367 @@ __global__ void __launch_bounds__(kThreads2d) k_conv2d_bwd(ConvDev p, Geo2d g) {
         for (int q = 0; q < tj; ++q) s += red[((q * g.cgt + cgo) * NACC + k) * CW + i];
         if (k < K * K) atomicAdd(p.dker + (long)k * D + cc, s);
         else if (p.dbias) atomicAdd(p.dbias + cc, s);
+    }
+}
+
+/* ------------------------------------------------------------------ */
+/* 2D backward, streamed rows                                          */
+/* ------------------------------------------------------------------ */
+
+/*
+ * Backward for 4-aligned channels (the config-3 shape), bound by HBM: one
+ * read of dy and input and one write of dinput.  A CTA covers R2_CG float4
+ * channel groups x R2_TJ columns of a strip of R2_TI rows and walks the
+ * strip downwards.  "Stage" m carries dy row rend+K-2-m and input row
+ * rend-1-m, each R2_TJ + 2(K-1) columns wide (the column halo, zero-filled
+ * outside the grid); row r = rend-1-n needs stages n .. n+K-1.  Stages are
+ * copied by cp.async into a ring of r2_nr<K>() shared rows, R2_PD stages
+ * ahead of the compute, so about 60 KB per SM is in flight.  A thread's
+ * K x K windows live in registers indexed by stage % K (the row loop is
+ * unrolled by K, so no window shifts) and only the new stage's K values
+ * per tensor come from shared memory each row.  Rows n .. n+K-1 share one
+ * cp.async wait and one barrier; a fast thread then issues stages
+ * n+PD .. n+PD+K-1 while a slow one may still read stage n-1, so the ring
+ * holds R2_PD + K + 1 rows.
+ */
+constexpr int R2_CG = 16;                 /* float4 channel groups per CTA */
+constexpr int R2_TJ = kThreads2d / R2_CG; /* columns per CTA */
+constexpr int R2_TI = 128;                /* rows per strip */
+constexpr int R2_PD = 6;                  /* stages in flight */
+
+/* ring rows: a fast thread issues stages n+PD .. n+PD+K-1 of its row group
+ * while a slow one may still read stage n-1 of the previous group */
+template <int K>
+__host__ __device__ constexpr int r2_nr() { return R2_PD + K + 1; }
+
+template <int K>
+__host__ __device__ constexpr int r2_ws() { return R2_TJ + 2 * (K - 1); }
+
+template <int K>
+__host__ __device__ constexpr size_t r2_smem_bytes() {
+    /* two rings of r2_nr rows; the final fold reuses the same space */
+    const size_t ring = 2ull * r2_nr<K>() * r2_ws<K>() * R2_CG * 16;
+    const size_t fold = (size_t)kThreads2d * (K * K + 1) * 16;
+    return ring > fold ? ring : fold;
+}
+
+template <int K>
+__global__ void __launch_bounds__(kThreads2d) k_conv2d_bwd_ring(ConvDev p, long ctiles,
+                                                                long jtiles, long strips) {
+    using V = Vec4p;
+    using T = float4;
+    constexpr int WS = r2_ws<K>();
+    constexpr int NR = r2_nr<K>();
+    constexpr int ROWF = WS * R2_CG * 4; /* floats per ring row */
+    constexpr int NACC = K * K + 1;
+    constexpr int CPT = (WS * R2_CG + kThreads2d - 1) / kThreads2d; /* copies per thread */
+    extern __shared__ __align__(16) float sm[];
+    float *ring_g = sm;               /* dy rows   [NR][WS][R2_CG][4] */
+    float *ring_i = sm + NR * ROWF;   /* input rows */
+
+    const int tid = threadIdx.x;
+    const int cg = tid % R2_CG;
+    const int jj = tid / R2_CG;
+    const long H = p.dims[0], W = p.dims[1], D = p.D;
+    const long ct = blockIdx.x % ctiles;
+    const long jt = blockIdx.x / ctiles;
+    const long c0 = ct * R2_CG * 4;
+    const long j0 = jt * R2_TJ;
+    const long j = j0 + jj;
+    const long b = blockIdx.z;
+    const long r0 = (long)blockIdx.y * R2_TI;
+    const long rend = min(H, r0 + R2_TI);
+    const int cnt = (int)(rend - r0);       /* rows of this strip */
+    const int nstage = cnt + K - 1;
+    const long jlo = j0 - (K - 1);
+    const bool act = j < W;
+    const float *gbase = p.dy + b * H * W * D + c0;
+    const float *ibase = p.in + b * H * W * D + c0;
+
+    /* this thread's copies of a stage: ring element e = tid + c * kThreads2d
+     * (column jlo + e / R2_CG, channel group e % R2_CG); only the row moves */
+    long coff[CPT];
+    bool cok[CPT];
+#pragma unroll
+    for (int c = 0; c < CPT; ++c) {
+        const int e = tid + c * kThreads2d;
+        const long col = jlo + e / R2_CG;
+        cok[c] = e < WS * R2_CG && col >= 0 && col < W;
+        coff[c] = col * D + (e % R2_CG) * 4;
+    }
+    const long rowst = W * D;
+    auto issue = [&](int m) {
+        if (m < nstage) {
+            const int slot = m % NR;
+            const long rg = rend + K - 2 - m, ri = rend - 1 - m;
+            float *dg = ring_g + slot * ROWF + tid * 4, *di = ring_i + slot * ROWF + tid * 4;
+            const float *sg = gbase + rg * rowst, *si = ibase + ri * rowst;
+#pragma unroll
+            for (int c = 0; c < CPT; ++c) {
+                if (tid + c * kThreads2d < WS * R2_CG) {
+                    const bool gok = cok[c] && rg < H;
+                    const bool iok = cok[c] && ri >= 0;
+                    kmb_cp_async16(dg + c * kThreads2d * 4, gok ? sg + coff[c] : gbase,
+                                   gok ? 16 : 0);
+                    kmb_cp_async16(di + c * kThreads2d * 4, iok ? si + coff[c] : ibase,
+                                   iok ? 16 : 0);
+                }
+            }
+        }
+        kmb_cp_async_commit();
+    };
+
+    T wk[K * K];
+#pragma unroll
+    for (int k = 0; k < K * K; ++k) wk[k] = V::load(p.ker + k * D + c0 + cg * 4);
+    T acc[NACC];
+#pragma unroll
+    for (int k = 0; k < NACC; ++k) acc[k] = V::zero();
+    T gw[K][K], iw[K][K]; /* [stage % K][column] */
+
+    /* the new stage's K dy values (columns j .. j+K-1) and K input values
+     * (columns j-K+1 .. j) of this thread */
+    auto fetch = [&](int m, T (&g)[K], T (&iv)[K]) {
+        const int slot = m % NR;
+        const float *sg = ring_g + slot * ROWF + (jj * R2_CG + cg) * 4;
+        const float *si = ring_i + slot * ROWF + (jj * R2_CG + cg) * 4;
+#pragma unroll
+        for (int q = 0; q < K; ++q) {
+            g[q] = *reinterpret_cast<const T *>(sg + (K - 1 + q) * R2_CG * 4);
+            iv[q] = *reinterpret_cast<const T *>(si + q * R2_CG * 4);
+        }
+    };
+
+#pragma unroll 1
+    for (int m = 0; m < R2_PD; ++m) issue(m);
+    /* stages 0 .. K-2 into the register windows */
+    kmb_cp_async_wait<R2_PD - (K - 1)>();
+    __syncthreads();
+#pragma unroll
+    for (int m = 0; m < K - 1; ++m) fetch(m, gw[m % K], iw[m % K]);
+
+    float *dbase = p.din + b * H * W * D + c0 + cg * 4;
+    /* one row at compile-time phase PH = n % K (its stages are resident) */
+    auto row = [&](int n, auto ph_tag) {
+        constexpr int PH = decltype(ph_tag)::value;
+        constexpr int NEW = (PH + K - 1) % K; /* slot of stage n+K-1 */
+        fetch(n + K - 1, gw[NEW], iw[NEW]);
+        if (act) {
+            const long r = rend - 1 - n;
+            /* dinput(r, j) = sum dy(r + K-1-k0, j + K-1-k1) w[k0][k1];
+             * dy row r + K-1-k0 is stage n + k0 */
+            T s = V::zero();
+#pragma unroll
+            for (int k0 = 0; k0 < K; ++k0)
+#pragma unroll
+                for (int k1 = 0; k1 < K; ++k1)
+                    s = V::fma(gw[(PH + k0) % K][K - 1 - k1], wk[k0 * K + k1], s);
+            V::store(dbase + (r * W + j) * D, s);
+            /* dkernel: dy(r, j) (stage n+K-1, column 0) times input
+             * (r - (K-1) + k0, j - (K-1) + k1) (stage n + K-1-k0) */
+            const T gy = gw[NEW][0];
+#pragma unroll
+            for (int k0 = 0; k0 < K; ++k0)
+#pragma unroll
+                for (int k1 = 0; k1 < K; ++k1)
+                    acc[k0 * K + k1] = V::fma(gy, iw[(PH + K - 1 - k0) % K][k1], acc[k0 * K + k1]);
+            acc[K * K] = V::add(acc[K * K], gy);
+        }
+    };
+    /* rows n .. n+K-1 share one wait and one barrier: they read stages
+     * n+K-1 .. n+2K-2, and stages n+PD .. n+PD+K-1 go out first */
+    for (int n = 0; n < cnt; n += K) {
+#pragma unroll
+        for (int i = 0; i < K; ++i) issue(n + R2_PD + i);
+        kmb_cp_async_wait<R2_PD - K + 1>();
+        __syncthreads();
+        row(n, std::integral_constant<int, 0>{});
+        if (K > 1 && n + 1 < cnt) row(n + 1, std::integral_constant<int, 1 % K>{});
+        if (K > 2 && n + 2 < cnt) row(n + 2, std::integral_constant<int, 2 % K>{});
+        if (K > 3 && n + 3 < cnt) row(n + 3, std::integral_constant<int, 3 % K>{});
+        if (K > 4 && n + 4 < cnt) row(n + 4, std::integral_constant<int, 4 % K>{});
+    }
+
+    /* the ring is reused for the fold: no copy may still be in flight */
+    kmb_cp_async_wait<0>();
+    __syncthreads();
+    float *red = sm; /* [kThreads2d][NACC][4] */
+#pragma unroll
+    for (int k = 0; k < NACC; ++k)
+        *reinterpret_cast<T *>(red + (tid * NACC + k) * 4) = act ? acc[k] : V::zero();
+    __syncthreads();
+    for (int o = tid; o < R2_CG * NACC * 4; o += kThreads2d) {
+        const int i = o % 4;
+        const int k = (o / 4) % NACC;
+        const int cgo = o / (4 * NACC);
+        const long cc = c0 + cgo * 4 + i;
+        float s = 0.f;
+        for (int q = 0; q < R2_TJ; ++q) s += red[((q * R2_CG + cgo) * NACC + k) * 4 + i];
+        if (k < K * K) atomicAdd(p.dker + (long)k * D + cc, s);
+        else if (p.dbias) atomicAdd(p.dbias + cc, s);
+    }
+}
+
+template <int K>
+cudaError_t launch2d_bwd_ring(const ConvDev &p, cudaStream_t s) {
+    const long ctiles = p.D / (4 * R2_CG);
+    const long jtiles = (p.dims[1] + R2_TJ - 1) / R2_TJ;
+    const long strips = (p.dims[0] + R2_TI - 1) / R2_TI;
+    const size_t smem = r2_smem_bytes<K>();
+    auto kern = k_conv2d_bwd_ring<K>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+    dim3 grid((unsigned)(ctiles * jtiles), (unsigned)strips, (unsigned)p.batch);
+    kern<<<grid, kThreads2d, smem, s>>>(p, ctiles, jtiles, strips);
+    return cudaGetLastError();
+}
+
+/*
+ * Forward with the same streamed rows: stage m is input row r0-(K-1)+m
+ * (R2_TJ + K-1 columns with the left halo); row r = r0+n reads stages
+ * n .. n+K-1 from its K x K register window.
+ */
+template <int K>
+__host__ __device__ constexpr int r2f_ws() { return R2_TJ + K - 1; }
+
+template <int K>
+__host__ __device__ constexpr size_t r2f_smem_bytes() {
+    return (size_t)r2_nr<K>() * r2f_ws<K>() * R2_CG * 16;
+}
+
+template <int K, class V>
+__global__ void __launch_bounds__(kThreads2d) k_conv2d_fwd_ring(ConvDev p, long ctiles) {
+    using T = float4;
+    constexpr int WS = r2f_ws<K>();
+    constexpr int NR = r2_nr<K>();
+    constexpr int ROWF = WS * R2_CG * 4;
+    constexpr int CPT = (WS * R2_CG + kThreads2d - 1) / kThreads2d;
+    extern __shared__ __align__(16) float sm[];
+
+    const int tid = threadIdx.x;
+    const int cg = tid % R2_CG;
+    const int jj = tid / R2_CG;
+    const long H = p.dims[0], W = p.dims[1], D = p.D;
+    const long ct = blockIdx.x % ctiles;
+    const long jt = blockIdx.x / ctiles;
+    const long c0 = ct * R2_CG * 4;
+    const long j0 = jt * R2_TJ;
+    const long j = j0 + jj;
+    const long b = blockIdx.z;
+    const long r0 = (long)blockIdx.y * R2_TI;
+    const long rend = min(H, r0 + R2_TI);
+    const int cnt = (int)(rend - r0);
+    const int nstage = cnt + K - 1;
+    const long jlo = j0 - (K - 1);
+    const bool act = j < W;
+    const float *ibase = p.in + b * H * W * D + c0;
+
+    long coff[CPT];
+    bool cok[CPT];
+#pragma unroll
+    for (int c = 0; c < CPT; ++c) {
+        const int e = tid + c * kThreads2d;
+        const long col = jlo + e / R2_CG;
+        cok[c] = e < WS * R2_CG && col >= 0 && col < W;
+        coff[c] = col * D + (e % R2_CG) * 4;
+    }
+    const long rowst = W * D;
+    auto issue = [&](int m) {
+        if (m < nstage) {
+            const long ri = r0 - (K - 1) + m;
+            float *di = sm + (m % NR) * ROWF + tid * 4;
+            const float *si = ibase + ri * rowst;
+#pragma unroll
+            for (int c = 0; c < CPT; ++c) {
+                if (tid + c * kThreads2d < WS * R2_CG) {
+                    const bool ok = cok[c] && ri >= 0;
+                    kmb_cp_async16(di + c * kThreads2d * 4, ok ? si + coff[c] : ibase,
+                                   ok ? 16 : 0);
+                }
+            }
+        }
+        kmb_cp_async_commit();
+    };
+
+    T wk[K * K];
+#pragma unroll
+    for (int k = 0; k < K * K; ++k) wk[k] = V::load(p.ker + k * D + c0 + cg * 4);
+    const T bias = p.bias ? V::load(p.bias + c0 + cg * 4) : V::zero();
+    T iw[K][K]; /* [stage % K][column] */
+    auto fetch = [&](int m, T (&iv)[K]) {
+        const float *si = sm + (m % NR) * ROWF + (jj * R2_CG + cg) * 4;
+#pragma unroll
+        for (int q = 0; q < K; ++q) iv[q] = *reinterpret_cast<const T *>(si + q * R2_CG * 4);
+    };
+
+#pragma unroll 1
+    for (int m = 0; m < R2_PD; ++m) issue(m);
+    kmb_cp_async_wait<R2_PD - (K - 1)>();
+    __syncthreads();
+#pragma unroll
+    for (int m = 0; m < K - 1; ++m) fetch(m, iw[m % K]);
+
+    float *obase = p.out + b * H * W * D + c0 + cg * 4;
+    auto row = [&](int n, auto ph_tag) {
+        constexpr int PH = decltype(ph_tag)::value;
+        fetch(n + K - 1, iw[(PH + K - 1) % K]);
+        if (act) {
+            T s = bias;
+#pragma unroll
+            for (int k0 = 0; k0 < K; ++k0)
+#pragma unroll
+                for (int k1 = 0; k1 < K; ++k1)
+                    s = V::fma(iw[(PH + k0) % K][k1], wk[k0 * K + k1], s);
+            V::store(obase + ((r0 + n) * W + j) * D, s);
+        }
+    };
+    for (int n = 0; n < cnt; n += K) {
+#pragma unroll
+        for (int i = 0; i < K; ++i) issue(n + R2_PD + i);
+        kmb_cp_async_wait<R2_PD - K + 1>();
+        __syncthreads();
+        row(n, std::integral_constant<int, 0>{});
+        if (K > 1 && n + 1 < cnt) row(n + 1, std::integral_constant<int, 1 % K>{});
+        if (K > 2 && n + 2 < cnt) row(n + 2, std::integral_constant<int, 2 % K>{});
+    }
+    kmb_cp_async_wait<0>();
+}
+
+template <int K>
+cudaError_t launch2d_fwd_ring(const ConvDev &p, cudaStream_t s) {
+    const long ctiles = p.D / (4 * R2_CG);
+    const long jtiles = (p.dims[1] + R2_TJ - 1) / R2_TJ;
+    const long strips = (p.dims[0] + R2_TI - 1) / R2_TI;
+    const size_t smem = r2f_smem_bytes<K>();
+    auto kern = k_conv2d_fwd_ring<K, Vec<4>>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+    dim3 grid((unsigned)(ctiles * jtiles), (unsigned)strips, (unsigned)p.batch);
+    kern<<<grid, kThreads2d, smem, s>>>(p, ctiles);
+    return cudaGetLastError();
+}
+
+/* K <= 3: the two K x K float4 windows, the taps and the accumulators fit
+ * the register file without spills up to K = 3 */
+constexpr int R2_KMAX = 3;
+
+cudaError_t dispatch2d_fwd_ring(const ConvDev &p, cudaStream_t s) {
+    switch (p.K) {
+    case 1: return launch2d_fwd_ring<1>(p, s);
+    case 2: return launch2d_fwd_ring<2>(p, s);
+    case 3: return launch2d_fwd_ring<3>(p, s);
+    default: return cudaErrorNotSupported;
+    }
+}
+
+cudaError_t dispatch2d_bwd_ring(const ConvDev &p, cudaStream_t s) {
+    switch (p.K) {
+    case 1: return launch2d_bwd_ring<1>(p, s);
+    case 2: return launch2d_bwd_ring<2>(p, s);
+    case 3: return launch2d_bwd_ring<3>(p, s);
+    default: return cudaErrorNotSupported;
     }
 }
 
@@ -438,7 +822,10 @@ extern "C" int kmb_launch_convnd_fwd(const KmbConvND *a, cudaStream_t s) {
     make_dev(a, &p);
     cudaError_t e;
     if (use_2d(p)) {
-        e = aligned4(a, false) ? dispatch2d<4>(p, false, s) : dispatch2d<1>(p, false, s);
+        if (aligned4(a, false) && p.D % (4 * R2_CG) == 0 && p.K <= R2_KMAX)
+            e = dispatch2d_fwd_ring(p, s);
+        else
+            e = aligned4(a, false) ? dispatch2d<4>(p, false, s) : dispatch2d<1>(p, false, s);
     } else {
         k_convnd_fwd_generic<<<grid_for(p.batch * p.P * p.D, 256), 256, 0, s>>>(p);
         e = cudaGetLastError();
@@ -454,7 +841,9 @@ extern "C" int kmb_launch_convnd_bwd(const KmbConvND *a, cudaStream_t s) {
     if (e == cudaSuccess && a->dbias) e = cudaMemsetAsync(a->dbias, 0, sizeof(float) * p.D, s);
     if (e != cudaSuccess) return kmb_cuda_fail(e, "convnd backward memset");
     if (use_2d(p)) {
-        e = aligned4(a, true) ? dispatch2d<4>(p, true, s) : dispatch2d<1>(p, true, s);
+        if (aligned4(a, true) && p.D % (4 * R2_CG) == 0 && p.K <= R2_KMAX)
+            e = dispatch2d_bwd_ring(p, s);
+        else e = aligned4(a, true) ? dispatch2d<4>(p, true, s) : dispatch2d<1>(p, true, s);
     } else {
         k_convnd_bwd_input_generic<<<grid_for(p.batch * p.P * p.D, 256), 256, 0, s>>>(p);
         e = cudaGetLastError();

@@ -82,11 +82,30 @@ def kb_conv(dims, batch, D, K, ti, tk, tb, out, tdy, din, dk, db):
     return a
 
 
+def dkernel_f64(dims, K, inp, dy):
+    """float64 dkernel / dbias of the reference's definition
+    (src/convnd.c): dker[k, d] = sum_p dy(p, d) in(p - (K-1-k_axis), d),
+    k row-major over axes, zero outside the grid; summed over the batch."""
+    nd = len(dims)
+    x = inp.astype(np.float64).reshape((inp.shape[0], *dims, -1))
+    g = dy.astype(np.float64).reshape((dy.shape[0], *dims, -1))
+    pad = [(0, 0)] + [(K - 1, 0)] * nd + [(0, 0)]
+    xp = np.pad(x, pad)
+    out = []
+    for k in np.ndindex(*([K] * nd)):
+        sl = (slice(None),) + tuple(slice(ka, ka + n) for ka, n in zip(k, dims)) + (slice(None),)
+        out.append((g * xp[sl]).sum(axis=tuple(range(nd + 1))))
+    return np.stack(out), g.sum(axis=tuple(range(nd + 1)))
+
+
 @pytest.mark.parametrize("dims,D,K,bias", [
     ([33, 17], 64, 3, True), ([20, 70], 8, 2, True), ([9, 11], 5, 3, True),
     ([16, 16], 12, 4, False), ([5, 40], 4, 5, True), ([1, 64], 16, 3, True),
     ([3, 300], 64, 1, True), ([13], 7, 3, True), ([6, 5, 7], 4, 3, True),
-    ([3, 4, 2, 5], 3, 2, False), ([60], 64, 4, True)])
+    ([3, 4, 2, 5], 3, 2, False), ([60], 64, 4, True),
+    # streamed-row backward (D % 64 == 0, K <= 3): several strips, ragged
+    # strips and column tiles
+    ([260, 33], 64, 3, True), ([150, 40], 128, 2, False), ([129, 16], 64, 3, True)])
 def test_batched_vs_oracle(lib, cuda, oracle, dims, D, K, bias):
     rng = np.random.default_rng(sum(dims) * 13 + D + K)
     batch = 3
@@ -106,9 +125,15 @@ def test_batched_vs_oracle(lib, cuda, oracle, dims, D, K, bias):
         assert rel_err(din[i], di) <= TOL
         dk_ref += dki
         db_ref += dbi
-    assert rel_err(dk, dk_ref) <= TOL
+    # dkernel / dbias are sums over batch * P points: held to the 1e-4 bar
+    # against float64, and to the fp32 oracle within that oracle's own
+    # rounding (its sequential fp32 sums drift ~1e-4 on 2.5e4 points)
+    dk64, db64 = dkernel_f64(dims, K, inp, dy)
+    assert rel_err(dk, dk64) <= TOL
+    assert rel_err(dk, dk_ref) <= TOL + rel_err(dk_ref, dk64)
     if bias:
-        assert rel_err(db, db_ref) <= TOL
+        assert rel_err(db, db64) <= TOL
+        assert rel_err(db, db_ref) <= TOL + rel_err(db_ref, db64)
 
 
 def test_config3_full_size(lib, cuda, oracle):
