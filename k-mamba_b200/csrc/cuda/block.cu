@@ -34,10 +34,13 @@ namespace {
 
 constexpr int kTM = 64, kTN = 64, kTK = 16;
 
-/* C[m*ldc + n] (+)= sum_k A[m*am + k*ak] * B[k*bk + n*bn] */
+/* C[m*ldc + n] (+)= sum_k A[m*am + k*ak] * B[k*bk + n*bn].  With ws set,
+ * CTA z of blockIdx.z sums k in [z*kchunk, (z+1)*kchunk) and writes its
+ * partial tile to ws[z][M][N] instead (split-K; k_gemm_reduce adds the
+ * partials in z order, so the result does not depend on scheduling). */
 __global__ void __launch_bounds__(256)
 k_gemm(int M, int N, int K, const float *A, long am, long ak, const float *B, long bk,
-       long bn, float *C, long ldc, int accumulate) {
+       long bn, float *C, long ldc, int accumulate, float *ws, int kchunk) {
     __shared__ float As[kTK][kTM + 4];
     __shared__ float Bs[kTK][kTN + 4];
     const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
@@ -48,18 +51,20 @@ k_gemm(int M, int N, int K, const float *A, long am, long ak, const float *B, lo
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
     const bool a_kfast = ak == 1, b_nfast = bn == 1;
-    for (int k0 = 0; k0 < K; k0 += kTK) {
+    const int kbeg = ws ? (int)blockIdx.z * kchunk : 0;
+    const int kend = ws ? min(K, kbeg + kchunk) : K;
+    for (int k0 = kbeg; k0 < kend; k0 += kTK) {
         for (int e = threadIdx.x; e < kTM * kTK; e += 256) {
             int mm, kk;
             if (a_kfast) { mm = e / kTK; kk = e % kTK; } else { kk = e / kTM; mm = e % kTM; }
             const int gm = m0 + mm, gk = k0 + kk;
-            As[kk][mm] = (gm < M && gk < K) ? A[gm * am + gk * ak] : 0.f;
+            As[kk][mm] = (gm < M && gk < kend) ? A[gm * am + gk * ak] : 0.f;
         }
         for (int e = threadIdx.x; e < kTK * kTN; e += 256) {
             int nn, kk;
             if (b_nfast) { kk = e / kTN; nn = e % kTN; } else { nn = e / kTK; kk = e % kTK; }
             const int gn = n0 + nn, gk = k0 + kk;
-            Bs[kk][nn] = (gn < N && gk < K) ? B[gk * bk + gn * bn] : 0.f;
+            Bs[kk][nn] = (gn < N && gk < kend) ? B[gk * bk + gn * bn] : 0.f;
         }
         __syncthreads();
 #pragma unroll
@@ -84,9 +89,58 @@ k_gemm(int M, int N, int K, const float *A, long am, long ak, const float *B, lo
         for (int j = 0; j < 4; ++j) {
             const int gn = n0 + tx * 4 + j;
             if (gn >= N) continue;
-            float *c = C + (long)gm * ldc + gn;
-            *c = accumulate ? *c + acc[i][j] : acc[i][j];
+            if (ws) {
+                ws[((long)blockIdx.z * M + gm) * N + gn] = acc[i][j];
+            } else {
+                float *c = C + (long)gm * ldc + gn;
+                *c = accumulate ? *c + acc[i][j] : acc[i][j];
+            }
         }
+    }
+}
+
+__global__ void k_gemm_reduce(const float *ws, int S, int M, int N, float *C, long ldc,
+                              int accumulate) {
+    const long tot = (long)M * N;
+    for (long e = (long)blockIdx.x * blockDim.x + threadIdx.x; e < tot;
+         e += (long)gridDim.x * blockDim.x) {
+        float s = 0.f;
+        for (int z = 0; z < S; ++z) s += ws[z * tot + e];
+        float *c = C + (e / N) * ldc + e % N;
+        *c = accumulate ? *c + s : s;
+    }
+}
+
+/* N = 1: C[m*ldc] (+)= sum_k A[m*am + k*ak] B[k*bk]; one warp per m */
+__global__ void k_gemv_n1(int M, int K, const float *A, long am, long ak, const float *B,
+                          long bk, float *C, long ldc, int accumulate) {
+    const int lane = threadIdx.x & 31;
+    const long m = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (m >= M) return;
+    float s = 0.f;
+    for (int k = lane; k < K; k += 32) s = fmaf(A[m * am + k * ak], B[k * bk], s);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) C[m * ldc] = accumulate ? C[m * ldc] + s : s;
+}
+
+/* M = 1: C[n] (+)= sum_k A[k*ak] B[k*bk + n*bn]; a CTA of 32 n x 8 k
+ * slices, the slices folded through shared memory in order */
+__global__ void __launch_bounds__(256) k_gemv_m1(int N, int K, const float *A, long ak,
+                                                 const float *B, long bk, long bn, float *C,
+                                                 int accumulate) {
+    __shared__ float red[8][33];
+    const int nn = threadIdx.x & 31, ks = threadIdx.x >> 5;
+    const long n = (long)blockIdx.x * 32 + nn;
+    float s = 0.f;
+    if (n < N)
+        for (int k = ks; k < K; k += 8) s = fmaf(A[k * ak], B[k * bk + n * bn], s);
+    red[ks][nn] = s;
+    __syncthreads();
+    if (ks == 0 && n < N) {
+        float t = 0.f;
+        for (int i = 0; i < 8; ++i) t += red[i][nn];
+        C[n] = accumulate ? C[n] + t : t;
     }
 }
 
@@ -178,202 +232,273 @@ struct ScanArgs {
     const float *theta;  /* [N/2] */
     float *h_hist;       /* [batch, L, N] or NULL */
     float *h_last;       /* [batch, N] final state, or NULL */
-    float *y;            /* [batch, L, R] */
+    float *part;         /* [batch, G, L, R (+2 backward)] per-warp partial sums */
     /* backward */
     const float *dy;     /* [batch, L, R] */
     float *dz;           /* [batch, L, W] (u, dt, lam, B, C columns) */
     float *dA;           /* [N], accumulated */
     float *dtheta;       /* [N/2], accumulated */
-    int L, N, R, W;
+    int L, N, R, W, G;   /* G = warps (32-pair groups) per sequence */
 };
 
-/* block-wide sum of `cnt` values (cnt <= kMaxR + 2); result in red[0..cnt) */
-__device__ __forceinline__ void block_sum(float *v, int cnt, float *red, int nwarps) {
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    for (int k = 0; k < cnt; ++k) {
-        float x = v[k];
+__device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-        if (lane == 0) red[k * 32 + w] = x;
-    }
-    __syncthreads();
-    if (threadIdx.x < cnt) {
-        float s = 0.f;
-        for (int i = 0; i < nwarps; ++i) s += red[threadIdx.x * 32 + i];
-        red[kMaxR * 32 + 64 + threadIdx.x] = s;
-    }
-    __syncthreads();
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
 }
 
-__global__ void __launch_bounds__(1024) k_m3_scan_fwd(ScanArgs a) {
-    __shared__ float red[(kMaxR + 2) * 32 + 64 + 16];
-    const int b = blockIdx.x;
+/* The controls of one step as a thread of pair (n0, n0+1) needs them; RT
+ * is a compile-time bound on the rank R so the arrays stay in registers. */
+template <int RT>
+struct StepIn {
+    float dt, lam;
+    float u[RT];
+    float2 b[RT], c[RT];
+    float2 h;      /* backward: the stored state pair h_t */
+    float dy[RT];  /* backward: dy_t */
+};
+
+/* the backward's extra per-step inputs of step t */
+template <int RT>
+__device__ __forceinline__ void load_step_bwd(const float *hb, const float *dyb, int t, int R,
+                                              int N, int n0, bool act, bool has1,
+                                              StepIn<RT> &s) {
+    s.h = make_float2(act ? hb[(long)t * N + n0] : 0.f, has1 ? hb[(long)t * N + n0 + 1] : 0.f);
+#pragma unroll
+    for (int r = 0; r < RT; ++r)
+        if (r < R) s.dy[r] = dyb[(long)t * R + r];
+}
+
+template <int RT>
+__device__ __forceinline__ void load_step(const float *row, int R, int N, int n0, bool act,
+                                          bool has1, StepIn<RT> &s) {
+    s.dt = row[R];
+    s.lam = row[R + 1];
+    const float *Bt = row + R + 2;
+    const float *Ct = Bt + R * N;
+#pragma unroll
+    for (int r = 0; r < RT; ++r) {
+        if (r < R) {
+            s.u[r] = row[r];
+            s.b[r] = make_float2(act ? Bt[r * N + n0] : 0.f, has1 ? Bt[r * N + n0 + 1] : 0.f);
+            s.c[r] = make_float2(act ? Ct[r * N + n0] : 0.f, has1 ? Ct[r * N + n0 + 1] : 0.f);
+        }
+    }
+}
+
+/*
+ * Mamba-3 scan.  A sequence runs on G one-warp CTAs, each owning 32 state
+ * pairs (2i, 2i+1) (the rotation couples only a pair); the pairs are
+ * independent chains, so only the sums over states (y, and in the
+ * backward du / ddt / dlambda) need the other warps.  They go to `part`
+ * and a second kernel adds the G partials in order.  Each step's controls
+ * are loaded one step ahead.
+ */
+template <int RT>
+__global__ void __launch_bounds__(32) k_m3_scan_fwd(ScanArgs a) {
+    const int b = blockIdx.y, g = blockIdx.x;
     const int N = a.N, R = a.R, W = a.W, L = a.L;
-    const int npairs = (N + 1) / 2;
-    const int i = threadIdx.x; /* pair index */
-    const bool act = i < npairs;
-    const int n0 = 2 * i, n1 = 2 * i + 1;
-    const bool has1 = act && n1 < N;
-    const bool rot = has1; /* an odd N leaves its last state unrotated */
+    const int i = g * 32 + threadIdx.x; /* pair index */
+    const int n0 = 2 * i;
+    const bool act = n0 < N;
+    const bool has1 = n0 + 1 < N; /* an odd N leaves its last state unrotated */
     float cv = 1.f, sv = 0.f, A0 = 0.f, A1 = 0.f;
     if (act) {
         A0 = a.A[n0];
-        if (has1) A1 = a.A[n1];
-        if (rot) {
+        if (has1) {
+            A1 = a.A[n0 + 1];
             const float th = a.theta[i];
             cv = cosf(th);
             sv = sinf(th);
         }
     }
     float h0 = 0.f, h1 = 0.f, pb0 = 0.f, pb1 = 0.f;
-    const int nw = (blockDim.x + 31) / 32;
     const float *zb = a.zact + (long)b * L * W;
-    for (int t = 0; t < L; ++t) {
-        const float *row = zb + (long)t * W;
-        const float dt = row[R], lam = row[R + 1];
-        const float *Bt = row + R + 2;
-        const float *Ct = Bt + R * N;
-        float yp[kMaxR];
-        for (int r = 0; r < R; ++r) yp[r] = 0.f;
-        if (act) {
-            float bu0 = 0.f, bu1 = 0.f;
-            for (int r = 0; r < R; ++r) {
-                const float ur = row[r];
-                bu0 += Bt[r * N + n0] * ur;
-                if (has1) bu1 += Bt[r * N + n1] * ur;
-            }
-            const float hr0 = rot ? cv * h0 - sv * h1 : h0;
-            const float hr1 = rot ? sv * h0 + cv * h1 : h1;
-            const float al0 = expf(dt * A0), al1 = expf(dt * A1);
-            const float be0 = (1.0f - lam) * dt * al0, be1 = (1.0f - lam) * dt * al1;
-            const float ga = lam * dt;
-            h0 = al0 * hr0 + be0 * pb0 + ga * bu0;
-            h1 = has1 ? al1 * hr1 + be1 * pb1 + ga * bu1 : 0.f;
-            pb0 = bu0;
-            pb1 = bu1;
-            if (a.h_hist) {
-                float *hh = a.h_hist + ((long)b * L + t) * N;
-                hh[n0] = h0;
-                if (has1) hh[n1] = h1;
-            }
-            for (int r = 0; r < R; ++r)
-                yp[r] = Ct[r * N + n0] * h0 + (has1 ? Ct[r * N + n1] * h1 : 0.f);
+    float *part = a.part + ((long)b * a.G + g) * L * R;
+    /* ring of PF steps loaded ahead; slot t % PF, compile-time in the
+     * unrolled loop */
+    constexpr int PF = RT <= 2 ? 4 : 2;
+    StepIn<RT> ring[PF];
+#pragma unroll
+    for (int k = 0; k < PF; ++k)
+        if (k < L) load_step(zb + (long)k * W, R, N, n0, act, has1, ring[k]);
+    for (int t0 = 0; t0 < L; t0 += PF)
+#pragma unroll
+    for (int k = 0; k < PF; ++k) {
+        const int t = t0 + k;
+        if (t >= L) break;
+        StepIn<RT> &cur = ring[k];
+        const float dt = cur.dt, lam = cur.lam;
+        float bu0 = 0.f, bu1 = 0.f;
+        for (int r = 0; r < RT; ++r) {
+            if (r >= R) break;
+            bu0 += cur.b[r].x * cur.u[r];
+            bu1 += cur.b[r].y * cur.u[r];
         }
-        block_sum(yp, R, red, nw);
-        if (threadIdx.x < R) a.y[((long)b * L + t) * R + threadIdx.x] = red[kMaxR * 32 + 64 + threadIdx.x];
+        const float hr0 = has1 ? cv * h0 - sv * h1 : h0;
+        const float hr1 = has1 ? sv * h0 + cv * h1 : h1;
+        const float al0 = expf(dt * A0), al1 = expf(dt * A1);
+        const float be0 = (1.0f - lam) * dt * al0, be1 = (1.0f - lam) * dt * al1;
+        const float ga = lam * dt;
+        h0 = act ? al0 * hr0 + be0 * pb0 + ga * bu0 : 0.f;
+        h1 = has1 ? al1 * hr1 + be1 * pb1 + ga * bu1 : 0.f;
+        pb0 = bu0;
+        pb1 = bu1;
+        if (a.h_hist && act) {
+            float *hh = a.h_hist + ((long)b * L + t) * N;
+            hh[n0] = h0;
+            if (has1) hh[n0 + 1] = h1;
+        }
+        for (int r = 0; r < RT; ++r) {
+            if (r >= R) break;
+            const float yp = warp_sum(cur.c[r].x * h0 + cur.c[r].y * h1);
+            if (threadIdx.x == 0) part[t * R + r] = yp;
+        }
+        if (t + PF < L) load_step(zb + (long)(t + PF) * W, R, N, n0, act, has1, cur);
     }
     if (a.h_last && act) {
         a.h_last[(long)b * N + n0] = h0;
-        if (has1) a.h_last[(long)b * N + n1] = h1;
+        if (has1) a.h_last[(long)b * N + n0 + 1] = h1;
     }
 }
 
-__global__ void __launch_bounds__(1024) k_m3_scan_bwd(ScanArgs a) {
-    __shared__ float red[(kMaxR + 2) * 32 + 64 + 16];
-    const int b = blockIdx.x;
+template <int RT>
+__global__ void __launch_bounds__(32) k_m3_scan_bwd(ScanArgs a) {
+    const int b = blockIdx.y, g = blockIdx.x;
     const int N = a.N, R = a.R, W = a.W, L = a.L;
-    const int npairs = (N + 1) / 2;
-    const int i = threadIdx.x;
-    const bool act = i < npairs;
-    const int n0 = 2 * i, n1 = 2 * i + 1;
-    const bool has1 = act && n1 < N;
+    const int i = g * 32 + threadIdx.x;
+    const int n0 = 2 * i;
+    const bool act = n0 < N;
+    const bool has1 = n0 + 1 < N;
     const bool rot = has1;
     float cv = 1.f, sv = 0.f, A0 = 0.f, A1 = 0.f;
     if (act) {
         A0 = a.A[n0];
-        if (has1) A1 = a.A[n1];
-        if (rot) {
+        if (has1) {
+            A1 = a.A[n0 + 1];
             const float th = a.theta[i];
             cv = cosf(th);
             sv = sinf(th);
         }
     }
-    const int nw = (blockDim.x + 31) / 32;
     const float *zb = a.zact + (long)b * L * W;
     float *dzb = a.dz + (long)b * L * W;
     const float *hb = a.h_hist + (long)b * L * N;
-    /* carry = R^T(alpha_{t+1} * G_{t+1});  bgn = beta_{t+1} * G_{t+1} */
+    const int RP = R + 2;
+    float *part = a.part + ((long)b * a.G + g) * L * RP;
+    /* carry = R^T(alpha_{t+1} * G_{t+1});  bg = beta_{t+1} * G_{t+1} */
     float c0 = 0.f, c1 = 0.f, bg0 = 0.f, bg1 = 0.f, sA0 = 0.f, sA1 = 0.f, sth = 0.f;
-    for (int t = L - 1; t >= 0; --t) {
-        const float *row = zb + (long)t * W;
-        const float dt = row[R], lam = row[R + 1];
-        const float *Bt = row + R + 2;
-        const float *Ct = Bt + R * N;
-        const float *dyt = a.dy + ((long)b * L + t) * R;
-        float part[kMaxR + 2];
-        for (int k = 0; k < R + 2; ++k) part[k] = 0.f;
-        if (act) {
-            float bu0 = 0.f, bu1 = 0.f, pb0 = 0.f, pb1 = 0.f;
-            for (int r = 0; r < R; ++r) {
-                const float ur = row[r];
-                bu0 += Bt[r * N + n0] * ur;
-                if (has1) bu1 += Bt[r * N + n1] * ur;
-            }
+    /* ring of PF steps t, t-1, ... loaded ahead; step t sits in slot
+     * (L-1-t) % PF, compile-time in the unrolled loop */
+    constexpr int PF = RT <= 2 ? 4 : 2;
+    StepIn<RT> ring[PF];
+    const float *dyb = a.dy + (long)b * L * R;
+#pragma unroll
+    for (int k = 0; k < PF; ++k) {
+        if (L - 1 - k >= 0) {
+            load_step(zb + (long)(L - 1 - k) * W, R, N, n0, act, has1, ring[k]);
+            load_step_bwd(hb, dyb, L - 1 - k, R, N, n0, act, has1, ring[k]);
+        }
+    }
+    for (int j0 = 0; j0 < L; j0 += PF)
+#pragma unroll
+    for (int k = 0; k < PF; ++k) {
+        const int t = L - 1 - (j0 + k);
+        if (t < 0) break;
+        StepIn<RT> &cur = ring[k];
+        const StepIn<RT> &prv = ring[(k + 1) % PF];
+        const float dt = cur.dt, lam = cur.lam;
+        const float *dyt = cur.dy;
+        float bu0 = 0.f, bu1 = 0.f, pb0 = 0.f, pb1 = 0.f;
+        for (int r = 0; r < RT; ++r) {
+            if (r >= R) break;
+            bu0 += cur.b[r].x * cur.u[r];
+            bu1 += cur.b[r].y * cur.u[r];
             if (t > 0) {
-                const float *prow = row - W;
-                const float *Bp = prow + R + 2;
-                for (int r = 0; r < R; ++r) {
-                    const float ur = prow[r];
-                    pb0 += Bp[r * N + n0] * ur;
-                    if (has1) pb1 += Bp[r * N + n1] * ur;
-                }
-            }
-            const float hp0 = t > 0 ? hb[(long)(t - 1) * N + n0] : 0.f;
-            const float hp1 = (t > 0 && has1) ? hb[(long)(t - 1) * N + n1] : 0.f;
-            const float ht0 = hb[(long)t * N + n0];
-            const float ht1 = has1 ? hb[(long)t * N + n1] : 0.f;
-            float G0 = c0, G1 = c1;
-            for (int r = 0; r < R; ++r) {
-                G0 = fmaf(Ct[r * N + n0], dyt[r], G0);
-                if (has1) G1 = fmaf(Ct[r * N + n1], dyt[r], G1);
-            }
-            const float hr0 = rot ? cv * hp0 - sv * hp1 : hp0;
-            const float hr1 = rot ? sv * hp0 + cv * hp1 : hp1;
-            const float al0 = expf(dt * A0), al1 = has1 ? expf(dt * A1) : 0.f;
-            const float oml = 1.0f - lam;
-            const float ga0 = G0 * (hr0 + oml * dt * pb0);
-            const float ga1 = G1 * (hr1 + oml * dt * pb1);
-            /* ddt, dlam */
-            part[R] = ga0 * A0 * al0 + G0 * (oml * al0 * pb0 + lam * bu0) +
-                      ga1 * A1 * al1 + G1 * (oml * al1 * pb1 + lam * bu1);
-            part[R + 1] = G0 * dt * (bu0 - al0 * pb0) + G1 * dt * (bu1 - al1 * pb1);
-            sA0 = fmaf(ga0 * dt, al0, sA0);
-            sA1 = fmaf(ga1 * dt, al1, sA1);
-            /* Bu_t feeds h_t (gamma) and h_{t+1} (beta_{t+1}) */
-            const float dbu0 = lam * dt * G0 + bg0;
-            const float dbu1 = lam * dt * G1 + bg1;
-            bg0 = oml * dt * al0 * G0;
-            bg1 = oml * dt * al1 * G1;
-            float *dzr = dzb + (long)t * W;
-            for (int r = 0; r < R; ++r) {
-                const float ur = row[r];
-                dzr[R + 2 + r * N + n0] = dbu0 * ur;
-                dzr[R + 2 + R * N + r * N + n0] = dyt[r] * ht0;
-                part[r] = dbu0 * Bt[r * N + n0];
-                if (has1) {
-                    dzr[R + 2 + r * N + n1] = dbu1 * ur;
-                    dzr[R + 2 + R * N + r * N + n1] = dyt[r] * ht1;
-                    part[r] += dbu1 * Bt[r * N + n1];
-                }
-            }
-            /* rotation: h_rot = R h_{t-1};  d h_rot = alpha * G */
-            const float dr0 = al0 * G0, dr1 = al1 * G1;
-            if (rot) {
-                sth += dr0 * (-sv * hp0 - cv * hp1) + dr1 * (cv * hp0 - sv * hp1);
-                c0 = cv * dr0 + sv * dr1;
-                c1 = -sv * dr0 + cv * dr1;
-            } else {
-                c0 = dr0;
-                c1 = dr1;
+                pb0 += prv.b[r].x * prv.u[r];
+                pb1 += prv.b[r].y * prv.u[r];
             }
         }
-        block_sum(part, R + 2, red, nw);
-        if (threadIdx.x < R + 2) dzb[(long)t * W + threadIdx.x] = red[kMaxR * 32 + 64 + threadIdx.x];
+        const float hp0 = t > 0 ? prv.h.x : 0.f;
+        const float hp1 = t > 0 ? prv.h.y : 0.f;
+        const float ht0 = cur.h.x, ht1 = cur.h.y;
+        float G0 = c0, G1 = c1;
+        for (int r = 0; r < RT; ++r) {
+            if (r >= R) break;
+            G0 = fmaf(cur.c[r].x, dyt[r], G0);
+            G1 = fmaf(cur.c[r].y, dyt[r], G1);
+        }
+        const float hr0 = rot ? cv * hp0 - sv * hp1 : hp0;
+        const float hr1 = rot ? sv * hp0 + cv * hp1 : hp1;
+        const float al0 = act ? expf(dt * A0) : 0.f, al1 = has1 ? expf(dt * A1) : 0.f;
+        const float oml = 1.0f - lam;
+        const float ga0 = G0 * (hr0 + oml * dt * pb0);
+        const float ga1 = G1 * (hr1 + oml * dt * pb1);
+        /* ddt, dlam */
+        const float ddt = ga0 * A0 * al0 + G0 * (oml * al0 * pb0 + lam * bu0) +
+                          ga1 * A1 * al1 + G1 * (oml * al1 * pb1 + lam * bu1);
+        const float dlm = G0 * dt * (bu0 - al0 * pb0) + G1 * dt * (bu1 - al1 * pb1);
+        sA0 = fmaf(ga0 * dt, al0, sA0);
+        sA1 = fmaf(ga1 * dt, al1, sA1);
+        /* Bu_t feeds h_t (gamma) and h_{t+1} (beta_{t+1}) */
+        const float dbu0 = lam * dt * G0 + bg0;
+        const float dbu1 = lam * dt * G1 + bg1;
+        bg0 = oml * dt * al0 * G0;
+        bg1 = oml * dt * al1 * G1;
+        float *dzr = dzb + (long)t * W;
+        for (int r = 0; r < RT; ++r) {
+            if (r >= R) break;
+            if (act) {
+                dzr[R + 2 + r * N + n0] = dbu0 * cur.u[r];
+                dzr[R + 2 + R * N + r * N + n0] = dyt[r] * ht0;
+            }
+            if (has1) {
+                dzr[R + 2 + r * N + n0 + 1] = dbu1 * cur.u[r];
+                dzr[R + 2 + R * N + r * N + n0 + 1] = dyt[r] * ht1;
+            }
+            const float du = warp_sum(dbu0 * cur.b[r].x + dbu1 * cur.b[r].y);
+            if (threadIdx.x == 0) part[t * RP + r] = du;
+        }
+        {
+            const float s_dt = warp_sum(ddt), s_lm = warp_sum(dlm);
+            if (threadIdx.x == 0) {
+                part[t * RP + R] = s_dt;
+                part[t * RP + R + 1] = s_lm;
+            }
+        }
+        /* rotation: h_rot = R h_{t-1};  d h_rot = alpha * G */
+        const float dr0 = al0 * G0, dr1 = al1 * G1;
+        if (rot) {
+            sth += dr0 * (-sv * hp0 - cv * hp1) + dr1 * (cv * hp0 - sv * hp1);
+            c0 = cv * dr0 + sv * dr1;
+            c1 = -sv * dr0 + cv * dr1;
+        } else {
+            c0 = dr0;
+            c1 = dr1;
+        }
+        if (t - PF >= 0) {
+            load_step(zb + (long)(t - PF) * W, R, N, n0, act, has1, cur);
+            load_step_bwd(hb, dyb, t - PF, R, N, n0, act, has1, cur);
+        }
     }
     if (act) {
         atomicAdd(a.dA + n0, sA0);
-        if (has1) atomicAdd(a.dA + n1, sA1);
+        if (has1) atomicAdd(a.dA + n0 + 1, sA1);
         if (rot) atomicAdd(a.dtheta + i, sth);
+    }
+}
+
+/* out[(b*L + t)*ldo + k] = sum_g part[((b*G + g)*L + t)*K + k], g in order */
+__global__ void k_m3_fold(const float *part, int batch, int G, int L, int K, float *out,
+                          long ldo) {
+    const long tot = (long)batch * L * K;
+    for (long e = (long)blockIdx.x * blockDim.x + threadIdx.x; e < tot;
+         e += (long)gridDim.x * blockDim.x) {
+        const long k = e % K, bt = e / K, t = bt % L, b = bt / L;
+        const float *p = part + ((b * G) * L + t) * K + k;
+        float s = 0.f;
+        for (int g = 0; g < G; ++g) s += p[(long)g * L * K];
+        out[bt * ldo + k] = s;
     }
 }
 
@@ -464,6 +589,55 @@ __global__ void k_adamw(float *p, const float *g, float *m, float *v, long n, fl
     }
 }
 
+/* Up to kMaxTens tensors per launch (blockIdx.y picks the tensor). */
+constexpr int kMaxTens = 16;
+struct AdamList {
+    float *p[kMaxTens];
+    const float *g[kMaxTens];
+    float *m[kMaxTens], *v[kMaxTens];
+    long n[kMaxTens];
+};
+struct SqList {
+    const float *x[kMaxTens];
+    long n[kMaxTens];
+    double *out[kMaxTens];
+};
+
+__global__ void k_adamw_multi(AdamList t, float lr, float b1, float b2, float eps, float wd,
+                              float bc1, float bc2) {
+    const int k = blockIdx.y;
+    float *p = t.p[k], *m = t.m[k], *v = t.v[k];
+    const float *g = t.g[k];
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < t.n[k];
+         i += (long)gridDim.x * blockDim.x) {
+        const float gi = g[i];
+        const float mi = b1 * m[i] + (1.0f - b1) * gi;
+        const float vi = b2 * v[i] + (1.0f - b2) * gi * gi;
+        m[i] = mi;
+        v[i] = vi;
+        const float mh = mi / bc1, vh = vi / bc2;
+        p[i] = p[i] * (1.0f - lr * wd) - lr * mh / (sqrtf(vh) + eps);
+    }
+}
+
+__global__ void __launch_bounds__(256) k_sumsq_multi(SqList t) {
+    __shared__ double red[8];
+    const int k = blockIdx.y;
+    const float *x = t.x[k];
+    double s = 0.0;
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < t.n[k];
+         i += (long)gridDim.x * blockDim.x)
+        s += (double)x[i] * x[i];
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double b = 0.0;
+        for (int w = 0; w < 8; ++w) b += red[w];
+        if (b != 0.0) atomicAdd(t.out[k], b); /* one atomic per block */
+    }
+}
+
 __global__ void k_sumsq(const float *x, long n, double *out) {
     double s = 0.0;
     for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
@@ -536,7 +710,8 @@ extern "C" unsigned long long kmb_block_launch_count(void) {
 }
 
 extern "C" int kmb_gemm(int M, int N, int K, const float *A, long am, long ak, const float *B,
-                        long bk, long bn, float *C, long ldc, int accumulate, cudaStream_t s) {
+                        long bk, long bn, float *C, long ldc, int accumulate, float *ws,
+                        size_t ws_elems, cudaStream_t s) {
     if (M <= 0 || N <= 0) return KMB_OK;
     if (K <= 0) {
         if (!accumulate) {
@@ -547,10 +722,48 @@ extern "C" int kmb_gemm(int M, int N, int K, const float *A, long am, long ak, c
         }
         return KMB_OK;
     }
-    dim3 grid((unsigned)((N + kTN - 1) / kTN), (unsigned)((M + kTM - 1) / kTM));
-    count_launch();
-    k_gemm<<<grid, 256, 0, s>>>(M, N, K, A, am, ak, B, bk, bn, C, ldc, accumulate);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e;
+    if (N == 1) {
+        count_launch();
+        k_gemv_n1<<<(unsigned)((M + 7) / 8), 256, 0, s>>>(M, K, A, am, ak, B, bk, C, ldc,
+                                                            accumulate);
+    } else if (M == 1) {
+        count_launch();
+        k_gemv_m1<<<(unsigned)((N + 31) / 32), 256, 0, s>>>(N, K, A, ak, B, bk, bn, C,
+                                                             accumulate);
+    } else {
+        const long tiles = (long)((N + kTN - 1) / kTN) * ((M + kTM - 1) / kTM);
+        /* split K when the output grid leaves most SMs idle: enough slices
+         * for ~2 CTAs per SM, each at least 2 k-tiles deep, within ws */
+        int S = 1;
+        if (ws && tiles < 148) {
+            long want = (296 + tiles - 1) / tiles;
+            long maxs = K / (2 * kTK);
+            long fit = (long)(ws_elems / ((size_t)M * N));
+            S = (int)min(want, min(maxs, fit));
+            if (S < 2) S = 1;
+        }
+        dim3 grid((unsigned)((N + kTN - 1) / kTN), (unsigned)((M + kTM - 1) / kTM), (unsigned)S);
+        if (S == 1) {
+            count_launch();
+            k_gemm<<<grid, 256, 0, s>>>(M, N, K, A, am, ak, B, bk, bn, C, ldc, accumulate,
+                                        nullptr, K);
+        } else {
+            const int kchunk = ((K + S - 1) / S + kTK - 1) / kTK * kTK;
+            S = (K + kchunk - 1) / kchunk;
+            grid.z = (unsigned)S;
+            count_launch();
+            k_gemm<<<grid, 256, 0, s>>>(M, N, K, A, am, ak, B, bk, bn, C, ldc, accumulate, ws,
+                                        kchunk);
+            e = cudaGetLastError();
+            if (e != cudaSuccess) return kmb_cuda_fail(e, "gemm launch");
+            const long tot = (long)M * N;
+            count_launch();
+            k_gemm_reduce<<<(unsigned)min((tot + 255) / 256, 148L * 8), 256, 0, s>>>(
+                ws, S, M, N, C, ldc, accumulate);
+        }
+    }
+    e = cudaGetLastError();
     return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "gemm launch");
 }
 
@@ -581,24 +794,36 @@ extern "C" int kmb_colsum_acc(const float *dz, long rows, int W, int c0, int nco
 extern "C" int kmb_m3_scan(int batch, int L, int N, int R, int W, const float *zact,
                            const float *A, const float *theta, float *h_hist, float *h_last,
                            float *y, const float *dy, float *dz, float *dA, float *dtheta,
-                           cudaStream_t s) {
+                           float *part, cudaStream_t s) {
     if (R > kMaxR) return kmb_fail(KMB_EUNSUPPORTED, "block: mimo_rank %d exceeds %d", R, kMaxR);
-    const int npairs = (N + 1) / 2;
-    if (npairs > 1024)
-        return kmb_fail(KMB_EUNSUPPORTED, "block: state_size %d exceeds 2048", N);
-    const int threads = ((npairs + 31) / 32) * 32;
     if (dy && !h_hist) return kmb_fail(KMB_EINVAL, "block scan backward needs the state history");
-    ScanArgs a{zact, A, theta, h_hist, h_last, y, dy, dz, dA, dtheta, L, N, R, W};
+    const int G = kmb_m3_scan_groups(N);
+    ScanArgs a{zact, A, theta, h_hist, h_last, part, dy, dz, dA, dtheta, L, N, R, W, G};
+    dim3 grid((unsigned)G, (unsigned)batch);
+    const int K = dy ? R + 2 : R;
+    count_launch();
     if (dy) {
-        count_launch();
-        k_m3_scan_bwd<<<batch, threads, 0, s>>>(a);
+        if (R <= 1) k_m3_scan_bwd<1><<<grid, 32, 0, s>>>(a);
+        else if (R <= 2) k_m3_scan_bwd<2><<<grid, 32, 0, s>>>(a);
+        else if (R <= 4) k_m3_scan_bwd<4><<<grid, 32, 0, s>>>(a);
+        else k_m3_scan_bwd<8><<<grid, 32, 0, s>>>(a);
     } else {
-        count_launch();
-        k_m3_scan_fwd<<<batch, threads, 0, s>>>(a);
+        if (R <= 1) k_m3_scan_fwd<1><<<grid, 32, 0, s>>>(a);
+        else if (R <= 2) k_m3_scan_fwd<2><<<grid, 32, 0, s>>>(a);
+        else if (R <= 4) k_m3_scan_fwd<4><<<grid, 32, 0, s>>>(a);
+        else k_m3_scan_fwd<8><<<grid, 32, 0, s>>>(a);
     }
     cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "block scan launch");
+    if (e != cudaSuccess) return kmb_cuda_fail(e, "block scan launch");
+    const long tot = (long)batch * L * K;
+    count_launch();
+    k_m3_fold<<<(unsigned)min((tot + 255) / 256, 148L * 8), 256, 0, s>>>(
+        part, batch, G, L, K, dy ? dz : y, dy ? (long)W : (long)R);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "block scan fold launch");
 }
+
+extern "C" int kmb_m3_scan_groups(int N) { return ((N + 1) / 2 + 31) / 32; }
 
 extern "C" int kmb_embed(const float *emb, const unsigned *tok, long L, long D, long V,
                          float *out, const float *dx_for_grad, float *gemb, cudaStream_t s) {
@@ -680,4 +905,45 @@ extern "C" int kmb_scaled_sub(float *p, const float *x, long n, float lr, float 
     count_launch();
     k_scaled_sub<<<grid1d(n), 256, 0, s>>>(p, x, n, lr, clip, sumsq);
     KMB_ELEMWISE_RET("scaled update launch");
+}
+
+/* AdamW over up to 16 tensors at once (the k_adamw rule per element) */
+extern "C" int kmb_adamw_multi(int cnt, float *const *p, const float *const *g, float *const *m,
+                               float *const *v, const long *n, float lr, float b1, float b2,
+                               float eps, float wd, float bc1, float bc2, cudaStream_t s) {
+    if (cnt <= 0) return KMB_OK;
+    if (cnt > kMaxTens) return kmb_fail(KMB_EINVAL, "adamw: at most %d tensors", kMaxTens);
+    AdamList t;
+    long mx = 1;
+    for (int k = 0; k < cnt; ++k) {
+        t.p[k] = p[k];
+        t.g[k] = g[k];
+        t.m[k] = m[k];
+        t.v[k] = v[k];
+        t.n[k] = n[k];
+        if (n[k] > mx) mx = n[k];
+    }
+    count_launch();
+    k_adamw_multi<<<dim3(grid1d(mx), (unsigned)cnt), 256, 0, s>>>(t, lr, b1, b2, eps, wd, bc1,
+                                                                 bc2);
+    KMB_ELEMWISE_RET("adamw launch");
+}
+
+/* out[k] += sum x_k^2 in double for up to 16 tensors */
+extern "C" int kmb_sumsq_multi(int cnt, const float *const *x, const long *n,
+                               double *const *out, cudaStream_t s) {
+    if (cnt <= 0) return KMB_OK;
+    if (cnt > kMaxTens) return kmb_fail(KMB_EINVAL, "sumsq: at most %d tensors", kMaxTens);
+    SqList t;
+    long mx = 1;
+    for (int k = 0; k < cnt; ++k) {
+        t.x[k] = x[k];
+        t.n[k] = n[k];
+        t.out[k] = out[k];
+        if (n[k] > mx) mx = n[k];
+    }
+    const unsigned gx = (unsigned)min((mx + 255) / 256, 148L * 2);
+    count_launch();
+    k_sumsq_multi<<<dim3(gx, (unsigned)cnt), 256, 0, s>>>(t);
+    KMB_ELEMWISE_RET("sumsq launch");
 }

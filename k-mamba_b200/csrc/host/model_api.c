@@ -138,7 +138,17 @@ typedef struct {
     float *g[P_COUNT]; /* gradients (NULL: parameter gradients not wanted) */
     float *m[P_COUNT]; /* first moments (NULL when no optimizer step) */
     float *v[P_COUNT]; /* second moments (AdamW) */
+    float *ws;         /* split-K workspace of the call (KMB_GEMM_WS floats) */
 } DevBlock;
+
+/* Split-K workspace per call: the split count is at most ceil(296 / tiles)
+ * for tiles < 148 64x64 output tiles, so S * M * N stays below
+ * (296 + 148) * 4096 floats. */
+#define KMB_GEMM_WS ((size_t)(296 + 148) * 4096)
+
+static float *gemm_ws(KmbStage *st) {
+    return (float *)kmb_scratch(st, KMB_GEMM_WS * sizeof(float));
+}
 
 static int block_check(const MambaBlock *b) {
     BlockDims d;
@@ -156,13 +166,15 @@ static int block_check(const MambaBlock *b) {
 
 /* Stages the parameters (updated in place when `writeback`), the gradient
  * buffers `g` (host arrays, accumulated when `g_accumulate`, else zeroed on
- * the device) and, when `mv` is set, the optimizer moments. */
+ * the device) and, when `mv` is set, the optimizer moments.  `ws` is the
+ * call's split-K workspace (NULL when the call runs no block GEMM). */
 static int dev_block_stage(KmbStage *st, const MambaBlock *b, DevBlock *db, int writeback,
-                           float **g, int g_accumulate, int mv) {
+                           float **g, int g_accumulate, int mv, float *ws) {
     float *hp[P_COUNT];
     memset(db, 0, sizeof *db);
     db->d = block_dims(b);
     db->cfg = b->config;
+    db->ws = ws;
     block_param_ptrs(b, hp);
     for (int i = 0; i < P_COUNT; ++i) {
         const size_t bytes = db->d.n[i] * sizeof(float);
@@ -213,6 +225,7 @@ typedef struct {
     float *zact; /* [rows, W] after activation (+ bias) */
     float *hh;   /* [rows, N] state history, or NULL */
     float *y;    /* [rows, R] scan output */
+    float *part; /* [rows, warps per sequence, R + 2] scan partial sums */
 } BlockActs;
 
 static int acts_alloc(KmbStage *st, const BlockDims *d, long rows, int hist, BlockActs *a) {
@@ -220,7 +233,9 @@ static int acts_alloc(KmbStage *st, const BlockDims *d, long rows, int hist, Blo
     a->zact = (float *)kmb_scratch(st, sizeof(float) * (size_t)rows * d->W);
     a->y = (float *)kmb_scratch(st, sizeof(float) * (size_t)rows * d->R);
     a->hh = hist ? (float *)kmb_scratch(st, sizeof(float) * (size_t)rows * d->N) : NULL;
-    if (!a->zraw || !a->zact || !a->y || (hist && !a->hh))
+    a->part = (float *)kmb_scratch(
+        st, sizeof(float) * (size_t)rows * kmb_m3_scan_groups(d->N) * (d->R + 2));
+    if (!a->zraw || !a->zact || !a->y || (hist && !a->hh) || !a->part)
         return st->status ? st->status : kmb_fail(KMB_ENOMEM, "block activations");
     return KMB_OK;
 }
@@ -244,16 +259,18 @@ static int blk_forward(const DevBlock *db, const float *x, float *out, long batc
     cudaError_t e;
     /* Z[:, c0:c0+n] = X Wpart^T  (Wpart [n, D] row-major) */
     for (int k = 0; k < 5; ++k)
-        TRY(kmb_gemm((int)rows, c_n[k], D, x, D, 1, wp[k], 1, D, a->zraw + c_off[k], W, 0, s));
+        TRY(kmb_gemm((int)rows, c_n[k], D, x, D, 1, wp[k], 1, D, a->zraw + c_off[k], W, 0,
+                     db->ws, KMB_GEMM_WS, s));
     TRY(kmb_block_act(a->zraw, a->zact, db->p[P_BB], db->p[P_BC], rows, W, R, NR,
                       db->cfg.dt_min, db->cfg.dt_max, d->has_dp, d->has_lp, db->cfg.dt_scale,
                       NULL, s));
     TRY(kmb_m3_scan((int)batch, (int)L, d->N, R, W, a->zact, db->p[P_A], db->p[P_TH], a->hh,
-                    h_last, a->y, NULL, NULL, NULL, NULL, s));
+                    h_last, a->y, NULL, NULL, NULL, NULL, a->part, s));
     /* out = x + y W_out^T  (W_out [D, R]) */
     e = cudaMemcpyAsync(out, x, sizeof(float) * (size_t)rows * D, cudaMemcpyDeviceToDevice, s);
     if (e != cudaSuccess) return kmb_cuda_fail(e, "block residual copy");
-    return kmb_gemm((int)rows, D, R, a->y, R, 1, db->p[P_WOUT], 1, R, out, D, 1, s);
+    return kmb_gemm((int)rows, D, R, a->y, R, 1, db->p[P_WOUT], 1, R, out, D, 1, db->ws,
+                    KMB_GEMM_WS, s);
 }
 
 /* Adjoint of blk_forward: dx = dY + d(block)/dx^T dY; parameter gradients
@@ -274,13 +291,15 @@ static int blk_backward(const DevBlock *db, const float *x, const BlockActs *a, 
     cudaError_t e;
 
     /* dy_r[t, r] = sum_d dY[t, d] W_out[d, r] */
-    TRY(kmb_gemm((int)rows, R, D, dY, D, 1, db->p[P_WOUT], R, 1, dyr, R, 0, s));
+    TRY(kmb_gemm((int)rows, R, D, dY, D, 1, db->p[P_WOUT], R, 1, dyr, R, 0, db->ws,
+                 KMB_GEMM_WS, s));
     /* g_W_out[d, r] += sum_t dY[t, d] y[t, r] */
     if (db->g[P_WOUT])
-        TRY(kmb_gemm(D, R, (int)rows, dY, 1, D, a->y, R, 1, db->g[P_WOUT], R, 1, s));
+        TRY(kmb_gemm(D, R, (int)rows, dY, 1, D, a->y, R, 1, db->g[P_WOUT], R, 1, db->ws,
+                     KMB_GEMM_WS, s));
     /* scan adjoint: dz (all W columns), dA, dtheta */
     TRY(kmb_m3_scan((int)batch, (int)L, d->N, R, W, a->zact, db->p[P_A], db->p[P_TH], a->hh,
-                    NULL, (float *)a->y, dyr, dz, dA, dth, s));
+                    NULL, (float *)a->y, dyr, dz, dA, dth, a->part, s));
     /* activations: dz becomes the gradient of the raw projections */
     TRY(kmb_block_act(a->zraw, a->zact, db->p[P_BB], db->p[P_BC], rows, W, R, NR,
                       db->cfg.dt_min, db->cfg.dt_max, d->has_dp, d->has_lp, db->cfg.dt_scale,
@@ -294,7 +313,7 @@ static int blk_backward(const DevBlock *db, const float *x, const BlockActs *a, 
         for (int k = 0; k < 5; ++k) {
             if ((k == 1 && !d->has_dp) || (k == 2 && !d->has_lp)) continue;
             TRY(kmb_gemm(c_n[k], D, (int)rows, dz + c_off[k], 1, W, x, D, 1, db->g[gi[k]], D, 1,
-                         s));
+                         db->ws, KMB_GEMM_WS, s));
         }
     }
     /* dx = dY + dz Wcat */
@@ -306,7 +325,8 @@ static int blk_backward(const DevBlock *db, const float *x, const BlockActs *a, 
             if (e != cudaSuccess) return kmb_cuda_fail(e, "block residual gradient copy");
         }
         for (int k = 0; k < 5; ++k)
-            TRY(kmb_gemm((int)rows, D, c_n[k], dz + c_off[k], W, 1, wp[k], D, 1, dx, D, 1, s));
+            TRY(kmb_gemm((int)rows, D, c_n[k], dz + c_off[k], W, 1, wp[k], D, 1, dx, D, 1,
+                         db->ws, KMB_GEMM_WS, s));
     }
     return KMB_OK;
 }
@@ -328,10 +348,17 @@ static int bwd_scratch(KmbStage *st, const BlockDims *d, long rows, BwdScratch *
 
 /* Squared-norm slots: one double per parameter tensor, zeroed here. */
 static int blk_sumsq(const DevBlock *db, double *slots, cudaStream_t s) {
+    const float *x[P_COUNT];
+    double *out[P_COUNT];
+    long n[P_COUNT];
     cudaError_t e = cudaMemsetAsync(slots, 0, sizeof(double) * P_COUNT, s);
     if (e != cudaSuccess) return kmb_cuda_fail(e, "sumsq zeroing");
-    for (int i = 0; i < P_COUNT; ++i) TRY(kmb_sumsq(db->g[i], (long)db->d.n[i], slots + i, s));
-    return KMB_OK;
+    for (int i = 0; i < P_COUNT; ++i) {
+        x[i] = db->g[i];
+        n[i] = (long)db->d.n[i];
+        out[i] = slots + i;
+    }
+    return kmb_sumsq_multi(P_COUNT, x, n, out, s);
 }
 
 /* Reference summation order of mamba_block_grad_sqnorm
@@ -363,9 +390,9 @@ static int muon_mat(KmbStage *st, float *p, const float *g, float *m, int rows, 
     if (e != cudaSuccess) return kmb_cuda_fail(e, "muon copy");
     for (int it = 0; it < 5; ++it) {
         /* GG[i, j] = sum_k G[i, k] G[j, k] */
-        TRY(kmb_gemm(rows, rows, cols, G, cols, 1, G, 1, cols, GG, rows, 0, s));
+        TRY(kmb_gemm(rows, rows, cols, G, cols, 1, G, 1, cols, GG, rows, 0, NULL, 0, s));
         /* T = GG G */
-        TRY(kmb_gemm(rows, cols, rows, GG, rows, 1, G, cols, 1, T, cols, 0, s));
+        TRY(kmb_gemm(rows, cols, rows, GG, rows, 1, G, cols, 1, T, cols, 0, NULL, 0, s));
         TRY(kmb_ns_combine(G, T, n, s));
     }
     e = cudaMemsetAsync(slot, 0, sizeof(double), s);
@@ -413,23 +440,61 @@ static int blk_opt_step(KmbStage *st, const DevBlock *db, OptimizerType type, si
     {
         const float bc1 = 1.0f - powf(0.9f, (float)step);
         const float bc2 = 1.0f - powf(0.999f, (float)step);
+        long n[P_COUNT];
         for (int i = 0; i < P_COUNT; ++i) {
             if (!db->m[i] || !db->v[i]) return kmb_fail(KMB_EINVAL, "AdamW: moment buffers missing");
-            TRY(kmb_adamw(db->p[i], db->g[i], db->m[i], db->v[i], (long)d->n[i], c->lr, 0.9f,
-                          0.999f, c->eps, c->weight_decay, bc1, bc2, s));
+            n[i] = (long)d->n[i];
         }
+        return kmb_adamw_multi(P_COUNT, db->p, (const float *const *)db->g, db->m, db->v, n,
+                               c->lr, 0.9f, 0.999f, c->eps, c->weight_decay, bc1, bc2, s);
     }
-    return KMB_OK;
 }
 
 /* ------------------------------------------------------------------ */
 /* block lifecycle (host memory, reference layout)                     */
 /* ------------------------------------------------------------------ */
 
+/*
+ * Tensors that every call copies to and from the device (parameters,
+ * gradients, optimizer moments, embedding, head) live in page-locked host
+ * memory when a GPU is present, so those copies run at the full PCIe rate.
+ * Without a GPU (host-only use: create, init, save, load) they are ordinary
+ * zeroed heap memory.  pinned_free tells the two apart.
+ */
+static int g_pinned = -1; /* -1 unknown, 0 no pinned allocation possible, 1 ok */
+
+static void *pinned_calloc(size_t n, size_t sz) {
+    const size_t bytes = (n ? n : 1) * sz;
+    void *p = NULL;
+    if (__atomic_load_n(&g_pinned, __ATOMIC_RELAXED) != 0) {
+        if (cudaMallocHost(&p, bytes) == cudaSuccess) {
+            __atomic_store_n(&g_pinned, 1, __ATOMIC_RELAXED);
+            memset(p, 0, bytes);
+            return p;
+        }
+        (void)cudaGetLastError();
+        if (__atomic_load_n(&g_pinned, __ATOMIC_RELAXED) == -1)
+            __atomic_store_n(&g_pinned, 0, __ATOMIC_RELAXED);
+    }
+    return calloc(1, bytes);
+}
+
+static void pinned_free(void *p) {
+    struct cudaPointerAttributes at;
+    if (!p) return;
+    if (__atomic_load_n(&g_pinned, __ATOMIC_RELAXED) == 1 &&
+        cudaPointerGetAttributes(&at, p) == cudaSuccess && at.type == cudaMemoryTypeHost) {
+        cudaFreeHost(p);
+        return;
+    }
+    (void)cudaGetLastError();
+    free(p);
+}
+
 static int mat_alloc(MBMatrix *m, size_t rows, size_t cols) {
     m->rows = rows;
     m->cols = cols;
-    m->data = (float *)calloc(rows * cols > 0 ? rows * cols : 1, sizeof(float));
+    m->data = (float *)pinned_calloc(rows * cols, sizeof(float));
     return m->data ? 0 : -1;
 }
 
@@ -457,9 +522,9 @@ MambaBlock *mamba_block_create(const MBConfig *config) {
         mamba_block_free(b);
         return NULL;
     }
-    b->b_B = (float *)calloc(N * R + 1, sizeof(float));
-    b->b_C = (float *)calloc(N * R + 1, sizeof(float));
-    b->theta = (float *)calloc(blk_TS(&b->config), sizeof(float));
+    b->b_B = (float *)pinned_calloc(N * R, sizeof(float));
+    b->b_C = (float *)pinned_calloc(N * R, sizeof(float));
+    b->theta = (float *)pinned_calloc(blk_TS(&b->config), sizeof(float));
     b->hidden = (float *)calloc(N + 1, sizeof(float));
     b->delta = (float *)calloc(L + 1, sizeof(float));
     b->scan_B = (float *)calloc(L * N * R + 1, sizeof(float));
@@ -492,16 +557,16 @@ MambaBlock *mamba_block_create(const MBConfig *config) {
 void mamba_block_free(MambaBlock *b) {
     if (!b) return;
     mamba_free_optimizer(b);
-    free(b->W_in.data);
-    free(b->W_out.data);
-    free(b->A_log.data);
-    free(b->W_B.data);
-    free(b->W_C.data);
-    free(b->delta_proj.data);
-    free(b->lambda_proj.data);
-    free(b->b_B);
-    free(b->b_C);
-    free(b->theta);
+    pinned_free(b->W_in.data);
+    pinned_free(b->W_out.data);
+    pinned_free(b->A_log.data);
+    pinned_free(b->W_B.data);
+    pinned_free(b->W_C.data);
+    pinned_free(b->delta_proj.data);
+    pinned_free(b->lambda_proj.data);
+    pinned_free(b->b_B);
+    pinned_free(b->b_C);
+    pinned_free(b->theta);
     free(b->hidden);
     free(b->delta);
     free(b->scan_B);
@@ -610,7 +675,7 @@ static int block_forward_impl(MambaBlock *b, MambaBlockWorkspace *ws, float *out
     rows = (long)batch * L;
     io_bytes = sizeof(float) * (size_t)rows * b->config.dim;
     kmb_stage_begin(&st);
-    rc = dev_block_stage(&st, b, &db, 0, NULL, 0, 0);
+    rc = dev_block_stage(&st, b, &db, 0, NULL, 0, 0, gemm_ws(&st));
     if (rc == KMB_OK) {
         x = (const float *)kmb_stage_in(&st, input, io_bytes);
         out = (float *)kmb_stage_out(&st, output, io_bytes, 0);
@@ -673,7 +738,7 @@ static int block_backward_impl(MambaBlock *b, const float *dY, const float *inpu
     io_bytes = sizeof(float) * (size_t)L * b->config.dim;
     if (gsrc) optstate_grad_ptrs(gsrc, g);
     kmb_stage_begin(&st);
-    rc = dev_block_stage(&st, b, &db, 0, gsrc ? g : NULL, 1, 0);
+    rc = dev_block_stage(&st, b, &db, 0, gsrc ? g : NULL, 1, 0, gemm_ws(&st));
     if (rc == KMB_OK) {
         x = (const float *)kmb_stage_in(&st, input, io_bytes);
         dy = (const float *)kmb_stage_in(&st, dY, io_bytes);
@@ -721,31 +786,24 @@ static int grads_alloc(MBOptimState *s, const MambaBlock *b) {
     float **g[P_COUNT] = {&s->g_W_in, &s->g_delta_proj, &s->g_lambda_proj, &s->g_W_B, &s->g_W_C,
                           &s->g_b_B,  &s->g_b_C,        &s->g_A_log,       &s->g_theta, &s->g_W_out};
     for (int i = 0; i < P_COUNT; ++i) {
-        *g[i] = (float *)calloc(d.n[i] ? d.n[i] : 1, sizeof(float));
+        *g[i] = (float *)pinned_calloc(d.n[i], sizeof(float));
         if (!*g[i]) return -1;
     }
     return 0;
 }
 
 static void grads_free(MBOptimState *s) {
-    free(s->g_W_in);
-    free(s->g_W_out);
-    free(s->g_A_log);
-    free(s->g_W_B);
-    free(s->g_W_C);
-    free(s->g_b_B);
-    free(s->g_b_C);
-    free(s->g_delta_proj);
-    free(s->g_lambda_proj);
-    free(s->g_theta);
+    float *g[P_COUNT];
+    optstate_grad_ptrs(s, g);
+    for (int i = 0; i < P_COUNT; ++i) pinned_free(g[i]);
 }
 
 static void moments_free(MBOptimState *s) {
     float *m[P_COUNT], *v[P_COUNT];
     optstate_moment_ptrs(s, m, v);
     for (int i = 0; i < P_COUNT; ++i) {
-        free(m[i]);
-        free(v[i]);
+        pinned_free(m[i]);
+        pinned_free(v[i]);
     }
 }
 
@@ -767,10 +825,10 @@ void mamba_attach_optimizer(MambaBlock *b, OptimizerType type, const MBOptimConf
                               &s->v_W_C,  &s->v_b_B,        &s->v_b_C,         &s->v_A_log,
                               &s->v_theta, &s->v_W_out};
         for (int i = 0; i < P_COUNT; ++i) {
-            *m[i] = (float *)calloc(d.n[i] ? d.n[i] : 1, sizeof(float));
+            *m[i] = (float *)pinned_calloc(d.n[i], sizeof(float));
             if (!*m[i]) goto fail;
             if (type == OPTIMIZER_ADAMW || type == OPTIMIZER_ADAM_CLIP) {
-                *v[i] = (float *)calloc(d.n[i] ? d.n[i] : 1, sizeof(float));
+                *v[i] = (float *)pinned_calloc(d.n[i], sizeof(float));
                 if (!*v[i]) goto fail;
             }
         }
@@ -810,7 +868,7 @@ float mamba_block_grad_sqnorm(const MambaBlock *b) {
     if (block_check(b) != KMB_OK) return 0.0f;
     optstate_grad_ptrs(b->opt_state, g);
     kmb_stage_begin(&st);
-    rc = dev_block_stage(&st, b, &db, 0, g, 1, 0);
+    rc = dev_block_stage(&st, b, &db, 0, g, 1, 0, NULL);
     slots = (double *)kmb_scratch(&st, sizeof(double) * P_COUNT);
     if (rc == KMB_OK) rc = st.status;
     if (rc == KMB_OK) rc = blk_sumsq(&db, slots, st.s);
@@ -837,7 +895,7 @@ void mamba_optimizer_step(MambaBlock *b, const MBOptimConfig *conf) {
     s->step++;
     optstate_grad_ptrs(s, g);
     kmb_stage_begin(&st);
-    rc = dev_block_stage(&st, b, &db, 1, g, 1, 1);
+    rc = dev_block_stage(&st, b, &db, 1, g, 1, 1, NULL);
     slots = (double *)kmb_scratch(&st, sizeof(double) * P_COUNT);
     if (rc == KMB_OK) rc = st.status;
     if (rc == KMB_OK) rc = blk_opt_step(&st, &db, s->type, s->step, conf, slots, st.s);
@@ -898,7 +956,7 @@ MBMatrix *mb_matrix_create(size_t rows, size_t cols) {
 
 void mb_matrix_free(MBMatrix *m) {
     if (!m) return;
-    free(m->data);
+    pinned_free(m->data);
     free(m);
 }
 
@@ -936,7 +994,7 @@ void mb_matrix_vec_mult(float *out, const MBMatrix *m, const float *v) {
     rc = st.status;
     if (rc == KMB_OK)
         rc = kmb_gemm((int)m->rows, 1, (int)m->cols, dm, (long)m->cols, 1, dv, 1, 1, dout, 1, 0,
-                      st.s);
+                      NULL, 0, st.s);
     (void)kmb_stage_finish(&st, rc);
 }
 
@@ -982,7 +1040,8 @@ void mb_compute_delta(float *delta_out, const MambaBlock *b, const float *delta_
     dout = (float *)kmb_stage_out(&st, delta_out, sizeof(float) * seq_len, 0);
     z = (float *)kmb_scratch(&st, sizeof(float) * seq_len);
     rc = st.status;
-    if (rc == KMB_OK) rc = kmb_gemm((int)seq_len, 1, (int)D, dx, (long)D, 1, dw, 1, 1, z, 1, 0, st.s);
+    if (rc == KMB_OK)
+        rc = kmb_gemm((int)seq_len, 1, (int)D, dx, (long)D, 1, dw, 1, 1, z, 1, 0, NULL, 0, st.s);
     if (rc == KMB_OK)
         rc = kmb_dt_act(z, dout, (long)seq_len, b->config.dt_min, b->config.dt_max, st.s);
     (void)kmb_stage_finish(&st, rc);
@@ -1004,9 +1063,10 @@ KMamba *kmamba_create(const KMambaConfig *cfg) {
         free(m);
         return NULL;
     }
-    m->embedding = (float *)calloc(m->cfg.vocab_size * m->cfg.dim, sizeof(float));
-    m->head = m->cfg.weight_tying ? m->embedding
-                                  : (float *)calloc(m->cfg.dim * m->cfg.vocab_size, sizeof(float));
+    m->embedding = (float *)pinned_calloc(m->cfg.vocab_size * m->cfg.dim, sizeof(float));
+    m->head = m->cfg.weight_tying
+                  ? m->embedding
+                  : (float *)pinned_calloc(m->cfg.dim * m->cfg.vocab_size, sizeof(float));
     m->layers = (MambaBlock **)calloc(m->cfg.n_layers, sizeof(MambaBlock *));
     if (!m->embedding || !m->head || !m->layers) {
         kmamba_free(m);
@@ -1042,12 +1102,12 @@ void kmamba_free(KMamba *m) {
         for (size_t i = 0; i < m->cfg.n_layers; ++i) mamba_block_free(m->layers[i]);
         free(m->layers);
     }
-    if (m->head != m->embedding) free(m->head);
-    free(m->embedding);
-    free(m->m_embedding);
-    free(m->v_embedding);
-    free(m->m_head);
-    free(m->v_head);
+    if (m->head != m->embedding) pinned_free(m->head);
+    pinned_free(m->embedding);
+    pinned_free(m->m_embedding);
+    pinned_free(m->v_embedding);
+    pinned_free(m->m_head);
+    pinned_free(m->v_head);
     free(m);
 }
 
@@ -1087,14 +1147,14 @@ int kmamba_enable_training_with_optimizer(KMamba *m, OptimizerType type,
         if (!m->layers[i]->opt_state) return -1;
     }
     VD = m->cfg.vocab_size * m->cfg.dim;
-    free(m->m_embedding);
-    free(m->v_embedding);
-    free(m->m_head);
-    free(m->v_head);
-    m->m_embedding = (float *)calloc(VD, sizeof(float));
-    m->v_embedding = (float *)calloc(VD, sizeof(float));
-    m->m_head = (float *)calloc(VD, sizeof(float));
-    m->v_head = (float *)calloc(VD, sizeof(float));
+    pinned_free(m->m_embedding);
+    pinned_free(m->v_embedding);
+    pinned_free(m->m_head);
+    pinned_free(m->v_head);
+    m->m_embedding = (float *)pinned_calloc(VD, sizeof(float));
+    m->v_embedding = (float *)pinned_calloc(VD, sizeof(float));
+    m->m_head = (float *)pinned_calloc(VD, sizeof(float));
+    m->v_head = (float *)pinned_calloc(VD, sizeof(float));
     m->step_embed_head = 0;
     if (!m->m_embedding || !m->v_embedding || !m->m_head || !m->v_head) return -1;
     return 0;
@@ -1266,13 +1326,13 @@ static int model_forward_dev(KmbStage *st, KMamba *m, ModelDev *md, long batch, 
     }
     /* logits = hidden [rows, D] @ head [D, V] */
     return kmb_gemm((int)rows, (int)V, (int)D, md->hs + (long)nl * rows * D, D, 1, md->head, V, 1,
-                    logits, V, 0, st->s);
+                    logits, V, 0, md->blk[0].ws, KMB_GEMM_WS, st->s);
 }
 
 int kmamba_forward(KMamba *m, const uint32_t *tokens, float *logits_out) {
     KmbStage st;
     ModelDev md;
-    float *logits;
+    float *logits, *ws;
     long L, D, V;
     int rc;
     if (!m || !tokens || !logits_out) return -1;
@@ -1293,8 +1353,9 @@ int kmamba_forward(KMamba *m, const uint32_t *tokens, float *logits_out) {
     }
     kmb_stage_begin(&st);
     rc = kmb_stage_reserve(&st, 16 + 24 * (int)m->cfg.n_layers);
+    ws = gemm_ws(&st);
     for (size_t i = 0; i < m->cfg.n_layers && rc == KMB_OK; ++i)
-        rc = dev_block_stage(&st, m->layers[i], &md.blk[i], 0, NULL, 0, 0);
+        rc = dev_block_stage(&st, m->layers[i], &md.blk[i], 0, NULL, 0, 0, ws);
     if (rc == KMB_OK) {
         md.emb = (float *)kmb_stage_in(&st, m->embedding, sizeof(float) * (size_t)(V * D));
         md.head = (float *)kmb_stage_in(&st, m->head, sizeof(float) * (size_t)(D * V));
@@ -1321,7 +1382,7 @@ static float model_train(KMamba *m, const uint32_t *tokens, size_t batch) {
     const long rows = (long)batch * L;
     const size_t nl = m->cfg.n_layers;
     float *logits = NULL, *dlogits = NULL, *row_loss = NULL, *g_head = NULL, *g_emb = NULL;
-    float *dcur = NULL, *dnext = NULL;
+    float *dcur = NULL, *dnext = NULL, *ws;
     double *slots = NULL;
     float *loss_host = NULL;
     double *slots_host = NULL;
@@ -1363,10 +1424,11 @@ static float model_train(KMamba *m, const uint32_t *tokens, size_t batch) {
 
     kmb_stage_begin(&st);
     rc = kmb_stage_reserve(&st, 64 + 64 * (int)nl);
+    ws = gemm_ws(&st);
     for (size_t i = 0; i < nl && rc == KMB_OK; ++i) {
         float *g[P_COUNT];
         optstate_grad_ptrs(m->layers[i]->opt_state, g);
-        rc = dev_block_stage(&st, m->layers[i], &md.blk[i], 1, g, 0, 1);
+        rc = dev_block_stage(&st, m->layers[i], &md.blk[i], 1, g, 0, 1, ws);
     }
     if (rc == KMB_OK) {
         const size_t VD = (size_t)(V * D);
@@ -1406,11 +1468,12 @@ static float model_train(KMamba *m, const uint32_t *tokens, size_t batch) {
         /* the CE kernel scales by 1/rows = 1/(batch*L) (invBL of the batch
          * path; 1/L for one sequence) */
         /* d_hidden = dlogits [rows, V] @ head^T */
-        rc = kmb_gemm((int)rows, (int)D, (int)V, dlogits, V, 1, md.head, 1, V, dcur, D, 0, st.s);
+        rc = kmb_gemm((int)rows, (int)D, (int)V, dlogits, V, 1, md.head, 1, V, dcur, D, 0,
+                      md.blk[0].ws, KMB_GEMM_WS, st.s);
         /* g_head = hidden^T @ dlogits */
         if (rc == KMB_OK)
             rc = kmb_gemm((int)D, (int)V, (int)rows, hidden, 1, D, dlogits, V, 1, g_head, V, 0,
-                          st.s);
+                          md.blk[0].ws, KMB_GEMM_WS, st.s);
     }
     for (size_t li = nl; li-- > 0 && rc == KMB_OK;) {
         float *t;
@@ -1431,8 +1494,12 @@ static float model_train(KMamba *m, const uint32_t *tokens, size_t batch) {
     if (rc == KMB_OK) {
         cudaError_t e = cudaMemsetAsync(slots + nl * P_COUNT, 0, 2 * sizeof(double), st.s);
         if (e != cudaSuccess) rc = kmb_cuda_fail(e, "norm zeroing");
-        if (rc == KMB_OK) rc = kmb_sumsq(g_head, V * D, slots + nl * P_COUNT, st.s);
-        if (rc == KMB_OK) rc = kmb_sumsq(g_emb, V * D, slots + nl * P_COUNT + 1, st.s);
+        if (rc == KMB_OK) {
+            const float *x[2] = {g_head, g_emb};
+            const long n[2] = {V * D, V * D};
+            double *out[2] = {slots + nl * P_COUNT, slots + nl * P_COUNT + 1};
+            rc = kmb_sumsq_multi(2, x, n, out, st.s);
+        }
     }
     if (rc == KMB_OK) {
         cudaError_t e = cudaMemcpyAsync(slots_host, slots, sizeof(double) * (P_COUNT * nl + 2),
@@ -1462,6 +1529,8 @@ static float model_train(KMamba *m, const uint32_t *tokens, size_t batch) {
         mh = (float *)kmb_stage_out(&st, m->m_head, sizeof(float) * (size_t)(V * D), 1);
         vh = (float *)kmb_stage_out(&st, m->v_head, sizeof(float) * (size_t)(V * D), 1);
         rc = st.status;
+        /* embedding then head (one buffer twice when tied, as in the
+         * reference): separate launches keep that order */
         if (rc == KMB_OK)
             rc = kmb_adamw(md.emb, g_emb, mem, vem, V * D, c->lr, 0.9f, 0.999f, c->eps,
                            c->weight_decay, bc1, bc2, st.s);

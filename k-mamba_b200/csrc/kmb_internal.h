@@ -58,19 +58,25 @@ int kmb_launch_scannd_fwd(const KmbNDLaunch *a, cudaStream_t s);
 int kmb_launch_scannd_bwd(const KmbNDLaunch *a, cudaStream_t s);
 
 /* Block / model kernels (csrc/cuda/block.cu). */
-/* C[m*ldc + n] (+)= sum_k A[m*am + k*ak] * B[k*bk + n*bn], fp32 */
+/* C[m*ldc + n] (+)= sum_k A[m*am + k*ak] * B[k*bk + n*bn], fp32.  ws
+ * (ws_elems floats, may be NULL) lets small output grids split K across
+ * CTAs; the partials are added in a fixed order. */
 int kmb_gemm(int M, int N, int K, const float *A, long am, long ak, const float *B, long bk,
-             long bn, float *C, long ldc, int accumulate, cudaStream_t s);
+             long bn, float *C, long ldc, int accumulate, float *ws, size_t ws_elems,
+             cudaStream_t s);
 /* projection activations (dz_inplace == NULL) or their backward in place */
 int kmb_block_act(const float *zraw, float *zact, const float *bB, const float *bC, long rows,
                   int W, int R, int NR, float dt_min, float dt_max, int has_dp, int has_lp,
                   float dt_scale, float *dz_inplace, cudaStream_t s);
 int kmb_colsum_acc(const float *dz, long rows, int W, int c0, int ncols, float *out,
                    cudaStream_t s);
-/* Mamba-3 scan forward (dy == NULL) or backward */
+/* Mamba-3 scan forward (dy == NULL) or backward.  `part` holds
+ * batch * kmb_m3_scan_groups(N) * L * (R + 2) floats of per-warp partial
+ * sums. */
 int kmb_m3_scan(int batch, int L, int N, int R, int W, const float *zact, const float *A,
                 const float *theta, float *h_hist, float *h_last, float *y, const float *dy,
-                float *dz, float *dA, float *dtheta, cudaStream_t s);
+                float *dz, float *dA, float *dtheta, float *part, cudaStream_t s);
+int kmb_m3_scan_groups(int N);
 /* embedding gather (gemb == NULL) or gradient scatter-add */
 int kmb_embed(const float *emb, const unsigned *tok, long L, long D, long V, float *out,
               const float *dx_for_grad, float *gemb, cudaStream_t s);
@@ -79,6 +85,12 @@ int kmb_softmax_ce(const float *logits, const unsigned *tgt, long L, long V, flo
 int kmb_adamw(float *p, const float *g, float *m, float *v, long n, float lr, float b1,
               float b2, float eps, float wd, float bc1, float bc2, cudaStream_t s);
 int kmb_sumsq(const float *x, long n, double *out, cudaStream_t s);
+/* the same over up to 16 tensors in one launch */
+int kmb_adamw_multi(int cnt, float *const *p, const float *const *g, float *const *m,
+                    float *const *v, const long *n, float lr, float b1, float b2, float eps,
+                    float wd, float bc1, float bc2, cudaStream_t s);
+int kmb_sumsq_multi(int cnt, const float *const *x, const long *n, double *const *out,
+                    cudaStream_t s);
 /* y = a*y + b*x (x may be NULL: y = a*y) */
 int kmb_axpby(float *y, const float *x, long n, float a, float b, cudaStream_t s);
 /* out = clamp(softplus(z), dt_min, dt_max) */
