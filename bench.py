@@ -502,21 +502,19 @@ def main():
     import torch
     import torch.distributed as dist
     import kmamba_b200 as kb
+    import kmb_dist
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
+    rank, world = kmb_dist.env_rank()
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+        kmb_dist.init("nccl", timeout_s=120, device_id=torch.device("cuda", local))
     lib = kb.load()
     stream = torch.cuda.current_stream()
     lib.kmb_set_stream(C.c_void_p(stream.cuda_stream))
     lib.kmb_set_sync(0)
 
-    x, dt, A, B, Cm, dy = make_inputs(seed=1000 + rank)
+    x, dt, A, B, Cm, dy = make_inputs(seed=kmb_dist.shard_seed(1000, rank))
     dev = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
     tx, tdt, tA, tB, tC, tdy = map(dev, (x, dt, A, B, Cm, dy))
     ty = torch.empty_like(tx)
@@ -547,8 +545,7 @@ def main():
         kb.check(lib, lib.kmb_scan1d_bwd(C.byref(ba)))
         if marks:
             marks[2].record(stream)
-        if world > 1:
-            dist.all_reduce(g["dA"])
+        kmb_dist.sum_grads([g["dA"]], world)
 
     for _ in range(args.warmup):
         step()
@@ -570,11 +567,8 @@ def main():
     elapsed = start.elapsed_time(stop) / 1e3
     fwd_ms = sum(m[0].elapsed_time(m[1]) for m in marks) / args.steps
     bwd_ms = sum(m[1].elapsed_time(m[2]) for m in marks) / args.steps
-    t_max = torch.tensor([elapsed], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
-    elapsed = float(t_max.item())
-    value = STEP_BYTES * world * args.steps / elapsed / 1e9
+    elapsed = kmb_dist.max_over_ranks(elapsed, world, device="cuda")
+    value = kmb_dist.weak_scaling_rate(STEP_BYTES, world, args.steps, elapsed)
 
     # ---------------- e2e through the public C ABI with host buffers ----------
     h2d = d2h = 0
@@ -608,10 +602,8 @@ def main():
             kb.check(lib, lib.kmb_scan1d_bwd(C.byref(eb)))
         torch.cuda.synchronize()
         te = (time.perf_counter() - t0) / args.e2e_steps
-        te_t = torch.tensor([te], dtype=torch.float64, device="cuda")
-        if world > 1:
-            dist.all_reduce(te_t, op=dist.ReduceOp.MAX)
-        e2e_val = STEP_BYTES * world / float(te_t.item()) / 1e9
+        te = kmb_dist.max_over_ranks(te, world, device="cuda")
+        e2e_val = kmb_dist.weak_scaling_rate(STEP_BYTES, world, 1, te)
         lib.kmb_set_sync(0)
 
     pk, pk_kind = peaks()
