@@ -1,0 +1,592 @@
+/*
+ * 2D selective scan over an H x W grid (ND scan with ndims = 2), forward
+ * and backward, for channel-shared B/C (the config-4 shape).  Semantics of
+ * the reference src/scan_nd.c:86-230 with theta = lambda = NULL, axis 0 the
+ * rows (predecessor p - W) and axis 1 the columns (p - 1):
+ *
+ *   dt_bar(p,d) = (delta_0(p,d) + delta_1(p,d)) / 2
+ *   h(p,d,m)    = dt_bar (B(p,m) x(p,d))
+ *               + exp(delta_0 A_0(d,m)) h(p-W,d,m) + exp(delta_1 A_1(d,m)) h(p-1,d,m)
+ *   y(p,d)      = sum_m C(p,m) h(p,d,m)
+ *
+ * and the full state history h [P, D, M] written, as the reference API
+ * requires (the backward reads it).
+ *
+ * Decomposition.  A CTA owns one batch item and 8 channels (a warp's lanes
+ * are 8 channels x 4 groups of 4 states, two FFMA2 pairs each) and sweeps
+ * the grid in strips of 64 columns.  Warp w of a strip owns 8 adjacent
+ * columns and runs one row behind warp w-1: at step t it computes row
+ * t - w, left to right, with the vertical carry h(i-1, .) of its columns
+ * in registers and the state of the column to its left taken from warp
+ * w-1's previous step (double-buffered shared slot; the first warp of a
+ * strip reads the previous strip's last column from an L2 scratch column).
+ * One CTA barrier per step.  Inputs are staged per warp by cp.async a few
+ * rows ahead.
+ *
+ * The backward walks the same strips right to left and bottom to top with
+ * the adjoint
+ *   G(p) = C(p) dy(p) + exp(delta_0(p+W) A_0) G(p+W) + exp(delta_1(p+1) A_1) G(p+1)
+ * carried the same way (vertical carry in registers, right neighbour from
+ * warp w+1), and per point
+ *   dx = dt_bar sum_m G B,   ddelta_a = (sum_m G B x) / 2 + sum_m G h(p-e_a) A_a e_a(p),
+ *   dA_a += G h(p-e_a) delta_a e_a(p),   dB(p,m) += G dt_bar x,  dC(p,m) += dy h
+ * with e_a(p) = exp(delta_a(p) A_a); dB / dC are folded over the CTA's 8
+ * channels by shuffles and added to global memory with one atomic per
+ * (point, state) and CTA.
+ */
+#include <string.h>
+
+#include "kmb_common.cuh"
+#include "../kmb_internal.h"
+
+namespace {
+
+constexpr int kWarps = 8;                 /* warps per CTA */
+constexpr int kCPW = 8;                   /* columns per warp */
+constexpr int kStrip = kWarps * kCPW;     /* columns per strip */
+constexpr int kCh = 8;                    /* channels per CTA */
+constexpr int kRing = 4;                  /* input rows staged ahead per warp */
+constexpr unsigned kFull = 0xffffffffu;
+
+/* floats of one staged row of a warp: x, delta_0, delta_1 as [col][ch],
+ * B and C as [col][16], and the left edge column (32 lanes x 4 states,
+ * used by the first warp of a strip) */
+constexpr int kSlotX = kCPW * kCh;
+constexpr int kSlotB = kCPW * 16;
+constexpr int kSlotE = 128;
+constexpr int kSlot = 3 * kSlotX + 2 * kSlotB + kSlotE;
+
+struct S2D {
+    const float *x, *d0, *d1, *A0, *A1, *B, *C, *dy, *h;
+    float *hout, *y, *edge;
+    float *dx, *dd0, *dd1, *dA0, *dA1, *dB, *dC;
+    long H, W, D, M;
+    long dl_bs; /* floats between batch items of each delta axis */
+};
+
+/* Stages row i (columns j0 .. j0+7) of this warp's inputs into slot `s`:
+ * 16-byte cp.async copies, zero-filled outside the grid. */
+__device__ __forceinline__ void stage_row(const S2D &p, long b, long i, long j0, long dch0,
+                                          float *s, int lane, const float *edge_row) {
+    const long W = p.W, D = p.D, M = p.M;
+    const bool rok = i >= 0 && i < p.H;
+    if (edge_row) /* 32 lanes x 16 bytes */
+        kmb_cp_async16(s + 3 * kSlotX + 2 * kSlotB + lane * 4, rok ? edge_row + lane * 4 : p.x,
+                       rok ? 16 : 0);
+    /* x / delta_0 / delta_1: per column 8 channels = 2 chunks -> 16 chunks each */
+    for (int e = lane; e < 3 * 16 + 2 * kCPW * 4; e += 32) {
+        if (e < 48) {
+            const int t = e / 16, r = e % 16, col = r / 2, half = r % 2;
+            const long j = j0 + col;
+            const bool ok = rok && j < W;
+            const float *base = t == 0 ? p.x + b * p.H * W * D
+                                       : (t == 1 ? p.d0 : p.d1) + b * p.dl_bs;
+            const float *src = ok ? base + (i * W + j) * D + dch0 + half * 4 : p.x;
+            kmb_cp_async16(s + t * kSlotX + col * kCh + half * 4, src, ok ? 16 : 0);
+        } else {
+            const int e2 = e - 48, t = e2 / (kCPW * 4), r = e2 % (kCPW * 4);
+            const int col = r / 4, q = r % 4;
+            const long j = j0 + col;
+            const bool ok = rok && j < W && q * 4 < M;
+            const float *base = (t == 0 ? p.B : p.C) + b * p.H * W * M;
+            const float *src = ok ? base + (i * W + j) * M + q * 4 : p.x;
+            kmb_cp_async16(s + 3 * kSlotX + t * kSlotB + col * 16 + q * 4, src, ok ? 16 : 0);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kWarps * 32) k_scan2d_fwd(S2D p) {
+    extern __shared__ __align__(16) float sm[];
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int c = lane >> 2, q = lane & 3;
+    const long b = blockIdx.y;
+    const long dch0 = (long)blockIdx.x * kCh;
+    const long d = dch0 + c;
+    const long H = p.H, W = p.W, D = p.D, M = p.M;
+    const bool qok = q * 4 < M;
+    float *ring = sm + w * kRing * kSlot;                      /* this warp's rows */
+    float *xbuf = sm + kWarps * kRing * kSlot;                 /* [warp][2][32][4] */
+    float *edge = p.edge + ((long)blockIdx.y * gridDim.x + blockIdx.x) * H * 128;
+
+    float2 A0p[2], A1p[2];
+#pragma unroll
+    for (int jp = 0; jp < 2; ++jp) {
+        const int m = q * 4 + 2 * jp;
+        const float a0 = m < M ? p.A0[d * M + m] : 0.f, a1 = m + 1 < M ? p.A0[d * M + m + 1] : 0.f;
+        const float e0 = m < M ? p.A1[d * M + m] : 0.f, e1 = m + 1 < M ? p.A1[d * M + m + 1] : 0.f;
+        A0p[jp] = kmb_f2(a0 * KMB_LOG2E, a1 * KMB_LOG2E);
+        A1p[jp] = kmb_f2(e0 * KMB_LOG2E, e1 * KMB_LOG2E);
+    }
+    const long nstrips = (W + kStrip - 1) / kStrip;
+    const long nsteps = H + kWarps - 1;
+    float *hb = p.hout + b * H * W * D * M;
+    float *yb = p.y + b * H * W * D;
+
+    for (long sidx = 0; sidx < nstrips; ++sidx) {
+        const long j0 = sidx * kStrip + w * kCPW; /* this warp's first column */
+        float2 hv[kCPW][2];                       /* h(i-1, j0 + k) */
+#pragma unroll
+        for (int k = 0; k < kCPW; ++k) hv[k][0] = hv[k][1] = kmb_f2s(0.f);
+        /* the first warp of a strip also stages the previous strip's last
+         * column, written by that strip's last warp (CTA barriers since) */
+        const bool use_edge = w == 0 && sidx > 0;
+        auto edge_row = [&](long r) { return use_edge ? edge + r * 128 : nullptr; };
+        /* prologue: rows 0 .. kRing-2 of this warp */
+#pragma unroll
+        for (int r = 0; r < kRing - 1; ++r) {
+            stage_row(p, b, r, j0, dch0, ring + r * kSlot, lane, edge_row(r));
+            kmb_cp_async_commit();
+        }
+        for (long t = 0; t < nsteps; ++t) {
+            const long i = t - w; /* this warp's row */
+            /* row i + kRing - 1 goes into the slot row i - 1 used; rows below
+             * kRing - 1 came with the prologue.  One commit per step keeps
+             * the group count uniform. */
+            if (i >= 0)
+                stage_row(p, b, i + kRing - 1, j0, dch0, ring + ((i + kRing - 1) % kRing) * kSlot,
+                          lane, edge_row(i + kRing - 1));
+            kmb_cp_async_commit();
+            kmb_cp_async_wait<kRing - 1>();
+            __syncwarp();
+            if (i >= 0 && i < H) {
+                const float *s = ring + (i % kRing) * kSlot;
+                /* left neighbour of column j0 at row i */
+                float2 hl[2];
+                if (w > 0) {
+                    const float4 v = *reinterpret_cast<const float4 *>(
+                        xbuf + (((w - 1) * 2 + ((t - 1) & 1)) * 32 + lane) * 4);
+                    hl[0] = kmb_f2(v.x, v.y);
+                    hl[1] = kmb_f2(v.z, v.w);
+                } else if (use_edge) {
+                    const float4 v = *reinterpret_cast<const float4 *>(s + 3 * kSlotX + 2 * kSlotB + lane * 4);
+                    hl[0] = kmb_f2(v.x, v.y);
+                    hl[1] = kmb_f2(v.z, v.w);
+                } else {
+                    hl[0] = hl[1] = kmb_f2s(0.f);
+                }
+                float yq[4];
+#pragma unroll
+                for (int k = 0; k < kCPW; ++k) {
+                    const long j = j0 + k;
+                    const float xv = s[k * kCh + c];
+                    const float dv0 = s[kSlotX + k * kCh + c];
+                    const float dv1 = s[2 * kSlotX + k * kCh + c];
+                    const float4 B4 = *reinterpret_cast<const float4 *>(s + 3 * kSlotX + k * 16 + q * 4);
+                    const float4 C4 = *reinterpret_cast<const float4 *>(s + 3 * kSlotX + kSlotB + k * 16 + q * 4);
+                    const float2 x2 = kmb_f2s(xv);
+                    const float2 dtb2 = kmb_f2s((dv0 + dv1) / 2.0f);
+                    const float2 dv02 = kmb_f2s(dv0), dv12 = kmb_f2s(dv1);
+                    const float2 Bp[2] = {kmb_f2(B4.x, B4.y), kmb_f2(B4.z, B4.w)};
+                    const float2 Cp[2] = {kmb_f2(C4.x, C4.y), kmb_f2(C4.z, C4.w)};
+                    float2 y2 = kmb_f2s(0.f);
+#pragma unroll
+                    for (int jp = 0; jp < 2; ++jp) {
+                        float2 hn = kmb_mul2(dtb2, kmb_mul2(Bp[jp], x2));
+                        const float2 e0 = kmb_exp2_decay2(kmb_mul2(dv02, A0p[jp]));
+                        const float2 e1 = kmb_exp2_decay2(kmb_mul2(dv12, A1p[jp]));
+                        hn = kmb_fma2(e0, hv[k][jp], hn);
+                        hn = kmb_fma2(e1, hl[jp], hn);
+                        hv[k][jp] = hn;
+                        hl[jp] = hn;
+                        y2 = kmb_fma2(Cp[jp], hn, y2);
+                    }
+                    if (j < W && qok)
+                        *reinterpret_cast<float4 *>(hb + ((i * W + j) * D + d) * M + q * 4) =
+                            make_float4(hv[k][0].x, hv[k][0].y, hv[k][1].x, hv[k][1].y);
+                    /* y: sum over the 4 state groups, 4 columns per fold */
+                    yq[k & 3] = y2.x + y2.y;
+                    if ((k & 3) == 3) {
+#pragma unroll
+                        for (int hh = 2; hh > 0; hh >>= 1) {
+                            const bool up = (q & hh) != 0;
+#pragma unroll
+                            for (int u = 0; u < hh; ++u) {
+                                const float send = up ? yq[u] : yq[u + hh];
+                                const float keep = up ? yq[u + hh] : yq[u];
+                                yq[u] = keep + __shfl_xor_sync(kFull, send, hh);
+                            }
+                        }
+                        const long jy = j0 + (k - 3) + q;
+                        if (jy < W) yb[(i * W + jy) * D + d] = yq[0];
+                    }
+                }
+                /* the last column's states go to the next warp (and, from
+                 * the last warp, to the next strip) */
+                const float4 last = make_float4(hl[0].x, hl[0].y, hl[1].x, hl[1].y);
+                *reinterpret_cast<float4 *>(xbuf + ((w * 2 + (t & 1)) * 32 + lane) * 4) = last;
+                if (w == kWarps - 1) *reinterpret_cast<float4 *>(edge + i * 128 + lane * 4) = last;
+            }
+            __syncthreads();
+        }
+        kmb_cp_async_wait<0>();
+        __syncthreads();
+    }
+}
+
+/* ------------------------------------------------------------------ */
+/* backward                                                            */
+/* ------------------------------------------------------------------ */
+
+constexpr int kBCPW = 4;                 /* columns per warp */
+constexpr int kBStrip = kWarps * kBCPW;  /* columns per strip */
+constexpr int kBRing = 3;                /* rows staged ahead per warp */
+/* one staged row of a warp (floats): x, delta_0, delta_1, dy as [col][ch];
+ * B, C as [col][16]; h of the row above [col][ch][16]; h of the column
+ * left of the warp [ch][16]; the right-edge carry [32 lanes][4] */
+constexpr int kBX = kBCPW * kCh;
+constexpr int kBB = kBCPW * 16;
+constexpr int kBH = kBCPW * kCh * 16;
+constexpr int kBL = kCh * 16;
+constexpr int kBE = 128;
+constexpr int kBSlot = 4 * kBX + 2 * kBB + kBH + kBL + kBE;
+
+/* stages row i of this warp (columns j0 .. j0+3): inputs of row i, h of
+ * row i-1 for the same columns and h(i, j0-1); zero outside the grid */
+__device__ __forceinline__ void stage_row_bwd(const S2D &p, long b, long i, long j0, long dch0,
+                                              float *s, int lane, const float *edge_row) {
+    const long H = p.H, W = p.W, D = p.D, M = p.M;
+    const bool rok = i >= 0 && i < H;
+    if (edge_row)
+        kmb_cp_async16(s + 4 * kBX + 2 * kBB + kBH + kBL + lane * 4,
+                       rok ? edge_row + lane * 4 : p.x, rok ? 16 : 0);
+    /* x, delta_0, delta_1, dy: 4 columns x 2 chunks each = 32 chunks */
+    {
+        const int t = lane / 8, r = lane % 8, col = r / 2, half = r % 2;
+        const long j = j0 + col;
+        const bool ok = rok && j < W;
+        const float *base = t == 0   ? p.x + b * H * W * D
+                            : t == 1 ? p.d0 + b * p.dl_bs
+                            : t == 2 ? p.d1 + b * p.dl_bs
+                                     : p.dy + b * H * W * D;
+        kmb_cp_async16(s + t * kBX + col * kCh + half * 4,
+                       ok ? base + (i * W + j) * D + dch0 + half * 4 : p.x, ok ? 16 : 0);
+    }
+    /* B, C: 4 columns x 4 chunks = 16 chunks each */
+    {
+        const int t = lane / 16, r = lane % 16, col = r / 4, q = r % 4;
+        const long j = j0 + col;
+        const bool ok = rok && j < W && q * 4 < M;
+        const float *base = (t == 0 ? p.B : p.C) + b * H * W * M;
+        kmb_cp_async16(s + 4 * kBX + t * kBB + col * 16 + q * 4,
+                       ok ? base + (i * W + j) * M + q * 4 : p.x, ok ? 16 : 0);
+    }
+    /* h(i-1, j0 .. j0+3) for the 8 channels: 4 x 8 x (M/4) chunks; and
+     * h(i, j0-1): 8 x (M/4) chunks */
+    const float *hbase = p.h + b * H * W * D * M;
+    for (int e = lane; e < (kBCPW + 1) * kCh * 4; e += 32) {
+        const int col = e / (kCh * 4), r = e % (kCh * 4), ch = r / 4, q = r % 4;
+        const long ii = col < kBCPW ? i - 1 : i;
+        const long j = col < kBCPW ? j0 + col : j0 - 1;
+        const bool ok = rok && ii >= 0 && j >= 0 && j < W && q * 4 < M;
+        float *dst = col < kBCPW ? s + 4 * kBX + 2 * kBB + (col * kCh + ch) * 16 + q * 4
+                                 : s + 4 * kBX + 2 * kBB + kBH + ch * 16 + q * 4;
+        kmb_cp_async16(dst, ok ? hbase + ((ii * W + j) * D + dch0 + ch) * M + q * 4 : p.x,
+                       ok ? 16 : 0);
+    }
+}
+
+/* Reduce-scatter of 8 values over the 8 lanes that share q (lane bits 2-4):
+ * afterwards lane 4c + q holds the sum of value 4 (c >> 2) + (c & 3). */
+__device__ __forceinline__ float rs8_channels(float (&v)[8], int lane) {
+#pragma unroll
+    for (int o = 16, half = 4; o >= 4; o >>= 1, half >>= 1) {
+        const bool up = (lane & o) != 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            if (k < half) {
+                const float send = up ? v[k] : v[k + half];
+                const float keep = up ? v[k + half] : v[k];
+                v[k] = keep + __shfl_xor_sync(kFull, send, o);
+            }
+        }
+    }
+    return v[0];
+}
+
+__global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_bwd(S2D p) {
+    extern __shared__ __align__(16) float sm[];
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int c = lane >> 2, q = lane & 3;
+    const long b = blockIdx.y;
+    const long dch0 = (long)blockIdx.x * kCh;
+    const long d = dch0 + c;
+    const long H = p.H, W = p.W, D = p.D, M = p.M;
+    const bool qok = q * 4 < M;
+    float *ring = sm + w * kBRing * kBSlot;
+    float *xbuf = sm + kWarps * kBRing * kBSlot; /* [warp][2][32][4] */
+    float *edge = p.edge + ((long)blockIdx.y * gridDim.x + blockIdx.x) * H * 128;
+
+    float2 A0p[2], A1p[2], Ar0[2], Ar1[2], dA0[2], dA1[2];
+#pragma unroll
+    for (int jp = 0; jp < 2; ++jp) {
+        const int m = q * 4 + 2 * jp;
+        const float a0 = m < M ? p.A0[d * M + m] : 0.f, a1 = m + 1 < M ? p.A0[d * M + m + 1] : 0.f;
+        const float e0 = m < M ? p.A1[d * M + m] : 0.f, e1 = m + 1 < M ? p.A1[d * M + m + 1] : 0.f;
+        Ar0[jp] = kmb_f2(a0, a1);
+        Ar1[jp] = kmb_f2(e0, e1);
+        A0p[jp] = kmb_f2(a0 * KMB_LOG2E, a1 * KMB_LOG2E);
+        A1p[jp] = kmb_f2(e0 * KMB_LOG2E, e1 * KMB_LOG2E);
+        dA0[jp] = dA1[jp] = kmb_f2s(0.f);
+    }
+    const long nstrips = (W + kBStrip - 1) / kBStrip;
+    const long nsteps = H + kWarps - 1;
+    const float *hb = p.h + b * H * W * D * M;
+    float *dxb = p.dx + b * H * W * D;
+    float *dd0b = p.dd0 + b * p.dl_bs;
+    float *dd1b = p.dd1 + b * p.dl_bs;
+    float *dBb = p.dB + b * H * W * M;
+    float *dCb = p.dC + b * H * W * M;
+    const int lead = kWarps - 1 - w; /* steps this warp runs behind the leader */
+
+    for (long sidx = nstrips - 1; sidx >= 0; --sidx) {
+        const long j0 = sidx * kBStrip + w * kBCPW;
+        /* step t handles row r(t) = H-1 - (t - lead) */
+        auto row_of = [&](long t) { return H - 1 - (t - lead); };
+        float2 qv[kBCPW][2];   /* e0(p) G(p) of the row below, per column */
+        float2 hc[kBCPW][2];   /* h(i, j0 + k) of the current row */
+#pragma unroll
+        for (int k = 0; k < kBCPW; ++k) {
+            qv[k][0] = qv[k][1] = kmb_f2s(0.f);
+            const long j = j0 + k;
+            if (j < W && qok) {
+                const float4 v = *reinterpret_cast<const float4 *>(
+                    hb + (((H - 1) * W + j) * D + d) * M + q * 4);
+                hc[k][0] = kmb_f2(v.x, v.y);
+                hc[k][1] = kmb_f2(v.z, v.w);
+            } else {
+                hc[k][0] = hc[k][1] = kmb_f2s(0.f);
+            }
+        }
+        const bool use_edge = w == kWarps - 1 && sidx + 1 < nstrips;
+        auto edge_row = [&](long r) { return use_edge ? edge + r * 128 : nullptr; };
+        /* prologue: the first kBRing-1 rows this warp will run (H-1, H-2, ..) */
+#pragma unroll
+        for (int r = 0; r < kBRing - 1; ++r) {
+            stage_row_bwd(p, b, H - 1 - r, j0, dch0, ring + r * kBSlot, lane, edge_row(H - 1 - r));
+            kmb_cp_async_commit();
+        }
+        for (long t = 0; t < nsteps; ++t) {
+            const long n = t - lead; /* rows this warp has done before this step */
+            if (n >= 0) {
+                const long nr = n + kBRing - 1;
+                stage_row_bwd(p, b, H - 1 - nr, j0, dch0, ring + (nr % kBRing) * kBSlot, lane,
+                              edge_row(H - 1 - nr));
+            }
+            kmb_cp_async_commit();
+            kmb_cp_async_wait<kBRing - 1>();
+            __syncwarp();
+            const long i = row_of(t);
+            if (n >= 0 && i >= 0) {
+                const float *s = ring + (n % kBRing) * kBSlot;
+                /* carry from the right neighbour column: e1(p+1) G(p+1) */
+                float2 qh[2];
+                if (w < kWarps - 1) {
+                    const float4 v = *reinterpret_cast<const float4 *>(
+                        xbuf + (((w + 1) * 2 + ((t - 1) & 1)) * 32 + lane) * 4);
+                    qh[0] = kmb_f2(v.x, v.y);
+                    qh[1] = kmb_f2(v.z, v.w);
+                } else if (use_edge) {
+                    const float4 v = *reinterpret_cast<const float4 *>(
+                        s + 4 * kBX + 2 * kBB + kBH + kBL + lane * 4);
+                    qh[0] = kmb_f2(v.x, v.y);
+                    qh[1] = kmb_f2(v.z, v.w);
+                } else {
+                    qh[0] = qh[1] = kmb_f2s(0.f);
+                }
+#pragma unroll
+                for (int k = kBCPW - 1; k >= 0; --k) {
+                    const long j = j0 + k;
+                    const float xv = s[k * kCh + c];
+                    const float dv0 = s[kBX + k * kCh + c];
+                    const float dv1 = s[2 * kBX + k * kCh + c];
+                    const float gy = s[3 * kBX + k * kCh + c];
+                    const float4 B4 = *reinterpret_cast<const float4 *>(s + 4 * kBX + k * 16 + q * 4);
+                    const float4 C4 = *reinterpret_cast<const float4 *>(s + 4 * kBX + kBB + k * 16 + q * 4);
+                    const float4 H0 = *reinterpret_cast<const float4 *>(
+                        s + 4 * kBX + 2 * kBB + (k * kCh + c) * 16 + q * 4); /* h(i-1, j) */
+                    float2 hl[2]; /* h(i, j-1) */
+                    if (k > 0) {
+                        hl[0] = hc[k > 0 ? k - 1 : 0][0];
+                        hl[1] = hc[k > 0 ? k - 1 : 0][1];
+                    } else {
+                        const float4 v = *reinterpret_cast<const float4 *>(
+                            s + 4 * kBX + 2 * kBB + kBH + c * 16 + q * 4);
+                        hl[0] = kmb_f2(v.x, v.y);
+                        hl[1] = kmb_f2(v.z, v.w);
+                    }
+                    const float2 hu[2] = {kmb_f2(H0.x, H0.y), kmb_f2(H0.z, H0.w)};
+                    const float2 Bp[2] = {kmb_f2(B4.x, B4.y), kmb_f2(B4.z, B4.w)};
+                    const float2 Cp[2] = {kmb_f2(C4.x, C4.y), kmb_f2(C4.z, C4.w)};
+                    const float dtb = (dv0 + dv1) / 2.0f;
+                    const float2 dtb2 = kmb_f2s(dtb), x2 = kmb_f2s(xv), gy2 = kmb_f2s(gy);
+                    const float2 dv02 = kmb_f2s(dv0), dv12 = kmb_f2s(dv1);
+                    float2 sx2 = kmb_f2s(0.f), sb2 = kmb_f2s(0.f), s02 = kmb_f2s(0.f),
+                           s12 = kmb_f2s(0.f);
+                    float vbc[8];
+#pragma unroll
+                    for (int jp = 0; jp < 2; ++jp) {
+                        const float2 e0 = kmb_exp2_decay2(kmb_mul2(dv02, A0p[jp]));
+                        const float2 e1 = kmb_exp2_decay2(kmb_mul2(dv12, A1p[jp]));
+                        const float2 G = kmb_add2(kmb_add2(kmb_mul2(Cp[jp], gy2), qv[k][jp]), qh[jp]);
+                        const float2 gdt = kmb_mul2(G, dtb2);
+                        sx2 = kmb_fma2(gdt, Bp[jp], sx2);
+                        sb2 = kmb_fma2(kmb_mul2(G, Bp[jp]), x2, sb2);
+                        const float2 gh0 = kmb_mul2(kmb_mul2(G, hu[jp]), e0);
+                        const float2 gh1 = kmb_mul2(kmb_mul2(G, hl[jp]), e1);
+                        dA0[jp] = kmb_fma2(gh0, dv02, dA0[jp]);
+                        dA1[jp] = kmb_fma2(gh1, dv12, dA1[jp]);
+                        s02 = kmb_fma2(gh0, Ar0[jp], s02);
+                        s12 = kmb_fma2(gh1, Ar1[jp], s12);
+                        const float2 vb = kmb_mul2(gdt, x2);       /* dB */
+                        const float2 vc = kmb_mul2(gy2, hc[k][jp]); /* dC */
+                        vbc[2 * jp] = vb.x;
+                        vbc[2 * jp + 1] = vb.y;
+                        vbc[4 + 2 * jp] = vc.x;
+                        vbc[4 + 2 * jp + 1] = vc.y;
+                        /* carries to the point above and to the left */
+                        qv[k][jp] = kmb_mul2(e0, G);
+                        qh[jp] = kmb_mul2(e1, G);
+                    }
+                    /* dx, ddelta: sums over the 16 states (4 lanes) */
+                    float sx = sx2.x + sx2.y, sb = sb2.x + sb2.y;
+                    float s0 = s02.x + s02.y, s1 = s12.x + s12.y;
+#pragma unroll
+                    for (int o = 1; o <= 2; o <<= 1) {
+                        sx += __shfl_xor_sync(kFull, sx, o);
+                        sb += __shfl_xor_sync(kFull, sb, o);
+                        s0 += __shfl_xor_sync(kFull, s0, o);
+                        s1 += __shfl_xor_sync(kFull, s1, o);
+                    }
+                    /* dB / dC: sums over the 8 channels, then 4 states into
+                     * one lane for a 128-bit atomic */
+                    float v8[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) v8[u] = vbc[u];
+                    const float r1 = rs8_channels(v8, lane);
+                    /* lane 16 arr + 4 st + q holds state 4q + st of array arr */
+                    const float r2 = __shfl_down_sync(kFull, r1, 4);
+                    const float r3 = __shfl_down_sync(kFull, r1, 8);
+                    const float r4 = __shfl_down_sync(kFull, r1, 12);
+                    if (j < W) {
+                        const long pt = i * W + j;
+                        if (q == 0) {
+                            dxb[pt * D + d] = sx;
+                            dd0b[pt * D + d] = s0 + sb / 2.0f;
+                            dd1b[pt * D + d] = s1 + sb / 2.0f;
+                        }
+                        if ((c & 3) == 0 && qok) {
+                            float *dst = ((c >> 2) ? dCb : dBb) + pt * M + q * 4;
+                            atomicAdd(reinterpret_cast<float4 *>(dst), make_float4(r1, r2, r3, r4));
+                        }
+                    }
+                }
+                /* hand the carries on: the left neighbour warp (next step) and
+                 * the next strip (its last warp) get e1 G of column j0 */
+                const float4 outq = make_float4(qh[0].x, qh[0].y, qh[1].x, qh[1].y);
+                *reinterpret_cast<float4 *>(xbuf + ((w * 2 + (t & 1)) * 32 + lane) * 4) = outq;
+                if (w == 0) *reinterpret_cast<float4 *>(edge + i * 128 + lane * 4) = outq;
+                /* h of row i-1 becomes the current row */
+#pragma unroll
+                for (int k = 0; k < kBCPW; ++k) {
+                    const float4 v = *reinterpret_cast<const float4 *>(
+                        s + 4 * kBX + 2 * kBB + (k * kCh + c) * 16 + q * 4);
+                    hc[k][0] = kmb_f2(v.x, v.y);
+                    hc[k][1] = kmb_f2(v.z, v.w);
+                }
+            }
+            __syncthreads();
+        }
+        kmb_cp_async_wait<0>();
+        __syncthreads();
+    }
+    const float dAs0[4] = {dA0[0].x, dA0[0].y, dA0[1].x, dA0[1].y};
+    const float dAs1[4] = {dA1[0].x, dA1[0].y, dA1[1].x, dA1[1].y};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        if (q * 4 + u < M) {
+            atomicAdd(p.dA0 + d * M + q * 4 + u, dAs0[u]);
+            atomicAdd(p.dA1 + d * M + q * 4 + u, dAs1[u]);
+        }
+    }
+}
+
+} // namespace
+
+extern "C" int kmb_scan2d_supported(const KmbNDLaunch *a) {
+    return a->nd == 2 && a->bc_shared && a->M % 4 == 0 && a->M <= 16 && a->D % kCh == 0 &&
+           a->dims[0] > 0 && a->dims[1] > 0;
+}
+
+static S2D make_s2d(const KmbNDLaunch *a) {
+    S2D p;
+    memset(&p, 0, sizeof p);
+    p.x = a->x;
+    p.d0 = a->delta[0];
+    p.d1 = a->delta[1];
+    p.A0 = a->A[0];
+    p.A1 = a->A[1];
+    p.B = a->B;
+    p.C = a->C;
+    p.dy = a->dy;
+    p.H = a->dims[0];
+    p.W = a->dims[1];
+    p.D = a->D;
+    p.M = a->M;
+    p.dl_bs = a->delta_bstride;
+    return p;
+}
+
+extern "C" size_t kmb_scan2d_scratch_elems(const KmbNDLaunch *a) {
+    /* one edge column (H rows x 32 lanes x 4 states) per CTA */
+    return (size_t)a->batch * (a->D / kCh) * a->dims[0] * 128;
+}
+
+extern "C" int kmb_launch_scan2d_fwd(const KmbNDLaunch *a, cudaStream_t s) {
+    if (!kmb_scan2d_supported(a)) return kmb_fail(KMB_EUNSUPPORTED, "scan2d: unsupported shape");
+    if (!a->scratch || a->scratch_elems < kmb_scan2d_scratch_elems(a))
+        return kmb_fail(KMB_EINVAL, "scan2d: scratch too small");
+    S2D p = make_s2d(a);
+    p.hout = a->h;
+    p.y = a->y;
+    p.edge = a->scratch;
+    const size_t smem = sizeof(float) * ((size_t)kWarps * kRing * kSlot + kWarps * 2 * 32 * 4);
+    cudaError_t e = cudaFuncSetAttribute(k_scan2d_fwd, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e == cudaSuccess) {
+        dim3 grid((unsigned)(a->D / kCh), (unsigned)a->batch);
+        k_scan2d_fwd<<<grid, kWarps * 32, smem, s>>>(p);
+        e = cudaGetLastError();
+    }
+    return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "scan2d forward");
+}
+
+extern "C" int kmb_launch_scan2d_bwd(const KmbNDLaunch *a, cudaStream_t s) {
+    if (!kmb_scan2d_supported(a)) return kmb_fail(KMB_EUNSUPPORTED, "scan2d: unsupported shape");
+    if (!a->scratch || a->scratch_elems < kmb_scan2d_scratch_elems(a))
+        return kmb_fail(KMB_EINVAL, "scan2d: scratch too small");
+    S2D p = make_s2d(a);
+    p.h = a->h;
+    p.edge = a->scratch;
+    p.dx = a->dx;
+    p.dd0 = a->ddelta[0];
+    p.dd1 = a->ddelta[1];
+    p.dA0 = a->dA[0];
+    p.dA1 = a->dA[1];
+    p.dB = a->dB;
+    p.dC = a->dC;
+    cudaError_t e = cudaMemsetAsync(a->dA[0], 0, sizeof(float) * a->D * a->M, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(a->dA[1], 0, sizeof(float) * a->D * a->M, s);
+    const size_t nb = sizeof(float) * a->batch * a->P * a->M;
+    if (e == cudaSuccess) e = cudaMemsetAsync(a->dB, 0, nb, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(a->dC, 0, nb, s);
+    const size_t smem = sizeof(float) * ((size_t)kWarps * kBRing * kBSlot + kWarps * 2 * 32 * 4);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k_scan2d_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem);
+    if (e == cudaSuccess) {
+        dim3 grid((unsigned)(a->D / kCh), (unsigned)a->batch);
+        k_scan2d_bwd<<<grid, kWarps * 32, smem, s>>>(p);
+        e = cudaGetLastError();
+    }
+    return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "scan2d backward");
+}

@@ -96,7 +96,14 @@ static int run(const KmbScanND *a, int bwd) {
     L.nd = (int)nd;
     L.nlevels = plan.nlevels;
     L.bc_shared = a->bc_shared;
-    rc = bwd ? kmb_launch_scannd_bwd(&L, st.s) : kmb_launch_scannd_fwd(&L, st.s);
+    for (long i = 0; i < nd; ++i) L.dims[i] = a->dims[i];
+    if (kmb_scan2d_supported(&L)) {
+        L.scratch_elems = kmb_scan2d_scratch_elems(&L);
+        L.scratch = (float *)kmb_scratch(&st, sizeof(float) * L.scratch_elems);
+        rc = st.status;
+        if (!rc) rc = bwd ? kmb_launch_scan2d_bwd(&L, st.s) : kmb_launch_scan2d_fwd(&L, st.s);
+    } else
+        rc = bwd ? kmb_launch_scannd_bwd(&L, st.s) : kmb_launch_scannd_fwd(&L, st.s);
     return kmb_stage_finish(&st, rc);
 }
 

@@ -52,10 +52,20 @@ typedef struct {
     const int *lvl_start, *lvl_off, *prev, *next;
     long P, D, M, batch;
     long delta_bstride; /* floats between batch items of each delta axis */
+    long dims[KMB_MAX_AXES];
+    float *scratch;       /* device scratch of the 2D kernels */
+    size_t scratch_elems;
     int nd, nlevels, bc_shared;
 } KmbNDLaunch;
 int kmb_launch_scannd_fwd(const KmbNDLaunch *a, cudaStream_t s);
 int kmb_launch_scannd_bwd(const KmbNDLaunch *a, cudaStream_t s);
+/* 2D wavefront kernels (csrc/cuda/scan2d.cu) for nd == 2 with channel-shared
+ * B/C, M a multiple of 4 up to 16 and D a multiple of 8; KMB_EUNSUPPORTED
+ * for other shapes (the generic ND kernels take those). */
+int kmb_launch_scan2d_fwd(const KmbNDLaunch *a, cudaStream_t s);
+int kmb_launch_scan2d_bwd(const KmbNDLaunch *a, cudaStream_t s);
+int kmb_scan2d_supported(const KmbNDLaunch *a);
+size_t kmb_scan2d_scratch_elems(const KmbNDLaunch *a);
 
 /* Block / model kernels (csrc/cuda/block.cu). */
 /* C[m*ldc + n] (+)= sum_k A[m*am + k*ak] * B[k*bk + n*bn], fp32.  ws

@@ -150,7 +150,13 @@ def test_scan2d_vs_oracle(lib, cuda, oracle, d1, d2, D, M):
 
 @pytest.mark.parametrize("dims,D,M,shared", [([6, 5], 4, 3, False), ([4, 4], 8, 16, True),
                                              ([3, 4, 5], 3, 2, True), ([2, 3, 2, 3], 2, 4, False),
-                                             ([40], 5, 4, True), ([9, 13], 37, 5, True)])
+                                             ([40], 5, 4, True), ([9, 13], 37, 5, True),
+                                             # 2D wavefront kernels (channel-shared B/C,
+                                             # M % 4 == 0 <= 16, D % 8 == 0): several
+                                             # strips with a ragged last one, more rows
+                                             # than the staging ring, M 8 and 12
+                                             ([70, 130], 16, 16, True), ([9, 64], 8, 8, True),
+                                             ([150, 20], 24, 12, True), ([1, 200], 8, 16, True)])
 def test_batched_fwd_bwd_vs_oracle(lib, cuda, oracle, dims, D, M, shared):
     import torch
     declare(lib)
