@@ -328,7 +328,7 @@ def run_secondary(args):
         lib.kmb_scannd_bwd.argtypes = [C.c_void_p]
         fwd = lambda: kb.check(lib, lib.kmb_scannd_fwd(C.byref(a)))  # noqa: E731
         bwd = lambda: kb.check(lib, lib.kmb_scannd_bwd(C.byref(a)))  # noqa: E731
-        names = ("k_scannd_fwd", "k_scannd_bwd")
+        names = ("k_scan2d_fwd", "k_scan2d_bwd")
         workload = (f"config4: 2D selective scan 256x256, batch {bsz}, D 256, N 16, fp32, "
                     "B/C shared, dt = softplus(N(0,1)-2) + ln 2 on both axes, fwd+bwd "
                     "(stored-state kernels of the reference API)")

@@ -64,38 +64,66 @@ struct S2D {
     long dl_bs; /* floats between batch items of each delta axis */
 };
 
-/* Stages row i (columns j0 .. j0+7) of this warp's inputs into slot `s`:
- * 16-byte cp.async copies, zero-filled outside the grid. */
-__device__ __forceinline__ void stage_row(const S2D &p, long b, long i, long j0, long dch0,
-                                          float *s, int lane, const float *edge_row) {
+/* The forward's copies of one staged row, per lane: chunk u of the lane
+ * is element lane + 32u of the slot's 112 16-byte chunks (x / delta_0 /
+ * delta_1: 16 each, B / C: 32 each).  Only the row changes between rows,
+ * so the source pointer at row 0, the row stride and the column validity
+ * are fixed for a strip. */
+struct FwdCopies {
+    const float *src[4];
+    long rs[4];
+    int dst[4];
+    bool ok[4];
+};
+
+__device__ __forceinline__ void fwd_copies(const S2D &p, long b, long j0, long dch0, int lane,
+                                           FwdCopies &f) {
     const long W = p.W, D = p.D, M = p.M;
-    const bool rok = i >= 0 && i < p.H;
-    if (edge_row) /* 32 lanes x 16 bytes */
-        kmb_cp_async16(s + 3 * kSlotX + 2 * kSlotB + lane * 4, rok ? edge_row + lane * 4 : p.x,
-                       rok ? 16 : 0);
-    /* x / delta_0 / delta_1: per column 8 channels = 2 chunks -> 16 chunks each */
-    for (int e = lane; e < 3 * 16 + 2 * kCPW * 4; e += 32) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const int e = lane + 32 * u;
         if (e < 48) {
             const int t = e / 16, r = e % 16, col = r / 2, half = r % 2;
             const long j = j0 + col;
-            const bool ok = rok && j < W;
             const float *base = t == 0 ? p.x + b * p.H * W * D
                                        : (t == 1 ? p.d0 : p.d1) + b * p.dl_bs;
-            const float *src = ok ? base + (i * W + j) * D + dch0 + half * 4 : p.x;
-            kmb_cp_async16(s + t * kSlotX + col * kCh + half * 4, src, ok ? 16 : 0);
-        } else {
+            f.src[u] = base + j * D + dch0 + half * 4;
+            f.rs[u] = W * D;
+            f.dst[u] = t * kSlotX + col * kCh + half * 4;
+            f.ok[u] = j < W;
+        } else if (e < 112) {
             const int e2 = e - 48, t = e2 / (kCPW * 4), r = e2 % (kCPW * 4);
             const int col = r / 4, q = r % 4;
             const long j = j0 + col;
-            const bool ok = rok && j < W && q * 4 < M;
-            const float *base = (t == 0 ? p.B : p.C) + b * p.H * W * M;
-            const float *src = ok ? base + (i * W + j) * M + q * 4 : p.x;
-            kmb_cp_async16(s + 3 * kSlotX + t * kSlotB + col * 16 + q * 4, src, ok ? 16 : 0);
+            f.src[u] = (t == 0 ? p.B : p.C) + b * p.H * W * M + j * M + q * 4;
+            f.rs[u] = W * M;
+            f.dst[u] = 3 * kSlotX + t * kSlotB + col * 16 + q * 4;
+            f.ok[u] = j < W && q * 4 < M;
+        } else {
+            f.src[u] = p.x;
+            f.rs[u] = 0;
+            f.dst[u] = -1;
+            f.ok[u] = false;
         }
     }
 }
 
-__global__ void __launch_bounds__(kWarps * 32) k_scan2d_fwd(S2D p) {
+__device__ __forceinline__ void stage_row_fast(const S2D &p, const FwdCopies &f, long i,
+                                               float *s, int lane, const float *edge_row) {
+    const bool rok = i >= 0 && i < p.H;
+    if (edge_row)
+        kmb_cp_async16(s + 3 * kSlotX + 2 * kSlotB + lane * 4, rok ? edge_row + lane * 4 : p.x,
+                       rok ? 16 : 0);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        if (f.dst[u] >= 0) {
+            const bool ok = rok && f.ok[u];
+            kmb_cp_async16(s + f.dst[u], ok ? f.src[u] + i * f.rs[u] : p.x, ok ? 16 : 0);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_fwd(S2D p) {
     extern __shared__ __align__(16) float sm[];
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const int c = lane >> 2, q = lane & 3;
@@ -131,10 +159,17 @@ __global__ void __launch_bounds__(kWarps * 32) k_scan2d_fwd(S2D p) {
          * column, written by that strip's last warp (CTA barriers since) */
         const bool use_edge = w == 0 && sidx > 0;
         auto edge_row = [&](long r) { return use_edge ? edge + r * 128 : nullptr; };
+        FwdCopies fc;
+        fwd_copies(p, b, j0, dch0, lane, fc);
+        /* h and y of this warp's first column at row 0; a row is W*D*M
+         * (W*D) floats further */
+        float *hcol = hb + (j0 * D + d) * M + q * 4;
+        float *ycol = yb + j0 * D + d;
+        const long hrow = W * D * M, yrow = W * D;
         /* prologue: rows 0 .. kRing-2 of this warp */
 #pragma unroll
         for (int r = 0; r < kRing - 1; ++r) {
-            stage_row(p, b, r, j0, dch0, ring + r * kSlot, lane, edge_row(r));
+            stage_row_fast(p, fc, r, ring + r * kSlot, lane, edge_row(r));
             kmb_cp_async_commit();
         }
         for (long t = 0; t < nsteps; ++t) {
@@ -143,8 +178,8 @@ __global__ void __launch_bounds__(kWarps * 32) k_scan2d_fwd(S2D p) {
              * kRing - 1 came with the prologue.  One commit per step keeps
              * the group count uniform. */
             if (i >= 0)
-                stage_row(p, b, i + kRing - 1, j0, dch0, ring + ((i + kRing - 1) % kRing) * kSlot,
-                          lane, edge_row(i + kRing - 1));
+                stage_row_fast(p, fc, i + kRing - 1, ring + ((i + kRing - 1) % kRing) * kSlot, lane,
+                               edge_row(i + kRing - 1));
             kmb_cp_async_commit();
             kmb_cp_async_wait<kRing - 1>();
             __syncwarp();
@@ -191,7 +226,7 @@ __global__ void __launch_bounds__(kWarps * 32) k_scan2d_fwd(S2D p) {
                         y2 = kmb_fma2(Cp[jp], hn, y2);
                     }
                     if (j < W && qok)
-                        *reinterpret_cast<float4 *>(hb + ((i * W + j) * D + d) * M + q * 4) =
+                        *reinterpret_cast<float4 *>(hcol + i * hrow + k * D * M) =
                             make_float4(hv[k][0].x, hv[k][0].y, hv[k][1].x, hv[k][1].y);
                     /* y: sum over the 4 state groups, 4 columns per fold */
                     yq[k & 3] = y2.x + y2.y;
@@ -207,7 +242,7 @@ __global__ void __launch_bounds__(kWarps * 32) k_scan2d_fwd(S2D p) {
                             }
                         }
                         const long jy = j0 + (k - 3) + q;
-                        if (jy < W) yb[(i * W + jy) * D + d] = yq[0];
+                        if (jy < W) ycol[i * yrow + ((k - 3) + q) * D] = yq[0];
                     }
                 }
                 /* the last column's states go to the next warp (and, from
@@ -240,48 +275,79 @@ constexpr int kBL = kCh * 16;
 constexpr int kBE = 128;
 constexpr int kBSlot = 4 * kBX + 2 * kBB + kBH + kBL + kBE;
 
-/* stages row i of this warp (columns j0 .. j0+3): inputs of row i, h of
- * row i-1 for the same columns and h(i, j0-1); zero outside the grid */
-__device__ __forceinline__ void stage_row_bwd(const S2D &p, long b, long i, long j0, long dch0,
-                                              float *s, int lane, const float *edge_row) {
+/* The backward's copies of one staged row, per lane, fixed for a strip:
+ * one chunk of x / delta_0 / delta_1 / dy (lane / 8 picks the tensor), one
+ * of B / C (lane / 16), and five of h: h(i-1, j0 + u) for u < 4 and
+ * h(i, j0-1) for u = 4, all for channel lane / 4 and states 4 (lane % 4).
+ * Sources are kept at row 0; a row further is W*D (inputs), W*M (B, C)
+ * or W*D*M (h) floats. */
+struct BwdCopies {
+    const float *in, *bc, *h;
+    int in_dst, bc_dst;
+    bool in_ok, bc_ok;
+    unsigned h_ok; /* bit u: column of h chunk u inside the grid and q*4 < M */
+};
+
+__device__ __forceinline__ void bwd_copies(const S2D &p, long b, long j0, long dch0, int lane,
+                                           BwdCopies &f) {
     const long H = p.H, W = p.W, D = p.D, M = p.M;
-    const bool rok = i >= 0 && i < H;
-    if (edge_row)
-        kmb_cp_async16(s + 4 * kBX + 2 * kBB + kBH + kBL + lane * 4,
-                       rok ? edge_row + lane * 4 : p.x, rok ? 16 : 0);
-    /* x, delta_0, delta_1, dy: 4 columns x 2 chunks each = 32 chunks */
     {
         const int t = lane / 8, r = lane % 8, col = r / 2, half = r % 2;
         const long j = j0 + col;
-        const bool ok = rok && j < W;
         const float *base = t == 0   ? p.x + b * H * W * D
                             : t == 1 ? p.d0 + b * p.dl_bs
                             : t == 2 ? p.d1 + b * p.dl_bs
                                      : p.dy + b * H * W * D;
-        kmb_cp_async16(s + t * kBX + col * kCh + half * 4,
-                       ok ? base + (i * W + j) * D + dch0 + half * 4 : p.x, ok ? 16 : 0);
+        f.in = base + j * D + dch0 + half * 4;
+        f.in_dst = t * kBX + col * kCh + half * 4;
+        f.in_ok = j < W;
     }
-    /* B, C: 4 columns x 4 chunks = 16 chunks each */
     {
         const int t = lane / 16, r = lane % 16, col = r / 4, q = r % 4;
         const long j = j0 + col;
-        const bool ok = rok && j < W && q * 4 < M;
-        const float *base = (t == 0 ? p.B : p.C) + b * H * W * M;
-        kmb_cp_async16(s + 4 * kBX + t * kBB + col * 16 + q * 4,
-                       ok ? base + (i * W + j) * M + q * 4 : p.x, ok ? 16 : 0);
+        f.bc = (t == 0 ? p.B : p.C) + b * H * W * M + j * M + q * 4;
+        f.bc_dst = 4 * kBX + t * kBB + col * 16 + q * 4;
+        f.bc_ok = j < W && q * 4 < M;
     }
-    /* h(i-1, j0 .. j0+3) for the 8 channels: 4 x 8 x (M/4) chunks; and
-     * h(i, j0-1): 8 x (M/4) chunks */
-    const float *hbase = p.h + b * H * W * D * M;
-    for (int e = lane; e < (kBCPW + 1) * kCh * 4; e += 32) {
-        const int col = e / (kCh * 4), r = e % (kCh * 4), ch = r / 4, q = r % 4;
-        const long ii = col < kBCPW ? i - 1 : i;
-        const long j = col < kBCPW ? j0 + col : j0 - 1;
-        const bool ok = rok && ii >= 0 && j >= 0 && j < W && q * 4 < M;
-        float *dst = col < kBCPW ? s + 4 * kBX + 2 * kBB + (col * kCh + ch) * 16 + q * 4
-                                 : s + 4 * kBX + 2 * kBB + kBH + ch * 16 + q * 4;
-        kmb_cp_async16(dst, ok ? hbase + ((ii * W + j) * D + dch0 + ch) * M + q * 4 : p.x,
-                       ok ? 16 : 0);
+    const int ch = lane / 4, q = lane % 4;
+    f.h = p.h + b * H * W * D * M + (j0 * D + dch0 + ch) * M + q * 4;
+    f.h_ok = 0;
+#pragma unroll
+    for (int u = 0; u < kBCPW + 1; ++u) {
+        const long j = u < kBCPW ? j0 + u : j0 - 1;
+        if (j >= 0 && j < W && q * 4 < M) f.h_ok |= 1u << u;
+    }
+}
+
+/* stages row i of this warp (columns j0 .. j0+3): inputs of row i, h of
+ * row i-1 for the same columns and h(i, j0-1); zero outside the grid */
+__device__ __forceinline__ void stage_row_bwd_fast(const S2D &p, const BwdCopies &f, long i,
+                                                   float *s, int lane, const float *edge_row) {
+    const bool rok = i >= 0 && i < p.H;
+    if (edge_row)
+        kmb_cp_async16(s + 4 * kBX + 2 * kBB + kBH + kBL + lane * 4,
+                       rok ? edge_row + lane * 4 : p.x, rok ? 16 : 0);
+    {
+        const bool ok = rok && f.in_ok;
+        kmb_cp_async16(s + f.in_dst, ok ? f.in + i * (p.W * p.D) : p.x, ok ? 16 : 0);
+    }
+    {
+        const bool ok = rok && f.bc_ok;
+        kmb_cp_async16(s + f.bc_dst, ok ? f.bc + i * (p.W * p.M) : p.x, ok ? 16 : 0);
+    }
+    const int ch = lane / 4, q = lane % 4;
+    const long h_col = p.D * p.M, h_rs = p.W * h_col;
+    const float *hrow = f.h + i * h_rs;
+#pragma unroll
+    for (int u = 0; u < kBCPW; ++u) {
+        const bool ok = rok && i >= 1 && ((f.h_ok >> u) & 1);
+        kmb_cp_async16(s + 4 * kBX + 2 * kBB + (u * kCh + ch) * 16 + q * 4,
+                       ok ? hrow - h_rs + u * h_col : p.x, ok ? 16 : 0);
+    }
+    {
+        const bool ok = rok && ((f.h_ok >> kBCPW) & 1);
+        kmb_cp_async16(s + 4 * kBX + 2 * kBB + kBH + ch * 16 + q * 4,
+                       ok ? hrow - h_col : p.x, ok ? 16 : 0);
     }
 }
 
@@ -359,18 +425,20 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_bwd(S2D p) {
         }
         const bool use_edge = w == kWarps - 1 && sidx + 1 < nstrips;
         auto edge_row = [&](long r) { return use_edge ? edge + r * 128 : nullptr; };
+        BwdCopies bc;
+        bwd_copies(p, b, j0, dch0, lane, bc);
         /* prologue: the first kBRing-1 rows this warp will run (H-1, H-2, ..) */
 #pragma unroll
         for (int r = 0; r < kBRing - 1; ++r) {
-            stage_row_bwd(p, b, H - 1 - r, j0, dch0, ring + r * kBSlot, lane, edge_row(H - 1 - r));
+            stage_row_bwd_fast(p, bc, H - 1 - r, ring + r * kBSlot, lane, edge_row(H - 1 - r));
             kmb_cp_async_commit();
         }
         for (long t = 0; t < nsteps; ++t) {
             const long n = t - lead; /* rows this warp has done before this step */
             if (n >= 0) {
                 const long nr = n + kBRing - 1;
-                stage_row_bwd(p, b, H - 1 - nr, j0, dch0, ring + (nr % kBRing) * kBSlot, lane,
-                              edge_row(H - 1 - nr));
+                stage_row_bwd_fast(p, bc, H - 1 - nr, ring + (nr % kBRing) * kBSlot, lane,
+                                   edge_row(H - 1 - nr));
             }
             kmb_cp_async_commit();
             kmb_cp_async_wait<kBRing - 1>();
