@@ -10,6 +10,7 @@
  * constant once per (channel, state) so that every discretisation step is
  * one multiply plus one MUFU ex2. */
 #define KMB_LOG2E 1.4426950408889634f
+#define KMB_LN2 0.6931471805599453f
 
 /* 2^x on the MUFU unit (PTX ex2.approx, subnormal results flushed to 0). */
 __device__ __forceinline__ float kmb_ex2(float x) {

@@ -64,6 +64,33 @@ struct S2D {
     long dl_bs; /* floats between batch items of each delta axis */
 };
 
+/* min over the lane's four states of |log2(e) A| */
+__device__ __forceinline__ float abs_min4(const float2 (&a)[2]) {
+    return fminf(fminf(fabsf(a[0].x), fabsf(a[0].y)), fminf(fabsf(a[1].x), fabsf(a[1].y)));
+}
+
+/* False only when every |w| = |delta A log2(e)| of the lane's states is at
+ * least 1/16, i.e. no element takes the weak-decay polynomial: rounding is
+ * monotonic, so |delta| amin >= 1/16 implies fl(|delta| |A_m|) >= 1/16 for
+ * every state m.  Lanes past the last state (`live` false) never count. */
+__device__ __forceinline__ bool weak_possible(float dv0, float dv1, float amin0, float amin1,
+                                              bool live) {
+    return live && (fabsf(dv0) * amin0 < 0.0625f || fabsf(dv1) * amin1 < 0.0625f);
+}
+
+/* e = 2^w for the four state pairs of one point (both axes, two pairs
+ * each), elementwise equal to kmb_exp2_decay2: the MUFU ex2 for all, and
+ * the polynomial path only when some lane of the warp may need it.  All 32
+ * lanes must run it. */
+__device__ __forceinline__ void exp2_decay_point(const float2 (&w)[4], float2 (&e)[4], bool weak) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) e[u] = kmb_f2(kmb_ex2(w[u].x), kmb_ex2(w[u].y));
+    if (__any_sync(kFull, weak)) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) e[u] = kmb_exp2_decay2(w[u]);
+    }
+}
+
 /* The forward's copies of one staged row, per lane: chunk u of the lane
  * is element lane + 32u of the slot's 112 16-byte chunks (x / delta_0 /
  * delta_1: 16 each, B / C: 32 each).  Only the row changes between rows,
@@ -71,7 +98,7 @@ struct S2D {
  * are fixed for a strip. */
 struct FwdCopies {
     const float *src[4];
-    long rs[4];
+    long rs1; /* row stride of chunk 1 (x / delta rows: W*D; B / C rows: W*M) */
     int dst[4];
     bool ok[4];
 };
@@ -88,7 +115,7 @@ __device__ __forceinline__ void fwd_copies(const S2D &p, long b, long j0, long d
             const float *base = t == 0 ? p.x + b * p.H * W * D
                                        : (t == 1 ? p.d0 : p.d1) + b * p.dl_bs;
             f.src[u] = base + j * D + dch0 + half * 4;
-            f.rs[u] = W * D;
+            if (u == 1) f.rs1 = W * D;
             f.dst[u] = t * kSlotX + col * kCh + half * 4;
             f.ok[u] = j < W;
         } else if (e < 112) {
@@ -96,12 +123,11 @@ __device__ __forceinline__ void fwd_copies(const S2D &p, long b, long j0, long d
             const int col = r / 4, q = r % 4;
             const long j = j0 + col;
             f.src[u] = (t == 0 ? p.B : p.C) + b * p.H * W * M + j * M + q * 4;
-            f.rs[u] = W * M;
+            if (u == 1) f.rs1 = W * M;
             f.dst[u] = 3 * kSlotX + t * kSlotB + col * 16 + q * 4;
             f.ok[u] = j < W && q * 4 < M;
         } else {
             f.src[u] = p.x;
-            f.rs[u] = 0;
             f.dst[u] = -1;
             f.ok[u] = false;
         }
@@ -118,7 +144,8 @@ __device__ __forceinline__ void stage_row_fast(const S2D &p, const FwdCopies &f,
     for (int u = 0; u < 4; ++u) {
         if (f.dst[u] >= 0) {
             const bool ok = rok && f.ok[u];
-            kmb_cp_async16(s + f.dst[u], ok ? f.src[u] + i * f.rs[u] : p.x, ok ? 16 : 0);
+            const long rs = u == 0 ? p.W * p.D : u == 1 ? f.rs1 : p.W * p.M;
+            kmb_cp_async16(s + f.dst[u], ok ? f.src[u] + i * rs : p.x, ok ? 16 : 0);
         }
     }
 }
@@ -145,6 +172,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_fwd(S2D p) {
         A0p[jp] = kmb_f2(a0 * KMB_LOG2E, a1 * KMB_LOG2E);
         A1p[jp] = kmb_f2(e0 * KMB_LOG2E, e1 * KMB_LOG2E);
     }
+    const float amin0 = abs_min4(A0p), amin1 = abs_min4(A1p);
     const long nstrips = (W + kStrip - 1) / kStrip;
     const long nsteps = H + kWarps - 1;
     float *hb = p.hout + b * H * W * D * M;
@@ -172,19 +200,20 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_fwd(S2D p) {
             stage_row_fast(p, fc, r, ring + r * kSlot, lane, edge_row(r));
             kmb_cp_async_commit();
         }
+        int slot = 0; /* i % kRing once i >= 0 */
         for (long t = 0; t < nsteps; ++t) {
             const long i = t - w; /* this warp's row */
             /* row i + kRing - 1 goes into the slot row i - 1 used; rows below
              * kRing - 1 came with the prologue.  One commit per step keeps
              * the group count uniform. */
             if (i >= 0)
-                stage_row_fast(p, fc, i + kRing - 1, ring + ((i + kRing - 1) % kRing) * kSlot, lane,
-                               edge_row(i + kRing - 1));
+                stage_row_fast(p, fc, i + kRing - 1, ring + (slot == 0 ? kRing - 1 : slot - 1) * kSlot,
+                               lane, edge_row(i + kRing - 1));
             kmb_cp_async_commit();
             kmb_cp_async_wait<kRing - 1>();
             __syncwarp();
             if (i >= 0 && i < H) {
-                const float *s = ring + (i % kRing) * kSlot;
+                const float *s = ring + slot * kSlot;
                 /* left neighbour of column j0 at row i */
                 float2 hl[2];
                 if (w > 0) {
@@ -208,17 +237,19 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_fwd(S2D p) {
                     const float dv1 = s[2 * kSlotX + k * kCh + c];
                     const float4 B4 = *reinterpret_cast<const float4 *>(s + 3 * kSlotX + k * 16 + q * 4);
                     const float4 C4 = *reinterpret_cast<const float4 *>(s + 3 * kSlotX + kSlotB + k * 16 + q * 4);
-                    const float2 x2 = kmb_f2s(xv);
-                    const float2 dtb2 = kmb_f2s((dv0 + dv1) / 2.0f);
+                    const float2 dtx2 = kmb_f2s((dv0 + dv1) / 2.0f * xv); /* dt_bar x */
                     const float2 dv02 = kmb_f2s(dv0), dv12 = kmb_f2s(dv1);
                     const float2 Bp[2] = {kmb_f2(B4.x, B4.y), kmb_f2(B4.z, B4.w)};
                     const float2 Cp[2] = {kmb_f2(C4.x, C4.y), kmb_f2(C4.z, C4.w)};
                     float2 y2 = kmb_f2s(0.f);
+                    const float2 wv[4] = {kmb_mul2(dv02, A0p[0]), kmb_mul2(dv02, A0p[1]),
+                                          kmb_mul2(dv12, A1p[0]), kmb_mul2(dv12, A1p[1])};
+                    float2 ev[4];
+                    exp2_decay_point(wv, ev, weak_possible(dv0, dv1, amin0, amin1, qok));
 #pragma unroll
                     for (int jp = 0; jp < 2; ++jp) {
-                        float2 hn = kmb_mul2(dtb2, kmb_mul2(Bp[jp], x2));
-                        const float2 e0 = kmb_exp2_decay2(kmb_mul2(dv02, A0p[jp]));
-                        const float2 e1 = kmb_exp2_decay2(kmb_mul2(dv12, A1p[jp]));
+                        float2 hn = kmb_mul2(Bp[jp], dtx2);
+                        const float2 e0 = ev[jp], e1 = ev[2 + jp];
                         hn = kmb_fma2(e0, hv[k][jp], hn);
                         hn = kmb_fma2(e1, hl[jp], hn);
                         hv[k][jp] = hn;
@@ -251,6 +282,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_fwd(S2D p) {
                 *reinterpret_cast<float4 *>(xbuf + ((w * 2 + (t & 1)) * 32 + lane) * 4) = last;
                 if (w == kWarps - 1) *reinterpret_cast<float4 *>(edge + i * 128 + lane * 4) = last;
             }
+            if (i >= 0) slot = slot == kRing - 1 ? 0 : slot + 1;
             __syncthreads();
         }
         kmb_cp_async_wait<0>();
@@ -382,18 +414,17 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_bwd(S2D p) {
     float *xbuf = sm + kWarps * kBRing * kBSlot; /* [warp][2][32][4] */
     float *edge = p.edge + ((long)blockIdx.y * gridDim.x + blockIdx.x) * H * 128;
 
-    float2 A0p[2], A1p[2], Ar0[2], Ar1[2], dA0[2], dA1[2];
+    float2 A0p[2], A1p[2], dA0[2], dA1[2];
 #pragma unroll
     for (int jp = 0; jp < 2; ++jp) {
         const int m = q * 4 + 2 * jp;
         const float a0 = m < M ? p.A0[d * M + m] : 0.f, a1 = m + 1 < M ? p.A0[d * M + m + 1] : 0.f;
         const float e0 = m < M ? p.A1[d * M + m] : 0.f, e1 = m + 1 < M ? p.A1[d * M + m + 1] : 0.f;
-        Ar0[jp] = kmb_f2(a0, a1);
-        Ar1[jp] = kmb_f2(e0, e1);
         A0p[jp] = kmb_f2(a0 * KMB_LOG2E, a1 * KMB_LOG2E);
         A1p[jp] = kmb_f2(e0 * KMB_LOG2E, e1 * KMB_LOG2E);
         dA0[jp] = dA1[jp] = kmb_f2s(0.f);
     }
+    const float amin0 = abs_min4(A0p), amin1 = abs_min4(A1p);
     const long nstrips = (W + kBStrip - 1) / kBStrip;
     const long nsteps = H + kWarps - 1;
     const float *hb = p.h + b * H * W * D * M;
@@ -433,11 +464,13 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_bwd(S2D p) {
             stage_row_bwd_fast(p, bc, H - 1 - r, ring + r * kBSlot, lane, edge_row(H - 1 - r));
             kmb_cp_async_commit();
         }
+        int slot = 0; /* n % kBRing once n >= 0 */
         for (long t = 0; t < nsteps; ++t) {
             const long n = t - lead; /* rows this warp has done before this step */
             if (n >= 0) {
                 const long nr = n + kBRing - 1;
-                stage_row_bwd_fast(p, bc, H - 1 - nr, ring + (nr % kBRing) * kBSlot, lane,
+                stage_row_bwd_fast(p, bc, H - 1 - nr,
+                                   ring + (slot == 0 ? kBRing - 1 : slot - 1) * kBSlot, lane,
                                    edge_row(H - 1 - nr));
             }
             kmb_cp_async_commit();
@@ -445,7 +478,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_bwd(S2D p) {
             __syncwarp();
             const long i = row_of(t);
             if (n >= 0 && i >= 0) {
-                const float *s = ring + (n % kBRing) * kBSlot;
+                const float *s = ring + slot * kBSlot;
                 /* carry from the right neighbour column: e1(p+1) G(p+1) */
                 float2 qh[2];
                 if (w < kWarps - 1) {
@@ -461,6 +494,9 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_bwd(S2D p) {
                 } else {
                     qh[0] = qh[1] = kmb_f2s(0.f);
                 }
+                /* offsets of (i, j0): channel d in [P, D] tensors, states
+                 * 4q.. in [P, M] ones */
+                const long ox = (i * W + j0) * D + d, obc = (i * W + j0) * M + q * 4;
 #pragma unroll
                 for (int k = kBCPW - 1; k >= 0; --k) {
                     const long j = j0 + k;
@@ -486,45 +522,48 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_bwd(S2D p) {
                     const float2 Bp[2] = {kmb_f2(B4.x, B4.y), kmb_f2(B4.z, B4.w)};
                     const float2 Cp[2] = {kmb_f2(C4.x, C4.y), kmb_f2(C4.z, C4.w)};
                     const float dtb = (dv0 + dv1) / 2.0f;
-                    const float2 dtb2 = kmb_f2s(dtb), x2 = kmb_f2s(xv), gy2 = kmb_f2s(gy);
+                    /* dB(p, m) gets G dt_bar x: one product per point */
+                    const float2 dtx2 = kmb_f2s(dtb * xv), gy2 = kmb_f2s(gy);
                     const float2 dv02 = kmb_f2s(dv0), dv12 = kmb_f2s(dv1);
-                    float2 sx2 = kmb_f2s(0.f), sb2 = kmb_f2s(0.f), s02 = kmb_f2s(0.f),
-                           s12 = kmb_f2s(0.f);
+                    float2 gb2 = kmb_f2s(0.f), s02 = kmb_f2s(0.f), s12 = kmb_f2s(0.f);
                     float vbc[8];
+                    const float2 wv[4] = {kmb_mul2(dv02, A0p[0]), kmb_mul2(dv02, A0p[1]),
+                                          kmb_mul2(dv12, A1p[0]), kmb_mul2(dv12, A1p[1])};
+                    float2 ev[4];
+                    exp2_decay_point(wv, ev, weak_possible(dv0, dv1, amin0, amin1, qok));
 #pragma unroll
                     for (int jp = 0; jp < 2; ++jp) {
-                        const float2 e0 = kmb_exp2_decay2(kmb_mul2(dv02, A0p[jp]));
-                        const float2 e1 = kmb_exp2_decay2(kmb_mul2(dv12, A1p[jp]));
-                        const float2 G = kmb_add2(kmb_add2(kmb_mul2(Cp[jp], gy2), qv[k][jp]), qh[jp]);
-                        const float2 gdt = kmb_mul2(G, dtb2);
-                        sx2 = kmb_fma2(gdt, Bp[jp], sx2);
-                        sb2 = kmb_fma2(kmb_mul2(G, Bp[jp]), x2, sb2);
-                        const float2 gh0 = kmb_mul2(kmb_mul2(G, hu[jp]), e0);
-                        const float2 gh1 = kmb_mul2(kmb_mul2(G, hl[jp]), e1);
+                        const float2 e0 = ev[jp], e1 = ev[2 + jp];
+                        const float2 G = kmb_add2(kmb_fma2(Cp[jp], gy2, qv[k][jp]), qh[jp]);
+                        gb2 = kmb_fma2(G, Bp[jp], gb2); /* sum_m G B */
+                        /* carries to the point above and to the left; the
+                         * h-weighted terms reuse them: G h e = (e G) h */
+                        qv[k][jp] = kmb_mul2(e0, G);
+                        qh[jp] = kmb_mul2(e1, G);
+                        const float2 gh0 = kmb_mul2(qv[k][jp], hu[jp]);
+                        const float2 gh1 = kmb_mul2(qh[jp], hl[jp]);
                         dA0[jp] = kmb_fma2(gh0, dv02, dA0[jp]);
                         dA1[jp] = kmb_fma2(gh1, dv12, dA1[jp]);
-                        s02 = kmb_fma2(gh0, Ar0[jp], s02);
-                        s12 = kmb_fma2(gh1, Ar1[jp], s12);
-                        const float2 vb = kmb_mul2(gdt, x2);       /* dB */
+                        s02 = kmb_fma2(gh0, A0p[jp], s02); /* log2(e) A_0: scaled by ln 2 below */
+                        s12 = kmb_fma2(gh1, A1p[jp], s12);
+                        const float2 vb = kmb_mul2(G, dtx2);        /* dB */
                         const float2 vc = kmb_mul2(gy2, hc[k][jp]); /* dC */
                         vbc[2 * jp] = vb.x;
                         vbc[2 * jp + 1] = vb.y;
                         vbc[4 + 2 * jp] = vc.x;
                         vbc[4 + 2 * jp + 1] = vc.y;
-                        /* carries to the point above and to the left */
-                        qv[k][jp] = kmb_mul2(e0, G);
-                        qh[jp] = kmb_mul2(e1, G);
                     }
-                    /* dx, ddelta: sums over the 16 states (4 lanes) */
-                    float sx = sx2.x + sx2.y, sb = sb2.x + sb2.y;
+                    /* sums over the 16 states (4 lanes): dx = dt_bar sum G B,
+                     * the x-term of ddelta = x sum G B / 2 */
+                    float gb = gb2.x + gb2.y;
                     float s0 = s02.x + s02.y, s1 = s12.x + s12.y;
 #pragma unroll
                     for (int o = 1; o <= 2; o <<= 1) {
-                        sx += __shfl_xor_sync(kFull, sx, o);
-                        sb += __shfl_xor_sync(kFull, sb, o);
+                        gb += __shfl_xor_sync(kFull, gb, o);
                         s0 += __shfl_xor_sync(kFull, s0, o);
                         s1 += __shfl_xor_sync(kFull, s1, o);
                     }
+                    const float sx = dtb * gb, sb = xv * gb;
                     /* dB / dC: sums over the 8 channels, then 4 states into
                      * one lane for a 128-bit atomic */
                     float v8[8];
@@ -536,14 +575,14 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_bwd(S2D p) {
                     const float r3 = __shfl_down_sync(kFull, r1, 8);
                     const float r4 = __shfl_down_sync(kFull, r1, 12);
                     if (j < W) {
-                        const long pt = i * W + j;
                         if (q == 0) {
-                            dxb[pt * D + d] = sx;
-                            dd0b[pt * D + d] = s0 + sb / 2.0f;
-                            dd1b[pt * D + d] = s1 + sb / 2.0f;
+                            const long o = ox + k * D;
+                            dxb[o] = sx;
+                            dd0b[o] = s0 * KMB_LN2 + sb / 2.0f;
+                            dd1b[o] = s1 * KMB_LN2 + sb / 2.0f;
                         }
                         if ((c & 3) == 0 && qok) {
-                            float *dst = ((c >> 2) ? dCb : dBb) + pt * M + q * 4;
+                            float *dst = ((c >> 2) ? dCb : dBb) + obc + k * M;
                             atomicAdd(reinterpret_cast<float4 *>(dst), make_float4(r1, r2, r3, r4));
                         }
                     }
@@ -562,6 +601,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_bwd(S2D p) {
                     hc[k][1] = kmb_f2(v.z, v.w);
                 }
             }
+            if (n >= 0) slot = slot == kBRing - 1 ? 0 : slot + 1;
             __syncthreads();
         }
         kmb_cp_async_wait<0>();
