@@ -25,20 +25,26 @@ __device__ __forceinline__ float kmb_ex2(float x) {
  * A recurrence h_t = a_t h_{t-1} + ... with a_t close to 1 carries the
  * relative error of each a_t over ~1/|ln a_t| steps, so a per-step bias of
  * one ulp in a_t grows into a 1e-3 error on a weak-decay sequence.  Where
- * |w| < 1/16 (memory longer than ~23 steps) 2^w is therefore evaluated
- * with a degree-4 polynomial fitted here for minimax relative error on
- * [-1/16, 1/16] (iteratively reweighted least squares on Chebyshev nodes,
- * 8e-11 in real arithmetic; 0.54 ulp and no measurable bias in fp32).
- * Elsewhere the memory is short and MUFU ex2 (~2 ulp) is used.  Both
- * are evaluated and selected, so a warp never diverges.
+ * |w| < KMB_DECAY_POLY_MAX = 1/32 (memory longer than ~46 steps) 2^w is
+ * therefore evaluated with a degree-3 polynomial fitted for minimax
+ * relative error on [-1/32, 1/32] (iteratively reweighted least squares on
+ * Chebyshev nodes: 1.1e-9 in real arithmetic, 0.55 ulp and a mean relative
+ * error of 1e-9 in fp32 Horner form).  Elsewhere the memory is short and
+ * MUFU ex2 (~2 ulp) is used.
  */
+#define KMB_DECAY_POLY_MAX 0.03125f
+
+__device__ __forceinline__ float kmb_decay_poly(float w) {
+    float p = fmaf(0.05550280585885048f, w, 0.24023589491844177f);
+    p = fmaf(p, w, 0.6931471824645996f);
+    return fmaf(p, w, 1.0f);
+}
+
+/* Scalar decay: both evaluated and selected, so a warp never diverges. */
 __device__ __forceinline__ float kmb_exp2_decay(float w) {
     const float m = kmb_ex2(w);
-    float p = fmaf(0.009617380797863007f, w, 0.055510617792606354f);
-    p = fmaf(p, w, 0.24022650718688965f);
-    p = fmaf(p, w, 0.6931471824645996f);
-    p = fmaf(p, w, 1.0f);
-    return fabsf(w) < 0.0625f ? p : m;
+    const float p = kmb_decay_poly(w);
+    return fabsf(w) < KMB_DECAY_POLY_MAX ? p : m;
 }
 
 /* Packed fp32 pairs (sm_100 FFMA2 / FMUL2 / FADD2): two single-precision
@@ -52,15 +58,24 @@ __device__ __forceinline__ float2 kmb_fma2(float2 a, float2 b, float2 c) {
 __device__ __forceinline__ float2 kmb_mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
 __device__ __forceinline__ float2 kmb_add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
 
-/* kmb_exp2_decay of two values: the polynomial runs on pairs, MUFU ex2
- * and the selection per element; each element equals kmb_exp2_decay. */
-__device__ __forceinline__ float2 kmb_exp2_decay2(float2 w) {
-    const float mx = kmb_ex2(w.x), my = kmb_ex2(w.y);
-    float2 p = kmb_fma2(kmb_f2s(0.009617380797863007f), w, kmb_f2s(0.055510617792606354f));
-    p = kmb_fma2(p, w, kmb_f2s(0.24022650718688965f));
+/* MUFU ex2 of both elements of a pair. */
+__device__ __forceinline__ float2 kmb_ex2_2(float2 w) {
+    return make_float2(kmb_ex2(w.x), kmb_ex2(w.y));
+}
+
+/* Given m = kmb_ex2_2(w), the pair kmb_exp2_decay would give: the
+ * polynomial on FFMA2 pairs where |w| < KMB_DECAY_POLY_MAX, m elsewhere. */
+__device__ __forceinline__ float2 kmb_decay_fix2(float2 w, float2 m) {
+    float2 p = kmb_fma2(kmb_f2s(0.05550280585885048f), w, kmb_f2s(0.24023589491844177f));
     p = kmb_fma2(p, w, kmb_f2s(0.6931471824645996f));
     p = kmb_fma2(p, w, kmb_f2s(1.0f));
-    return kmb_f2(fabsf(w.x) < 0.0625f ? p.x : mx, fabsf(w.y) < 0.0625f ? p.y : my);
+    return kmb_f2(fabsf(w.x) < KMB_DECAY_POLY_MAX ? p.x : m.x,
+                  fabsf(w.y) < KMB_DECAY_POLY_MAX ? p.y : m.y);
+}
+
+/* kmb_exp2_decay of two values; each element equals kmb_exp2_decay. */
+__device__ __forceinline__ float2 kmb_exp2_decay2(float2 w) {
+    return kmb_decay_fix2(w, kmb_ex2_2(w));
 }
 
 /* Asynchronous global->shared copies (cp.async, sm_80+).  A source size
@@ -87,6 +102,46 @@ __device__ __forceinline__ void kmb_cp_async_commit() {
 template <int N>
 __device__ __forceinline__ void kmb_cp_async_wait() {
     asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+/*
+ * kmb_load_tile with a compile-time tile shape (ROWS x COLS): the element
+ * -> (row, column) split is a constant division, and the loop has a fixed
+ * trip count.
+ */
+template <int NT, int ROWS, int COLS>
+__device__ __forceinline__ void kmb_load_tile_c(float *s, int s_ld, const float *g, long g_ld,
+                                                int rows_valid, int cols_valid, bool vec,
+                                                int tid) {
+    if (vec) {
+        constexpr int C4 = (COLS + 3) >> 2;
+        constexpr int TOTAL = ROWS * C4;
+#pragma unroll
+        for (int i0 = 0; i0 < TOTAL; i0 += NT) {
+            const int i = i0 + tid;
+            if (TOTAL % NT == 0 || i < TOTAL) {
+                const int r = i / C4;
+                const int c = (i - r * C4) << 2;
+                int bytes = 0;
+                if (r < rows_valid) {
+                    const int left = cols_valid - c;
+                    bytes = left >= 4 ? 16 : (left > 0 ? left * 4 : 0);
+                }
+                const float *src = bytes ? g + (long)r * g_ld + c : g;
+                kmb_cp_async16(s + r * s_ld + c, src, bytes);
+            }
+        }
+    } else {
+        constexpr int TOTAL = ROWS * COLS;
+#pragma unroll 4
+        for (int i = tid; i < TOTAL; i += NT) {
+            const int r = i / COLS;
+            const int c = i - r * COLS;
+            const bool ok = (r < rows_valid) && (c < cols_valid);
+            const float *src = ok ? g + (long)r * g_ld + c : g;
+            kmb_cp_async4(s + r * s_ld + c, src, ok);
+        }
+    }
 }
 
 /*

@@ -188,14 +188,6 @@ __device__ __forceinline__ void stgv(float *dst, bool gok, int N, int n0, const 
     }
 }
 
-template <int G>
-__device__ __forceinline__ bool clamp_hitv(float hmax, const float (&h)[G]) {
-    bool nan = false;
-#pragma unroll
-    for (int j = 0; j < G; ++j) nan |= h[j] != h[j];
-    return !(hmax < 1000.f) || nan;
-}
-
 /* ------------------------------------------------------------------ */
 /* forward                                                             */
 /* ------------------------------------------------------------------ */
@@ -228,10 +220,12 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_fwd(Scan1DDev p) {
     const bool gok = n0 < N;
     const int dvalid = (int)min((long)DT, D - d0);
 
-    const int BWr = bc_row_stride(SHARED, G * P, N);
-    const int xs_sz = TT * DT;
-    const int bs_sz = TT * BWr;
-    const int stage_sz = 3 * xs_sz + 2 * bs_sz; /* x, dt, y, B, C */
+    /* shared-memory row of channel-shared B / C: bc_row_stride(true, G*P, N),
+     * which is G*P (at least 4) for every N the launcher maps to this P */
+    constexpr int BW = SHARED ? (G * P >= 4 ? G * P : 4) : 0;
+    constexpr int xs_sz = TT * DT;
+    constexpr int bs_sz = TT * BW;
+    constexpr int stage_sz = 3 * xs_sz + 2 * bs_sz; /* x, dt, y, B, C */
 
     float A2[G], h[G];
 #pragma unroll
@@ -248,8 +242,6 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_fwd(Scan1DDev p) {
     const long boff = SHARED ? b * L * N : (b * L * D + d0) * N;
     const float *Bg = p.B + boff;
     const float *Cg = p.C + boff;
-    const int bcols = SHARED ? BWr : DT * N; /* padded columns are zero-filled */
-    const int bvalid = SHARED ? N : dvalid * N;
     const bool vxd = p.vec_xd, vbc = p.vec_bc;
     float *const hall = p.h_all ? p.h_all + (b * L * D + d) * N + n0 : nullptr;
     float *const ckpt = p.ckpt ? p.ckpt + (b * p.nslots * D + d) * N + n0 : nullptr;
@@ -260,13 +252,14 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_fwd(Scan1DDev p) {
         float *st = smem + (k % ST) * stage_sz;
         const long t0 = (long)k * TT;
         const int rv = (int)min((long)TT, L - t0);
-        kmb_load_tile<kNT>(st, DT, xg + t0 * D, D, TT, DT, rv, dvalid, vxd, tid);
-        kmb_load_tile<kNT>(st + xs_sz, DT, dg + t0 * D, D, TT, DT, rv, dvalid, vxd, tid);
-        if (SHARED) {
-            kmb_load_tile<kNT>(st + 3 * xs_sz, BWr, Bg + t0 * bld, bld, TT, bcols, rv, bvalid,
-                               vbc, tid);
-            kmb_load_tile<kNT>(st + 3 * xs_sz + bs_sz, BWr, Cg + t0 * bld, bld, TT, bcols, rv,
-                               bvalid, vbc, tid);
+        kmb_load_tile_c<kNT, TT, DT>(st, DT, xg + t0 * D, D, rv, dvalid, vxd, tid);
+        kmb_load_tile_c<kNT, TT, DT>(st + xs_sz, DT, dg + t0 * D, D, rv, dvalid, vxd, tid);
+        if constexpr (SHARED) {
+            /* columns past N are zero-filled */
+            kmb_load_tile_c<kNT, TT, BW>(st + 3 * xs_sz, BW, Bg + t0 * bld, bld, rv, N, vbc,
+                                         tid);
+            kmb_load_tile_c<kNT, TT, BW>(st + 3 * xs_sz + bs_sz, BW, Cg + t0 * bld, bld, rv, N,
+                                         vbc, tid);
         }
     };
     /* coalesced store of the y tile of tile k (rows rv, channels dvalid) */
@@ -324,8 +317,8 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_fwd(Scan1DDev p) {
                 const float u = dv * xs[i * DT];
                 float bv[G], cv[G];
                 if (SHARED) {
-                    ldsv<G>(bs + i * BWr, bv);
-                    ldsv<G>(cs + i * BWr, cv);
+                    ldsv<G>(bs + i * BW, bv);
+                    ldsv<G>(cs + i * BW, cv);
                 } else {
                     ldgv<G, VEC>(bgl + (t0 + i) * hstride, gok && dok, N, dok ? n0 : N, bv);
                     ldgv<G, VEC>(cgl + (t0 + i) * hstride, gok && dok, N, dok ? n0 : N, cv);
@@ -349,14 +342,22 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_fwd(Scan1DDev p) {
         };
 
         if (rv == TT && !hall) {
-            /* fast path: no clamp on the critical path; the detector tracks
-             * max|h| and a flagged tile is replayed exactly from its start.
-             * Callers asking for the state history (h_all) take the exact
-             * per-step path below instead. */
+            /* fast path: no clamp on the critical path; a detector sums h^2
+             * over the tile (any |h| > 1000, or a NaN, pushes the sum to at
+             * least 1e6) and a flagged tile is replayed exactly from its
+             * start.  The tile is straight-line code: decays are
+             * kmb_exp2_decay2 (MUFU ex2 and the weak-decay polynomial,
+             * selected per element), because a warp-uniform branch per step
+             * that skips the polynomial splits the tile into blocks the
+             * scheduler cannot overlap and measured slower.  Callers asking
+             * for the state history (h_all) take the exact per-step path
+             * below instead. */
             float hst[G];
 #pragma unroll
             for (int j = 0; j < G; ++j) hst[j] = h[j];
-            float hmax = 0.f;
+            float2 sq[G / 2];
+#pragma unroll
+            for (int jp = 0; jp < G / 2; ++jp) sq[jp] = kmb_f2s(0.f);
 #pragma unroll
             for (int i0 = 0; i0 < TT; i0 += P) {
                 float yq[P];
@@ -367,22 +368,25 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_fwd(Scan1DDev p) {
                     const float u = dv * xs[i * DT];
                     float bv[G], cv[G];
                     if (SHARED) {
-                        ldsv<G>(bs + i * BWr, bv);
-                        ldsv<G>(cs + i * BWr, cv);
+                        ldsv<G>(bs + i * BW, bv);
+                        ldsv<G>(cs + i * BW, cv);
                     } else {
                         ldgv<G, VEC>(bgl + (t0 + i) * hstride, gok && dok, N, dok ? n0 : N, bv);
                         ldgv<G, VEC>(cgl + (t0 + i) * hstride, gok && dok, N, dok ? n0 : N, cv);
                     }
                     /* state pairs on FFMA2 / FMUL2 (same per-element rounding) */
                     const float2 dv2 = kmb_f2s(dv), u2 = kmb_f2s(u);
+                    float2 a[G / 2];
+#pragma unroll
+                    for (int jp = 0; jp < G / 2; ++jp)
+                        a[jp] = kmb_exp2_decay2(kmb_mul2(dv2, kmb_f2(A2[2 * jp], A2[2 * jp + 1])));
                     float2 y2 = kmb_f2s(0.f);
 #pragma unroll
                     for (int jp = 0; jp < G / 2; ++jp) {
                         const int j = 2 * jp;
-                        const float2 a = kmb_exp2_decay2(kmb_mul2(dv2, kmb_f2(A2[j], A2[j + 1])));
-                        const float2 hn = kmb_fma2(a, kmb_f2(h[j], h[j + 1]),
+                        const float2 hn = kmb_fma2(a[jp], kmb_f2(h[j], h[j + 1]),
                                                    kmb_mul2(kmb_f2(bv[j], bv[j + 1]), u2));
-                        if (CLAMP) hmax = fmaxf(hmax, fmaxf(fabsf(hn.x), fabsf(hn.y)));
+                        if (CLAMP) sq[jp] = kmb_fma2(hn, hn, sq[jp]);
                         h[j] = hn.x;
                         h[j + 1] = hn.y;
                         y2 = kmb_fma2(kmb_f2(cv[j], cv[j + 1]), hn, y2);
@@ -393,10 +397,15 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_fwd(Scan1DDev p) {
                 }
                 ys[(i0 + g) * DT] = rs_sum<P>(yq, lane);
             }
-            if (CLAMP && __any_sync(kFull, clamp_hitv<G>(hmax, h))) {
+            if (CLAMP) {
+                float ss = 0.f;
 #pragma unroll
-                for (int j = 0; j < G; ++j) h[j] = hst[j];
-                slow_tile(TT);
+                for (int jp = 0; jp < G / 2; ++jp) ss += sq[jp].x + sq[jp].y;
+                if (__any_sync(kFull, !(ss < 1e6f))) {
+#pragma unroll
+                    for (int j = 0; j < G; ++j) h[j] = hst[j];
+                    slow_tile(TT);
+                }
             }
         } else {
             slow_tile(rv);
@@ -472,11 +481,13 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
     const bool gok = n0 < N;
     const int dvalid = (int)min((long)DT, D - d0);
 
-    const int BWr = bc_row_stride(SHARED, NP, N);
-    const int xs_sz = T * DT;
-    const int bs_sz = T * BWr;
-    const int ck_sz = HALL ? 0 : DT * NP; /* checkpointed chunk-start states [DT][NP] */
-    const int stage_sz = 3 * xs_sz + 2 * bs_sz + ck_sz;
+    /* shared-memory row of channel-shared B / C: bc_row_stride(true, NP, N),
+     * which is NP for every N the launcher maps to this P */
+    constexpr int BW = SHARED ? NP : 0;
+    constexpr int xs_sz = T * DT;
+    constexpr int bs_sz = T * BW;
+    constexpr int ck_sz = HALL ? 0 : DT * NP; /* checkpointed chunk-start states [DT][NP] */
+    constexpr int stage_sz = 3 * xs_sz + 2 * bs_sz + ck_sz;
     /* per-thread dB / dC contributions of the chunk, [T][DT][NP] each
      * (SHARED only): thread (dl, g) writes 16 bytes at 16 * tid, so the
      * 128-bit stores are conflict-free; folded once per chunk */
@@ -504,8 +515,6 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
     const long boff = SHARED ? b * L * N : (b * L * D + d0) * N;
     const float *Bg = p.B + boff;
     const float *Cg = p.C + boff;
-    const int bcols = SHARED ? BWr : DT * N; /* padded columns are zero-filled */
-    const int bvalid = SHARED ? N : dvalid * N;
     const bool vxd = p.vec_xd, vbc = p.vec_bc;
     const long hstride = D * N;
     const float *hall = HALL ? p.h_all + (b * L * D + d) * N + n0 : nullptr;
@@ -515,21 +524,21 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
         float *st = smem + stage * stage_sz;
         const long t0 = (long)c * T;
         const int rv = (int)min((long)T, L - t0);
-        kmb_load_tile<kNT>(st, DT, xg + t0 * D, D, T, DT, rv, dvalid, vxd, tid);
-        kmb_load_tile<kNT>(st + xs_sz, DT, dg + t0 * D, D, T, DT, rv, dvalid, vxd, tid);
-        kmb_load_tile<kNT>(st + 2 * xs_sz, DT, yg + t0 * D, D, T, DT, rv, dvalid, vxd, tid);
-        if (SHARED) {
-            kmb_load_tile<kNT>(st + 3 * xs_sz, BWr, Bg + t0 * bld, bld, T, bcols, rv, bvalid,
-                               vbc, tid);
-            kmb_load_tile<kNT>(st + 3 * xs_sz + bs_sz, BWr, Cg + t0 * bld, bld, T, bcols, rv,
-                               bvalid, vbc, tid);
+        kmb_load_tile_c<kNT, T, DT>(st, DT, xg + t0 * D, D, rv, dvalid, vxd, tid);
+        kmb_load_tile_c<kNT, T, DT>(st + xs_sz, DT, dg + t0 * D, D, rv, dvalid, vxd, tid);
+        kmb_load_tile_c<kNT, T, DT>(st + 2 * xs_sz, DT, yg + t0 * D, D, rv, dvalid, vxd, tid);
+        if constexpr (SHARED) {
+            /* columns past N are zero-filled */
+            kmb_load_tile_c<kNT, T, BW>(st + 3 * xs_sz, BW, Bg + t0 * bld, bld, rv, N, vbc, tid);
+            kmb_load_tile_c<kNT, T, BW>(st + 3 * xs_sz + bs_sz, BW, Cg + t0 * bld, bld, rv, N,
+                                        vbc, tid);
         }
         if (!HALL && c > 0) {
             /* the forward's checkpoint of the state before this chunk: the
              * CTA's DT channels x N states are contiguous */
             const float *src = p.ckpt_in + ((b * p.nslots + c - 1) * D + d0) * N;
-            kmb_load_tile<kNT>(st + 3 * xs_sz + 2 * bs_sz, NP, src, N, DT, NP, dvalid, N,
-                               VEC, tid);
+            kmb_load_tile_c<kNT, DT, NP>(st + 3 * xs_sz + 2 * bs_sz, NP, src, N, dvalid, N, VEC,
+                                         tid);
         }
     };
 
@@ -604,42 +613,45 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
         constexpr bool FULL = SHARED && !HALL;
         {
             /* forward recompute of the chunk's states (registers).  Without
-             * the clamp on the critical path; when a state reaches the clamp
-             * bound (or NaN) the chunk is recomputed with the exact clamp, so
-             * the states match the forward's bit for bit either way. */
+             * the clamp on the critical path: a detector sums h^2 over the
+             * chunk (any |h| > 1000, or a NaN, pushes it to at least 1e6),
+             * and a flagged chunk is recomputed with the exact clamp, so the
+             * states match the forward's bit for bit either way.  Decays are
+             * kmb_exp2_decay2 (MUFU ex2 and the weak-decay polynomial,
+             * selected per element): a warp-uniform branch per step, as in
+             * the forward, costs registers that the chunk's states need. */
             float2 hr[HALL ? 1 : T][2]; /* states h_t of the chunk */
             float2 ar[HALL ? 1 : T][2]; /* decays a_t, reused by the reverse sweep */
             if (!HALL) {
                 auto recompute = [&](auto exact_tag) {
                     constexpr bool EXACT = decltype(exact_tag)::value;
                     float2 hh[2] = {hsp[0], hsp[1]};
-                    float hmax = 0.f;
+                    float2 sq = kmb_f2s(0.f);
 #pragma unroll
                     for (int i = 0; i < T; ++i) {
                         if (FULL || i < len) {
                             const float dv = ds[i * DT];
                             const float2 dv2 = kmb_f2s(dv), u2 = kmb_f2s(dv * xs[i * DT]);
-                            float2 bp[2];
-                            row_pairs(bs + i * BWr, bgl, t0 + i, bp);
+                            float2 bp[2], a[2];
+                            row_pairs(bs + i * BW, bgl, t0 + i, bp);
+#pragma unroll
+                            for (int jp = 0; jp < 2; ++jp) a[jp] = kmb_exp2_decay2(kmb_mul2(dv2, A2p[jp]));
 #pragma unroll
                             for (int jp = 0; jp < 2; ++jp) {
-                                const float2 a = kmb_exp2_decay2(kmb_mul2(dv2, A2p[jp]));
-                                float2 hn = kmb_fma2(a, hh[jp], kmb_mul2(bp[jp], u2));
+                                float2 hn = kmb_fma2(a[jp], hh[jp], kmb_mul2(bp[jp], u2));
                                 if (EXACT) {
                                     hn.x = clamp1000(hn.x);
                                     hn.y = clamp1000(hn.y);
                                 } else if (CLAMP) {
-                                    hmax = fmaxf(hmax, fmaxf(fabsf(hn.x), fabsf(hn.y)));
+                                    sq = kmb_fma2(hn, hn, sq);
                                 }
                                 hh[jp] = hn;
                                 hr[i][jp] = hn;
-                                ar[i][jp] = a;
+                                ar[i][jp] = a[jp];
                             }
                         }
                     }
-                    return CLAMP && !EXACT &&
-                           (!(hmax < 1000.f) || hh[0].x != hh[0].x || hh[0].y != hh[0].y ||
-                            hh[1].x != hh[1].x || hh[1].y != hh[1].y);
+                    return CLAMP && !EXACT && !(sq.x + sq.y < 1e6f);
                 };
                 if (__any_sync(kFull, recompute(std::false_type{})))
                     recompute(std::true_type{});
@@ -661,8 +673,8 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
                         const float2 dv2 = kmb_f2s(dv), dyv2 = kmb_f2s(dyv);
                         const float2 u2 = kmb_f2s(dv * xv);
                         float2 bp[2], cp[2], hp[2], ht[2];
-                        row_pairs(bs + i * BWr, bgl, t0 + i, bp);
-                        row_pairs(cs + i * BWr, cgl, t0 + i, cp);
+                        row_pairs(bs + i * BW, bgl, t0 + i, bp);
+                        row_pairs(cs + i * BW, cgl, t0 + i, cp);
                         if (HALL) {
                             float f[kG], q[kG];
                             if (dok) {
@@ -805,6 +817,303 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd(Scan1DDev p) {
     }
 }
 
+/*
+ * Backward for channel-shared B/C with 16-byte aligned rows (x / dt / dy
+ * rows of D floats, B / C rows of N floats, D and N multiples of 4): the
+ * arithmetic of k_scan1d_bwd (checkpointed chunk recompute, reverse sweep
+ * on state pairs) with the per-chunk bookkeeping reduced:
+ *
+ *  - staging: every 16-byte unit of a chunk's x, dt, dy, B, C rows and of
+ *    its checkpoint row is a fixed copy job; a thread's jobs (source at
+ *    chunk 0, destination in the stage, row, column bytes) are set up once,
+ *    so a chunk costs each thread NJ cp.async plus an address update;
+ *  - dx / ddt: each lane stores its partial (sum_n e B, sum_n A q h) to a
+ *    shared [T][DT][P] tile; after the sweep the CTA folds the P partials
+ *    of every (step, channel) and writes dx / ddt rows with coalesced
+ *    stores (no shuffles, no per-lane scattered stores);
+ *  - dB / dC: the shared-tile fold of k_scan1d_bwd, without per-channel
+ *    bounds checks when the CTA's channel tile is full.
+ */
+template <int P, bool CLAMP>
+__global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd_sh(Scan1DDev p) {
+    constexpr int DT = kNT / P;
+    constexpr int T = kChunk;
+    constexpr int NP = kG * P;
+    constexpr int XS = T * DT;  /* x / dt / dy tile [T][DT] */
+    constexpr int BS = T * NP;  /* B / C tile [T][NP] */
+    constexpr int CK = DT * NP; /* checkpointed chunk-start states [DT][NP] */
+    constexpr int STAGE = 3 * XS + 2 * BS + CK;
+    constexpr int UX = XS / 4, UB = BS / 4, UC = CK / 4;
+    constexpr int UTOT = 3 * UX + 2 * UB + UC;
+    constexpr int NJ = (UTOT + kNT - 1) / kNT;
+    static_assert(XS % 4 == 0 && DT % 4 == 0 && STAGE < 65536, "stage layout");
+    static_assert((2 * STAGE + 2 * T * DT * NP) % 4 == 0, "partX alignment");
+    extern __shared__ __align__(16) float smem[];
+    float *partB = smem + 2 * STAGE;    /* [T][DT][NP] dB contributions */
+    float *partC = partB + T * DT * NP; /* [T][DT][NP] dC contributions */
+    float2 *partX = reinterpret_cast<float2 *>(partC + T * DT * NP); /* [T][DT][P] */
+
+    const int tid = threadIdx.x;
+    const int g = tid % P;
+    const int dl = tid / P;
+    const int n0 = g * kG;
+    const long b = blockIdx.y;
+    const long D = p.D, L = p.L;
+    const int N = (int)p.N;
+    const long d0 = (long)blockIdx.x * DT;
+    const long d = d0 + dl;
+    const bool dok = d < D;
+    const int dvalid = (int)min((long)DT, D - d0);
+    const int nch = (int)((L + T - 1) / T);
+
+    /* copy jobs: info = dst (bits 0-15) | row (16-23) | column bytes
+     * (24-28) | kind (29-30: 0 x/dt/dy row, 1 B/C row, 2 checkpoint,
+     * 3 none); src is the source at chunk 0 (checkpoint: slot 0) */
+    const float *jsrc[NJ];
+    unsigned jinfo[NJ];
+#pragma unroll
+    for (int k = 0; k < NJ; ++k) {
+        const int e = tid + k * kNT;
+        const float *src = p.x;
+        unsigned info = 3u << 29;
+        auto cbytes = [](int left) { return left >= 4 ? 16 : (left > 0 ? 4 * left : 0); };
+        if (e < 3 * UX) {
+            const int arr = e / UX, u = e % UX;
+            const int r = u / (DT / 4), col = (u % (DT / 4)) * 4;
+            const float *base = arr == 0 ? p.x : (arr == 1 ? p.dt : p.dy);
+            const int cb = cbytes(dvalid - col);
+            if (cb) src = base + (b * L + r) * D + d0 + col;
+            info = (unsigned)(arr * XS + r * DT + col) | ((unsigned)r << 16) |
+                   ((unsigned)cb << 24) | (0u << 29);
+        } else if (e < 3 * UX + 2 * UB) {
+            const int u0 = e - 3 * UX;
+            const int arr = u0 / UB, u = u0 % UB;
+            const int r = u / (NP / 4), col = (u % (NP / 4)) * 4;
+            const int cb = cbytes(N - col);
+            if (cb) src = (arr ? p.C : p.B) + (b * L + r) * N + col;
+            info = (unsigned)(3 * XS + arr * BS + r * NP + col) | ((unsigned)r << 16) |
+                   ((unsigned)cb << 24) | (1u << 29);
+        } else if (e < UTOT) {
+            const int u = e - 3 * UX - 2 * UB;
+            const int r = u / (NP / 4), col = (u % (NP / 4)) * 4;
+            const int cb = r < dvalid ? cbytes(N - col) : 0;
+            if (cb) src = p.ckpt_in + ((b * p.nslots) * D + d0 + r) * N + col;
+            info = (unsigned)(3 * XS + 2 * BS + r * NP + col) | ((unsigned)cb << 24) | (2u << 29);
+        }
+        jsrc[k] = src;
+        jinfo[k] = info;
+    }
+    const long strideX = (long)T * D, strideB = (long)T * N, strideK = D * N;
+    auto load = [&](int c, int stage) {
+        float *st = smem + stage * STAGE;
+        const long t0 = (long)c * T;
+#pragma unroll
+        for (int k = 0; k < NJ; ++k) {
+            const unsigned info = jinfo[k];
+            const unsigned kind = info >> 29;
+            if (kind == 3u || (kind == 2u && c == 0)) continue;
+            const int row = (int)((info >> 16) & 0xffu);
+            int bytes = (int)((info >> 24) & 0x1fu);
+            if (kind != 2u && t0 + row >= L) bytes = 0;
+            const long off = kind == 0u ? (long)c * strideX
+                                        : (kind == 1u ? (long)c * strideB : (long)(c - 1) * strideK);
+            kmb_cp_async16(st + (info & 0xffffu), bytes ? jsrc[k] + off : p.x, bytes);
+        }
+    };
+
+    /* per-state values live as pairs: the FFMA2 / FMUL2 operands */
+    float2 A2p[2], Arp[2], gcp[2], dAp[2];
+#pragma unroll
+    for (int jp = 0; jp < 2; ++jp) {
+        const int j = n0 + 2 * jp;
+        const float a0 = (dok && j < N) ? __ldg(p.A + d * N + j) : 0.f;
+        const float a1 = (dok && j + 1 < N) ? __ldg(p.A + d * N + j + 1) : 0.f;
+        Arp[jp] = kmb_f2(a0, a1);
+        A2p[jp] = kmb_f2(a0 * KMB_LOG2E, a1 * KMB_LOG2E);
+        gcp[jp] = kmb_f2s(0.f);
+        dAp[jp] = kmb_f2s(0.f);
+    }
+
+    load(nch - 1, 0);
+    kmb_cp_async_commit();
+
+    for (int c = nch - 1, it = 0; c >= 0; --c, ++it) {
+        kmb_cp_async_wait<0>();
+        __syncthreads();
+        if (c > 0) load(c - 1, (it + 1) & 1);
+        kmb_cp_async_commit();
+
+        const float *st = smem + (it & 1) * STAGE;
+        const float *xs = st + dl;
+        const float *ds = st + XS + dl;
+        const float *dys = st + 2 * XS + dl;
+        const float *bs = st + 3 * XS + n0;
+        const float *cs = bs + BS;
+        const long t0 = (long)c * T;
+        const int len = (int)min((long)T, L - t0);
+
+        /* state before the chunk's first step */
+        float2 hsp[2];
+        if (c > 0) {
+            float hs[kG];
+            lds4u(st + 3 * XS + 2 * BS + dl * NP + n0, hs);
+            hsp[0] = kmb_f2(hs[0], hs[1]);
+            hsp[1] = kmb_f2(hs[2], hs[3]);
+        } else {
+            float hs[kG];
+#pragma unroll
+            for (int j = 0; j < kG; ++j)
+                hs[j] = (dok && n0 + j < N && p.h0) ? p.h0[(b * D + d) * N + n0 + j] : 0.f;
+            hsp[0] = kmb_f2(hs[0], hs[1]);
+            hsp[1] = kmb_f2(hs[2], hs[3]);
+        }
+
+        /* forward recompute of the chunk's states, as in k_scan1d_bwd.
+         * Steps past the end of the sequence (last chunk only) have
+         * zero-filled rows: dt = 0 gives a decay of exactly 1 and u = 0,
+         * so they are identity steps with zero gradient terms. */
+        float2 hr[T][2], ar[T][2];
+        auto recompute = [&](auto exact_tag) {
+            constexpr bool EXACT = decltype(exact_tag)::value;
+            float2 hh[2] = {hsp[0], hsp[1]};
+            float2 sq = kmb_f2s(0.f);
+#pragma unroll
+            for (int i = 0; i < T; ++i) {
+                const float dv = ds[i * DT];
+                const float2 dv2 = kmb_f2s(dv), u2 = kmb_f2s(dv * xs[i * DT]);
+                const float4 b4 = *reinterpret_cast<const float4 *>(bs + i * NP);
+                const float2 bp[2] = {kmb_f2(b4.x, b4.y), kmb_f2(b4.z, b4.w)};
+#pragma unroll
+                for (int jp = 0; jp < 2; ++jp) {
+                    const float2 a = kmb_exp2_decay2(kmb_mul2(dv2, A2p[jp]));
+                    float2 hn = kmb_fma2(a, hh[jp], kmb_mul2(bp[jp], u2));
+                    if (EXACT) {
+                        hn.x = clamp1000(hn.x);
+                        hn.y = clamp1000(hn.y);
+                    } else if (CLAMP) {
+                        sq = kmb_fma2(hn, hn, sq);
+                    }
+                    hh[jp] = hn;
+                    hr[i][jp] = hn;
+                    ar[i][jp] = a;
+                }
+            }
+            return CLAMP && !EXACT && !(sq.x + sq.y < 1e6f);
+        };
+        if (__any_sync(kFull, recompute(std::false_type{}))) recompute(std::true_type{});
+
+        /* reverse sweep */
+#pragma unroll
+        for (int i = T - 1; i >= 0; --i) {
+            const float xv = xs[i * DT];
+            const float dv = ds[i * DT];
+            const float dyv = dys[i * DT];
+            const float2 dv2 = kmb_f2s(dv), dyv2 = kmb_f2s(dyv);
+            const float2 u2 = kmb_f2s(dv * xv);
+            const float4 b4 = *reinterpret_cast<const float4 *>(bs + i * NP);
+            const float4 c4 = *reinterpret_cast<const float4 *>(cs + i * NP);
+            const float2 bp[2] = {kmb_f2(b4.x, b4.y), kmb_f2(b4.z, b4.w)};
+            const float2 cp[2] = {kmb_f2(c4.x, c4.y), kmb_f2(c4.z, c4.w)};
+            float2 dxs2 = kmb_f2s(0.f), dts2 = kmb_f2s(0.f), vb[2], vc[2];
+#pragma unroll
+            for (int jp = 0; jp < 2; ++jp) {
+                const float2 hp = i > 0 ? hr[i > 0 ? i - 1 : 0][jp] : hsp[jp];
+                const float2 ah = kmb_fma2(dyv2, cp[jp], gcp[jp]);
+                const float2 q = kmb_mul2(ah, ar[i][jp]);
+                const float2 qh = kmb_mul2(q, hp);
+                dAp[jp] = kmb_fma2(dv2, qh, dAp[jp]);
+                dts2 = kmb_fma2(Arp[jp], qh, dts2);
+                dxs2 = kmb_fma2(ah, bp[jp], dxs2);
+                vb[jp] = kmb_mul2(ah, u2);        /* dB contribution */
+                vc[jp] = kmb_mul2(dyv2, hr[i][jp]); /* dC contribution */
+                gcp[jp] = q;
+            }
+            partX[(i * DT + dl) * P + g] = kmb_f2(dxs2.x + dxs2.y, dts2.x + dts2.y);
+            const int o = (i * DT + dl) * NP + n0;
+            *reinterpret_cast<float4 *>(partB + o) = make_float4(vb[0].x, vb[0].y, vb[1].x, vb[1].y);
+            *reinterpret_cast<float4 *>(partC + o) = make_float4(vc[0].x, vc[0].y, vc[1].x, vc[1].y);
+        }
+        __syncthreads();
+
+        /* dx / ddt of the chunk: fold the P lane partials of each (step,
+         * channel); a warp writes consecutive channels of one step */
+#pragma unroll
+        for (int o = tid; o < T * DT; o += kNT) {
+            const int i = o / DT, dd = o % DT;
+            const float2 *src = partX + (i * DT + dd) * P;
+            float2 sum = src[0];
+#pragma unroll
+            for (int q = 1; q < P; ++q) sum = kmb_add2(sum, src[q]);
+            if (i < len && dd < dvalid) {
+                const long t = (b * L + t0 + i) * D + d0 + dd;
+                p.dx[t] = sum.x * st[XS + i * DT + dd];
+                p.ddt[t] = fmaf(st[i * DT + dd], sum.x, sum.y);
+            }
+        }
+
+        /* channel sums of the chunk's dB / dC: HR threads per 4-state
+         * output, each summing every HR-th channel, folded by shuffles; one
+         * 128-bit atomic per output and CTA */
+        {
+            constexpr int NQ = NP / 4;
+            constexpr int HR = NP >= 32 ? 1 : 32 / NP;
+            constexpr int OUTS = 2 * T * NQ;
+            constexpr int ITER = (OUTS * HR + kNT - 1) / kNT;
+            const bool full = dvalid == DT;
+#pragma unroll
+            for (int r = 0; r < ITER; ++r) {
+                const int e = r * kNT + tid;
+                const int o = e / HR, hh = e % HR;
+                const int arr = o / (T * NQ);
+                const int i = (o % (T * NQ)) / NQ;
+                const int q = o % NQ;
+                const bool live = o < OUTS && i < len && q * 4 < N;
+                float2 lo = kmb_f2s(0.f), hi = kmb_f2s(0.f);
+                if (live) {
+                    const float *src = (arr ? partC : partB) + i * DT * NP + q * 4;
+                    if (full) {
+#pragma unroll
+                        for (int k = 0; k < DT / HR; ++k) {
+                            const float4 t4 =
+                                *reinterpret_cast<const float4 *>(src + (k * HR + hh) * NP);
+                            lo = kmb_add2(lo, kmb_f2(t4.x, t4.y));
+                            hi = kmb_add2(hi, kmb_f2(t4.z, t4.w));
+                        }
+                    } else {
+                        for (int k = 0; k < DT / HR; ++k) {
+                            const int dlx = k * HR + hh;
+                            if (dlx < dvalid) {
+                                const float4 t4 = *reinterpret_cast<const float4 *>(src + dlx * NP);
+                                lo = kmb_add2(lo, kmb_f2(t4.x, t4.y));
+                                hi = kmb_add2(hi, kmb_f2(t4.z, t4.w));
+                            }
+                        }
+                    }
+                }
+#pragma unroll
+                for (int m = HR / 2; m > 0; m >>= 1) {
+                    lo.x += __shfl_xor_sync(kFull, lo.x, m);
+                    lo.y += __shfl_xor_sync(kFull, lo.y, m);
+                    hi.x += __shfl_xor_sync(kFull, hi.x, m);
+                    hi.y += __shfl_xor_sync(kFull, hi.y, m);
+                }
+                if (live && hh == 0) {
+                    float *dst = (arr ? p.dC : p.dB) + (b * L + t0 + i) * N + q * 4;
+                    atomicAdd(reinterpret_cast<float4 *>(dst), make_float4(lo.x, lo.y, hi.x, hi.y));
+                }
+            }
+        }
+    }
+    kmb_cp_async_wait<0>();
+
+    {
+        const float dAs[kG] = {dAp[0].x, dAp[0].y, dAp[1].x, dAp[1].y};
+#pragma unroll
+        for (int j = 0; j < kG; ++j)
+            if (dok && n0 + j < N) atomicAdd(p.dA + d * N + n0 + j, dAs[j]);
+    }
+}
+
 /* M = 1 backward with per-channel A/B/C and a per-step delta shared by all
  * channels (reference cpu/scan1d_backward.c:23-191).  One thread per
  * channel walks t downwards; ddelta[t] is a sum over channels. */
@@ -873,6 +1182,7 @@ template <int P, int G, bool SHARED, bool VEC, bool CLAMP>
 cudaError_t launch_fwd_t(const Scan1DDev &p, long batch, cudaStream_t s) {
     using Cfg = FwdCfg<P, SHARED>;
     const int BWr = bc_row_stride(SHARED, G * P, (int)p.N);
+    if (SHARED && BWr != (G * P >= 4 ? G * P : 4)) return cudaErrorInvalidValue;
     const size_t smem = sizeof(float) * Cfg::ST * (3 * Cfg::TT * Cfg::DT + 2 * Cfg::TT * BWr);
     auto kern = k_scan1d_fwd<P, G, SHARED, VEC, CLAMP>;
     if (smem > 48 * 1024) {
@@ -889,6 +1199,7 @@ template <int P, bool SHARED, bool VEC, bool HALL, bool CLAMP>
 cudaError_t launch_bwd_t(const Scan1DDev &p, long batch, cudaStream_t s) {
     constexpr int DT = kNT / P;
     const int BWr = bc_row_stride(SHARED, kG * P, (int)p.N);
+    if (SHARED && BWr != kG * P) return cudaErrorInvalidValue;
     const int ck = HALL ? 0 : DT * kG * P;
     size_t smem = sizeof(float) * 2 * (3 * kChunk * DT + 2 * kChunk * BWr + ck);
     if (SHARED) smem += sizeof(float) * 2 * kChunk * DT * (kG * P);
@@ -901,6 +1212,29 @@ cudaError_t launch_bwd_t(const Scan1DDev &p, long batch, cudaStream_t s) {
     dim3 grid((unsigned)((p.D + DT - 1) / DT), (unsigned)batch);
     kern<<<grid, kNT, smem, s>>>(p);
     return cudaGetLastError();
+}
+
+template <int P, bool CLAMP>
+cudaError_t launch_bwd_sh_t(const Scan1DDev &p, long batch, cudaStream_t s) {
+    constexpr int DT = kNT / P;
+    constexpr int NP = kG * P;
+    constexpr int STAGE = 3 * kChunk * DT + 2 * kChunk * NP + DT * NP;
+    const size_t smem = sizeof(float) * (2 * STAGE + 2 * kChunk * DT * NP) +
+                        sizeof(float2) * kChunk * DT * P;
+    auto kern = k_scan1d_bwd_sh<P, CLAMP>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    dim3 grid((unsigned)((p.D + DT - 1) / DT), (unsigned)batch);
+    kern<<<grid, kNT, smem, s>>>(p);
+    return cudaGetLastError();
+}
+
+template <int P>
+cudaError_t bwd_sh(const Scan1DDev &p, long batch, bool clamp, cudaStream_t s) {
+    return clamp ? launch_bwd_sh_t<P, true>(p, batch, s) : launch_bwd_sh_t<P, false>(p, batch, s);
 }
 
 template <int P, bool SHARED>
@@ -1013,6 +1347,20 @@ extern "C" int kmb_launch_scan1d_bwd(const KmbScan1D *a, const float *ckpt_in,
         if (e == cudaSuccess) e = cudaMemsetAsync(a->dC, 0, nb, s);
     }
     if (e != cudaSuccess) return kmb_cuda_fail(e, "scan1d backward memset");
+    /* channel-shared B/C, 16-byte rows and checkpoints: the lean kernel */
+    if (shared && !hall && p.vec_xd && p.vec_bc && ckpt_in && ((uintptr_t)ckpt_in & 15u) == 0 &&
+        P <= 32) {
+        switch (P) {
+        case 1: e = bwd_sh<1>(p, a->batch, clamp, s); break;
+        case 2: e = bwd_sh<2>(p, a->batch, clamp, s); break;
+        case 4: e = bwd_sh<4>(p, a->batch, clamp, s); break;
+        case 8: e = bwd_sh<8>(p, a->batch, clamp, s); break;
+        case 16: e = bwd_sh<16>(p, a->batch, clamp, s); break;
+        default: e = bwd_sh<32>(p, a->batch, clamp, s); break;
+        }
+        if (e != cudaSuccess) return kmb_cuda_fail(e, "scan1d backward launch");
+        return KMB_OK;
+    }
     switch (P) {
     case 1: e = bwd_p<1>(p, a->batch, shared, vec, hall, clamp, s); break;
     case 2: e = bwd_p<2>(p, a->batch, shared, vec, hall, clamp, s); break;

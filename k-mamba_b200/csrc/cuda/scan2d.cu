@@ -70,12 +70,14 @@ __device__ __forceinline__ float abs_min4(const float2 (&a)[2]) {
 }
 
 /* False only when every |w| = |delta A log2(e)| of the lane's states is at
- * least 1/16, i.e. no element takes the weak-decay polynomial: rounding is
- * monotonic, so |delta| amin >= 1/16 implies fl(|delta| |A_m|) >= 1/16 for
+ * least KMB_DECAY_POLY_MAX, i.e. no element takes the weak-decay polynomial:
+ * rounding is monotonic, so |delta| amin >= that bound implies
+ * fl(|delta| |A_m|) >= it for
  * every state m.  Lanes past the last state (`live` false) never count. */
 __device__ __forceinline__ bool weak_possible(float dv0, float dv1, float amin0, float amin1,
                                               bool live) {
-    return live && (fabsf(dv0) * amin0 < 0.0625f || fabsf(dv1) * amin1 < 0.0625f);
+    return live && (fabsf(dv0) * amin0 < KMB_DECAY_POLY_MAX ||
+                    fabsf(dv1) * amin1 < KMB_DECAY_POLY_MAX);
 }
 
 /* e = 2^w for the four state pairs of one point (both axes, two pairs
