@@ -866,58 +866,74 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd_sh(Scan1DDev p) {
     const int dvalid = (int)min((long)DT, D - d0);
     const int nch = (int)((L + T - 1) / T);
 
-    /* copy jobs: info = dst (bits 0-15) | row (16-23) | column bytes
-     * (24-28) | kind (29-30: 0 x/dt/dy row, 1 B/C row, 2 checkpoint,
-     * 3 none); src is the source at chunk 0 (checkpoint: slot 0) */
+    /* Copy jobs.  Every 16-byte unit of a stage is one job; thread tid
+     * runs jobs tid + k * kNT.  Per job: the source at the last chunk
+     * (row jobs) or at the last checkpoint slot, moved back by a fixed
+     * stride per chunk; the destination offset in the stage (bits 0-15),
+     * the row within the chunk (16-23, 255 for checkpoint jobs) and the
+     * bytes of the unit inside the tensor's columns (24-28).  Rows past
+     * the sequence exist only in the first chunk processed (the last one),
+     * so later chunks skip the row check. */
     const float *jsrc[NJ];
+    int jstr[NJ];
     unsigned jinfo[NJ];
+    const long clast = nch - 1;
 #pragma unroll
     for (int k = 0; k < NJ; ++k) {
         const int e = tid + k * kNT;
         const float *src = p.x;
-        unsigned info = 3u << 29;
+        unsigned info = 0;
+        int stride = 0;
         auto cbytes = [](int left) { return left >= 4 ? 16 : (left > 0 ? 4 * left : 0); };
         if (e < 3 * UX) {
             const int arr = e / UX, u = e % UX;
             const int r = u / (DT / 4), col = (u % (DT / 4)) * 4;
             const float *base = arr == 0 ? p.x : (arr == 1 ? p.dt : p.dy);
             const int cb = cbytes(dvalid - col);
-            if (cb) src = base + (b * L + r) * D + d0 + col;
-            info = (unsigned)(arr * XS + r * DT + col) | ((unsigned)r << 16) |
-                   ((unsigned)cb << 24) | (0u << 29);
+            src = base + (b * L + clast * T + r) * D + d0 + col;
+            stride = T * (int)D;
+            info = (unsigned)(arr * XS + r * DT + col) | ((unsigned)r << 16) | ((unsigned)cb << 24);
         } else if (e < 3 * UX + 2 * UB) {
             const int u0 = e - 3 * UX;
             const int arr = u0 / UB, u = u0 % UB;
             const int r = u / (NP / 4), col = (u % (NP / 4)) * 4;
             const int cb = cbytes(N - col);
-            if (cb) src = (arr ? p.C : p.B) + (b * L + r) * N + col;
+            src = (arr ? p.C : p.B) + (b * L + clast * T + r) * N + col;
+            stride = T * N;
             info = (unsigned)(3 * XS + arr * BS + r * NP + col) | ((unsigned)r << 16) |
-                   ((unsigned)cb << 24) | (1u << 29);
+                   ((unsigned)cb << 24);
         } else if (e < UTOT) {
             const int u = e - 3 * UX - 2 * UB;
             const int r = u / (NP / 4), col = (u % (NP / 4)) * 4;
             const int cb = r < dvalid ? cbytes(N - col) : 0;
-            if (cb) src = p.ckpt_in + ((b * p.nslots) * D + d0 + r) * N + col;
-            info = (unsigned)(3 * XS + 2 * BS + r * NP + col) | ((unsigned)cb << 24) | (2u << 29);
+            /* chunk c reads slot c - 1; the first chunk with a checkpoint
+             * is nch - 1 */
+            src = p.ckpt_in + ((b * p.nslots + (clast > 0 ? clast - 1 : 0)) * D + d0 + r) * N + col;
+            stride = (int)(D * N);
+            info = (unsigned)(3 * XS + 2 * BS + r * NP + col) | (255u << 16) | ((unsigned)cb << 24);
         }
         jsrc[k] = src;
+        jstr[k] = stride;
         jinfo[k] = info;
     }
-    const long strideX = (long)T * D, strideB = (long)T * N, strideK = D * N;
-    auto load = [&](int c, int stage) {
+    /* issue the copies of chunk c (chunks are loaded from the last one
+     * down, once each) and move every job one chunk back */
+    auto load = [&](int c, int stage, bool first) {
         float *st = smem + stage * STAGE;
-        const long t0 = (long)c * T;
 #pragma unroll
         for (int k = 0; k < NJ; ++k) {
-            const unsigned info = jinfo[k];
-            const unsigned kind = info >> 29;
-            if (kind == 3u || (kind == 2u && c == 0)) continue;
-            const int row = (int)((info >> 16) & 0xffu);
-            int bytes = (int)((info >> 24) & 0x1fu);
-            if (kind != 2u && t0 + row >= L) bytes = 0;
-            const long off = kind == 0u ? (long)c * strideX
-                                        : (kind == 1u ? (long)c * strideB : (long)(c - 1) * strideK);
-            kmb_cp_async16(st + (info & 0xffffu), bytes ? jsrc[k] + off : p.x, bytes);
+            if (tid + k * kNT < UTOT) {
+                const unsigned info = jinfo[k];
+                const unsigned row = (info >> 16) & 0xffu;
+                int bytes = (int)(info >> 24);
+                if (row == 255u) {
+                    if (c == 0) continue; /* no checkpoint before chunk 0 */
+                } else if (first && (long)c * T + row >= L) {
+                    bytes = 0;
+                }
+                kmb_cp_async16(st + (info & 0xffffu), bytes ? jsrc[k] : p.x, bytes);
+                if (row != 255u || c > 1) jsrc[k] -= jstr[k];
+            }
         }
     };
 
@@ -934,13 +950,20 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd_sh(Scan1DDev p) {
         dAp[jp] = kmb_f2s(0.f);
     }
 
-    load(nch - 1, 0);
+    load(nch - 1, 0, true);
     kmb_cp_async_commit();
+
+    /* dx / ddt rows this thread writes (see the fold below): outputs
+     * o = tid + r kNT of a chunk are (step o / DT, channel o % DT) */
+    constexpr int NXO = (T * DT + kNT - 1) / kNT;
+    const int xdd = tid % DT;
+    const bool xok = xdd < dvalid;
+    long xoff = (b * L + clast * T + tid / DT) * D + d0 + xdd;
 
     for (int c = nch - 1, it = 0; c >= 0; --c, ++it) {
         kmb_cp_async_wait<0>();
         __syncthreads();
-        if (c > 0) load(c - 1, (it + 1) & 1);
+        if (c > 0) load(c - 1, (it + 1) & 1, false);
         kmb_cp_async_commit();
 
         const float *st = smem + (it & 1) * STAGE;
@@ -1038,18 +1061,22 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd_sh(Scan1DDev p) {
         /* dx / ddt of the chunk: fold the P lane partials of each (step,
          * channel); a warp writes consecutive channels of one step */
 #pragma unroll
-        for (int o = tid; o < T * DT; o += kNT) {
-            const int i = o / DT, dd = o % DT;
-            const float2 *src = partX + (i * DT + dd) * P;
-            float2 sum = src[0];
+        for (int r = 0; r < NXO; ++r) {
+            const int o = tid + r * kNT;
+            if ((T * DT) % kNT == 0 || o < T * DT) {
+                const int i = o / DT;
+                const float2 *src = partX + o * P;
+                float2 sum = src[0];
 #pragma unroll
-            for (int q = 1; q < P; ++q) sum = kmb_add2(sum, src[q]);
-            if (i < len && dd < dvalid) {
-                const long t = (b * L + t0 + i) * D + d0 + dd;
-                p.dx[t] = sum.x * st[XS + i * DT + dd];
-                p.ddt[t] = fmaf(st[i * DT + dd], sum.x, sum.y);
+                for (int q = 1; q < P; ++q) sum = kmb_add2(sum, src[q]);
+                if (xok && i < len) {
+                    const long t = xoff + (long)(r * (kNT / DT)) * D;
+                    p.dx[t] = sum.x * st[XS + o];
+                    p.ddt[t] = fmaf(st[o], sum.x, sum.y);
+                }
             }
         }
+        xoff -= (long)T * D;
 
         /* channel sums of the chunk's dB / dC: HR threads per 4-state
          * output, each summing every HR-th channel, folded by shuffles; one
@@ -1349,7 +1376,7 @@ extern "C" int kmb_launch_scan1d_bwd(const KmbScan1D *a, const float *ckpt_in,
     if (e != cudaSuccess) return kmb_cuda_fail(e, "scan1d backward memset");
     /* channel-shared B/C, 16-byte rows and checkpoints: the lean kernel */
     if (shared && !hall && p.vec_xd && p.vec_bc && ckpt_in && ((uintptr_t)ckpt_in & 15u) == 0 &&
-        P <= 32) {
+        P <= 32 && a->D * a->N < (1L << 31) && kChunk * a->D < (1L << 31)) {
         switch (P) {
         case 1: e = bwd_sh<1>(p, a->batch, clamp, s); break;
         case 2: e = bwd_sh<2>(p, a->batch, clamp, s); break;
