@@ -201,6 +201,42 @@ def test_batched_fwd_bwd_vs_oracle(lib, cuda, oracle, bsz, L, D, N, shared):
         assert rel_err(g[k], g_r[k]) <= TOL, k
 
 
+@pytest.mark.parametrize("case", ["weak", "clamp"])
+@pytest.mark.parametrize("shared", [True, False])
+def test_decay_regime_switches_vs_oracle(lib, cuda, oracle, shared, case):
+    """Sequences that move between strong decays (MUFU ex2 alone) and
+    windows of weak decays (|dt A log2 e| < 2^-8: the polynomial path,
+    entered by replaying a tile or chunk and then predicted for the next
+    ones), with a few channels weak throughout; or ("clamp") a burst that
+    drives states past the +-1000 clamp (the exact path) between strong
+    steps."""
+    rng = np.random.default_rng(77 if case == "weak" else 78)
+    bsz, L, D, N = 2, 520, 48, 16
+    x = rng.normal(0, 1, (bsz, L, D)).astype(f32)
+    dt = np.log1p(np.exp(rng.normal(0, 1, (bsz, L, D)) - 2)).astype(f32)
+    if case == "weak":
+        dt[:, 96:200] *= 1e-3
+        dt[1, 330:337] *= 1e-4
+        dt[:, :, 5:7] = rng.uniform(1e-5, 1e-3, (bsz, L, 2)).astype(f32)
+    else:
+        x[0, 410:414, 20:30] *= 5e4
+    A = (-np.exp(rng.uniform(0, np.log(16), (D, N)))).astype(f32)
+    bs = (bsz, L, N) if shared else (bsz, L, D, N)
+    B = rng.normal(0, 1, bs).astype(f32)
+    Cm = rng.normal(0, 1, bs).astype(f32)
+    dy = rng.normal(0, 1, (bsz, L, D)).astype(f32)
+    y, hl, g = run_batched(lib, x, A, B, Cm, dt, dy, shared)
+    y_r, hl_r, g_r = oracle_batched(oracle, x, A, B, Cm, dt, dy, shared)
+    if case == "clamp":
+        assert np.max(np.abs(hl_r)) > 0 and np.any(np.abs(y_r) > 1e3)
+    for b in range(bsz):
+        assert rel_err(y[b], y_r[b]) <= TOL, b
+        assert rel_err(hl[b], hl_r[b]) <= TOL, b
+        for k in ("dx", "ddt", "dB", "dC"):
+            assert rel_err(g[k][b], g_r[k][b]) <= TOL, (b, k)
+    assert rel_err(g["dA"], g_r["dA"]) <= TOL
+
+
 @pytest.mark.parametrize("mode", ["ckpt", "internal", "h_all"])
 def test_backward_state_sources_agree(lib, cuda, oracle, mode):
     rng = np.random.default_rng(5)
