@@ -607,7 +607,8 @@ def main():
         lib.kmb_set_sync(0)
 
     pk, pk_kind = peaks()
-    dom_ms, dom_bytes, dom_name = ((bwd_ms, BWD_BYTES, "k_scan1d_bwd") if bwd_ms >= fwd_ms
+    # config 2 (channel-shared B/C, 16-byte rows) runs k_scan1d_fwd and k_scan1d_bwd_sh
+    dom_ms, dom_bytes, dom_name = ((bwd_ms, BWD_BYTES, "k_scan1d_bwd_sh") if bwd_ms >= fwd_ms
                                    else (fwd_ms, FWD_BYTES, "k_scan1d_fwd"))
     achieved = dom_bytes / (dom_ms / 1e3) / 1e9
     tr = traffic_from_profile()
@@ -618,7 +619,7 @@ def main():
     line = None
     if rank == 0:
         cpu = None
-        if not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline:
             nth = cpu_threads()
             per = 64
             secs, nch, kind = cpu_reference_sample(nth, per)

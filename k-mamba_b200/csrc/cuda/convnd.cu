@@ -22,7 +22,7 @@
  *
  *  - streamed rows (D a multiple of 64, K <= 3, 16-byte aligned tensors;
  *    the config-3 shape): a CTA covers 64 channels x 16 columns of a
- *    128-row strip; whole rows with their column halo are copied by
+ *    128-row (forward) or 256-row (backward) strip; whole rows with their column halo are copied by
  *    cp.async into a shared ring several rows ahead of the compute (deep
  *    enough to cover HBM latency at one CTA per SM), and each row reads
  *    only its new K values per tensor from shared memory;
@@ -278,25 +278,39 @@ __global__ void __launch_bounds__(kThreads2d) k_conv2d_bwd(ConvDev p, Geo2d g) {
 /* ------------------------------------------------------------------ */
 
 /*
- * Backward for 4-aligned channels (the config-3 shape), bound by HBM: one
- * read of dy and input and one write of dinput.  A CTA covers R2_CG float4
- * channel groups x R2_TJ columns of a strip of R2_TI rows and walks the
- * strip downwards.  "Stage" m carries dy row rend+K-2-m and input row
- * rend-1-m, each R2_TJ + 2(K-1) columns wide (the column halo, zero-filled
+ * Backward for 64-channel tiles (D a multiple of 64: the config-3 shape),
+ * bound by HBM: one read of dy and input and one write of dinput.  A CTA
+ * of R2B_NT threads covers 64 channels as R2B_CG groups of R2B_CW channels
+ * (a thread's float4) x R2B_TJ columns of a strip of R2B_TI rows and walks
+ * the strip downwards.  "Stage" m carries dy row rend+K-2-m and input row
+ * rend-1-m, each R2B_TJ + 2(K-1) columns wide (the column halo, zero-filled
  * outside the grid); row r = rend-1-n needs stages n .. n+K-1.  Stages are
- * copied by cp.async into a ring of r2_nr<K>() shared rows, R2_PD stages
- * ahead of the compute, so about 60 KB per SM is in flight.  A thread's
- * K x K windows live in registers indexed by stage % K (the row loop is
- * unrolled by K, so no window shifts) and only the new stage's K values
- * per tensor come from shared memory each row.  Rows n .. n+K-1 share one
- * cp.async wait and one barrier; a fast thread then issues stages
- * n+PD .. n+PD+K-1 while a slow one may still read stage n-1, so the ring
- * holds R2_PD + K + 1 rows.
+ * copied by cp.async (16-byte units) into a ring of r2b_nr<K>() shared
+ * rows, R2B_PD stages ahead of the compute.  A thread's K x K windows live
+ * in registers indexed by stage % K (the row loop is unrolled by K, so no
+ * window shifts) and only the new stage's K values per tensor come from
+ * shared memory each row.  Rows n .. n+K-1 share one cp.async wait and one
+ * barrier; a fast thread then issues stages n+PD .. n+PD+K-1 while a slow
+ * one may still read stage n-1, so the ring holds R2B_PD + K + 1 rows.
+ *
+ * Tuning, config 3 on one B200 (backward, % of the measured copy
+ * bandwidth): float4 channels, 256 threads, 6 stages, 256-row strips and
+ * a register budget of one CTA per SM (196 registers) 76.7 %; the same
+ * with 128-row strips 75.2 %, with 8 or 10 stages 76.1 / 76.6 %; float2
+ * channel pairs (110 registers, 16 warps per SM) 72-74.7 %; the earlier
+ * 182-register build 68.7 %.
  */
-constexpr int R2_CG = 16;                 /* float4 channel groups per CTA */
-constexpr int R2_TJ = kThreads2d / R2_CG; /* columns per CTA */
+constexpr int R2_CG = 16;                 /* float4 channel groups per CTA (forward) */
+constexpr int R2_TJ = kThreads2d / R2_CG; /* columns per CTA (forward) */
 constexpr int R2_TI = 128;                /* rows per strip */
 constexpr int R2_PD = 6;                  /* stages in flight */
+constexpr int R2B_PD = 6;                  /* stages in flight */
+constexpr int R2B_TI = 256;                /* rows per strip */
+constexpr int R2B_CW = 4;                  /* channels per thread (a float4) */
+constexpr int R2B_NT = 256;                /* threads per CTA */
+constexpr int R2B_CG = 64 / R2B_CW;        /* channel groups per CTA */
+constexpr int R2B_TJ = R2B_NT / R2B_CG;    /* columns per CTA */
+using R2BVec = Vec4p;
 
 /* ring rows: a fast thread issues stages n+PD .. n+PD+K-1 of its row group
  * while a slow one may still read stage n-1 of the previous group */
@@ -304,42 +318,47 @@ template <int K>
 __host__ __device__ constexpr int r2_nr() { return R2_PD + K + 1; }
 
 template <int K>
-__host__ __device__ constexpr int r2_ws() { return R2_TJ + 2 * (K - 1); }
+__host__ __device__ constexpr int r2b_ws() { return R2B_TJ + 2 * (K - 1); }
+
+template <int K>
+__host__ __device__ constexpr int r2b_nr() { return R2B_PD + K + 1; }
 
 template <int K>
 __host__ __device__ constexpr size_t r2_smem_bytes() {
-    /* two rings of r2_nr rows; the final fold reuses the same space */
-    const size_t ring = 2ull * r2_nr<K>() * r2_ws<K>() * R2_CG * 16;
-    const size_t fold = (size_t)kThreads2d * (K * K + 1) * 16;
+    /* two rings of r2b_nr rows of 64 channels; the final fold reuses them */
+    const size_t ring = 2ull * r2b_nr<K>() * r2b_ws<K>() * 64 * 4;
+    const size_t fold = (size_t)R2B_NT * (K * K + 1) * R2B_CW * 4;
     return ring > fold ? ring : fold;
 }
 
 template <int K>
-__global__ void __launch_bounds__(kThreads2d) k_conv2d_bwd_ring(ConvDev p, long ctiles,
-                                                                long jtiles, long strips) {
-    using V = Vec4p;
-    using T = float4;
-    constexpr int WS = r2_ws<K>();
-    constexpr int NR = r2_nr<K>();
-    constexpr int ROWF = WS * R2_CG * 4; /* floats per ring row */
+__global__ void __launch_bounds__(R2B_NT, 1) k_conv2d_bwd_ring(ConvDev p, long ctiles,
+                                                               long jtiles, long strips) {
+    using V = R2BVec;
+    using T = typename V::T;
+    constexpr int CW = R2B_CW, CG = R2B_CG, TJ = R2B_TJ, NT = R2B_NT;
+    constexpr int WS = r2b_ws<K>();
+    constexpr int NR = r2b_nr<K>();
+    constexpr int ROWF = WS * 64; /* floats per ring row */
     constexpr int NACC = K * K + 1;
-    constexpr int CPT = (WS * R2_CG + kThreads2d - 1) / kThreads2d; /* copies per thread */
+    constexpr int UNITS = WS * 16;                   /* 16-byte copies per row */
+    constexpr int CPT = (UNITS + NT - 1) / NT;       /* copies per thread */
     extern __shared__ __align__(16) float sm[];
-    float *ring_g = sm;               /* dy rows   [NR][WS][R2_CG][4] */
-    float *ring_i = sm + NR * ROWF;   /* input rows */
+    float *ring_g = sm;             /* dy rows   [NR][WS][64] */
+    float *ring_i = sm + NR * ROWF; /* input rows */
 
     const int tid = threadIdx.x;
-    const int cg = tid % R2_CG;
-    const int jj = tid / R2_CG;
+    const int cg = tid % CG;
+    const int jj = tid / CG;
     const long H = p.dims[0], W = p.dims[1], D = p.D;
     const long ct = blockIdx.x % ctiles;
     const long jt = blockIdx.x / ctiles;
-    const long c0 = ct * R2_CG * 4;
-    const long j0 = jt * R2_TJ;
+    const long c0 = ct * 64;
+    const long j0 = jt * TJ;
     const long j = j0 + jj;
     const long b = blockIdx.z;
-    const long r0 = (long)blockIdx.y * R2_TI;
-    const long rend = min(H, r0 + R2_TI);
+    const long r0 = (long)blockIdx.y * R2B_TI;
+    const long rend = min(H, r0 + R2B_TI);
     const int cnt = (int)(rend - r0);       /* rows of this strip */
     const int nstage = cnt + K - 1;
     const long jlo = j0 - (K - 1);
@@ -347,16 +366,16 @@ __global__ void __launch_bounds__(kThreads2d) k_conv2d_bwd_ring(ConvDev p, long 
     const float *gbase = p.dy + b * H * W * D + c0;
     const float *ibase = p.in + b * H * W * D + c0;
 
-    /* this thread's copies of a stage: ring element e = tid + c * kThreads2d
-     * (column jlo + e / R2_CG, channel group e % R2_CG); only the row moves */
+    /* this thread's copies of a stage: unit e = tid + c * NT of a row
+     * (column jlo + e / 16, channels 4 (e % 16) ..); only the row moves */
     long coff[CPT];
     bool cok[CPT];
 #pragma unroll
     for (int c = 0; c < CPT; ++c) {
-        const int e = tid + c * kThreads2d;
-        const long col = jlo + e / R2_CG;
-        cok[c] = e < WS * R2_CG && col >= 0 && col < W;
-        coff[c] = col * D + (e % R2_CG) * 4;
+        const int e = tid + c * NT;
+        const long col = jlo + e / 16;
+        cok[c] = e < UNITS && col >= 0 && col < W;
+        coff[c] = col * D + (e % 16) * 4;
     }
     const long rowst = W * D;
     auto issue = [&](int m) {
@@ -367,13 +386,11 @@ __global__ void __launch_bounds__(kThreads2d) k_conv2d_bwd_ring(ConvDev p, long 
             const float *sg = gbase + rg * rowst, *si = ibase + ri * rowst;
 #pragma unroll
             for (int c = 0; c < CPT; ++c) {
-                if (tid + c * kThreads2d < WS * R2_CG) {
+                if (UNITS % NT == 0 || tid + c * NT < UNITS) {
                     const bool gok = cok[c] && rg < H;
                     const bool iok = cok[c] && ri >= 0;
-                    kmb_cp_async16(dg + c * kThreads2d * 4, gok ? sg + coff[c] : gbase,
-                                   gok ? 16 : 0);
-                    kmb_cp_async16(di + c * kThreads2d * 4, iok ? si + coff[c] : ibase,
-                                   iok ? 16 : 0);
+                    kmb_cp_async16(dg + c * NT * 4, gok ? sg + coff[c] : gbase, gok ? 16 : 0);
+                    kmb_cp_async16(di + c * NT * 4, iok ? si + coff[c] : ibase, iok ? 16 : 0);
                 }
             }
         }
@@ -382,7 +399,7 @@ __global__ void __launch_bounds__(kThreads2d) k_conv2d_bwd_ring(ConvDev p, long 
 
     T wk[K * K];
 #pragma unroll
-    for (int k = 0; k < K * K; ++k) wk[k] = V::load(p.ker + k * D + c0 + cg * 4);
+    for (int k = 0; k < K * K; ++k) wk[k] = V::load(p.ker + k * D + c0 + cg * CW);
     T acc[NACC];
 #pragma unroll
     for (int k = 0; k < NACC; ++k) acc[k] = V::zero();
@@ -392,24 +409,24 @@ __global__ void __launch_bounds__(kThreads2d) k_conv2d_bwd_ring(ConvDev p, long 
      * (columns j-K+1 .. j) of this thread */
     auto fetch = [&](int m, T (&g)[K], T (&iv)[K]) {
         const int slot = m % NR;
-        const float *sg = ring_g + slot * ROWF + (jj * R2_CG + cg) * 4;
-        const float *si = ring_i + slot * ROWF + (jj * R2_CG + cg) * 4;
+        const float *sg = ring_g + slot * ROWF + jj * 64 + cg * CW;
+        const float *si = ring_i + slot * ROWF + jj * 64 + cg * CW;
 #pragma unroll
         for (int q = 0; q < K; ++q) {
-            g[q] = *reinterpret_cast<const T *>(sg + (K - 1 + q) * R2_CG * 4);
-            iv[q] = *reinterpret_cast<const T *>(si + q * R2_CG * 4);
+            g[q] = *reinterpret_cast<const T *>(sg + (K - 1 + q) * 64);
+            iv[q] = *reinterpret_cast<const T *>(si + q * 64);
         }
     };
 
 #pragma unroll 1
-    for (int m = 0; m < R2_PD; ++m) issue(m);
+    for (int m = 0; m < R2B_PD; ++m) issue(m);
     /* stages 0 .. K-2 into the register windows */
-    kmb_cp_async_wait<R2_PD - (K - 1)>();
+    kmb_cp_async_wait<R2B_PD - (K - 1)>();
     __syncthreads();
 #pragma unroll
     for (int m = 0; m < K - 1; ++m) fetch(m, gw[m % K], iw[m % K]);
 
-    float *dbase = p.din + b * H * W * D + c0 + cg * 4;
+    float *dbase = p.din + b * H * W * D + c0 + cg * CW;
     /* one row at compile-time phase PH = n % K (its stages are resident) */
     auto row = [&](int n, auto ph_tag) {
         constexpr int PH = decltype(ph_tag)::value;
@@ -441,8 +458,8 @@ __global__ void __launch_bounds__(kThreads2d) k_conv2d_bwd_ring(ConvDev p, long 
      * n+K-1 .. n+2K-2, and stages n+PD .. n+PD+K-1 go out first */
     for (int n = 0; n < cnt; n += K) {
 #pragma unroll
-        for (int i = 0; i < K; ++i) issue(n + R2_PD + i);
-        kmb_cp_async_wait<R2_PD - K + 1>();
+        for (int i = 0; i < K; ++i) issue(n + R2B_PD + i);
+        kmb_cp_async_wait<R2B_PD - K + 1>();
         __syncthreads();
         row(n, std::integral_constant<int, 0>{});
         if (K > 1 && n + 1 < cnt) row(n + 1, std::integral_constant<int, 1 % K>{});
@@ -454,18 +471,18 @@ __global__ void __launch_bounds__(kThreads2d) k_conv2d_bwd_ring(ConvDev p, long 
     /* the ring is reused for the fold: no copy may still be in flight */
     kmb_cp_async_wait<0>();
     __syncthreads();
-    float *red = sm; /* [kThreads2d][NACC][4] */
+    float *red = sm; /* [NT][NACC][CW] */
 #pragma unroll
     for (int k = 0; k < NACC; ++k)
-        *reinterpret_cast<T *>(red + (tid * NACC + k) * 4) = act ? acc[k] : V::zero();
+        *reinterpret_cast<T *>(red + (tid * NACC + k) * CW) = act ? acc[k] : V::zero();
     __syncthreads();
-    for (int o = tid; o < R2_CG * NACC * 4; o += kThreads2d) {
-        const int i = o % 4;
-        const int k = (o / 4) % NACC;
-        const int cgo = o / (4 * NACC);
-        const long cc = c0 + cgo * 4 + i;
+    for (int o = tid; o < CG * NACC * CW; o += NT) {
+        const int i = o % CW;
+        const int k = (o / CW) % NACC;
+        const int cgo = o / (CW * NACC);
+        const long cc = c0 + cgo * CW + i;
         float s = 0.f;
-        for (int q = 0; q < R2_TJ; ++q) s += red[((q * R2_CG + cgo) * NACC + k) * 4 + i];
+        for (int q = 0; q < TJ; ++q) s += red[((q * CG + cgo) * NACC + k) * CW + i];
         if (k < K * K) atomicAdd(p.dker + (long)k * D + cc, s);
         else if (p.dbias) atomicAdd(p.dbias + cc, s);
     }
@@ -473,16 +490,16 @@ __global__ void __launch_bounds__(kThreads2d) k_conv2d_bwd_ring(ConvDev p, long 
 
 template <int K>
 cudaError_t launch2d_bwd_ring(const ConvDev &p, cudaStream_t s) {
-    const long ctiles = p.D / (4 * R2_CG);
-    const long jtiles = (p.dims[1] + R2_TJ - 1) / R2_TJ;
-    const long strips = (p.dims[0] + R2_TI - 1) / R2_TI;
+    const long ctiles = p.D / 64;
+    const long jtiles = (p.dims[1] + R2B_TJ - 1) / R2B_TJ;
+    const long strips = (p.dims[0] + R2B_TI - 1) / R2B_TI;
     const size_t smem = r2_smem_bytes<K>();
     auto kern = k_conv2d_bwd_ring<K>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return e;
     dim3 grid((unsigned)(ctiles * jtiles), (unsigned)strips, (unsigned)p.batch);
-    kern<<<grid, kThreads2d, smem, s>>>(p, ctiles, jtiles, strips);
+    kern<<<grid, R2B_NT, smem, s>>>(p, ctiles, jtiles, strips);
     return cudaGetLastError();
 }
 
