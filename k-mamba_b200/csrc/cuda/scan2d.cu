@@ -36,6 +36,8 @@
  */
 #include <string.h>
 
+#include <type_traits>
+
 #include "kmb_common.cuh"
 #include "../kmb_internal.h"
 
@@ -99,8 +101,8 @@ __device__ __forceinline__ void exp2_decay_point(const float2 (&w)[4], float2 (&
  * so the source pointer at row 0, the row stride and the column validity
  * are fixed for a strip. */
 struct FwdCopies {
-    const float *src[4];
-    long rs1; /* row stride of chunk 1 (x / delta rows: W*D; B / C rows: W*M) */
+    const float *src[4]; /* source of the next row staged */
+    long rs[4];          /* row stride (x / delta rows: W*D; B / C rows: W*M) */
     int dst[4];
     bool ok[4];
 };
@@ -117,7 +119,7 @@ __device__ __forceinline__ void fwd_copies(const S2D &p, long b, long j0, long d
             const float *base = t == 0 ? p.x + b * p.H * W * D
                                        : (t == 1 ? p.d0 : p.d1) + b * p.dl_bs;
             f.src[u] = base + j * D + dch0 + half * 4;
-            if (u == 1) f.rs1 = W * D;
+            f.rs[u] = W * D;
             f.dst[u] = t * kSlotX + col * kCh + half * 4;
             f.ok[u] = j < W;
         } else if (e < 112) {
@@ -125,19 +127,22 @@ __device__ __forceinline__ void fwd_copies(const S2D &p, long b, long j0, long d
             const int col = r / 4, q = r % 4;
             const long j = j0 + col;
             f.src[u] = (t == 0 ? p.B : p.C) + b * p.H * W * M + j * M + q * 4;
-            if (u == 1) f.rs1 = W * M;
+            f.rs[u] = W * M;
             f.dst[u] = 3 * kSlotX + t * kSlotB + col * 16 + q * 4;
             f.ok[u] = j < W && q * 4 < M;
         } else {
             f.src[u] = p.x;
+            f.rs[u] = 0;
             f.dst[u] = -1;
             f.ok[u] = false;
         }
     }
 }
 
-__device__ __forceinline__ void stage_row_fast(const S2D &p, const FwdCopies &f, long i,
-                                               float *s, int lane, const float *edge_row) {
+/* stages row i (rows are staged in order 0, 1, 2, ... once each: the
+ * sources then move one row down) */
+__device__ __forceinline__ void stage_row_fast(const S2D &p, FwdCopies &f, long i, float *s,
+                                               int lane, const float *edge_row) {
     const bool rok = i >= 0 && i < p.H;
     if (edge_row)
         kmb_cp_async16(s + 3 * kSlotX + 2 * kSlotB + lane * 4, rok ? edge_row + lane * 4 : p.x,
@@ -146,8 +151,8 @@ __device__ __forceinline__ void stage_row_fast(const S2D &p, const FwdCopies &f,
     for (int u = 0; u < 4; ++u) {
         if (f.dst[u] >= 0) {
             const bool ok = rok && f.ok[u];
-            const long rs = u == 0 ? p.W * p.D : u == 1 ? f.rs1 : p.W * p.M;
-            kmb_cp_async16(s + f.dst[u], ok ? f.src[u] + i * rs : p.x, ok ? 16 : 0);
+            kmb_cp_async16(s + f.dst[u], ok ? f.src[u] : p.x, ok ? 16 : 0);
+            f.src[u] += f.rs[u];
         }
     }
 }
@@ -196,6 +201,10 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_fwd(S2D p) {
         float *hcol = hb + (j0 * D + d) * M + q * 4;
         float *ycol = yb + j0 * D + d;
         const long hrow = W * D * M, yrow = W * D;
+        const int hcolst = (int)(D * M), ycolst = (int)D; /* one column further */
+        /* every column of this warp inside the grid and every lane's states
+         * inside M: the per-point guards are all true */
+        const bool full = j0 + kCPW <= W && M == 16;
         /* prologue: rows 0 .. kRing-2 of this warp */
 #pragma unroll
         for (int r = 0; r < kRing - 1; ++r) {
@@ -230,6 +239,11 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_fwd(S2D p) {
                 } else {
                     hl[0] = hl[1] = kmb_f2s(0.f);
                 }
+                /* this step's row of h / y (32-bit column offsets below) */
+                float *const hrowp = hcol + i * hrow;
+                float *const yrowp = ycol + i * yrow;
+                auto points = [&](auto full_tag) {
+                constexpr bool FULL = decltype(full_tag)::value;
                 float yq[4];
 #pragma unroll
                 for (int k = 0; k < kCPW; ++k) {
@@ -258,8 +272,8 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_fwd(S2D p) {
                         hl[jp] = hn;
                         y2 = kmb_fma2(Cp[jp], hn, y2);
                     }
-                    if (j < W && qok)
-                        *reinterpret_cast<float4 *>(hcol + i * hrow + k * D * M) =
+                    if (FULL || (j < W && qok))
+                        *reinterpret_cast<float4 *>(hrowp + k * hcolst) =
                             make_float4(hv[k][0].x, hv[k][0].y, hv[k][1].x, hv[k][1].y);
                     /* y: sum over the 4 state groups, 4 columns per fold */
                     yq[k & 3] = y2.x + y2.y;
@@ -275,9 +289,12 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_fwd(S2D p) {
                             }
                         }
                         const long jy = j0 + (k - 3) + q;
-                        if (jy < W) ycol[i * yrow + ((k - 3) + q) * D] = yq[0];
+                        if (FULL || jy < W) yrowp[((k - 3) + q) * ycolst] = yq[0];
                     }
                 }
+                };
+                if (full) points(std::true_type{});
+                else points(std::false_type{});
                 /* the last column's states go to the next warp (and, from
                  * the last warp, to the next strip) */
                 const float4 last = make_float4(hl[0].x, hl[0].y, hl[1].x, hl[1].y);
@@ -316,7 +333,9 @@ constexpr int kBSlot = 4 * kBX + 2 * kBB + kBH + kBL + kBE;
  * Sources are kept at row 0; a row further is W*D (inputs), W*M (B, C)
  * or W*D*M (h) floats. */
 struct BwdCopies {
-    const float *in, *bc, *h;
+    const float *in, *bc, *h; /* sources at the next row staged */
+    int in_rs, bc_rs, h_rs;   /* row strides: W*D, W*M, W*D*M floats */
+    int h_col;                /* one column of h: D*M floats */
     int in_dst, bc_dst;
     bool in_ok, bc_ok;
     unsigned h_ok; /* bit u: column of h chunk u inside the grid and q*4 < M */
@@ -345,6 +364,14 @@ __device__ __forceinline__ void bwd_copies(const S2D &p, long b, long j0, long d
     }
     const int ch = lane / 4, q = lane % 4;
     f.h = p.h + b * H * W * D * M + (j0 * D + dch0 + ch) * M + q * 4;
+    f.in_rs = (int)(W * D);
+    f.bc_rs = (int)(W * M);
+    f.h_rs = (int)(W * D * M);
+    f.h_col = (int)(D * M);
+    /* rows are staged from the last one up */
+    f.in += (H - 1) * W * D;
+    f.bc += (H - 1) * W * M;
+    f.h += (H - 1) * W * D * M;
     f.h_ok = 0;
 #pragma unroll
     for (int u = 0; u < kBCPW + 1; ++u) {
@@ -354,35 +381,39 @@ __device__ __forceinline__ void bwd_copies(const S2D &p, long b, long j0, long d
 }
 
 /* stages row i of this warp (columns j0 .. j0+3): inputs of row i, h of
- * row i-1 for the same columns and h(i, j0-1); zero outside the grid */
-__device__ __forceinline__ void stage_row_bwd_fast(const S2D &p, const BwdCopies &f, long i,
-                                                   float *s, int lane, const float *edge_row) {
+ * row i-1 for the same columns and h(i, j0-1); zero outside the grid.
+ * Rows are staged in order H-1, H-2, ... once each: the sources then move
+ * one row up. */
+__device__ __forceinline__ void stage_row_bwd_fast(const S2D &p, BwdCopies &f, long i, float *s,
+                                                   int lane, const float *edge_row) {
     const bool rok = i >= 0 && i < p.H;
     if (edge_row)
         kmb_cp_async16(s + 4 * kBX + 2 * kBB + kBH + kBL + lane * 4,
                        rok ? edge_row + lane * 4 : p.x, rok ? 16 : 0);
     {
         const bool ok = rok && f.in_ok;
-        kmb_cp_async16(s + f.in_dst, ok ? f.in + i * (p.W * p.D) : p.x, ok ? 16 : 0);
+        kmb_cp_async16(s + f.in_dst, ok ? f.in : p.x, ok ? 16 : 0);
     }
     {
         const bool ok = rok && f.bc_ok;
-        kmb_cp_async16(s + f.bc_dst, ok ? f.bc + i * (p.W * p.M) : p.x, ok ? 16 : 0);
+        kmb_cp_async16(s + f.bc_dst, ok ? f.bc : p.x, ok ? 16 : 0);
     }
     const int ch = lane / 4, q = lane % 4;
-    const long h_col = p.D * p.M, h_rs = p.W * h_col;
-    const float *hrow = f.h + i * h_rs;
+    const float *hup = f.h - f.h_rs;
 #pragma unroll
     for (int u = 0; u < kBCPW; ++u) {
         const bool ok = rok && i >= 1 && ((f.h_ok >> u) & 1);
         kmb_cp_async16(s + 4 * kBX + 2 * kBB + (u * kCh + ch) * 16 + q * 4,
-                       ok ? hrow - h_rs + u * h_col : p.x, ok ? 16 : 0);
+                       ok ? hup + u * f.h_col : p.x, ok ? 16 : 0);
     }
     {
         const bool ok = rok && ((f.h_ok >> kBCPW) & 1);
         kmb_cp_async16(s + 4 * kBX + 2 * kBB + kBH + ch * 16 + q * 4,
-                       ok ? hrow - h_col : p.x, ok ? 16 : 0);
+                       ok ? f.h - f.h_col : p.x, ok ? 16 : 0);
     }
+    f.in -= f.in_rs;
+    f.bc -= f.bc_rs;
+    f.h -= f.h_rs;
 }
 
 /* Reduce-scatter of 8 values over the 8 lanes that share q (lane bits 2-4):
@@ -458,6 +489,9 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_bwd(S2D p) {
         }
         const bool use_edge = w == kWarps - 1 && sidx + 1 < nstrips;
         auto edge_row = [&](long r) { return use_edge ? edge + r * 128 : nullptr; };
+        /* every column of this warp inside the grid and every lane's states
+         * inside M: the per-point guards are all true */
+        const bool full = j0 + kBCPW <= W && M == 16;
         BwdCopies bc;
         bwd_copies(p, b, j0, dch0, lane, bc);
         /* prologue: the first kBRing-1 rows this warp will run (H-1, H-2, ..) */
@@ -499,6 +533,9 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_bwd(S2D p) {
                 /* offsets of (i, j0): channel d in [P, D] tensors, states
                  * 4q.. in [P, M] ones */
                 const long ox = (i * W + j0) * D + d, obc = (i * W + j0) * M + q * 4;
+                float *const dxr = dxb + ox, *const dd0r = dd0b + ox, *const dd1r = dd1b + ox;
+                auto points = [&](auto full_tag) {
+                constexpr bool FULL = decltype(full_tag)::value;
 #pragma unroll
                 for (int k = kBCPW - 1; k >= 0; --k) {
                     const long j = j0 + k;
@@ -576,19 +613,21 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_bwd(S2D p) {
                     const float r2 = __shfl_down_sync(kFull, r1, 4);
                     const float r3 = __shfl_down_sync(kFull, r1, 8);
                     const float r4 = __shfl_down_sync(kFull, r1, 12);
-                    if (j < W) {
+                    if (FULL || j < W) {
                         if (q == 0) {
-                            const long o = ox + k * D;
-                            dxb[o] = sx;
-                            dd0b[o] = s0 * KMB_LN2 + sb / 2.0f;
-                            dd1b[o] = s1 * KMB_LN2 + sb / 2.0f;
+                            dxr[k * D] = sx;
+                            dd0r[k * D] = s0 * KMB_LN2 + sb / 2.0f;
+                            dd1r[k * D] = s1 * KMB_LN2 + sb / 2.0f;
                         }
-                        if ((c & 3) == 0 && qok) {
+                        if ((c & 3) == 0 && (FULL || qok)) {
                             float *dst = ((c >> 2) ? dCb : dBb) + obc + k * M;
                             atomicAdd(reinterpret_cast<float4 *>(dst), make_float4(r1, r2, r3, r4));
                         }
                     }
                 }
+                };
+                if (full) points(std::true_type{});
+                else points(std::false_type{});
                 /* hand the carries on: the left neighbour warp (next step) and
                  * the next strip (its last warp) get e1 G of column j0 */
                 const float4 outq = make_float4(qh[0].x, qh[0].y, qh[1].x, qh[1].y);
@@ -624,7 +663,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_bwd(S2D p) {
 
 extern "C" int kmb_scan2d_supported(const KmbNDLaunch *a) {
     return a->nd == 2 && a->bc_shared && a->M % 4 == 0 && a->M <= 16 && a->D % kCh == 0 &&
-           a->dims[0] > 0 && a->dims[1] > 0;
+           a->dims[0] > 0 && a->dims[1] > 0 && a->D * a->M < (1L << 24);
 }
 
 static S2D make_s2d(const KmbNDLaunch *a) {
