@@ -201,6 +201,29 @@ def test_batched_fwd_bwd_vs_oracle(lib, cuda, oracle, bsz, L, D, N, shared):
         assert rel_err(g[k], g_r[k]) <= TOL, k
 
 
+@pytest.mark.parametrize("bsz,L,D,N", [(2, 70, 24, 4), (2, 77, 36, 8), (1, 45, 20, 32),
+                                        (1, 30, 8, 128), (2, 64, 132, 16), (1, 9, 4, 12)])
+def test_channel_shared_backward_lane_groups_vs_oracle(lib, cuda, oracle, bsz, L, D, N):
+    """The channel-shared backward for 16-byte rows (D and N multiples of
+    4) at every lane-group width: N = 4, 8, 32, 128 give 1, 2, 8, 32 lanes
+    per channel; D = 36 and 132 leave a partial channel tile, L not a
+    multiple of the 8-step chunk a partial last chunk."""
+    rng = np.random.default_rng(bsz * 31 + L + D + N)
+    x = rng.normal(0, 1, (bsz, L, D)).astype(f32)
+    dt = np.log1p(np.exp(rng.normal(0, 1, (bsz, L, D)) - 2)).astype(f32)
+    A = (-np.exp(rng.uniform(0, np.log(16), (D, N)))).astype(f32)
+    B = rng.normal(0, 1, (bsz, L, N)).astype(f32)
+    Cm = rng.normal(0, 1, (bsz, L, N)).astype(f32)
+    dy = rng.normal(0, 1, (bsz, L, D)).astype(f32)
+    h0 = rng.normal(0, 0.5, (bsz, D, N)).astype(f32)
+    y, hl, g = run_batched(lib, x, A, B, Cm, dt, dy, True, h0=h0)
+    y_r, hl_r, g_r = oracle_batched(oracle, x, A, B, Cm, dt, dy, True, h0=h0)
+    assert rel_err(y, y_r) <= TOL
+    assert rel_err(hl, hl_r) <= TOL
+    for k in g:
+        assert rel_err(g[k], g_r[k]) <= TOL, k
+
+
 @pytest.mark.parametrize("case", ["weak", "clamp"])
 @pytest.mark.parametrize("shared", [True, False])
 def test_decay_regime_switches_vs_oracle(lib, cuda, oracle, shared, case):
