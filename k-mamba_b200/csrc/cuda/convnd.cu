@@ -652,6 +652,199 @@ cudaError_t dispatch2d_bwd_ring(const ConvDev &p, cudaStream_t s) {
 }
 
 /* ------------------------------------------------------------------ */
+/* 3D (the Mamba-ND volumes)                                           */
+/* ------------------------------------------------------------------ */
+
+/*
+ * 3D causal depthwise convolution for K <= 3, D a multiple of 4 and
+ * 16-byte aligned tensors.  A thread owns one point and 4 consecutive
+ * channels (float4); a CTA covers 16 consecutive points (in row-major
+ * z, y, x order) x 64 channels, with the block's K^3 x 64 taps in shared
+ * memory.  The forward and the gather-form dinput read the K^3 neighbours
+ * straight from global memory: tap offsets are compile-time multiples of
+ * the axis strides, the causal bounds are checked once per axis, and the
+ * neighbourhoods of adjacent points come from L1 / L2, so HBM sees one
+ * read of the input and one write of the output.  dkernel / dbias keep
+ * K^3 + 1 float4 accumulators per thread over a run of points and fold
+ * them across the CTA in shared memory, one atomic per (tap, channel).
+ */
+constexpr int C3_PTS = 16; /* points per CTA (x 16 channel groups = 256 threads) */
+
+struct Geo3 {
+    int Z, Y, X;
+    long sz, sy, sx; /* strides in floats of one step along z, y, x */
+};
+
+__device__ __forceinline__ Geo3 geo3(const ConvDev &p) {
+    Geo3 g;
+    g.Z = (int)p.dims[0];
+    g.Y = (int)p.dims[1];
+    g.X = (int)p.dims[2];
+    g.sx = p.D;
+    g.sy = (long)g.X * p.D;
+    g.sz = (long)g.Y * g.X * p.D;
+    return g;
+}
+
+/* taps of this CTA's 64 channels: tap kl, channel group g at [kl * 16 + g] */
+template <int K>
+__device__ __forceinline__ void load_taps3(const ConvDev &p, float4 *taps, long c0, int tid) {
+    constexpr int KV = K * K * K;
+    for (int i = tid; i < KV * 16; i += 256) {
+        const int kl = i / 16, g = i % 16;
+        const long c = c0 + g * 4;
+        taps[i] = c < p.D ? __ldg(reinterpret_cast<const float4 *>(p.ker + kl * p.D + c))
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+}
+
+/* SGN = -1: out(q) = bias + sum_k in(q - (K-1-k)) w_k (forward);
+ * SGN = +1: din(q) = sum_k dy(q + (K-1-k)) w_k (gather form of dinput). */
+template <int K, int SGN>
+__global__ void __launch_bounds__(256) k_conv3d_gather(ConvDev p) {
+    using V = Vec4p;
+    constexpr int KV = K * K * K;
+    __shared__ float4 taps[KV * 16];
+    const int tid = threadIdx.x, cg = tid & 15, pl = tid >> 4;
+    const long c0 = (long)blockIdx.y * 64;
+    const long c = c0 + cg * 4;
+    const long b = blockIdx.z;
+    load_taps3<K>(p, taps, c0, tid);
+    __syncthreads();
+    const long pt = (long)blockIdx.x * C3_PTS + pl;
+    if (pt >= p.P || c >= p.D) return;
+    const Geo3 g = geo3(p);
+    const int x = (int)(pt % g.X);
+    const long yz = pt / g.X;
+    const int y = (int)(yz % g.Y), z = (int)(yz / g.Y);
+    const float *src = (SGN < 0 ? p.in : p.dy) + (b * p.P + pt) * p.D + c;
+    float4 s = (SGN < 0 && p.bias) ? __ldg(reinterpret_cast<const float4 *>(p.bias + c))
+                                   : V::zero();
+#pragma unroll
+    for (int kz = 0; kz < K; ++kz) {
+        const int oz = K - 1 - kz;
+        if (SGN < 0 ? z < oz : z + oz >= g.Z) continue;
+#pragma unroll
+        for (int ky = 0; ky < K; ++ky) {
+            const int oy = K - 1 - ky;
+            if (SGN < 0 ? y < oy : y + oy >= g.Y) continue;
+#pragma unroll
+            for (int kx = 0; kx < K; ++kx) {
+                const int ox = K - 1 - kx;
+                if (SGN < 0 ? x < ox : x + ox >= g.X) continue;
+                const long off = SGN * (oz * g.sz + oy * g.sy + ox * g.sx);
+                const float4 v = __ldg(reinterpret_cast<const float4 *>(src + off));
+                s = V::fma(v, taps[((kz * K + ky) * K + kx) * 16 + cg], s);
+            }
+        }
+    }
+    *reinterpret_cast<float4 *>((SGN < 0 ? p.out : p.din) + (b * p.P + pt) * p.D + c) = s;
+}
+
+/* dkernel(k, d) = sum_q dy(q, d) in(q - (K-1-k), d), dbias(d) = sum_q dy(q, d):
+ * point lane pl of a CTA walks points p0 + pl, p0 + pl + 16, ... of the
+ * CTA's run; the 16 lanes of a channel group are folded in shared memory. */
+template <int K>
+__global__ void __launch_bounds__(256) k_conv3d_param(ConvDev p, long run) {
+    using V = Vec4p;
+    constexpr int KV = K * K * K;
+    __shared__ float4 red[C3_PTS * 16];
+    const int tid = threadIdx.x, cg = tid & 15, pl = tid >> 4;
+    const long c = (long)blockIdx.y * 64 + cg * 4;
+    const long b = blockIdx.z;
+    const bool cok = c < p.D;
+    const Geo3 g = geo3(p);
+    float4 acc[KV + 1];
+#pragma unroll
+    for (int k = 0; k <= KV; ++k) acc[k] = V::zero();
+    const long p0 = (long)blockIdx.x * run;
+    const long p1 = min(p.P, p0 + run);
+    if (cok) {
+        for (long pt = p0 + pl; pt < p1; pt += C3_PTS) {
+            const int x = (int)(pt % g.X);
+            const long yz = pt / g.X;
+            const int y = (int)(yz % g.Y), z = (int)(yz / g.Y);
+            const long o = (b * p.P + pt) * p.D + c;
+            const float4 gy = __ldg(reinterpret_cast<const float4 *>(p.dy + o));
+            const float *src = p.in + o;
+            acc[KV] = V::add(acc[KV], gy);
+#pragma unroll
+            for (int kz = 0; kz < K; ++kz) {
+                const int oz = K - 1 - kz;
+                if (z < oz) continue;
+#pragma unroll
+                for (int ky = 0; ky < K; ++ky) {
+                    const int oy = K - 1 - ky;
+                    if (y < oy) continue;
+#pragma unroll
+                    for (int kx = 0; kx < K; ++kx) {
+                        const int ox = K - 1 - kx;
+                        if (x < ox) continue;
+                        const float4 v = __ldg(reinterpret_cast<const float4 *>(
+                            src - (oz * g.sz + oy * g.sy + ox * g.sx)));
+                        const int kl = (kz * K + ky) * K + kx;
+                        acc[kl] = V::fma(gy, v, acc[kl]);
+                    }
+                }
+            }
+        }
+    }
+    /* fold the 16 point lanes of each channel group, one tap at a time */
+#pragma unroll 1
+    for (int k = 0; k <= KV; ++k) {
+        red[pl * 16 + cg] = acc[k];
+        __syncthreads();
+        if (tid < 16 && (long)blockIdx.y * 64 + tid * 4 < p.D) {
+            float4 s = red[tid];
+            for (int q = 1; q < C3_PTS; ++q) s = V::add(s, red[q * 16 + tid]);
+            const long cc = (long)blockIdx.y * 64 + tid * 4;
+            float *dst = k < KV ? p.dker + (long)k * p.D + cc : p.dbias;
+            if (k < KV || dst) {
+                if (k == KV) dst += cc;
+                atomicAdd(dst + 0, s.x);
+                atomicAdd(dst + 1, s.y);
+                atomicAdd(dst + 2, s.z);
+                atomicAdd(dst + 3, s.w);
+            }
+        }
+        __syncthreads();
+    }
+}
+
+template <int K>
+cudaError_t launch3d(const ConvDev &p, bool bwd, cudaStream_t s) {
+    const unsigned ct = (unsigned)((p.D + 63) / 64);
+    dim3 grid((unsigned)((p.P + C3_PTS - 1) / C3_PTS), ct, (unsigned)p.batch);
+    if (!bwd) {
+        k_conv3d_gather<K, -1><<<grid, 256, 0, s>>>(p);
+        return cudaGetLastError();
+    }
+    k_conv3d_gather<K, +1><<<grid, 256, 0, s>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    /* runs of points per CTA for dkernel: about 4 CTAs per SM in total */
+    const long ctas = (long)ct * p.batch;
+    long nrun = (4L * 148 + ctas - 1) / ctas;
+    if (nrun < 1) nrun = 1;
+    long run = (p.P + nrun - 1) / nrun;
+    run = (run + C3_PTS - 1) / C3_PTS * C3_PTS;
+    dim3 pg((unsigned)((p.P + run - 1) / run), ct, (unsigned)p.batch);
+    k_conv3d_param<K><<<pg, 256, 0, s>>>(p, run);
+    return cudaGetLastError();
+}
+
+cudaError_t dispatch3d(const ConvDev &p, bool bwd, cudaStream_t s) {
+    switch (p.K) {
+    case 1: return launch3d<1>(p, bwd, s);
+    case 2: return launch3d<2>(p, bwd, s);
+    case 3: return launch3d<3>(p, bwd, s);
+    default: return cudaErrorNotSupported;
+    }
+}
+
+bool use_3d(const ConvDev &p) { return p.nd == 3 && p.K >= 1 && p.K <= 3; }
+
+/* ------------------------------------------------------------------ */
 /* generic ND                                                          */
 /* ------------------------------------------------------------------ */
 
@@ -843,6 +1036,8 @@ extern "C" int kmb_launch_convnd_fwd(const KmbConvND *a, cudaStream_t s) {
             e = dispatch2d_fwd_ring(p, s);
         else
             e = aligned4(a, false) ? dispatch2d<4>(p, false, s) : dispatch2d<1>(p, false, s);
+    } else if (use_3d(p) && aligned4(a, false)) {
+        e = dispatch3d(p, false, s);
     } else {
         k_convnd_fwd_generic<<<grid_for(p.batch * p.P * p.D, 256), 256, 0, s>>>(p);
         e = cudaGetLastError();
@@ -861,6 +1056,8 @@ extern "C" int kmb_launch_convnd_bwd(const KmbConvND *a, cudaStream_t s) {
         if (aligned4(a, true) && p.D % (4 * R2_CG) == 0 && p.K <= R2_KMAX)
             e = dispatch2d_bwd_ring(p, s);
         else e = aligned4(a, true) ? dispatch2d<4>(p, true, s) : dispatch2d<1>(p, true, s);
+    } else if (use_3d(p) && aligned4(a, true) && (uintptr_t)a->dkernel % 16 == 0) {
+        e = dispatch3d(p, true, s);
     } else {
         k_convnd_bwd_input_generic<<<grid_for(p.batch * p.P * p.D, 256), 256, 0, s>>>(p);
         e = cudaGetLastError();
