@@ -44,6 +44,7 @@ struct NDDev {
     const float *delta[kMaxAxes];
     const float *A[kMaxAxes];
     const int *lvl_start, *lvl_off, *prev, *next;
+    const int *sprev, *snext; /* prev / next in level-slot order */
     long P, D, M;
     long x_bs;      /* batch stride of x, y, dx (P*D) */
     long dl_bs;     /* batch stride of every delta / ddelta axis */
@@ -197,6 +198,329 @@ __global__ void __launch_bounds__(kThreads) k_scannd_bwd(NDDev p) {
     }
 }
 
+/* ------------------------------------------------------------------ */
+/* warp-per-point kernels (channel-shared B/C, M % 4 == 0 <= 16,        */
+/* D % 8 == 0, 3 or 4 axes: the Mamba-ND volumes)                       */
+/* ------------------------------------------------------------------ */
+
+/*
+ * A CTA owns one batch item and 8 channels and walks the levels in order
+ * (backward: in reverse) with one CTA barrier per level, as above.  A warp
+ * handles one point at a time: lane 4c + q holds channel c of the group
+ * and states 4q .. 4q+3, so the predecessor states h(p - e_axis) of the
+ * warp are one coalesced 512-byte row per axis, B / C rows are one float4
+ * per lane, and the sums over states fold over the 4 lanes of a channel.
+ * The level's points are spread over the warps; predecessors were written
+ * by this CTA before the last barrier, so they are read with plain
+ * (L2-coherent) loads.
+ */
+constexpr int kWCh = 8;      /* channels per CTA */
+constexpr int kWWarps = 8;   /* warps per CTA */
+constexpr unsigned kWFull = 0xffffffffu;
+
+/* points a warp keeps in flight: their index, input and predecessor loads
+ * are issued before any of them is computed */
+constexpr int kWU = 4;
+
+template <int ND>
+__global__ void __launch_bounds__(kWWarps * 32) k_scannd_fwd_w(NDDev p) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int c = lane >> 2, q = lane & 3;
+    const long b = blockIdx.y;
+    const long d = (long)blockIdx.x * kWCh + c;
+    const long D = p.D, M = p.M;
+    const bool qok = q * 4 < M;
+    float2 A2[ND][2];
+#pragma unroll
+    for (int a = 0; a < ND; ++a)
+#pragma unroll
+        for (int jp = 0; jp < 2; ++jp) {
+            const int m = q * 4 + 2 * jp;
+            A2[a][jp] = kmb_f2(m < M ? p.A[a][d * M + m] * KMB_LOG2E : 0.f,
+                               m + 1 < M ? p.A[a][d * M + m + 1] * KMB_LOG2E : 0.f);
+        }
+    const float *x = p.x + b * p.x_bs;
+    const float *Bb = p.B + b * p.bc_bs;
+    const float *Cb = p.C + b * p.bc_bs;
+    float *h = p.h + b * p.h_bs;
+    float *y = p.y + b * p.x_bs;
+    const float *dl[ND];
+#pragma unroll
+    for (int a = 0; a < ND; ++a) dl[a] = p.delta[a] + b * p.dl_bs;
+
+    for (int l = 0; l < p.nlevels; ++l) {
+        const int s0 = p.lvl_start[l], s1 = p.lvl_start[l + 1];
+        for (int sb = s0 + w * kWU; sb < s1; sb += kWWarps * kWU) {
+            /* indices, inputs and predecessor states of kWU points */
+            long pt[kWU];
+            int pv[kWU][ND];
+            float xv[kWU], dta[kWU][ND];
+            float4 B4[kWU], C4[kWU], hp[kWU][ND];
+#pragma unroll
+            for (int u = 0; u < kWU; ++u) {
+                pt[u] = sb + u < s1 ? p.lvl_off[sb + u] : -1;
+#pragma unroll
+                for (int a = 0; a < ND; ++a)
+                    pv[u][a] = sb + u < s1 ? p.sprev[(long)(sb + u) * ND + a] : -1;
+            }
+#pragma unroll
+            for (int u = 0; u < kWU; ++u) {
+                const bool ok = pt[u] >= 0;
+                const long ptu = ok ? pt[u] : 0;
+                xv[u] = ok ? x[ptu * D + d] : 0.f;
+#pragma unroll
+                for (int a = 0; a < ND; ++a) {
+                    dta[u][a] = ok ? dl[a][ptu * D + d] : 0.f;
+                }
+                B4[u] = C4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (ok && qok) {
+                    B4[u] = *reinterpret_cast<const float4 *>(Bb + ptu * M + q * 4);
+                    C4[u] = *reinterpret_cast<const float4 *>(Cb + ptu * M + q * 4);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kWU; ++u)
+#pragma unroll
+                for (int a = 0; a < ND; ++a) {
+                    hp[u][a] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (pv[u][a] >= 0 && qok)
+                        hp[u][a] = *reinterpret_cast<const float4 *>(
+                            h + ((long)pv[u][a] * D + d) * M + q * 4);
+                }
+#pragma unroll
+            for (int u = 0; u < kWU; ++u) {
+                float dt_bar = 0.f;
+#pragma unroll
+                for (int a = 0; a < ND; ++a) dt_bar += dta[u][a];
+                dt_bar /= (float)ND;
+                /* dt_bar (B x), in the reference's association */
+                const float2 u2 = kmb_f2s(dt_bar), x2 = kmb_f2s(xv[u]);
+                float2 hn[2] = {kmb_mul2(u2, kmb_mul2(kmb_f2(B4[u].x, B4[u].y), x2)),
+                                kmb_mul2(u2, kmb_mul2(kmb_f2(B4[u].z, B4[u].w), x2))};
+#pragma unroll
+                for (int a = 0; a < ND; ++a) {
+                    if (pv[u][a] >= 0) {
+                        const float2 dv2 = kmb_f2s(dta[u][a]);
+                        const float2 e0 = kmb_exp2_decay2(kmb_mul2(dv2, A2[a][0]));
+                        const float2 e1 = kmb_exp2_decay2(kmb_mul2(dv2, A2[a][1]));
+                        hn[0] = kmb_fma2(e0, kmb_f2(hp[u][a].x, hp[u][a].y), hn[0]);
+                        hn[1] = kmb_fma2(e1, kmb_f2(hp[u][a].z, hp[u][a].w), hn[1]);
+                    }
+                }
+                if (pt[u] >= 0 && qok)
+                    *reinterpret_cast<float4 *>(h + (pt[u] * D + d) * M + q * 4) =
+                        make_float4(hn[0].x, hn[0].y, hn[1].x, hn[1].y);
+                const float2 y2 = kmb_fma2(kmb_f2(C4[u].z, C4[u].w), hn[1],
+                                           kmb_mul2(kmb_f2(C4[u].x, C4[u].y), hn[0]));
+                float yv = y2.x + y2.y;
+                yv += __shfl_xor_sync(kWFull, yv, 1);
+                yv += __shfl_xor_sync(kWFull, yv, 2);
+                if (q == 0 && pt[u] >= 0) y[pt[u] * D + d] = yv;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+/* Reduce-scatter of 8 values over the 8 lanes that share q (lane bits
+ * 2-4): afterwards lane 4c + q holds the sum of value 4 (c >> 2) + (c & 3). */
+__device__ __forceinline__ float rs8_ch(float (&v)[8], int lane) {
+#pragma unroll
+    for (int o = 16, half = 4; o >= 4; o >>= 1, half >>= 1) {
+        const bool up = (lane & o) != 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            if (k < half) {
+                const float send = up ? v[k] : v[k + half];
+                const float keep = up ? v[k + half] : v[k];
+                v[k] = keep + __shfl_xor_sync(kWFull, send, o);
+            }
+        }
+    }
+    return v[0];
+}
+
+/* Backward of k_scannd_fwd_w, levels in reverse (the adjoint of the
+ * generic backward above, same per-state terms):
+ *   G(p) = C dy + sum_axis e_axis(p+e) G(p+e),   G stored in the scratch,
+ *   dC += dy h,  dB += G dt_bar x  (folded over the 8 channels, one
+ *   128-bit atomic per point, state quad and array),
+ *   dx = sum_m (G dt_bar) B,  ddelta_axis = sum_m (G h(p-e)) e A_axis
+ *   + sum_m (G B) x / ndims,  dA_axis += (G h(p-e)) e delta_axis. */
+template <int ND>
+__global__ void __launch_bounds__(kWWarps * 32) k_scannd_bwd_w(NDDev p) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int c = lane >> 2, q = lane & 3;
+    const long b = blockIdx.y;
+    const long d = (long)blockIdx.x * kWCh + c;
+    const long D = p.D, M = p.M;
+    const bool qok = q * 4 < M;
+    float2 A2[ND][2], Ar[ND][2], dAp[ND][2];
+#pragma unroll
+    for (int a = 0; a < ND; ++a)
+#pragma unroll
+        for (int jp = 0; jp < 2; ++jp) {
+            const int m = q * 4 + 2 * jp;
+            const float a0 = m < M ? p.A[a][d * M + m] : 0.f;
+            const float a1 = m + 1 < M ? p.A[a][d * M + m + 1] : 0.f;
+            Ar[a][jp] = kmb_f2(a0, a1);
+            A2[a][jp] = kmb_f2(a0 * KMB_LOG2E, a1 * KMB_LOG2E);
+            dAp[a][jp] = kmb_f2s(0.f);
+        }
+    const float *x = p.x + b * p.x_bs;
+    const float *dy = p.dy + b * p.x_bs;
+    const float *Bb = p.B + b * p.bc_bs;
+    const float *Cb = p.C + b * p.bc_bs;
+    const float *h = p.h + b * p.h_bs;
+    float *G = p.G + b * p.h_bs;
+    float *dx = p.dx + b * p.x_bs;
+    float *dBb = p.dB + b * p.bc_bs;
+    float *dCb = p.dC + b * p.bc_bs;
+    const float *dl[ND];
+    float *ddl[ND];
+#pragma unroll
+    for (int a = 0; a < ND; ++a) {
+        dl[a] = p.delta[a] + b * p.dl_bs;
+        ddl[a] = p.ddelta[a] + b * p.dl_bs;
+    }
+    constexpr int U = kWU / 2; /* points in flight (the backward keeps more per point) */
+
+    for (int l = p.nlevels - 1; l >= 0; --l) {
+        const int s0 = p.lvl_start[l], s1 = p.lvl_start[l + 1];
+        for (int sb = s0 + w * U; sb < s1; sb += kWWarps * U) {
+            long pt[U];
+            int nx[U][ND], pv[U][ND];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const bool ok = sb + u < s1;
+                pt[u] = ok ? p.lvl_off[sb + u] : -1;
+#pragma unroll
+                for (int a = 0; a < ND; ++a) {
+                    nx[u][a] = ok ? p.snext[(long)(sb + u) * ND + a] : -1;
+                    pv[u][a] = ok ? p.sprev[(long)(sb + u) * ND + a] : -1;
+                }
+            }
+            /* every load of the U points before any arithmetic */
+            float xv[U], gy[U], dta[U][ND], dtn[U][ND];
+            float4 B4[U], C4[U], H4[U], gn[U][ND], hp[U][ND];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const bool ok = pt[u] >= 0;
+                const long od = (ok ? pt[u] : 0) * D + d;
+                xv[u] = ok ? x[od] : 0.f;
+                gy[u] = ok ? dy[od] : 0.f;
+                const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+                B4[u] = C4[u] = H4[u] = z4;
+                if (ok && qok) {
+                    B4[u] = *reinterpret_cast<const float4 *>(Bb + pt[u] * M + q * 4);
+                    C4[u] = *reinterpret_cast<const float4 *>(Cb + pt[u] * M + q * 4);
+                    H4[u] = *reinterpret_cast<const float4 *>(h + od * M + q * 4);
+                }
+#pragma unroll
+                for (int a = 0; a < ND; ++a) {
+                    dta[u][a] = ok ? dl[a][od] : 0.f;
+                    const long on = (long)nx[u][a] * D + d, op = (long)pv[u][a] * D + d;
+                    dtn[u][a] = nx[u][a] >= 0 ? dl[a][on] : 0.f;
+                    gn[u][a] = hp[u][a] = z4;
+                    if (qok && nx[u][a] >= 0)
+                        gn[u][a] = *reinterpret_cast<const float4 *>(G + on * M + q * 4);
+                    if (qok && pv[u][a] >= 0)
+                        hp[u][a] = *reinterpret_cast<const float4 *>(h + op * M + q * 4);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const long od = (pt[u] >= 0 ? pt[u] : 0) * D + d;
+                float dt_bar = 0.f;
+#pragma unroll
+                for (int a = 0; a < ND; ++a) dt_bar += dta[u][a];
+                dt_bar /= (float)ND;
+                const float2 gy2 = kmb_f2s(gy[u]);
+                float2 gg[2] = {kmb_mul2(kmb_f2(C4[u].x, C4[u].y), gy2),
+                                kmb_mul2(kmb_f2(C4[u].z, C4[u].w), gy2)};
+#pragma unroll
+                for (int a = 0; a < ND; ++a) {
+                    if (nx[u][a] >= 0) {
+                        const float2 dn2 = kmb_f2s(dtn[u][a]);
+                        const float2 e0 = kmb_exp2_decay2(kmb_mul2(dn2, A2[a][0]));
+                        const float2 e1 = kmb_exp2_decay2(kmb_mul2(dn2, A2[a][1]));
+                        gg[0] = kmb_fma2(e0, kmb_f2(gn[u][a].x, gn[u][a].y), gg[0]);
+                        gg[1] = kmb_fma2(e1, kmb_f2(gn[u][a].z, gn[u][a].w), gg[1]);
+                    }
+                }
+                if (pt[u] >= 0 && qok)
+                    *reinterpret_cast<float4 *>(G + od * M + q * 4) =
+                        make_float4(gg[0].x, gg[0].y, gg[1].x, gg[1].y);
+                const float2 Bp[2] = {kmb_f2(B4[u].x, B4[u].y), kmb_f2(B4[u].z, B4[u].w)};
+                const float2 dtb2 = kmb_f2s(dt_bar), xv2 = kmb_f2s(xv[u]);
+                float2 sx2 = kmb_f2s(0.f), sb2 = kmb_f2s(0.f), sdt2[ND];
+                float v8[8];
+#pragma unroll
+                for (int jp = 0; jp < 2; ++jp) {
+                    sx2 = kmb_fma2(kmb_mul2(gg[jp], dtb2), Bp[jp], sx2);
+                    sb2 = kmb_fma2(kmb_mul2(gg[jp], Bp[jp]), xv2, sb2);
+                    const float2 vb = kmb_mul2(kmb_mul2(gg[jp], dtb2), xv2); /* dB */
+                    const float2 vc =
+                        kmb_mul2(gy2, jp ? kmb_f2(H4[u].z, H4[u].w) : kmb_f2(H4[u].x, H4[u].y));
+                    v8[2 * jp] = vb.x;
+                    v8[2 * jp + 1] = vb.y;
+                    v8[4 + 2 * jp] = vc.x;
+                    v8[4 + 2 * jp + 1] = vc.y;
+                }
+#pragma unroll
+                for (int a = 0; a < ND; ++a) {
+                    sdt2[a] = kmb_f2s(0.f);
+                    if (pv[u][a] >= 0) {
+                        const float2 dv2 = kmb_f2s(dta[u][a]);
+                        const float2 hpp[2] = {kmb_f2(hp[u][a].x, hp[u][a].y),
+                                               kmb_f2(hp[u][a].z, hp[u][a].w)};
+#pragma unroll
+                        for (int jp = 0; jp < 2; ++jp) {
+                            const float2 e = kmb_exp2_decay2(kmb_mul2(dv2, A2[a][jp]));
+                            const float2 gh = kmb_mul2(kmb_mul2(gg[jp], hpp[jp]), e);
+                            dAp[a][jp] = kmb_fma2(gh, dv2, dAp[a][jp]);
+                            sdt2[a] = kmb_fma2(gh, Ar[a][jp], sdt2[a]);
+                        }
+                    }
+                }
+                /* sums over the 16 states (the 4 lanes of a channel) */
+                float sx = sx2.x + sx2.y, sbv = sb2.x + sb2.y, sdt[ND];
+#pragma unroll
+                for (int a = 0; a < ND; ++a) sdt[a] = sdt2[a].x + sdt2[a].y;
+#pragma unroll
+                for (int o = 1; o <= 2; o <<= 1) {
+                    sx += __shfl_xor_sync(kWFull, sx, o);
+                    sbv += __shfl_xor_sync(kWFull, sbv, o);
+#pragma unroll
+                    for (int a = 0; a < ND; ++a) sdt[a] += __shfl_xor_sync(kWFull, sdt[a], o);
+                }
+                if (q == 0 && pt[u] >= 0) {
+                    dx[od] = sx;
+#pragma unroll
+                    for (int a = 0; a < ND; ++a) ddl[a][od] = sdt[a] + sbv / (float)ND;
+                }
+                /* dB / dC: sums over the 8 channels, then 4 states into one lane */
+                const float r1 = rs8_ch(v8, lane);
+                const float r2 = __shfl_down_sync(kWFull, r1, 4);
+                const float r3 = __shfl_down_sync(kWFull, r1, 8);
+                const float r4 = __shfl_down_sync(kWFull, r1, 12);
+                if ((c & 3) == 0 && qok && pt[u] >= 0) {
+                    float *dst = ((c >> 2) ? dCb : dBb) + pt[u] * M + q * 4;
+                    atomicAdd(reinterpret_cast<float4 *>(dst), make_float4(r1, r2, r3, r4));
+                }
+            }
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int a = 0; a < ND; ++a) {
+        const float v[4] = {dAp[a][0].x, dAp[a][0].y, dAp[a][1].x, dAp[a][1].y};
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            if (q * 4 + j < M) atomicAdd(p.dA[a] + d * M + q * 4 + j, v[j]);
+    }
+}
+
 /* Channel tile of a CTA: a power of two dividing 256, small enough that
  * the grid has >= 2 CTAs per SM (every CTA walks all levels, so CTAs are
  * the only parallelism across chains), and within the backward's shared
@@ -222,6 +546,7 @@ void fill_dev(const KmbNDLaunch *a, NDDev *p) {
         p->ddelta[i] = a->ddelta[i];
     }
     p->lvl_start = a->lvl_start; p->lvl_off = a->lvl_off; p->prev = a->prev; p->next = a->next;
+    p->sprev = a->sprev; p->snext = a->snext;
     p->P = a->P; p->D = a->D; p->M = a->M; p->nd = a->nd; p->nlevels = a->nlevels;
     p->x_bs = a->P * a->D;
     p->dl_bs = a->delta_bstride;
@@ -233,9 +558,31 @@ void fill_dev(const KmbNDLaunch *a, NDDev *p) {
 
 } // namespace
 
+/* the warp-per-point kernels: channel-shared B/C with 16-byte rows,
+ * M % 4 == 0 <= 16, D % 8 == 0, 3 or 4 axes */
+static bool use_w(const KmbNDLaunch *a) {
+    auto al = [](const void *q) { return q == nullptr || ((uintptr_t)q & 15u) == 0; };
+    return (a->nd == 3 || a->nd == 4) && a->bc_shared && a->M % 4 == 0 && a->M <= 16 &&
+           a->D % kWCh == 0 && al(a->B) && al(a->C) && al(a->h) && al(a->G) && al(a->dB) &&
+           al(a->dC);
+}
+
+template <int ND>
+static cudaError_t launch_w(const NDDev &p, const KmbNDLaunch *a, bool bwd, cudaStream_t s) {
+    dim3 grid((unsigned)(a->D / kWCh), (unsigned)a->batch);
+    if (bwd) k_scannd_bwd_w<ND><<<grid, kWWarps * 32, 0, s>>>(p);
+    else k_scannd_fwd_w<ND><<<grid, kWWarps * 32, 0, s>>>(p);
+    return cudaGetLastError();
+}
+
 extern "C" int kmb_launch_scannd_fwd(const KmbNDLaunch *a, cudaStream_t s) {
     NDDev p;
     fill_dev(a, &p);
+    if (use_w(a)) {
+        const cudaError_t e = a->nd == 3 ? launch_w<3>(p, a, false, s) : launch_w<4>(p, a, false, s);
+        if (e != cudaSuccess) return kmb_cuda_fail(e, "scannd forward launch");
+        return KMB_OK;
+    }
     p.dtile = pick_dtile(a->D, a->nd, a->M, false, a->batch);
     dim3 grid((unsigned)((a->D + p.dtile - 1) / p.dtile), (unsigned)a->batch);
     k_scannd_fwd<<<grid, kThreads, 0, s>>>(p);
@@ -259,6 +606,11 @@ extern "C" int kmb_launch_scannd_bwd(const KmbNDLaunch *a, cudaStream_t s) {
         if (e == cudaSuccess) e = cudaMemsetAsync(a->dC, 0, nb, s);
     }
     if (e != cudaSuccess) return kmb_cuda_fail(e, "scannd backward memset");
+    if (use_w(a)) {
+        e = a->nd == 3 ? launch_w<3>(p, a, true, s) : launch_w<4>(p, a, true, s);
+        if (e != cudaSuccess) return kmb_cuda_fail(e, "scannd backward launch");
+        return KMB_OK;
+    }
     const size_t smem = sizeof(float) * a->nd * p.dtile * a->M;
     if (smem > 48 * 1024) {
         e = cudaFuncSetAttribute(k_scannd_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize,

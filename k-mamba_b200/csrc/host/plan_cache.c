@@ -54,7 +54,7 @@ static int build(const long *dims, long nd, PlanSlot *slot) {
     n_st = (size_t)pl->max_level + 2;
     n_off = (size_t)pl->total_points;
     n_pn = (size_t)pl->total_points * (size_t)nd;
-    total = n_st + n_off + 2 * n_pn;
+    total = n_st + n_off + 4 * n_pn;
     host = (int *)malloc(total * sizeof(int));
     if (!host) {
         km_wavefront_plan_free(pl);
@@ -73,6 +73,16 @@ static int build(const long *dims, long nd, PlanSlot *slot) {
                 next[p * nd + a] = co[a] + 1 < dims[a] ? (int)(p + strides[a]) : -1;
             }
         }
+        /* the same tables in level-slot order, so a kernel reading slot s
+         * gets a point's neighbours without first loading its offset */
+        int *sprev = next + n_pn;
+        int *snext = sprev + n_pn;
+        const int *off = host + n_st;
+        for (size_t s = 0; s < n_off; ++s)
+            for (long a = 0; a < nd; ++a) {
+                sprev[s * nd + a] = prev[(size_t)off[s] * nd + a];
+                snext[s * nd + a] = next[(size_t)off[s] * nd + a];
+            }
     }
     e = cudaMalloc((void **)&slot->buf, total * sizeof(int));
     if (e == cudaSuccess)
@@ -88,6 +98,8 @@ static int build(const long *dims, long nd, PlanSlot *slot) {
     slot->plan.lvl_off = slot->buf + n_st;
     slot->plan.prev = slot->buf + n_st + n_off;
     slot->plan.next = slot->buf + n_st + n_off + n_pn;
+    slot->plan.sprev = slot->buf + n_st + n_off + 2 * n_pn;
+    slot->plan.snext = slot->buf + n_st + n_off + 3 * n_pn;
     slot->plan.P = pl->total_points;
     slot->plan.nlevels = (int)(pl->max_level + 1);
     slot->plan.nd = (int)nd;

@@ -89,6 +89,8 @@ static int run(const KmbScanND *a, int bwd) {
     L.lvl_off = plan.lvl_off;
     L.prev = plan.prev;
     L.next = plan.next;
+    L.sprev = plan.sprev;
+    L.snext = plan.snext;
     L.P = P;
     L.D = a->D;
     L.M = a->M;
@@ -208,6 +210,8 @@ void scan2d(Scan2DParams *p) {
         L.lvl_off = plan.lvl_off;
         L.prev = plan.prev;
         L.next = plan.next;
+        L.sprev = plan.sprev;
+        L.snext = plan.snext;
         L.P = P;
         L.D = p->D;
         L.M = p->M;

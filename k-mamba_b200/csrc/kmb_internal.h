@@ -50,6 +50,7 @@ typedef struct {
     float *dA[KMB_MAX_AXES];
     float *ddelta[KMB_MAX_AXES];
     const int *lvl_start, *lvl_off, *prev, *next;
+    const int *sprev, *snext; /* prev / next in level-slot order */
     long P, D, M, batch;
     long delta_bstride; /* floats between batch items of each delta axis */
     long dims[KMB_MAX_AXES];
@@ -120,6 +121,8 @@ typedef struct {
     const int *lvl_off;   /* [P] */
     const int *prev;      /* [P * nd] */
     const int *next;      /* [P * nd] */
+    const int *sprev;     /* [P * nd]: prev of the point in level slot s at [s * nd] */
+    const int *snext;     /* [P * nd]: next, in the same slot order */
     long P;
     int nlevels;
     int nd;

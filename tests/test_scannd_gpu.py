@@ -156,7 +156,12 @@ def test_scan2d_vs_oracle(lib, cuda, oracle, d1, d2, D, M):
                                              # strips with a ragged last one, more rows
                                              # than the staging ring, M 8 and 12
                                              ([70, 130], 16, 16, True), ([9, 64], 8, 8, True),
-                                             ([150, 20], 24, 12, True), ([1, 200], 8, 16, True)])
+                                             ([150, 20], 24, 12, True), ([1, 200], 8, 16, True),
+                                             # warp-per-point 3D / 4D kernels (channel-shared
+                                             # B/C, M % 4 == 0 <= 16, D % 8 == 0)
+                                             ([5, 6, 7], 16, 16, True), ([4, 5, 3], 8, 4, True),
+                                             ([9, 2, 10], 24, 12, True), ([8, 8, 8], 64, 16, True),
+                                             ([3, 4, 5, 2], 8, 8, True), ([1, 7, 1], 8, 16, True)])
 def test_batched_fwd_bwd_vs_oracle(lib, cuda, oracle, dims, D, M, shared):
     import torch
     declare(lib)
