@@ -366,6 +366,96 @@ def run_secondary(args):
 
 
 # --------------------------------------------------------------------------
+# config 5 at kernel level: one Mamba-ND layer's ConvND + ND scan over 64^3
+# --------------------------------------------------------------------------
+
+def run_nd5(args):
+    """Kernel-level stand-in for BASELINE config 5, whose 24-layer model is
+    not built: one layer's causal depthwise ConvND (K 3) and 3-axis ND
+    selective scan (N 16, B/C shared across channels, per-axis A and delta),
+    forward and backward, over 64^3 volumes with dim channels (default
+    1024), batch per GPU (default 1: the reference API's state history h and
+    the backward's adjoint G are [P, D, N] each, 17 GB per item at dim
+    1024).  Reports volume tokens per second of that layer; no projection
+    GEMMs, gating or optimizer step are in the timed region."""
+    import torch
+    import kmamba_b200 as kb
+    lib = kb.load()
+    stream = torch.cuda.current_stream()
+    lib.kmb_set_stream(C.c_void_p(stream.cuda_stream))
+    lib.kmb_set_sync(0)
+    bsz = args.batch or 1
+    dims, Dc, Nn, K = [64, 64, 64], 1024, 16, 3
+    nd, Pn = 3, 64 ** 3
+    g = torch.Generator(device="cuda").manual_seed(1234)
+    rn = lambda *sh: torch.randn(*sh, device="cuda", generator=g)  # noqa: E731
+    x = rn(bsz, Pn, Dc)
+    delta = (torch.nn.functional.softplus(rn(bsz, nd, Pn, Dc) - 2) + float(np.log(3))).contiguous()
+    A = -torch.exp(torch.rand(nd, Dc, Nn, device="cuda", generator=g) * float(np.log(16)))
+    B, Cm, dy = rn(bsz, Pn, Nn), rn(bsz, Pn, Nn), rn(bsz, Pn, Dc)
+    h = torch.empty((bsz, Pn, Dc, Nn), device="cuda")
+    y, dx = torch.empty_like(x), torch.empty_like(x)
+    ddl, dA, dB, dC = (torch.empty_like(t) for t in (delta, A, B, Cm))
+    ker, bias = rn(K ** nd, Dc) / 5, rn(Dc) * 0.1
+    cout, cdin = torch.empty_like(x), torch.empty_like(x)
+    dk, db = torch.empty_like(ker), torch.empty_like(bias)
+
+    class KmbScanND(C.Structure):
+        _fields_ = [(n, C.c_void_p) for n in ("x", "delta", "A", "B", "C", "h", "y", "dy",
+                                              "dx", "ddelta", "dA", "dB", "dC")] + [
+            ("dims", C.c_long * 8), ("ndims", C.c_long), ("batch", C.c_long),
+            ("D", C.c_long), ("M", C.c_long), ("bc_shared", C.c_int), ("flags", C.c_int)]
+    a = KmbScanND()
+    a.x, a.delta, a.A, a.B, a.C, a.h, a.y = (t.data_ptr() for t in (x, delta, A, B, Cm, h, y))
+    a.dy, a.dx, a.ddelta, a.dA, a.dB, a.dC = (t.data_ptr() for t in (dy, dx, ddl, dA, dB, dC))
+    for i, v in enumerate(dims):
+        a.dims[i] = v
+    a.ndims, a.batch, a.D, a.M, a.bc_shared = nd, bsz, Dc, Nn, 1
+    lib.kmb_scannd_fwd.argtypes = [C.c_void_p]
+    lib.kmb_scannd_bwd.argtypes = [C.c_void_p]
+    c = kb.KmbConvND()
+    c.input, c.kernel, c.bias, c.output = (t.data_ptr() for t in (x, ker, bias, cout))
+    c.dy, c.dinput, c.dkernel, c.dbias = (t.data_ptr() for t in (dy, cdin, dk, db))
+    for i, v in enumerate(dims):
+        c.dims[i] = v
+    c.ndims, c.batch, c.D, c.K = nd, bsz, Dc, K
+    ops = (("conv_fwd", lambda: kb.check(lib, lib.kmb_convnd_fwd(C.byref(c)))),
+           ("scan_fwd", lambda: kb.check(lib, lib.kmb_scannd_fwd(C.byref(a)))),
+           ("scan_bwd", lambda: kb.check(lib, lib.kmb_scannd_bwd(C.byref(a)))),
+           ("conv_bwd", lambda: kb.check(lib, lib.kmb_convnd_bwd(C.byref(c)))))
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+    for _ in range(args.warmup):
+        for _, f in ops:
+            f()
+    torch.cuda.synchronize()
+    marks = [[ev() for _ in range(len(ops) + 1)] for _ in range(args.steps)]
+    with Clocks(0) as clk:
+        for m in marks:
+            m[0].record(stream)
+            for i, (_, f) in enumerate(ops):
+                f()
+                m[i + 1].record(stream)
+        torch.cuda.synchronize()
+    per = {name: sum(m[i].elapsed_time(m[i + 1]) for m in marks) / args.steps
+           for i, (name, _) in enumerate(ops)}
+    ms = sum(per.values())
+    E = bsz * Pn * Dc
+    hbytes = 4 * E * Nn
+    print(json.dumps({
+        "metric": "Mamba-ND layer tokens/s (kernel level: ConvND 3D + ND scan 3D, fwd+bwd)",
+        "value": bsz * Pn / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"config5 kernels: 64^3 volume, dim {Dc}, N {Nn}, K {K}, "
+                               f"batch {bsz}, B/C shared, fp32 (one layer's ConvND + ND scan; "
+                               "the 24-layer model is not built)",
+                   **{k + "_ms": v for k, v in per.items()},
+                   "scan_mufu_bound_ms_per_pass": E * Nn * nd / (148 * 16 * 1.965e9) * 1e3,
+                   "scan_state_history_GB": hbytes / 1e9},
+        "gpu_launches": 5 * args.steps, "clocks": clk.summary()}), flush=True)
+
+
+# --------------------------------------------------------------------------
 # config 1: the README KMamba model through kmamba.h
 # --------------------------------------------------------------------------
 
@@ -483,7 +573,7 @@ def main():
                     help="batch items per GPU (profiling of small cases only; default: "
                          "the workload's BASELINE batch)")
     ap.add_argument("--workload", default="scan1d",
-                    choices=["scan1d", "conv3", "scan2d4", "model1"],
+                    choices=["scan1d", "conv3", "scan2d4", "model1", "nd5"],
                     help="scan1d = BASELINE config 2 (the headline); conv3 / scan2d4 time "
                          "configs 3 and 4 for their roofline evidence")
     args = ap.parse_args()
@@ -494,6 +584,9 @@ def main():
         return
     if args.workload == "model1":
         run_model1(args)
+        return
+    if args.workload == "nd5":
+        run_nd5(args)
         return
     if args.workload != "scan1d":
         run_secondary(args)
