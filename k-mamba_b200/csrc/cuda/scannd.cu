@@ -228,65 +228,66 @@ __global__ void __launch_bounds__(kWWarps * 32) k_scannd_fwd_w(NDDev p) {
     const int c = lane >> 2, q = lane & 3;
     const long b = blockIdx.y;
     const long d = (long)blockIdx.x * kWCh + c;
-    const long D = p.D, M = p.M;
-    const bool qok = q * 4 < M;
+    const unsigned Du = (unsigned)p.D, Mu = (unsigned)p.M;
+    const bool qok = q * 4u < Mu;
     float2 A2[ND][2];
 #pragma unroll
     for (int a = 0; a < ND; ++a)
 #pragma unroll
         for (int jp = 0; jp < 2; ++jp) {
-            const int m = q * 4 + 2 * jp;
-            A2[a][jp] = kmb_f2(m < M ? p.A[a][d * M + m] * KMB_LOG2E : 0.f,
-                               m + 1 < M ? p.A[a][d * M + m + 1] * KMB_LOG2E : 0.f);
+            const unsigned m = q * 4 + 2 * jp;
+            A2[a][jp] = kmb_f2(m < Mu ? p.A[a][d * Mu + m] * KMB_LOG2E : 0.f,
+                               m + 1 < Mu ? p.A[a][d * Mu + m + 1] * KMB_LOG2E : 0.f);
         }
-    const float *x = p.x + b * p.x_bs;
-    const float *Bb = p.B + b * p.bc_bs;
-    const float *Cb = p.C + b * p.bc_bs;
-    float *h = p.h + b * p.h_bs;
-    float *y = p.y + b * p.x_bs;
-    const float *dl[ND];
+    /* per-lane bases: a point pt is element pt * D of the [P, D] tensors
+     * (32-bit, P * D < 2^31) and row pt of the [P, M] ones; states of
+     * point pt are at hq + (pt * D) * M */
+    const float *xq = p.x + b * p.x_bs + d;
+    const float *Bq = p.B + b * p.bc_bs + q * 4;
+    const float *Cq = p.C + b * p.bc_bs + q * 4;
+    float *hq = p.h + b * p.h_bs + d * Mu + q * 4;
+    float *yq = p.y + b * p.x_bs + d;
+    const float *dq[ND];
 #pragma unroll
-    for (int a = 0; a < ND; ++a) dl[a] = p.delta[a] + b * p.dl_bs;
+    for (int a = 0; a < ND; ++a) dq[a] = p.delta[a] + b * p.dl_bs + d;
+    const int *lvl_off = p.lvl_off, *sprev = p.sprev, *lvl_start = p.lvl_start;
+    const int nlevels = p.nlevels;
 
-    for (int l = 0; l < p.nlevels; ++l) {
-        const int s0 = p.lvl_start[l], s1 = p.lvl_start[l + 1];
+    for (int l = 0; l < nlevels; ++l) {
+        const int s0 = lvl_start[l], s1 = lvl_start[l + 1];
         for (int sb = s0 + w * kWU; sb < s1; sb += kWWarps * kWU) {
             /* indices, inputs and predecessor states of kWU points */
-            long pt[kWU];
+            unsigned pt[kWU], od[kWU];
+            bool ok[kWU];
             int pv[kWU][ND];
+#pragma unroll
+            for (int u = 0; u < kWU; ++u) {
+                ok[u] = sb + u < s1;
+                const int su = ok[u] ? sb + u : s0; /* a valid slot; results unused */
+                pt[u] = (unsigned)lvl_off[su];
+                od[u] = pt[u] * Du;
+#pragma unroll
+                for (int a = 0; a < ND; ++a) pv[u][a] = ok[u] ? sprev[su * ND + a] : -1;
+            }
             float xv[kWU], dta[kWU][ND];
             float4 B4[kWU], C4[kWU], hp[kWU][ND];
 #pragma unroll
             for (int u = 0; u < kWU; ++u) {
-                pt[u] = sb + u < s1 ? p.lvl_off[sb + u] : -1;
+                xv[u] = xq[od[u]];
+#pragma unroll
+                for (int a = 0; a < ND; ++a) dta[u][a] = dq[a][od[u]];
+                if (qok) {
+                    B4[u] = *reinterpret_cast<const float4 *>(Bq + (size_t)pt[u] * Mu);
+                    C4[u] = *reinterpret_cast<const float4 *>(Cq + (size_t)pt[u] * Mu);
+                } else {
+                    B4[u] = C4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
 #pragma unroll
                 for (int a = 0; a < ND; ++a)
-                    pv[u][a] = sb + u < s1 ? p.sprev[(long)(sb + u) * ND + a] : -1;
-            }
-#pragma unroll
-            for (int u = 0; u < kWU; ++u) {
-                const bool ok = pt[u] >= 0;
-                const long ptu = ok ? pt[u] : 0;
-                xv[u] = ok ? x[ptu * D + d] : 0.f;
-#pragma unroll
-                for (int a = 0; a < ND; ++a) {
-                    dta[u][a] = ok ? dl[a][ptu * D + d] : 0.f;
-                }
-                B4[u] = C4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (ok && qok) {
-                    B4[u] = *reinterpret_cast<const float4 *>(Bb + ptu * M + q * 4);
-                    C4[u] = *reinterpret_cast<const float4 *>(Cb + ptu * M + q * 4);
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < kWU; ++u)
-#pragma unroll
-                for (int a = 0; a < ND; ++a) {
-                    hp[u][a] = make_float4(0.f, 0.f, 0.f, 0.f);
                     if (pv[u][a] >= 0 && qok)
                         hp[u][a] = *reinterpret_cast<const float4 *>(
-                            h + ((long)pv[u][a] * D + d) * M + q * 4);
-                }
+                            hq + (size_t)((unsigned)pv[u][a] * Du) * Mu);
+            }
 #pragma unroll
             for (int u = 0; u < kWU; ++u) {
                 float dt_bar = 0.f;
@@ -299,7 +300,7 @@ __global__ void __launch_bounds__(kWWarps * 32) k_scannd_fwd_w(NDDev p) {
                                 kmb_mul2(u2, kmb_mul2(kmb_f2(B4[u].z, B4[u].w), x2))};
 #pragma unroll
                 for (int a = 0; a < ND; ++a) {
-                    if (pv[u][a] >= 0) {
+                    if (pv[u][a] >= 0 && qok) {
                         const float2 dv2 = kmb_f2s(dta[u][a]);
                         const float2 e0 = kmb_exp2_decay2(kmb_mul2(dv2, A2[a][0]));
                         const float2 e1 = kmb_exp2_decay2(kmb_mul2(dv2, A2[a][1]));
@@ -307,15 +308,17 @@ __global__ void __launch_bounds__(kWWarps * 32) k_scannd_fwd_w(NDDev p) {
                         hn[1] = kmb_fma2(e1, kmb_f2(hp[u][a].z, hp[u][a].w), hn[1]);
                     }
                 }
-                if (pt[u] >= 0 && qok)
-                    *reinterpret_cast<float4 *>(h + (pt[u] * D + d) * M + q * 4) =
-                        make_float4(hn[0].x, hn[0].y, hn[1].x, hn[1].y);
                 const float2 y2 = kmb_fma2(kmb_f2(C4[u].z, C4[u].w), hn[1],
                                            kmb_mul2(kmb_f2(C4[u].x, C4[u].y), hn[0]));
                 float yv = y2.x + y2.y;
                 yv += __shfl_xor_sync(kWFull, yv, 1);
                 yv += __shfl_xor_sync(kWFull, yv, 2);
-                if (q == 0 && pt[u] >= 0) y[pt[u] * D + d] = yv;
+                if (ok[u]) {
+                    if (qok)
+                        *reinterpret_cast<float4 *>(hq + (size_t)od[u] * Mu) =
+                            make_float4(hn[0].x, hn[0].y, hn[1].x, hn[1].y);
+                    if (q == 0) yq[od[u]] = yv;
+                }
             }
         }
         __syncthreads();
@@ -563,8 +566,8 @@ void fill_dev(const KmbNDLaunch *a, NDDev *p) {
 static bool use_w(const KmbNDLaunch *a) {
     auto al = [](const void *q) { return q == nullptr || ((uintptr_t)q & 15u) == 0; };
     return (a->nd == 3 || a->nd == 4) && a->bc_shared && a->M % 4 == 0 && a->M <= 16 &&
-           a->D % kWCh == 0 && al(a->B) && al(a->C) && al(a->h) && al(a->G) && al(a->dB) &&
-           al(a->dC);
+           a->D % kWCh == 0 && a->P * a->D < (1L << 31) && al(a->B) && al(a->C) && al(a->h) &&
+           al(a->G) && al(a->dB) && al(a->dC);
 }
 
 template <int ND>
