@@ -718,6 +718,8 @@ __global__ void __launch_bounds__(256) k_conv3d_gather(ConvDev p) {
     const long yz = pt / g.X;
     const int y = (int)(yz % g.Y), z = (int)(yz / g.Y);
     const float *src = (SGN < 0 ? p.in : p.dy) + (b * p.P + pt) * p.D + c;
+    /* element strides of the three axes (P * D < 2^31) */
+    const int sz = (int)g.sz, sy = (int)g.sy, sx = (int)g.sx;
     float4 s = (SGN < 0 && p.bias) ? __ldg(reinterpret_cast<const float4 *>(p.bias + c))
                                    : V::zero();
 #pragma unroll
@@ -732,7 +734,7 @@ __global__ void __launch_bounds__(256) k_conv3d_gather(ConvDev p) {
             for (int kx = 0; kx < K; ++kx) {
                 const int ox = K - 1 - kx;
                 if (SGN < 0 ? x < ox : x + ox >= g.X) continue;
-                const long off = SGN * (oz * g.sz + oy * g.sy + ox * g.sx);
+                const int off = SGN * (oz * sz + oy * sy + ox * sx);
                 const float4 v = __ldg(reinterpret_cast<const float4 *>(src + off));
                 s = V::fma(v, taps[((kz * K + ky) * K + kx) * 16 + cg], s);
             }
@@ -741,22 +743,28 @@ __global__ void __launch_bounds__(256) k_conv3d_gather(ConvDev p) {
     *reinterpret_cast<float4 *>((SGN < 0 ? p.out : p.din) + (b * p.P + pt) * p.D + c) = s;
 }
 
-/* dkernel(k, d) = sum_q dy(q, d) in(q - (K-1-k), d), dbias(d) = sum_q dy(q, d):
- * point lane pl of a CTA walks points p0 + pl, p0 + pl + 16, ... of the
- * CTA's run; the 16 lanes of a channel group are folded in shared memory. */
+/* dkernel(k, d) = sum_q dy(q, d) in(q - (K-1-k), d), dbias(d) = sum_q dy(q, d).
+ * A CTA covers the K x K taps of one z offset (blockIdx.z = b K + kz; the
+ * kz = 0 slice also sums dbias) for a run of points: point lane pl walks
+ * points p0 + pl, p0 + pl + 16, ... with K^2 (+1) float4 accumulators, so
+ * the point's K^2 neighbour loads are issued together; the 16 lanes of a
+ * channel group are folded in shared memory. */
 template <int K>
 __global__ void __launch_bounds__(256) k_conv3d_param(ConvDev p, long run) {
     using V = Vec4p;
-    constexpr int KV = K * K * K;
+    constexpr int KK = K * K;
     __shared__ float4 red[C3_PTS * 16];
     const int tid = threadIdx.x, cg = tid & 15, pl = tid >> 4;
     const long c = (long)blockIdx.y * 64 + cg * 4;
-    const long b = blockIdx.z;
+    const long b = blockIdx.z / K;
+    const int kz = (int)(blockIdx.z % K), oz = K - 1 - kz;
+    const bool with_bias = kz == 0 && p.dbias;
     const bool cok = c < p.D;
     const Geo3 g = geo3(p);
-    float4 acc[KV + 1];
+    const int sz = (int)g.sz, sy = (int)g.sy, sx = (int)g.sx;
+    float4 acc[KK + 1];
 #pragma unroll
-    for (int k = 0; k <= KV; ++k) acc[k] = V::zero();
+    for (int k = 0; k <= KK; ++k) acc[k] = V::zero();
     const long p0 = (long)blockIdx.x * run;
     const long p1 = min(p.P, p0 + run);
     if (cok) {
@@ -766,46 +774,38 @@ __global__ void __launch_bounds__(256) k_conv3d_param(ConvDev p, long run) {
             const int y = (int)(yz % g.Y), z = (int)(yz / g.Y);
             const long o = (b * p.P + pt) * p.D + c;
             const float4 gy = __ldg(reinterpret_cast<const float4 *>(p.dy + o));
-            const float *src = p.in + o;
-            acc[KV] = V::add(acc[KV], gy);
+            if (with_bias) acc[KK] = V::add(acc[KK], gy);
+            if (z < oz) continue;
+            const float *src = p.in + o - oz * sz;
+            float4 v[KK];
 #pragma unroll
-            for (int kz = 0; kz < K; ++kz) {
-                const int oz = K - 1 - kz;
-                if (z < oz) continue;
+            for (int ky = 0; ky < K; ++ky)
 #pragma unroll
-                for (int ky = 0; ky < K; ++ky) {
-                    const int oy = K - 1 - ky;
-                    if (y < oy) continue;
-#pragma unroll
-                    for (int kx = 0; kx < K; ++kx) {
-                        const int ox = K - 1 - kx;
-                        if (x < ox) continue;
-                        const float4 v = __ldg(reinterpret_cast<const float4 *>(
-                            src - (oz * g.sz + oy * g.sy + ox * g.sx)));
-                        const int kl = (kz * K + ky) * K + kx;
-                        acc[kl] = V::fma(gy, v, acc[kl]);
-                    }
+                for (int kx = 0; kx < K; ++kx) {
+                    const int oy = K - 1 - ky, ox = K - 1 - kx;
+                    v[ky * K + kx] = (y >= oy && x >= ox)
+                        ? __ldg(reinterpret_cast<const float4 *>(src - (oy * sy + ox * sx)))
+                        : V::zero();
                 }
-            }
+#pragma unroll
+            for (int k = 0; k < KK; ++k) acc[k] = V::fma(gy, v[k], acc[k]);
         }
     }
     /* fold the 16 point lanes of each channel group, one tap at a time */
 #pragma unroll 1
-    for (int k = 0; k <= KV; ++k) {
+    for (int k = 0; k <= KK; ++k) {
+        if (k == KK && !with_bias) break;
         red[pl * 16 + cg] = acc[k];
         __syncthreads();
         if (tid < 16 && (long)blockIdx.y * 64 + tid * 4 < p.D) {
-            float4 s = red[tid];
-            for (int q = 1; q < C3_PTS; ++q) s = V::add(s, red[q * 16 + tid]);
+            float4 t = red[tid];
+            for (int q = 1; q < C3_PTS; ++q) t = V::add(t, red[q * 16 + tid]);
             const long cc = (long)blockIdx.y * 64 + tid * 4;
-            float *dst = k < KV ? p.dker + (long)k * p.D + cc : p.dbias;
-            if (k < KV || dst) {
-                if (k == KV) dst += cc;
-                atomicAdd(dst + 0, s.x);
-                atomicAdd(dst + 1, s.y);
-                atomicAdd(dst + 2, s.z);
-                atomicAdd(dst + 3, s.w);
-            }
+            float *dst = k < KK ? p.dker + (long)(kz * KK + k) * p.D + cc : p.dbias + cc;
+            atomicAdd(dst + 0, t.x);
+            atomicAdd(dst + 1, t.y);
+            atomicAdd(dst + 2, t.z);
+            atomicAdd(dst + 3, t.w);
         }
         __syncthreads();
     }
@@ -822,13 +822,13 @@ cudaError_t launch3d(const ConvDev &p, bool bwd, cudaStream_t s) {
     k_conv3d_gather<K, +1><<<grid, 256, 0, s>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    /* runs of points per CTA for dkernel: about 4 CTAs per SM in total */
-    const long ctas = (long)ct * p.batch;
-    long nrun = (4L * 148 + ctas - 1) / ctas;
+    /* runs of points per CTA for dkernel: about 8 CTAs per SM in total */
+    const long ctas = (long)ct * p.batch * K;
+    long nrun = (8L * 148 + ctas - 1) / ctas;
     if (nrun < 1) nrun = 1;
     long run = (p.P + nrun - 1) / nrun;
     run = (run + C3_PTS - 1) / C3_PTS * C3_PTS;
-    dim3 pg((unsigned)((p.P + run - 1) / run), ct, (unsigned)p.batch);
+    dim3 pg((unsigned)((p.P + run - 1) / run), ct, (unsigned)(p.batch * K));
     k_conv3d_param<K><<<pg, 256, 0, s>>>(p, run);
     return cudaGetLastError();
 }
@@ -1036,7 +1036,7 @@ extern "C" int kmb_launch_convnd_fwd(const KmbConvND *a, cudaStream_t s) {
             e = dispatch2d_fwd_ring(p, s);
         else
             e = aligned4(a, false) ? dispatch2d<4>(p, false, s) : dispatch2d<1>(p, false, s);
-    } else if (use_3d(p) && aligned4(a, false)) {
+    } else if (use_3d(p) && aligned4(a, false) && p.P * p.D < (1L << 31)) {
         e = dispatch3d(p, false, s);
     } else {
         k_convnd_fwd_generic<<<grid_for(p.batch * p.P * p.D, 256), 256, 0, s>>>(p);
@@ -1056,7 +1056,7 @@ extern "C" int kmb_launch_convnd_bwd(const KmbConvND *a, cudaStream_t s) {
         if (aligned4(a, true) && p.D % (4 * R2_CG) == 0 && p.K <= R2_KMAX)
             e = dispatch2d_bwd_ring(p, s);
         else e = aligned4(a, true) ? dispatch2d<4>(p, true, s) : dispatch2d<1>(p, true, s);
-    } else if (use_3d(p) && aligned4(a, true) && (uintptr_t)a->dkernel % 16 == 0) {
+    } else if (use_3d(p) && aligned4(a, true) && p.P * p.D < (1L << 31)) {
         e = dispatch3d(p, true, s);
     } else {
         k_convnd_bwd_input_generic<<<grid_for(p.batch * p.P * p.D, 256), 256, 0, s>>>(p);
