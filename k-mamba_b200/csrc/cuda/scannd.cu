@@ -215,15 +215,21 @@ __global__ void __launch_bounds__(kThreads) k_scannd_bwd(NDDev p) {
  * (L2-coherent) loads.
  */
 constexpr int kWCh = 8;      /* channels per CTA */
-constexpr int kWWarps = 8;   /* warps per CTA */
+/* warps per CTA (forward / backward) and points a warp keeps in flight:
+ * measured on 64^3 x 256 channels (forward / backward ms): 8 warps x 4 / 2
+ * points 23.8 / 64.0, 16 x 2 / 1 16.6 / 47.3, 32 x 1 11.8 / 48.6 (the
+ * backward spills at 64 registers) */
+constexpr int kWWarpsF = 32;
+constexpr int kWWarpsB = 16;
 constexpr unsigned kWFull = 0xffffffffu;
 
 /* points a warp keeps in flight: their index, input and predecessor loads
  * are issued before any of them is computed */
-constexpr int kWU = 4;
+constexpr int kWU = 1;
+constexpr int kWUB = 1;
 
 template <int ND>
-__global__ void __launch_bounds__(kWWarps * 32) k_scannd_fwd_w(NDDev p) {
+__global__ void __launch_bounds__(kWWarpsF * 32) k_scannd_fwd_w(NDDev p) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int c = lane >> 2, q = lane & 3;
     const long b = blockIdx.y;
@@ -255,7 +261,7 @@ __global__ void __launch_bounds__(kWWarps * 32) k_scannd_fwd_w(NDDev p) {
 
     for (int l = 0; l < nlevels; ++l) {
         const int s0 = lvl_start[l], s1 = lvl_start[l + 1];
-        for (int sb = s0 + w * kWU; sb < s1; sb += kWWarps * kWU) {
+        for (int sb = s0 + w * kWU; sb < s1; sb += kWWarpsF * kWU) {
             /* indices, inputs and predecessor states of kWU points */
             unsigned pt[kWU], od[kWU];
             bool ok[kWU];
@@ -351,7 +357,7 @@ __device__ __forceinline__ float rs8_ch(float (&v)[8], int lane) {
  *   dx = sum_m (G dt_bar) B,  ddelta_axis = sum_m (G h(p-e)) e A_axis
  *   + sum_m (G B) x / ndims,  dA_axis += (G h(p-e)) e delta_axis. */
 template <int ND>
-__global__ void __launch_bounds__(kWWarps * 32) k_scannd_bwd_w(NDDev p) {
+__global__ void __launch_bounds__(kWWarpsB * 32) k_scannd_bwd_w(NDDev p) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int c = lane >> 2, q = lane & 3;
     const long b = blockIdx.y;
@@ -386,11 +392,11 @@ __global__ void __launch_bounds__(kWWarps * 32) k_scannd_bwd_w(NDDev p) {
         dl[a] = p.delta[a] + b * p.dl_bs;
         ddl[a] = p.ddelta[a] + b * p.dl_bs;
     }
-    constexpr int U = kWU / 2; /* points in flight (the backward keeps more per point) */
+    constexpr int U = kWUB; /* points in flight (the backward keeps more per point) */
 
     for (int l = p.nlevels - 1; l >= 0; --l) {
         const int s0 = p.lvl_start[l], s1 = p.lvl_start[l + 1];
-        for (int sb = s0 + w * U; sb < s1; sb += kWWarps * U) {
+        for (int sb = s0 + w * U; sb < s1; sb += kWWarpsB * U) {
             long pt[U];
             int nx[U][ND], pv[U][ND];
 #pragma unroll
@@ -573,8 +579,8 @@ static bool use_w(const KmbNDLaunch *a) {
 template <int ND>
 static cudaError_t launch_w(const NDDev &p, const KmbNDLaunch *a, bool bwd, cudaStream_t s) {
     dim3 grid((unsigned)(a->D / kWCh), (unsigned)a->batch);
-    if (bwd) k_scannd_bwd_w<ND><<<grid, kWWarps * 32, 0, s>>>(p);
-    else k_scannd_fwd_w<ND><<<grid, kWWarps * 32, 0, s>>>(p);
+    if (bwd) k_scannd_bwd_w<ND><<<grid, kWWarpsB * 32, 0, s>>>(p);
+    else k_scannd_fwd_w<ND><<<grid, kWWarpsF * 32, 0, s>>>(p);
     return cudaGetLastError();
 }
 
