@@ -205,7 +205,8 @@ __global__ void __launch_bounds__(kThreads) k_scannd_bwd(NDDev p) {
 
 /*
  * A CTA owns one batch item and 8 channels and walks the levels in order
- * (backward: in reverse) with one CTA barrier per level, as above.  A warp
+ * (the backward's adjoint sweep: in reverse) with one CTA barrier per
+ * level, as above.  A warp
  * handles one point at a time: lane 4c + q holds channel c of the group
  * and states 4q .. 4q+3, so the predecessor states h(p - e_axis) of the
  * warp are one coalesced 512-byte row per axis, B / C rows are one float4
@@ -215,18 +216,15 @@ __global__ void __launch_bounds__(kThreads) k_scannd_bwd(NDDev p) {
  * (L2-coherent) loads.
  */
 constexpr int kWCh = 8;      /* channels per CTA */
-/* warps per CTA (forward / backward) and points a warp keeps in flight:
- * measured on 64^3 x 256 channels (forward / backward ms): 8 warps x 4 / 2
- * points 23.8 / 64.0, 16 x 2 / 1 16.6 / 47.3, 32 x 1 11.8 / 48.6 (the
- * backward spills at 64 registers) */
+/* warps per CTA of the forward and points a warp keeps in flight:
+ * measured on 64^3 x 256 channels: 8 warps x 4 points 23.8 ms, 16 x 2
+ * 16.6 ms, 32 x 1 11.8 ms */
 constexpr int kWWarpsF = 32;
-constexpr int kWWarpsB = 16;
 constexpr unsigned kWFull = 0xffffffffu;
 
 /* points a warp keeps in flight: their index, input and predecessor loads
  * are issued before any of them is computed */
 constexpr int kWU = 1;
-constexpr int kWUB = 1;
 
 template <int ND>
 __global__ void __launch_bounds__(kWWarpsF * 32) k_scannd_fwd_w(NDDev p) {
@@ -349,184 +347,223 @@ __device__ __forceinline__ float rs8_ch(float (&v)[8], int lane) {
     return v[0];
 }
 
-/* Backward of k_scannd_fwd_w, levels in reverse (the adjoint of the
- * generic backward above, same per-state terms):
- *   G(p) = C dy + sum_axis e_axis(p+e) G(p+e),   G stored in the scratch,
+/* The backward in two passes.  (A) k_scannd_adj_w walks the levels in
+ * reverse and only carries the adjoint
+ *   G(p) = C dy + sum_axis e_axis(p+e) G(p+e)
+ * into the scratch G (few registers: 32 warps per CTA).  (B)
+ * k_scannd_grad_w then has no dependency between points and runs over all
+ * of them in parallel: per point
  *   dC += dy h,  dB += G dt_bar x  (folded over the 8 channels, one
  *   128-bit atomic per point, state quad and array),
  *   dx = sum_m (G dt_bar) B,  ddelta_axis = sum_m (G h(p-e)) e A_axis
- *   + sum_m (G B) x / ndims,  dA_axis += (G h(p-e)) e delta_axis. */
+ *   + sum_m (G B) x / ndims,  dA_axis += (G h(p-e)) e delta_axis,
+ * with dA folded per CTA in shared memory (the adjoint of the generic
+ * backward above, same per-state terms). */
+constexpr int kWWarpsA = 32;
+
 template <int ND>
-__global__ void __launch_bounds__(kWWarpsB * 32) k_scannd_bwd_w(NDDev p) {
+__global__ void __launch_bounds__(kWWarpsA * 32) k_scannd_adj_w(NDDev p) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int c = lane >> 2, q = lane & 3;
     const long b = blockIdx.y;
     const long d = (long)blockIdx.x * kWCh + c;
-    const long D = p.D, M = p.M;
-    const bool qok = q * 4 < M;
+    const unsigned Du = (unsigned)p.D, Mu = (unsigned)p.M;
+    const bool qok = q * 4u < Mu;
+    float2 A2[ND][2];
+#pragma unroll
+    for (int a = 0; a < ND; ++a)
+#pragma unroll
+        for (int jp = 0; jp < 2; ++jp) {
+            const unsigned m = q * 4 + 2 * jp;
+            A2[a][jp] = kmb_f2(m < Mu ? p.A[a][d * Mu + m] * KMB_LOG2E : 0.f,
+                               m + 1 < Mu ? p.A[a][d * Mu + m + 1] * KMB_LOG2E : 0.f);
+        }
+    const float *dyq = p.dy + b * p.x_bs + d;
+    const float *Cq = p.C + b * p.bc_bs + q * 4;
+    float *Gq = p.G + b * p.h_bs + d * Mu + q * 4;
+    const float *dq[ND];
+#pragma unroll
+    for (int a = 0; a < ND; ++a) dq[a] = p.delta[a] + b * p.dl_bs + d;
+    const int *lvl_off = p.lvl_off, *snext = p.snext, *lvl_start = p.lvl_start;
+
+    for (int l = p.nlevels - 1; l >= 0; --l) {
+        const int s0 = lvl_start[l], s1 = lvl_start[l + 1];
+        for (int s = s0 + w; s < s1; s += kWWarpsA) {
+            const unsigned pt = (unsigned)lvl_off[s];
+            const unsigned od = pt * Du;
+            int nx[ND];
+#pragma unroll
+            for (int a = 0; a < ND; ++a) nx[a] = snext[s * ND + a];
+            const float gy = dyq[od];
+            float4 C4 = make_float4(0.f, 0.f, 0.f, 0.f), gn[ND];
+            float dtn[ND];
+            if (qok) C4 = *reinterpret_cast<const float4 *>(Cq + (size_t)pt * Mu);
+#pragma unroll
+            for (int a = 0; a < ND; ++a) {
+                const unsigned on = (unsigned)nx[a] * Du;
+                dtn[a] = nx[a] >= 0 ? dq[a][on] : 0.f;
+                if (nx[a] >= 0 && qok)
+                    gn[a] = *reinterpret_cast<const float4 *>(Gq + (size_t)on * Mu);
+            }
+            const float2 gy2 = kmb_f2s(gy);
+            float2 gg[2] = {kmb_mul2(kmb_f2(C4.x, C4.y), gy2), kmb_mul2(kmb_f2(C4.z, C4.w), gy2)};
+#pragma unroll
+            for (int a = 0; a < ND; ++a) {
+                if (nx[a] >= 0 && qok) {
+                    const float2 dn2 = kmb_f2s(dtn[a]);
+                    const float2 e0 = kmb_exp2_decay2(kmb_mul2(dn2, A2[a][0]));
+                    const float2 e1 = kmb_exp2_decay2(kmb_mul2(dn2, A2[a][1]));
+                    gg[0] = kmb_fma2(e0, kmb_f2(gn[a].x, gn[a].y), gg[0]);
+                    gg[1] = kmb_fma2(e1, kmb_f2(gn[a].z, gn[a].w), gg[1]);
+                }
+            }
+            if (qok)
+                *reinterpret_cast<float4 *>(Gq + (size_t)od * Mu) =
+                    make_float4(gg[0].x, gg[0].y, gg[1].x, gg[1].y);
+        }
+        __syncthreads();
+    }
+}
+
+constexpr int kGWarps = 8;    /* warps per CTA of the gradient pass */
+constexpr int kGPts = 2048;   /* points per CTA of the gradient pass */
+
+template <int ND>
+__global__ void __launch_bounds__(kGWarps * 32) k_scannd_grad_w(NDDev p) {
+    __shared__ float sdA[kGWarps][ND][32][4];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int c = lane >> 2, q = lane & 3;
+    const long b = blockIdx.z;
+    const long d = (long)blockIdx.y * kWCh + c;
+    const unsigned Du = (unsigned)p.D, Mu = (unsigned)p.M;
+    const bool qok = q * 4u < Mu;
     float2 A2[ND][2], Ar[ND][2], dAp[ND][2];
 #pragma unroll
     for (int a = 0; a < ND; ++a)
 #pragma unroll
         for (int jp = 0; jp < 2; ++jp) {
-            const int m = q * 4 + 2 * jp;
-            const float a0 = m < M ? p.A[a][d * M + m] : 0.f;
-            const float a1 = m + 1 < M ? p.A[a][d * M + m + 1] : 0.f;
+            const unsigned m = q * 4 + 2 * jp;
+            const float a0 = m < Mu ? p.A[a][d * Mu + m] : 0.f;
+            const float a1 = m + 1 < Mu ? p.A[a][d * Mu + m + 1] : 0.f;
             Ar[a][jp] = kmb_f2(a0, a1);
             A2[a][jp] = kmb_f2(a0 * KMB_LOG2E, a1 * KMB_LOG2E);
             dAp[a][jp] = kmb_f2s(0.f);
         }
-    const float *x = p.x + b * p.x_bs;
-    const float *dy = p.dy + b * p.x_bs;
-    const float *Bb = p.B + b * p.bc_bs;
-    const float *Cb = p.C + b * p.bc_bs;
-    const float *h = p.h + b * p.h_bs;
-    float *G = p.G + b * p.h_bs;
-    float *dx = p.dx + b * p.x_bs;
+    const float *xq = p.x + b * p.x_bs + d;
+    const float *dyq = p.dy + b * p.x_bs + d;
+    const float *Bq = p.B + b * p.bc_bs + q * 4;
+    const float *hq = p.h + b * p.h_bs + d * Mu + q * 4;
+    const float *Gq = p.G + b * p.h_bs + d * Mu + q * 4;
+    float *dxq = p.dx + b * p.x_bs + d;
     float *dBb = p.dB + b * p.bc_bs;
     float *dCb = p.dC + b * p.bc_bs;
-    const float *dl[ND];
-    float *ddl[ND];
+    const float *dq[ND];
+    float *ddq[ND];
 #pragma unroll
     for (int a = 0; a < ND; ++a) {
-        dl[a] = p.delta[a] + b * p.dl_bs;
-        ddl[a] = p.ddelta[a] + b * p.dl_bs;
+        dq[a] = p.delta[a] + b * p.dl_bs + d;
+        ddq[a] = p.ddelta[a] + b * p.dl_bs + d;
     }
-    constexpr int U = kWUB; /* points in flight (the backward keeps more per point) */
-
-    for (int l = p.nlevels - 1; l >= 0; --l) {
-        const int s0 = p.lvl_start[l], s1 = p.lvl_start[l + 1];
-        for (int sb = s0 + w * U; sb < s1; sb += kWWarpsB * U) {
-            long pt[U];
-            int nx[U][ND], pv[U][ND];
+    const long p0 = (long)blockIdx.x * kGPts;
+    const long p1 = min(p.P, p0 + kGPts);
+    for (long pl = p0 + w; pl < p1; pl += kGWarps) {
+        const unsigned pt = (unsigned)pl;
+        const unsigned od = pt * Du;
+        int pv[ND];
 #pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const bool ok = sb + u < s1;
-                pt[u] = ok ? p.lvl_off[sb + u] : -1;
+        for (int a = 0; a < ND; ++a) pv[a] = p.prev[(size_t)pt * ND + a];
+        const float xv = xq[od], gy = dyq[od];
+        float dta[ND];
+        float dt_bar = 0.f;
 #pragma unroll
-                for (int a = 0; a < ND; ++a) {
-                    nx[u][a] = ok ? p.snext[(long)(sb + u) * ND + a] : -1;
-                    pv[u][a] = ok ? p.sprev[(long)(sb + u) * ND + a] : -1;
-                }
-            }
-            /* every load of the U points before any arithmetic */
-            float xv[U], gy[U], dta[U][ND], dtn[U][ND];
-            float4 B4[U], C4[U], H4[U], gn[U][ND], hp[U][ND];
+        for (int a = 0; a < ND; ++a) {
+            dta[a] = dq[a][od];
+            dt_bar += dta[a];
+        }
+        dt_bar /= (float)ND;
+        float4 B4 = make_float4(0.f, 0.f, 0.f, 0.f), H4 = B4, G4 = B4, hp[ND];
+        if (qok) {
+            B4 = *reinterpret_cast<const float4 *>(Bq + (size_t)pt * Mu);
+            H4 = *reinterpret_cast<const float4 *>(hq + (size_t)od * Mu);
+            G4 = *reinterpret_cast<const float4 *>(Gq + (size_t)od * Mu);
+        }
 #pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const bool ok = pt[u] >= 0;
-                const long od = (ok ? pt[u] : 0) * D + d;
-                xv[u] = ok ? x[od] : 0.f;
-                gy[u] = ok ? dy[od] : 0.f;
-                const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
-                B4[u] = C4[u] = H4[u] = z4;
-                if (ok && qok) {
-                    B4[u] = *reinterpret_cast<const float4 *>(Bb + pt[u] * M + q * 4);
-                    C4[u] = *reinterpret_cast<const float4 *>(Cb + pt[u] * M + q * 4);
-                    H4[u] = *reinterpret_cast<const float4 *>(h + od * M + q * 4);
-                }
+        for (int a = 0; a < ND; ++a)
+            if (pv[a] >= 0 && qok)
+                hp[a] = *reinterpret_cast<const float4 *>(hq + (size_t)((unsigned)pv[a] * Du) * Mu);
+        const float2 gg[2] = {kmb_f2(G4.x, G4.y), kmb_f2(G4.z, G4.w)};
+        const float2 Bp[2] = {kmb_f2(B4.x, B4.y), kmb_f2(B4.z, B4.w)};
+        const float2 gy2 = kmb_f2s(gy), dtb2 = kmb_f2s(dt_bar), xv2 = kmb_f2s(xv);
+        float2 sx2 = kmb_f2s(0.f), sb2 = kmb_f2s(0.f), sdt2[ND];
+        float v8[8];
 #pragma unroll
-                for (int a = 0; a < ND; ++a) {
-                    dta[u][a] = ok ? dl[a][od] : 0.f;
-                    const long on = (long)nx[u][a] * D + d, op = (long)pv[u][a] * D + d;
-                    dtn[u][a] = nx[u][a] >= 0 ? dl[a][on] : 0.f;
-                    gn[u][a] = hp[u][a] = z4;
-                    if (qok && nx[u][a] >= 0)
-                        gn[u][a] = *reinterpret_cast<const float4 *>(G + on * M + q * 4);
-                    if (qok && pv[u][a] >= 0)
-                        hp[u][a] = *reinterpret_cast<const float4 *>(h + op * M + q * 4);
-                }
-            }
+        for (int jp = 0; jp < 2; ++jp) {
+            sx2 = kmb_fma2(kmb_mul2(gg[jp], dtb2), Bp[jp], sx2);
+            sb2 = kmb_fma2(kmb_mul2(gg[jp], Bp[jp]), xv2, sb2);
+            const float2 vb = kmb_mul2(kmb_mul2(gg[jp], dtb2), xv2); /* dB */
+            const float2 vc = kmb_mul2(gy2, jp ? kmb_f2(H4.z, H4.w) : kmb_f2(H4.x, H4.y));
+            v8[2 * jp] = vb.x;
+            v8[2 * jp + 1] = vb.y;
+            v8[4 + 2 * jp] = vc.x;
+            v8[4 + 2 * jp + 1] = vc.y;
+        }
 #pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const long od = (pt[u] >= 0 ? pt[u] : 0) * D + d;
-                float dt_bar = 0.f;
-#pragma unroll
-                for (int a = 0; a < ND; ++a) dt_bar += dta[u][a];
-                dt_bar /= (float)ND;
-                const float2 gy2 = kmb_f2s(gy[u]);
-                float2 gg[2] = {kmb_mul2(kmb_f2(C4[u].x, C4[u].y), gy2),
-                                kmb_mul2(kmb_f2(C4[u].z, C4[u].w), gy2)};
-#pragma unroll
-                for (int a = 0; a < ND; ++a) {
-                    if (nx[u][a] >= 0) {
-                        const float2 dn2 = kmb_f2s(dtn[u][a]);
-                        const float2 e0 = kmb_exp2_decay2(kmb_mul2(dn2, A2[a][0]));
-                        const float2 e1 = kmb_exp2_decay2(kmb_mul2(dn2, A2[a][1]));
-                        gg[0] = kmb_fma2(e0, kmb_f2(gn[u][a].x, gn[u][a].y), gg[0]);
-                        gg[1] = kmb_fma2(e1, kmb_f2(gn[u][a].z, gn[u][a].w), gg[1]);
-                    }
-                }
-                if (pt[u] >= 0 && qok)
-                    *reinterpret_cast<float4 *>(G + od * M + q * 4) =
-                        make_float4(gg[0].x, gg[0].y, gg[1].x, gg[1].y);
-                const float2 Bp[2] = {kmb_f2(B4[u].x, B4[u].y), kmb_f2(B4[u].z, B4[u].w)};
-                const float2 dtb2 = kmb_f2s(dt_bar), xv2 = kmb_f2s(xv[u]);
-                float2 sx2 = kmb_f2s(0.f), sb2 = kmb_f2s(0.f), sdt2[ND];
-                float v8[8];
+        for (int a = 0; a < ND; ++a) {
+            sdt2[a] = kmb_f2s(0.f);
+            if (pv[a] >= 0 && qok) {
+                const float2 dv2 = kmb_f2s(dta[a]);
+                const float2 hpp[2] = {kmb_f2(hp[a].x, hp[a].y), kmb_f2(hp[a].z, hp[a].w)};
 #pragma unroll
                 for (int jp = 0; jp < 2; ++jp) {
-                    sx2 = kmb_fma2(kmb_mul2(gg[jp], dtb2), Bp[jp], sx2);
-                    sb2 = kmb_fma2(kmb_mul2(gg[jp], Bp[jp]), xv2, sb2);
-                    const float2 vb = kmb_mul2(kmb_mul2(gg[jp], dtb2), xv2); /* dB */
-                    const float2 vc =
-                        kmb_mul2(gy2, jp ? kmb_f2(H4[u].z, H4[u].w) : kmb_f2(H4[u].x, H4[u].y));
-                    v8[2 * jp] = vb.x;
-                    v8[2 * jp + 1] = vb.y;
-                    v8[4 + 2 * jp] = vc.x;
-                    v8[4 + 2 * jp + 1] = vc.y;
-                }
-#pragma unroll
-                for (int a = 0; a < ND; ++a) {
-                    sdt2[a] = kmb_f2s(0.f);
-                    if (pv[u][a] >= 0) {
-                        const float2 dv2 = kmb_f2s(dta[u][a]);
-                        const float2 hpp[2] = {kmb_f2(hp[u][a].x, hp[u][a].y),
-                                               kmb_f2(hp[u][a].z, hp[u][a].w)};
-#pragma unroll
-                        for (int jp = 0; jp < 2; ++jp) {
-                            const float2 e = kmb_exp2_decay2(kmb_mul2(dv2, A2[a][jp]));
-                            const float2 gh = kmb_mul2(kmb_mul2(gg[jp], hpp[jp]), e);
-                            dAp[a][jp] = kmb_fma2(gh, dv2, dAp[a][jp]);
-                            sdt2[a] = kmb_fma2(gh, Ar[a][jp], sdt2[a]);
-                        }
-                    }
-                }
-                /* sums over the 16 states (the 4 lanes of a channel) */
-                float sx = sx2.x + sx2.y, sbv = sb2.x + sb2.y, sdt[ND];
-#pragma unroll
-                for (int a = 0; a < ND; ++a) sdt[a] = sdt2[a].x + sdt2[a].y;
-#pragma unroll
-                for (int o = 1; o <= 2; o <<= 1) {
-                    sx += __shfl_xor_sync(kWFull, sx, o);
-                    sbv += __shfl_xor_sync(kWFull, sbv, o);
-#pragma unroll
-                    for (int a = 0; a < ND; ++a) sdt[a] += __shfl_xor_sync(kWFull, sdt[a], o);
-                }
-                if (q == 0 && pt[u] >= 0) {
-                    dx[od] = sx;
-#pragma unroll
-                    for (int a = 0; a < ND; ++a) ddl[a][od] = sdt[a] + sbv / (float)ND;
-                }
-                /* dB / dC: sums over the 8 channels, then 4 states into one lane */
-                const float r1 = rs8_ch(v8, lane);
-                const float r2 = __shfl_down_sync(kWFull, r1, 4);
-                const float r3 = __shfl_down_sync(kWFull, r1, 8);
-                const float r4 = __shfl_down_sync(kWFull, r1, 12);
-                if ((c & 3) == 0 && qok && pt[u] >= 0) {
-                    float *dst = ((c >> 2) ? dCb : dBb) + pt[u] * M + q * 4;
-                    atomicAdd(reinterpret_cast<float4 *>(dst), make_float4(r1, r2, r3, r4));
+                    const float2 e = kmb_exp2_decay2(kmb_mul2(dv2, A2[a][jp]));
+                    const float2 gh = kmb_mul2(kmb_mul2(gg[jp], hpp[jp]), e);
+                    dAp[a][jp] = kmb_fma2(gh, dv2, dAp[a][jp]);
+                    sdt2[a] = kmb_fma2(gh, Ar[a][jp], sdt2[a]);
                 }
             }
         }
-        __syncthreads();
+        /* sums over the 16 states (the 4 lanes of a channel) */
+        float sx = sx2.x + sx2.y, sbv = sb2.x + sb2.y, sdt[ND];
+#pragma unroll
+        for (int a = 0; a < ND; ++a) sdt[a] = sdt2[a].x + sdt2[a].y;
+#pragma unroll
+        for (int o = 1; o <= 2; o <<= 1) {
+            sx += __shfl_xor_sync(kWFull, sx, o);
+            sbv += __shfl_xor_sync(kWFull, sbv, o);
+#pragma unroll
+            for (int a = 0; a < ND; ++a) sdt[a] += __shfl_xor_sync(kWFull, sdt[a], o);
+        }
+        if (q == 0) {
+            dxq[od] = sx;
+#pragma unroll
+            for (int a = 0; a < ND; ++a) ddq[a][od] = sdt[a] + sbv / (float)ND;
+        }
+        /* dB / dC: sums over the 8 channels, then 4 states into one lane */
+        const float r1 = rs8_ch(v8, lane);
+        const float r2 = __shfl_down_sync(kWFull, r1, 4);
+        const float r3 = __shfl_down_sync(kWFull, r1, 8);
+        const float r4 = __shfl_down_sync(kWFull, r1, 12);
+        if ((c & 3) == 0 && qok) {
+            float *dst = ((c >> 2) ? dCb : dBb) + (size_t)pt * Mu + q * 4;
+            atomicAdd(reinterpret_cast<float4 *>(dst), make_float4(r1, r2, r3, r4));
+        }
     }
+    /* dA: fold the CTA's warps, one atomic per (axis, channel, state) */
 #pragma unroll
     for (int a = 0; a < ND; ++a) {
-        const float v[4] = {dAp[a][0].x, dAp[a][0].y, dAp[a][1].x, dAp[a][1].y};
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-            if (q * 4 + j < M) atomicAdd(p.dA[a] + d * M + q * 4 + j, v[j]);
+        sdA[w][a][lane][0] = dAp[a][0].x;
+        sdA[w][a][lane][1] = dAp[a][0].y;
+        sdA[w][a][lane][2] = dAp[a][1].x;
+        sdA[w][a][lane][3] = dAp[a][1].y;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < ND * 32 * 4; i += kGWarps * 32) {
+        const int a = i / 128, ln = (i / 4) % 32, j = i % 4;
+        float t = 0.f;
+        for (int ww = 0; ww < kGWarps; ++ww) t += sdA[ww][a][ln][j];
+        const int cc = ln >> 2, qq = ln & 3;
+        const unsigned m = qq * 4 + j;
+        if (m < Mu) atomicAdd(p.dA[a] + ((long)blockIdx.y * kWCh + cc) * Mu + m, t);
     }
 }
 
@@ -579,8 +616,15 @@ static bool use_w(const KmbNDLaunch *a) {
 template <int ND>
 static cudaError_t launch_w(const NDDev &p, const KmbNDLaunch *a, bool bwd, cudaStream_t s) {
     dim3 grid((unsigned)(a->D / kWCh), (unsigned)a->batch);
-    if (bwd) k_scannd_bwd_w<ND><<<grid, kWWarpsB * 32, 0, s>>>(p);
-    else k_scannd_fwd_w<ND><<<grid, kWWarpsF * 32, 0, s>>>(p);
+    if (!bwd) {
+        k_scannd_fwd_w<ND><<<grid, kWWarpsF * 32, 0, s>>>(p);
+        return cudaGetLastError();
+    }
+    k_scannd_adj_w<ND><<<grid, kWWarpsA * 32, 0, s>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    dim3 gg((unsigned)((a->P + kGPts - 1) / kGPts), (unsigned)(a->D / kWCh), (unsigned)a->batch);
+    k_scannd_grad_w<ND><<<gg, kGWarps * 32, 0, s>>>(p);
     return cudaGetLastError();
 }
 
