@@ -162,7 +162,7 @@ def test_scan2d_vs_oracle(lib, cuda, oracle, d1, d2, D, M):
                                              ([5, 6, 7], 16, 16, True), ([4, 5, 3], 8, 4, True),
                                              ([9, 2, 10], 24, 12, True), ([8, 8, 8], 64, 16, True),
                                              ([3, 4, 5, 2], 8, 8, True), ([1, 7, 1], 8, 16, True)])
-def test_batched_fwd_bwd_vs_oracle(lib, cuda, oracle, dims, D, M, shared):
+def test_batched_fwd_bwd_vs_oracle(lib, cuda, oracle, dims, D, M, shared, weak=False):
     import torch
     declare(lib)
     rng = np.random.default_rng(sum(dims) * 7 + D + M)
@@ -174,6 +174,11 @@ def test_batched_fwd_bwd_vs_oracle(lib, cuda, oracle, dims, D, M, shared):
     B = rng.normal(0, 1, bs).astype(f32)
     Cm = rng.normal(0, 1, bs).astype(f32)
     delta = (np.log1p(np.exp(rng.normal(0, 1, (batch, nd, P, D)) - 2)) + 0.3).astype(f32)
+    if weak:
+        # weak decays (|delta A log2 e| < 1/32, the polynomial path) in every
+        # other point and on one channel everywhere; strong elsewhere
+        delta[:, :, ::2, :] *= 1e-3
+        delta[:, :, :, 1] = rng.uniform(1e-5, 1e-2, (batch, nd, P)).astype(f32)
     dy = rng.normal(0, 1, (batch, P, D)).astype(f32)
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
     tx, tA, tB, tC, tdl, tdy = map(t, (x, A, B, Cm, delta, dy))
@@ -202,3 +207,12 @@ def test_batched_fwd_bwd_vs_oracle(lib, cuda, oracle, dims, D, M, shared):
         for name, want in (("dx", dx), ("dB", dB), ("dC", dC), ("ddelta", ddl)):
             assert rel_err(g[name][b].cpu().numpy(), want) <= TOL, name
     assert rel_err(g["dA"].cpu().numpy(), dA_ref) <= TOL
+
+
+@pytest.mark.parametrize("dims,D,M", [([5, 6, 7], 16, 16), ([3, 4, 5, 2], 8, 8), ([6, 5], 8, 16)])
+def test_batched_weak_decays_vs_oracle(lib, cuda, oracle, dims, D, M):
+    """The warp-per-point (3D / 4D) and 2D wavefront kernels with weak and
+    strong decays mixed within a warp's points and channels: the
+    warp-uniform MUFU-only shortcut must fall back to the weak-decay
+    polynomial wherever a lane needs it."""
+    test_batched_fwd_bwd_vs_oracle(lib, cuda, oracle, dims, D, M, True, weak=True)
