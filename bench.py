@@ -452,7 +452,7 @@ def run_nd5(args):
                    **{k + "_ms": v for k, v in per.items()},
                    "scan_mufu_bound_ms_per_pass": E * Nn * nd / (148 * 16 * 1.965e9) * 1e3,
                    "scan_state_history_GB": hbytes / 1e9},
-        "gpu_launches": 5 * args.steps, "clocks": clk.summary()}), flush=True)
+        "gpu_launches": 6 * args.steps, "clocks": clk.summary()}), flush=True)
 
 
 # --------------------------------------------------------------------------
