@@ -385,7 +385,7 @@ def run_nd5(args):
     lib.kmb_set_stream(C.c_void_p(stream.cuda_stream))
     lib.kmb_set_sync(0)
     bsz = args.batch or 1
-    dims, Dc, Nn, K = [64, 64, 64], 1024, 16, 3
+    dims, Dc, Nn, K = [64, 64, 64], args.dim or 1024, 16, 3
     nd, Pn = 3, 64 ** 3
     g = torch.Generator(device="cuda").manual_seed(1234)
     rn = lambda *sh: torch.randn(*sh, device="cuda", generator=g)  # noqa: E731
@@ -572,6 +572,8 @@ def main():
     ap.add_argument("--batch", type=int, default=None,
                     help="batch items per GPU (profiling of small cases only; default: "
                          "the workload's BASELINE batch)")
+    ap.add_argument("--dim", type=int, default=None,
+                    help="nd5 only: channels (default 1024; smaller for profiling captures)")
     ap.add_argument("--workload", default="scan1d",
                     choices=["scan1d", "conv3", "scan2d4", "model1", "nd5"],
                     help="scan1d = BASELINE config 2 (the headline); conv3 / scan2d4 time "

@@ -425,6 +425,81 @@ __global__ void __launch_bounds__(kWWarpsA * 32) k_scannd_adj_w(NDDev p) {
     }
 }
 
+/* Gradient terms of one point for the two-pass backward below: lane
+ * 4c + q holds channel c and states 4q .. 4q+3 of the point's G, h and B,
+ * the predecessor states hp[a] (used where pv[a] >= 0), and the point's
+ * x, dy and per-axis delta.  Writes dx (dxp) and ddelta (ddq[a] + od),
+ * adds the point's dB / dC (rows dBrow / dCrow, folded over the warp's 8
+ * channels: one 128-bit atomic per state quad) and accumulates dA in dAp. */
+template <int ND>
+__device__ __forceinline__ void grad_point(
+    const float4 &B4, const float4 &H4, const float4 &G4, const float4 (&hp)[ND],
+    const int (&pv)[ND], float xv, float gy, const float (&dta)[ND],
+    const float2 (&A2)[ND][2], const float2 (&Ar)[ND][2], float2 (&dAp)[ND][2], bool qok,
+    int lane, int c, int q, float *dxp, float *const (&ddq)[ND], long od, float *dBrow,
+    float *dCrow) {
+    float dt_bar = 0.f;
+#pragma unroll
+    for (int a = 0; a < ND; ++a) dt_bar += dta[a];
+    dt_bar /= (float)ND;
+    const float2 gg[2] = {kmb_f2(G4.x, G4.y), kmb_f2(G4.z, G4.w)};
+    const float2 Bp[2] = {kmb_f2(B4.x, B4.y), kmb_f2(B4.z, B4.w)};
+    const float2 gy2 = kmb_f2s(gy), dtb2 = kmb_f2s(dt_bar), xv2 = kmb_f2s(xv);
+    float2 sx2 = kmb_f2s(0.f), sb2 = kmb_f2s(0.f), sdt2[ND];
+    float v8[8];
+#pragma unroll
+    for (int jp = 0; jp < 2; ++jp) {
+        sx2 = kmb_fma2(kmb_mul2(gg[jp], dtb2), Bp[jp], sx2);
+        sb2 = kmb_fma2(kmb_mul2(gg[jp], Bp[jp]), xv2, sb2);
+        const float2 vb = kmb_mul2(kmb_mul2(gg[jp], dtb2), xv2); /* dB */
+        const float2 vc = kmb_mul2(gy2, jp ? kmb_f2(H4.z, H4.w) : kmb_f2(H4.x, H4.y));
+        v8[2 * jp] = vb.x;
+        v8[2 * jp + 1] = vb.y;
+        v8[4 + 2 * jp] = vc.x;
+        v8[4 + 2 * jp + 1] = vc.y;
+    }
+#pragma unroll
+    for (int a = 0; a < ND; ++a) {
+        sdt2[a] = kmb_f2s(0.f);
+        if (pv[a] >= 0 && qok) {
+            const float2 dv2 = kmb_f2s(dta[a]);
+            const float2 hpp[2] = {kmb_f2(hp[a].x, hp[a].y), kmb_f2(hp[a].z, hp[a].w)};
+#pragma unroll
+            for (int jp = 0; jp < 2; ++jp) {
+                const float2 e = kmb_exp2_decay2(kmb_mul2(dv2, A2[a][jp]));
+                const float2 gh = kmb_mul2(kmb_mul2(gg[jp], hpp[jp]), e);
+                dAp[a][jp] = kmb_fma2(gh, dv2, dAp[a][jp]);
+                sdt2[a] = kmb_fma2(gh, Ar[a][jp], sdt2[a]);
+            }
+        }
+    }
+    /* sums over the 16 states (the 4 lanes of a channel) */
+    float sx = sx2.x + sx2.y, sbv = sb2.x + sb2.y, sdt[ND];
+#pragma unroll
+    for (int a = 0; a < ND; ++a) sdt[a] = sdt2[a].x + sdt2[a].y;
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) {
+        sx += __shfl_xor_sync(kWFull, sx, o);
+        sbv += __shfl_xor_sync(kWFull, sbv, o);
+#pragma unroll
+        for (int a = 0; a < ND; ++a) sdt[a] += __shfl_xor_sync(kWFull, sdt[a], o);
+    }
+    if (q == 0) {
+        dxp[0] = sx;
+#pragma unroll
+        for (int a = 0; a < ND; ++a) ddq[a][od] = sdt[a] + sbv / (float)ND;
+    }
+    /* dB / dC: sums over the 8 channels, then 4 states into one lane */
+    const float r1 = rs8_ch(v8, lane);
+    const float r2 = __shfl_down_sync(kWFull, r1, 4);
+    const float r3 = __shfl_down_sync(kWFull, r1, 8);
+    const float r4 = __shfl_down_sync(kWFull, r1, 12);
+    if ((c & 3) == 0 && qok) {
+        float *dst = ((c >> 2) ? dCrow : dBrow) + q * 4;
+        atomicAdd(reinterpret_cast<float4 *>(dst), make_float4(r1, r2, r3, r4));
+    }
+}
+
 constexpr int kGWarps = 8;    /* warps per CTA of the gradient pass */
 constexpr int kGPts = 2048;   /* points per CTA of the gradient pass */
 
@@ -474,13 +549,8 @@ __global__ void __launch_bounds__(kGWarps * 32) k_scannd_grad_w(NDDev p) {
         for (int a = 0; a < ND; ++a) pv[a] = p.prev[(size_t)pt * ND + a];
         const float xv = xq[od], gy = dyq[od];
         float dta[ND];
-        float dt_bar = 0.f;
 #pragma unroll
-        for (int a = 0; a < ND; ++a) {
-            dta[a] = dq[a][od];
-            dt_bar += dta[a];
-        }
-        dt_bar /= (float)ND;
+        for (int a = 0; a < ND; ++a) dta[a] = dq[a][od];
         float4 B4 = make_float4(0.f, 0.f, 0.f, 0.f), H4 = B4, G4 = B4, hp[ND];
         if (qok) {
             B4 = *reinterpret_cast<const float4 *>(Bq + (size_t)pt * Mu);
@@ -491,62 +561,8 @@ __global__ void __launch_bounds__(kGWarps * 32) k_scannd_grad_w(NDDev p) {
         for (int a = 0; a < ND; ++a)
             if (pv[a] >= 0 && qok)
                 hp[a] = *reinterpret_cast<const float4 *>(hq + (size_t)((unsigned)pv[a] * Du) * Mu);
-        const float2 gg[2] = {kmb_f2(G4.x, G4.y), kmb_f2(G4.z, G4.w)};
-        const float2 Bp[2] = {kmb_f2(B4.x, B4.y), kmb_f2(B4.z, B4.w)};
-        const float2 gy2 = kmb_f2s(gy), dtb2 = kmb_f2s(dt_bar), xv2 = kmb_f2s(xv);
-        float2 sx2 = kmb_f2s(0.f), sb2 = kmb_f2s(0.f), sdt2[ND];
-        float v8[8];
-#pragma unroll
-        for (int jp = 0; jp < 2; ++jp) {
-            sx2 = kmb_fma2(kmb_mul2(gg[jp], dtb2), Bp[jp], sx2);
-            sb2 = kmb_fma2(kmb_mul2(gg[jp], Bp[jp]), xv2, sb2);
-            const float2 vb = kmb_mul2(kmb_mul2(gg[jp], dtb2), xv2); /* dB */
-            const float2 vc = kmb_mul2(gy2, jp ? kmb_f2(H4.z, H4.w) : kmb_f2(H4.x, H4.y));
-            v8[2 * jp] = vb.x;
-            v8[2 * jp + 1] = vb.y;
-            v8[4 + 2 * jp] = vc.x;
-            v8[4 + 2 * jp + 1] = vc.y;
-        }
-#pragma unroll
-        for (int a = 0; a < ND; ++a) {
-            sdt2[a] = kmb_f2s(0.f);
-            if (pv[a] >= 0 && qok) {
-                const float2 dv2 = kmb_f2s(dta[a]);
-                const float2 hpp[2] = {kmb_f2(hp[a].x, hp[a].y), kmb_f2(hp[a].z, hp[a].w)};
-#pragma unroll
-                for (int jp = 0; jp < 2; ++jp) {
-                    const float2 e = kmb_exp2_decay2(kmb_mul2(dv2, A2[a][jp]));
-                    const float2 gh = kmb_mul2(kmb_mul2(gg[jp], hpp[jp]), e);
-                    dAp[a][jp] = kmb_fma2(gh, dv2, dAp[a][jp]);
-                    sdt2[a] = kmb_fma2(gh, Ar[a][jp], sdt2[a]);
-                }
-            }
-        }
-        /* sums over the 16 states (the 4 lanes of a channel) */
-        float sx = sx2.x + sx2.y, sbv = sb2.x + sb2.y, sdt[ND];
-#pragma unroll
-        for (int a = 0; a < ND; ++a) sdt[a] = sdt2[a].x + sdt2[a].y;
-#pragma unroll
-        for (int o = 1; o <= 2; o <<= 1) {
-            sx += __shfl_xor_sync(kWFull, sx, o);
-            sbv += __shfl_xor_sync(kWFull, sbv, o);
-#pragma unroll
-            for (int a = 0; a < ND; ++a) sdt[a] += __shfl_xor_sync(kWFull, sdt[a], o);
-        }
-        if (q == 0) {
-            dxq[od] = sx;
-#pragma unroll
-            for (int a = 0; a < ND; ++a) ddq[a][od] = sdt[a] + sbv / (float)ND;
-        }
-        /* dB / dC: sums over the 8 channels, then 4 states into one lane */
-        const float r1 = rs8_ch(v8, lane);
-        const float r2 = __shfl_down_sync(kWFull, r1, 4);
-        const float r3 = __shfl_down_sync(kWFull, r1, 8);
-        const float r4 = __shfl_down_sync(kWFull, r1, 12);
-        if ((c & 3) == 0 && qok) {
-            float *dst = ((c >> 2) ? dCb : dBb) + (size_t)pt * Mu + q * 4;
-            atomicAdd(reinterpret_cast<float4 *>(dst), make_float4(r1, r2, r3, r4));
-        }
+        grad_point<ND>(B4, H4, G4, hp, pv, xv, gy, dta, A2, Ar, dAp, qok, lane, c, q,
+                       dxq + od, ddq, od, dBb + (size_t)pt * Mu, dCb + (size_t)pt * Mu);
     }
     /* dA: fold the CTA's warps, one atomic per (axis, channel, state) */
 #pragma unroll
@@ -564,6 +580,297 @@ __global__ void __launch_bounds__(kGWarps * 32) k_scannd_grad_w(NDDev p) {
         const int cc = ln >> 2, qq = ln & 3;
         const unsigned m = qq * 4 + j;
         if (m < Mu) atomicAdd(p.dA[a] + ((long)blockIdx.y * kWCh + cc) * Mu + m, t);
+    }
+}
+
+/* Staged gradient pass: the per-point terms of k_scannd_grad_w with the
+ * loads batched, for M = 16.  A CTA of kSW warps takes the 8 channels of
+ * one channel group over a range of PR consecutive points (a multiple of
+ * kST; a z-slice of a 64^3 grid) and streams it in stages of kST points
+ * through a cp.async pipeline SS stages deep: per stage the G rows of its
+ * points (128 floats: 8 channels x 16 states), the h rows of their
+ * predecessors along the NF far axes (stride > kNR; the leading axes of
+ * the row-major grid), and their x, dy, delta, B and predecessor-table
+ * entries.  The points' own h rows go to a ring of R rows, from which the
+ * predecessors along the near axes (stride <= kNR) are read: kNR rows
+ * before the range are staged first.  Each warp then computes kST / kSW
+ * points of the stage from shared memory, so all global loads of a stage
+ * are in flight together.  The layout is fixed at compile time (shared
+ * memory offsets are immediates). */
+constexpr int kSW = 16; /* warps per CTA */
+constexpr int kST = 32; /* points per stage */
+constexpr int kNR = 64; /* largest axis stride read from the ring */
+
+template <int ND, int NF>
+struct GSLayout {
+    static constexpr int ROW = kWCh * 16;                    /* floats per state row */
+    static constexpr int O_G = 0;                            /* [kST][ROW] */
+    static constexpr int O_FAR = O_G + kST * ROW;            /* [NF][kST][ROW] */
+    static constexpr int O_X = O_FAR + NF * kST * ROW;       /* [2 + ND][kST][kWCh] */
+    static constexpr int O_B = O_X + (2 + ND) * kST * kWCh;  /* [kST][16] */
+    static constexpr int O_PV = O_B + kST * 16;              /* [kST][ND] ints */
+    static constexpr int STAGE = (O_PV + kST * ND + 3) & ~3;
+    static constexpr size_t bytes(int ss) {
+        return sizeof(float) * ((size_t)(ss * kST + kNR) * ROW + (size_t)ss * STAGE);
+    }
+    static constexpr int SS = bytes(3) <= 227 * 1024 ? 3 : 2; /* stages in flight */
+    /* ring rows: stage k + SS - 1 is loaded while stage k reads kNR rows back */
+    static constexpr int R = SS * kST + kNR;
+    static constexpr size_t SMEM = bytes(SS);
+    static_assert(bytes(SS) <= 227 * 1024, "staged gradient layout");
+    static_assert((2 + ND) * 2 * kST + 4 * kST <= kSW * 32, "stage copy threads");
+};
+
+struct GradS {
+    int stride[kMaxAxes]; /* point stride of each axis (row-major) */
+    int PR;               /* points per CTA, a multiple of kST */
+};
+
+/* grad_point's terms with the sums over a channel's 4 lanes reduce-
+ * scattered: lane q stores dx (q 0) or ddelta_{q-1}; a fifth value
+ * (ddelta_3 of 4 axes) is summed by butterfly and stored by lane 0. */
+template <int ND>
+__device__ __forceinline__ void grad_point16(
+    const float4 &B4, const float4 &H4, const float4 &G4, const float4 (&hp)[ND],
+    const int (&pv)[ND], float xv, float gy, const float (&dta)[ND],
+    const float2 (&A2)[ND][2], const float2 (&Ar)[ND][2], float2 (&dAp)[ND][2], int lane,
+    int c, int q, float *out0, float *out4, float *dBrow, float *dCrow) {
+    float dt_bar = 0.f;
+#pragma unroll
+    for (int a = 0; a < ND; ++a) dt_bar += dta[a];
+    dt_bar /= (float)ND;
+    const float2 gg[2] = {kmb_f2(G4.x, G4.y), kmb_f2(G4.z, G4.w)};
+    const float2 Bp[2] = {kmb_f2(B4.x, B4.y), kmb_f2(B4.z, B4.w)};
+    const float2 gy2 = kmb_f2s(gy), dtb2 = kmb_f2s(dt_bar), xv2 = kmb_f2s(xv);
+    float2 sx2 = kmb_f2s(0.f), sb2 = kmb_f2s(0.f), sdt2[ND];
+    float v8[8];
+#pragma unroll
+    for (int jp = 0; jp < 2; ++jp) {
+        const float2 gd = kmb_mul2(gg[jp], dtb2);
+        sx2 = kmb_fma2(gd, Bp[jp], sx2);
+        sb2 = kmb_fma2(kmb_mul2(gg[jp], Bp[jp]), xv2, sb2);
+        const float2 vb = kmb_mul2(gd, xv2); /* dB */
+        const float2 vc = kmb_mul2(gy2, jp ? kmb_f2(H4.z, H4.w) : kmb_f2(H4.x, H4.y));
+        v8[2 * jp] = vb.x;
+        v8[2 * jp + 1] = vb.y;
+        v8[4 + 2 * jp] = vc.x;
+        v8[4 + 2 * jp + 1] = vc.y;
+    }
+#pragma unroll
+    for (int a = 0; a < ND; ++a) {
+        sdt2[a] = kmb_f2s(0.f);
+        if (pv[a] >= 0) {
+            const float2 dv2 = kmb_f2s(dta[a]);
+            const float2 hpp[2] = {kmb_f2(hp[a].x, hp[a].y), kmb_f2(hp[a].z, hp[a].w)};
+#pragma unroll
+            for (int jp = 0; jp < 2; ++jp) {
+                const float2 e = kmb_exp2_decay2(kmb_mul2(dv2, A2[a][jp]));
+                const float2 gh = kmb_mul2(kmb_mul2(gg[jp], hpp[jp]), e);
+                dAp[a][jp] = kmb_fma2(gh, dv2, dAp[a][jp]);
+                sdt2[a] = kmb_fma2(gh, Ar[a][jp], sdt2[a]);
+            }
+        }
+    }
+    /* per-lane partial sums: dx, then ddelta_a = sum G h(p-e) e A_a + (sum G B x) / ND */
+    const float sbn = (sb2.x + sb2.y) / (float)ND;
+    float v[4] = {sx2.x + sx2.y, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int a = 0; a < ND && a < 3; ++a) v[1 + a] = sdt2[a].x + sdt2[a].y + sbn;
+    /* reduce-scatter over the channel's 4 lanes (q = lane bits 0-1) */
+    const bool hi = q & 2, lo = q & 1;
+    float k0 = hi ? v[2] : v[0], k1 = hi ? v[3] : v[1];
+    const float s0 = hi ? v[0] : v[2], s1 = hi ? v[1] : v[3];
+    k0 += __shfl_xor_sync(kWFull, s0, 2);
+    k1 += __shfl_xor_sync(kWFull, s1, 2);
+    const float keep = lo ? k1 : k0, send = lo ? k0 : k1;
+    const float mine = keep + __shfl_xor_sync(kWFull, send, 1);
+    if (q <= ND) *out0 = mine;
+    if constexpr (ND == 4) {
+        float v4 = sdt2[3].x + sdt2[3].y + sbn;
+        v4 += __shfl_xor_sync(kWFull, v4, 1);
+        v4 += __shfl_xor_sync(kWFull, v4, 2);
+        if (q == 0) *out4 = v4;
+    }
+    /* dB / dC: sums over the 8 channels, then 4 states into one lane */
+    const float r1 = rs8_ch(v8, lane);
+    const float r2 = __shfl_down_sync(kWFull, r1, 4);
+    const float r3 = __shfl_down_sync(kWFull, r1, 8);
+    const float r4 = __shfl_down_sync(kWFull, r1, 12);
+    if ((c & 3) == 0) {
+        float *dst = ((c >> 2) ? dCrow : dBrow) + q * 4;
+        atomicAdd(reinterpret_cast<float4 *>(dst), make_float4(r1, r2, r3, r4));
+    }
+}
+
+template <int ND, int NF>
+__global__ void __launch_bounds__(kSW * 32, 1) k_scannd_grad_s(NDDev p, GradS g) {
+    using L = GSLayout<ND, NF>;
+    constexpr int ROW = L::ROW, SS = L::SS, R = L::R;
+    extern __shared__ __align__(16) float sm[];
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int c = lane >> 2, q = lane & 3;
+    const long b = blockIdx.z;
+    const long d0 = (long)blockIdx.y * kWCh;
+    const long d = d0 + c;
+    float2 A2[ND][2], Ar[ND][2], dAp[ND][2];
+#pragma unroll
+    for (int a = 0; a < ND; ++a)
+#pragma unroll
+        for (int jp = 0; jp < 2; ++jp) {
+            const float *ap = p.A[a] + d * 16 + q * 4 + 2 * jp;
+            const float2 av = kmb_f2(ap[0], ap[1]);
+            Ar[a][jp] = av;
+            A2[a][jp] = kmb_f2(av.x * KMB_LOG2E, av.y * KMB_LOG2E);
+            dAp[a][jp] = kmb_f2s(0.f);
+        }
+    const long D = p.D;
+    const size_t hrow = (size_t)D * 16; /* floats between two points' state rows */
+    const float *hg = p.h + b * p.h_bs + d0 * 16 + lane * 4;
+    const float *Gg = p.G + b * p.h_bs + d0 * 16 + lane * 4;
+    const float *dlg[ND];
+#pragma unroll
+    for (int a = 0; a < ND; ++a) dlg[a] = p.delta[a] + b * p.dl_bs + d0;
+    /* this lane's output of the dx / ddelta reduce-scatter */
+    float *ob = p.dx + b * p.x_bs + d;
+#pragma unroll
+    for (int a = 0; a < ND && a < 3; ++a)
+        if (q == a + 1) ob = p.ddelta[a] + b * p.dl_bs + d;
+    float *ob4 = p.ddelta[ND - 1] + b * p.dl_bs + d; /* 4 axes: ddelta_3 */
+    float *dBb = p.dB + b * p.bc_bs, *dCb = p.dC + b * p.bc_bs;
+
+    const long pb = (long)blockIdx.x * g.PR;     /* first point computed */
+    const long pe = min(p.P, pb + (long)g.PR);   /* end of the range */
+    const long ps = pb > kNR ? pb - kNR : 0;     /* first point staged */
+    const int nst = (int)((pe - ps + kST - 1) / kST);
+    float *ring = sm;
+    float *stages = sm + R * ROW;
+
+    /* copy jobs of this thread that do not change between stages */
+    constexpr int NA = (2 + ND) * 2 * kST; /* x, dy, delta rows: 2 chunks a point */
+    const bool j_arr = tid < NA;
+    const int arr = tid / (2 * kST), aj = tid % (2 * kST);
+    const float *abase = p.x + b * p.x_bs + d0;
+    if (arr == 1) abase = p.dy + b * p.x_bs + d0;
+#pragma unroll
+    for (int a = 0; a < ND; ++a)
+        if (arr == 2 + a) abase = dlg[a];
+    const long aoff = (long)(aj >> 1) * D + (aj & 1) * 4;
+    const int adst = L::O_X + (arr * kST + (aj >> 1)) * kWCh + (aj & 1) * 4;
+    const bool j_b = tid >= NA && tid < NA + 4 * kST;
+    const int bj = tid - NA;
+    const float *bbase = p.B + b * p.bc_bs;
+    const int boff = (bj >> 2) * 16 + (bj & 3) * 4;
+    const bool j_pv = tid < ND * kST;
+
+    auto load = [&](int k) {
+        const long s0 = ps + (long)k * kST;
+        float *rs = ring + (k % (R / kST)) * kST * ROW + lane * 4;
+        float *st = stages + (k % SS) * L::STAGE;
+#pragma unroll
+        for (int u = 0; u < kST / kSW; ++u) {
+            const int r = w + u * kSW;
+            const long pt = s0 + r;
+            const bool ok = pt < pe;
+            kmb_cp_async16(rs + r * ROW, hg + (ok ? pt * hrow : 0), ok ? 16 : 0);
+        }
+        if (s0 < pb) return; /* rows before the range: the ring only */
+#pragma unroll
+        for (int u = 0; u < kST / kSW; ++u) {
+            const int r = w + u * kSW;
+            const long pt = s0 + r;
+            const bool ok = pt < pe;
+            kmb_cp_async16(st + L::O_G + r * ROW + lane * 4, Gg + (ok ? pt * hrow : 0),
+                           ok ? 16 : 0);
+#pragma unroll
+            for (int f = 0; f < NF; ++f) {
+                const long pp = pt - g.stride[f];
+                const bool okf = ok && pp >= 0;
+                kmb_cp_async16(st + L::O_FAR + (f * kST + r) * ROW + lane * 4,
+                               hg + (okf ? pp * hrow : 0), okf ? 16 : 0);
+            }
+        }
+        if (j_arr) {
+            const bool ok = s0 + (aj >> 1) < pe;
+            kmb_cp_async16(st + adst, abase + (ok ? s0 * D + aoff : 0), ok ? 16 : 0);
+        }
+        if (j_b) {
+            const bool ok = s0 + (bj >> 2) < pe;
+            kmb_cp_async16(st + L::O_B + boff, bbase + (ok ? s0 * 16 + boff : 0), ok ? 16 : 0);
+        }
+        if (j_pv) {
+            const bool ok = s0 + tid / ND < pe;
+            kmb_cp_async4(st + L::O_PV + tid, p.prev + (ok ? s0 * ND + tid : 0), ok);
+        }
+    };
+
+#pragma unroll 1
+    for (int k = 0; k < SS - 1; ++k) {
+        if (k < nst) load(k);
+        kmb_cp_async_commit();
+    }
+#pragma unroll 1
+    for (int k = 0; k < nst; ++k) {
+        kmb_cp_async_wait<SS - 2>();
+        __syncthreads();
+        if (k + SS - 1 < nst) load(k + SS - 1);
+        kmb_cp_async_commit();
+        const long s0 = ps + (long)k * kST;
+        if (s0 < pb) continue;
+        const float *st = stages + (k % SS) * L::STAGE;
+        const int *spv = reinterpret_cast<const int *>(st + L::O_PV);
+        const int sb = (k % (R / kST)) * kST; /* ring row of the stage's first point */
+        /* a warp's points interleaved (3 axes; 4 would spill) */
+        constexpr int kUnroll = ND == 3 ? kST / kSW : 1;
+#pragma unroll kUnroll
+        for (int u = 0; u < kST / kSW; ++u) {
+            const int r = w + u * kSW;
+            const long pt = s0 + r;
+            if (pt >= pe) break;
+            int pv[ND];
+            float dta[ND];
+            float4 hp[ND];
+#pragma unroll
+            for (int a = 0; a < ND; ++a) {
+                pv[a] = spv[r * ND + a];
+                dta[a] = st[L::O_X + ((2 + a) * kST + r) * kWCh + c];
+            }
+            const float xv = st[L::O_X + r * kWCh + c];
+            const float gy = st[L::O_X + (kST + r) * kWCh + c];
+            const float4 B4 = *reinterpret_cast<const float4 *>(st + L::O_B + r * 16 + q * 4);
+            const float4 G4 = *reinterpret_cast<const float4 *>(st + L::O_G + r * ROW + lane * 4);
+            const float4 H4 = *reinterpret_cast<const float4 *>(ring + (sb + r) * ROW + lane * 4);
+#pragma unroll
+            for (int a = 0; a < ND; ++a)
+                if (pv[a] >= 0) {
+                    const float *src;
+                    if (a < NF) {
+                        src = st + L::O_FAR + (a * kST + r) * ROW;
+                    } else {
+                        int sl = sb + r - g.stride[a];
+                        if (sl < 0) sl += R;
+                        src = ring + sl * ROW;
+                    }
+                    hp[a] = *reinterpret_cast<const float4 *>(src + lane * 4);
+                }
+            const long od = pt * D;
+            grad_point16<ND>(B4, H4, G4, hp, pv, xv, gy, dta, A2, Ar, dAp, lane, c, q, ob + od,
+                             ob4 + od, dBb + pt * 16, dCb + pt * 16);
+        }
+    }
+    kmb_cp_async_wait<0>();
+    __syncthreads();
+    /* dA: fold the CTA's warps, one atomic per (axis, channel, state) */
+    float *sdA = sm; /* [kSW][ND][32][4] */
+#pragma unroll
+    for (int a = 0; a < ND; ++a)
+        *reinterpret_cast<float4 *>(sdA + ((w * ND + a) * 32 + lane) * 4) =
+            make_float4(dAp[a][0].x, dAp[a][0].y, dAp[a][1].x, dAp[a][1].y);
+    __syncthreads();
+    for (int i = tid; i < ND * 32 * 4; i += kSW * 32) {
+        const int a = i / 128, ln = (i / 4) % 32, j = i % 4;
+        float t = 0.f;
+        for (int ww = 0; ww < kSW; ++ww) t += sdA[((ww * ND + a) * 32 + ln) * 4 + j];
+        atomicAdd(p.dA[a] + (d0 + (ln >> 2)) * 16 + (ln & 3) * 4 + j, t);
     }
 }
 
@@ -613,6 +920,44 @@ static bool use_w(const KmbNDLaunch *a) {
            al(a->G) && al(a->dB) && al(a->dC);
 }
 
+/* Far-axis count and range size of k_scannd_grad_s for this launch; -1
+ * when it does not apply (M != 16 or rows not 16-byte aligned:
+ * k_scannd_grad_w then runs).  Strides do not grow with the axis index,
+ * so the far axes (stride > kNR) are the leading ones. */
+static int grad_s_cfg(const KmbNDLaunch *a, GradS *g) {
+    auto al = [](const void *q) { return ((uintptr_t)q & 15u) == 0; };
+    if (a->M != 16 || !al(a->x) || !al(a->dy) || a->delta_bstride % 4 != 0) return -1;
+    for (int i = 0; i < a->nd; ++i)
+        if (!al(a->delta[i])) return -1;
+    memset(g, 0, sizeof *g);
+    long st = 1;
+    int nf = 0;
+    for (int i = a->nd - 1; i >= 0; --i) {
+        if (st > (1L << 30)) return -1;
+        g->stride[i] = (int)st;
+        st *= a->dims[i];
+    }
+    for (int i = 0; i < a->nd; ++i) nf += g->stride[i] > kNR;
+    /* points per CTA: 4096-point ranges unless the grid gets thin */
+    const long groups = a->batch * (a->D / kWCh);
+    int pr = 4096;
+    while (pr > 4 * kST && ((a->P + pr - 1) / pr) * groups < 2 * 148) pr >>= 1;
+    g->PR = pr;
+    return nf;
+}
+
+template <int ND, int NF>
+static cudaError_t launch_grad_s(const NDDev &p, const KmbNDLaunch *a, const GradS &g,
+                                 cudaStream_t s) {
+    constexpr size_t smem = GSLayout<ND, NF>::SMEM;
+    cudaError_t e = cudaFuncSetAttribute(k_scannd_grad_s<ND, NF>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    dim3 grid((unsigned)((a->P + g.PR - 1) / g.PR), (unsigned)(a->D / kWCh), (unsigned)a->batch);
+    k_scannd_grad_s<ND, NF><<<grid, kSW * 32, smem, s>>>(p, g);
+    return cudaGetLastError();
+}
+
 template <int ND>
 static cudaError_t launch_w(const NDDev &p, const KmbNDLaunch *a, bool bwd, cudaStream_t s) {
     dim3 grid((unsigned)(a->D / kWCh), (unsigned)a->batch);
@@ -623,6 +968,16 @@ static cudaError_t launch_w(const NDDev &p, const KmbNDLaunch *a, bool bwd, cuda
     k_scannd_adj_w<ND><<<grid, kWWarpsA * 32, 0, s>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
+    GradS g;
+    switch (grad_s_cfg(a, &g)) {
+    case 0: return launch_grad_s<ND, 0>(p, a, g, s);
+    case 1: return launch_grad_s<ND, 1>(p, a, g, s);
+    case 2: return launch_grad_s<ND, 2>(p, a, g, s);
+    case 3:
+        if constexpr (ND == 4) return launch_grad_s<ND, 3>(p, a, g, s);
+        break;
+    default: break;
+    }
     dim3 gg((unsigned)((a->P + kGPts - 1) / kGPts), (unsigned)(a->D / kWCh), (unsigned)a->batch);
     k_scannd_grad_w<ND><<<gg, kGWarps * 32, 0, s>>>(p);
     return cudaGetLastError();

@@ -161,7 +161,16 @@ def test_scan2d_vs_oracle(lib, cuda, oracle, d1, d2, D, M):
                                              # B/C, M % 4 == 0 <= 16, D % 8 == 0)
                                              ([5, 6, 7], 16, 16, True), ([4, 5, 3], 8, 4, True),
                                              ([9, 2, 10], 24, 12, True), ([8, 8, 8], 64, 16, True),
-                                             ([3, 4, 5, 2], 8, 8, True), ([1, 7, 1], 8, 16, True)])
+                                             ([3, 4, 5, 2], 8, 8, True), ([1, 7, 1], 8, 16, True),
+                                             # staged gradient pass (M 16): axes of stride
+                                             # > 64 fetched per stage (1, 2 and 3 such
+                                             # axes, a stride just above 64), ranges of
+                                             # 128 points with a ragged last one; M 8 on
+                                             # the same grid takes the unstaged pass
+                                             ([6, 9, 10], 8, 16, True), ([2, 5, 66], 16, 16, True),
+                                             ([3, 70, 70], 8, 16, True), ([3, 3, 9, 10], 8, 16, True),
+                                             ([2, 3, 5, 70], 8, 16, True),
+                                             ([2, 3, 5, 70], 8, 8, True)])
 def test_batched_fwd_bwd_vs_oracle(lib, cuda, oracle, dims, D, M, shared, weak=False):
     import torch
     declare(lib)
@@ -209,7 +218,8 @@ def test_batched_fwd_bwd_vs_oracle(lib, cuda, oracle, dims, D, M, shared, weak=F
     assert rel_err(g["dA"].cpu().numpy(), dA_ref) <= TOL
 
 
-@pytest.mark.parametrize("dims,D,M", [([5, 6, 7], 16, 16), ([3, 4, 5, 2], 8, 8), ([6, 5], 8, 16)])
+@pytest.mark.parametrize("dims,D,M", [([5, 6, 7], 16, 16), ([3, 4, 5, 2], 8, 8), ([6, 5], 8, 16),
+                                      ([6, 9, 10], 8, 16), ([3, 4, 5, 2], 8, 16)])
 def test_batched_weak_decays_vs_oracle(lib, cuda, oracle, dims, D, M):
     """The warp-per-point (3D / 4D) and 2D wavefront kernels with weak and
     strong decays mixed within a warp's points and channels: the
