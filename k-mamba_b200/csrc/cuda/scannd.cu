@@ -222,9 +222,6 @@ constexpr int kWCh = 8;      /* channels per CTA */
 constexpr int kWWarpsF = 32;
 constexpr unsigned kWFull = 0xffffffffu;
 
-/* points a warp keeps in flight: their index, input and predecessor loads
- * are issued before any of them is computed */
-constexpr int kWU = 1;
 
 template <int ND>
 __global__ void __launch_bounds__(kWWarpsF * 32) k_scannd_fwd_w(NDDev p) {
@@ -257,73 +254,71 @@ __global__ void __launch_bounds__(kWWarpsF * 32) k_scannd_fwd_w(NDDev p) {
     const int *lvl_off = p.lvl_off, *sprev = p.sprev, *lvl_start = p.lvl_start;
     const int nlevels = p.nlevels;
 
+    __shared__ int sidx[kWWarpsF][32][ND + 1];
     for (int l = 0; l < nlevels; ++l) {
         const int s0 = lvl_start[l], s1 = lvl_start[l + 1];
-        for (int sb = s0 + w * kWU; sb < s1; sb += kWWarpsF * kWU) {
-            /* indices, inputs and predecessor states of kWU points */
-            unsigned pt[kWU], od[kWU];
-            bool ok[kWU];
-            int pv[kWU][ND];
+        /* the warp's slots of the level are s0 + w + kWWarpsF j: lane j loads
+         * the point and predecessor indices of slot j of each batch of 32 at
+         * once into the warp's shared slot, from which they are read back
+         * point by point */
+        for (int base = s0 + w; base < s1; base += kWWarpsF * 32) {
+            const int sl = base + kWWarpsF * lane;
+            if (sl < s1) {
+                sidx[w][lane][0] = lvl_off[sl];
 #pragma unroll
-            for (int u = 0; u < kWU; ++u) {
-                ok[u] = sb + u < s1;
-                const int su = ok[u] ? sb + u : s0; /* a valid slot; results unused */
-                pt[u] = (unsigned)lvl_off[su];
-                od[u] = pt[u] * Du;
-#pragma unroll
-                for (int a = 0; a < ND; ++a) pv[u][a] = ok[u] ? sprev[su * ND + a] : -1;
+                for (int a = 0; a < ND; ++a) sidx[w][lane][1 + a] = sprev[sl * ND + a];
             }
-            float xv[kWU], dta[kWU][ND];
-            float4 B4[kWU], C4[kWU], hp[kWU][ND];
+            __syncwarp();
+            const int cnt = min(32, (s1 - base + kWWarpsF - 1) / kWWarpsF);
+            for (int j = 0; j < cnt; ++j) {
+                const unsigned pt = (unsigned)sidx[w][j][0];
+                const unsigned od = pt * Du;
+                int pv[ND];
 #pragma unroll
-            for (int u = 0; u < kWU; ++u) {
-                xv[u] = xq[od[u]];
+                for (int a = 0; a < ND; ++a) pv[a] = sidx[w][j][1 + a];
+                const float xv = xq[od];
+                float dta[ND];
+                float4 B4 = make_float4(0.f, 0.f, 0.f, 0.f), C4 = B4, hp[ND];
 #pragma unroll
-                for (int a = 0; a < ND; ++a) dta[u][a] = dq[a][od[u]];
+                for (int a = 0; a < ND; ++a) dta[a] = dq[a][od];
                 if (qok) {
-                    B4[u] = *reinterpret_cast<const float4 *>(Bq + (size_t)pt[u] * Mu);
-                    C4[u] = *reinterpret_cast<const float4 *>(Cq + (size_t)pt[u] * Mu);
-                } else {
-                    B4[u] = C4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    B4 = *reinterpret_cast<const float4 *>(Bq + (size_t)pt * Mu);
+                    C4 = *reinterpret_cast<const float4 *>(Cq + (size_t)pt * Mu);
                 }
 #pragma unroll
                 for (int a = 0; a < ND; ++a)
-                    if (pv[u][a] >= 0 && qok)
-                        hp[u][a] = *reinterpret_cast<const float4 *>(
-                            hq + (size_t)((unsigned)pv[u][a] * Du) * Mu);
-            }
-#pragma unroll
-            for (int u = 0; u < kWU; ++u) {
+                    if (pv[a] >= 0 && qok)
+                        hp[a] = *reinterpret_cast<const float4 *>(
+                            hq + (size_t)((unsigned)pv[a] * Du) * Mu);
                 float dt_bar = 0.f;
 #pragma unroll
-                for (int a = 0; a < ND; ++a) dt_bar += dta[u][a];
+                for (int a = 0; a < ND; ++a) dt_bar += dta[a];
                 dt_bar /= (float)ND;
                 /* dt_bar (B x), in the reference's association */
-                const float2 u2 = kmb_f2s(dt_bar), x2 = kmb_f2s(xv[u]);
-                float2 hn[2] = {kmb_mul2(u2, kmb_mul2(kmb_f2(B4[u].x, B4[u].y), x2)),
-                                kmb_mul2(u2, kmb_mul2(kmb_f2(B4[u].z, B4[u].w), x2))};
+                const float2 u2 = kmb_f2s(dt_bar), x2 = kmb_f2s(xv);
+                float2 hn[2] = {kmb_mul2(u2, kmb_mul2(kmb_f2(B4.x, B4.y), x2)),
+                                kmb_mul2(u2, kmb_mul2(kmb_f2(B4.z, B4.w), x2))};
 #pragma unroll
                 for (int a = 0; a < ND; ++a) {
-                    if (pv[u][a] >= 0 && qok) {
-                        const float2 dv2 = kmb_f2s(dta[u][a]);
+                    if (pv[a] >= 0 && qok) {
+                        const float2 dv2 = kmb_f2s(dta[a]);
                         const float2 e0 = kmb_exp2_decay2(kmb_mul2(dv2, A2[a][0]));
                         const float2 e1 = kmb_exp2_decay2(kmb_mul2(dv2, A2[a][1]));
-                        hn[0] = kmb_fma2(e0, kmb_f2(hp[u][a].x, hp[u][a].y), hn[0]);
-                        hn[1] = kmb_fma2(e1, kmb_f2(hp[u][a].z, hp[u][a].w), hn[1]);
+                        hn[0] = kmb_fma2(e0, kmb_f2(hp[a].x, hp[a].y), hn[0]);
+                        hn[1] = kmb_fma2(e1, kmb_f2(hp[a].z, hp[a].w), hn[1]);
                     }
                 }
-                const float2 y2 = kmb_fma2(kmb_f2(C4[u].z, C4[u].w), hn[1],
-                                           kmb_mul2(kmb_f2(C4[u].x, C4[u].y), hn[0]));
+                const float2 y2 = kmb_fma2(kmb_f2(C4.z, C4.w), hn[1],
+                                           kmb_mul2(kmb_f2(C4.x, C4.y), hn[0]));
                 float yv = y2.x + y2.y;
                 yv += __shfl_xor_sync(kWFull, yv, 1);
                 yv += __shfl_xor_sync(kWFull, yv, 2);
-                if (ok[u]) {
-                    if (qok)
-                        *reinterpret_cast<float4 *>(hq + (size_t)od[u] * Mu) =
-                            make_float4(hn[0].x, hn[0].y, hn[1].x, hn[1].y);
-                    if (q == 0) yq[od[u]] = yv;
-                }
+                if (qok)
+                    *reinterpret_cast<float4 *>(hq + (size_t)od * Mu) =
+                        make_float4(hn[0].x, hn[0].y, hn[1].x, hn[1].y);
+                if (q == 0) yq[od] = yv;
             }
+            __syncwarp(); /* the slot is rewritten by the next batch */
         }
         __syncthreads();
     }
@@ -388,38 +383,52 @@ __global__ void __launch_bounds__(kWWarpsA * 32) k_scannd_adj_w(NDDev p) {
 
     for (int l = p.nlevels - 1; l >= 0; --l) {
         const int s0 = lvl_start[l], s1 = lvl_start[l + 1];
-        for (int s = s0 + w; s < s1; s += kWWarpsA) {
-            const unsigned pt = (unsigned)lvl_off[s];
-            const unsigned od = pt * Du;
-            int nx[ND];
+        /* indices of 32 of the warp's slots loaded at once, handed out by
+         * shuffle (as in k_scannd_fwd_w) */
+        for (int base = s0 + w; base < s1; base += kWWarpsA * 32) {
+            const int sl = base + kWWarpsA * lane;
+            int myoff = 0, mynx[ND];
 #pragma unroll
-            for (int a = 0; a < ND; ++a) nx[a] = snext[s * ND + a];
-            const float gy = dyq[od];
-            float4 C4 = make_float4(0.f, 0.f, 0.f, 0.f), gn[ND];
-            float dtn[ND];
-            if (qok) C4 = *reinterpret_cast<const float4 *>(Cq + (size_t)pt * Mu);
+            for (int a = 0; a < ND; ++a) mynx[a] = -1;
+            if (sl < s1) {
+                myoff = lvl_off[sl];
 #pragma unroll
-            for (int a = 0; a < ND; ++a) {
-                const unsigned on = (unsigned)nx[a] * Du;
-                dtn[a] = nx[a] >= 0 ? dq[a][on] : 0.f;
-                if (nx[a] >= 0 && qok)
-                    gn[a] = *reinterpret_cast<const float4 *>(Gq + (size_t)on * Mu);
+                for (int a = 0; a < ND; ++a) mynx[a] = snext[sl * ND + a];
             }
-            const float2 gy2 = kmb_f2s(gy);
-            float2 gg[2] = {kmb_mul2(kmb_f2(C4.x, C4.y), gy2), kmb_mul2(kmb_f2(C4.z, C4.w), gy2)};
+            const int cnt = min(32, (s1 - base + kWWarpsA - 1) / kWWarpsA);
+            for (int j = 0; j < cnt; ++j) {
+                const unsigned pt = (unsigned)__shfl_sync(kWFull, myoff, j);
+                const unsigned od = pt * Du;
+                int nx[ND];
 #pragma unroll
-            for (int a = 0; a < ND; ++a) {
-                if (nx[a] >= 0 && qok) {
-                    const float2 dn2 = kmb_f2s(dtn[a]);
-                    const float2 e0 = kmb_exp2_decay2(kmb_mul2(dn2, A2[a][0]));
-                    const float2 e1 = kmb_exp2_decay2(kmb_mul2(dn2, A2[a][1]));
-                    gg[0] = kmb_fma2(e0, kmb_f2(gn[a].x, gn[a].y), gg[0]);
-                    gg[1] = kmb_fma2(e1, kmb_f2(gn[a].z, gn[a].w), gg[1]);
+                for (int a = 0; a < ND; ++a) nx[a] = __shfl_sync(kWFull, mynx[a], j);
+                const float gy = dyq[od];
+                float4 C4 = make_float4(0.f, 0.f, 0.f, 0.f), gn[ND];
+                float dtn[ND];
+                if (qok) C4 = *reinterpret_cast<const float4 *>(Cq + (size_t)pt * Mu);
+#pragma unroll
+                for (int a = 0; a < ND; ++a) {
+                    const unsigned on = (unsigned)nx[a] * Du;
+                    dtn[a] = nx[a] >= 0 ? dq[a][on] : 0.f;
+                    if (nx[a] >= 0 && qok)
+                        gn[a] = *reinterpret_cast<const float4 *>(Gq + (size_t)on * Mu);
                 }
+                const float2 gy2 = kmb_f2s(gy);
+                float2 gg[2] = {kmb_mul2(kmb_f2(C4.x, C4.y), gy2), kmb_mul2(kmb_f2(C4.z, C4.w), gy2)};
+#pragma unroll
+                for (int a = 0; a < ND; ++a) {
+                    if (nx[a] >= 0 && qok) {
+                        const float2 dn2 = kmb_f2s(dtn[a]);
+                        const float2 e0 = kmb_exp2_decay2(kmb_mul2(dn2, A2[a][0]));
+                        const float2 e1 = kmb_exp2_decay2(kmb_mul2(dn2, A2[a][1]));
+                        gg[0] = kmb_fma2(e0, kmb_f2(gn[a].x, gn[a].y), gg[0]);
+                        gg[1] = kmb_fma2(e1, kmb_f2(gn[a].z, gn[a].w), gg[1]);
+                    }
+                }
+                if (qok)
+                    *reinterpret_cast<float4 *>(Gq + (size_t)od * Mu) =
+                        make_float4(gg[0].x, gg[0].y, gg[1].x, gg[1].y);
             }
-            if (qok)
-                *reinterpret_cast<float4 *>(Gq + (size_t)od * Mu) =
-                    make_float4(gg[0].x, gg[0].y, gg[1].x, gg[1].y);
         }
         __syncthreads();
     }
