@@ -656,188 +656,184 @@ cudaError_t dispatch2d_bwd_ring(const ConvDev &p, cudaStream_t s) {
 /* ------------------------------------------------------------------ */
 
 /*
- * 3D causal depthwise convolution for K <= 3, D a multiple of 4 and
- * 16-byte aligned tensors.  A thread owns one point and 4 consecutive
- * channels (float4); a CTA covers 16 consecutive points (in row-major
- * z, y, x order) x 64 channels, with the block's K^3 x 64 taps in shared
- * memory.  The forward and the gather-form dinput read the K^3 neighbours
- * straight from global memory: tap offsets are compile-time multiples of
- * the axis strides, the causal bounds are checked once per axis, and the
- * neighbourhoods of adjacent points come from L1 / L2, so HBM sees one
- * read of the input and one write of the output.  dkernel / dbias keep
- * K^3 + 1 float4 accumulators per thread over a run of points and fold
- * them across the CTA in shared memory, one atomic per (tap, channel).
+ * 3D causal depthwise convolution (the Mamba-ND volumes) for K <= 3, D a
+ * multiple of 4 and 16-byte aligned tensors.  A warp owns one (y, x)
+ * column of the volume and 64 channels (2 per lane); a CTA is a 4 x 4
+ * tile of columns.  The lane keeps its channels' K^3 taps in registers
+ * and walks z, so each input slice is read
+ * once (its K x K in-plane neighbours: the tile's own columns, from L1)
+ * and feeds K rolling output accumulators:
+ *   forward (z ascending)  out(z) = bias + sum_o in(z - oz, y - oy, x - ox) w[K-1-o]
+ *   dinput  (z descending) din(z) = sum_o dy(z + oz, y + oy, x + ox) w[K-1-o]
+ * after slice s the accumulator of the output at s is complete.  dkernel
+ * keeps K^3 accumulators and a window of K dy slices instead:
+ *   dker[K-1-o] += dy(s + oz, y, x) in(s, y - oy, x - ox),  dbias += dy(s)
+ * and folds them over the CTA's 16 columns, one atomic per (tap, channel).
+ * HBM sees one read of each input and one write of each output.
  */
-constexpr int C3_PTS = 16; /* points per CTA (x 16 channel groups = 256 threads) */
+constexpr int Z3_TY = 4, Z3_TX = 4;           /* columns of a CTA */
+constexpr int Z3_CH = 64;                     /* channels of a CTA (a warp) */
+constexpr int Z3_THREADS = Z3_TY * Z3_TX * 32;
 
-struct Geo3 {
-    int Z, Y, X;
-    long sz, sy, sx; /* strides in floats of one step along z, y, x */
+struct Col3 {
+    int Z, Y, X, y, x;
+    int sz, sy;  /* element strides of z and y (P * D < 2^31) */
+    long c;      /* first of the lane's 2 channels */
+    long base;   /* element offset of (b, z = 0, y, x, c) */
+    bool on;     /* column and channels inside the volume */
 };
 
-__device__ __forceinline__ Geo3 geo3(const ConvDev &p) {
-    Geo3 g;
-    g.Z = (int)p.dims[0];
-    g.Y = (int)p.dims[1];
-    g.X = (int)p.dims[2];
-    g.sx = p.D;
-    g.sy = (long)g.X * p.D;
-    g.sz = (long)g.Y * g.X * p.D;
-    return g;
+__device__ __forceinline__ Col3 col3(const ConvDev &p) {
+    Col3 q;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    q.Z = (int)p.dims[0];
+    q.Y = (int)p.dims[1];
+    q.X = (int)p.dims[2];
+    const int ntx = (q.X + Z3_TX - 1) / Z3_TX;
+    q.y = (int)(blockIdx.x / ntx) * Z3_TY + w / Z3_TX;
+    q.x = (int)(blockIdx.x % ntx) * Z3_TX + w % Z3_TX;
+    q.c = (long)blockIdx.y * Z3_CH + lane * 2;
+    q.sy = q.X * (int)p.D;
+    q.sz = q.Y * q.sy;
+    q.base = (long)blockIdx.z * p.P * p.D + ((long)q.y * q.X + q.x) * p.D + q.c;
+    q.on = q.y < q.Y && q.x < q.X && q.c < p.D;
+    return q;
 }
 
-/* taps of this CTA's 64 channels: tap kl, channel group g at [kl * 16 + g] */
-template <int K>
-__device__ __forceinline__ void load_taps3(const ConvDev &p, float4 *taps, long c0, int tid) {
-    constexpr int KV = K * K * K;
-    for (int i = tid; i < KV * 16; i += 256) {
-        const int kl = i / 16, g = i % 16;
-        const long c = c0 + g * 4;
-        taps[i] = c < p.D ? __ldg(reinterpret_cast<const float4 *>(p.ker + kl * p.D + c))
-                          : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+__device__ __forceinline__ float2 ld2(const float *a) {
+    return __ldg(reinterpret_cast<const float2 *>(a));
 }
 
-/* SGN = -1: out(q) = bias + sum_k in(q - (K-1-k)) w_k (forward);
- * SGN = +1: din(q) = sum_k dy(q + (K-1-k)) w_k (gather form of dinput). */
+/* SGN = -1: forward; SGN = +1: dinput (gather form) */
 template <int K, int SGN>
-__global__ void __launch_bounds__(256) k_conv3d_gather(ConvDev p) {
-    using V = Vec4p;
-    constexpr int KV = K * K * K;
-    __shared__ float4 taps[KV * 16];
-    const int tid = threadIdx.x, cg = tid & 15, pl = tid >> 4;
-    const long c0 = (long)blockIdx.y * 64;
-    const long c = c0 + cg * 4;
-    const long b = blockIdx.z;
-    load_taps3<K>(p, taps, c0, tid);
-    __syncthreads();
-    const long pt = (long)blockIdx.x * C3_PTS + pl;
-    if (pt >= p.P || c >= p.D) return;
-    const Geo3 g = geo3(p);
-    const int x = (int)(pt % g.X);
-    const long yz = pt / g.X;
-    const int y = (int)(yz % g.Y), z = (int)(yz / g.Y);
-    const float *src = (SGN < 0 ? p.in : p.dy) + (b * p.P + pt) * p.D + c;
-    /* element strides of the three axes (P * D < 2^31) */
-    const int sz = (int)g.sz, sy = (int)g.sy, sx = (int)g.sx;
-    float4 s = (SGN < 0 && p.bias) ? __ldg(reinterpret_cast<const float4 *>(p.bias + c))
-                                   : V::zero();
+__global__ void __launch_bounds__(Z3_THREADS, 1) k_conv3d_zwalk(ConvDev p) {
+    constexpr int KK = K * K, KV = K * KK;
+    const Col3 q = col3(p);
+    if (!q.on) return;
+    float2 wt[KV];
 #pragma unroll
-    for (int kz = 0; kz < K; ++kz) {
-        const int oz = K - 1 - kz;
-        if (SGN < 0 ? z < oz : z + oz >= g.Z) continue;
+    for (int k = 0; k < KV; ++k) wt[k] = ld2(p.ker + k * p.D + q.c);
+    /* in-plane neighbours j = oy K + ox: offset and causal bound */
+    int off[KK];
+    bool ok[KK];
 #pragma unroll
-        for (int ky = 0; ky < K; ++ky) {
-            const int oy = K - 1 - ky;
-            if (SGN < 0 ? y < oy : y + oy >= g.Y) continue;
+    for (int oy = 0; oy < K; ++oy)
 #pragma unroll
-            for (int kx = 0; kx < K; ++kx) {
-                const int ox = K - 1 - kx;
-                if (SGN < 0 ? x < ox : x + ox >= g.X) continue;
-                const int off = SGN * (oz * sz + oy * sy + ox * sx);
-                const float4 v = __ldg(reinterpret_cast<const float4 *>(src + off));
-                s = V::fma(v, taps[((kz * K + ky) * K + kx) * 16 + cg], s);
-            }
+        for (int ox = 0; ox < K; ++ox) {
+            off[oy * K + ox] = SGN * (oy * q.sy + ox * (int)p.D);
+            ok[oy * K + ox] = SGN < 0 ? (q.y >= oy && q.x >= ox)
+                                      : (q.y + oy < q.Y && q.x + ox < q.X);
         }
-    }
-    *reinterpret_cast<float4 *>((SGN < 0 ? p.out : p.din) + (b * p.P + pt) * p.D + c) = s;
-}
-
-/* dkernel(k, d) = sum_q dy(q, d) in(q - (K-1-k), d), dbias(d) = sum_q dy(q, d).
- * A CTA covers the K x K taps of one z offset (blockIdx.z = b K + kz; the
- * kz = 0 slice also sums dbias) for a run of points: point lane pl walks
- * points p0 + pl, p0 + pl + 16, ... with K^2 (+1) float4 accumulators, so
- * the point's K^2 neighbour loads are issued together; the 16 lanes of a
- * channel group are folded in shared memory. */
-template <int K>
-__global__ void __launch_bounds__(256) k_conv3d_param(ConvDev p, long run) {
-    using V = Vec4p;
-    constexpr int KK = K * K;
-    __shared__ float4 red[C3_PTS * 16];
-    const int tid = threadIdx.x, cg = tid & 15, pl = tid >> 4;
-    const long c = (long)blockIdx.y * 64 + cg * 4;
-    const long b = blockIdx.z / K;
-    const int kz = (int)(blockIdx.z % K), oz = K - 1 - kz;
-    const bool with_bias = kz == 0 && p.dbias;
-    const bool cok = c < p.D;
-    const Geo3 g = geo3(p);
-    const int sz = (int)g.sz, sy = (int)g.sy, sx = (int)g.sx;
-    float4 acc[KK + 1];
+    const float *src = (SGN < 0 ? p.in : p.dy) + q.base;
+    float *dst = (SGN < 0 ? p.out : p.din) + q.base;
+    const float2 b2 = (SGN < 0 && p.bias) ? ld2(p.bias + q.c) : kmb_f2s(0.f);
+    float2 acc[K];
 #pragma unroll
-    for (int k = 0; k <= KK; ++k) acc[k] = V::zero();
-    const long p0 = (long)blockIdx.x * run;
-    const long p1 = min(p.P, p0 + run);
-    if (cok) {
-        for (long pt = p0 + pl; pt < p1; pt += C3_PTS) {
-            const int x = (int)(pt % g.X);
-            const long yz = pt / g.X;
-            const int y = (int)(yz % g.Y), z = (int)(yz / g.Y);
-            const long o = (b * p.P + pt) * p.D + c;
-            const float4 gy = __ldg(reinterpret_cast<const float4 *>(p.dy + o));
-            if (with_bias) acc[KK] = V::add(acc[KK], gy);
-            if (z < oz) continue;
-            const float *src = p.in + o - oz * sz;
-            float4 v[KK];
-#pragma unroll
-            for (int ky = 0; ky < K; ++ky)
-#pragma unroll
-                for (int kx = 0; kx < K; ++kx) {
-                    const int oy = K - 1 - ky, ox = K - 1 - kx;
-                    v[ky * K + kx] = (y >= oy && x >= ox)
-                        ? __ldg(reinterpret_cast<const float4 *>(src - (oy * sy + ox * sx)))
-                        : V::zero();
-                }
-#pragma unroll
-            for (int k = 0; k < KK; ++k) acc[k] = V::fma(gy, v[k], acc[k]);
-        }
-    }
-    /* fold the 16 point lanes of each channel group, one tap at a time */
+    for (int i = 0; i < K; ++i) acc[i] = b2;
+    int zo = SGN < 0 ? 0 : (q.Z - 1) * q.sz; /* offset of the current slice */
+    const int zstep = SGN < 0 ? q.sz : -q.sz;
 #pragma unroll 1
-    for (int k = 0; k <= KK; ++k) {
-        if (k == KK && !with_bias) break;
-        red[pl * 16 + cg] = acc[k];
-        __syncthreads();
-        if (tid < 16 && (long)blockIdx.y * 64 + tid * 4 < p.D) {
-            float4 t = red[tid];
-            for (int q = 1; q < C3_PTS; ++q) t = V::add(t, red[q * 16 + tid]);
-            const long cc = (long)blockIdx.y * 64 + tid * 4;
-            float *dst = k < KK ? p.dker + (long)(kz * KK + k) * p.D + cc : p.dbias + cc;
-            atomicAdd(dst + 0, t.x);
-            atomicAdd(dst + 1, t.y);
-            atomicAdd(dst + 2, t.z);
-            atomicAdd(dst + 3, t.w);
-        }
-        __syncthreads();
+    for (int t = 0; t < q.Z; ++t, zo += zstep) {
+        float2 v[KK];
+#pragma unroll
+        for (int j = 0; j < KK; ++j) v[j] = ok[j] ? ld2(src + zo + off[j]) : kmb_f2s(0.f);
+#pragma unroll
+        for (int oz = 0; oz < K; ++oz)
+#pragma unroll
+            for (int j = 0; j < KK; ++j)
+                acc[oz] = kmb_fma2(v[j], wt[KV - 1 - (oz * KK + j)], acc[oz]);
+        *reinterpret_cast<float2 *>(dst + zo) = acc[0];
+#pragma unroll
+        for (int i = 0; i + 1 < K; ++i) acc[i] = acc[i + 1];
+        acc[K - 1] = b2;
     }
 }
 
 template <int K>
-cudaError_t launch3d(const ConvDev &p, bool bwd, cudaStream_t s) {
-    const unsigned ct = (unsigned)((p.D + 63) / 64);
-    dim3 grid((unsigned)((p.P + C3_PTS - 1) / C3_PTS), ct, (unsigned)p.batch);
+__global__ void __launch_bounds__(Z3_THREADS, 1) k_conv3d_zwalk_param(ConvDev p) {
+    constexpr int KK = K * K, KV = K * KK;
+    __shared__ float2 red[Z3_THREADS / 32][32];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const Col3 q = col3(p);
+    float2 acc[KV], accb = kmb_f2s(0.f);
+#pragma unroll
+    for (int k = 0; k < KV; ++k) acc[k] = kmb_f2s(0.f);
+    if (q.on) {
+        int off[KK];
+        bool ok[KK];
+#pragma unroll
+        for (int oy = 0; oy < K; ++oy)
+#pragma unroll
+            for (int ox = 0; ox < K; ++ox) {
+                off[oy * K + ox] = -(oy * q.sy + ox * (int)p.D);
+                ok[oy * K + ox] = q.y >= oy && q.x >= ox;
+            }
+        const float *inp = p.in + q.base;
+        const float *dyp = p.dy + q.base;
+        float2 dyw[K]; /* dy of this column at slices s .. s + K - 1 */
+#pragma unroll
+        for (int i = 0; i + 1 < K; ++i) dyw[i] = i < q.Z ? ld2(dyp + i * q.sz) : kmb_f2s(0.f);
+        int zo = 0;
+#pragma unroll 1
+        for (int s = 0; s < q.Z; ++s, zo += q.sz) {
+            dyw[K - 1] = s + K - 1 < q.Z ? ld2(dyp + zo + (K - 1) * q.sz) : kmb_f2s(0.f);
+            float2 v[KK];
+#pragma unroll
+            for (int j = 0; j < KK; ++j) v[j] = ok[j] ? ld2(inp + zo + off[j]) : kmb_f2s(0.f);
+#pragma unroll
+            for (int oz = 0; oz < K; ++oz)
+#pragma unroll
+                for (int j = 0; j < KK; ++j)
+                    acc[KV - 1 - (oz * KK + j)] = kmb_fma2(dyw[oz], v[j], acc[KV - 1 - (oz * KK + j)]);
+            accb = kmb_add2(accb, dyw[0]);
+#pragma unroll
+            for (int i = 0; i + 1 < K; ++i) dyw[i] = dyw[i + 1];
+        }
+    }
+    /* fold the CTA's 16 columns, one tap at a time */
+    const int ntap = p.dbias ? KV + 1 : KV;
+#pragma unroll
+    for (int k = 0; k < KV + 1; ++k) {
+        if (k < ntap) {
+            red[w][lane] = k < KV ? acc[k] : accb;
+            __syncthreads();
+            if (w == 0 && q.c < p.D) {
+                float2 t = red[0][lane];
+                for (int ww = 1; ww < Z3_THREADS / 32; ++ww) t = kmb_add2(t, red[ww][lane]);
+                float *d = k < KV ? p.dker + k * p.D + q.c : p.dbias + q.c;
+                if (((uintptr_t)d & 7u) == 0) {
+                    atomicAdd(reinterpret_cast<float2 *>(d), t);
+                } else { /* dkernel / dbias need not be 8-byte aligned */
+                    atomicAdd(d, t.x);
+                    atomicAdd(d + 1, t.y);
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+template <int K>
+cudaError_t launch3d_zwalk(const ConvDev &p, bool bwd, cudaStream_t s) {
+    const unsigned tiles = (unsigned)(((p.dims[1] + Z3_TY - 1) / Z3_TY) *
+                                      ((p.dims[2] + Z3_TX - 1) / Z3_TX));
+    dim3 grid(tiles, (unsigned)((p.D + Z3_CH - 1) / Z3_CH), (unsigned)p.batch);
     if (!bwd) {
-        k_conv3d_gather<K, -1><<<grid, 256, 0, s>>>(p);
+        k_conv3d_zwalk<K, -1><<<grid, Z3_THREADS, 0, s>>>(p);
         return cudaGetLastError();
     }
-    k_conv3d_gather<K, +1><<<grid, 256, 0, s>>>(p);
+    k_conv3d_zwalk<K, +1><<<grid, Z3_THREADS, 0, s>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    /* runs of points per CTA for dkernel: about 8 CTAs per SM in total */
-    const long ctas = (long)ct * p.batch * K;
-    long nrun = (8L * 148 + ctas - 1) / ctas;
-    if (nrun < 1) nrun = 1;
-    long run = (p.P + nrun - 1) / nrun;
-    run = (run + C3_PTS - 1) / C3_PTS * C3_PTS;
-    dim3 pg((unsigned)((p.P + run - 1) / run), ct, (unsigned)(p.batch * K));
-    k_conv3d_param<K><<<pg, 256, 0, s>>>(p, run);
+    k_conv3d_zwalk_param<K><<<grid, Z3_THREADS, 0, s>>>(p);
     return cudaGetLastError();
 }
 
 cudaError_t dispatch3d(const ConvDev &p, bool bwd, cudaStream_t s) {
     switch (p.K) {
-    case 1: return launch3d<1>(p, bwd, s);
-    case 2: return launch3d<2>(p, bwd, s);
-    case 3: return launch3d<3>(p, bwd, s);
+    case 1: return launch3d_zwalk<1>(p, bwd, s);
+    case 2: return launch3d_zwalk<2>(p, bwd, s);
+    case 3: return launch3d_zwalk<3>(p, bwd, s);
     default: return cudaErrorNotSupported;
     }
 }

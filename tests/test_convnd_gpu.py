@@ -109,7 +109,7 @@ def dkernel_f64(dims, K, inp, dy):
     # 3D kernels (D % 4 == 0, K <= 3): partial 64-channel tiles, K 1..3,
     # edges on every axis
     ([9, 10, 11], 64, 3, True), ([5, 7, 6], 68, 2, False), ([4, 4, 33], 8, 1, True),
-    ([12, 13, 14], 128, 3, True), ([3, 1, 40], 20, 3, True)])
+    ([12, 13, 14], 128, 3, True), ([3, 1, 40], 20, 3, True), ([16, 20, 24], 192, 3, True)])
 def test_batched_vs_oracle(lib, cuda, oracle, dims, D, K, bias):
     rng = np.random.default_rng(sum(dims) * 13 + D + K)
     batch = 3
