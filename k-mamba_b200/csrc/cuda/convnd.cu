@@ -660,7 +660,8 @@ cudaError_t dispatch2d_bwd_ring(const ConvDev &p, cudaStream_t s) {
  * multiple of 4 and 16-byte aligned tensors.  A warp owns one (y, x)
  * column of the volume and 64 channels (2 per lane); a CTA is a 4 x 4
  * tile of columns.  The lane keeps its channels' K^3 taps in registers
- * and walks z, so each input slice is read
+ * and walks z (the loads of two slices issued together), so each input
+ * slice is read
  * once (its K x K in-plane neighbours: the tile's own columns, from L1)
  * and feeds K rolling output accumulators:
  *   forward (z ascending)  out(z) = bias + sum_o in(z - oz, y - oy, x - ox) w[K-1-o]
@@ -672,6 +673,7 @@ cudaError_t dispatch2d_bwd_ring(const ConvDev &p, cudaStream_t s) {
  * HBM sees one read of each input and one write of each output.
  */
 constexpr int Z3_TY = 4, Z3_TX = 4;           /* columns of a CTA */
+constexpr int Z3_UZ = 2; /* slices whose loads are issued together */
 constexpr int Z3_CH = 64;                     /* channels of a CTA (a warp) */
 constexpr int Z3_THREADS = Z3_TY * Z3_TX * 32;
 
@@ -690,9 +692,9 @@ __device__ __forceinline__ Col3 col3(const ConvDev &p) {
     q.Y = (int)p.dims[1];
     q.X = (int)p.dims[2];
     const int ntx = (q.X + Z3_TX - 1) / Z3_TX;
-    q.y = (int)(blockIdx.x / ntx) * Z3_TY + w / Z3_TX;
-    q.x = (int)(blockIdx.x % ntx) * Z3_TX + w % Z3_TX;
-    q.c = (long)blockIdx.y * Z3_CH + lane * 2;
+    q.y = (int)(blockIdx.y / ntx) * Z3_TY + w / Z3_TX;
+    q.x = (int)(blockIdx.y % ntx) * Z3_TX + w % Z3_TX;
+    q.c = (long)blockIdx.x * Z3_CH + lane * 2;
     q.sy = q.X * (int)p.D;
     q.sz = q.Y * q.sy;
     q.base = (long)blockIdx.z * p.P * p.D + ((long)q.y * q.X + q.x) * p.D + q.c;
@@ -733,19 +735,29 @@ __global__ void __launch_bounds__(Z3_THREADS, 1) k_conv3d_zwalk(ConvDev p) {
     int zo = SGN < 0 ? 0 : (q.Z - 1) * q.sz; /* offset of the current slice */
     const int zstep = SGN < 0 ? q.sz : -q.sz;
 #pragma unroll 1
-    for (int t = 0; t < q.Z; ++t, zo += zstep) {
-        float2 v[KK];
+    for (int t = 0; t < q.Z; t += Z3_UZ) {
+        /* the loads of Z3_UZ slices first, then their outputs */
+        float2 v[Z3_UZ][KK];
 #pragma unroll
-        for (int j = 0; j < KK; ++j) v[j] = ok[j] ? ld2(src + zo + off[j]) : kmb_f2s(0.f);
-#pragma unroll
-        for (int oz = 0; oz < K; ++oz)
+        for (int u = 0; u < Z3_UZ; ++u)
 #pragma unroll
             for (int j = 0; j < KK; ++j)
-                acc[oz] = kmb_fma2(v[j], wt[KV - 1 - (oz * KK + j)], acc[oz]);
-        *reinterpret_cast<float2 *>(dst + zo) = acc[0];
+                v[u][j] = ok[j] && t + u < q.Z ? ld2(src + zo + u * zstep + off[j])
+                                               : kmb_f2s(0.f);
 #pragma unroll
-        for (int i = 0; i + 1 < K; ++i) acc[i] = acc[i + 1];
-        acc[K - 1] = b2;
+        for (int u = 0; u < Z3_UZ; ++u) {
+            if (t + u >= q.Z) break;
+#pragma unroll
+            for (int oz = 0; oz < K; ++oz)
+#pragma unroll
+                for (int j = 0; j < KK; ++j)
+                    acc[oz] = kmb_fma2(v[u][j], wt[KV - 1 - (oz * KK + j)], acc[oz]);
+            *reinterpret_cast<float2 *>(dst + zo) = acc[0];
+#pragma unroll
+            for (int i = 0; i + 1 < K; ++i) acc[i] = acc[i + 1];
+            acc[K - 1] = b2;
+            zo += zstep;
+        }
     }
 }
 
@@ -775,22 +787,34 @@ __global__ void __launch_bounds__(Z3_THREADS, 1) k_conv3d_zwalk_param(ConvDev p)
         for (int i = 0; i + 1 < K; ++i) dyw[i] = i < q.Z ? ld2(dyp + i * q.sz) : kmb_f2s(0.f);
         int zo = 0;
 #pragma unroll 1
-        for (int s = 0; s < q.Z; ++s, zo += q.sz) {
-            dyw[K - 1] = s + K - 1 < q.Z ? ld2(dyp + zo + (K - 1) * q.sz) : kmb_f2s(0.f);
-            float2 v[KK];
+        for (int s = 0; s < q.Z; s += Z3_UZ) {
+            /* the loads of Z3_UZ slices first */
+            float2 v[Z3_UZ][KK], dn[Z3_UZ];
 #pragma unroll
-            for (int j = 0; j < KK; ++j) v[j] = ok[j] ? ld2(inp + zo + off[j]) : kmb_f2s(0.f);
-#pragma unroll
-            for (int oz = 0; oz < K; ++oz)
+            for (int u = 0; u < Z3_UZ; ++u) {
+                dn[u] = s + u + K - 1 < q.Z ? ld2(dyp + zo + (u + K - 1) * q.sz) : kmb_f2s(0.f);
 #pragma unroll
                 for (int j = 0; j < KK; ++j)
-                    acc[KV - 1 - (oz * KK + j)] = kmb_fma2(dyw[oz], v[j], acc[KV - 1 - (oz * KK + j)]);
-            accb = kmb_add2(accb, dyw[0]);
+                    v[u][j] = ok[j] && s + u < q.Z ? ld2(inp + zo + u * q.sz + off[j])
+                                                   : kmb_f2s(0.f);
+            }
 #pragma unroll
-            for (int i = 0; i + 1 < K; ++i) dyw[i] = dyw[i + 1];
+            for (int u = 0; u < Z3_UZ; ++u) {
+                dyw[K - 1] = dn[u];
+#pragma unroll
+                for (int oz = 0; oz < K; ++oz)
+#pragma unroll
+                    for (int j = 0; j < KK; ++j)
+                        acc[KV - 1 - (oz * KK + j)] =
+                            kmb_fma2(dyw[oz], v[u][j], acc[KV - 1 - (oz * KK + j)]);
+                accb = kmb_add2(accb, dyw[0]);
+#pragma unroll
+                for (int i = 0; i + 1 < K; ++i) dyw[i] = dyw[i + 1];
+            }
+            zo += Z3_UZ * q.sz;
         }
     }
-    /* fold the CTA's 16 columns, one tap at a time */
+    /* fold the CTA's columns, one tap at a time */
     const int ntap = p.dbias ? KV + 1 : KV;
 #pragma unroll
     for (int k = 0; k < KV + 1; ++k) {
@@ -817,7 +841,9 @@ template <int K>
 cudaError_t launch3d_zwalk(const ConvDev &p, bool bwd, cudaStream_t s) {
     const unsigned tiles = (unsigned)(((p.dims[1] + Z3_TY - 1) / Z3_TY) *
                                       ((p.dims[2] + Z3_TX - 1) / Z3_TX));
-    dim3 grid(tiles, (unsigned)((p.D + Z3_CH - 1) / Z3_CH), (unsigned)p.batch);
+    /* channel blocks fastest: the CTAs of a tile run together and read
+     * whole point vectors of each slice at about the same time */
+    dim3 grid((unsigned)((p.D + Z3_CH - 1) / Z3_CH), tiles, (unsigned)p.batch);
     if (!bwd) {
         k_conv3d_zwalk<K, -1><<<grid, Z3_THREADS, 0, s>>>(p);
         return cudaGetLastError();
