@@ -27,6 +27,8 @@
  * walked in reverse level order; G is kept in a [P,D,M] scratch buffer and
  * dA in shared memory per CTA.
  */
+#include <type_traits>
+
 #include "kmb_common.cuh"
 #include "../kmb_internal.h"
 
@@ -324,6 +326,186 @@ __global__ void __launch_bounds__(kWWarpsF * 32) k_scannd_fwd_w(NDDev p) {
     }
 }
 
+/* Smallest |A log2 e| over a lane's 4 states of one axis.  |delta| times
+ * it bounds the lane's decay exponents |delta A log2 e| from below
+ * (products round monotonically), so a bound >= KMB_DECAY_POLY_MAX means
+ * kmb_exp2_decay2 returns the MUFU values for every state. */
+__device__ __forceinline__ float lane_amin(const float2 (&A2)[2]) {
+    return fminf(fminf(fabsf(A2[0].x), fabsf(A2[0].y)), fminf(fabsf(A2[1].x), fabsf(A2[1].y)));
+}
+
+/* k_scannd_fwd_w with each warp's loads pipelined, for M = 16.  After a
+ * level's barrier the inputs of all its points and their predecessors'
+ * states are in memory, so a warp streams its points of the level
+ * through a ring of S point slots in shared memory (cp.async): the
+ * predecessor rows (kWCh x 16 states), and x, delta, B and C of point j +
+ * S - 1 are in flight while point j is computed from its slot. */
+template <int ND>
+struct FwdPSlot {
+    static constexpr int HP = 0;                 /* [ND][128] predecessor rows */
+    static constexpr int X = ND * kWCh * 16;      /* [8] */
+    static constexpr int DL = X + kWCh;           /* [ND][8] */
+    static constexpr int B = DL + ND * kWCh;      /* [16] */
+    static constexpr int C = B + 16;              /* [16] */
+    static constexpr int SIZE = C + 16;           /* floats, a multiple of 4 */
+    static constexpr int NSMALL = 2 + 2 * ND + 8; /* 16-byte chunks of x, delta, B, C */
+    static_assert(SIZE % 4 == 0 && NSMALL <= 32, "slot layout");
+};
+
+template <int ND, int S>
+__global__ void __launch_bounds__(kWWarpsF * 32) k_scannd_fwd_p(NDDev p) {
+    using L = FwdPSlot<ND>;
+    extern __shared__ __align__(16) float fsm[];
+    __shared__ int sidx[kWWarpsF][32][ND + 1];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int c = lane >> 2, q = lane & 3;
+    const long b = blockIdx.y;
+    const long d0 = (long)blockIdx.x * kWCh;
+    const long d = d0 + c;
+    const unsigned Du = (unsigned)p.D;
+    float2 A2[ND][2];
+#pragma unroll
+    for (int a = 0; a < ND; ++a)
+#pragma unroll
+        for (int jp = 0; jp < 2; ++jp) {
+            const float *ap = p.A[a] + d * 16 + q * 4 + 2 * jp;
+            A2[a][jp] = kmb_f2(ap[0] * KMB_LOG2E, ap[1] * KMB_LOG2E);
+        }
+    float amin[ND];
+#pragma unroll
+    for (int a = 0; a < ND; ++a) amin[a] = lane_amin(A2[a]);
+    float *wb = fsm + w * S * L::SIZE; /* this warp's ring of S slots */
+    const float *hg = p.h + b * p.h_bs + d0 * 16 + lane * 4; /* + point * D * 16 */
+    float *hq = p.h + b * p.h_bs + d0 * 16 + lane * 4;
+    float *yq = p.y + b * p.x_bs + d;
+    /* this lane's chunk of x, delta, B or C: source base, point multiplier
+     * and slot offset (lanes >= NSMALL copy none) */
+    const float *ssrc = p.x + b * p.x_bs + d0 + lane * 4;
+    unsigned smul = Du;
+    int sdst = L::X + lane * 4;
+#pragma unroll
+    for (int a = 0; a < ND; ++a)
+        if (lane >= 2 + 2 * a && lane < 4 + 2 * a) {
+            ssrc = p.delta[a] + b * p.dl_bs + d0 + (lane - 2 - 2 * a) * 4;
+            sdst = L::DL + a * kWCh + (lane - 2 - 2 * a) * 4;
+        }
+    if (lane >= 2 + 2 * ND && lane < 2 + 2 * ND + 4) {
+        ssrc = p.B + b * p.bc_bs + (lane - 2 - 2 * ND) * 4;
+        smul = 16;
+        sdst = L::B + (lane - 2 - 2 * ND) * 4;
+    } else if (lane >= 2 + 2 * ND + 4) {
+        ssrc = p.C + b * p.bc_bs + (lane - 6 - 2 * ND) * 4;
+        smul = 16;
+        sdst = L::C + (lane - 6 - 2 * ND) * 4;
+    }
+    const bool scopy = lane < L::NSMALL;
+    const size_t hrow = (size_t)Du * 16;
+    const int *lvl_off = p.lvl_off, *sprev = p.sprev, *lvl_start = p.lvl_start;
+    const int nlevels = p.nlevels;
+
+    for (int l = 0; l < nlevels; ++l) {
+        const int s0 = lvl_start[l], s1 = lvl_start[l + 1];
+        for (int base = s0 + w; base < s1; base += kWWarpsF * 32) {
+            const int sl = base + kWWarpsF * lane;
+            if (sl < s1) {
+                sidx[w][lane][0] = lvl_off[sl];
+#pragma unroll
+                for (int a = 0; a < ND; ++a) sidx[w][lane][1 + a] = sprev[sl * ND + a];
+            }
+            __syncwarp();
+            const int cnt = min(32, (s1 - base + kWWarpsF - 1) / kWWarpsF);
+            auto issue = [&](int j) {
+                float *bf = wb + (j % S) * L::SIZE;
+                const unsigned pt = (unsigned)sidx[w][j][0];
+#pragma unroll
+                for (int a = 0; a < ND; ++a) {
+                    const int pv = sidx[w][j][1 + a];
+                    if (pv >= 0)
+                        kmb_cp_async16(bf + L::HP + a * kWCh * 16 + lane * 4,
+                                       hg + (size_t)(unsigned)pv * hrow, 16);
+                }
+                if (scopy) kmb_cp_async16(bf + sdst, ssrc + (size_t)pt * smul, 16);
+            };
+#pragma unroll
+            for (int j = 0; j < S - 1; ++j) {
+                if (j < cnt) issue(j);
+                kmb_cp_async_commit();
+            }
+            for (int j = 0; j < cnt; ++j) {
+                if (j + S - 1 < cnt) issue(j + S - 1);
+                kmb_cp_async_commit();
+                kmb_cp_async_wait<S - 1>();
+                __syncwarp();
+                const float *bf = wb + (j % S) * L::SIZE;
+                const unsigned pt = (unsigned)sidx[w][j][0];
+                const unsigned od = pt * Du;
+                int pv[ND];
+                float dta[ND];
+                bool weak = false;
+#pragma unroll
+                for (int a = 0; a < ND; ++a) {
+                    pv[a] = sidx[w][j][1 + a];
+                    dta[a] = bf[L::DL + a * kWCh + c];
+                    weak |= pv[a] >= 0 && fabsf(dta[a]) * amin[a] < KMB_DECAY_POLY_MAX;
+                }
+                /* MUFU only where no lane of the warp needs the polynomial */
+                const bool fast = !__any_sync(kWFull, weak);
+                const float xv = bf[L::X + c];
+                const float4 B4 = *reinterpret_cast<const float4 *>(bf + L::B + q * 4);
+                const float4 C4 = *reinterpret_cast<const float4 *>(bf + L::C + q * 4);
+                float dt_bar = 0.f;
+#pragma unroll
+                for (int a = 0; a < ND; ++a) dt_bar += dta[a];
+                dt_bar /= (float)ND;
+                /* dt_bar (B x), in the reference's association */
+                const float2 u2 = kmb_f2s(dt_bar), x2 = kmb_f2s(xv);
+                float2 hn[2] = {kmb_mul2(u2, kmb_mul2(kmb_f2(B4.x, B4.y), x2)),
+                                kmb_mul2(u2, kmb_mul2(kmb_f2(B4.z, B4.w), x2))};
+                auto carry = [&](auto fast_tag) {
+                    constexpr bool FAST = decltype(fast_tag)::value;
+#pragma unroll
+                    for (int a = 0; a < ND; ++a) {
+                        if (pv[a] >= 0) {
+                            const float4 hp = *reinterpret_cast<const float4 *>(
+                                bf + L::HP + a * kWCh * 16 + lane * 4);
+                            const float2 dv2 = kmb_f2s(dta[a]);
+                            const float2 w0 = kmb_mul2(dv2, A2[a][0]);
+                            const float2 w1 = kmb_mul2(dv2, A2[a][1]);
+                            const float2 e0 = FAST ? kmb_ex2_2(w0) : kmb_exp2_decay2(w0);
+                            const float2 e1 = FAST ? kmb_ex2_2(w1) : kmb_exp2_decay2(w1);
+                            hn[0] = kmb_fma2(e0, kmb_f2(hp.x, hp.y), hn[0]);
+                            hn[1] = kmb_fma2(e1, kmb_f2(hp.z, hp.w), hn[1]);
+                        }
+                    }
+                };
+                if (fast)
+                    carry(std::true_type{});
+                else
+                    carry(std::false_type{});
+                const float2 y2 = kmb_fma2(kmb_f2(C4.z, C4.w), hn[1],
+                                           kmb_mul2(kmb_f2(C4.x, C4.y), hn[0]));
+                float yv = y2.x + y2.y;
+                yv += __shfl_xor_sync(kWFull, yv, 1);
+                yv += __shfl_xor_sync(kWFull, yv, 2);
+                *reinterpret_cast<float4 *>(hq + (size_t)od * 16) =
+                    make_float4(hn[0].x, hn[0].y, hn[1].x, hn[1].y);
+                if (q == 0) yq[od] = yv;
+                __syncwarp(); /* slot j % S is refilled next */
+            }
+        }
+        __syncthreads();
+    }
+}
+
+/* ring depth of k_scannd_fwd_p within 227 KB of shared memory */
+template <int ND>
+constexpr int fwd_p_stages() {
+    return (size_t)kWWarpsF * 3 * FwdPSlot<ND>::SIZE * 4 + kWWarpsF * 32 * (ND + 1) * 4 <=
+                   227 * 1024
+               ? 3
+               : 2;
+}
+
 /* Reduce-scatter of 8 values over the 8 lanes that share q (lane bits
  * 2-4): afterwards lane 4c + q holds the sum of value 4 (c >> 2) + (c & 3). */
 __device__ __forceinline__ float rs8_ch(float (&v)[8], int lane) {
@@ -507,6 +689,157 @@ __device__ __forceinline__ void grad_point(
         float *dst = ((c >> 2) ? dCrow : dBrow) + q * 4;
         atomicAdd(reinterpret_cast<float4 *>(dst), make_float4(r1, r2, r3, r4));
     }
+}
+
+/* k_scannd_adj_w with each warp's loads pipelined through a ring of S
+ * point slots (cp.async), for M = 16: the successors' adjoint rows G(p +
+ * e_axis) and delta_axis(p + e_axis), and the point's dy and C, of point
+ * j + S - 1 are in flight while point j is computed. */
+template <int ND>
+struct AdjPSlot {
+    static constexpr int GN = 0;                  /* [ND][128] successor rows */
+    static constexpr int DY = ND * kWCh * 16;      /* [8] */
+    static constexpr int DTN = DY + kWCh;          /* [ND][8] successor deltas */
+    static constexpr int C = DTN + ND * kWCh;      /* [16] */
+    static constexpr int SIZE = C + 16;
+    static constexpr int NSMALL = 2 + 2 * ND + 4;  /* 16-byte chunks of dy, delta, C */
+    static_assert(SIZE % 4 == 0 && NSMALL <= 32, "slot layout");
+};
+
+template <int ND, int S>
+__global__ void __launch_bounds__(kWWarpsA * 32) k_scannd_adj_p(NDDev p) {
+    using L = AdjPSlot<ND>;
+    extern __shared__ __align__(16) float asm_[];
+    __shared__ int sidx[kWWarpsA][32][ND + 1];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int c = lane >> 2, q = lane & 3;
+    const long b = blockIdx.y;
+    const long d0 = (long)blockIdx.x * kWCh;
+    const unsigned Du = (unsigned)p.D;
+    float2 A2[ND][2];
+#pragma unroll
+    for (int a = 0; a < ND; ++a)
+#pragma unroll
+        for (int jp = 0; jp < 2; ++jp) {
+            const float *ap = p.A[a] + (d0 + c) * 16 + q * 4 + 2 * jp;
+            A2[a][jp] = kmb_f2(ap[0] * KMB_LOG2E, ap[1] * KMB_LOG2E);
+        }
+    float amin[ND];
+#pragma unroll
+    for (int a = 0; a < ND; ++a) amin[a] = lane_amin(A2[a]);
+    float *wb = asm_ + w * S * L::SIZE;
+    const float *gg_src = p.G + b * p.h_bs + d0 * 16 + lane * 4; /* + point * D * 16 */
+    float *gq = p.G + b * p.h_bs + d0 * 16 + lane * 4;
+    /* this lane's chunk: dy (lanes 0-1), delta_a of a successor (2 + 2a,
+     * 3 + 2a; its row is the successor's, chosen per point), C (4 lanes) */
+    const float *ssrc = p.dy + b * p.x_bs + d0 + lane * 4;
+    unsigned smul = Du;
+    int sdst = L::DY + lane * 4, sax = -1;
+#pragma unroll
+    for (int a = 0; a < ND; ++a)
+        if (lane >= 2 + 2 * a && lane < 4 + 2 * a) {
+            ssrc = p.delta[a] + b * p.dl_bs + d0 + (lane - 2 - 2 * a) * 4;
+            sdst = L::DTN + a * kWCh + (lane - 2 - 2 * a) * 4;
+            sax = a;
+        }
+    if (lane >= 2 + 2 * ND) {
+        ssrc = p.C + b * p.bc_bs + (lane - 2 - 2 * ND) * 4;
+        smul = 16;
+        sdst = L::C + (lane - 2 - 2 * ND) * 4;
+    }
+    const bool scopy = lane < L::NSMALL;
+    const size_t hrow = (size_t)Du * 16;
+    const int *lvl_off = p.lvl_off, *snext = p.snext, *lvl_start = p.lvl_start;
+
+    for (int l = p.nlevels - 1; l >= 0; --l) {
+        const int s0 = lvl_start[l], s1 = lvl_start[l + 1];
+        for (int base = s0 + w; base < s1; base += kWWarpsA * 32) {
+            const int sl = base + kWWarpsA * lane;
+            if (sl < s1) {
+                sidx[w][lane][0] = lvl_off[sl];
+#pragma unroll
+                for (int a = 0; a < ND; ++a) sidx[w][lane][1 + a] = snext[sl * ND + a];
+            }
+            __syncwarp();
+            const int cnt = min(32, (s1 - base + kWWarpsA - 1) / kWWarpsA);
+            auto issue = [&](int j) {
+                float *bf = wb + (j % S) * L::SIZE;
+#pragma unroll
+                for (int a = 0; a < ND; ++a) {
+                    const int nx = sidx[w][j][1 + a];
+                    if (nx >= 0)
+                        kmb_cp_async16(bf + L::GN + a * kWCh * 16 + lane * 4,
+                                       gg_src + (size_t)(unsigned)nx * hrow, 16);
+                }
+                if (scopy) {
+                    const int row = sidx[w][j][sax + 1]; /* sax -1: the point itself */
+                    if (row >= 0) kmb_cp_async16(bf + sdst, ssrc + (size_t)(unsigned)row * smul, 16);
+                }
+            };
+#pragma unroll
+            for (int j = 0; j < S - 1; ++j) {
+                if (j < cnt) issue(j);
+                kmb_cp_async_commit();
+            }
+            for (int j = 0; j < cnt; ++j) {
+                if (j + S - 1 < cnt) issue(j + S - 1);
+                kmb_cp_async_commit();
+                kmb_cp_async_wait<S - 1>();
+                __syncwarp();
+                const float *bf = wb + (j % S) * L::SIZE;
+                const unsigned pt = (unsigned)sidx[w][j][0];
+                int nx[ND];
+                float dtn[ND];
+                bool weak = false;
+#pragma unroll
+                for (int a = 0; a < ND; ++a) {
+                    nx[a] = sidx[w][j][1 + a];
+                    dtn[a] = bf[L::DTN + a * kWCh + c];
+                    weak |= nx[a] >= 0 && fabsf(dtn[a]) * amin[a] < KMB_DECAY_POLY_MAX;
+                }
+                /* MUFU only where no lane of the warp needs the polynomial */
+                const bool fast = !__any_sync(kWFull, weak);
+                const float gy = bf[L::DY + c];
+                const float4 C4 = *reinterpret_cast<const float4 *>(bf + L::C + q * 4);
+                const float2 gy2 = kmb_f2s(gy);
+                float2 gg[2] = {kmb_mul2(kmb_f2(C4.x, C4.y), gy2),
+                                kmb_mul2(kmb_f2(C4.z, C4.w), gy2)};
+                auto carry = [&](auto fast_tag) {
+                    constexpr bool FAST = decltype(fast_tag)::value;
+#pragma unroll
+                    for (int a = 0; a < ND; ++a) {
+                        if (nx[a] >= 0) {
+                            const float4 gn = *reinterpret_cast<const float4 *>(
+                                bf + L::GN + a * kWCh * 16 + lane * 4);
+                            const float2 dn2 = kmb_f2s(dtn[a]);
+                            const float2 w0 = kmb_mul2(dn2, A2[a][0]);
+                            const float2 w1 = kmb_mul2(dn2, A2[a][1]);
+                            const float2 e0 = FAST ? kmb_ex2_2(w0) : kmb_exp2_decay2(w0);
+                            const float2 e1 = FAST ? kmb_ex2_2(w1) : kmb_exp2_decay2(w1);
+                            gg[0] = kmb_fma2(e0, kmb_f2(gn.x, gn.y), gg[0]);
+                            gg[1] = kmb_fma2(e1, kmb_f2(gn.z, gn.w), gg[1]);
+                        }
+                    }
+                };
+                if (fast)
+                    carry(std::true_type{});
+                else
+                    carry(std::false_type{});
+                *reinterpret_cast<float4 *>(gq + (size_t)(pt * Du) * 16) =
+                    make_float4(gg[0].x, gg[0].y, gg[1].x, gg[1].y);
+                __syncwarp(); /* slot j % S is refilled next */
+            }
+        }
+        __syncthreads();
+    }
+}
+
+template <int ND>
+constexpr int adj_p_stages() {
+    return (size_t)kWWarpsA * 3 * AdjPSlot<ND>::SIZE * 4 + kWWarpsA * 32 * (ND + 1) * 4 <=
+                   227 * 1024
+               ? 3
+               : 2;
 }
 
 constexpr int kGWarps = 8;    /* warps per CTA of the gradient pass */
@@ -967,15 +1300,43 @@ static cudaError_t launch_grad_s(const NDDev &p, const KmbNDLaunch *a, const Gra
     return cudaGetLastError();
 }
 
+/* the pipelined warp kernels copy 16-byte chunks of the M = 16 state
+ * rows and of the per-point rows of x or dy (xdy) and delta */
+static bool staged_rows(const KmbNDLaunch *a, const void *xdy) {
+    auto al = [](const void *q) { return ((uintptr_t)q & 15u) == 0; };
+    bool ok = a->M == 16 && al(xdy) && a->delta_bstride % 4 == 0;
+    for (int i = 0; i < a->nd; ++i) ok = ok && al(a->delta[i]);
+    return ok;
+}
+
 template <int ND>
 static cudaError_t launch_w(const NDDev &p, const KmbNDLaunch *a, bool bwd, cudaStream_t s) {
     dim3 grid((unsigned)(a->D / kWCh), (unsigned)a->batch);
     if (!bwd) {
+        if (staged_rows(a, a->x)) {
+            constexpr int S = fwd_p_stages<ND>();
+            constexpr size_t smem = (size_t)kWWarpsF * S * FwdPSlot<ND>::SIZE * sizeof(float);
+            cudaError_t e = cudaFuncSetAttribute(
+                k_scannd_fwd_p<ND, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+            k_scannd_fwd_p<ND, S><<<grid, kWWarpsF * 32, smem, s>>>(p);
+            return cudaGetLastError();
+        }
         k_scannd_fwd_w<ND><<<grid, kWWarpsF * 32, 0, s>>>(p);
         return cudaGetLastError();
     }
-    k_scannd_adj_w<ND><<<grid, kWWarpsA * 32, 0, s>>>(p);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e;
+    if (staged_rows(a, a->dy)) {
+        constexpr int S = adj_p_stages<ND>();
+        constexpr size_t smem = (size_t)kWWarpsA * S * AdjPSlot<ND>::SIZE * sizeof(float);
+        e = cudaFuncSetAttribute(k_scannd_adj_p<ND, S>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        k_scannd_adj_p<ND, S><<<grid, kWWarpsA * 32, smem, s>>>(p);
+    } else {
+        k_scannd_adj_w<ND><<<grid, kWWarpsA * 32, 0, s>>>(p);
+    }
+    e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     GradS g;
     switch (grad_s_cfg(a, &g)) {
