@@ -339,24 +339,42 @@ __device__ __forceinline__ float lane_amin(const float2 (&A2)[2]) {
  * states are in memory, so a warp streams its points of the level
  * through a ring of S point slots in shared memory (cp.async): the
  * predecessor rows (kWCh x 16 states), and x, delta, B and C of point j +
- * S - 1 are in flight while point j is computed from its slot. */
+ * S - 1 are in flight while point j is computed from its slot.  Per
+ * channel, the point's deltas and x sit side by side in the slot (one
+ * 4-byte copy per lane, one 16-byte read per lane). */
 template <int ND>
 struct FwdPSlot {
-    static constexpr int HP = 0;                 /* [ND][128] predecessor rows */
-    static constexpr int X = ND * kWCh * 16;      /* [8] */
-    static constexpr int DL = X + kWCh;           /* [ND][8] */
-    static constexpr int B = DL + ND * kWCh;      /* [16] */
-    static constexpr int C = B + 16;              /* [16] */
-    static constexpr int SIZE = C + 16;           /* floats, a multiple of 4 */
-    static constexpr int NSMALL = 2 + 2 * ND + 8; /* 16-byte chunks of x, delta, B, C */
-    static_assert(SIZE % 4 == 0 && NSMALL <= 32, "slot layout");
+    static constexpr int XW = ND + 1 <= 4 ? 4 : 8; /* floats per channel: delta_a, then x */
+    static constexpr int HP = 0;                    /* [ND][128] predecessor rows */
+    static constexpr int DX = ND * kWCh * 16;       /* [8][XW] */
+    static constexpr int B = DX + kWCh * XW;        /* [16] */
+    static constexpr int C = B + 16;                /* [16] */
+    static constexpr int SIZE = C + 16;             /* floats, a multiple of 4 */
+    static constexpr int NJ = (kWCh * (ND + 1) + 31) / 32; /* 4-byte copies a lane */
+    static_assert(SIZE % 4 == 0, "slot layout");
 };
+
+/* the index row (point, then one neighbour per axis) of slot j */
+template <int ND>
+__device__ __forceinline__ void load_idx(const int (&row)[ND + 1], int (&ix)[ND + 1]) {
+    if constexpr (ND == 3) {
+        const int4 t = *reinterpret_cast<const int4 *>(row);
+        ix[0] = t.x;
+        ix[1] = t.y;
+        ix[2] = t.z;
+        ix[3] = t.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i <= ND; ++i) ix[i] = row[i];
+    }
+}
 
 template <int ND, int S>
 __global__ void __launch_bounds__(kWWarpsF * 32) k_scannd_fwd_p(NDDev p) {
     using L = FwdPSlot<ND>;
+    constexpr float kInvND = 1.0f / ND;
     extern __shared__ __align__(16) float fsm[];
-    __shared__ int sidx[kWWarpsF][32][ND + 1];
+    __shared__ __align__(16) int sidx[kWWarpsF][32][ND + 1];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int c = lane >> 2, q = lane & 3;
     const long b = blockIdx.y;
@@ -378,27 +396,24 @@ __global__ void __launch_bounds__(kWWarpsF * 32) k_scannd_fwd_p(NDDev p) {
     const float *hg = p.h + b * p.h_bs + d0 * 16 + lane * 4; /* + point * D * 16 */
     float *hq = p.h + b * p.h_bs + d0 * 16 + lane * 4;
     float *yq = p.y + b * p.x_bs + d;
-    /* this lane's chunk of x, delta, B or C: source base, point multiplier
-     * and slot offset (lanes >= NSMALL copy none) */
-    const float *ssrc = p.x + b * p.x_bs + d0 + lane * 4;
-    unsigned smul = Du;
-    int sdst = L::X + lane * 4;
+    /* this lane's 4-byte copies: value v of channel ch (delta_v, x for v = ND) */
+    const float *vsrc[L::NJ];
+    int vdst[L::NJ];
+    bool vok[L::NJ];
 #pragma unroll
-    for (int a = 0; a < ND; ++a)
-        if (lane >= 2 + 2 * a && lane < 4 + 2 * a) {
-            ssrc = p.delta[a] + b * p.dl_bs + d0 + (lane - 2 - 2 * a) * 4;
-            sdst = L::DL + a * kWCh + (lane - 2 - 2 * a) * 4;
-        }
-    if (lane >= 2 + 2 * ND && lane < 2 + 2 * ND + 4) {
-        ssrc = p.B + b * p.bc_bs + (lane - 2 - 2 * ND) * 4;
-        smul = 16;
-        sdst = L::B + (lane - 2 - 2 * ND) * 4;
-    } else if (lane >= 2 + 2 * ND + 4) {
-        ssrc = p.C + b * p.bc_bs + (lane - 6 - 2 * ND) * 4;
-        smul = 16;
-        sdst = L::C + (lane - 6 - 2 * ND) * 4;
+    for (int i = 0; i < L::NJ; ++i) {
+        const int e = lane + 32 * i, v = e / kWCh, ch = e % kWCh;
+        vok[i] = v <= ND;
+        const float *src = p.x + b * p.x_bs;
+#pragma unroll
+        for (int a = 0; a < ND; ++a)
+            if (v == a) src = p.delta[a] + b * p.dl_bs;
+        vsrc[i] = src + d0 + ch;
+        vdst[i] = L::DX + ch * L::XW + v;
     }
-    const bool scopy = lane < L::NSMALL;
+    /* B (lanes 0-3) and C (lanes 4-7): one 16-byte chunk each */
+    const float *bcsrc = (lane < 4 ? p.B : p.C) + b * p.bc_bs + (lane & 3) * 4;
+    const int bcdst = (lane < 4 ? L::B : L::C) + (lane & 3) * 4;
     const size_t hrow = (size_t)Du * 16;
     const int *lvl_off = p.lvl_off, *sprev = p.sprev, *lvl_start = p.lvl_start;
     const int nlevels = p.nlevels;
@@ -414,61 +429,72 @@ __global__ void __launch_bounds__(kWWarpsF * 32) k_scannd_fwd_p(NDDev p) {
             }
             __syncwarp();
             const int cnt = min(32, (s1 - base + kWWarpsF - 1) / kWWarpsF);
-            auto issue = [&](int j) {
-                float *bf = wb + (j % S) * L::SIZE;
-                const unsigned pt = (unsigned)sidx[w][j][0];
+            auto issue = [&](int j, int slot) {
+                float *bf = wb + slot * L::SIZE;
+                int ix[ND + 1];
+                load_idx<ND>(sidx[w][j], ix);
 #pragma unroll
-                for (int a = 0; a < ND; ++a) {
-                    const int pv = sidx[w][j][1 + a];
-                    if (pv >= 0)
+                for (int a = 0; a < ND; ++a)
+                    if (ix[1 + a] >= 0)
                         kmb_cp_async16(bf + L::HP + a * kWCh * 16 + lane * 4,
-                                       hg + (size_t)(unsigned)pv * hrow, 16);
-                }
-                if (scopy) kmb_cp_async16(bf + sdst, ssrc + (size_t)pt * smul, 16);
+                                       hg + (size_t)(unsigned)ix[1 + a] * hrow, 16);
+                const size_t od = (size_t)(unsigned)ix[0] * Du;
+#pragma unroll
+                for (int i = 0; i < L::NJ; ++i)
+                    if (vok[i]) kmb_cp_async4(bf + vdst[i], vsrc[i] + od, true);
+                if (lane < 8) kmb_cp_async16(bf + bcdst, bcsrc + (size_t)(unsigned)ix[0] * 16, 16);
             };
+            int si = 0, sc = 0; /* ring slots of the next issue and of the next compute */
 #pragma unroll
             for (int j = 0; j < S - 1; ++j) {
-                if (j < cnt) issue(j);
+                if (j < cnt) {
+                    issue(j, si);
+                    si = si + 1 == S ? 0 : si + 1;
+                }
                 kmb_cp_async_commit();
             }
             for (int j = 0; j < cnt; ++j) {
-                if (j + S - 1 < cnt) issue(j + S - 1);
+                if (j + S - 1 < cnt) {
+                    issue(j + S - 1, si);
+                    si = si + 1 == S ? 0 : si + 1;
+                }
                 kmb_cp_async_commit();
                 kmb_cp_async_wait<S - 1>();
                 __syncwarp();
-                const float *bf = wb + (j % S) * L::SIZE;
-                const unsigned pt = (unsigned)sidx[w][j][0];
-                const unsigned od = pt * Du;
-                int pv[ND];
-                float dta[ND];
-                bool weak = false;
+                const float *bf = wb + sc * L::SIZE;
+                sc = sc + 1 == S ? 0 : sc + 1;
+                int ix[ND + 1];
+                load_idx<ND>(sidx[w][j], ix);
+                const unsigned od = (unsigned)ix[0] * Du;
+                float dx[L::XW];
 #pragma unroll
-                for (int a = 0; a < ND; ++a) {
-                    pv[a] = sidx[w][j][1 + a];
-                    dta[a] = bf[L::DL + a * kWCh + c];
-                    weak |= pv[a] >= 0 && fabsf(dta[a]) * amin[a] < KMB_DECAY_POLY_MAX;
-                }
-                /* MUFU only where no lane of the warp needs the polynomial */
-                const bool fast = !__any_sync(kWFull, weak);
-                const float xv = bf[L::X + c];
-                const float4 B4 = *reinterpret_cast<const float4 *>(bf + L::B + q * 4);
-                const float4 C4 = *reinterpret_cast<const float4 *>(bf + L::C + q * 4);
+                for (int i = 0; i < L::XW; i += 4)
+                    *reinterpret_cast<float4 *>(dx + i) =
+                        *reinterpret_cast<const float4 *>(bf + L::DX + c * L::XW + i);
+                bool weak = false;
                 float dt_bar = 0.f;
 #pragma unroll
-                for (int a = 0; a < ND; ++a) dt_bar += dta[a];
-                dt_bar /= (float)ND;
+                for (int a = 0; a < ND; ++a) {
+                    dt_bar += dx[a];
+                    weak |= (ix[1 + a] >= 0) & (fabsf(dx[a]) * amin[a] < KMB_DECAY_POLY_MAX);
+                }
+                dt_bar *= kInvND;
+                /* MUFU only where no lane of the warp needs the polynomial */
+                const bool fast = !__any_sync(kWFull, weak);
+                const float4 B4 = *reinterpret_cast<const float4 *>(bf + L::B + q * 4);
+                const float4 C4 = *reinterpret_cast<const float4 *>(bf + L::C + q * 4);
                 /* dt_bar (B x), in the reference's association */
-                const float2 u2 = kmb_f2s(dt_bar), x2 = kmb_f2s(xv);
+                const float2 u2 = kmb_f2s(dt_bar), x2 = kmb_f2s(dx[ND]);
                 float2 hn[2] = {kmb_mul2(u2, kmb_mul2(kmb_f2(B4.x, B4.y), x2)),
                                 kmb_mul2(u2, kmb_mul2(kmb_f2(B4.z, B4.w), x2))};
                 auto carry = [&](auto fast_tag) {
                     constexpr bool FAST = decltype(fast_tag)::value;
 #pragma unroll
                     for (int a = 0; a < ND; ++a) {
-                        if (pv[a] >= 0) {
+                        if (ix[1 + a] >= 0) {
                             const float4 hp = *reinterpret_cast<const float4 *>(
                                 bf + L::HP + a * kWCh * 16 + lane * 4);
-                            const float2 dv2 = kmb_f2s(dta[a]);
+                            const float2 dv2 = kmb_f2s(dx[a]);
                             const float2 w0 = kmb_mul2(dv2, A2[a][0]);
                             const float2 w1 = kmb_mul2(dv2, A2[a][1]);
                             const float2 e0 = FAST ? kmb_ex2_2(w0) : kmb_exp2_decay2(w0);
@@ -490,7 +516,7 @@ __global__ void __launch_bounds__(kWWarpsF * 32) k_scannd_fwd_p(NDDev p) {
                 *reinterpret_cast<float4 *>(hq + (size_t)od * 16) =
                     make_float4(hn[0].x, hn[0].y, hn[1].x, hn[1].y);
                 if (q == 0) yq[od] = yv;
-                __syncwarp(); /* slot j % S is refilled next */
+                __syncwarp(); /* the slot is refilled next */
             }
         }
         __syncthreads();
@@ -693,24 +719,25 @@ __device__ __forceinline__ void grad_point(
 
 /* k_scannd_adj_w with each warp's loads pipelined through a ring of S
  * point slots (cp.async), for M = 16: the successors' adjoint rows G(p +
- * e_axis) and delta_axis(p + e_axis), and the point's dy and C, of point
- * j + S - 1 are in flight while point j is computed. */
+ * e_axis) and deltas delta_axis(p + e_axis), and the point's dy and C, of
+ * point j + S - 1 are in flight while point j is computed.  Per channel
+ * the successors' deltas and dy sit side by side in the slot. */
 template <int ND>
 struct AdjPSlot {
-    static constexpr int GN = 0;                  /* [ND][128] successor rows */
-    static constexpr int DY = ND * kWCh * 16;      /* [8] */
-    static constexpr int DTN = DY + kWCh;          /* [ND][8] successor deltas */
-    static constexpr int C = DTN + ND * kWCh;      /* [16] */
+    static constexpr int XW = ND + 1 <= 4 ? 4 : 8; /* floats per channel: delta_a, then dy */
+    static constexpr int GN = 0;                    /* [ND][128] successor rows */
+    static constexpr int DD = ND * kWCh * 16;       /* [8][XW] */
+    static constexpr int C = DD + kWCh * XW;        /* [16] */
     static constexpr int SIZE = C + 16;
-    static constexpr int NSMALL = 2 + 2 * ND + 4;  /* 16-byte chunks of dy, delta, C */
-    static_assert(SIZE % 4 == 0 && NSMALL <= 32, "slot layout");
+    static constexpr int NJ = (kWCh * (ND + 1) + 31) / 32;
+    static_assert(SIZE % 4 == 0, "slot layout");
 };
 
 template <int ND, int S>
 __global__ void __launch_bounds__(kWWarpsA * 32) k_scannd_adj_p(NDDev p) {
     using L = AdjPSlot<ND>;
     extern __shared__ __align__(16) float asm_[];
-    __shared__ int sidx[kWWarpsA][32][ND + 1];
+    __shared__ __align__(16) int sidx[kWWarpsA][32][ND + 1];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int c = lane >> 2, q = lane & 3;
     const long b = blockIdx.y;
@@ -730,24 +757,26 @@ __global__ void __launch_bounds__(kWWarpsA * 32) k_scannd_adj_p(NDDev p) {
     float *wb = asm_ + w * S * L::SIZE;
     const float *gg_src = p.G + b * p.h_bs + d0 * 16 + lane * 4; /* + point * D * 16 */
     float *gq = p.G + b * p.h_bs + d0 * 16 + lane * 4;
-    /* this lane's chunk: dy (lanes 0-1), delta_a of a successor (2 + 2a,
-     * 3 + 2a; its row is the successor's, chosen per point), C (4 lanes) */
-    const float *ssrc = p.dy + b * p.x_bs + d0 + lane * 4;
-    unsigned smul = Du;
-    int sdst = L::DY + lane * 4, sax = -1;
+    /* this lane's 4-byte copies: value v of channel ch: delta_v of the
+     * successor along axis v, or dy of the point (v = ND); vrow indexes
+     * the slot's index row (1 + v, or 0 for the point itself) */
+    const float *vsrc[L::NJ];
+    int vdst[L::NJ], vrow[L::NJ];
+    bool vok[L::NJ];
 #pragma unroll
-    for (int a = 0; a < ND; ++a)
-        if (lane >= 2 + 2 * a && lane < 4 + 2 * a) {
-            ssrc = p.delta[a] + b * p.dl_bs + d0 + (lane - 2 - 2 * a) * 4;
-            sdst = L::DTN + a * kWCh + (lane - 2 - 2 * a) * 4;
-            sax = a;
-        }
-    if (lane >= 2 + 2 * ND) {
-        ssrc = p.C + b * p.bc_bs + (lane - 2 - 2 * ND) * 4;
-        smul = 16;
-        sdst = L::C + (lane - 2 - 2 * ND) * 4;
+    for (int i = 0; i < L::NJ; ++i) {
+        const int e = lane + 32 * i, v = e / kWCh, ch = e % kWCh;
+        vok[i] = v <= ND;
+        const float *src = p.dy + b * p.x_bs;
+#pragma unroll
+        for (int a = 0; a < ND; ++a)
+            if (v == a) src = p.delta[a] + b * p.dl_bs;
+        vsrc[i] = src + d0 + ch;
+        vdst[i] = L::DD + ch * L::XW + v;
+        vrow[i] = v < ND ? 1 + v : 0;
     }
-    const bool scopy = lane < L::NSMALL;
+    const float *csrc = p.C + b * p.bc_bs + (lane & 3) * 4;
+    const int cdst = L::C + (lane & 3) * 4;
     const size_t hrow = (size_t)Du * 16;
     const int *lvl_off = p.lvl_off, *snext = p.snext, *lvl_start = p.lvl_start;
 
@@ -762,56 +791,67 @@ __global__ void __launch_bounds__(kWWarpsA * 32) k_scannd_adj_p(NDDev p) {
             }
             __syncwarp();
             const int cnt = min(32, (s1 - base + kWWarpsA - 1) / kWWarpsA);
-            auto issue = [&](int j) {
-                float *bf = wb + (j % S) * L::SIZE;
+            auto issue = [&](int j, int slot) {
+                float *bf = wb + slot * L::SIZE;
+                int ix[ND + 1];
+                load_idx<ND>(sidx[w][j], ix);
 #pragma unroll
-                for (int a = 0; a < ND; ++a) {
-                    const int nx = sidx[w][j][1 + a];
-                    if (nx >= 0)
+                for (int a = 0; a < ND; ++a)
+                    if (ix[1 + a] >= 0)
                         kmb_cp_async16(bf + L::GN + a * kWCh * 16 + lane * 4,
-                                       gg_src + (size_t)(unsigned)nx * hrow, 16);
+                                       gg_src + (size_t)(unsigned)ix[1 + a] * hrow, 16);
+#pragma unroll
+                for (int i = 0; i < L::NJ; ++i) {
+                    const int row = sidx[w][j][vrow[i]];
+                    if (vok[i] && row >= 0)
+                        kmb_cp_async4(bf + vdst[i], vsrc[i] + (size_t)(unsigned)row * Du, true);
                 }
-                if (scopy) {
-                    const int row = sidx[w][j][sax + 1]; /* sax -1: the point itself */
-                    if (row >= 0) kmb_cp_async16(bf + sdst, ssrc + (size_t)(unsigned)row * smul, 16);
-                }
+                if (lane < 4) kmb_cp_async16(bf + cdst, csrc + (size_t)(unsigned)ix[0] * 16, 16);
             };
+            int si = 0, sc = 0; /* ring slots of the next issue and of the next compute */
 #pragma unroll
             for (int j = 0; j < S - 1; ++j) {
-                if (j < cnt) issue(j);
+                if (j < cnt) {
+                    issue(j, si);
+                    si = si + 1 == S ? 0 : si + 1;
+                }
                 kmb_cp_async_commit();
             }
             for (int j = 0; j < cnt; ++j) {
-                if (j + S - 1 < cnt) issue(j + S - 1);
+                if (j + S - 1 < cnt) {
+                    issue(j + S - 1, si);
+                    si = si + 1 == S ? 0 : si + 1;
+                }
                 kmb_cp_async_commit();
                 kmb_cp_async_wait<S - 1>();
                 __syncwarp();
-                const float *bf = wb + (j % S) * L::SIZE;
-                const unsigned pt = (unsigned)sidx[w][j][0];
-                int nx[ND];
-                float dtn[ND];
+                const float *bf = wb + sc * L::SIZE;
+                sc = sc + 1 == S ? 0 : sc + 1;
+                int ix[ND + 1];
+                load_idx<ND>(sidx[w][j], ix);
+                float dd[L::XW];
+#pragma unroll
+                for (int i = 0; i < L::XW; i += 4)
+                    *reinterpret_cast<float4 *>(dd + i) =
+                        *reinterpret_cast<const float4 *>(bf + L::DD + c * L::XW + i);
                 bool weak = false;
 #pragma unroll
-                for (int a = 0; a < ND; ++a) {
-                    nx[a] = sidx[w][j][1 + a];
-                    dtn[a] = bf[L::DTN + a * kWCh + c];
-                    weak |= nx[a] >= 0 && fabsf(dtn[a]) * amin[a] < KMB_DECAY_POLY_MAX;
-                }
+                for (int a = 0; a < ND; ++a)
+                    weak |= (ix[1 + a] >= 0) & (fabsf(dd[a]) * amin[a] < KMB_DECAY_POLY_MAX);
                 /* MUFU only where no lane of the warp needs the polynomial */
                 const bool fast = !__any_sync(kWFull, weak);
-                const float gy = bf[L::DY + c];
                 const float4 C4 = *reinterpret_cast<const float4 *>(bf + L::C + q * 4);
-                const float2 gy2 = kmb_f2s(gy);
+                const float2 gy2 = kmb_f2s(dd[ND]);
                 float2 gg[2] = {kmb_mul2(kmb_f2(C4.x, C4.y), gy2),
                                 kmb_mul2(kmb_f2(C4.z, C4.w), gy2)};
                 auto carry = [&](auto fast_tag) {
                     constexpr bool FAST = decltype(fast_tag)::value;
 #pragma unroll
                     for (int a = 0; a < ND; ++a) {
-                        if (nx[a] >= 0) {
+                        if (ix[1 + a] >= 0) {
                             const float4 gn = *reinterpret_cast<const float4 *>(
                                 bf + L::GN + a * kWCh * 16 + lane * 4);
-                            const float2 dn2 = kmb_f2s(dtn[a]);
+                            const float2 dn2 = kmb_f2s(dd[a]);
                             const float2 w0 = kmb_mul2(dn2, A2[a][0]);
                             const float2 w1 = kmb_mul2(dn2, A2[a][1]);
                             const float2 e0 = FAST ? kmb_ex2_2(w0) : kmb_exp2_decay2(w0);
@@ -825,9 +865,9 @@ __global__ void __launch_bounds__(kWWarpsA * 32) k_scannd_adj_p(NDDev p) {
                     carry(std::true_type{});
                 else
                     carry(std::false_type{});
-                *reinterpret_cast<float4 *>(gq + (size_t)(pt * Du) * 16) =
+                *reinterpret_cast<float4 *>(gq + (size_t)((unsigned)ix[0] * Du) * 16) =
                     make_float4(gg[0].x, gg[0].y, gg[1].x, gg[1].y);
-                __syncwarp(); /* slot j % S is refilled next */
+                __syncwarp(); /* the slot is refilled next */
             }
         }
         __syncthreads();
