@@ -990,8 +990,9 @@ struct GSLayout {
     static constexpr int O_FAR = O_G + kST * ROW;            /* [NF][kST][ROW] */
     static constexpr int O_X = O_FAR + NF * kST * ROW;       /* [2 + ND][kST][kWCh] */
     static constexpr int O_B = O_X + (2 + ND) * kST * kWCh;  /* [kST][16] */
-    static constexpr int O_PV = O_B + kST * 16;              /* [kST][ND] ints */
-    static constexpr int STAGE = (O_PV + kST * ND + 3) & ~3;
+    static constexpr int PVW = ND == 3 ? 4 : ND;              /* ints per point (3 axes: padded) */
+    static constexpr int O_PV = O_B + kST * 16;              /* [kST][PVW] ints */
+    static constexpr int STAGE = (O_PV + kST * PVW + 3) & ~3;
     static constexpr size_t bytes(int ss) {
         return sizeof(float) * ((size_t)(ss * kST + kNR) * ROW + (size_t)ss * STAGE);
     }
@@ -1017,10 +1018,11 @@ __device__ __forceinline__ void grad_point16(
     const int (&pv)[ND], float xv, float gy, const float (&dta)[ND],
     const float2 (&A2)[ND][2], const float2 (&Ar)[ND][2], float2 (&dAp)[ND][2], int lane,
     int c, int q, float *out0, float *out4, float *dBrow, float *dCrow) {
+    constexpr float kInvND = 1.0f / ND; /* the mean within 1 ulp of a division */
     float dt_bar = 0.f;
 #pragma unroll
     for (int a = 0; a < ND; ++a) dt_bar += dta[a];
-    dt_bar /= (float)ND;
+    dt_bar *= kInvND;
     const float2 gg[2] = {kmb_f2(G4.x, G4.y), kmb_f2(G4.z, G4.w)};
     const float2 Bp[2] = {kmb_f2(B4.x, B4.y), kmb_f2(B4.z, B4.w)};
     const float2 gy2 = kmb_f2s(gy), dtb2 = kmb_f2s(dt_bar), xv2 = kmb_f2s(xv);
@@ -1054,7 +1056,7 @@ __device__ __forceinline__ void grad_point16(
         }
     }
     /* per-lane partial sums: dx, then ddelta_a = sum G h(p-e) e A_a + (sum G B x) / ND */
-    const float sbn = (sb2.x + sb2.y) / (float)ND;
+    const float sbn = (sb2.x + sb2.y) * kInvND;
     float v[4] = {sx2.x + sx2.y, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int a = 0; a < ND && a < 3; ++a) v[1 + a] = sdt2[a].x + sdt2[a].y + sbn;
@@ -1180,8 +1182,9 @@ __global__ void __launch_bounds__(kSW * 32, 1) k_scannd_grad_s(NDDev p, GradS g)
             kmb_cp_async16(st + L::O_B + boff, bbase + (ok ? s0 * 16 + boff : 0), ok ? 16 : 0);
         }
         if (j_pv) {
-            const bool ok = s0 + tid / ND < pe;
-            kmb_cp_async4(st + L::O_PV + tid, p.prev + (ok ? s0 * ND + tid : 0), ok);
+            const int r = tid / ND, a = tid % ND;
+            const bool ok = s0 + r < pe;
+            kmb_cp_async4(st + L::O_PV + r * L::PVW + a, p.prev + (ok ? s0 * ND + tid : 0), ok);
         }
     };
 
@@ -1211,11 +1214,18 @@ __global__ void __launch_bounds__(kSW * 32, 1) k_scannd_grad_s(NDDev p, GradS g)
             int pv[ND];
             float dta[ND];
             float4 hp[ND];
+            if constexpr (L::PVW == 4) {
+                const int4 t = *reinterpret_cast<const int4 *>(spv + r * 4);
+                pv[0] = t.x;
+                pv[1] = t.y;
+                pv[2] = t.z;
+                if constexpr (ND == 4) pv[ND - 1] = t.w;
+            } else {
 #pragma unroll
-            for (int a = 0; a < ND; ++a) {
-                pv[a] = spv[r * ND + a];
-                dta[a] = st[L::O_X + ((2 + a) * kST + r) * kWCh + c];
+                for (int a = 0; a < ND; ++a) pv[a] = spv[r * L::PVW + a];
             }
+#pragma unroll
+            for (int a = 0; a < ND; ++a) dta[a] = st[L::O_X + ((2 + a) * kST + r) * kWCh + c];
             const float xv = st[L::O_X + r * kWCh + c];
             const float gy = st[L::O_X + (kST + r) * kWCh + c];
             const float4 B4 = *reinterpret_cast<const float4 *>(st + L::O_B + r * 16 + q * 4);
