@@ -659,11 +659,10 @@ cudaError_t dispatch2d_bwd_ring(const ConvDev &p, cudaStream_t s) {
  * 3D causal depthwise convolution (the Mamba-ND volumes) for K <= 3, D a
  * multiple of 4 and 16-byte aligned tensors.  A warp owns one (y, x)
  * column of the volume and 64 channels (2 per lane); a CTA is a 4 x 4
- * tile of columns.  The lane keeps its channels' K^3 taps in registers
- * and walks z (the loads of two slices issued together), so each input
- * slice is read
- * once (its K x K in-plane neighbours: the tile's own columns, from L1)
- * and feeds K rolling output accumulators:
+ * tile of columns, and channel blocks are the fastest grid dimension (a
+ * tile's CTAs read whole point vectors together).  The lane keeps its
+ * channels' K^3 taps in registers and walks z, so each input slice is
+ * read once and feeds K rolling output accumulators:
  *   forward (z ascending)  out(z) = bias + sum_o in(z - oz, y - oy, x - ox) w[K-1-o]
  *   dinput  (z descending) din(z) = sum_o dy(z + oz, y + oy, x + ox) w[K-1-o]
  * after slice s the accumulator of the output at s is complete.  dkernel
@@ -673,7 +672,6 @@ cudaError_t dispatch2d_bwd_ring(const ConvDev &p, cudaStream_t s) {
  * HBM sees one read of each input and one write of each output.
  */
 constexpr int Z3_TY = 4, Z3_TX = 4;           /* columns of a CTA */
-constexpr int Z3_UZ = 2; /* slices whose loads are issued together */
 constexpr int Z3_CH = 64;                     /* channels of a CTA (a warp) */
 constexpr int Z3_THREADS = Z3_TY * Z3_TX * 32;
 
@@ -706,113 +704,204 @@ __device__ __forceinline__ float2 ld2(const float *a) {
     return __ldg(reinterpret_cast<const float2 *>(a));
 }
 
-/* SGN = -1: forward; SGN = +1: dinput (gather form) */
+/*
+ * The slices are staged: the CTA's input slices (its 4 x 4 columns and
+ * the K - 1 halo columns on each in-plane axis, 64 channels) stream
+ * through a ring of ZS_R slices in shared memory (cp.async, 16-byte
+ * chunks, zero-filled outside the volume), ZS_R - 1 slices ahead of the
+ * compute, so the loads in flight no longer cost registers.  A lane reads
+ * its K x K neighbours from the slice (8-byte reads of a 256-byte column
+ * row); taps and accumulators stay in registers as in the z-walk.
+ * dkernel stages the dy slice of its own columns K - 1 slices ahead of
+ * the input slice, for its window of dy.
+ */
+constexpr int ZS_R = 8; /* slices in the ring */
+
+template <int K>
+struct ZSLayout {
+    static constexpr int CY = Z3_TY + K - 1, CX = Z3_TX + K - 1; /* staged columns */
+    static constexpr int NCOL = CY * CX;
+    static constexpr int SL = NCOL * Z3_CH;            /* floats of a staged input slice */
+    static constexpr int SLD = Z3_TY * Z3_TX * Z3_CH;  /* floats of a dy slice (dkernel) */
+    static constexpr int NJ = (NCOL * (Z3_CH / 4) + Z3_THREADS - 1) / Z3_THREADS; /* chunks a thread */
+};
+
+/* the 16-byte chunk jobs of a thread for one staged slice: element offset
+ * of slice 0 (or -1 when the column or the channels are outside) and the
+ * offset in the slot */
 template <int K, int SGN>
-__global__ void __launch_bounds__(Z3_THREADS, 1) k_conv3d_zwalk(ConvDev p) {
+struct ZSJobs {
+    long src[ZSLayout<K>::NJ];
+    int dst[ZSLayout<K>::NJ];
+    __device__ __forceinline__ void init(const ConvDev &p, int y0, int x0, long c0, int tid) {
+        using L = ZSLayout<K>;
+        const int Y = (int)p.dims[1], X = (int)p.dims[2];
+#pragma unroll
+        for (int i = 0; i < L::NJ; ++i) {
+            const int e = tid + i * Z3_THREADS;
+            const int col = e / (Z3_CH / 4), ch = e % (Z3_CH / 4);
+            const int cy = col / L::CX, cx = col % L::CX;
+            const int y = SGN < 0 ? y0 - (K - 1) + cy : y0 + cy;
+            const int x = SGN < 0 ? x0 - (K - 1) + cx : x0 + cx;
+            const long c = c0 + ch * 4;
+            const bool ok = e < L::NCOL * (Z3_CH / 4) && y >= 0 && y < Y && x >= 0 && x < X &&
+                            c < p.D;
+            src[i] = ok ? (long)blockIdx.z * p.P * p.D + ((long)y * X + x) * p.D + c : -1;
+            dst[i] = e < L::NCOL * (Z3_CH / 4) ? col * Z3_CH + ch * 4 : -1;
+        }
+    }
+    __device__ __forceinline__ void issue(float *slot, const float *base, long zoff) const {
+#pragma unroll
+        for (int i = 0; i < ZSLayout<K>::NJ; ++i)
+            if (dst[i] >= 0)
+                kmb_cp_async16(slot + dst[i], base + (src[i] >= 0 ? src[i] + zoff : 0),
+                               src[i] >= 0 ? 16 : 0);
+    }
+};
+
+/* SGN = -1: forward (z ascending); SGN = +1: dinput (z descending) */
+template <int K, int SGN>
+__global__ void __launch_bounds__(Z3_THREADS, 1) k_conv3d_zring(ConvDev p) {
+    using L = ZSLayout<K>;
     constexpr int KK = K * K, KV = K * KK;
+    extern __shared__ __align__(16) float zsm[];
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int ty = w / Z3_TX, tx = w % Z3_TX;
     const Col3 q = col3(p);
-    if (!q.on) return;
+    const long c0 = (long)blockIdx.x * Z3_CH;
+    const int y0 = q.y - ty, x0 = q.x - tx;
     float2 wt[KV];
 #pragma unroll
-    for (int k = 0; k < KV; ++k) wt[k] = ld2(p.ker + k * p.D + q.c);
-    /* in-plane neighbours j = oy K + ox: offset and causal bound */
-    int off[KK];
-    bool ok[KK];
+    for (int k = 0; k < KV; ++k)
+        wt[k] = q.on ? ld2(p.ker + k * p.D + q.c) : kmb_f2s(0.f);
+    ZSJobs<K, SGN> jobs;
+    jobs.init(p, y0, x0, c0, tid);
+    const float *src = SGN < 0 ? p.in : p.dy;
+    float *dst = (SGN < 0 ? p.out : p.din) + q.base;
+    const float2 b2 = (SGN < 0 && p.bias && q.on) ? ld2(p.bias + q.c) : kmb_f2s(0.f);
+    float2 acc[K];
+#pragma unroll
+    for (int i = 0; i < K; ++i) acc[i] = b2;
+    /* slice t of the walk is z = t (forward) or Z - 1 - t (dinput) */
+    auto zof = [&](int t) { return (long)(SGN < 0 ? t : q.Z - 1 - t) * q.sz; };
+#pragma unroll 1
+    for (int t = 0; t < ZS_R - 1; ++t) {
+        if (t < q.Z) jobs.issue(zsm + t * L::SL, src, zof(t));
+        kmb_cp_async_commit();
+    }
+    /* this lane's neighbour j = oy K + ox in a staged slice */
+    int nb[KK];
 #pragma unroll
     for (int oy = 0; oy < K; ++oy)
 #pragma unroll
         for (int ox = 0; ox < K; ++ox) {
-            off[oy * K + ox] = SGN * (oy * q.sy + ox * (int)p.D);
-            ok[oy * K + ox] = SGN < 0 ? (q.y >= oy && q.x >= ox)
-                                      : (q.y + oy < q.Y && q.x + ox < q.X);
+            const int cy = SGN < 0 ? ty + (K - 1) - oy : ty + oy;
+            const int cx = SGN < 0 ? tx + (K - 1) - ox : tx + ox;
+            nb[oy * K + ox] = (cy * L::CX + cx) * Z3_CH + lane * 2;
         }
-    const float *src = (SGN < 0 ? p.in : p.dy) + q.base;
-    float *dst = (SGN < 0 ? p.out : p.din) + q.base;
-    const float2 b2 = (SGN < 0 && p.bias) ? ld2(p.bias + q.c) : kmb_f2s(0.f);
-    float2 acc[K];
-#pragma unroll
-    for (int i = 0; i < K; ++i) acc[i] = b2;
-    int zo = SGN < 0 ? 0 : (q.Z - 1) * q.sz; /* offset of the current slice */
-    const int zstep = SGN < 0 ? q.sz : -q.sz;
+    int slot = 0;
 #pragma unroll 1
-    for (int t = 0; t < q.Z; t += Z3_UZ) {
-        /* the loads of Z3_UZ slices first, then their outputs */
-        float2 v[Z3_UZ][KK];
+    for (int t = 0; t < q.Z; ++t) {
+        kmb_cp_async_wait<ZS_R - 2>();
+        __syncthreads();
+        if (t + ZS_R - 1 < q.Z) {
+            const int ns = slot == 0 ? ZS_R - 1 : slot - 1; /* (t + ZS_R - 1) % ZS_R */
+            jobs.issue(zsm + ns * L::SL, src, zof(t + ZS_R - 1));
+        }
+        kmb_cp_async_commit();
+        const float *sl = zsm + slot * L::SL;
+        slot = slot + 1 == ZS_R ? 0 : slot + 1;
+        float2 v[KK];
 #pragma unroll
-        for (int u = 0; u < Z3_UZ; ++u)
+        for (int j = 0; j < KK; ++j) v[j] = *reinterpret_cast<const float2 *>(sl + nb[j]);
+#pragma unroll
+        for (int oz = 0; oz < K; ++oz)
 #pragma unroll
             for (int j = 0; j < KK; ++j)
-                v[u][j] = ok[j] && t + u < q.Z ? ld2(src + zo + u * zstep + off[j])
-                                               : kmb_f2s(0.f);
+                acc[oz] = kmb_fma2(v[j], wt[KV - 1 - (oz * KK + j)], acc[oz]);
+        if (q.on) *reinterpret_cast<float2 *>(dst + zof(t)) = acc[0];
 #pragma unroll
-        for (int u = 0; u < Z3_UZ; ++u) {
-            if (t + u >= q.Z) break;
-#pragma unroll
-            for (int oz = 0; oz < K; ++oz)
-#pragma unroll
-                for (int j = 0; j < KK; ++j)
-                    acc[oz] = kmb_fma2(v[u][j], wt[KV - 1 - (oz * KK + j)], acc[oz]);
-            *reinterpret_cast<float2 *>(dst + zo) = acc[0];
-#pragma unroll
-            for (int i = 0; i + 1 < K; ++i) acc[i] = acc[i + 1];
-            acc[K - 1] = b2;
-            zo += zstep;
-        }
+        for (int i = 0; i + 1 < K; ++i) acc[i] = acc[i + 1];
+        acc[K - 1] = b2;
     }
 }
 
 template <int K>
-__global__ void __launch_bounds__(Z3_THREADS, 1) k_conv3d_zwalk_param(ConvDev p) {
+__global__ void __launch_bounds__(Z3_THREADS, 1) k_conv3d_zring_param(ConvDev p) {
+    using L = ZSLayout<K>;
     constexpr int KK = K * K, KV = K * KK;
+    constexpr int SLOT = L::SL + L::SLD;
+    extern __shared__ __align__(16) float zsm[];
     __shared__ float2 red[Z3_THREADS / 32][32];
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int ty = w / Z3_TX, tx = w % Z3_TX;
     const Col3 q = col3(p);
+    const long c0 = (long)blockIdx.x * Z3_CH;
+    const int y0 = q.y - ty, x0 = q.x - tx;
+    ZSJobs<K, -1> jobs;
+    jobs.init(p, y0, x0, c0, tid);
+    /* dy of the CTA's own columns: one 16-byte chunk for threads < 256 */
+    const int dcol = tid / (Z3_CH / 4), dch = tid % (Z3_CH / 4);
+    const int dyy = y0 + dcol / Z3_TX, dxx = x0 + dcol % Z3_TX;
+    const bool dok = tid < Z3_TY * Z3_TX * (Z3_CH / 4) && dyy < q.Y && dxx < q.X &&
+                     c0 + dch * 4 < p.D;
+    const long dsrc = dok ? (long)blockIdx.z * p.P * p.D + ((long)dyy * q.X + dxx) * p.D + c0 +
+                                dch * 4
+                          : 0;
+    const int ddst = L::SL + dcol * Z3_CH + dch * 4;
+    auto issue = [&](int s) { /* input slice s and dy slice s + K - 1 */
+        float *slot = zsm + (s % ZS_R) * SLOT;
+        jobs.issue(slot, p.in, (long)s * q.sz);
+        if (tid < Z3_TY * Z3_TX * (Z3_CH / 4)) {
+            const bool ok = dok && s + K - 1 < q.Z;
+            kmb_cp_async16(slot + ddst, p.dy + (ok ? dsrc + (long)(s + K - 1) * q.sz : 0),
+                           ok ? 16 : 0);
+        }
+    };
+#pragma unroll 1
+    for (int s = 0; s < ZS_R - 1; ++s) {
+        if (s < q.Z) issue(s);
+        kmb_cp_async_commit();
+    }
+    int nb[KK];
+#pragma unroll
+    for (int oy = 0; oy < K; ++oy)
+#pragma unroll
+        for (int ox = 0; ox < K; ++ox)
+            nb[oy * K + ox] = ((ty + (K - 1) - oy) * L::CX + tx + (K - 1) - ox) * Z3_CH + lane * 2;
+    const int dme = L::SL + w * Z3_CH + lane * 2; /* this lane's dy in a slot */
     float2 acc[KV], accb = kmb_f2s(0.f);
 #pragma unroll
     for (int k = 0; k < KV; ++k) acc[k] = kmb_f2s(0.f);
-    if (q.on) {
-        int off[KK];
-        bool ok[KK];
+    float2 dyw[K]; /* dy of this column at slices s .. s + K - 1 */
 #pragma unroll
-        for (int oy = 0; oy < K; ++oy)
-#pragma unroll
-            for (int ox = 0; ox < K; ++ox) {
-                off[oy * K + ox] = -(oy * q.sy + ox * (int)p.D);
-                ok[oy * K + ox] = q.y >= oy && q.x >= ox;
-            }
-        const float *inp = p.in + q.base;
-        const float *dyp = p.dy + q.base;
-        float2 dyw[K]; /* dy of this column at slices s .. s + K - 1 */
-#pragma unroll
-        for (int i = 0; i + 1 < K; ++i) dyw[i] = i < q.Z ? ld2(dyp + i * q.sz) : kmb_f2s(0.f);
-        int zo = 0;
+    for (int i = 0; i + 1 < K; ++i)
+        dyw[i] = q.on && i < q.Z ? ld2(p.dy + q.base + (long)i * q.sz) : kmb_f2s(0.f);
 #pragma unroll 1
-        for (int s = 0; s < q.Z; s += Z3_UZ) {
-            /* the loads of Z3_UZ slices first */
-            float2 v[Z3_UZ][KK], dn[Z3_UZ];
+    for (int s = 0; s < q.Z; ++s) {
+        kmb_cp_async_wait<ZS_R - 2>();
+        __syncthreads();
+        if (s + ZS_R - 1 < q.Z) issue(s + ZS_R - 1);
+        kmb_cp_async_commit();
+        const float *sl = zsm + (s % ZS_R) * SLOT;
+        dyw[K - 1] = *reinterpret_cast<const float2 *>(sl + dme);
+        float2 v[KK];
 #pragma unroll
-            for (int u = 0; u < Z3_UZ; ++u) {
-                dn[u] = s + u + K - 1 < q.Z ? ld2(dyp + zo + (u + K - 1) * q.sz) : kmb_f2s(0.f);
+        for (int j = 0; j < KK; ++j) v[j] = *reinterpret_cast<const float2 *>(sl + nb[j]);
 #pragma unroll
-                for (int j = 0; j < KK; ++j)
-                    v[u][j] = ok[j] && s + u < q.Z ? ld2(inp + zo + u * q.sz + off[j])
-                                                   : kmb_f2s(0.f);
-            }
+        for (int oz = 0; oz < K; ++oz)
 #pragma unroll
-            for (int u = 0; u < Z3_UZ; ++u) {
-                dyw[K - 1] = dn[u];
+            for (int j = 0; j < KK; ++j)
+                acc[KV - 1 - (oz * KK + j)] =
+                    kmb_fma2(dyw[oz], v[j], acc[KV - 1 - (oz * KK + j)]);
+        accb = kmb_add2(accb, dyw[0]);
 #pragma unroll
-                for (int oz = 0; oz < K; ++oz)
+        for (int i = 0; i + 1 < K; ++i) dyw[i] = dyw[i + 1];
+    }
+    if (!q.on) {
+        accb = kmb_f2s(0.f);
 #pragma unroll
-                    for (int j = 0; j < KK; ++j)
-                        acc[KV - 1 - (oz * KK + j)] =
-                            kmb_fma2(dyw[oz], v[u][j], acc[KV - 1 - (oz * KK + j)]);
-                accb = kmb_add2(accb, dyw[0]);
-#pragma unroll
-                for (int i = 0; i + 1 < K; ++i) dyw[i] = dyw[i + 1];
-            }
-            zo += Z3_UZ * q.sz;
-        }
+        for (int k = 0; k < KV; ++k) acc[k] = kmb_f2s(0.f);
     }
     /* fold the CTA's columns, one tap at a time */
     const int ntap = p.dbias ? KV + 1 : KV;
@@ -838,28 +927,39 @@ __global__ void __launch_bounds__(Z3_THREADS, 1) k_conv3d_zwalk_param(ConvDev p)
 }
 
 template <int K>
-cudaError_t launch3d_zwalk(const ConvDev &p, bool bwd, cudaStream_t s) {
+cudaError_t launch3d_zring(const ConvDev &p, bool bwd, cudaStream_t s) {
+    using L = ZSLayout<K>;
     const unsigned tiles = (unsigned)(((p.dims[1] + Z3_TY - 1) / Z3_TY) *
                                       ((p.dims[2] + Z3_TX - 1) / Z3_TX));
-    /* channel blocks fastest: the CTAs of a tile run together and read
-     * whole point vectors of each slice at about the same time */
     dim3 grid((unsigned)((p.D + Z3_CH - 1) / Z3_CH), tiles, (unsigned)p.batch);
+    const size_t sm1 = sizeof(float) * ZS_R * L::SL;
+    const size_t sm2 = sizeof(float) * ZS_R * (L::SL + L::SLD);
+    cudaError_t e;
     if (!bwd) {
-        k_conv3d_zwalk<K, -1><<<grid, Z3_THREADS, 0, s>>>(p);
+        e = cudaFuncSetAttribute(k_conv3d_zring<K, -1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)sm1);
+        if (e != cudaSuccess) return e;
+        k_conv3d_zring<K, -1><<<grid, Z3_THREADS, sm1, s>>>(p);
         return cudaGetLastError();
     }
-    k_conv3d_zwalk<K, +1><<<grid, Z3_THREADS, 0, s>>>(p);
-    cudaError_t e = cudaGetLastError();
+    e = cudaFuncSetAttribute(k_conv3d_zring<K, +1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)sm1);
     if (e != cudaSuccess) return e;
-    k_conv3d_zwalk_param<K><<<grid, Z3_THREADS, 0, s>>>(p);
+    k_conv3d_zring<K, +1><<<grid, Z3_THREADS, sm1, s>>>(p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(k_conv3d_zring_param<K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)sm2);
+    if (e != cudaSuccess) return e;
+    k_conv3d_zring_param<K><<<grid, Z3_THREADS, sm2, s>>>(p);
     return cudaGetLastError();
 }
 
 cudaError_t dispatch3d(const ConvDev &p, bool bwd, cudaStream_t s) {
     switch (p.K) {
-    case 1: return launch3d_zwalk<1>(p, bwd, s);
-    case 2: return launch3d_zwalk<2>(p, bwd, s);
-    case 3: return launch3d_zwalk<3>(p, bwd, s);
+    case 1: return launch3d_zring<1>(p, bwd, s);
+    case 2: return launch3d_zring<2>(p, bwd, s);
+    case 3: return launch3d_zring<3>(p, bwd, s);
     default: return cudaErrorNotSupported;
     }
 }
