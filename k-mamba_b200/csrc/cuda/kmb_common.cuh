@@ -95,6 +95,18 @@ __device__ __forceinline__ void kmb_cp_async16(void *smem, const void *gmem,
                  "l"(gmem), "r"(src_bytes));
 }
 
+/* The same with the destination as a shared-window address (the result
+ * of __cvta_generic_to_shared), for loops that keep a base address. */
+__device__ __forceinline__ void kmb_cp_async16_s(unsigned s, const void *gmem, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem),
+                 "r"(src_bytes));
+}
+
+__device__ __forceinline__ void kmb_cp_async4_s(unsigned s, const void *gmem, int src_bytes) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(s), "l"(gmem),
+                 "r"(src_bytes));
+}
+
 __device__ __forceinline__ void kmb_cp_async_commit() {
     asm volatile("cp.async.commit_group;\n" ::);
 }

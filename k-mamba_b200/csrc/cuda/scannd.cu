@@ -393,6 +393,7 @@ __global__ void __launch_bounds__(kWWarpsF * 32) k_scannd_fwd_p(NDDev p) {
 #pragma unroll
     for (int a = 0; a < ND; ++a) amin[a] = lane_amin(A2[a]);
     float *wb = fsm + w * S * L::SIZE; /* this warp's ring of S slots */
+    const unsigned wbs = (unsigned)__cvta_generic_to_shared(wb);
     const float *hg = p.h + b * p.h_bs + d0 * 16 + lane * 4; /* + point * D * 16 */
     float *hq = p.h + b * p.h_bs + d0 * 16 + lane * 4;
     float *yq = p.y + b * p.x_bs + d;
@@ -414,7 +415,6 @@ __global__ void __launch_bounds__(kWWarpsF * 32) k_scannd_fwd_p(NDDev p) {
     /* B (lanes 0-3) and C (lanes 4-7): one 16-byte chunk each */
     const float *bcsrc = (lane < 4 ? p.B : p.C) + b * p.bc_bs + (lane & 3) * 4;
     const int bcdst = (lane < 4 ? L::B : L::C) + (lane & 3) * 4;
-    const size_t hrow = (size_t)Du * 16;
     const int *lvl_off = p.lvl_off, *sprev = p.sprev, *lvl_start = p.lvl_start;
     const int nlevels = p.nlevels;
 
@@ -430,19 +430,22 @@ __global__ void __launch_bounds__(kWWarpsF * 32) k_scannd_fwd_p(NDDev p) {
             __syncwarp();
             const int cnt = min(32, (s1 - base + kWWarpsF - 1) / kWWarpsF);
             auto issue = [&](int j, int slot) {
-                float *bf = wb + slot * L::SIZE;
+                const unsigned bs = wbs + slot * (L::SIZE * 4); /* shared address of the slot */
                 int ix[ND + 1];
                 load_idx<ND>(sidx[w][j], ix);
+                /* a missing predecessor's row is zero-filled: it adds exactly 0 */
 #pragma unroll
-                for (int a = 0; a < ND; ++a)
-                    if (ix[1 + a] >= 0)
-                        kmb_cp_async16(bf + L::HP + a * kWCh * 16 + lane * 4,
-                                       hg + (size_t)(unsigned)ix[1 + a] * hrow, 16);
-                const size_t od = (size_t)(unsigned)ix[0] * Du;
+                for (int a = 0; a < ND; ++a) {
+                    const bool ok = ix[1 + a] >= 0;
+                    kmb_cp_async16_s(bs + (L::HP + a * kWCh * 16 + lane * 4) * 4,
+                                     hg + (ok ? (size_t)((unsigned)ix[1 + a] * Du) * 16 : 0),
+                                     ok ? 16 : 0);
+                }
+                const unsigned od = (unsigned)ix[0] * Du;
 #pragma unroll
                 for (int i = 0; i < L::NJ; ++i)
-                    if (vok[i]) kmb_cp_async4(bf + vdst[i], vsrc[i] + od, true);
-                if (lane < 8) kmb_cp_async16(bf + bcdst, bcsrc + (size_t)(unsigned)ix[0] * 16, 16);
+                    if (vok[i]) kmb_cp_async4_s(bs + vdst[i] * 4, vsrc[i] + od, 4);
+                if (lane < 8) kmb_cp_async16_s(bs + bcdst * 4, bcsrc + (unsigned)ix[0] * 16, 16);
             };
             int si = 0, sc = 0; /* ring slots of the next issue and of the next compute */
 #pragma unroll
@@ -476,7 +479,7 @@ __global__ void __launch_bounds__(kWWarpsF * 32) k_scannd_fwd_p(NDDev p) {
 #pragma unroll
                 for (int a = 0; a < ND; ++a) {
                     dt_bar += dx[a];
-                    weak |= (ix[1 + a] >= 0) & (fabsf(dx[a]) * amin[a] < KMB_DECAY_POLY_MAX);
+                    weak |= fabsf(dx[a]) * amin[a] < KMB_DECAY_POLY_MAX;
                 }
                 dt_bar *= kInvND;
                 /* MUFU only where no lane of the warp needs the polynomial */
@@ -490,18 +493,16 @@ __global__ void __launch_bounds__(kWWarpsF * 32) k_scannd_fwd_p(NDDev p) {
                 auto carry = [&](auto fast_tag) {
                     constexpr bool FAST = decltype(fast_tag)::value;
 #pragma unroll
-                    for (int a = 0; a < ND; ++a) {
-                        if (ix[1 + a] >= 0) {
-                            const float4 hp = *reinterpret_cast<const float4 *>(
-                                bf + L::HP + a * kWCh * 16 + lane * 4);
-                            const float2 dv2 = kmb_f2s(dx[a]);
-                            const float2 w0 = kmb_mul2(dv2, A2[a][0]);
-                            const float2 w1 = kmb_mul2(dv2, A2[a][1]);
-                            const float2 e0 = FAST ? kmb_ex2_2(w0) : kmb_exp2_decay2(w0);
-                            const float2 e1 = FAST ? kmb_ex2_2(w1) : kmb_exp2_decay2(w1);
-                            hn[0] = kmb_fma2(e0, kmb_f2(hp.x, hp.y), hn[0]);
-                            hn[1] = kmb_fma2(e1, kmb_f2(hp.z, hp.w), hn[1]);
-                        }
+                    for (int a = 0; a < ND; ++a) { /* zero rows for missing predecessors */
+                        const float4 hp = *reinterpret_cast<const float4 *>(
+                            bf + L::HP + a * kWCh * 16 + lane * 4);
+                        const float2 dv2 = kmb_f2s(dx[a]);
+                        const float2 w0 = kmb_mul2(dv2, A2[a][0]);
+                        const float2 w1 = kmb_mul2(dv2, A2[a][1]);
+                        const float2 e0 = FAST ? kmb_ex2_2(w0) : kmb_exp2_decay2(w0);
+                        const float2 e1 = FAST ? kmb_ex2_2(w1) : kmb_exp2_decay2(w1);
+                        hn[0] = kmb_fma2(e0, kmb_f2(hp.x, hp.y), hn[0]);
+                        hn[1] = kmb_fma2(e1, kmb_f2(hp.z, hp.w), hn[1]);
                     }
                 };
                 if (fast)
@@ -755,6 +756,7 @@ __global__ void __launch_bounds__(kWWarpsA * 32) k_scannd_adj_p(NDDev p) {
 #pragma unroll
     for (int a = 0; a < ND; ++a) amin[a] = lane_amin(A2[a]);
     float *wb = asm_ + w * S * L::SIZE;
+    const unsigned wbs = (unsigned)__cvta_generic_to_shared(wb);
     const float *gg_src = p.G + b * p.h_bs + d0 * 16 + lane * 4; /* + point * D * 16 */
     float *gq = p.G + b * p.h_bs + d0 * 16 + lane * 4;
     /* this lane's 4-byte copies: value v of channel ch: delta_v of the
@@ -777,7 +779,6 @@ __global__ void __launch_bounds__(kWWarpsA * 32) k_scannd_adj_p(NDDev p) {
     }
     const float *csrc = p.C + b * p.bc_bs + (lane & 3) * 4;
     const int cdst = L::C + (lane & 3) * 4;
-    const size_t hrow = (size_t)Du * 16;
     const int *lvl_off = p.lvl_off, *snext = p.snext, *lvl_start = p.lvl_start;
 
     for (int l = p.nlevels - 1; l >= 0; --l) {
@@ -792,21 +793,26 @@ __global__ void __launch_bounds__(kWWarpsA * 32) k_scannd_adj_p(NDDev p) {
             __syncwarp();
             const int cnt = min(32, (s1 - base + kWWarpsA - 1) / kWWarpsA);
             auto issue = [&](int j, int slot) {
-                float *bf = wb + slot * L::SIZE;
+                const unsigned bs = wbs + slot * (L::SIZE * 4); /* shared address of the slot */
                 int ix[ND + 1];
                 load_idx<ND>(sidx[w][j], ix);
+                /* a missing successor's row and delta are zero-filled: the row adds 0 */
 #pragma unroll
-                for (int a = 0; a < ND; ++a)
-                    if (ix[1 + a] >= 0)
-                        kmb_cp_async16(bf + L::GN + a * kWCh * 16 + lane * 4,
-                                       gg_src + (size_t)(unsigned)ix[1 + a] * hrow, 16);
+                for (int a = 0; a < ND; ++a) {
+                    const bool ok = ix[1 + a] >= 0;
+                    kmb_cp_async16_s(bs + (L::GN + a * kWCh * 16 + lane * 4) * 4,
+                                     gg_src + (ok ? (size_t)((unsigned)ix[1 + a] * Du) * 16 : 0),
+                                     ok ? 16 : 0);
+                }
 #pragma unroll
                 for (int i = 0; i < L::NJ; ++i) {
                     const int row = sidx[w][j][vrow[i]];
-                    if (vok[i] && row >= 0)
-                        kmb_cp_async4(bf + vdst[i], vsrc[i] + (size_t)(unsigned)row * Du, true);
+                    const bool ok = row >= 0;
+                    if (vok[i])
+                        kmb_cp_async4_s(bs + vdst[i] * 4, vsrc[i] + (ok ? (unsigned)row * Du : 0),
+                                        ok ? 4 : 0);
                 }
-                if (lane < 4) kmb_cp_async16(bf + cdst, csrc + (size_t)(unsigned)ix[0] * 16, 16);
+                if (lane < 4) kmb_cp_async16_s(bs + cdst * 4, csrc + (unsigned)ix[0] * 16, 16);
             };
             int si = 0, sc = 0; /* ring slots of the next issue and of the next compute */
 #pragma unroll
@@ -836,8 +842,7 @@ __global__ void __launch_bounds__(kWWarpsA * 32) k_scannd_adj_p(NDDev p) {
                         *reinterpret_cast<const float4 *>(bf + L::DD + c * L::XW + i);
                 bool weak = false;
 #pragma unroll
-                for (int a = 0; a < ND; ++a)
-                    weak |= (ix[1 + a] >= 0) & (fabsf(dd[a]) * amin[a] < KMB_DECAY_POLY_MAX);
+                for (int a = 0; a < ND; ++a) weak |= fabsf(dd[a]) * amin[a] < KMB_DECAY_POLY_MAX;
                 /* MUFU only where no lane of the warp needs the polynomial */
                 const bool fast = !__any_sync(kWFull, weak);
                 const float4 C4 = *reinterpret_cast<const float4 *>(bf + L::C + q * 4);
@@ -847,18 +852,16 @@ __global__ void __launch_bounds__(kWWarpsA * 32) k_scannd_adj_p(NDDev p) {
                 auto carry = [&](auto fast_tag) {
                     constexpr bool FAST = decltype(fast_tag)::value;
 #pragma unroll
-                    for (int a = 0; a < ND; ++a) {
-                        if (ix[1 + a] >= 0) {
-                            const float4 gn = *reinterpret_cast<const float4 *>(
-                                bf + L::GN + a * kWCh * 16 + lane * 4);
-                            const float2 dn2 = kmb_f2s(dd[a]);
-                            const float2 w0 = kmb_mul2(dn2, A2[a][0]);
-                            const float2 w1 = kmb_mul2(dn2, A2[a][1]);
-                            const float2 e0 = FAST ? kmb_ex2_2(w0) : kmb_exp2_decay2(w0);
-                            const float2 e1 = FAST ? kmb_ex2_2(w1) : kmb_exp2_decay2(w1);
-                            gg[0] = kmb_fma2(e0, kmb_f2(gn.x, gn.y), gg[0]);
-                            gg[1] = kmb_fma2(e1, kmb_f2(gn.z, gn.w), gg[1]);
-                        }
+                    for (int a = 0; a < ND; ++a) { /* zero rows for missing successors */
+                        const float4 gn = *reinterpret_cast<const float4 *>(
+                            bf + L::GN + a * kWCh * 16 + lane * 4);
+                        const float2 dn2 = kmb_f2s(dd[a]);
+                        const float2 w0 = kmb_mul2(dn2, A2[a][0]);
+                        const float2 w1 = kmb_mul2(dn2, A2[a][1]);
+                        const float2 e0 = FAST ? kmb_ex2_2(w0) : kmb_exp2_decay2(w0);
+                        const float2 e1 = FAST ? kmb_ex2_2(w1) : kmb_exp2_decay2(w1);
+                        gg[0] = kmb_fma2(e0, kmb_f2(gn.x, gn.y), gg[0]);
+                        gg[1] = kmb_fma2(e1, kmb_f2(gn.z, gn.w), gg[1]);
                     }
                 };
                 if (fast)
