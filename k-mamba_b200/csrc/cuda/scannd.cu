@@ -1014,12 +1014,14 @@ struct GradS {
 
 /* grad_point's terms with the sums over a channel's 4 lanes reduce-
  * scattered: lane q stores dx (q 0) or ddelta_{q-1}; a fifth value
- * (ddelta_3 of 4 axes) is summed by butterfly and stored by lane 0. */
-template <int ND>
+ * (ddelta_3 of 4 axes) is summed by butterfly and stored by lane 0.
+ * FAST: no decay exponent of the point is in the polynomial range, so
+ * kmb_exp2_decay2 would return the MUFU values, which are used directly. */
+template <int ND, bool FAST>
 __device__ __forceinline__ void grad_point16(
     const float4 &B4, const float4 &H4, const float4 &G4, const float4 (&hp)[ND],
     const int (&pv)[ND], float xv, float gy, const float (&dta)[ND],
-    const float2 (&A2)[ND][2], const float2 (&Ar)[ND][2], float2 (&dAp)[ND][2], int lane,
+    const float2 (&A2)[ND][2], float2 (&dAp)[ND][2], int lane,
     int c, int q, float *out0, float *out4, float *dBrow, float *dCrow) {
     constexpr float kInvND = 1.0f / ND; /* the mean within 1 ulp of a division */
     float dt_bar = 0.f;
@@ -1051,10 +1053,11 @@ __device__ __forceinline__ void grad_point16(
             const float2 hpp[2] = {kmb_f2(hp[a].x, hp[a].y), kmb_f2(hp[a].z, hp[a].w)};
 #pragma unroll
             for (int jp = 0; jp < 2; ++jp) {
-                const float2 e = kmb_exp2_decay2(kmb_mul2(dv2, A2[a][jp]));
+                const float2 wv = kmb_mul2(dv2, A2[a][jp]);
+                const float2 e = FAST ? kmb_ex2_2(wv) : kmb_exp2_decay2(wv);
                 const float2 gh = kmb_mul2(kmb_mul2(gg[jp], hpp[jp]), e);
                 dAp[a][jp] = kmb_fma2(gh, dv2, dAp[a][jp]);
-                sdt2[a] = kmb_fma2(gh, Ar[a][jp], sdt2[a]);
+                sdt2[a] = kmb_fma2(gh, A2[a][jp], sdt2[a]); /* A log2 e: times ln 2 below */
             }
         }
     }
@@ -1062,7 +1065,7 @@ __device__ __forceinline__ void grad_point16(
     const float sbn = (sb2.x + sb2.y) * kInvND;
     float v[4] = {sx2.x + sx2.y, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int a = 0; a < ND && a < 3; ++a) v[1 + a] = sdt2[a].x + sdt2[a].y + sbn;
+    for (int a = 0; a < ND && a < 3; ++a) v[1 + a] = (sdt2[a].x + sdt2[a].y) * KMB_LN2 + sbn;
     /* reduce-scatter over the channel's 4 lanes (q = lane bits 0-1) */
     const bool hi = q & 2, lo = q & 1;
     float k0 = hi ? v[2] : v[0], k1 = hi ? v[3] : v[1];
@@ -1073,7 +1076,7 @@ __device__ __forceinline__ void grad_point16(
     const float mine = keep + __shfl_xor_sync(kWFull, send, 1);
     if (q <= ND) *out0 = mine;
     if constexpr (ND == 4) {
-        float v4 = sdt2[3].x + sdt2[3].y + sbn;
+        float v4 = (sdt2[3].x + sdt2[3].y) * KMB_LN2 + sbn;
         v4 += __shfl_xor_sync(kWFull, v4, 1);
         v4 += __shfl_xor_sync(kWFull, v4, 2);
         if (q == 0) *out4 = v4;
@@ -1099,17 +1102,19 @@ __global__ void __launch_bounds__(kSW * 32, 1) k_scannd_grad_s(NDDev p, GradS g)
     const long b = blockIdx.z;
     const long d0 = (long)blockIdx.y * kWCh;
     const long d = d0 + c;
-    float2 A2[ND][2], Ar[ND][2], dAp[ND][2];
+    float2 A2[ND][2], dAp[ND][2];
 #pragma unroll
     for (int a = 0; a < ND; ++a)
 #pragma unroll
         for (int jp = 0; jp < 2; ++jp) {
             const float *ap = p.A[a] + d * 16 + q * 4 + 2 * jp;
             const float2 av = kmb_f2(ap[0], ap[1]);
-            Ar[a][jp] = av;
             A2[a][jp] = kmb_f2(av.x * KMB_LOG2E, av.y * KMB_LOG2E);
             dAp[a][jp] = kmb_f2s(0.f);
         }
+    float amin[ND];
+#pragma unroll
+    for (int a = 0; a < ND; ++a) amin[a] = lane_amin(A2[a]);
     const long D = p.D;
     const size_t hrow = (size_t)D * 16; /* floats between two points' state rows */
     const float *hg = p.h + b * p.h_bs + d0 * 16 + lane * 4;
@@ -1207,6 +1212,19 @@ __global__ void __launch_bounds__(kSW * 32, 1) k_scannd_grad_s(NDDev p, GradS g)
         const float *st = stages + (k % SS) * L::STAGE;
         const int *spv = reinterpret_cast<const int *>(st + L::O_PV);
         const int sb = (k % (R / kST)) * kST; /* ring row of the stage's first point */
+        /* MUFU only where no lane needs the polynomial for the warp's points
+         * (missing predecessors are included: conservative) */
+        bool weak = false;
+#pragma unroll
+        for (int u = 0; u < kST / kSW; ++u) {
+            const int r = w + u * kSW;
+#pragma unroll
+            for (int a = 0; a < ND; ++a)
+                weak |= fabsf(st[L::O_X + ((2 + a) * kST + r) * kWCh + c]) * amin[a] <
+                        KMB_DECAY_POLY_MAX;
+        }
+        auto points = [&](auto fast_tag) {
+        constexpr bool FAST = decltype(fast_tag)::value;
         /* a warp's points interleaved (3 axes; 4 would spill) */
         constexpr int kUnroll = ND == 3 ? kST / kSW : 1;
 #pragma unroll kUnroll
@@ -1248,9 +1266,14 @@ __global__ void __launch_bounds__(kSW * 32, 1) k_scannd_grad_s(NDDev p, GradS g)
                     hp[a] = *reinterpret_cast<const float4 *>(src + lane * 4);
                 }
             const long od = pt * D;
-            grad_point16<ND>(B4, H4, G4, hp, pv, xv, gy, dta, A2, Ar, dAp, lane, c, q, ob + od,
-                             ob4 + od, dBb + pt * 16, dCb + pt * 16);
+            grad_point16<ND, FAST>(B4, H4, G4, hp, pv, xv, gy, dta, A2, dAp, lane, c, q,
+                                   ob + od, ob4 + od, dBb + pt * 16, dCb + pt * 16);
         }
+        };
+        if (__any_sync(kWFull, weak))
+            points(std::false_type{});
+        else
+            points(std::true_type{});
     }
     kmb_cp_async_wait<0>();
     __syncthreads();
