@@ -422,10 +422,14 @@ __global__ void __launch_bounds__(kWWarpsF * 32) k_scannd_fwd_p(NDDev p) {
         const int s0 = lvl_start[l], s1 = lvl_start[l + 1];
         for (int base = s0 + w; base < s1; base += kWWarpsF * 32) {
             const int sl = base + kWWarpsF * lane;
-            if (sl < s1) {
+            if (sl < s1) { /* the point; predecessors as element offsets (index x D,
+                            * < 2^31) or -1 */
                 sidx[w][lane][0] = lvl_off[sl];
 #pragma unroll
-                for (int a = 0; a < ND; ++a) sidx[w][lane][1 + a] = sprev[sl * ND + a];
+                for (int a = 0; a < ND; ++a) {
+                    const int pv = sprev[sl * ND + a];
+                    sidx[w][lane][1 + a] = pv >= 0 ? pv * (int)Du : -1;
+                }
             }
             __syncwarp();
             const int cnt = min(32, (s1 - base + kWWarpsF - 1) / kWWarpsF);
@@ -438,7 +442,7 @@ __global__ void __launch_bounds__(kWWarpsF * 32) k_scannd_fwd_p(NDDev p) {
                 for (int a = 0; a < ND; ++a) {
                     const bool ok = ix[1 + a] >= 0;
                     kmb_cp_async16_s(bs + (L::HP + a * kWCh * 16 + lane * 4) * 4,
-                                     hg + (ok ? (size_t)((unsigned)ix[1 + a] * Du) * 16 : 0),
+                                     hg + (size_t)(unsigned)(ok ? ix[1 + a] : 0) * 16,
                                      ok ? 16 : 0);
                 }
                 const unsigned od = (unsigned)ix[0] * Du;
@@ -764,6 +768,7 @@ __global__ void __launch_bounds__(kWWarpsA * 32) k_scannd_adj_p(NDDev p) {
      * the slot's index row (1 + v, or 0 for the point itself) */
     const float *vsrc[L::NJ];
     int vdst[L::NJ], vrow[L::NJ];
+    unsigned vmul[L::NJ]; /* D for dy (the slot holds the point index), 1 for the deltas */
     bool vok[L::NJ];
 #pragma unroll
     for (int i = 0; i < L::NJ; ++i) {
@@ -776,6 +781,7 @@ __global__ void __launch_bounds__(kWWarpsA * 32) k_scannd_adj_p(NDDev p) {
         vsrc[i] = src + d0 + ch;
         vdst[i] = L::DD + ch * L::XW + v;
         vrow[i] = v < ND ? 1 + v : 0;
+        vmul[i] = v < ND ? 1u : Du;
     }
     const float *csrc = p.C + b * p.bc_bs + (lane & 3) * 4;
     const int cdst = L::C + (lane & 3) * 4;
@@ -785,10 +791,14 @@ __global__ void __launch_bounds__(kWWarpsA * 32) k_scannd_adj_p(NDDev p) {
         const int s0 = lvl_start[l], s1 = lvl_start[l + 1];
         for (int base = s0 + w; base < s1; base += kWWarpsA * 32) {
             const int sl = base + kWWarpsA * lane;
-            if (sl < s1) {
+            if (sl < s1) { /* the point; successors as element offsets (index x D,
+                            * < 2^31) or -1 */
                 sidx[w][lane][0] = lvl_off[sl];
 #pragma unroll
-                for (int a = 0; a < ND; ++a) sidx[w][lane][1 + a] = snext[sl * ND + a];
+                for (int a = 0; a < ND; ++a) {
+                    const int nx = snext[sl * ND + a];
+                    sidx[w][lane][1 + a] = nx >= 0 ? nx * (int)Du : -1;
+                }
             }
             __syncwarp();
             const int cnt = min(32, (s1 - base + kWWarpsA - 1) / kWWarpsA);
@@ -801,7 +811,7 @@ __global__ void __launch_bounds__(kWWarpsA * 32) k_scannd_adj_p(NDDev p) {
                 for (int a = 0; a < ND; ++a) {
                     const bool ok = ix[1 + a] >= 0;
                     kmb_cp_async16_s(bs + (L::GN + a * kWCh * 16 + lane * 4) * 4,
-                                     gg_src + (ok ? (size_t)((unsigned)ix[1 + a] * Du) * 16 : 0),
+                                     gg_src + (size_t)(unsigned)(ok ? ix[1 + a] : 0) * 16,
                                      ok ? 16 : 0);
                 }
 #pragma unroll
@@ -809,8 +819,8 @@ __global__ void __launch_bounds__(kWWarpsA * 32) k_scannd_adj_p(NDDev p) {
                     const int row = sidx[w][j][vrow[i]];
                     const bool ok = row >= 0;
                     if (vok[i])
-                        kmb_cp_async4_s(bs + vdst[i] * 4, vsrc[i] + (ok ? (unsigned)row * Du : 0),
-                                        ok ? 4 : 0);
+                        kmb_cp_async4_s(bs + vdst[i] * 4,
+                                        vsrc[i] + (unsigned)(ok ? row : 0) * vmul[i], ok ? 4 : 0);
                 }
                 if (lane < 4) kmb_cp_async16_s(bs + cdst * 4, csrc + (unsigned)ix[0] * 16, 16);
             };
