@@ -223,6 +223,10 @@ constexpr int kWCh = 8;      /* channels per CTA */
  * 16.6 ms, 32 x 1 11.8 ms */
 constexpr int kWWarpsF = 32;
 constexpr unsigned kWFull = 0xffffffffu;
+/* warps per CTA of the pipelined sweeps (k_scannd_fwd_p / adj_p), 64^3 x
+ * 1024 forward ms: 16 warps 9.8, 20 9.5, 24 8.2, 32 8.9 (at 32 the
+ * 64-register cap makes the compiler recompute values in the loop) */
+constexpr int kPW = 24;
 
 
 template <int ND>
@@ -370,11 +374,11 @@ __device__ __forceinline__ void load_idx(const int (&row)[ND + 1], int (&ix)[ND 
 }
 
 template <int ND, int S>
-__global__ void __launch_bounds__(kWWarpsF * 32) k_scannd_fwd_p(NDDev p) {
+__global__ void __launch_bounds__(kPW * 32) k_scannd_fwd_p(NDDev p) {
     using L = FwdPSlot<ND>;
     constexpr float kInvND = 1.0f / ND;
     extern __shared__ __align__(16) float fsm[];
-    __shared__ __align__(16) int sidx[kWWarpsF][32][ND + 1];
+    __shared__ __align__(16) int sidx[kPW][32][ND + 1];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int c = lane >> 2, q = lane & 3;
     const long b = blockIdx.y;
@@ -420,8 +424,8 @@ __global__ void __launch_bounds__(kWWarpsF * 32) k_scannd_fwd_p(NDDev p) {
 
     for (int l = 0; l < nlevels; ++l) {
         const int s0 = lvl_start[l], s1 = lvl_start[l + 1];
-        for (int base = s0 + w; base < s1; base += kWWarpsF * 32) {
-            const int sl = base + kWWarpsF * lane;
+        for (int base = s0 + w; base < s1; base += kPW * 32) {
+            const int sl = base + kPW * lane;
             if (sl < s1) { /* the point; predecessors as element offsets (index x D,
                             * < 2^31) or -1 */
                 sidx[w][lane][0] = lvl_off[sl];
@@ -432,7 +436,7 @@ __global__ void __launch_bounds__(kWWarpsF * 32) k_scannd_fwd_p(NDDev p) {
                 }
             }
             __syncwarp();
-            const int cnt = min(32, (s1 - base + kWWarpsF - 1) / kWWarpsF);
+            const int cnt = min(32, (s1 - base + kPW - 1) / kPW);
             auto issue = [&](int j, int slot) {
                 const unsigned bs = wbs + slot * (L::SIZE * 4); /* shared address of the slot */
                 int ix[ND + 1];
@@ -531,7 +535,7 @@ __global__ void __launch_bounds__(kWWarpsF * 32) k_scannd_fwd_p(NDDev p) {
 /* ring depth of k_scannd_fwd_p within 227 KB of shared memory */
 template <int ND>
 constexpr int fwd_p_stages() {
-    return (size_t)kWWarpsF * 3 * FwdPSlot<ND>::SIZE * 4 + kWWarpsF * 32 * (ND + 1) * 4 <=
+    return (size_t)kPW * 3 * FwdPSlot<ND>::SIZE * 4 + kPW * 32 * (ND + 1) * 4 <=
                    227 * 1024
                ? 3
                : 2;
@@ -739,10 +743,10 @@ struct AdjPSlot {
 };
 
 template <int ND, int S>
-__global__ void __launch_bounds__(kWWarpsA * 32) k_scannd_adj_p(NDDev p) {
+__global__ void __launch_bounds__(kPW * 32) k_scannd_adj_p(NDDev p) {
     using L = AdjPSlot<ND>;
     extern __shared__ __align__(16) float asm_[];
-    __shared__ __align__(16) int sidx[kWWarpsA][32][ND + 1];
+    __shared__ __align__(16) int sidx[kPW][32][ND + 1];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int c = lane >> 2, q = lane & 3;
     const long b = blockIdx.y;
@@ -789,8 +793,8 @@ __global__ void __launch_bounds__(kWWarpsA * 32) k_scannd_adj_p(NDDev p) {
 
     for (int l = p.nlevels - 1; l >= 0; --l) {
         const int s0 = lvl_start[l], s1 = lvl_start[l + 1];
-        for (int base = s0 + w; base < s1; base += kWWarpsA * 32) {
-            const int sl = base + kWWarpsA * lane;
+        for (int base = s0 + w; base < s1; base += kPW * 32) {
+            const int sl = base + kPW * lane;
             if (sl < s1) { /* the point; successors as element offsets (index x D,
                             * < 2^31) or -1 */
                 sidx[w][lane][0] = lvl_off[sl];
@@ -801,7 +805,7 @@ __global__ void __launch_bounds__(kWWarpsA * 32) k_scannd_adj_p(NDDev p) {
                 }
             }
             __syncwarp();
-            const int cnt = min(32, (s1 - base + kWWarpsA - 1) / kWWarpsA);
+            const int cnt = min(32, (s1 - base + kPW - 1) / kPW);
             auto issue = [&](int j, int slot) {
                 const unsigned bs = wbs + slot * (L::SIZE * 4); /* shared address of the slot */
                 int ix[ND + 1];
@@ -889,7 +893,7 @@ __global__ void __launch_bounds__(kWWarpsA * 32) k_scannd_adj_p(NDDev p) {
 
 template <int ND>
 constexpr int adj_p_stages() {
-    return (size_t)kWWarpsA * 3 * AdjPSlot<ND>::SIZE * 4 + kWWarpsA * 32 * (ND + 1) * 4 <=
+    return (size_t)kPW * 3 * AdjPSlot<ND>::SIZE * 4 + kPW * 32 * (ND + 1) * 4 <=
                    227 * 1024
                ? 3
                : 2;
@@ -1401,11 +1405,11 @@ static cudaError_t launch_w(const NDDev &p, const KmbNDLaunch *a, bool bwd, cuda
     if (!bwd) {
         if (staged_rows(a, a->x)) {
             constexpr int S = fwd_p_stages<ND>();
-            constexpr size_t smem = (size_t)kWWarpsF * S * FwdPSlot<ND>::SIZE * sizeof(float);
+            constexpr size_t smem = (size_t)kPW * S * FwdPSlot<ND>::SIZE * sizeof(float);
             cudaError_t e = cudaFuncSetAttribute(
                 k_scannd_fwd_p<ND, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
             if (e != cudaSuccess) return e;
-            k_scannd_fwd_p<ND, S><<<grid, kWWarpsF * 32, smem, s>>>(p);
+            k_scannd_fwd_p<ND, S><<<grid, kPW * 32, smem, s>>>(p);
             return cudaGetLastError();
         }
         k_scannd_fwd_w<ND><<<grid, kWWarpsF * 32, 0, s>>>(p);
@@ -1414,11 +1418,11 @@ static cudaError_t launch_w(const NDDev &p, const KmbNDLaunch *a, bool bwd, cuda
     cudaError_t e;
     if (staged_rows(a, a->dy)) {
         constexpr int S = adj_p_stages<ND>();
-        constexpr size_t smem = (size_t)kWWarpsA * S * AdjPSlot<ND>::SIZE * sizeof(float);
+        constexpr size_t smem = (size_t)kPW * S * AdjPSlot<ND>::SIZE * sizeof(float);
         e = cudaFuncSetAttribute(k_scannd_adj_p<ND, S>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
-        k_scannd_adj_p<ND, S><<<grid, kWWarpsA * 32, smem, s>>>(p);
+        k_scannd_adj_p<ND, S><<<grid, kPW * 32, smem, s>>>(p);
     } else {
         k_scannd_adj_w<ND><<<grid, kWWarpsA * 32, 0, s>>>(p);
     }
