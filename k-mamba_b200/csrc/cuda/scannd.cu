@@ -559,12 +559,14 @@ __device__ __forceinline__ float rs8_ch(float (&v)[8], int lane) {
     return v[0];
 }
 
-/* The backward in two passes.  (A) k_scannd_adj_w walks the levels in
- * reverse and only carries the adjoint
+/* The backward in two passes.  (A) An adjoint sweep (k_scannd_adj_p for
+ * M = 16, k_scannd_adj_w otherwise) walks the levels in reverse and only
+ * carries the adjoint
  *   G(p) = C dy + sum_axis e_axis(p+e) G(p+e)
- * into the scratch G (few registers: 32 warps per CTA).  (B)
- * k_scannd_grad_w then has no dependency between points and runs over all
- * of them in parallel: per point
+ * into the scratch G (few registers, many warps per CTA).  (B) The
+ * gradient pass (k_scannd_grad_s, or k_scannd_grad_w) then has no
+ * dependency between points and runs over all of them in parallel: per
+ * point
  *   dC += dy h,  dB += G dt_bar x  (folded over the 8 channels, one
  *   128-bit atomic per point, state quad and array),
  *   dx = sum_m (G dt_bar) B,  ddelta_axis = sum_m (G h(p-e)) e A_axis
@@ -899,8 +901,11 @@ constexpr int adj_p_stages() {
                : 2;
 }
 
-constexpr int kGWarps = 8;    /* warps per CTA of the gradient pass */
-constexpr int kGPts = 2048;   /* points per CTA of the gradient pass */
+/* k_scannd_grad_w: the gradient pass with per-point loads, for what the
+ * staged k_scannd_grad_s below does not take (M != 16, rows not 16-byte
+ * aligned) */
+constexpr int kGWarps = 8;    /* warps per CTA */
+constexpr int kGPts = 2048;   /* points per CTA */
 
 template <int ND>
 __global__ void __launch_bounds__(kGWarps * 32) k_scannd_grad_w(NDDev p) {
