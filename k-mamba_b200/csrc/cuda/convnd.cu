@@ -657,65 +657,71 @@ cudaError_t dispatch2d_bwd_ring(const ConvDev &p, cudaStream_t s) {
 
 /*
  * 3D causal depthwise convolution (the Mamba-ND volumes) for K <= 3, D a
- * multiple of 4 and 16-byte aligned tensors.  A warp owns one (y, x)
- * column of the volume and 64 channels (2 per lane); a CTA is a 4 x 4
- * tile of columns, and channel blocks are the fastest grid dimension (a
- * tile's CTAs read whole point vectors together).  The lane keeps its
+ * multiple of 4 and 16-byte aligned tensors.  A warp owns two x-adjacent
+ * (y, x) columns of the volume and 64 channels (2 per lane); a CTA is a
+ * 4 x 8 tile of columns, and channel blocks are the fastest grid dimension
+ * (a tile's CTAs read whole point vectors together).  The lane keeps its
  * channels' K^3 taps in registers and walks z, so each input slice is
- * read once and feeds K rolling output accumulators:
+ * read once and feeds K rolling output accumulators per column:
  *   forward (z ascending)  out(z) = bias + sum_o in(z - oz, y - oy, x - ox) w[K-1-o]
  *   dinput  (z descending) din(z) = sum_o dy(z + oz, y + oy, x + ox) w[K-1-o]
  * after slice s the accumulator of the output at s is complete.  dkernel
- * keeps K^3 accumulators and a window of K dy slices instead:
+ * keeps K^3 accumulators and a window of K dy slices per column instead:
  *   dker[K-1-o] += dy(s + oz, y, x) in(s, y - oy, x - ox),  dbias += dy(s)
- * and folds them over the CTA's 16 columns, one atomic per (tap, channel).
- * HBM sees one read of each input and one write of each output.
+ * and folds them over the CTA's warps, one atomic per (tap, channel).
+ *
+ * The slices are staged: the CTA's input slices (its columns and the K - 1
+ * halo columns on each in-plane axis, 64 channels) stream through a ring
+ * of ZS_R slices in shared memory (cp.async, 16-byte chunks, zero-filled
+ * outside the volume), ZS_R - 1 slices ahead of the compute, so the loads
+ * in flight cost no registers.  A lane reads the K x (K + 1) neighbours
+ * of its column pair from the slice (8-byte reads of 256-byte column
+ * rows).  dkernel stages the dy slice of its own columns K - 1 slices
+ * ahead of the input slice, for its windows of dy.  HBM sees one read of
+ * each input and one write of each output.
  */
-constexpr int Z3_TY = 4, Z3_TX = 4;           /* columns of a CTA */
-constexpr int Z3_CH = 64;                     /* channels of a CTA (a warp) */
-constexpr int Z3_THREADS = Z3_TY * Z3_TX * 32;
+constexpr int Z3_TY = 4, Z3_TX = 8;                      /* columns of a CTA */
+constexpr int Z3_PX = 2;                                 /* x-adjacent columns of a warp */
+constexpr int Z3_CH = 64;                                /* channels of a CTA (a warp) */
+constexpr int Z3_THREADS = Z3_TY * Z3_TX / Z3_PX * 32;
+constexpr int ZS_R = 8;                                  /* slices in the ring */
 
-struct Col3 {
-    int Z, Y, X, y, x;
-    int sz, sy;  /* element strides of z and y (P * D < 2^31) */
-    long c;      /* first of the lane's 2 channels */
-    long base;   /* element offset of (b, z = 0, y, x, c) */
-    bool on;     /* column and channels inside the volume */
+/* the warp's columns: tile origin (y0, x0), in-tile row wy and first
+ * column wx, and per column the element offset of (b, z = 0, y, x, c) */
+struct Tile3 {
+    int Z, Y, X, y0, x0, wy, wx;
+    int sz;                /* element stride of z (P * D < 2^31) */
+    long c;                /* first of the lane's 2 channels */
+    long base[Z3_PX];
+    bool on[Z3_PX];        /* column and channels inside the volume */
 };
 
-__device__ __forceinline__ Col3 col3(const ConvDev &p) {
-    Col3 q;
+__device__ __forceinline__ Tile3 tile3(const ConvDev &p) {
+    Tile3 t;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    q.Z = (int)p.dims[0];
-    q.Y = (int)p.dims[1];
-    q.X = (int)p.dims[2];
-    const int ntx = (q.X + Z3_TX - 1) / Z3_TX;
-    q.y = (int)(blockIdx.y / ntx) * Z3_TY + w / Z3_TX;
-    q.x = (int)(blockIdx.y % ntx) * Z3_TX + w % Z3_TX;
-    q.c = (long)blockIdx.x * Z3_CH + lane * 2;
-    q.sy = q.X * (int)p.D;
-    q.sz = q.Y * q.sy;
-    q.base = (long)blockIdx.z * p.P * p.D + ((long)q.y * q.X + q.x) * p.D + q.c;
-    q.on = q.y < q.Y && q.x < q.X && q.c < p.D;
-    return q;
+    t.Z = (int)p.dims[0];
+    t.Y = (int)p.dims[1];
+    t.X = (int)p.dims[2];
+    const int ntx = (t.X + Z3_TX - 1) / Z3_TX;
+    t.y0 = (int)(blockIdx.y / ntx) * Z3_TY;
+    t.x0 = (int)(blockIdx.y % ntx) * Z3_TX;
+    t.wy = w / (Z3_TX / Z3_PX);
+    t.wx = (w % (Z3_TX / Z3_PX)) * Z3_PX;
+    t.c = (long)blockIdx.x * Z3_CH + lane * 2;
+    t.sz = t.Y * t.X * (int)p.D;
+    const int y = t.y0 + t.wy;
+#pragma unroll
+    for (int u = 0; u < Z3_PX; ++u) {
+        const int x = t.x0 + t.wx + u;
+        t.on[u] = y < t.Y && x < t.X && t.c < p.D;
+        t.base[u] = (long)blockIdx.z * p.P * p.D + ((long)y * t.X + x) * p.D + t.c;
+    }
+    return t;
 }
 
 __device__ __forceinline__ float2 ld2(const float *a) {
     return __ldg(reinterpret_cast<const float2 *>(a));
 }
-
-/*
- * The slices are staged: the CTA's input slices (its 4 x 4 columns and
- * the K - 1 halo columns on each in-plane axis, 64 channels) stream
- * through a ring of ZS_R slices in shared memory (cp.async, 16-byte
- * chunks, zero-filled outside the volume), ZS_R - 1 slices ahead of the
- * compute, so the loads in flight no longer cost registers.  A lane reads
- * its K x K neighbours from the slice (8-byte reads of a 256-byte column
- * row); taps and accumulators stay in registers as in the z-walk.
- * dkernel stages the dy slice of its own columns K - 1 slices ahead of
- * the input slice, for its window of dy.
- */
-constexpr int ZS_R = 8; /* slices in the ring */
 
 template <int K>
 struct ZSLayout {
@@ -724,6 +730,8 @@ struct ZSLayout {
     static constexpr int SL = NCOL * Z3_CH;            /* floats of a staged input slice */
     static constexpr int SLD = Z3_TY * Z3_TX * Z3_CH;  /* floats of a dy slice (dkernel) */
     static constexpr int NJ = (NCOL * (Z3_CH / 4) + Z3_THREADS - 1) / Z3_THREADS; /* chunks a thread */
+    static constexpr int NV = Z3_PX + K - 1;           /* neighbour columns of a warp per row */
+    static_assert(Z3_TY * Z3_TX * (Z3_CH / 4) <= Z3_THREADS, "one dy chunk a thread");
 };
 
 /* the 16-byte chunk jobs of a thread for one staged slice: element offset
@@ -763,162 +771,176 @@ struct ZSJobs {
 template <int K, int SGN>
 __global__ void __launch_bounds__(Z3_THREADS, 1) k_conv3d_zring(ConvDev p) {
     using L = ZSLayout<K>;
-    constexpr int KK = K * K, KV = K * KK;
+    constexpr int KK = K * K, KV = K * KK, NV = L::NV;
     extern __shared__ __align__(16) float zsm[];
-    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-    const int ty = w / Z3_TX, tx = w % Z3_TX;
-    const Col3 q = col3(p);
+    const int tid = threadIdx.x, lane = tid & 31;
+    const Tile3 t = tile3(p);
     const long c0 = (long)blockIdx.x * Z3_CH;
-    const int y0 = q.y - ty, x0 = q.x - tx;
+    const bool cok = t.c < p.D;
     float2 wt[KV];
 #pragma unroll
-    for (int k = 0; k < KV; ++k)
-        wt[k] = q.on ? ld2(p.ker + k * p.D + q.c) : kmb_f2s(0.f);
+    for (int k = 0; k < KV; ++k) wt[k] = cok ? ld2(p.ker + k * p.D + t.c) : kmb_f2s(0.f);
     ZSJobs<K, SGN> jobs;
-    jobs.init(p, y0, x0, c0, tid);
+    jobs.init(p, t.y0, t.x0, c0, tid);
     const float *src = SGN < 0 ? p.in : p.dy;
-    float *dst = (SGN < 0 ? p.out : p.din) + q.base;
-    const float2 b2 = (SGN < 0 && p.bias && q.on) ? ld2(p.bias + q.c) : kmb_f2s(0.f);
-    float2 acc[K];
+    float *dst = SGN < 0 ? p.out : p.din;
+    const float2 b2 = (SGN < 0 && p.bias && cok) ? ld2(p.bias + t.c) : kmb_f2s(0.f);
+    float2 acc[Z3_PX][K];
 #pragma unroll
-    for (int i = 0; i < K; ++i) acc[i] = b2;
+    for (int u = 0; u < Z3_PX; ++u)
+#pragma unroll
+        for (int i = 0; i < K; ++i) acc[u][i] = b2;
     /* slice t of the walk is z = t (forward) or Z - 1 - t (dinput) */
-    auto zof = [&](int t) { return (long)(SGN < 0 ? t : q.Z - 1 - t) * q.sz; };
+    auto zof = [&](int s) { return (long)(SGN < 0 ? s : t.Z - 1 - s) * t.sz; };
 #pragma unroll 1
-    for (int t = 0; t < ZS_R - 1; ++t) {
-        if (t < q.Z) jobs.issue(zsm + t * L::SL, src, zof(t));
+    for (int s = 0; s < ZS_R - 1; ++s) {
+        if (s < t.Z) jobs.issue(zsm + s * L::SL, src, zof(s));
         kmb_cp_async_commit();
     }
-    /* this lane's neighbour j = oy K + ox in a staged slice */
-    int nb[KK];
+    /* neighbour column i of in-plane row oy in a staged slice: forward
+     * x0 + wx + i - (K - 1) at row y - oy; dinput x0 + wx + i at row y + oy */
+    int nb[K];
 #pragma unroll
-    for (int oy = 0; oy < K; ++oy)
-#pragma unroll
-        for (int ox = 0; ox < K; ++ox) {
-            const int cy = SGN < 0 ? ty + (K - 1) - oy : ty + oy;
-            const int cx = SGN < 0 ? tx + (K - 1) - ox : tx + ox;
-            nb[oy * K + ox] = (cy * L::CX + cx) * Z3_CH + lane * 2;
-        }
+    for (int oy = 0; oy < K; ++oy) {
+        const int cy = SGN < 0 ? t.wy + (K - 1) - oy : t.wy + oy;
+        nb[oy] = (cy * L::CX + t.wx) * Z3_CH + lane * 2;
+    }
     int slot = 0;
 #pragma unroll 1
-    for (int t = 0; t < q.Z; ++t) {
+    for (int s = 0; s < t.Z; ++s) {
         kmb_cp_async_wait<ZS_R - 2>();
         __syncthreads();
-        if (t + ZS_R - 1 < q.Z) {
-            const int ns = slot == 0 ? ZS_R - 1 : slot - 1; /* (t + ZS_R - 1) % ZS_R */
-            jobs.issue(zsm + ns * L::SL, src, zof(t + ZS_R - 1));
+        if (s + ZS_R - 1 < t.Z) {
+            const int ns = slot == 0 ? ZS_R - 1 : slot - 1; /* (s + ZS_R - 1) % ZS_R */
+            jobs.issue(zsm + ns * L::SL, src, zof(s + ZS_R - 1));
         }
         kmb_cp_async_commit();
         const float *sl = zsm + slot * L::SL;
         slot = slot + 1 == ZS_R ? 0 : slot + 1;
-        float2 v[KK];
+        float2 v[K][NV];
 #pragma unroll
-        for (int j = 0; j < KK; ++j) v[j] = *reinterpret_cast<const float2 *>(sl + nb[j]);
+        for (int oy = 0; oy < K; ++oy)
 #pragma unroll
-        for (int oz = 0; oz < K; ++oz)
+            for (int i = 0; i < NV; ++i)
+                v[oy][i] = *reinterpret_cast<const float2 *>(sl + nb[oy] + i * Z3_CH);
 #pragma unroll
-            for (int j = 0; j < KK; ++j)
-                acc[oz] = kmb_fma2(v[j], wt[KV - 1 - (oz * KK + j)], acc[oz]);
-        if (q.on) *reinterpret_cast<float2 *>(dst + zof(t)) = acc[0];
+        for (int u = 0; u < Z3_PX; ++u)
 #pragma unroll
-        for (int i = 0; i + 1 < K; ++i) acc[i] = acc[i + 1];
-        acc[K - 1] = b2;
+            for (int oz = 0; oz < K; ++oz)
+#pragma unroll
+                for (int oy = 0; oy < K; ++oy)
+#pragma unroll
+                    for (int ox = 0; ox < K; ++ox)
+                        acc[u][oz] = kmb_fma2(v[oy][SGN < 0 ? u + (K - 1) - ox : u + ox],
+                                              wt[KV - 1 - (oz * KK + oy * K + ox)], acc[u][oz]);
+        const long zo = zof(s);
+#pragma unroll
+        for (int u = 0; u < Z3_PX; ++u) {
+            if (t.on[u]) *reinterpret_cast<float2 *>(dst + t.base[u] + zo) = acc[u][0];
+#pragma unroll
+            for (int i = 0; i + 1 < K; ++i) acc[u][i] = acc[u][i + 1];
+            acc[u][K - 1] = b2;
+        }
     }
 }
 
 template <int K>
 __global__ void __launch_bounds__(Z3_THREADS, 1) k_conv3d_zring_param(ConvDev p) {
     using L = ZSLayout<K>;
-    constexpr int KK = K * K, KV = K * KK;
+    constexpr int KK = K * K, KV = K * KK, NV = L::NV;
     constexpr int SLOT = L::SL + L::SLD;
     extern __shared__ __align__(16) float zsm[];
     __shared__ float2 red[Z3_THREADS / 32][32];
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-    const int ty = w / Z3_TX, tx = w % Z3_TX;
-    const Col3 q = col3(p);
+    const Tile3 t = tile3(p);
     const long c0 = (long)blockIdx.x * Z3_CH;
-    const int y0 = q.y - ty, x0 = q.x - tx;
     ZSJobs<K, -1> jobs;
-    jobs.init(p, y0, x0, c0, tid);
-    /* dy of the CTA's own columns: one 16-byte chunk for threads < 256 */
+    jobs.init(p, t.y0, t.x0, c0, tid);
+    /* dy of the CTA's own columns: one 16-byte chunk a thread */
     const int dcol = tid / (Z3_CH / 4), dch = tid % (Z3_CH / 4);
-    const int dyy = y0 + dcol / Z3_TX, dxx = x0 + dcol % Z3_TX;
-    const bool dok = tid < Z3_TY * Z3_TX * (Z3_CH / 4) && dyy < q.Y && dxx < q.X &&
-                     c0 + dch * 4 < p.D;
-    const long dsrc = dok ? (long)blockIdx.z * p.P * p.D + ((long)dyy * q.X + dxx) * p.D + c0 +
+    const int dyy = t.y0 + dcol / Z3_TX, dxx = t.x0 + dcol % Z3_TX;
+    const bool dok = dyy < t.Y && dxx < t.X && c0 + dch * 4 < p.D;
+    const long dsrc = dok ? (long)blockIdx.z * p.P * p.D + ((long)dyy * t.X + dxx) * p.D + c0 +
                                 dch * 4
                           : 0;
     const int ddst = L::SL + dcol * Z3_CH + dch * 4;
     auto issue = [&](int s) { /* input slice s and dy slice s + K - 1 */
         float *slot = zsm + (s % ZS_R) * SLOT;
-        jobs.issue(slot, p.in, (long)s * q.sz);
-        if (tid < Z3_TY * Z3_TX * (Z3_CH / 4)) {
-            const bool ok = dok && s + K - 1 < q.Z;
-            kmb_cp_async16(slot + ddst, p.dy + (ok ? dsrc + (long)(s + K - 1) * q.sz : 0),
-                           ok ? 16 : 0);
-        }
+        jobs.issue(slot, p.in, (long)s * t.sz);
+        const bool ok = dok && s + K - 1 < t.Z;
+        kmb_cp_async16(slot + ddst, p.dy + (ok ? dsrc + (long)(s + K - 1) * t.sz : 0),
+                       ok ? 16 : 0);
     };
 #pragma unroll 1
     for (int s = 0; s < ZS_R - 1; ++s) {
-        if (s < q.Z) issue(s);
+        if (s < t.Z) issue(s);
         kmb_cp_async_commit();
     }
-    int nb[KK];
+    int nb[K];
 #pragma unroll
     for (int oy = 0; oy < K; ++oy)
-#pragma unroll
-        for (int ox = 0; ox < K; ++ox)
-            nb[oy * K + ox] = ((ty + (K - 1) - oy) * L::CX + tx + (K - 1) - ox) * Z3_CH + lane * 2;
-    const int dme = L::SL + w * Z3_CH + lane * 2; /* this lane's dy in a slot */
+        nb[oy] = ((t.wy + (K - 1) - oy) * L::CX + t.wx) * Z3_CH + lane * 2;
+    /* this lane's dy of its columns in a slot */
+    const int dme = L::SL + (t.wy * Z3_TX + t.wx) * Z3_CH + lane * 2;
     float2 acc[KV], accb = kmb_f2s(0.f);
 #pragma unroll
     for (int k = 0; k < KV; ++k) acc[k] = kmb_f2s(0.f);
-    float2 dyw[K]; /* dy of this column at slices s .. s + K - 1 */
+    float2 dyw[Z3_PX][K]; /* dy of each column at slices s .. s + K - 1 */
 #pragma unroll
-    for (int i = 0; i + 1 < K; ++i)
-        dyw[i] = q.on && i < q.Z ? ld2(p.dy + q.base + (long)i * q.sz) : kmb_f2s(0.f);
+    for (int u = 0; u < Z3_PX; ++u)
+#pragma unroll
+        for (int i = 0; i + 1 < K; ++i)
+            dyw[u][i] = t.on[u] && i < t.Z ? ld2(p.dy + t.base[u] + (long)i * t.sz)
+                                           : kmb_f2s(0.f);
 #pragma unroll 1
-    for (int s = 0; s < q.Z; ++s) {
+    for (int s = 0; s < t.Z; ++s) {
         kmb_cp_async_wait<ZS_R - 2>();
         __syncthreads();
-        if (s + ZS_R - 1 < q.Z) issue(s + ZS_R - 1);
+        if (s + ZS_R - 1 < t.Z) issue(s + ZS_R - 1);
         kmb_cp_async_commit();
         const float *sl = zsm + (s % ZS_R) * SLOT;
-        dyw[K - 1] = *reinterpret_cast<const float2 *>(sl + dme);
-        float2 v[KK];
 #pragma unroll
-        for (int j = 0; j < KK; ++j) v[j] = *reinterpret_cast<const float2 *>(sl + nb[j]);
+        for (int u = 0; u < Z3_PX; ++u)
+            dyw[u][K - 1] = *reinterpret_cast<const float2 *>(sl + dme + u * Z3_CH);
+        float2 v[K][NV];
 #pragma unroll
-        for (int oz = 0; oz < K; ++oz)
+        for (int oy = 0; oy < K; ++oy)
 #pragma unroll
-            for (int j = 0; j < KK; ++j)
-                acc[KV - 1 - (oz * KK + j)] =
-                    kmb_fma2(dyw[oz], v[j], acc[KV - 1 - (oz * KK + j)]);
-        accb = kmb_add2(accb, dyw[0]);
+            for (int i = 0; i < NV; ++i)
+                v[oy][i] = *reinterpret_cast<const float2 *>(sl + nb[oy] + i * Z3_CH);
 #pragma unroll
-        for (int i = 0; i + 1 < K; ++i) dyw[i] = dyw[i + 1];
+        for (int u = 0; u < Z3_PX; ++u) {
+#pragma unroll
+            for (int oz = 0; oz < K; ++oz)
+#pragma unroll
+                for (int oy = 0; oy < K; ++oy)
+#pragma unroll
+                    for (int ox = 0; ox < K; ++ox) {
+                        const int k = KV - 1 - (oz * KK + oy * K + ox);
+                        acc[k] = kmb_fma2(dyw[u][oz], v[oy][u + (K - 1) - ox], acc[k]);
+                    }
+            accb = kmb_add2(accb, dyw[u][0]);
+#pragma unroll
+            for (int i = 0; i + 1 < K; ++i) dyw[u][i] = dyw[u][i + 1];
+        }
     }
-    if (!q.on) {
-        accb = kmb_f2s(0.f);
-#pragma unroll
-        for (int k = 0; k < KV; ++k) acc[k] = kmb_f2s(0.f);
-    }
-    /* fold the CTA's columns, one tap at a time */
+    /* fold the CTA's warps, one tap at a time (columns outside the volume
+     * and channels past D hold zeros) */
     const int ntap = p.dbias ? KV + 1 : KV;
 #pragma unroll
     for (int k = 0; k < KV + 1; ++k) {
         if (k < ntap) {
             red[w][lane] = k < KV ? acc[k] : accb;
             __syncthreads();
-            if (w == 0 && q.c < p.D) {
-                float2 t = red[0][lane];
-                for (int ww = 1; ww < Z3_THREADS / 32; ++ww) t = kmb_add2(t, red[ww][lane]);
-                float *d = k < KV ? p.dker + k * p.D + q.c : p.dbias + q.c;
+            if (w == 0 && t.c < p.D) {
+                float2 r = red[0][lane];
+                for (int ww = 1; ww < Z3_THREADS / 32; ++ww) r = kmb_add2(r, red[ww][lane]);
+                float *d = k < KV ? p.dker + k * p.D + t.c : p.dbias + t.c;
                 if (((uintptr_t)d & 7u) == 0) {
-                    atomicAdd(reinterpret_cast<float2 *>(d), t);
+                    atomicAdd(reinterpret_cast<float2 *>(d), r);
                 } else { /* dkernel / dbias need not be 8-byte aligned */
-                    atomicAdd(d, t.x);
-                    atomicAdd(d + 1, t.y);
+                    atomicAdd(d, r.x);
+                    atomicAdd(d + 1, r.y);
                 }
             }
             __syncthreads();
