@@ -602,8 +602,8 @@ __global__ void __launch_bounds__(kWWarpsA * 32) k_scannd_adj_w(NDDev p) {
 
     for (int l = p.nlevels - 1; l >= 0; --l) {
         const int s0 = lvl_start[l], s1 = lvl_start[l + 1];
-        /* indices of 32 of the warp's slots loaded at once, handed out by
-         * shuffle (as in k_scannd_fwd_w) */
+        /* indices of 32 of the warp's slots loaded at once and handed out
+         * by shuffle (k_scannd_fwd_w hands them out through a shared slot) */
         for (int base = s0 + w; base < s1; base += kWWarpsA * 32) {
             const int sl = base + kWWarpsA * lane;
             int myoff = 0, mynx[ND];
