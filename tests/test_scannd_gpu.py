@@ -170,7 +170,11 @@ def test_scan2d_vs_oracle(lib, cuda, oracle, d1, d2, D, M):
                                              ([6, 9, 10], 8, 16, True), ([2, 5, 66], 16, 16, True),
                                              ([3, 70, 70], 8, 16, True), ([3, 3, 9, 10], 8, 16, True),
                                              ([2, 3, 5, 70], 8, 16, True),
-                                             ([2, 3, 5, 70], 8, 8, True)])
+                                             ([2, 3, 5, 70], 8, 8, True),
+                                             # levels of up to ~1280 points: more than
+                                             # one batch of 32 slots per warp in the
+                                             # pipelined sweeps
+                                             ([20, 64, 64], 8, 16, True)])
 def test_batched_fwd_bwd_vs_oracle(lib, cuda, oracle, dims, D, M, shared, weak=False):
     import torch
     declare(lib)
