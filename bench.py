@@ -29,7 +29,6 @@ import os
 import statistics
 import subprocess
 import sys
-import threading
 import tempfile
 import time
 
@@ -151,66 +150,55 @@ def traffic_from_profile():
 # reference CPU arm / CPU baseline
 # --------------------------------------------------------------------------
 
-def cpu_reference_sample(nthreads, chans_per_thread, seed=1):
-    """Times the reference's CPU path on nthreads independent channel
-    slices (one batch item each): scannd_ref (1D) for y and the state
-    history, then scan1d_backward.  Returns (seconds, channel_sequences)."""
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle  # noqa: WPS433  (CPU baseline leg only)
-    import kmamba_b200 as kb
-    ref = oracle.ref_lib()
-    kind = "reference"
-    if ref is None:
-        ref = None
-        kind = "port"
-    rng = np.random.default_rng(seed)
-    f = np.float32
-    jobs = []
-    for t in range(nthreads):
-        dch = chans_per_thread
-        x = rng.standard_normal((L, dch), dtype=f)
-        dt = np.log1p(np.exp(rng.standard_normal((L, dch), dtype=f) - 2)).astype(f)
-        A = (-np.exp(rng.uniform(0, np.log(16), (dch, N)))).astype(f)
-        Bs = rng.standard_normal((L, N), dtype=f)
-        Cs = rng.standard_normal((L, N), dtype=f)
-        dy = rng.standard_normal((L, dch), dtype=f)
-        Bx = np.ascontiguousarray(np.broadcast_to(Bs[:, None, :], (L, dch, N)))
-        Cx = np.ascontiguousarray(np.broadcast_to(Cs[:, None, :], (L, dch, N)))
-        jobs.append(dict(x=x, dt=dt, A=A, B=Bx, C=Cx, dy=dy, dch=dch,
-                         h=np.zeros((L, dch, N), f), y=np.zeros((L, dch), f),
-                         dx=np.zeros((L, dch), f), ddt=np.zeros((L, dch), f),
-                         dA=np.zeros((dch, N), f), dB=np.zeros((L, dch, N), f),
-                         dC=np.zeros((L, dch, N), f)))
+CPU_SLICES, CPU_CHANS = 96, 16  # one batch item: 96 slices x 16 channels = D
 
-    P = lambda a: a.ctypes.data  # noqa: E731
 
-    def run(j):
-        if ref is not None:
-            dims = np.array([L], np.int64)
-            j["dims"] = dims
-            p = kb.ScanNDParams(P(dims), 1, j["dch"], N, P(j["x"]), P(j["A"]), P(j["B"]),
-                                P(j["C"]), P(j["dt"]), P(j["h"]), P(j["y"]), None, None)
-            ref.scannd_ref(C.byref(p))
-            bp = kb.ScanBackwardParams(P(j["x"]), P(j["A"]), P(j["B"]), P(j["C"]), P(j["dt"]),
-                                       None, P(j["h"]), P(j["dy"]), P(j["dx"]), P(j["dA"]),
-                                       P(j["dB"]), P(j["dC"]), P(j["ddt"]), L, j["dch"], N)
-            ref.scan1d_backward(C.byref(bp))
-        else:
-            y, _, h = oracle.scan1d_fwd(j["x"], j["dt"], j["A"], j["B"], j["C"], clamp=False,
-                                        want_h_all=True)
-            oracle.scan1d_bwd(j["x"], j["dt"], j["A"], j["B"], j["C"], h, j["dy"])
+def cpu_bench_lib():
+    """The OpenMP driver of the reference's own CPU path (oracle/_ref,
+    kind "reference"), or of its C restatement when the reference build is
+    absent (kind "port").  Test infrastructure: bench.py's CPU legs only."""
+    ref = os.path.join(ROOT, "oracle", "_ref", "libkmb_refbench.so")
+    if os.path.exists(ref):
+        lib, kind = C.CDLL(ref), "reference"
+    else:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle  # noqa: WPS433  (CPU baseline leg only)
+        if not os.path.exists(oracle.ORACLE_SO):
+            oracle.build()
+        lib, kind = C.CDLL(oracle.ORACLE_SO), "port"
+    lib.kmb_cpu_bench_create.restype = C.c_void_p
+    lib.kmb_cpu_bench_create.argtypes = [C.c_int, C.c_int, C.c_long, C.c_int, C.c_ulonglong,
+                                         C.c_int]
+    lib.kmb_cpu_bench_pass.restype = C.c_double
+    lib.kmb_cpu_bench_pass.argtypes = [C.c_void_p]
+    lib.kmb_cpu_bench_free.argtypes = [C.c_void_p]
+    return lib, kind
 
-    if ref is not None:
-        ref.scannd_ref.argtypes = [C.POINTER(kb.ScanNDParams)]
-        ref.scannd_ref.restype = C.c_int
-        ref.scan1d_backward.argtypes = [C.POINTER(kb.ScanBackwardParams)]
-    threads = [threading.Thread(target=run, args=(j,)) for j in jobs]
-    t0 = time.perf_counter()
-    for th in threads:
-        th.start()
-    for th in threads:
-        th.join()
-    return time.perf_counter() - t0, nthreads * chans_per_thread, kind
+
+def cpu_sample_desc(nth):
+    return (f"one of the {BATCH} batch items per step: all {D} channels as "
+            f"{CPU_SLICES} slices x {CPU_CHANS} channels, full L={L}, N={N}, B/C expanded to "
+            f"the reference's [L,D,N] layout; reference scannd_ref (ndims 1) forward + "
+            f"scan1d_backward per slice under one OpenMP parallel loop on {nth} host threads "
+            f"(one thread-local reference pool per OpenMP worker); inputs pre-touched by "
+            f"their worker outside the timed region")
+
+
+def cpu_reference_run(nth, warmup, steps, seed=1):
+    """Seconds per pass (mean of `steps` timed passes after `warmup`) of the
+    reference's CPU path over one batch item of config 2.  Returns
+    (seconds, channel_sequences, kind)."""
+    lib, kind = cpu_bench_lib()
+    h = lib.kmb_cpu_bench_create(CPU_SLICES, CPU_CHANS, L, N, seed, nth)
+    if not h:
+        raise RuntimeError("CPU baseline: host allocation failed")
+    try:
+        for _ in range(warmup):
+            lib.kmb_cpu_bench_pass(h)
+        secs = [lib.kmb_cpu_bench_pass(h) for _ in range(max(1, steps))]
+    finally:
+        lib.kmb_cpu_bench_free(h)
+    return sum(secs) / len(secs), CPU_SLICES * CPU_CHANS, kind
 
 
 def cpu_threads():
@@ -218,7 +206,7 @@ def cpu_threads():
         n = len(os.sched_getaffinity(0))
     except AttributeError:
         n = os.cpu_count() or 1
-    return max(1, min(n, 32))
+    return max(1, min(n, 96))
 
 
 def bytes_for_channels(nch):
@@ -229,25 +217,16 @@ def run_reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    os.environ["OMP_NUM_THREADS"] = "1"  # scannd_ref's inner OpenMP loop races
     nth = cpu_threads()
-    per = 32
-    times = []
-    kind = "reference"
-    for i in range(args.warmup + args.steps):
-        dt, nch, kind = cpu_reference_sample(nth, per, seed=100 + i)
-        if i >= args.warmup:
-            times.append(dt)
-    t = sum(times) / len(times)
-    v = bytes_for_channels(nth * per) / t / 1e9
-    sample = (f"{nth} threads x {per} channels of one batch item, full L={L}, N={N} "
-              f"(B/C expanded to [L,D,N] for the reference API): {nth * per} of "
-              f"{BATCH * D} channel-sequences per step")
+    t, nch, kind = cpu_reference_run(nth, args.warmup, args.steps, seed=100)
+    v = bytes_for_channels(nch) / t / 1e9
+    sample = cpu_sample_desc(nth)
     line = {"metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3 * BATCH * D / nch,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "impl": "reference",
-            "config": {"workload": WORKLOAD, "batch": BATCH, "L": L, "D": D, "N": N},
+            "config": {"workload": WORKLOAD, "batch": BATCH, "L": L, "D": D, "N": N,
+                       "ms_per_sampled_pass": t * 1e3},
             "cpu_baseline": {"value": v, "unit": "GB/s", "cores": nth, "kind": kind,
                              "sample": sample},
             "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0,
@@ -716,14 +695,10 @@ def main():
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             nth = cpu_threads()
-            per = 64
-            secs, nch, kind = cpu_reference_sample(nth, per)
+            secs, nch, kind = cpu_reference_run(nth, 1, 3, seed=100)
             cpu = {"value": bytes_for_channels(nch) / secs / 1e9, "unit": "GB/s", "cores": nth,
-                   "kind": kind,
-                   "sample": (f"{nth} host threads x {per} channel-sequences (L={L}, N={N}) "
-                              f"of one batch item: reference scannd_ref (1D) forward + "
-                              f"scan1d_backward, {nch} of {BATCH * D} sequences, "
-                              f"{secs:.1f} s")}
+                   "kind": kind, "sample": cpu_sample_desc(nth) +
+                   f", 3 timed passes of {secs:.2f} s"}
         line = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,

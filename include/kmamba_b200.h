@@ -118,13 +118,19 @@ int kmb_scan1d_bwd(const KmbScan1D *args);
  * synchronisation cudaMalloc / cudaFree may impose, or a plugin host that
  * forbids allocations outside its own set-up phase.  It allocates nothing
  * and stages nothing: every pointer must be device memory, h_all and ckpt
- * must be NULL.  The forward checkpoints live in a static device array of
- * KMB_NOALLOC_CKPT_ELEMS floats (8 MiB, held by every GPU that loads the
- * library until exit); a call needing more -- batch * ceil(L /
- * KMB_SCAN1D_CHUNK) * D * N floats -- is rejected with KMB_EUNSUPPORTED.
- * The first call on each device looks up the array's device address
- * (cudaGetSymbolAddress), so make it before any stream capture.  All
- * calls share the array: calls that overlap on the GPU race on it.
+ * must be NULL.  Every tensor must be memory of the current device.  The
+ * forward checkpoints live in a static device array of
+ * KMB_NOALLOC_CKPT_ELEMS floats (8 MiB, held by every GPU that has loaded
+ * the library's device code, until exit); a call needing more -- batch *
+ * ceil(L / KMB_SCAN1D_CHUNK) * D * N floats -- is rejected with
+ * KMB_EUNSUPPORTED.  The first call on each device looks up the array's
+ * device address (cudaGetSymbolAddress); with lazy module loading, the
+ * CUDA 12 default, that lookup is also what loads the module and its
+ * 8 MiB onto the device, which allocates and can synchronise.  So make a
+ * warm-up call during your own set-up phase, before any stream capture.
+ * The address is cached per device and not refreshed after
+ * cudaDeviceReset: do not use the entry point across a reset.  All calls
+ * share the array: calls that overlap on the GPU race on it.
  */
 #define KMB_NOALLOC_CKPT_ELEMS (2L * 1024 * 1024)
 int kmb_scan1d_bwd_noalloc(const KmbScan1D *args);

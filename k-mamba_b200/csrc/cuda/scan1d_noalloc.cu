@@ -13,7 +13,12 @@
  *
  * In host code the array's name only stands for the symbol; its device
  * address is looked up once per device with cudaGetSymbolAddress (with
- * that device current) by the first call on that device, and cached.
+ * that device current) by the first call on that device, and cached.  With
+ * lazy module loading (the CUDA 12 default) that first lookup is also what
+ * loads this module onto the device, allocating the array and possibly
+ * synchronising: callers make their first call during their own set-up
+ * phase.  The cached address is not refreshed after cudaDeviceReset, so
+ * the entry point must not be used across a reset.
  *
  * All calls share the array and it keeps the last call's contents: every
  * checkpoint a call reads is written earlier in the same call, so nothing
@@ -56,7 +61,19 @@ int scratch_address(float **out) {
     return KMB_OK;
 }
 
-bool on_device(const void *p) { return p == nullptr || kmb_is_device_ptr(p); }
+/* NULL, or device (or managed) memory of the current device: memory of
+ * another GPU would be read over the peer link, or fault without peer
+ * access. */
+bool on_device(const void *p, int dev) {
+    if (!p) return true;
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return false;
+    }
+    if (at.type == cudaMemoryTypeManaged) return true;
+    return at.type == cudaMemoryTypeDevice && at.device == dev;
+}
 
 } // namespace
 
@@ -79,12 +96,16 @@ extern "C" int kmb_scan1d_bwd_noalloc(const KmbScan1D *a) {
                         "scan1d noalloc: needs %ld checkpoint floats, the static scratch holds "
                         "%ld (batch * ceil(L/%d) * D * N must not exceed it)",
                         need, (long)KMB_NOALLOC_CKPT_ELEMS, KMB_SCAN1D_CHUNK);
+    int cur = 0;
+    const cudaError_t de = cudaGetDevice(&cur);
+    if (de != cudaSuccess) return kmb_cuda_fail(de, "scan1d noalloc: cudaGetDevice");
     const void *ptrs[] = {a->x, a->dt, a->A, a->B, a->C, a->h0, a->dy,
                           a->dx, a->ddt, a->dA, a->dB, a->dC};
     for (const void *q : ptrs)
-        if (!on_device(q))
+        if (!on_device(q, cur))
             return kmb_fail(KMB_EINVAL, "scan1d noalloc: every tensor must be device memory "
-                                        "(host buffers would need staging allocations)");
+                                        "of the current device (host buffers would need "
+                                        "staging allocations)");
     kmb_clear_error();
 
     float *ck = nullptr;

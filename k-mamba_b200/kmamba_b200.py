@@ -266,6 +266,14 @@ PROTOTYPES = {
     "km_ravel_index": (lg, [fp, fp, fp, lg]),
     "km_power_long": (lg, [lg, lg]),
     "km_normalize_spatial_topology": (C.c_int, [fp, fp, C.c_size_t, C.c_int, fp, lg]),
+    # km_memory_pool.h over device memory
+    "km_memory_pool_create": (C.c_void_p, []),
+    "km_memory_pool_destroy": (None, [C.c_void_p]),
+    "km_pool_alloc": (C.c_void_p, [C.c_void_p, C.c_size_t]),
+    "km_pool_free": (None, [C.c_void_p, C.c_void_p]),
+    "km_pool_clear": (None, [C.c_void_p]),
+    "km_memory_pool_threadlocal": (C.c_void_p, []),
+    "km_memory_pool_destroy_all_threadlocal": (None, []),
 }
 
 
