@@ -201,6 +201,49 @@ typedef struct {
 int kmb_scannd_fwd(const KmbScanND *args);
 int kmb_scannd_bwd(const KmbScanND *args);
 
+/* ------------------------------------------------------------------ */
+/* bf16 GEMM on the tensor cores (block projections)                   */
+/* ------------------------------------------------------------------ */
+/*
+ * C[m, n] = act(sum_k A(m, k) B(n, k) + bias[n]) + residual[m, n]
+ * (+ the previous C when accumulate), fp32 accumulation (tcgen05 / TMEM).
+ * Replaces the reference's cuBLAS SGEMM projections (cuda/mamba_block.cu:
+ * 54-72) on the bf16-compute path.
+ *
+ * A and B are bf16 device memory, 16-byte aligned, lda / ldb multiples of
+ * 8 elements.  K-major storage: A[m * lda + k], B[n * ldb + k];
+ * a_mn_major / b_mn_major select the transposed storage A[k * lda + m],
+ * B[k * ldb + n] (the input- and weight-gradient GEMMs of a linear layer).
+ * C is fp32 (c_bf16 = 0) or bf16 rounded to nearest even, row stride ldc;
+ * bias [N] and residual [M, ldr] are fp32 and optional.  act: 0 identity,
+ * 1 SiLU.  Runs on the library stream; synchronous when kmb_set_sync(1).
+ */
+typedef struct {
+    const void *A;
+    const void *B;
+    void *C;
+    const float *bias;
+    const float *residual;
+    long M;
+    long N;
+    long K;
+    long lda;
+    long ldb;
+    long ldc;
+    long ldr;
+    int a_mn_major;
+    int b_mn_major;
+    int c_bf16;
+    int act;
+    int accumulate;
+    int pad_;
+} KmbGemm;
+
+int kmb_gemm_bf16(const KmbGemm *args);
+/* KMB_ETIMEOUT when a GEMM launch's bounded pipeline wait gave up since
+ * the last check (synchronous calls check it themselves). */
+int kmb_gemm_check_error(void);
+
 #ifdef __cplusplus
 }
 #endif

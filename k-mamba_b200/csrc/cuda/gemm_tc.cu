@@ -1,0 +1,454 @@
+/*
+ * bf16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM), fed by
+ * TMA, with a fused epilogue.  Used by the projections of the Mamba block
+ * (the reference runs them as cuBLAS SGEMM: cuda/mamba_block.cu:54-72,
+ * call sites :404-436 and :781-833).
+ *
+ *   C[m, n] = act( sum_k A(m, k) B(n, k) + bias[n] ) + residual[m, n]  (+ C)
+ *
+ * A is [M, K] and B is [N, K], bf16.  Each operand is stored either
+ * K-major (row-major with K contiguous: A[m * lda + k]) or MN-major (the
+ * transposed storage: A[k * lda + m]), so the three GEMMs of a linear
+ * layer -- forward, input gradient, weight gradient -- all run without a
+ * transpose copy.  Accumulation is fp32 in tensor memory; C is fp32 or
+ * bf16 (round to nearest even).
+ *
+ * CTA tile BM x BN x BK = 128 x BN x 64, STAGES shared-memory stages.
+ * Warp roles inside a CTA of 128 threads:
+ *   warp 0, one elected lane: TMA producer (two 2D tensor-map loads per
+ *                             stage, 128-byte swizzle, no multicast);
+ *   warp 1, one elected lane: MMA issuer (4 tcgen05.mma of K = 16 per
+ *                             stage; tcgen05.commit frees the stage);
+ *   warps 0-3:                epilogue, after the last commit: warp w
+ *                             reads accumulator rows 32w..32w+31 from TMEM
+ *                             (tcgen05.ld 32x32b) and writes C.
+ * Every wait on an mbarrier is bounded (about 2^31 clock cycles); on
+ * expiry the thread sets the CTA's abort flag and the launch's device
+ * error word and leaves its loop, so the CTA still reaches the TMEM
+ * release and exits.
+ *
+ * Tensor maps cover this GPU's own memory only (the caller's A and B).
+ */
+#include <stdint.h>
+#include <string.h>
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include "kmb_common.cuh"
+#include "../kmb_internal.h"
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;        /* bf16: 128 bytes, one swizzle row */
+constexpr int kThreads = 128;
+constexpr unsigned long long kWaitCycles = 1ull << 31;
+
+__device__ int g_gemm_error; /* set by a launch whose wait expired */
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+/* Waits for the phase of the given parity; false (and the abort flag set)
+ * when the wait gives up or another role already aborted. */
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort) {
+    const unsigned long long t0 = clock64();
+    while (!mbar_test(bar, parity)) {
+        if (*abort) return false;
+        if (clock64() - t0 > kWaitCycles) {
+            *abort = 1;
+            atomicExch(&g_gemm_error, 1);
+            return false;
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
+                                            uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+/*
+ * Shared-memory matrix descriptor of tcgen05.mma for a 128-byte swizzled
+ * tile (start address >> 4 in bits 0-13, leading byte offset >> 4 in
+ * 16-29, stride byte offset >> 4 in 32-45, descriptor version 1 in 46-47,
+ * swizzle mode 2 = 128B in 61-63).
+ *   K-major tile (rows of 64 K values, 128 B each): rows in groups of 8
+ *     1024 B apart (stride offset); the leading offset is unused (1).
+ *   MN-major tile (rows of 64 M or N values, one row per K): groups of 8
+ *     K-rows 1024 B apart (stride offset); 64-wide M/N blocks `lbo` bytes
+ *     apart (leading offset).
+ */
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes) {
+    return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)(1024u >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+/* tcgen05 instruction descriptor, kind::f16: fp32 accumulator (bits 4-5 =
+ * 1), bf16 A and B (bits 7-9, 10-12 = 1), A / B major (bits 15, 16: 0 =
+ * K-major, 1 = MN-major), N >> 3 (bits 17-22), M >> 4 (bits 24-28). */
+template <int BN, bool AMN, bool BMN>
+__host__ __device__ constexpr uint32_t instr_desc() {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((AMN ? 1u : 0u) << 15) | ((BMN ? 1u : 0u) << 16) |
+           ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+}
+
+struct GemmDev {
+    void *C;
+    const float *bias;
+    const float *residual;
+    long M, N, K, ldc, ldr;
+    int c_bf16, act, accumulate;
+};
+
+__device__ __forceinline__ float silu(float v) { return v / (1.f + __expf(-v)); }
+
+template <int BN, int STAGES, bool AMN, bool BMN>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
+              GemmDev p) {
+    constexpr int A_BYTES = kBM * kBK * 2;
+    constexpr int B_BYTES = BN * kBK * 2;
+    constexpr uint32_t TMEM_COLS = BN; /* fp32 accumulator: one column per n */
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    /* 1024-byte alignment of every tile (the swizzle pattern repeats
+     * every 8 rows of 128 B) */
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sA = smem;
+    uint8_t *sB = smem + STAGES * A_BYTES;
+    uint64_t *full = reinterpret_cast<uint64_t *>(sB + STAGES * B_BYTES);
+    uint64_t *empty = full + STAGES;
+    uint64_t *acc_full = empty + STAGES;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
+    volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kBM;
+    const int nk = (int)((p.K + kBK - 1) / kBK);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(acc_full, 1);
+        *abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mapA)));
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mapB)));
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    const uint32_t tmem = *tmem_slot;
+
+    int issued = 0; /* stages the producer has loaded */
+    if (warp == 0 && lane == 0) {
+        /* TMA producer */
+        for (int kb = 0; kb < nk; ++kb) {
+            const int s = kb % STAGES;
+            const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
+            if (!mbar_wait(&empty[s], ph ^ 1u, abort)) break;
+            issued = kb + 1;
+            mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
+            const int k0 = kb * kBK;
+            if (AMN) {
+                tma_load_2d(sA + s * A_BYTES, &mapA, m0, k0, &full[s]);
+                tma_load_2d(sA + s * A_BYTES + kBK * 128, &mapA, m0 + 64, k0, &full[s]);
+            } else {
+                tma_load_2d(sA + s * A_BYTES, &mapA, k0, m0, &full[s]);
+            }
+            if (BMN) {
+#pragma unroll
+                for (int j = 0; j < BN / 64; ++j)
+                    tma_load_2d(sB + s * B_BYTES + j * kBK * 128, &mapB, n0 + 64 * j, k0, &full[s]);
+            } else {
+                tma_load_2d(sB + s * B_BYTES, &mapB, k0, n0, &full[s]);
+            }
+        }
+    } else if (warp == 1 && lane == 0) {
+        /* MMA issuer */
+        constexpr uint32_t idesc = instr_desc<BN, AMN, BMN>();
+        for (int kb = 0; kb < nk; ++kb) {
+            const int s = kb % STAGES;
+            const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
+            if (!mbar_wait(&full[s], ph, abort)) break;
+            asm volatile("tcgen05.fence::after_thread_sync;");
+            const uint32_t a_addr = smem_u32(sA + s * A_BYTES);
+            const uint32_t b_addr = smem_u32(sB + s * B_BYTES);
+#pragma unroll
+            for (int k = 0; k < kBK / 16; ++k) {
+                /* K step of 16: 32 bytes along a K-major row; 16 rows
+                 * (2 swizzle groups of 1024 B) of an MN-major tile */
+                const uint64_t da = AMN ? smem_desc(a_addr + k * 2048, kBK * 128)
+                                        : smem_desc(a_addr + k * 32, 16);
+                const uint64_t db = BMN ? smem_desc(b_addr + k * 2048, kBK * 128)
+                                        : smem_desc(b_addr + k * 32, 16);
+                const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+                asm volatile(
+                    "{\n\t.reg .pred p;\n\t"
+                    "setp.ne.b32 p, %4, 0;\n\t"
+                    "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+                    "l"(da), "l"(db), "r"(idesc), "r"(accum));
+            }
+            /* the stage is free once these MMAs have read it */
+            asm volatile(
+                "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                    smem_u32(&empty[s]))
+                : "memory");
+        }
+        asm volatile(
+            "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                smem_u32(acc_full))
+            : "memory");
+    }
+    __syncwarp();
+
+    /* epilogue: all four warps */
+    const bool ok = nk > 0 && mbar_wait(acc_full, 0, abort);
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    const long row = m0 + warp * 32 + lane;
+    const bool row_ok = ok && row < p.M;
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t r[16];
+        const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0;
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, "
+            "%10, %11, %12, %13, %14, %15}, [%16];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+              "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
+              "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+            : "r"(taddr));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (!row_ok) continue;
+        const long n = n0 + c0;
+        if (n >= p.N) continue;
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            float t = __uint_as_float(r[j]);
+            if (p.bias && n + j < p.N) t += p.bias[n + j];
+            if (p.act == 1) t = silu(t);
+            if (p.residual && n + j < p.N) t += p.residual[row * p.ldr + n + j];
+            v[j] = t;
+        }
+        const bool full16 = n + 16 <= p.N;
+        if (p.c_bf16) {
+            __nv_bfloat16 *c = reinterpret_cast<__nv_bfloat16 *>(p.C) + row * p.ldc + n;
+            if (full16 && !p.accumulate && ((reinterpret_cast<uintptr_t>(c) & 15) == 0)) {
+                uint32_t w[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+                    w[j] = *reinterpret_cast<const uint32_t *>(&h2);
+                }
+                reinterpret_cast<uint4 *>(c)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                reinterpret_cast<uint4 *>(c)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+            } else {
+                for (int j = 0; j < 16 && n + j < p.N; ++j) {
+                    float t = v[j];
+                    if (p.accumulate) t += __bfloat162float(c[j]);
+                    c[j] = __float2bfloat16_rn(t);
+                }
+            }
+        } else {
+            float *c = reinterpret_cast<float *>(p.C) + row * p.ldc + n;
+            if (full16 && ((reinterpret_cast<uintptr_t>(c) & 15) == 0)) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float4 t = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                    if (p.accumulate) {
+                        const float4 o = reinterpret_cast<const float4 *>(c)[j];
+                        t.x += o.x; t.y += o.y; t.z += o.z; t.w += o.w;
+                    }
+                    reinterpret_cast<float4 *>(c)[j] = t;
+                }
+            } else {
+                for (int j = 0; j < 16 && n + j < p.N; ++j) c[j] = p.accumulate ? c[j] + v[j] : v[j];
+            }
+        }
+    }
+
+    if (warp == 0 && lane == 0 && *abort) {
+        /* after an abort, let the copies still in flight land before the
+         * CTA's shared memory goes away (each wait bounded again) */
+        for (int kb = issued > STAGES ? issued - STAGES : 0; kb < issued; ++kb) {
+            const unsigned long long t0 = clock64();
+            while (!mbar_test(&full[kb % STAGES], (uint32_t)(kb / STAGES) & 1u) &&
+                   clock64() - t0 < kWaitCycles) {
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(TMEM_COLS));
+    }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+        else
+            (void)cudaGetLastError();
+    }
+    return fn;
+}
+
+/* 2D bf16 tensor map over a [rows, cols] row-major operand (cols
+ * contiguous, ld elements between rows), box = box_cols x box_rows with a
+ * 128-byte swizzle; reads past the edges return zeros. */
+int make_map(CUtensorMap *m, const void *base, long rows, long cols, long ld, int box_cols,
+             int box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return kmb_fail(KMB_ECUDA, "gemm: cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims,
+                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return kmb_fail(KMB_EINVAL, "gemm: tensor map rejected (CUresult %d)", (int)r);
+    return KMB_OK;
+}
+
+template <int BN, int STAGES, bool AMN, bool BMN>
+int launch(const KmbGemm *g, cudaStream_t s) {
+    CUtensorMap ma, mb;
+    /* K-major operand: rows = M (or N), cols = K, box 64 x rows-of-tile;
+     * MN-major operand: rows = K, cols = M (or N), box 64 x 64 (K rows) */
+    int rc = AMN ? make_map(&ma, g->A, g->K, g->M, g->lda, 64, kBK)
+                 : make_map(&ma, g->A, g->M, g->K, g->lda, kBK, kBM);
+    if (rc) return rc;
+    rc = BMN ? make_map(&mb, g->B, g->K, g->N, g->ldb, 64, kBK)
+             : make_map(&mb, g->B, g->N, g->K, g->ldb, kBK, BN);
+    if (rc) return rc;
+    GemmDev p;
+    p.C = g->C;
+    p.bias = g->bias;
+    p.residual = g->residual;
+    p.M = g->M; p.N = g->N; p.K = g->K; p.ldc = g->ldc; p.ldr = g->ldr;
+    p.c_bf16 = g->c_bf16; p.act = g->act; p.accumulate = g->accumulate;
+    const size_t smem = 1024 + (size_t)STAGES * (kBM + BN) * kBK * 2 + (2 * STAGES + 1) * 8 + 16;
+    auto kern = k_gemm_tc<BN, STAGES, AMN, BMN>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return kmb_cuda_fail(e, "gemm: smem attribute");
+    dim3 grid((unsigned)((g->N + BN - 1) / BN), (unsigned)((g->M + kBM - 1) / kBM));
+    kern<<<grid, kThreads, smem, s>>>(ma, mb, p);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "gemm: launch");
+}
+
+template <int BN, int STAGES>
+int dispatch(const KmbGemm *g, cudaStream_t s) {
+    const bool amn = g->a_mn_major, bmn = g->b_mn_major;
+    if (!amn && !bmn) return launch<BN, STAGES, false, false>(g, s);
+    if (!amn && bmn) return launch<BN, STAGES, false, true>(g, s);
+    if (amn && !bmn) return launch<BN, STAGES, true, false>(g, s);
+    return launch<BN, STAGES, true, true>(g, s);
+}
+
+bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
+
+} // namespace
+
+extern "C" int kmb_launch_gemm_bf16(const KmbGemm *g, cudaStream_t s) {
+    if (g->N > 128) return dispatch<256, 4>(g, s);
+    return dispatch<128, 6>(g, s);
+}
+
+extern "C" int kmb_gemm_bf16(const KmbGemm *g) {
+    if (!g) return kmb_fail(KMB_EINVAL, "gemm: NULL arguments");
+    if (g->M <= 0 || g->N <= 0 || g->K <= 0)
+        return kmb_fail(KMB_EINVAL, "gemm: M, N and K must be positive");
+    if (!g->A || !g->B || !g->C) return kmb_fail(KMB_EINVAL, "gemm: A, B and C are required");
+    if (g->act < 0 || g->act > 1) return kmb_fail(KMB_EINVAL, "gemm: unknown activation %d", g->act);
+    if (!aligned16(g->A) || !aligned16(g->B) || g->lda % 8 || g->ldb % 8)
+        return kmb_fail(KMB_EUNSUPPORTED,
+                        "gemm: A and B must be 16-byte aligned with lda, ldb multiples of 8");
+    const long a_inner = g->a_mn_major ? g->M : g->K, b_inner = g->b_mn_major ? g->N : g->K;
+    if (g->lda < a_inner || g->ldb < b_inner || g->ldc < g->N || (g->residual && g->ldr < g->N))
+        return kmb_fail(KMB_EINVAL, "gemm: leading dimension smaller than the row");
+    if (g->M >= (1L << 31) || g->N >= (1L << 31) || g->K >= (1L << 31))
+        return kmb_fail(KMB_EUNSUPPORTED, "gemm: dimensions must be below 2^31");
+    const void *ptrs[] = {g->A, g->B, g->C, g->bias, g->residual};
+    for (const void *q : ptrs)
+        if (q && !kmb_is_device_ptr(q))
+            return kmb_fail(KMB_EINVAL, "gemm: operands must be device memory");
+    kmb_clear_error();
+    const cudaStream_t s = kmb_stream();
+    int rc = kmb_launch_gemm_bf16(g, s);
+    if (rc) return rc;
+    if (kmb_sync_enabled()) {
+        cudaError_t e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) return kmb_cuda_fail(e, "gemm: stream synchronize");
+        return kmb_gemm_check_error();
+    }
+    return KMB_OK;
+}
+
+/* KMB_ETIMEOUT (and the flag cleared) when a launch's bounded wait gave up
+ * since the last check. */
+extern "C" int kmb_gemm_check_error(void) {
+    int flag = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&flag, g_gemm_error, sizeof flag);
+    if (e != cudaSuccess) return kmb_cuda_fail(e, "gemm: error word");
+    if (flag) {
+        const int zero = 0;
+        (void)cudaMemcpyToSymbol(g_gemm_error, &zero, sizeof zero);
+        return kmb_fail(KMB_ETIMEOUT, "gemm: a pipeline wait expired (device error word set)");
+    }
+    return KMB_OK;
+}

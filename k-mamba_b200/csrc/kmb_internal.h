@@ -68,6 +68,9 @@ int kmb_launch_scan2d_bwd(const KmbNDLaunch *a, cudaStream_t s);
 int kmb_scan2d_supported(const KmbNDLaunch *a);
 size_t kmb_scan2d_scratch_elems(const KmbNDLaunch *a);
 
+/* tcgen05 bf16 GEMM (csrc/cuda/gemm_tc.cu); operands already validated. */
+int kmb_launch_gemm_bf16(const KmbGemm *g, cudaStream_t s);
+
 /* Block / model kernels (csrc/cuda/block.cu). */
 /* C[m*ldc + n] (+)= sum_k A[m*am + k*ak] * B[k*bk + n*bn], fp32.  ws
  * (ws_elems floats, may be NULL) lets small output grids split K across

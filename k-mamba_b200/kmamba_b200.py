@@ -68,6 +68,13 @@ class KMWavefrontPlan(C.Structure):
                 ("level_starts", C.POINTER(lg)), ("level_offsets", C.POINTER(lg))]
 
 
+class KmbGemm(C.Structure):
+    _fields_ = [(n, fp) for n in ("A", "B", "C", "bias", "residual")] + [
+        (n, lg) for n in ("M", "N", "K", "lda", "ldb", "ldc", "ldr")] + [
+        (n, C.c_int) for n in ("a_mn_major", "b_mn_major", "c_bf16", "act", "accumulate",
+                               "pad_")]
+
+
 class KmbScan1D(C.Structure):
     _fields_ = [(n, fp) for n in ("x", "dt", "A", "B", "C", "h0", "y", "h_last", "h_all",
                                   "ckpt", "dy", "dx", "ddt", "dA", "dB", "dC")] + [
@@ -221,6 +228,9 @@ PROTOTYPES = {
     "kmb_pool_trim": (C.c_size_t, []),
     "kmb_pool_bytes_held": (C.c_size_t, []),
     "kmb_block_launch_count": (C.c_ulonglong, []),
+    # tensor-core GEMM
+    "kmb_gemm_bf16": (C.c_int, [C.POINTER(KmbGemm)]),
+    "kmb_gemm_check_error": (C.c_int, []),
     # 1D scan
     "kmb_scan1d_ckpt_elems": (lg, [lg, lg, lg, lg]),
     "kmb_scan1d_fwd": (C.c_int, [C.POINTER(KmbScan1D)]),
