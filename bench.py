@@ -345,6 +345,86 @@ def run_secondary(args):
 
 
 # --------------------------------------------------------------------------
+# tensor-core GEMM of the block projections (kmb_gemm_bf16)
+# --------------------------------------------------------------------------
+
+def run_gemm(args):
+    """Times kmb_gemm_bf16 on the projection shapes of a dim-1024 Mamba-ND
+    block: in_proj [T, 1024] x [2048, 1024]^T and
+    out_proj [T, 1024] x [1024, 1024]^T with T = --gemm-m tokens, bf16
+    operands and output, fp32 accumulation; plus the two gradient GEMMs of
+    in_proj (MN-major operands).  Reports TFLOP/s against the measured
+    cuBLAS bf16 peak."""
+    import torch
+    import kmamba_b200 as kb
+    lib = kb.load()
+    stream = torch.cuda.current_stream()
+    lib.kmb_set_stream(C.c_void_p(stream.cuda_stream))
+    lib.kmb_set_sync(0)
+    T = args.gemm_m
+    g = torch.Generator(device="cuda").manual_seed(1234)
+    bf = torch.bfloat16
+    x = torch.randn(T, 1024, device="cuda", generator=g).to(bf)
+    w_in = (torch.randn(2048, 1024, device="cuda", generator=g) / 32).to(bf)
+    w_out = (torch.randn(1024, 1024, device="cuda", generator=g) / 32).to(bf)
+    z = torch.empty(T, 2048, device="cuda", dtype=bf)
+    y = torch.empty(T, 1024, device="cuda", dtype=bf)
+    dz = torch.randn(T, 2048, device="cuda", generator=g).to(bf)
+    dx = torch.empty(T, 1024, device="cuda", dtype=bf)
+    dw = torch.empty(2048, 1024, device="cuda", dtype=torch.float32)
+
+    def mk(A, B, Cc, M, N, K, lda, ldb, ldc, amn=0, bmn=0, c16=1):
+        a = kb.KmbGemm()
+        a.A, a.B, a.C = A.data_ptr(), B.data_ptr(), Cc.data_ptr()
+        a.M, a.N, a.K, a.lda, a.ldb, a.ldc = M, N, K, lda, ldb, ldc
+        a.a_mn_major, a.b_mn_major, a.c_bf16 = amn, bmn, c16
+        return a
+    ops = [("in_proj", mk(x, w_in, z, T, 2048, 1024, 1024, 1024, 2048), 2 * T * 2048 * 1024),
+           ("out_proj", mk(x, w_out, y, T, 1024, 1024, 1024, 1024, 1024), 2 * T * 1024 * 1024),
+           # dx = dz W_in: A = dz [T, 2048] K-major, B = W_in^T: [1024, 2048] stored [2048, 1024]
+           ("in_proj_dx", mk(dz, w_in, dx, T, 1024, 2048, 2048, 1024, 1024, 0, 1),
+            2 * T * 1024 * 2048),
+           # dW = dz^T x: A = dz^T [2048, T] stored [T, 2048], B = x^T [1024, T] stored [T, 1024]
+           ("in_proj_dw", mk(dz, x, dw, 2048, 1024, T, 2048, 1024, 1024, 1, 1, 0),
+            2 * T * 2048 * 1024)]
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+    for _ in range(args.warmup):
+        for _, a, _ in ops:
+            kb.check(lib, lib.kmb_gemm_bf16(C.byref(a)))
+    torch.cuda.synchronize()
+    marks = [[ev() for _ in range(len(ops) + 1)] for _ in range(args.steps)]
+    with Clocks(0) as clk:
+        for m in marks:
+            m[0].record(stream)
+            for i, (_, a, _) in enumerate(ops):
+                kb.check(lib, lib.kmb_gemm_bf16(C.byref(a)))
+                m[i + 1].record(stream)
+        torch.cuda.synchronize()
+    kb.check(lib, lib.kmb_gemm_check_error())
+    per = {name: sum(m[i].elapsed_time(m[i + 1]) for m in marks) / args.steps
+           for i, (name, _, _) in enumerate(ops)}
+    flops = sum(f for _, _, f in ops)
+    ms = sum(per.values())
+    pk, pk_kind = peaks()
+    tf = {name: f / (per[name] / 1e3) / 1e12 for name, _, f in ops}
+    dom = max(per, key=per.get)
+    print(json.dumps({
+        "metric": "bf16 GEMM TFLOP/s (block projections, tcgen05)", "value": flops / (ms / 1e3) / 1e12,
+        "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"dim-1024 block projections, T={T} tokens: in_proj, out_proj, "
+                               "in_proj input and weight gradients",
+                   **{k + "_ms": v for k, v in per.items()},
+                   **{k + "_TFLOPs": v for k, v in tf.items()}},
+        "roofline": {"bound": "tensor", "kernel": "k_gemm_tc (" + dom + ")",
+                     "achieved": tf[dom], "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": tf[dom] / pk["bf16_tflops"],
+                     "peak_source": f"{pk_kind} bf16_tflops (cuBLAS burst)", "traffic": None},
+        "gpu_launches": len(ops) * args.steps, "clocks": clk.summary()}), flush=True)
+
+
+# --------------------------------------------------------------------------
 # config 5 at kernel level: one Mamba-ND layer's ConvND + ND scan over 64^3
 # --------------------------------------------------------------------------
 
@@ -553,8 +633,10 @@ def main():
                          "the workload's BASELINE batch)")
     ap.add_argument("--dim", type=int, default=None,
                     help="nd5 only: channels (default 1024; smaller for profiling captures)")
+    ap.add_argument("--gemm-m", type=int, default=32768,
+                    help="gemm only: tokens (rows) of the projection GEMMs")
     ap.add_argument("--workload", default="scan1d",
-                    choices=["scan1d", "conv3", "scan2d4", "model1", "nd5"],
+                    choices=["scan1d", "conv3", "scan2d4", "model1", "nd5", "gemm"],
                     help="scan1d = BASELINE config 2 (the headline); conv3 / scan2d4 time "
                          "configs 3 and 4 for their roofline evidence")
     args = ap.parse_args()
@@ -568,6 +650,9 @@ def main():
         return
     if args.workload == "nd5":
         run_nd5(args)
+        return
+    if args.workload == "gemm":
+        run_gemm(args)
         return
     if args.workload != "scan1d":
         run_secondary(args)
