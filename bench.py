@@ -17,8 +17,10 @@ cpu/scan1d_backward.c for the backward) on the host cores, on bounded
 samples of the same workload, with the same metric.
 
 Multi-GPU (torchrun): every rank runs a full config-2 batch of its own
-(weak scaling); the only exchange is the sum of the parameter gradient dA
-over ranks (NCCL all-reduce), as data-parallel training needs.
+(weak scaling), or with --shard-batch the config's batch of 8 is split over
+the ranks (strong scaling).  The only exchange is the sum of the parameter
+gradient dA over ranks, all-reduced by the library's own NCCL communicator
+(kmamba_distributed.h) on a side stream while the next forward runs.
 """
 from __future__ import annotations
 
@@ -633,6 +635,9 @@ def main():
                          "the workload's BASELINE batch)")
     ap.add_argument("--dim", type=int, default=None,
                     help="nd5 only: channels (default 1024; smaller for profiling captures)")
+    ap.add_argument("--shard-batch", action="store_true",
+                    help="scan1d: split the config's batch over the ranks (strong scaling) "
+                         "instead of a full batch per rank (weak scaling, the default)")
     ap.add_argument("--gemm-m", type=int, default=32768,
                     help="gemm only: tokens (rows) of the projection GEMMs")
     ap.add_argument("--workload", default="scan1d",
@@ -666,12 +671,34 @@ def main():
     rank, world = kmb_dist.env_rank()
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
+    global_batch = BATCH
+    if args.shard_batch:
+        # strong scaling: the config's batch split over the ranks (earlier
+        # ranks take the extra items, kmamba_distributed_split_batch's rule)
+        set_batch(global_batch // world + (1 if rank < global_batch % world else 0))
+        if BATCH == 0:
+            raise SystemExit(f"--shard-batch: {world} ranks for a batch of {global_batch}")
+    global_bytes = STEP_BYTES * global_batch / BATCH if args.shard_batch else STEP_BYTES * world
     if world > 1:
         kmb_dist.init("nccl", timeout_s=120, device_id=torch.device("cuda", local))
     lib = kb.load()
     stream = torch.cuda.current_stream()
-    lib.kmb_set_stream(C.c_void_p(stream.cuda_stream))
+    sp = C.c_void_p(stream.cuda_stream)
+    lib.kmb_set_stream(sp)
     lib.kmb_set_sync(0)
+    # the data-parallel exchange (dA) runs on the library's own NCCL
+    # communicator; torch.distributed only carries its id, the barriers and
+    # the max-over-ranks timing
+    ctx = None
+    if world > 1:
+        uid = C.create_string_buffer(128)
+        if rank == 0:
+            kb.check(lib, lib.kmb_dist_get_unique_id(uid))
+        box = [uid.raw if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        ctx = lib.kmb_dist_init_with_id(world, rank, local, C.create_string_buffer(box[0], 128))
+        if not ctx:
+            raise RuntimeError(kb.last_error(lib))
 
     x, dt, A, B, Cm, dy = make_inputs(seed=kmb_dist.shard_seed(1000, rank))
     dev = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
@@ -699,12 +726,18 @@ def main():
         if marks:
             marks[0].record(stream)
         kb.check(lib, lib.kmb_scan1d_fwd(C.byref(fa)))
+        if ctx:
+            # the previous step's dA reduction (overlapped with this
+            # forward) must end before this backward overwrites dA
+            kb.check(lib, lib.kmb_dist_wait(ctx, sp))
         if marks:
             marks[1].record(stream)
         kb.check(lib, lib.kmb_scan1d_bwd(C.byref(ba)))
         if marks:
             marks[2].record(stream)
-        kmb_dist.sum_grads([g["dA"]], world)
+        if ctx:
+            kb.check(lib, lib.kmb_dist_bucket_add(ctx, g["dA"].data_ptr(), D * N, 0, sp))
+            kb.check(lib, lib.kmb_dist_bucket_flush(ctx, sp))
 
     for _ in range(args.warmup):
         step()
@@ -719,6 +752,8 @@ def main():
         start.record(stream)
         for i in range(args.steps):
             step(marks[i])
+        if ctx:
+            kb.check(lib, lib.kmb_dist_wait(ctx, sp))  # the last step's reduction
         stop.record(stream)
         torch.cuda.synchronize()
     if world > 1:
@@ -727,7 +762,7 @@ def main():
     fwd_ms = sum(m[0].elapsed_time(m[1]) for m in marks) / args.steps
     bwd_ms = sum(m[1].elapsed_time(m[2]) for m in marks) / args.steps
     elapsed = kmb_dist.max_over_ranks(elapsed, world, device="cuda")
-    value = kmb_dist.weak_scaling_rate(STEP_BYTES, world, args.steps, elapsed)
+    value = global_bytes * args.steps / elapsed / 1e9
 
     # ---------------- e2e through the public C ABI with host buffers ----------
     h2d = d2h = 0
@@ -762,7 +797,7 @@ def main():
         torch.cuda.synchronize()
         te = (time.perf_counter() - t0) / args.e2e_steps
         te = kmb_dist.max_over_ranks(te, world, device="cuda")
-        e2e_val = kmb_dist.weak_scaling_rate(STEP_BYTES, world, 1, te)
+        e2e_val = global_bytes / te / 1e9
         lib.kmb_set_sync(0)
 
     pk, pk_kind = peaks()
@@ -788,10 +823,14 @@ def main():
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (config-2 distributions, seeded per rank)",
-            "config": {"workload": WORKLOAD, "batch_per_gpu": BATCH, "L": L, "D": D, "N": N,
-                       "parallelism": f"dp{world} (independent batch per rank, dA all-reduce)",
+            "scaling": "strong" if args.shard_batch else "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (config-2 distributions, seeded per rank)",
+            "config": {"workload": WORKLOAD, "batch_per_gpu": BATCH,
+                       "global_batch": global_batch if args.shard_batch else BATCH * world,
+                       "L": L, "D": D, "N": N,
+                       "parallelism": (f"dp{world} ({'the config batch split over the ranks' if args.shard_batch else 'independent batch per rank'}; "
+                                       "dA all-reduced by the library's NCCL communicator on a "
+                                       "side stream, overlapped with the next forward)"),
                        "l2": "inputs larger than L2 (each [B,L,D] tensor is 201 MB)",
                        "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
                        "fwd_GBps": FWD_BYTES / fwd_ms / 1e6, "bwd_GBps": BWD_BYTES / bwd_ms / 1e6},
@@ -808,6 +847,8 @@ def main():
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)
+    if ctx:
+        lib.kmamba_distributed_fini_nccl(ctx)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -75,6 +75,19 @@ class KmbGemm(C.Structure):
                                "pad_")]
 
 
+class KMambaDistributedConfig(C.Structure):
+    _fields_ = [("world_size", C.c_int), ("rank", C.c_int), ("local_rank", C.c_int),
+                ("layer_start", C.c_size_t), ("layer_end", C.c_size_t),
+                ("batch_start", C.c_size_t), ("batch_end", C.c_size_t),
+                ("use_nccl", C.c_int), ("use_p2p", C.c_int)]
+
+
+class KMambaDistributedContext(C.Structure):
+    _fields_ = [("config", KMambaDistributedConfig), ("nccl_comm", C.c_void_p),
+                ("stream", C.c_void_p), ("nccl_scratch", C.c_void_p),
+                ("scratch_size", C.c_size_t)]
+
+
 class KmbScan1D(C.Structure):
     _fields_ = [(n, fp) for n in ("x", "dt", "A", "B", "C", "h0", "y", "h_last", "h_all",
                                   "ckpt", "dy", "dx", "ddt", "dA", "dB", "dC")] + [
@@ -228,6 +241,33 @@ PROTOTYPES = {
     "kmb_pool_trim": (C.c_size_t, []),
     "kmb_pool_bytes_held": (C.c_size_t, []),
     "kmb_block_launch_count": (C.c_ulonglong, []),
+    # NCCL data parallelism (kmamba_distributed.h)
+    "kmamba_distributed_init_nccl": (C.POINTER(KMambaDistributedContext), [C.c_int, C.c_int]),
+    "kmamba_distributed_fini_nccl": (None, [C.POINTER(KMambaDistributedContext)]),
+    "kmamba_allreduce_gradients_nccl": (C.c_int, [C.POINTER(KMambaDistributedContext), fp,
+                                                  C.c_size_t]),
+    "kmamba_broadcast_params_nccl": (C.c_int, [C.POINTER(KMambaDistributedContext), fp,
+                                               C.c_size_t]),
+    "kmamba_distributed_init_pipeline": (C.POINTER(KMambaDistributedContext), [C.c_int]),
+    "kmamba_distributed_fini_pipeline": (None, [C.POINTER(KMambaDistributedContext)]),
+    "kmamba_pipeline_send_recv": (C.c_int, [C.POINTER(KMambaDistributedContext), fp, fp,
+                                            C.c_size_t, C.c_int, C.c_int]),
+    "kmamba_distributed_split_batch": (None, [C.POINTER(KMambaDistributedConfig), C.c_size_t,
+                                              C.c_size_t]),
+    "kmamba_distributed_split_layers": (None, [C.POINTER(KMambaDistributedConfig),
+                                               C.c_size_t, C.c_size_t]),
+    "kmb_dist_get_unique_id": (C.c_int, [C.c_void_p]),
+    "kmb_dist_init_with_id": (C.POINTER(KMambaDistributedContext), [C.c_int, C.c_int, C.c_int,
+                                                                    C.c_void_p]),
+    "kmb_dist_rendezvous_file": (C.c_int, [C.c_char_p, C.c_int, C.c_void_p, C.c_size_t,
+                                           C.c_double]),
+    "kmb_dist_set_bucket_bytes": (C.c_int, [C.POINTER(KMambaDistributedContext), C.c_size_t]),
+    "kmb_dist_bucket_add": (C.c_int, [C.POINTER(KMambaDistributedContext), fp, C.c_size_t,
+                                      C.c_int, C.c_void_p]),
+    "kmb_dist_bucket_flush": (C.c_int, [C.POINTER(KMambaDistributedContext), C.c_void_p]),
+    "kmb_dist_wait": (C.c_int, [C.POINTER(KMambaDistributedContext), C.c_void_p]),
+    "kmb_dist_stats": (C.c_int, [C.POINTER(KMambaDistributedContext),
+                                 C.POINTER(C.c_ulonglong), C.POINTER(C.c_ulonglong)]),
     # tensor-core GEMM
     "kmb_gemm_bf16": (C.c_int, [C.POINTER(KmbGemm)]),
     "kmb_gemm_check_error": (C.c_int, []),

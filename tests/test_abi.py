@@ -19,6 +19,8 @@ def declared_functions():
         txt = open(h).read()
         txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
         txt = re.sub(r"typedef[^;]*;", "", txt)
+        # header-only helpers (static inline, as in the reference) are not exports
+        txt = re.sub(r"static\s+inline[^;{]*\{.*?\n\}", "", txt, flags=re.S)
         for m in DECL.finditer(txt):
             name = m.group(1)
             if name in ("if", "while", "return", "sizeof"):
