@@ -108,6 +108,18 @@ int kmb_scan1d_fwd(const KmbScan1D *args);
 int kmb_scan1d_bwd(const KmbScan1D *args);
 
 /*
+ * bf16-I/O variants of the same forward and backward (the reference has
+ * only host-side bf16 conversions, include/kmamba_mixed_precision.h:
+ * 106-112, which truncate).  x, dt, B, C, y, dy, dx, ddt, dB and dC point to
+ * bf16 (rounded to nearest even on output); A, dA, h0, h_last and ckpt stay
+ * fp32; arithmetic is fp32.  Device memory only, for the channel-shared
+ * layout: bc_shared = 1, N = 16, D a multiple of 32, h_all = NULL, 16-byte
+ * aligned tensors; other shapes return KMB_EUNSUPPORTED.
+ */
+int kmb_scan1d_fwd_bf16(const KmbScan1D *args);
+int kmb_scan1d_bwd_bf16(const KmbScan1D *args);
+
+/*
  * kmb_scan1d_bwd_noalloc -- no counterpart in the reference.
  *
  * The same backward as kmb_scan1d_bwd with h_all = ckpt = NULL, for

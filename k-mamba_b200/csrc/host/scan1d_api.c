@@ -5,6 +5,7 @@
  * csrc/cuda/scan1d.cu.
  */
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "../kmb_internal.h"
@@ -273,6 +274,56 @@ static int scan1d_pipelined(const KmbScan1D *a, int bwd) {
     return kmb_stage_finish(&st, rc);
 }
 
+/* ------------------------------------------------------------------ */
+/* sequence-split kernels (channel-shared B/C, N = 16, D % 32 == 0)     */
+/* ------------------------------------------------------------------ */
+
+/* KMB_SCAN1D_SEGMENTS=0 keeps the whole-sequence kernels for fp32 calls
+ * (a value >= 1 fixes the number of segments; default: planned). */
+static int seg_enabled(void) {
+    const char *e = getenv("KMB_SCAN1D_SEGMENTS");
+    return !(e && e[0] == '0' && e[1] == 0);
+}
+
+/* Forward through the sequence-split kernels on device pointers `d`. */
+static int seg_forward(KmbStage *st, const KmbScan1D *d, int bf16) {
+    int S = 1, seg_len = 0;
+    kmb_scan1d_seg_plan(d->batch, d->L, d->D, &S, &seg_len);
+    float *state = (float *)kmb_scratch(st, sizeof(float) * (size_t)d->batch * S * d->D * 16);
+    int *flag = (int *)kmb_scratch(st, sizeof(int) * (size_t)d->batch * (d->D / 32) * S);
+    if (!state || !flag) return st->status;
+    return kmb_launch_scan1d_fwd_seg(d, bf16, S, seg_len, state, flag, st->s);
+}
+
+/* Backward through the sequence-split kernels; computes the checkpoints
+ * into scratch first when the caller has none. */
+static int seg_backward(KmbStage *st, const KmbScan1D *d, int bf16) {
+    const float *ck = d->ckpt;
+    int rc;
+    if (!ck) {
+        KmbScan1D f = *d;
+        f.ckpt = (float *)kmb_scratch(
+            st, sizeof(float) * (size_t)kmb_scan1d_ckpt_elems(d->batch, d->L, d->D, d->N));
+        if (!f.ckpt) return st->status;
+        f.y = NULL;
+        f.h_last = NULL;
+        if ((rc = seg_forward(st, &f, bf16))) return rc;
+        ck = f.ckpt;
+    }
+    int S = 1, seg_len = 0;
+    kmb_scan1d_seg_plan(d->batch, d->L, d->D, &S, &seg_len);
+    float *state = (float *)kmb_scratch(st, sizeof(float) * (size_t)d->batch * S * d->D * 16);
+    int *flag = (int *)kmb_scratch(st, sizeof(int) * (size_t)d->batch * (d->D / 32) * S);
+    float *dB32 = d->dB, *dC32 = d->dC;
+    if (bf16) {
+        const size_t nbc = sizeof(float) * (size_t)d->batch * d->L * 16;
+        dB32 = (float *)kmb_scratch(st, nbc);
+        dC32 = (float *)kmb_scratch(st, nbc);
+    }
+    if (!state || !flag || !dB32 || !dC32) return st->status;
+    return kmb_launch_scan1d_bwd_seg(d, ck, bf16, S, seg_len, state, flag, dB32, dC32, st->s);
+}
+
 int kmb_scan1d_fwd(const KmbScan1D *a) {
     KmbStage st;
     KmbScan1D d;
@@ -282,7 +333,46 @@ int kmb_scan1d_fwd(const KmbScan1D *a) {
     kmb_stage_begin(&st);
     stage_args(&st, a, &d, 0);
     if (st.status) return kmb_stage_finish(&st, st.status);
-    rc = kmb_launch_scan1d_fwd(&d, st.s);
+    if (seg_enabled() && kmb_scan1d_seg_supported(&d, 4))
+        rc = seg_forward(&st, &d, 0);
+    else
+        rc = kmb_launch_scan1d_fwd(&d, st.s);
+    return kmb_stage_finish(&st, rc);
+}
+
+/* bf16 I/O variants: device memory only, the channel-shared layout. */
+static int validate_bf16(const KmbScan1D *a, int bwd) {
+    int rc = validate_common(a);
+    if (rc) return rc;
+    if (!kmb_scan1d_seg_supported(a, 2))
+        return kmb_fail(KMB_EUNSUPPORTED,
+                        "scan1d bf16: needs B/C shared across channels, N = 16, D a multiple of "
+                        "32, no h_all and 16-byte aligned tensors");
+    if (bwd && (!a->dy || !a->dx || !a->ddt || !a->dA || !a->dB || !a->dC))
+        return kmb_fail(KMB_EINVAL, "scan1d bf16 backward: dy and every gradient are required");
+    const void *ptrs[] = {a->x, a->dt, a->A, a->B, a->C, a->h0, a->y, a->h_last, a->ckpt,
+                          a->dy, a->dx, a->ddt, a->dA, a->dB, a->dC};
+    for (size_t i = 0; i < sizeof ptrs / sizeof *ptrs; ++i)
+        if (ptrs[i] && !kmb_is_device_ptr(ptrs[i]))
+            return kmb_fail(KMB_EINVAL, "scan1d bf16: every tensor must be device memory");
+    return KMB_OK;
+}
+
+int kmb_scan1d_fwd_bf16(const KmbScan1D *a) {
+    KmbStage st;
+    int rc = validate_bf16(a, 0);
+    if (rc) return rc;
+    kmb_stage_begin(&st);
+    rc = seg_forward(&st, a, 1);
+    return kmb_stage_finish(&st, rc);
+}
+
+int kmb_scan1d_bwd_bf16(const KmbScan1D *a) {
+    KmbStage st;
+    int rc = validate_bf16(a, 1);
+    if (rc) return rc;
+    kmb_stage_begin(&st);
+    rc = seg_backward(&st, a, 1);
     return kmb_stage_finish(&st, rc);
 }
 
@@ -298,6 +388,8 @@ int kmb_scan1d_bwd(const KmbScan1D *a) {
     kmb_stage_begin(&st);
     stage_args(&st, a, &d, 1);
     if (st.status) return kmb_stage_finish(&st, st.status);
+    if (seg_enabled() && kmb_scan1d_seg_supported(&d, 4))
+        return kmb_stage_finish(&st, seg_backward(&st, &d, 0));
     ck = d.ckpt;
     if (!d.h_all && !ck) {
         /* No stored states: run the forward once to produce checkpoints. */

@@ -26,6 +26,17 @@ int kmb_cuda_fail(cudaError_t e, const char *where);
 int kmb_launch_scan1d_fwd(const KmbScan1D *a, cudaStream_t s);
 int kmb_launch_scan1d_bwd(const KmbScan1D *a, const float *ckpt_in,
                           cudaStream_t s);
+/* Sequence-split kernels for the channel-shared layout (csrc/cuda/
+ * scan1d_seg.cu).  bf16: x, dt, B, C, y, dy, dx, ddt (and dB / dC after the
+ * fp32 accumulation in dB32 / dC32) are bf16.  seg_state holds batch * S *
+ * D * 16 floats, flag batch * (D / 32) * S ints. */
+int kmb_scan1d_seg_supported(const KmbScan1D *a, int elem_bytes);
+int kmb_scan1d_seg_plan(long batch, long L, long D, int *S, int *seg_len);
+int kmb_launch_scan1d_fwd_seg(const KmbScan1D *a, int bf16, int S, int seg_len,
+                              float *seg_state, int *flag, cudaStream_t s);
+int kmb_launch_scan1d_bwd_seg(const KmbScan1D *a, const float *ckpt_in, int bf16, int S,
+                              int seg_len, float *seg_state, int *flag, float *dB32,
+                              float *dC32, cudaStream_t s);
 int kmb_launch_scan1d_bwd_m1_shared(const float *x, const float *A,
                                     const float *A_diag, const float *B,
                                     const float *C, const float *delta,

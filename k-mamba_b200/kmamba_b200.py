@@ -276,6 +276,8 @@ PROTOTYPES = {
     "kmb_scan1d_fwd": (C.c_int, [C.POINTER(KmbScan1D)]),
     "kmb_scan1d_bwd": (C.c_int, [C.POINTER(KmbScan1D)]),
     "kmb_scan1d_bwd_noalloc": (C.c_int, [C.POINTER(KmbScan1D)]),
+    "kmb_scan1d_fwd_bf16": (C.c_int, [C.POINTER(KmbScan1D)]),
+    "kmb_scan1d_bwd_bf16": (C.c_int, [C.POINTER(KmbScan1D)]),
     "scan1d": (None, [C.POINTER(ScanParams)]),
     "scan1d_backward": (None, [C.POINTER(ScanBackwardParams)]),
     "scan1d_backward_m1_shared_bc": (None, [C.POINTER(ScanBackwardSharedParams)]),
