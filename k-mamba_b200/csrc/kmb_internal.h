@@ -82,6 +82,21 @@ size_t kmb_scan2d_scratch_elems(const KmbNDLaunch *a);
 /* tcgen05 bf16 GEMM (csrc/cuda/gemm_tc.cu); operands already validated. */
 int kmb_launch_gemm_bf16(const KmbGemm *g, cudaStream_t s);
 
+/* Mamba-ND block pieces (csrc/cuda/ndblock.cu). */
+int kmb_nd_to_bf16(const float *src, long lds, void *dst, long ldd, long rows, long cols,
+                   cudaStream_t s);
+int kmb_nd_silu(const float *v, float *c, const float *dc, float *dv, long n, cudaStream_t s);
+int kmb_nd_dt_bc(const float *q, long qld, const float *dtb, float *delta, float *B, float *C,
+                 long batch, long P, long d, cudaStream_t s);
+int kmb_nd_gate(const float *y, const float *z, void *g16, const float *dg, float *dy,
+                void *dz16, long n, cudaStream_t s);
+int kmb_nd_dt_bwd(const float *ddelta, const float *q, long qld, const float *dtb,
+                  const float *dB, const float *dC, float *dq, float *ddtb, long batch, long P,
+                  long d, cudaStream_t s);
+int kmb_nd_neg_exp(const float *A_log, float *A, float *dA_inout, long n, cudaStream_t s);
+int kmb_nd_roll_targets(const unsigned *tok, unsigned *tgt, long batch, long P, cudaStream_t s);
+int kmb_nd_mean(const float *x, long n, float *out, cudaStream_t s);
+
 /* Block / model kernels (csrc/cuda/block.cu). */
 /* C[m*ldc + n] (+)= sum_k A[m*am + k*ak] * B[k*bk + n*bn], fp32.  ws
  * (ws_elems floats, may be NULL) lets small output grids split K across

@@ -88,6 +88,11 @@ class KMambaDistributedContext(C.Structure):
                 ("scratch_size", C.c_size_t)]
 
 
+class KmbNDModelConfig(C.Structure):
+    _fields_ = [("dims", lg * 3), ("dim", lg), ("n_layers", lg), ("vocab", lg),
+                ("seed", C.c_ulonglong)]
+
+
 class KmbScan1D(C.Structure):
     _fields_ = [(n, fp) for n in ("x", "dt", "A", "B", "C", "h0", "y", "h_last", "h_all",
                                   "ckpt", "dy", "dx", "ddt", "dA", "dB", "dC")] + [
@@ -268,6 +273,19 @@ PROTOTYPES = {
     "kmb_dist_wait": (C.c_int, [C.POINTER(KMambaDistributedContext), C.c_void_p]),
     "kmb_dist_stats": (C.c_int, [C.POINTER(KMambaDistributedContext),
                                  C.POINTER(C.c_ulonglong), C.POINTER(C.c_ulonglong)]),
+    # Mamba-ND model (kmamba_ndmodel.h)
+    "kmb_ndmodel_create": (C.c_void_p, [C.POINTER(KmbNDModelConfig)]),
+    "kmb_ndmodel_free": (None, [C.c_void_p]),
+    "kmb_ndmodel_param_count": (lg, [C.c_void_p]),
+    "kmb_ndmodel_params": (C.c_void_p, [C.c_void_p]),
+    "kmb_ndmodel_grads": (C.c_void_p, [C.c_void_p]),
+    "kmb_ndmodel_sync_weights": (C.c_int, [C.c_void_p]),
+    "kmb_ndmodel_set_dist": (C.c_int, [C.c_void_p, C.POINTER(KMambaDistributedContext)]),
+    "kmb_ndmodel_forward": (C.c_int, [C.c_void_p, C.c_void_p, lg, C.POINTER(C.c_float)]),
+    "kmb_ndmodel_backward": (C.c_int, [C.c_void_p, C.c_void_p, lg, C.POINTER(C.c_float)]),
+    "kmb_ndmodel_step": (C.c_int, [C.c_void_p, C.c_float, C.c_float]),
+    "kmb_ndmodel_train_step": (C.c_int, [C.c_void_p, C.c_void_p, lg, C.c_float, C.c_float,
+                                         C.POINTER(C.c_float)]),
     # tensor-core GEMM
     "kmb_gemm_bf16": (C.c_int, [C.POINTER(KmbGemm)]),
     "kmb_gemm_check_error": (C.c_int, []),

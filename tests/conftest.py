@@ -63,7 +63,14 @@ def rel_err(a, b):
     fp32 CPU path against float64 scores 4e-6..9e-6 on this metric (and
     2.5e-4..3.4e-4 with a 1e-3 * rms floor, which is below fp32 noise for
     long recurrences), so the 1e-4 bar leaves room for the reordering of
-    fp32 sums on the GPU while any real error scores O(1)."""
+    fp32 sums on the GPU while any real error scores O(1).
+
+    What the floor covers, measured on config-2 distributions (one batch
+    item, L 4096, 128 channels, N 16): 54 % of y, 66 % of dx, 49 % of ddt,
+    24 % of dA and 9 % of dB / dC entries lie below 1 % of their tensor's
+    peak (heavy tails: the peak is 50-100x a typical entry), and for those
+    the bar is an absolute error of 1e-6 x peak; 7 %, 14 %, 7 %, 2.6 % and
+    0.9 % lie below 0.1 % of the peak."""
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)
     if b.size == 0:
