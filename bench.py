@@ -517,6 +517,125 @@ def run_nd5(args):
 
 
 # --------------------------------------------------------------------------
+# config 5: the Mamba-ND model (kmamba_ndmodel.h), tokens/s of a train step
+# --------------------------------------------------------------------------
+
+def run_nd5_model(args):
+    """BASELINE config 5 through kmamba_ndmodel.h: 24 ND blocks (dim 1024,
+    16 states, ConvND K 3) over 64^3 volumes of byte tokens (uniform in
+    [0, 256), seeded per rank), fp32 masters with bf16 GEMMs, one
+    kmb_ndmodel_train_step (forward, per-layer recompute + backward, NCCL
+    average of the gradients when N > 1, AdamW) per step.  value = tokens
+    of all ranks per second (max over ranks); e2e = the same with each
+    step's tokens copied from pinned host memory and the loss read back.
+    Batch per GPU defaults to 1 volume (the stored-state ND scan keeps a
+    [P, d, 16] history for the layer being differentiated: 17 GB per
+    volume at dim 1024)."""
+    import torch
+    import torch.distributed as dist
+    import kmamba_b200 as kb
+    import kmb_dist
+    rank, world = kmb_dist.env_rank()
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        kmb_dist.init("nccl", timeout_s=300, device_id=torch.device("cuda", local))
+    lib = kb.load()
+    stream = torch.cuda.current_stream()
+    sp = C.c_void_p(stream.cuda_stream)
+    lib.kmb_set_stream(sp)
+    lib.kmb_set_sync(0)
+    dims = [args.nd_side] * 3
+    P = int(np.prod(dims))
+    bsz = args.batch or 1
+    cfg = kb.KmbNDModelConfig()
+    for i in range(3):
+        cfg.dims[i] = dims[i]
+    cfg.dim, cfg.n_layers, cfg.vocab, cfg.seed = args.dim or 1024, args.layers, 256, 1234
+    m = lib.kmb_ndmodel_create(C.byref(cfg))
+    if not m:
+        raise RuntimeError(kb.last_error(lib))
+    ctx = None
+    if world > 1:
+        uid = C.create_string_buffer(128)
+        if rank == 0:
+            kb.check(lib, lib.kmb_dist_get_unique_id(uid))
+        box = [uid.raw if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        ctx = lib.kmb_dist_init_with_id(world, rank, local, C.create_string_buffer(box[0], 128))
+        if not ctx:
+            raise RuntimeError(kb.last_error(lib))
+        # identical initial weights on every rank (rank 0's)
+        if lib.kmamba_broadcast_params_nccl(ctx, lib.kmb_ndmodel_params(m),
+                                            lib.kmb_ndmodel_param_count(m)) != 0:
+            raise RuntimeError(kb.last_error(lib))
+        kb.check(lib, lib.kmb_ndmodel_sync_weights(m))
+        kb.check(lib, lib.kmb_ndmodel_set_dist(m, ctx))
+    rng = np.random.default_rng(kmb_dist.shard_seed(5000, rank))
+    tok = rng.integers(0, 256, (bsz, P), dtype=np.uint32)
+    dtok = torch.from_numpy(tok.astype(np.int32)).cuda()
+    loss = C.c_float()
+    lr, wd = 1e-4, 0.0
+
+    def step(ptr):
+        kb.check(lib, lib.kmb_ndmodel_train_step(m, ptr, bsz, lr, wd, C.byref(loss)))
+
+    for _ in range(args.warmup):
+        step(dtok.data_ptr())
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+    start, stop = ev(), ev()
+    with Clocks(local) as clk:
+        start.record(stream)
+        for _ in range(args.steps):
+            step(dtok.data_ptr())
+        stop.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    elapsed = kmb_dist.max_over_ranks(start.elapsed_time(stop) / 1e3, world, device="cuda")
+    value = bsz * P * world * args.steps / elapsed
+    # e2e: tokens from pinned host memory every step, loss read back
+    htok = torch.from_numpy(tok.astype(np.int32)).pin_memory()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(max(1, args.e2e_steps)):
+        step(htok.data_ptr())
+    torch.cuda.synchronize()
+    te = kmb_dist.max_over_ranks((time.perf_counter() - t0) / max(1, args.e2e_steps), world,
+                                 device="cuda")
+    if ctx:
+        lib.kmamba_distributed_fini_nccl(ctx)
+    lib.kmb_ndmodel_free(m)
+    if rank == 0:
+        # projection FLOPs of a step: forward a, z, out (3 d^2), the
+        # backward's recompute of a, z (2 d^2) and its six gradient GEMMs
+        # (6 d^2), per token and layer, x 2 FLOP per multiply-add
+        gemm_flops = 2 * bsz * P * 11 * cfg.dim * cfg.dim * cfg.n_layers
+        print(json.dumps({
+            "metric": "Mamba-ND model train tokens/s (config 5)", "value": value,
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16 GEMMs, fp32 scan / conv / masters",
+            "data": "synthetic byte tokens, uniform in [0, 256), seeded per rank",
+            "config": {"workload": f"config5: {cfg.n_layers} ND blocks, dim {cfg.dim}, 16 states, "
+                                   f"ConvND K 3, {dims[0]}^3 volume, batch {bsz} per GPU "
+                                   f"(global {bsz * world}; BASELINE names 64)",
+                       "parallelism": f"dp{world}: kmamba_distributed.h NCCL buckets per layer, "
+                                      "average, overlapped with the backward",
+                       "loss": loss.value,
+                       "projection_TFLOPs_per_gpu": gemm_flops * args.steps / elapsed / 1e12},
+            "e2e": {"value": bsz * P * world / te, "unit": "tokens/s",
+                    "h2d_bytes_per_step": 4 * bsz * P, "d2h_bytes_per_step": 4},
+            "gpu_launches": None, "clocks": clk.summary()}), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# --------------------------------------------------------------------------
 # config 1: the README KMamba model through kmamba.h
 # --------------------------------------------------------------------------
 
@@ -635,13 +754,15 @@ def main():
                          "the workload's BASELINE batch)")
     ap.add_argument("--dim", type=int, default=None,
                     help="nd5 only: channels (default 1024; smaller for profiling captures)")
+    ap.add_argument("--layers", type=int, default=24, help="nd5model only: ND blocks")
+    ap.add_argument("--nd-side", type=int, default=64, help="nd5model only: volume side")
     ap.add_argument("--shard-batch", action="store_true",
                     help="scan1d: split the config's batch over the ranks (strong scaling) "
                          "instead of a full batch per rank (weak scaling, the default)")
     ap.add_argument("--gemm-m", type=int, default=32768,
                     help="gemm only: tokens (rows) of the projection GEMMs")
     ap.add_argument("--workload", default="scan1d",
-                    choices=["scan1d", "conv3", "scan2d4", "model1", "nd5", "gemm"],
+                    choices=["scan1d", "conv3", "scan2d4", "model1", "nd5", "nd5model", "gemm"],
                     help="scan1d = BASELINE config 2 (the headline); conv3 / scan2d4 time "
                          "configs 3 and 4 for their roofline evidence")
     args = ap.parse_args()
@@ -658,6 +779,9 @@ def main():
         return
     if args.workload == "gemm":
         run_gemm(args)
+        return
+    if args.workload == "nd5model":
+        run_nd5_model(args)
         return
     if args.workload != "scan1d":
         run_secondary(args)
