@@ -528,9 +528,11 @@ def run_nd5_model(args):
     average of the gradients when N > 1, AdamW) per step.  value = tokens
     of all ranks per second (max over ranks); e2e = the same with each
     step's tokens copied from pinned host memory and the loss read back.
-    Batch per GPU defaults to 1 volume (the stored-state ND scan keeps a
-    [P, d, 16] history for the layer being differentiated: 17 GB per
-    volume at dim 1024)."""
+    Batch per GPU defaults to BASELINE's 64 volumes over 8 GPUs = 8, run as
+    micro-batches of as many volumes as fit (one at dim 1024: the
+    stored-state ND scan keeps a [P, d, 16] history for the layer being
+    differentiated, 17 GB per volume) whose gradients accumulate before the
+    NCCL average and AdamW."""
     import torch
     import torch.distributed as dist
     import kmamba_b200 as kb
@@ -547,7 +549,7 @@ def run_nd5_model(args):
     lib.kmb_set_sync(0)
     dims = [args.nd_side] * 3
     P = int(np.prod(dims))
-    bsz = args.batch or 1
+    bsz = args.batch or 8
     cfg = kb.KmbNDModelConfig()
     for i in range(3):
         cfg.dims[i] = dims[i]
@@ -621,8 +623,9 @@ def run_nd5_model(args):
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16 GEMMs, fp32 scan / conv / masters",
             "data": "synthetic byte tokens, uniform in [0, 256), seeded per rank",
             "config": {"workload": f"config5: {cfg.n_layers} ND blocks, dim {cfg.dim}, 16 states, "
-                                   f"ConvND K 3, {dims[0]}^3 volume, batch {bsz} per GPU "
-                                   f"(global {bsz * world}; BASELINE names 64)",
+                                   f"ConvND K 3, {dims[0]}^3 volumes, batch {bsz} per GPU "
+                                   f"(global {bsz * world}; BASELINE: 64 over 8 GPUs), "
+                                   "micro-batches sized to the free memory",
                        "parallelism": f"dp{world}: kmamba_distributed.h NCCL buckets per layer, "
                                       "average, overlapped with the backward",
                        "loss": loss.value,

@@ -25,7 +25,11 @@
  * bf16 copies of their operands (round to nearest even) and accumulate in
  * fp32; everything else is fp32.  The backward recomputes each layer's
  * activations from its stored input (one layer's activations live at a
- * time).  The optimizer is AdamW over all parameters.
+ * time).  A batch larger than the micro-batch runs as consecutive passes
+ * of micro_batch volumes whose gradients accumulate (each pass's loss
+ * weighted by its share of the batch), so the step's gradient is that of
+ * the whole batch's mean loss.  The optimizer is AdamW over all
+ * parameters.
  *
  * Flat parameter layout (fp32, kmb_ndmodel_params), in order:
  *   embedding [vocab, d], head [vocab, d], then per layer
@@ -48,6 +52,7 @@ typedef struct {
     long n_layers;
     long vocab;              /* token ids < vocab (256 for byte tokens) */
     unsigned long long seed; /* initialisation */
+    long micro_batch;        /* volumes per pass (0: as many as fit in free memory) */
 } KmbNDModelConfig;
 
 typedef struct KmbNDModel KmbNDModel;

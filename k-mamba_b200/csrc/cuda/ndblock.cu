@@ -223,18 +223,33 @@ extern "C" int kmb_nd_gate(const float *y, const float *z, void *g16, const floa
 }
 
 extern "C" int kmb_nd_dt_bwd(const float *ddelta, const float *q, long qld, const float *dtb,
-                             const float *dB, const float *dC, float *dq, float *ddtb, long batch,
-                             long P, long d, cudaStream_t s) {
+                             const float *dB, const float *dC, float *dq, float *ddtb, int acc,
+                             long batch, long P, long d, cudaStream_t s) {
     const long T = batch * P;
     k_dt_bwd_rows<<<grid_for(T * 32), 256, 0, s>>>(ddelta, q, qld, dtb, dB, dC, dq, batch, P, d);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return kmb_cuda_fail(e, "nd: dt backward rows");
-    e = cudaMemsetAsync(ddtb, 0, sizeof(float) * 3 * d, s);
+    if (!acc) e = cudaMemsetAsync(ddtb, 0, sizeof(float) * 3 * d, s);
     if (e != cudaSuccess) return kmb_cuda_fail(e, "nd: dt bias memset");
     const long rows = 256;
     dim3 grid((unsigned)((d + 255) / 256), (unsigned)((T + rows - 1) / rows), 3);
     k_dt_bwd_cols<<<grid, 256, 0, s>>>(ddelta, q, qld, dtb, ddtb, batch, P, d, rows);
     KMB_ND_RET("nd: dt backward columns");
+}
+
+/* g (+)= dA * (-exp(A_log)): the A_log gradient of a scan's dA */
+__global__ void k_dalog(const float *A_log, const float *dA, float *g, int acc, long n) {
+    for (long e = (long)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+         e += (long)gridDim.x * blockDim.x) {
+        const float v = -dA[e] * __expf(A_log[e]);
+        g[e] = acc ? g[e] + v : v;
+    }
+}
+
+extern "C" int kmb_nd_dalog(const float *A_log, const float *dA, float *g, int acc, long n,
+                            cudaStream_t s) {
+    k_dalog<<<grid_for(n), 256, 0, s>>>(A_log, dA, g, acc, n);
+    KMB_ND_RET("nd: A_log gradient");
 }
 
 extern "C" int kmb_nd_neg_exp(const float *A_log, float *A, float *dA_inout, long n,

@@ -36,7 +36,8 @@ typedef struct {
     float *delta, *ddelta;    /* [batch, 3, P, d] */
     float *Bs, *Cs, *dBs, *dCs; /* [T, 16] */
     float *h;                 /* [T, d, 16] scan history */
-    float *A;                 /* [3, d, 16] */
+    float *A, *dA_tmp;        /* [3, d, 16] */
+    float *ck_tmp, *cb_tmp;   /* conv kernel / bias gradients of one pass */
     float *logits, *dlogits;  /* [T, vocab] */
     uint16_t *l16;            /* bf16 dlogits [T, vocab] */
     float *row_loss;          /* [T] */
@@ -162,7 +163,8 @@ static void *dalloc(size_t bytes, int *rc) {
 static void work_free(Work *w) {
     void *all[] = {w->x_store, w->x16, w->g16, w->d16a, w->d16b, w->a, w->z, w->v, w->c, w->y,
                    w->tmp1, w->tmp2, w->tmp3, w->q, w->dq, w->delta, w->ddelta, w->Bs, w->Cs,
-                   w->dBs, w->dCs, w->h, w->A, w->logits, w->dlogits, w->l16, w->row_loss,
+                   w->dBs, w->dCs, w->h, w->A, w->dA_tmp, w->ck_tmp, w->cb_tmp, w->logits,
+                   w->dlogits, w->l16, w->row_loss,
                    w->tok, w->tgt, w->loss_dev, w->gemm_ws};
     for (size_t i = 0; i < sizeof all / sizeof *all; ++i)
         if (all[i]) cudaFree(all[i]);
@@ -199,6 +201,9 @@ static int work_ensure(KmbNDModel *m, long batch) {
     w->dCs = dalloc(sizeof(float) * (size_t)T * NDM_STATE, &rc);
     w->h = dalloc(4 * td * NDM_STATE, &rc);
     w->A = dalloc(sizeof(float) * 3 * (size_t)d * NDM_STATE, &rc);
+    w->dA_tmp = dalloc(sizeof(float) * 3 * (size_t)d * NDM_STATE, &rc);
+    w->ck_tmp = dalloc(sizeof(float) * 27 * (size_t)d, &rc);
+    w->cb_tmp = dalloc(sizeof(float) * (size_t)d, &rc);
     w->logits = dalloc(sizeof(float) * (size_t)T * V, &rc);
     w->dlogits = dalloc(sizeof(float) * (size_t)T * V, &rc);
     w->l16 = dalloc(2 * (size_t)T * V, &rc);
@@ -276,7 +281,7 @@ static int block_forward(KmbNDModel *m, long l, long batch, const float *x_in, f
 /* Backward of layer l: dx_out (fp32 [T, d], the gradient of x_out) in,
  * dx_in out (may not alias dx_out); parameter gradients into m->grads. */
 static int block_backward(KmbNDModel *m, long l, long batch, const float *x_in,
-                          const float *dx_out, float *dx_in, cudaStream_t s) {
+                          const float *dx_out, float *dx_in, int acc, cudaStream_t s) {
     Work *w = &m->w;
     const long d = m->d, P = m->P, T = batch * P;
     LayerPtrs p = layer_ptrs(m->params, m, l);
@@ -289,7 +294,7 @@ static int block_backward(KmbNDModel *m, long l, long batch, const float *x_in,
     if ((rc = kmb_nd_to_bf16(dx_out, d, dxo16, d, T, d, s))) return rc;
     /* out_proj: dg = dx_out W_out, dW_out = dx_out^T g */
     if ((rc = gemm16(dxo16, w16 + 2 * d * d, dg, T, d, d, d, d, d, 0, 1, 0, NULL, 0, s))) return rc;
-    if ((rc = gemm16(dxo16, w->g16, gp.W_out, d, d, T, d, d, d, 1, 1, 0, NULL, 0, s))) return rc;
+    if ((rc = gemm16(dxo16, w->g16, gp.W_out, d, d, T, d, d, d, 1, 1, 0, NULL, acc, s))) return rc;
     /* gate */
     uint16_t *dz16 = w->d16b;
     if ((rc = kmb_nd_gate(w->y, w->z, NULL, dg, dys, dz16, T * d, s))) return rc;
@@ -306,7 +311,7 @@ static int block_backward(KmbNDModel *m, long l, long batch, const float *x_in,
     sn.dy = dys;
     sn.dx = dc;
     sn.ddelta = w->ddelta;
-    sn.dA = gp.A_log;
+    sn.dA = w->dA_tmp;
     sn.dB = w->dBs;
     sn.dC = w->dCs;
     for (int i = 0; i < 3; ++i) sn.dims[i] = m->cfg.dims[i];
@@ -316,14 +321,14 @@ static int block_backward(KmbNDModel *m, long l, long batch, const float *x_in,
     sn.M = NDM_STATE;
     sn.bc_shared = 1;
     if ((rc = kmb_scannd_bwd(&sn))) return rc;
-    if ((rc = kmb_nd_neg_exp(p.A_log, NULL, gp.A_log, 3 * d * NDM_STATE, s))) return rc;
+    if ((rc = kmb_nd_dalog(p.A_log, w->dA_tmp, gp.A_log, acc, 3 * d * NDM_STATE, s))) return rc;
     /* dt / B / C projection */
     if ((rc = kmb_nd_dt_bwd(w->ddelta, w->q, NDM_QC, p.dt_bias, w->dBs, w->dCs, w->dq, gp.dt_bias,
-                            batch, P, d, s)))
+                            acc, batch, P, d, s)))
         return rc;
     if ((rc = kmb_gemm((int)T, (int)d, NDM_QC, w->dq, NDM_QC, 1, p.W_p, d, 1, dc, d, 1, NULL, 0, s)))
         return rc;
-    if ((rc = kmb_gemm(NDM_QC, (int)d, (int)T, w->dq, 1, NDM_QC, w->c, d, 1, gp.W_p, d, 0,
+    if ((rc = kmb_gemm(NDM_QC, (int)d, (int)T, w->dq, 1, NDM_QC, w->c, d, 1, gp.W_p, d, acc,
                        w->gemm_ws, w->gemm_ws_elems, s)))
         return rc;
     /* silu, then ConvND backward: da in tmp1 (dg is dead) */
@@ -335,21 +340,24 @@ static int block_backward(KmbNDModel *m, long l, long batch, const float *x_in,
     cv.kernel = p.conv_kernel;
     cv.dy = dv;
     cv.dinput = da;
-    cv.dkernel = gp.conv_kernel;
-    cv.dbias = gp.conv_bias;
+    cv.dkernel = acc ? w->ck_tmp : gp.conv_kernel;
+    cv.dbias = acc ? w->cb_tmp : gp.conv_bias;
     for (int i = 0; i < 3; ++i) cv.dims[i] = m->cfg.dims[i];
     cv.ndims = 3;
     cv.batch = batch;
     cv.D = d;
     cv.K = NDM_K;
     if ((rc = kmb_launch_convnd_bwd(&cv, s))) return rc;
+    if (acc && ((rc = kmb_axpby(gp.conv_kernel, w->ck_tmp, 27 * d, 1.f, 1.f, s)) ||
+                (rc = kmb_axpby(gp.conv_bias, w->cb_tmp, d, 1.f, 1.f, s))))
+        return rc;
     /* in_proj: dx_in = dx_out + da W_a + dz W_z; dW_a = da^T x, dW_z = dz^T x */
     uint16_t *da16 = w->d16a;
     if ((rc = kmb_nd_to_bf16(da, d, da16, d, T, d, s))) return rc;
     if ((rc = gemm16(da16, w16, dx_in, T, d, d, d, d, d, 0, 1, 0, dx_out, 0, s))) return rc;
     if ((rc = gemm16(dz16, w16 + d * d, dx_in, T, d, d, d, d, d, 0, 1, 0, NULL, 1, s))) return rc;
-    if ((rc = gemm16(da16, w->x16, gp.W_a, d, d, T, d, d, d, 1, 1, 0, NULL, 0, s))) return rc;
-    return gemm16(dz16, w->x16, gp.W_z, d, d, T, d, d, d, 1, 1, 0, NULL, 0, s);
+    if ((rc = gemm16(da16, w->x16, gp.W_a, d, d, T, d, d, d, 1, 1, 0, NULL, acc, s))) return rc;
+    return gemm16(dz16, w->x16, gp.W_z, d, d, T, d, d, d, 1, 1, 0, NULL, acc, s);
 }
 
 /* ------------------------------------------------------------------ */
@@ -457,11 +465,11 @@ int kmb_ndmodel_set_dist(KmbNDModel *m, KMambaDistributedContext *ctx) {
 
 /* Tokens to the workspace, forward through every layer and the head;
  * leaves logits, dlogits (of the mean loss) and the loss on the device. */
-static int forward_all(KmbNDModel *m, const unsigned *tokens, long batch, cudaStream_t s) {
+static int forward_all(KmbNDModel *m, const unsigned *tokens, long batch, float weight,
+                       cudaStream_t s) {
     Work *w = &m->w;
     const long d = m->d, T = batch * m->P;
-    int rc = work_ensure(m, batch);
-    if (rc) return rc;
+    int rc = KMB_OK;
     const cudaError_t e = cudaMemcpyAsync(w->tok, tokens, sizeof(unsigned) * (size_t)T,
                                           cudaMemcpyDefault, s);
     if (e != cudaSuccess) return kmb_cuda_fail(e, "ndmodel: tokens");
@@ -476,7 +484,28 @@ static int forward_all(KmbNDModel *m, const unsigned *tokens, long batch, cudaSt
         return rc;
     if ((rc = kmb_nd_roll_targets(w->tok, w->tgt, batch, m->P, s))) return rc;
     if ((rc = kmb_softmax_ce(w->logits, w->tgt, T, m->V, w->dlogits, w->row_loss, s))) return rc;
+    /* this pass's share of the batch mean */
+    if (weight != 1.f && (rc = kmb_axpby(w->dlogits, NULL, T * m->V, weight, 0.f, s))) return rc;
     return kmb_nd_mean(w->row_loss, T, w->loss_dev, s);
+}
+
+/* Volumes per pass: the configured micro-batch, or as many as fit in
+ * 85 % of the free device memory (at least one). */
+static long micro_batch(KmbNDModel *m, long batch) {
+    if (m->cfg.micro_batch > 0) return m->cfg.micro_batch < batch ? m->cfg.micro_batch : batch;
+    if (m->w.batch > 0 && m->w.batch <= batch) return m->w.batch;
+    size_t freeb = 0, total = 0;
+    if (cudaMemGetInfo(&freeb, &total) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return 1;
+    }
+    /* per volume: residual stream of every layer, ~14 [P, d] fp32
+     * activations, 6 for the two delta tensors, the scan history and the
+     * scan's adjoint buffer (16 each), and the head's [P, vocab] buffers */
+    const double per = 4.0 * m->P * m->d * (m->L + 1 + 14 + 6 + 32) + 12.0 * m->P * m->V;
+    long mb = (long)(0.85 * (double)freeb / per);
+    if (mb < 1) mb = 1;
+    return mb < batch ? mb : batch;
 }
 
 static int read_loss(KmbNDModel *m, float *loss, cudaStream_t s) {
@@ -497,20 +526,32 @@ int kmb_ndmodel_forward(KmbNDModel *m, const unsigned *tokens, long batch, float
     int rc = check_call(m, tokens, batch);
     if (rc) return rc;
     const cudaStream_t s = kmb_stream();
-    rc = forward_all(m, tokens, batch, s);
-    if (!rc) rc = read_loss(m, loss, s);
+    const long mb = micro_batch(m, batch);
+    if ((rc = work_ensure(m, mb))) return rc;
+    double total = 0.0;
+    for (long i0 = 0; i0 < batch && !rc; i0 += mb) {
+        const long bi = batch - i0 < mb ? batch - i0 : mb;
+        float li = 0.f;
+        rc = forward_all(m, tokens + i0 * m->P, bi, 1.f, s);
+        if (!rc) rc = read_loss(m, &li, s);
+        total += (double)li * (double)bi;
+    }
+    if (!rc && loss) *loss = (float)(total / (double)batch);
     return finish(rc);
 }
 
-int kmb_ndmodel_backward(KmbNDModel *m, const unsigned *tokens, long batch, float *loss) {
-    int rc = check_call(m, tokens, batch);
+/* One pass of forward + backward over `batch` volumes; gradients are
+ * written (acc == 0) or added (acc == 1); the NCCL buckets are fed when
+ * `last`. */
+static int pass_backward(KmbNDModel *m, const unsigned *tokens, long batch, float weight,
+                         int acc, int last, float *loss, cudaStream_t s) {
+    int rc = forward_all(m, tokens, batch, weight, s);
     if (rc) return rc;
-    const cudaStream_t s = kmb_stream();
-    if ((rc = forward_all(m, tokens, batch, s))) return rc;
     Work *w = &m->w;
     const long d = m->d, T = batch * m->P, V = m->V;
     const size_t td = (size_t)T * d;
     void *sp = (void *)s;
+    const int feed = last && m->dist;
     float *g_emb = m->grads, *g_head = m->grads + V * d;
     /* Gradient slots: the residual stream x_l sits in x_store slot l.  Once
      * layer l's backward has read x_l (its recompute converts it to bf16
@@ -518,28 +559,47 @@ int kmb_ndmodel_backward(KmbNDModel *m, const unsigned *tokens, long batch, floa
      * is in slot l + 1 at that point.  x_L's slot takes d x_L after the
      * head's backward, whose weight gradient reads the bf16 copy of x_L. */
     if ((rc = kmb_nd_to_bf16(w->dlogits, V, w->l16, V, T, V, s))) return rc;
-    if ((rc = gemm16(w->l16, w->x16, g_head, V, d, T, V, d, d, 1, 1, 0, NULL, 0, s))) return rc;
+    if ((rc = gemm16(w->l16, w->x16, g_head, V, d, T, V, d, d, 1, 1, 0, NULL, acc, s))) return rc;
     if ((rc = gemm16(w->l16, w16_head(m), w->x_store + (size_t)m->L * td, T, d, V, V, d, d, 0,
                      1, 0, NULL, 0, s)))
         return rc;
-    if (m->dist && (rc = kmb_dist_bucket_add(m->dist, g_head, (size_t)V * d, 1, sp))) return rc;
+    if (feed && (rc = kmb_dist_bucket_add(m->dist, g_head, (size_t)V * d, 1, sp))) return rc;
     for (long l = m->L - 1; l >= 0; --l) {
         float *slot = w->x_store + (size_t)l * td;
-        if ((rc = block_backward(m, l, batch, slot, slot + td, slot, s))) return rc;
+        if ((rc = block_backward(m, l, batch, slot, slot + td, slot, acc, s))) return rc;
         LayerPtrs gp = layer_ptrs(m->grads, m, l);
-        if (m->dist && (rc = kmb_dist_bucket_add(m->dist, gp.W_a, (size_t)m->per_layer, 1, sp)))
+        if (feed && (rc = kmb_dist_bucket_add(m->dist, gp.W_a, (size_t)m->per_layer, 1, sp)))
             return rc;
     }
     /* embedding: scatter-add d x_0 */
-    cudaError_t e = cudaMemsetAsync(g_emb, 0, sizeof(float) * (size_t)V * d, s);
-    if (e != cudaSuccess) return kmb_cuda_fail(e, "ndmodel: embedding gradient memset");
+    if (!acc) {
+        const cudaError_t e = cudaMemsetAsync(g_emb, 0, sizeof(float) * (size_t)V * d, s);
+        if (e != cudaSuccess) return kmb_cuda_fail(e, "ndmodel: embedding gradient memset");
+    }
     if ((rc = kmb_embed(NULL, w->tok, T, d, V, NULL, w->x_store, g_emb, s))) return rc;
-    if (m->dist) {
+    if (feed) {
         if ((rc = kmb_dist_bucket_add(m->dist, g_emb, (size_t)V * d, 1, sp))) return rc;
         if ((rc = kmb_dist_bucket_flush(m->dist, sp))) return rc;
         if ((rc = kmb_dist_wait(m->dist, sp))) return rc;
     }
-    rc = read_loss(m, loss, s);
+    return read_loss(m, loss, s);
+}
+
+int kmb_ndmodel_backward(KmbNDModel *m, const unsigned *tokens, long batch, float *loss) {
+    int rc = check_call(m, tokens, batch);
+    if (rc) return rc;
+    const cudaStream_t s = kmb_stream();
+    const long mb = micro_batch(m, batch);
+    if ((rc = work_ensure(m, mb))) return rc;
+    double total = 0.0;
+    for (long i0 = 0; i0 < batch && !rc; i0 += mb) {
+        const long bi = batch - i0 < mb ? batch - i0 : mb;
+        float li = 0.f;
+        rc = pass_backward(m, tokens + i0 * m->P, bi, (float)bi / (float)batch, i0 > 0,
+                           i0 + bi >= batch, &li, s);
+        total += (double)li * (double)bi;
+    }
+    if (!rc && loss) *loss = (float)(total / (double)batch);
     return finish(rc);
 }
 

@@ -90,7 +90,7 @@ class KMambaDistributedContext(C.Structure):
 
 class KmbNDModelConfig(C.Structure):
     _fields_ = [("dims", lg * 3), ("dim", lg), ("n_layers", lg), ("vocab", lg),
-                ("seed", C.c_ulonglong)]
+                ("seed", C.c_ulonglong), ("micro_batch", lg)]
 
 
 class KmbScan1D(C.Structure):

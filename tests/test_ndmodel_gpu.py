@@ -2,7 +2,8 @@
 against its float64 torch restatement (oracle/ndmodel_ref.py), at a small
 volume: the loss of a forward, every parameter gradient of a backward
 (torch autograd of the restatement, with the same bf16 rounding of every
-GEMM operand), and one AdamW step.
+GEMM operand), and one AdamW step; also with the batch run as micro-batches
+whose gradients accumulate.
 
 Tolerances: the loss to 1e-4 relative; gradients to 2e-2 (the bar
 BASELINE sets for bf16 compute) on the parity metric of every test, with
@@ -61,15 +62,19 @@ def device_array(ptr, n):
     return buf.cpu().numpy()
 
 
-@pytest.mark.parametrize("dims,d,L,batch", [([3, 4, 5], 32, 2, 2), ([4, 4, 4], 64, 1, 1)])
-def test_ndmodel_loss_gradients_and_step(lib, cuda, dims, d, L, batch):
+@pytest.mark.parametrize("dims,d,L,batch,micro", [([3, 4, 5], 32, 2, 2, 0), ([4, 4, 4], 64, 1, 1, 0),
+                                                  # a batch of 3 run as passes of 1 and 2
+                                                  # volumes whose gradients accumulate
+                                                  ([4, 5, 3], 32, 2, 3, 1),
+                                                  ([4, 5, 3], 32, 2, 3, 2)])
+def test_ndmodel_loss_gradients_and_step(lib, cuda, dims, d, L, batch, micro):
     import torch
     import ndmodel_ref as ref
     V = 256
     cfg = kb.KmbNDModelConfig()
     for i in range(3):
         cfg.dims[i] = dims[i]
-    cfg.dim, cfg.n_layers, cfg.vocab, cfg.seed = d, L, V, 1234
+    cfg.dim, cfg.n_layers, cfg.vocab, cfg.seed, cfg.micro_batch = d, L, V, 1234, micro
     m = lib.kmb_ndmodel_create(C.byref(cfg))
     assert m, kb.last_error(lib)
     try:
@@ -125,3 +130,4 @@ def test_ndmodel_rejects_bad_config(lib):
     cfg.dim, cfg.n_layers, cfg.vocab = 48, 1, 256     # dim not a multiple of 32
     assert not lib.kmb_ndmodel_create(C.byref(cfg))
     assert b"multiple of 32" in lib.kmb_last_error()
+
