@@ -13,7 +13,7 @@
  *
  *   a = x W_a^T, z = x W_z^T                    bf16 tensor-core GEMMs
  *   c = silu(ConvND(a) + conv_bias)
- *   q = c W_p^T                                 [T, 35], fp32
+ *   q = c W_p^T                                 [T, 35], bf16 GEMM
  *   delta_k = ln 3 + softplus(q[:, k] + dt_bias[k]),  B = q[:, 3:19],
  *   C = q[:, 19:35],  A = -1 - exp(A_log)       (every decay <= 1/3)
  *   y = ScanND(c, delta, A, B, C)               channel-shared B / C

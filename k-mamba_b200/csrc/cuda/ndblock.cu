@@ -33,21 +33,32 @@ unsigned grid_for(long n, int threads = 256) {
     return (unsigned)(g < 1 ? 1 : g);
 }
 
+/* one row per CTA iteration (no per-element division) */
 __global__ void k_to_bf16(const float *src, long lds, __nv_bfloat16 *dst, long ldd, long rows,
                           long cols) {
-    const long n = rows * cols;
-    for (long e = (long)blockIdx.x * blockDim.x + threadIdx.x; e < n;
-         e += (long)gridDim.x * blockDim.x) {
-        const long r = e / cols, c = e - r * cols;
-        dst[r * ldd + c] = __float2bfloat16_rn(src[r * lds + c]);
+    for (long r = blockIdx.x; r < rows; r += gridDim.x) {
+        const float *s = src + r * lds;
+        __nv_bfloat16 *d = dst + r * ldd;
+        for (long c = threadIdx.x; c < cols; c += blockDim.x) d[c] = __float2bfloat16_rn(s[c]);
     }
 }
 
-__global__ void k_silu(const float *v, float *c, long n) {
+/* contiguous, 16-byte aligned, n a multiple of 4: four values per thread */
+__global__ void k_to_bf16_flat(const float4 *src, uint2 *dst, long n4) {
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
+         i += (long)gridDim.x * blockDim.x) {
+        const float4 v = src[i];
+        __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+        dst[i] = make_uint2(*reinterpret_cast<unsigned *>(&a), *reinterpret_cast<unsigned *>(&b));
+    }
+}
+
+__global__ void k_silu(const float *v, float *c, __nv_bfloat16 *c16, long n) {
     for (long e = (long)blockIdx.x * blockDim.x + threadIdx.x; e < n;
          e += (long)gridDim.x * blockDim.x) {
-        const float x = v[e];
-        c[e] = x * sigm(x);
+        const float x = v[e], y = x * sigm(x);
+        c[e] = y;
+        if (c16) c16[e] = __float2bfloat16_rn(y);
     }
 }
 
@@ -62,18 +73,23 @@ __global__ void k_silu_bwd(const float *dc, const float *v, float *dv, long n) {
 
 __global__ void k_dt_bc(const float *q, long qld, const float *dtb, float *delta, float *B,
                         float *C, long batch, long P, long d) {
-    const long T = batch * P, n = T * d;
-    for (long e = (long)blockIdx.x * blockDim.x + threadIdx.x; e < n;
-         e += (long)gridDim.x * blockDim.x) {
-        const long t = e / d, j = e - t * d;
-        const long b = t / P, p = t - b * P;
-        const float *qr = q + t * qld;
-#pragma unroll
-        for (int k = 0; k < 3; ++k)
-            delta[((b * 3 + k) * P + p) * d + j] = 1.0986122886681098f + softplus(qr[k] + dtb[k * d + j]);
-        if (j < kState) {
-            B[t * kState + j] = qr[3 + j];
-            C[t * kState + j] = qr[3 + kState + j];
+    for (long b = 0; b < batch; ++b) {
+        for (long p = blockIdx.x; p < P; p += gridDim.x) {
+            const long t = b * P + p;
+            const float *qr = q + t * qld;
+            const float q0 = qr[0], q1 = qr[1], q2 = qr[2];
+            float *d0 = delta + ((b * 3 + 0) * P + p) * d;
+            float *d1 = delta + ((b * 3 + 1) * P + p) * d;
+            float *d2 = delta + ((b * 3 + 2) * P + p) * d;
+            for (long j = threadIdx.x; j < d; j += blockDim.x) {
+                d0[j] = 1.0986122886681098f + softplus(q0 + dtb[j]);
+                d1[j] = 1.0986122886681098f + softplus(q1 + dtb[d + j]);
+                d2[j] = 1.0986122886681098f + softplus(q2 + dtb[2 * d + j]);
+            }
+            if (threadIdx.x < kState) {
+                B[t * kState + threadIdx.x] = qr[3 + threadIdx.x];
+                C[t * kState + threadIdx.x] = qr[3 + kState + threadIdx.x];
+            }
         }
     }
 }
@@ -97,31 +113,36 @@ __global__ void k_gate_bwd(const float *dg, const float *y, const float *z, floa
     }
 }
 
-/* dq[t, k] for k < 3 (one warp per token), dq[t, 3 + n] = dB, dq[t, 19 + n] = dC */
+/* dq[t, k] for k < 3 (one warp per token), dq[t, 3 + n] = dB, dq[t, 19 + n]
+ * = dC, written as bf16 rows of dq_ld values (the tensor-core GEMM operand;
+ * the columns from 35 to dq_ld are zero) */
 __global__ void k_dt_bwd_rows(const float *ddelta, const float *q, long qld, const float *dtb,
-                              const float *dB, const float *dC, float *dq, long batch, long P,
-                              long d) {
-    const long T = batch * P;
+                              const float *dB, const float *dC, __nv_bfloat16 *dq, long dq_ld,
+                              long batch, long P, long d) {
     const int lane = threadIdx.x & 31;
     const long warp = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const long nwarps = ((long)gridDim.x * blockDim.x) >> 5;
-    for (long t = warp; t < T; t += nwarps) {
-        const long b = t / P, p = t - b * P;
-        const float *qr = q + t * qld;
-        float *out = dq + t * qld;
+    for (long b = 0; b < batch; ++b) {
+        for (long p = warp; p < P; p += nwarps) {
+            const long t = b * P + p;
+            const float *qr = q + t * qld;
+            __nv_bfloat16 *out = dq + t * dq_ld;
 #pragma unroll
-        for (int k = 0; k < 3; ++k) {
-            const float *dd = ddelta + ((b * 3 + k) * P + p) * d;
-            const float qk = qr[k];
-            float acc = 0.f;
-            for (long j = lane; j < d; j += 32) acc = fmaf(dd[j], sigm(qk + dtb[k * d + j]), acc);
+            for (int k = 0; k < 3; ++k) {
+                const float *dd = ddelta + ((b * 3 + k) * P + p) * d;
+                const float qk = qr[k];
+                float acc = 0.f;
+                for (long j = lane; j < d; j += 32)
+                    acc = fmaf(dd[j], sigm(qk + dtb[k * d + j]), acc);
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-            if (lane == 0) out[k] = acc;
-        }
-        if (lane < kState) {
-            out[3 + lane] = dB[t * kState + lane];
-            out[3 + kState + lane] = dC[t * kState + lane];
+                for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+                if (lane == 0) out[k] = __float2bfloat16_rn(acc);
+            }
+            if (lane < kState) {
+                out[3 + lane] = __float2bfloat16_rn(dB[t * kState + lane]);
+                out[3 + kState + lane] = __float2bfloat16_rn(dC[t * kState + lane]);
+            }
+            for (long c = 3 + 2 * kState + lane; c < dq_ld; c += 32) out[c] = __float2bfloat16_rn(0.f);
         }
     }
 }
@@ -129,16 +150,17 @@ __global__ void k_dt_bwd_rows(const float *ddelta, const float *q, long qld, con
 /* d dt_bias[k, j] += sum over a chunk of tokens (atomics per chunk) */
 __global__ void k_dt_bwd_cols(const float *ddelta, const float *q, long qld, const float *dtb,
                               float *ddtb, long batch, long P, long d, long rows_per_cta) {
-    const long T = batch * P;
-    const long t0 = (long)blockIdx.y * rows_per_cta;
-    const long t1 = min(T, t0 + rows_per_cta);
+    /* rows [p0, p1) of every batch item */
+    const long p0 = (long)blockIdx.y * rows_per_cta;
+    const long p1 = min(P, p0 + rows_per_cta);
     const int k = blockIdx.z;
     for (long j = (long)blockIdx.x * blockDim.x + threadIdx.x; j < d; j += (long)gridDim.x * blockDim.x) {
         const float bias = dtb[k * d + j];
         float acc = 0.f;
-        for (long t = t0; t < t1; ++t) {
-            const long b = t / P, p = t - b * P;
-            acc = fmaf(ddelta[((b * 3 + k) * P + p) * d + j], sigm(q[t * qld + k] + bias), acc);
+        for (long b = 0; b < batch; ++b) {
+            const float *dd = ddelta + ((b * 3 + k) * P) * d + j;
+            const float *qc = q + (b * P) * qld + k;
+            for (long p = p0; p < p1; ++p) acc = fmaf(dd[p * d], sigm(qc[p * qld] + bias), acc);
         }
         atomicAdd(ddtb + k * d + j, acc);
     }
@@ -196,22 +218,30 @@ extern "C" int kmb_nd_mean(const float *x, long n, float *out, cudaStream_t s) {
 extern "C" int kmb_nd_to_bf16(const float *src, long lds, void *dst, long ldd, long rows,
                               long cols, cudaStream_t s) {
     if (rows <= 0 || cols <= 0) return KMB_OK;
-    k_to_bf16<<<grid_for(rows * cols), 256, 0, s>>>(src, lds, static_cast<__nv_bfloat16 *>(dst),
-                                                    ldd, rows, cols);
+    const long n = rows * cols;
+    if (lds == cols && ldd == cols && n % 4 == 0 && ((uintptr_t)src & 15u) == 0 &&
+        ((uintptr_t)dst & 7u) == 0) {
+        k_to_bf16_flat<<<grid_for(n / 4), 256, 0, s>>>(reinterpret_cast<const float4 *>(src),
+                                                       static_cast<uint2 *>(dst), n / 4);
+    } else {
+        const unsigned g = (unsigned)(rows < 148L * 16 ? rows : 148L * 16);
+        k_to_bf16<<<g, 256, 0, s>>>(src, lds, static_cast<__nv_bfloat16 *>(dst), ldd, rows, cols);
+    }
     KMB_ND_RET("nd: bf16 conversion");
 }
 
-extern "C" int kmb_nd_silu(const float *v, float *c, const float *dc, float *dv, long n,
-                           cudaStream_t s) {
+extern "C" int kmb_nd_silu(const float *v, float *c, void *c16, const float *dc, float *dv,
+                           long n, cudaStream_t s) {
     if (n <= 0) return KMB_OK;
     if (dc) k_silu_bwd<<<grid_for(n), 256, 0, s>>>(dc, v, dv, n);
-    else k_silu<<<grid_for(n), 256, 0, s>>>(v, c, n);
+    else k_silu<<<grid_for(n), 256, 0, s>>>(v, c, static_cast<__nv_bfloat16 *>(c16), n);
     KMB_ND_RET("nd: silu");
 }
 
 extern "C" int kmb_nd_dt_bc(const float *q, long qld, const float *dtb, float *delta, float *B,
                             float *C, long batch, long P, long d, cudaStream_t s) {
-    k_dt_bc<<<grid_for(batch * P * d), 256, 0, s>>>(q, qld, dtb, delta, B, C, batch, P, d);
+    k_dt_bc<<<(unsigned)(P < 148L * 16 ? P : 148L * 16), 256, 0, s>>>(q, qld, dtb, delta, B, C,
+                                                                        batch, P, d);
     KMB_ND_RET("nd: dt / B / C");
 }
 
@@ -223,16 +253,17 @@ extern "C" int kmb_nd_gate(const float *y, const float *z, void *g16, const floa
 }
 
 extern "C" int kmb_nd_dt_bwd(const float *ddelta, const float *q, long qld, const float *dtb,
-                             const float *dB, const float *dC, float *dq, float *ddtb, int acc,
-                             long batch, long P, long d, cudaStream_t s) {
-    const long T = batch * P;
-    k_dt_bwd_rows<<<grid_for(T * 32), 256, 0, s>>>(ddelta, q, qld, dtb, dB, dC, dq, batch, P, d);
+                             const float *dB, const float *dC, void *dq16, long dq_ld,
+                             float *ddtb, int acc, long batch, long P, long d, cudaStream_t s) {
+    k_dt_bwd_rows<<<grid_for(P * 32), 256, 0, s>>>(ddelta, q, qld, dtb, dB, dC,
+                                                   static_cast<__nv_bfloat16 *>(dq16), dq_ld,
+                                                   batch, P, d);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return kmb_cuda_fail(e, "nd: dt backward rows");
     if (!acc) e = cudaMemsetAsync(ddtb, 0, sizeof(float) * 3 * d, s);
     if (e != cudaSuccess) return kmb_cuda_fail(e, "nd: dt bias memset");
     const long rows = 256;
-    dim3 grid((unsigned)((d + 255) / 256), (unsigned)((T + rows - 1) / rows), 3);
+    dim3 grid((unsigned)((d + 255) / 256), (unsigned)((P + rows - 1) / rows), 3);
     k_dt_bwd_cols<<<grid, 256, 0, s>>>(ddelta, q, qld, dtb, ddtb, batch, P, d, rows);
     KMB_ND_RET("nd: dt backward columns");
 }

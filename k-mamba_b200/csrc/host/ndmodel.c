@@ -21,7 +21,8 @@
 
 #define NDM_K 3
 #define NDM_STATE 16
-#define NDM_QC 35 /* q columns: 3 dt inputs, 16 B, 16 C */
+#define NDM_QC 35  /* q columns: 3 dt inputs, 16 B, 16 C */
+#define NDM_QLD 40 /* row stride of the bf16 dq operand (a multiple of 8) */
 
 typedef struct {
     float *W_a, *W_z, *W_out, *W_p, *dt_bias, *A_log, *conv_kernel, *conv_bias;
@@ -30,9 +31,10 @@ typedef struct {
 typedef struct {
     long batch;
     float *x_store;           /* [(L + 1), T, d] residual stream */
-    uint16_t *x16, *g16, *d16a, *d16b; /* bf16 [T, d] GEMM operands */
+    uint16_t *x16, *g16, *d16a, *d16b, *c16; /* bf16 [T, d] GEMM operands */
     float *a, *z, *v, *c, *y, *tmp1, *tmp2, *tmp3; /* fp32 [T, d] */
-    float *q, *dq;            /* [T, 35] */
+    float *q;                 /* [T, 35] */
+    uint16_t *dq16;           /* bf16 [T, NDM_QLD] */
     float *delta, *ddelta;    /* [batch, 3, P, d] */
     float *Bs, *Cs, *dBs, *dCs; /* [T, 16] */
     float *h;                 /* [T, d, 16] scan history */
@@ -43,15 +45,13 @@ typedef struct {
     float *row_loss;          /* [T] */
     unsigned *tok, *tgt;      /* [T] */
     float *loss_dev;          /* [1] */
-    float *gemm_ws;           /* split-K workspace of the fp32 projections */
-    size_t gemm_ws_elems;
 } Work;
 
 struct KmbNDModel {
     KmbNDModelConfig cfg;
     long P, d, L, V, per_layer, n;
     float *params, *grads, *m, *v; /* device, flat */
-    uint16_t *w16;                 /* bf16 copies: [L][3 d d] then head [V d] */
+    uint16_t *w16;                 /* bf16 copies: [L][(3 d + 35) d] then head [V d] */
     long step;
     KMambaDistributedContext *dist;
     Work w;
@@ -78,8 +78,11 @@ static LayerPtrs layer_ptrs(float *base, const KmbNDModel *m, long l) {
     return r;
 }
 
-static uint16_t *w16_layer(const KmbNDModel *m, long l) { return m->w16 + l * 3 * m->d * m->d; }
-static uint16_t *w16_head(const KmbNDModel *m) { return m->w16 + m->L * 3 * m->d * m->d; }
+/* bf16 copies of a layer's W_a, W_z, W_out, W_p (contiguous, as in the
+ * fp32 layout), then the head */
+static long w16_layer_elems(const KmbNDModel *m) { return (3 * m->d + NDM_QC) * m->d; }
+static uint16_t *w16_layer(const KmbNDModel *m, long l) { return m->w16 + l * w16_layer_elems(m); }
+static uint16_t *w16_head(const KmbNDModel *m) { return m->w16 + m->L * w16_layer_elems(m); }
 
 /* ------------------------------------------------------------------ */
 /* initialisation (host, counter-based normals)                         */
@@ -161,11 +164,12 @@ static void *dalloc(size_t bytes, int *rc) {
 }
 
 static void work_free(Work *w) {
-    void *all[] = {w->x_store, w->x16, w->g16, w->d16a, w->d16b, w->a, w->z, w->v, w->c, w->y,
-                   w->tmp1, w->tmp2, w->tmp3, w->q, w->dq, w->delta, w->ddelta, w->Bs, w->Cs,
+    void *all[] = {w->x_store, w->x16, w->g16, w->d16a, w->d16b, w->c16, w->dq16, w->a, w->z,
+                   w->v, w->c, w->y, w->tmp1, w->tmp2, w->tmp3, w->q, w->delta, w->ddelta, w->Bs,
+                   w->Cs,
                    w->dBs, w->dCs, w->h, w->A, w->dA_tmp, w->ck_tmp, w->cb_tmp, w->logits,
                    w->dlogits, w->l16, w->row_loss,
-                   w->tok, w->tgt, w->loss_dev, w->gemm_ws};
+                   w->tok, w->tgt, w->loss_dev};
     for (size_t i = 0; i < sizeof all / sizeof *all; ++i)
         if (all[i]) cudaFree(all[i]);
     memset(w, 0, sizeof *w);
@@ -183,6 +187,8 @@ static int work_ensure(KmbNDModel *m, long batch) {
     w->g16 = dalloc(2 * td, &rc);
     w->d16a = dalloc(2 * td, &rc);
     w->d16b = dalloc(2 * td, &rc);
+    w->c16 = dalloc(2 * td, &rc);
+    w->dq16 = dalloc(2 * (size_t)T * NDM_QLD, &rc);
     w->a = dalloc(4 * td, &rc);
     w->z = dalloc(4 * td, &rc);
     w->v = dalloc(4 * td, &rc);
@@ -192,7 +198,6 @@ static int work_ensure(KmbNDModel *m, long batch) {
     w->tmp2 = dalloc(4 * td, &rc);
     w->tmp3 = dalloc(4 * td, &rc);
     w->q = dalloc(sizeof(float) * (size_t)T * NDM_QC, &rc);
-    w->dq = dalloc(sizeof(float) * (size_t)T * NDM_QC, &rc);
     w->delta = dalloc(4 * 3 * td, &rc);
     w->ddelta = dalloc(4 * 3 * td, &rc);
     w->Bs = dalloc(sizeof(float) * (size_t)T * NDM_STATE, &rc);
@@ -211,8 +216,6 @@ static int work_ensure(KmbNDModel *m, long batch) {
     w->tok = dalloc(sizeof(unsigned) * (size_t)T, &rc);
     w->tgt = dalloc(sizeof(unsigned) * (size_t)T, &rc);
     w->loss_dev = dalloc(sizeof(float), &rc);
-    w->gemm_ws_elems = (size_t)NDM_QC * d * 64;
-    w->gemm_ws = dalloc(sizeof(float) * w->gemm_ws_elems, &rc);
     if (rc) {
         work_free(w);
         return rc;
@@ -249,9 +252,9 @@ static int block_forward(KmbNDModel *m, long l, long batch, const float *x_in, f
     cv.D = d;
     cv.K = NDM_K;
     if ((rc = kmb_launch_convnd_fwd(&cv, s))) return rc;
-    if ((rc = kmb_nd_silu(w->v, w->c, NULL, NULL, T * d, s))) return rc;
-    if ((rc = kmb_gemm((int)T, NDM_QC, (int)d, w->c, d, 1, p.W_p, 1, d, w->q, NDM_QC, 0,
-                       w->gemm_ws, w->gemm_ws_elems, s)))
+    if ((rc = kmb_nd_silu(w->v, w->c, w->c16, NULL, NULL, T * d, s))) return rc;
+    if ((rc = gemm16(w->c16, w16 + 3 * d * d, w->q, T, NDM_QC, d, d, d, NDM_QC, 0, 0, 0, NULL, 0,
+                     s)))
         return rc;
     if ((rc = kmb_nd_dt_bc(w->q, NDM_QC, p.dt_bias, w->delta, w->Bs, w->Cs, batch, P, d, s)))
         return rc;
@@ -323,17 +326,18 @@ static int block_backward(KmbNDModel *m, long l, long batch, const float *x_in,
     if ((rc = kmb_scannd_bwd(&sn))) return rc;
     if ((rc = kmb_nd_dalog(p.A_log, w->dA_tmp, gp.A_log, acc, 3 * d * NDM_STATE, s))) return rc;
     /* dt / B / C projection */
-    if ((rc = kmb_nd_dt_bwd(w->ddelta, w->q, NDM_QC, p.dt_bias, w->dBs, w->dCs, w->dq, gp.dt_bias,
-                            acc, batch, P, d, s)))
+    if ((rc = kmb_nd_dt_bwd(w->ddelta, w->q, NDM_QC, p.dt_bias, w->dBs, w->dCs, w->dq16, NDM_QLD,
+                            gp.dt_bias, acc, batch, P, d, s)))
         return rc;
-    if ((rc = kmb_gemm((int)T, (int)d, NDM_QC, w->dq, NDM_QC, 1, p.W_p, d, 1, dc, d, 1, NULL, 0, s)))
+    /* dc += dq W_p, dW_p = dq^T c (bf16 operands, K of 35 zero-padded to the tile) */
+    if ((rc = gemm16(w->dq16, w16 + 3 * d * d, dc, T, d, NDM_QC, NDM_QLD, d, d, 0, 1, 0, NULL, 1,
+                     s)))
         return rc;
-    if ((rc = kmb_gemm(NDM_QC, (int)d, (int)T, w->dq, 1, NDM_QC, w->c, d, 1, gp.W_p, d, acc,
-                       w->gemm_ws, w->gemm_ws_elems, s)))
+    if ((rc = gemm16(w->dq16, w->c16, gp.W_p, NDM_QC, d, T, NDM_QLD, d, d, 1, 1, 0, NULL, acc, s)))
         return rc;
     /* silu, then ConvND backward: da in tmp1 (dg is dead) */
     float *dv = dys, *da = dg;
-    if ((rc = kmb_nd_silu(w->v, NULL, dc, dv, T * d, s))) return rc;
+    if ((rc = kmb_nd_silu(w->v, NULL, NULL, dc, dv, T * d, s))) return rc;
     KmbConvND cv;
     memset(&cv, 0, sizeof cv);
     cv.input = w->a;
@@ -368,7 +372,7 @@ static int refresh_w16(KmbNDModel *m, cudaStream_t s) {
     const long d = m->d;
     for (long l = 0; l < m->L; ++l) {
         LayerPtrs p = layer_ptrs(m->params, m, l);
-        int rc = kmb_nd_to_bf16(p.W_a, d, w16_layer(m, l), d, 3 * d, d, s);
+        int rc = kmb_nd_to_bf16(p.W_a, d, w16_layer(m, l), d, 3 * d + NDM_QC, d, s);
         if (rc) return rc;
     }
     return kmb_nd_to_bf16(m->params + m->V * d, d, w16_head(m), d, m->V, d, s);
@@ -407,7 +411,7 @@ KmbNDModel *kmb_ndmodel_create(const KmbNDModelConfig *cfg) {
     m->grads = dalloc(nb, &rc);
     m->m = dalloc(nb, &rc);
     m->v = dalloc(nb, &rc);
-    m->w16 = dalloc(2 * ((size_t)m->L * 3 * m->d * m->d + (size_t)m->V * m->d), &rc);
+    m->w16 = dalloc(2 * ((size_t)m->L * w16_layer_elems(m) + (size_t)m->V * m->d), &rc);
     float *host = rc ? NULL : (float *)malloc(nb);
     if (!rc && !host) rc = kmb_fail(KMB_ENOMEM, "ndmodel: host allocation failed");
     if (!rc) {

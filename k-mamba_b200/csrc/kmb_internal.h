@@ -85,14 +85,15 @@ int kmb_launch_gemm_bf16(const KmbGemm *g, cudaStream_t s);
 /* Mamba-ND block pieces (csrc/cuda/ndblock.cu). */
 int kmb_nd_to_bf16(const float *src, long lds, void *dst, long ldd, long rows, long cols,
                    cudaStream_t s);
-int kmb_nd_silu(const float *v, float *c, const float *dc, float *dv, long n, cudaStream_t s);
+int kmb_nd_silu(const float *v, float *c, void *c16, const float *dc, float *dv, long n,
+                cudaStream_t s);
 int kmb_nd_dt_bc(const float *q, long qld, const float *dtb, float *delta, float *B, float *C,
                  long batch, long P, long d, cudaStream_t s);
 int kmb_nd_gate(const float *y, const float *z, void *g16, const float *dg, float *dy,
                 void *dz16, long n, cudaStream_t s);
 int kmb_nd_dt_bwd(const float *ddelta, const float *q, long qld, const float *dtb,
-                  const float *dB, const float *dC, float *dq, float *ddtb, int acc, long batch,
-                  long P, long d, cudaStream_t s);
+                  const float *dB, const float *dC, void *dq16, long dq_ld, float *ddtb, int acc,
+                  long batch, long P, long d, cudaStream_t s);
 int kmb_nd_dalog(const float *A_log, const float *dA, float *g, int acc, long n, cudaStream_t s);
 int kmb_nd_neg_exp(const float *A_log, float *A, float *dA_inout, long n, cudaStream_t s);
 int kmb_nd_roll_targets(const unsigned *tok, unsigned *tgt, long batch, long P, cudaStream_t s);

@@ -19,7 +19,7 @@ Model (dims d = dim, N = 16 states, K = 3, 3 axes, P points per volume):
     a  = bf(x) bf(W_a)^T          z = bf(x) bf(W_z)^T    (bf16 GEMMs)
     v  = ConvND(a) + conv_bias
     c  = silu(v)
-    q  = c W_p^T                                          [P, 35] (fp32)
+    q  = bf(c) bf(W_p)^T                                  [P, 35] (bf16 GEMM)
     delta_k = ln 3 + softplus(q[:, k] + dt_bias[k])       k = 0, 1, 2
     B  = q[:, 3:19],  C = q[:, 19:35]
     y  = ScanND(c, delta, A = -1 - exp(A_log), B, C)
@@ -113,7 +113,7 @@ def forward_loss(params, tokens, dims, K=3):
             z = Bf16Linear.apply(x, layer["W_z"])
             v = conv3d_causal(a, layer["conv_kernel"], layer["conv_bias"], dims, K)
             c = v * torch.sigmoid(v)
-            q = c @ layer["W_p"].T
+            q = Bf16Linear.apply(c, layer["W_p"])
             delta = torch.stack([LN3 + torch.nn.functional.softplus(q[:, k][:, None] +
                                                                     layer["dt_bias"][k])
                                  for k in range(3)])
