@@ -928,9 +928,17 @@ def main():
         lib.kmb_set_sync(0)
 
     pk, pk_kind = peaks()
-    # config 2 (channel-shared B/C, 16-byte rows) runs k_scan1d_fwd and k_scan1d_bwd_sh
-    dom_ms, dom_bytes, dom_name = ((bwd_ms, BWD_BYTES, "k_scan1d_bwd_sh") if bwd_ms >= fwd_ms
-                                   else (fwd_ms, FWD_BYTES, "k_scan1d_fwd"))
+    # config 2 (channel-shared B/C, 16-byte rows, D a multiple of 32) runs the
+    # sequence-split kernels (plus their fixer launches when L is split)
+    # unless KMB_SCAN1D_SEGMENTS=0 selects the whole-sequence ones
+    seg_on = os.environ.get("KMB_SCAN1D_SEGMENTS", "") != "0"
+    n_seg, seg_len = C.c_int(1), C.c_int(0)
+    kb.check(lib, lib.kmb_scan1d_seg_plan(BATCH, L, D, C.byref(n_seg), C.byref(seg_len)))
+    fwd_name, bwd_name = (("k_scan1d_fwd_seg", "k_scan1d_bwd_seg") if seg_on
+                          else ("k_scan1d_fwd", "k_scan1d_bwd_sh"))
+    launches_per_step = 4 if seg_on and n_seg.value > 1 else 2
+    dom_ms, dom_bytes, dom_name = ((bwd_ms, BWD_BYTES, bwd_name) if bwd_ms >= fwd_ms
+                                   else (fwd_ms, FWD_BYTES, fwd_name))
     achieved = dom_bytes / (dom_ms / 1e3) / 1e9
     tr = traffic_from_profile()
     traffic = None
@@ -955,6 +963,7 @@ def main():
             "config": {"workload": WORKLOAD, "batch_per_gpu": BATCH,
                        "global_batch": global_batch if args.shard_batch else BATCH * world,
                        "L": L, "D": D, "N": N,
+                       "l_segments": n_seg.value if seg_on else 1,
                        "parallelism": (f"dp{world} ({'the config batch split over the ranks' if args.shard_batch else 'independent batch per rank'}; "
                                        "dA all-reduced by the library's NCCL communicator on a "
                                        "side stream, overlapped with the next forward)"),
@@ -970,7 +979,7 @@ def main():
                     "d2h_bytes_per_step": d2h,
                     "path": "kmb_scan1d_fwd + kmb_scan1d_bwd on pinned host buffers "
                             "(staged through the library's device pool)"},
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": launches_per_step * args.steps,
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)

@@ -291,6 +291,8 @@ PROTOTYPES = {
     "kmb_gemm_check_error": (C.c_int, []),
     # 1D scan
     "kmb_scan1d_ckpt_elems": (lg, [lg, lg, lg, lg]),
+    # segments and steps per segment the 1D entry points split L into
+    "kmb_scan1d_seg_plan": (C.c_int, [lg, lg, lg, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     "kmb_scan1d_fwd": (C.c_int, [C.POINTER(KmbScan1D)]),
     "kmb_scan1d_bwd": (C.c_int, [C.POINTER(KmbScan1D)]),
     "kmb_scan1d_bwd_noalloc": (C.c_int, [C.POINTER(KmbScan1D)]),
