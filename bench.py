@@ -255,15 +255,20 @@ def run_secondary(args):
     f = np.float32
     rng = np.random.default_rng(7)
     dev = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=f)).cuda()  # noqa: E731
+    dtype = "f32"
     if args.workload == "conv3":
         bsz, H, W, Dc, K = (args.batch or 16), 512, 512, 64, 3
         Pn = H * W
         E3 = bsz * Pn * Dc
-        fwd_b, bwd_b = 4 * (2 * E3 + 640), 4 * (3 * E3 + 1280)
-        inp = dev(rng.standard_normal((bsz, Pn, Dc), dtype=f))
+        # activations (input, output, dy, dinput) in fp32 or bf16; taps,
+        # bias and their gradients fp32
+        ab = 2 if args.io == "bf16" else 4
+        fwd_b, bwd_b = ab * 2 * E3 + 4 * 640, ab * 3 * E3 + 4 * 1280
+        act = (lambda a: dev(a).to(torch.bfloat16)) if ab == 2 else dev
+        inp = act(rng.standard_normal((bsz, Pn, Dc), dtype=f))
         ker = dev(rng.standard_normal((9, Dc), dtype=f) / 3)
         bias = dev(rng.standard_normal((Dc,), dtype=f) * 0.1)
-        dy = dev(rng.standard_normal((bsz, Pn, Dc), dtype=f))
+        dy = act(rng.standard_normal((bsz, Pn, Dc), dtype=f))
         out, din = torch.empty_like(inp), torch.empty_like(inp)
         dk, db = torch.empty_like(ker), torch.empty_like(bias)
         a = kb.KmbConvND()
@@ -271,10 +276,14 @@ def run_secondary(args):
         a.dy, a.dinput, a.dkernel, a.dbias = (t.data_ptr() for t in (dy, din, dk, db))
         a.dims[0], a.dims[1] = H, W
         a.ndims, a.batch, a.D, a.K = 2, bsz, Dc, K
-        fwd = lambda: kb.check(lib, lib.kmb_convnd_fwd(C.byref(a)))  # noqa: E731
-        bwd = lambda: kb.check(lib, lib.kmb_convnd_bwd(C.byref(a)))  # noqa: E731
-        names = ("k_conv2d_fwd", "k_conv2d_bwd")
-        workload = f"config3: ConvND 2D 512x512, D 64, K 3, batch {bsz}, fp32, fwd+bwd"
+        ffn, bfn = ((lib.kmb_convnd_fwd_bf16, lib.kmb_convnd_bwd_bf16) if ab == 2
+                    else (lib.kmb_convnd_fwd, lib.kmb_convnd_bwd))
+        fwd = lambda: kb.check(lib, ffn(C.byref(a)))  # noqa: E731
+        bwd = lambda: kb.check(lib, bfn(C.byref(a)))  # noqa: E731
+        names = ("k_conv2d_fwd_ring", "k_conv2d_bwd_ring")
+        dtype = "bf16 I/O, fp32 math" if ab == 2 else "f32"
+        workload = (f"config3: ConvND 2D 512x512, D 64, K 3, batch {bsz}, "
+                    f"{'bf16 activations' if ab == 2 else 'fp32'}, fwd+bwd")
         metric = "ConvND HBM GB/s (algorithmic bytes / device time)"
     else:
         bsz, H, W, Dc, Nn = (args.batch or 8), 256, 256, 256, 16
@@ -336,7 +345,7 @@ def run_secondary(args):
     print(json.dumps({
         "metric": metric, "value": (fwd_b + bwd_b) / ((fms + bms) / 1e3) / 1e9, "unit": "GB/s",
         "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": fms + bms,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype,
         "data": "synthetic", "config": {"workload": workload, "fwd_ms": fms, "bwd_ms": bms,
                                         "fwd_GBps": fwd_b / fms / 1e6,
                                         "bwd_GBps": bwd_b / bms / 1e6},
@@ -757,6 +766,8 @@ def main():
                          "the workload's BASELINE batch)")
     ap.add_argument("--dim", type=int, default=None,
                     help="nd5 only: channels (default 1024; smaller for profiling captures)")
+    ap.add_argument("--io", choices=["f32", "bf16"], default="f32",
+                    help="conv3 only: activation element type of the ConvND calls")
     ap.add_argument("--layers", type=int, default=24, help="nd5model only: ND blocks")
     ap.add_argument("--nd-side", type=int, default=64, help="nd5model only: volume side")
     ap.add_argument("--shard-batch", action="store_true",

@@ -175,6 +175,16 @@ typedef struct {
 int kmb_convnd_fwd(const KmbConvND *args);
 int kmb_convnd_bwd(const KmbConvND *args);
 
+/*
+ * The same with bf16 activations: input, output, dy and dinput point to
+ * bf16 device memory (output and dinput rounded to nearest even); kernel,
+ * bias, dkernel and dbias stay fp32, and every product and sum is fp32.
+ * Shapes: 2D with D a multiple of 64, or 3D with D a multiple of 8; K <= 3;
+ * 16-byte aligned device tensors (KMB_EUNSUPPORTED otherwise).
+ */
+int kmb_convnd_fwd_bf16(const KmbConvND *args);
+int kmb_convnd_bwd_bf16(const KmbConvND *args);
+
 /* ------------------------------------------------------------------ */
 /* Batched ND selective scan with stored states                        */
 /* ------------------------------------------------------------------ */

@@ -35,6 +35,8 @@
 
 #include <type_traits>
 
+#include <cuda_bf16.h>
+
 #include "kmb_common.cuh"
 #include "../kmb_internal.h"
 
@@ -95,6 +97,47 @@ struct Vec<1> {
     __device__ static T fma(T a, T b, T c) { return fmaf(a, b, c); }
     __device__ static T add(T a, T b) { return a + b; }
     __device__ static float get(T v, int) { return v; }
+};
+
+/* Activation element access of the streamed kernels.  The input, output,
+ * dy and dinput tensors are E = float or bf16 in memory and fp32 in
+ * registers; taps, bias, dkernel and dbias stay fp32.  bf16 results are
+ * rounded to nearest even. */
+template <typename E>
+struct CIO;
+template <>
+struct CIO<float> {
+    __device__ static float4 ld4(const float *s) { return *reinterpret_cast<const float4 *>(s); }
+    __device__ static float2 ld2(const float *s) { return *reinterpret_cast<const float2 *>(s); }
+    __device__ static float2 ldg2(const float *g) {
+        return __ldg(reinterpret_cast<const float2 *>(g));
+    }
+    __device__ static void st4(float *g, float4 v) { *reinterpret_cast<float4 *>(g) = v; }
+    __device__ static void st2(float *g, float2 v) { *reinterpret_cast<float2 *>(g) = v; }
+};
+template <>
+struct CIO<__nv_bfloat16> {
+    using E = __nv_bfloat16;
+    __device__ static float2 cvt(unsigned u) {
+        return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u));
+    }
+    __device__ static unsigned pack(float a, float b) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<const unsigned *>(&h);
+    }
+    __device__ static float4 ld4(const E *s) {
+        const uint2 u = *reinterpret_cast<const uint2 *>(s);
+        const float2 a = cvt(u.x), b = cvt(u.y);
+        return make_float4(a.x, a.y, b.x, b.y);
+    }
+    __device__ static float2 ld2(const E *s) { return cvt(*reinterpret_cast<const unsigned *>(s)); }
+    __device__ static float2 ldg2(const E *g) {
+        return cvt(__ldg(reinterpret_cast<const unsigned *>(g)));
+    }
+    __device__ static void st4(E *g, float4 v) {
+        *reinterpret_cast<uint2 *>(g) = make_uint2(pack(v.x, v.y), pack(v.z, v.w));
+    }
+    __device__ static void st2(E *g, float2 v) { *reinterpret_cast<unsigned *>(g) = pack(v.x, v.y); }
 };
 
 /* Launch geometry of the 2D kernels: CGT channel groups x TJ columns per
@@ -285,13 +328,15 @@ __global__ void __launch_bounds__(kThreads2d) k_conv2d_bwd(ConvDev p, Geo2d g) {
  * the strip downwards.  "Stage" m carries dy row rend+K-2-m and input row
  * rend-1-m, each R2B_TJ + 2(K-1) columns wide (the column halo, zero-filled
  * outside the grid); row r = rend-1-n needs stages n .. n+K-1.  Stages are
- * copied by cp.async (16-byte units) into a ring of r2b_nr<K>() shared
- * rows, R2B_PD stages ahead of the compute.  A thread's K x K windows live
+ * copied by cp.async (16-byte units) into a ring of r2b_nr<K, E>() shared
+ * rows, PD = r2b_pd<E>() stages ahead of the compute (R2B_PD for fp32
+ * activations, twice that for bf16 ones, whose rows carry half the bytes).
+ * A thread's K x K windows live
  * in registers indexed by stage % K (the row loop is unrolled by K, so no
  * window shifts) and only the new stage's K values per tensor come from
  * shared memory each row.  Rows n .. n+K-1 share one cp.async wait and one
  * barrier; a fast thread then issues stages n+PD .. n+PD+K-1 while a slow
- * one may still read stage n-1, so the ring holds R2B_PD + K + 1 rows.
+ * one may still read stage n-1, so the ring holds PD + K + 1 rows.
  *
  * Tuning, config 3 on one B200 (backward, % of the measured copy
  * bandwidth): float4 channels, 256 threads, 6 stages, 256-row strips and
@@ -314,38 +359,55 @@ using R2BVec = Vec4p;
 
 /* ring rows: a fast thread issues stages n+PD .. n+PD+K-1 of its row group
  * while a slow one may still read stage n-1 of the previous group */
-template <int K>
-__host__ __device__ constexpr int r2_nr() { return R2_PD + K + 1; }
+/* bf16 rows carry half the bytes: more stages keep the bytes in flight
+ * per SM up */
+#ifndef KMB_CONV_BF16_PD_MUL
+#define KMB_CONV_BF16_PD_MUL 2
+#endif
+template <typename E>
+__host__ __device__ constexpr int r2_pd() {
+    return sizeof(E) == 2 ? KMB_CONV_BF16_PD_MUL * R2_PD : R2_PD;
+}
+template <typename E>
+__host__ __device__ constexpr int r2b_pd() {
+    return sizeof(E) == 2 ? KMB_CONV_BF16_PD_MUL * R2B_PD : R2B_PD;
+}
+
+template <int K, typename E>
+__host__ __device__ constexpr int r2_nr() { return r2_pd<E>() + K + 1; }
 
 template <int K>
 __host__ __device__ constexpr int r2b_ws() { return R2B_TJ + 2 * (K - 1); }
 
-template <int K>
-__host__ __device__ constexpr int r2b_nr() { return R2B_PD + K + 1; }
+template <int K, typename E>
+__host__ __device__ constexpr int r2b_nr() { return r2b_pd<E>() + K + 1; }
 
-template <int K>
+template <int K, typename E>
 __host__ __device__ constexpr size_t r2_smem_bytes() {
     /* two rings of r2b_nr rows of 64 channels; the final fold reuses them */
-    const size_t ring = 2ull * r2b_nr<K>() * r2b_ws<K>() * 64 * 4;
+    const size_t ring = 2ull * r2b_nr<K, E>() * r2b_ws<K>() * 64 * sizeof(E);
     const size_t fold = (size_t)R2B_NT * (K * K + 1) * R2B_CW * 4;
     return ring > fold ? ring : fold;
 }
 
-template <int K>
+template <int K, typename E>
 __global__ void __launch_bounds__(R2B_NT, 1) k_conv2d_bwd_ring(ConvDev p, long ctiles,
                                                                long jtiles, long strips) {
     using V = R2BVec;
     using T = typename V::T;
     constexpr int CW = R2B_CW, CG = R2B_CG, TJ = R2B_TJ, NT = R2B_NT;
     constexpr int WS = r2b_ws<K>();
-    constexpr int NR = r2b_nr<K>();
-    constexpr int ROWF = WS * 64; /* floats per ring row */
+    constexpr int NR = r2b_nr<K, E>();
+    constexpr int PD = r2b_pd<E>();
+    constexpr int ROWF = WS * 64;                    /* elements per ring row */
     constexpr int NACC = K * K + 1;
-    constexpr int UNITS = WS * 16;                   /* 16-byte copies per row */
+    constexpr int EPU = 16 / (int)sizeof(E);         /* elements per 16-byte copy */
+    constexpr int UPC = 64 / EPU;                    /* copies per column */
+    constexpr int UNITS = WS * UPC;                  /* 16-byte copies per row */
     constexpr int CPT = (UNITS + NT - 1) / NT;       /* copies per thread */
     extern __shared__ __align__(16) float sm[];
-    float *ring_g = sm;             /* dy rows   [NR][WS][64] */
-    float *ring_i = sm + NR * ROWF; /* input rows */
+    E *ring_g = reinterpret_cast<E *>(sm); /* dy rows   [NR][WS][64] */
+    E *ring_i = ring_g + NR * ROWF;        /* input rows */
 
     const int tid = threadIdx.x;
     const int cg = tid % CG;
@@ -363,34 +425,34 @@ __global__ void __launch_bounds__(R2B_NT, 1) k_conv2d_bwd_ring(ConvDev p, long c
     const int nstage = cnt + K - 1;
     const long jlo = j0 - (K - 1);
     const bool act = j < W;
-    const float *gbase = p.dy + b * H * W * D + c0;
-    const float *ibase = p.in + b * H * W * D + c0;
+    const E *gbase = reinterpret_cast<const E *>(p.dy) + b * H * W * D + c0;
+    const E *ibase = reinterpret_cast<const E *>(p.in) + b * H * W * D + c0;
 
     /* this thread's copies of a stage: unit e = tid + c * NT of a row
-     * (column jlo + e / 16, channels 4 (e % 16) ..); only the row moves */
+     * (column jlo + e / UPC, channels EPU (e % UPC) ..); only the row moves */
     long coff[CPT];
     bool cok[CPT];
 #pragma unroll
     for (int c = 0; c < CPT; ++c) {
         const int e = tid + c * NT;
-        const long col = jlo + e / 16;
+        const long col = jlo + e / UPC;
         cok[c] = e < UNITS && col >= 0 && col < W;
-        coff[c] = col * D + (e % 16) * 4;
+        coff[c] = col * D + (e % UPC) * EPU;
     }
     const long rowst = W * D;
     auto issue = [&](int m) {
         if (m < nstage) {
             const int slot = m % NR;
             const long rg = rend + K - 2 - m, ri = rend - 1 - m;
-            float *dg = ring_g + slot * ROWF + tid * 4, *di = ring_i + slot * ROWF + tid * 4;
-            const float *sg = gbase + rg * rowst, *si = ibase + ri * rowst;
+            E *dg = ring_g + slot * ROWF + tid * EPU, *di = ring_i + slot * ROWF + tid * EPU;
+            const E *sg = gbase + rg * rowst, *si = ibase + ri * rowst;
 #pragma unroll
             for (int c = 0; c < CPT; ++c) {
                 if (UNITS % NT == 0 || tid + c * NT < UNITS) {
                     const bool gok = cok[c] && rg < H;
                     const bool iok = cok[c] && ri >= 0;
-                    kmb_cp_async16(dg + c * NT * 4, gok ? sg + coff[c] : gbase, gok ? 16 : 0);
-                    kmb_cp_async16(di + c * NT * 4, iok ? si + coff[c] : ibase, iok ? 16 : 0);
+                    kmb_cp_async16(dg + c * NT * EPU, gok ? sg + coff[c] : gbase, gok ? 16 : 0);
+                    kmb_cp_async16(di + c * NT * EPU, iok ? si + coff[c] : ibase, iok ? 16 : 0);
                 }
             }
         }
@@ -409,24 +471,24 @@ __global__ void __launch_bounds__(R2B_NT, 1) k_conv2d_bwd_ring(ConvDev p, long c
      * (columns j-K+1 .. j) of this thread */
     auto fetch = [&](int m, T (&g)[K], T (&iv)[K]) {
         const int slot = m % NR;
-        const float *sg = ring_g + slot * ROWF + jj * 64 + cg * CW;
-        const float *si = ring_i + slot * ROWF + jj * 64 + cg * CW;
+        const E *sg = ring_g + slot * ROWF + jj * 64 + cg * CW;
+        const E *si = ring_i + slot * ROWF + jj * 64 + cg * CW;
 #pragma unroll
         for (int q = 0; q < K; ++q) {
-            g[q] = *reinterpret_cast<const T *>(sg + (K - 1 + q) * 64);
-            iv[q] = *reinterpret_cast<const T *>(si + q * 64);
+            g[q] = CIO<E>::ld4(sg + (K - 1 + q) * 64);
+            iv[q] = CIO<E>::ld4(si + q * 64);
         }
     };
 
 #pragma unroll 1
-    for (int m = 0; m < R2B_PD; ++m) issue(m);
+    for (int m = 0; m < PD; ++m) issue(m);
     /* stages 0 .. K-2 into the register windows */
-    kmb_cp_async_wait<R2B_PD - (K - 1)>();
+    kmb_cp_async_wait<PD - (K - 1)>();
     __syncthreads();
 #pragma unroll
     for (int m = 0; m < K - 1; ++m) fetch(m, gw[m % K], iw[m % K]);
 
-    float *dbase = p.din + b * H * W * D + c0 + cg * CW;
+    E *dbase = reinterpret_cast<E *>(p.din) + b * H * W * D + c0 + cg * CW;
     /* one row at compile-time phase PH = n % K (its stages are resident) */
     auto row = [&](int n, auto ph_tag) {
         constexpr int PH = decltype(ph_tag)::value;
@@ -442,7 +504,7 @@ __global__ void __launch_bounds__(R2B_NT, 1) k_conv2d_bwd_ring(ConvDev p, long c
 #pragma unroll
                 for (int k1 = 0; k1 < K; ++k1)
                     s = V::fma(gw[(PH + k0) % K][K - 1 - k1], wk[k0 * K + k1], s);
-            V::store(dbase + (r * W + j) * D, s);
+            CIO<E>::st4(dbase + (r * W + j) * D, s);
             /* dkernel: dy(r, j) (stage n+K-1, column 0) times input
              * (r - (K-1) + k0, j - (K-1) + k1) (stage n + K-1-k0) */
             const T gy = gw[NEW][0];
@@ -458,8 +520,8 @@ __global__ void __launch_bounds__(R2B_NT, 1) k_conv2d_bwd_ring(ConvDev p, long c
      * n+K-1 .. n+2K-2, and stages n+PD .. n+PD+K-1 go out first */
     for (int n = 0; n < cnt; n += K) {
 #pragma unroll
-        for (int i = 0; i < K; ++i) issue(n + R2B_PD + i);
-        kmb_cp_async_wait<R2B_PD - K + 1>();
+        for (int i = 0; i < K; ++i) issue(n + PD + i);
+        kmb_cp_async_wait<PD - K + 1>();
         __syncthreads();
         row(n, std::integral_constant<int, 0>{});
         if (K > 1 && n + 1 < cnt) row(n + 1, std::integral_constant<int, 1 % K>{});
@@ -488,13 +550,13 @@ __global__ void __launch_bounds__(R2B_NT, 1) k_conv2d_bwd_ring(ConvDev p, long c
     }
 }
 
-template <int K>
+template <int K, typename E>
 cudaError_t launch2d_bwd_ring(const ConvDev &p, cudaStream_t s) {
     const long ctiles = p.D / 64;
     const long jtiles = (p.dims[1] + R2B_TJ - 1) / R2B_TJ;
     const long strips = (p.dims[0] + R2B_TI - 1) / R2B_TI;
-    const size_t smem = r2_smem_bytes<K>();
-    auto kern = k_conv2d_bwd_ring<K>;
+    const size_t smem = r2_smem_bytes<K, E>();
+    auto kern = k_conv2d_bwd_ring<K, E>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return e;
@@ -511,19 +573,24 @@ cudaError_t launch2d_bwd_ring(const ConvDev &p, cudaStream_t s) {
 template <int K>
 __host__ __device__ constexpr int r2f_ws() { return R2_TJ + K - 1; }
 
-template <int K>
+template <int K, typename E>
 __host__ __device__ constexpr size_t r2f_smem_bytes() {
-    return (size_t)r2_nr<K>() * r2f_ws<K>() * R2_CG * 16;
+    return (size_t)r2_nr<K, E>() * r2f_ws<K>() * R2_CG * 4 * sizeof(E);
 }
 
-template <int K, class V>
+template <int K, class V, typename E>
 __global__ void __launch_bounds__(kThreads2d) k_conv2d_fwd_ring(ConvDev p, long ctiles) {
     using T = float4;
     constexpr int WS = r2f_ws<K>();
-    constexpr int NR = r2_nr<K>();
-    constexpr int ROWF = WS * R2_CG * 4;
-    constexpr int CPT = (WS * R2_CG + kThreads2d - 1) / kThreads2d;
-    extern __shared__ __align__(16) float sm[];
+    constexpr int NR = r2_nr<K, E>();
+    constexpr int PD = r2_pd<E>();
+    constexpr int ROWF = WS * R2_CG * 4;             /* elements per ring row */
+    constexpr int EPU = 16 / (int)sizeof(E);         /* elements per 16-byte copy */
+    constexpr int UPC = R2_CG * 4 / EPU;             /* copies per column */
+    constexpr int UNITS = WS * UPC;
+    constexpr int CPT = (UNITS + kThreads2d - 1) / kThreads2d;
+    extern __shared__ __align__(16) float smf[];
+    E *sm = reinterpret_cast<E *>(smf);
 
     const int tid = threadIdx.x;
     const int cg = tid % R2_CG;
@@ -541,28 +608,28 @@ __global__ void __launch_bounds__(kThreads2d) k_conv2d_fwd_ring(ConvDev p, long 
     const int nstage = cnt + K - 1;
     const long jlo = j0 - (K - 1);
     const bool act = j < W;
-    const float *ibase = p.in + b * H * W * D + c0;
+    const E *ibase = reinterpret_cast<const E *>(p.in) + b * H * W * D + c0;
 
     long coff[CPT];
     bool cok[CPT];
 #pragma unroll
     for (int c = 0; c < CPT; ++c) {
         const int e = tid + c * kThreads2d;
-        const long col = jlo + e / R2_CG;
-        cok[c] = e < WS * R2_CG && col >= 0 && col < W;
-        coff[c] = col * D + (e % R2_CG) * 4;
+        const long col = jlo + e / UPC;
+        cok[c] = e < UNITS && col >= 0 && col < W;
+        coff[c] = col * D + (e % UPC) * EPU;
     }
     const long rowst = W * D;
     auto issue = [&](int m) {
         if (m < nstage) {
             const long ri = r0 - (K - 1) + m;
-            float *di = sm + (m % NR) * ROWF + tid * 4;
-            const float *si = ibase + ri * rowst;
+            E *di = sm + (m % NR) * ROWF + tid * EPU;
+            const E *si = ibase + ri * rowst;
 #pragma unroll
             for (int c = 0; c < CPT; ++c) {
-                if (tid + c * kThreads2d < WS * R2_CG) {
+                if (tid + c * kThreads2d < UNITS) {
                     const bool ok = cok[c] && ri >= 0;
-                    kmb_cp_async16(di + c * kThreads2d * 4, ok ? si + coff[c] : ibase,
+                    kmb_cp_async16(di + c * kThreads2d * EPU, ok ? si + coff[c] : ibase,
                                    ok ? 16 : 0);
                 }
             }
@@ -576,19 +643,19 @@ __global__ void __launch_bounds__(kThreads2d) k_conv2d_fwd_ring(ConvDev p, long 
     const T bias = p.bias ? V::load(p.bias + c0 + cg * 4) : V::zero();
     T iw[K][K]; /* [stage % K][column] */
     auto fetch = [&](int m, T (&iv)[K]) {
-        const float *si = sm + (m % NR) * ROWF + (jj * R2_CG + cg) * 4;
+        const E *si = sm + (m % NR) * ROWF + (jj * R2_CG + cg) * 4;
 #pragma unroll
-        for (int q = 0; q < K; ++q) iv[q] = *reinterpret_cast<const T *>(si + q * R2_CG * 4);
+        for (int q = 0; q < K; ++q) iv[q] = CIO<E>::ld4(si + q * R2_CG * 4);
     };
 
 #pragma unroll 1
-    for (int m = 0; m < R2_PD; ++m) issue(m);
-    kmb_cp_async_wait<R2_PD - (K - 1)>();
+    for (int m = 0; m < PD; ++m) issue(m);
+    kmb_cp_async_wait<PD - (K - 1)>();
     __syncthreads();
 #pragma unroll
     for (int m = 0; m < K - 1; ++m) fetch(m, iw[m % K]);
 
-    float *obase = p.out + b * H * W * D + c0 + cg * 4;
+    E *obase = reinterpret_cast<E *>(p.out) + b * H * W * D + c0 + cg * 4;
     auto row = [&](int n, auto ph_tag) {
         constexpr int PH = decltype(ph_tag)::value;
         fetch(n + K - 1, iw[(PH + K - 1) % K]);
@@ -599,13 +666,13 @@ __global__ void __launch_bounds__(kThreads2d) k_conv2d_fwd_ring(ConvDev p, long 
 #pragma unroll
                 for (int k1 = 0; k1 < K; ++k1)
                     s = V::fma(iw[(PH + k0) % K][k1], wk[k0 * K + k1], s);
-            V::store(obase + ((r0 + n) * W + j) * D, s);
+            CIO<E>::st4(obase + ((r0 + n) * W + j) * D, s);
         }
     };
     for (int n = 0; n < cnt; n += K) {
 #pragma unroll
-        for (int i = 0; i < K; ++i) issue(n + R2_PD + i);
-        kmb_cp_async_wait<R2_PD - K + 1>();
+        for (int i = 0; i < K; ++i) issue(n + PD + i);
+        kmb_cp_async_wait<PD - K + 1>();
         __syncthreads();
         row(n, std::integral_constant<int, 0>{});
         if (K > 1 && n + 1 < cnt) row(n + 1, std::integral_constant<int, 1 % K>{});
@@ -614,13 +681,13 @@ __global__ void __launch_bounds__(kThreads2d) k_conv2d_fwd_ring(ConvDev p, long 
     kmb_cp_async_wait<0>();
 }
 
-template <int K>
+template <int K, typename E>
 cudaError_t launch2d_fwd_ring(const ConvDev &p, cudaStream_t s) {
     const long ctiles = p.D / (4 * R2_CG);
     const long jtiles = (p.dims[1] + R2_TJ - 1) / R2_TJ;
     const long strips = (p.dims[0] + R2_TI - 1) / R2_TI;
-    const size_t smem = r2f_smem_bytes<K>();
-    auto kern = k_conv2d_fwd_ring<K, Vec<4>>;
+    const size_t smem = r2f_smem_bytes<K, E>();
+    auto kern = k_conv2d_fwd_ring<K, Vec4p, E>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return e;
@@ -633,20 +700,22 @@ cudaError_t launch2d_fwd_ring(const ConvDev &p, cudaStream_t s) {
  * the register file without spills up to K = 3 */
 constexpr int R2_KMAX = 3;
 
+template <typename E>
 cudaError_t dispatch2d_fwd_ring(const ConvDev &p, cudaStream_t s) {
     switch (p.K) {
-    case 1: return launch2d_fwd_ring<1>(p, s);
-    case 2: return launch2d_fwd_ring<2>(p, s);
-    case 3: return launch2d_fwd_ring<3>(p, s);
+    case 1: return launch2d_fwd_ring<1, E>(p, s);
+    case 2: return launch2d_fwd_ring<2, E>(p, s);
+    case 3: return launch2d_fwd_ring<3, E>(p, s);
     default: return cudaErrorNotSupported;
     }
 }
 
+template <typename E>
 cudaError_t dispatch2d_bwd_ring(const ConvDev &p, cudaStream_t s) {
     switch (p.K) {
-    case 1: return launch2d_bwd_ring<1>(p, s);
-    case 2: return launch2d_bwd_ring<2>(p, s);
-    case 3: return launch2d_bwd_ring<3>(p, s);
+    case 1: return launch2d_bwd_ring<1, E>(p, s);
+    case 2: return launch2d_bwd_ring<2, E>(p, s);
+    case 3: return launch2d_bwd_ring<3, E>(p, s);
     default: return cudaErrorNotSupported;
     }
 }
@@ -723,44 +792,47 @@ __device__ __forceinline__ float2 ld2(const float *a) {
     return __ldg(reinterpret_cast<const float2 *>(a));
 }
 
-template <int K>
+template <int K, typename E>
 struct ZSLayout {
     static constexpr int CY = Z3_TY + K - 1, CX = Z3_TX + K - 1; /* staged columns */
     static constexpr int NCOL = CY * CX;
-    static constexpr int SL = NCOL * Z3_CH;            /* floats of a staged input slice */
-    static constexpr int SLD = Z3_TY * Z3_TX * Z3_CH;  /* floats of a dy slice (dkernel) */
-    static constexpr int NJ = (NCOL * (Z3_CH / 4) + Z3_THREADS - 1) / Z3_THREADS; /* chunks a thread */
+    static constexpr int EPU = 16 / (int)sizeof(E);    /* elements per 16-byte chunk */
+    static constexpr int UPC = Z3_CH / EPU;            /* chunks per column */
+    static constexpr int SL = NCOL * Z3_CH;            /* elements of a staged input slice */
+    static constexpr int SLD = Z3_TY * Z3_TX * Z3_CH;  /* elements of a dy slice (dkernel) */
+    static constexpr int NJ = (NCOL * UPC + Z3_THREADS - 1) / Z3_THREADS; /* chunks a thread */
     static constexpr int NV = Z3_PX + K - 1;           /* neighbour columns of a warp per row */
-    static_assert(Z3_TY * Z3_TX * (Z3_CH / 4) <= Z3_THREADS, "one dy chunk a thread");
+    static constexpr int DYJ = Z3_TY * Z3_TX * UPC;    /* dy chunks of a slice (dkernel) */
+    static_assert(DYJ <= Z3_THREADS, "at most one dy chunk a thread");
 };
 
 /* the 16-byte chunk jobs of a thread for one staged slice: element offset
  * of slice 0 (or -1 when the column or the channels are outside) and the
  * offset in the slot */
-template <int K, int SGN>
+template <int K, int SGN, typename E>
 struct ZSJobs {
-    long src[ZSLayout<K>::NJ];
-    int dst[ZSLayout<K>::NJ];
+    using L = ZSLayout<K, E>;
+    long src[L::NJ];
+    int dst[L::NJ];
     __device__ __forceinline__ void init(const ConvDev &p, int y0, int x0, long c0, int tid) {
-        using L = ZSLayout<K>;
         const int Y = (int)p.dims[1], X = (int)p.dims[2];
 #pragma unroll
         for (int i = 0; i < L::NJ; ++i) {
             const int e = tid + i * Z3_THREADS;
-            const int col = e / (Z3_CH / 4), ch = e % (Z3_CH / 4);
+            const int col = e / L::UPC, ch = e % L::UPC;
             const int cy = col / L::CX, cx = col % L::CX;
             const int y = SGN < 0 ? y0 - (K - 1) + cy : y0 + cy;
             const int x = SGN < 0 ? x0 - (K - 1) + cx : x0 + cx;
-            const long c = c0 + ch * 4;
-            const bool ok = e < L::NCOL * (Z3_CH / 4) && y >= 0 && y < Y && x >= 0 && x < X &&
+            const long c = c0 + ch * L::EPU;
+            const bool ok = e < L::NCOL * L::UPC && y >= 0 && y < Y && x >= 0 && x < X &&
                             c < p.D;
             src[i] = ok ? (long)blockIdx.z * p.P * p.D + ((long)y * X + x) * p.D + c : -1;
-            dst[i] = e < L::NCOL * (Z3_CH / 4) ? col * Z3_CH + ch * 4 : -1;
+            dst[i] = e < L::NCOL * L::UPC ? col * Z3_CH + ch * L::EPU : -1;
         }
     }
-    __device__ __forceinline__ void issue(float *slot, const float *base, long zoff) const {
+    __device__ __forceinline__ void issue(E *slot, const E *base, long zoff) const {
 #pragma unroll
-        for (int i = 0; i < ZSLayout<K>::NJ; ++i)
+        for (int i = 0; i < L::NJ; ++i)
             if (dst[i] >= 0)
                 kmb_cp_async16(slot + dst[i], base + (src[i] >= 0 ? src[i] + zoff : 0),
                                src[i] >= 0 ? 16 : 0);
@@ -768,11 +840,12 @@ struct ZSJobs {
 };
 
 /* SGN = -1: forward (z ascending); SGN = +1: dinput (z descending) */
-template <int K, int SGN>
+template <int K, int SGN, typename E>
 __global__ void __launch_bounds__(Z3_THREADS, 1) k_conv3d_zring(ConvDev p) {
-    using L = ZSLayout<K>;
+    using L = ZSLayout<K, E>;
     constexpr int KK = K * K, KV = K * KK, NV = L::NV;
-    extern __shared__ __align__(16) float zsm[];
+    extern __shared__ __align__(16) float zsmf[];
+    E *zsm = reinterpret_cast<E *>(zsmf);
     const int tid = threadIdx.x, lane = tid & 31;
     const Tile3 t = tile3(p);
     const long c0 = (long)blockIdx.x * Z3_CH;
@@ -780,10 +853,10 @@ __global__ void __launch_bounds__(Z3_THREADS, 1) k_conv3d_zring(ConvDev p) {
     float2 wt[KV];
 #pragma unroll
     for (int k = 0; k < KV; ++k) wt[k] = cok ? ld2(p.ker + k * p.D + t.c) : kmb_f2s(0.f);
-    ZSJobs<K, SGN> jobs;
+    ZSJobs<K, SGN, E> jobs;
     jobs.init(p, t.y0, t.x0, c0, tid);
-    const float *src = SGN < 0 ? p.in : p.dy;
-    float *dst = SGN < 0 ? p.out : p.din;
+    const E *src = reinterpret_cast<const E *>(SGN < 0 ? p.in : p.dy);
+    E *dst = reinterpret_cast<E *>(SGN < 0 ? p.out : p.din);
     const float2 b2 = (SGN < 0 && p.bias && cok) ? ld2(p.bias + t.c) : kmb_f2s(0.f);
     float2 acc[Z3_PX][K];
 #pragma unroll
@@ -815,14 +888,14 @@ __global__ void __launch_bounds__(Z3_THREADS, 1) k_conv3d_zring(ConvDev p) {
             jobs.issue(zsm + ns * L::SL, src, zof(s + ZS_R - 1));
         }
         kmb_cp_async_commit();
-        const float *sl = zsm + slot * L::SL;
+        const E *sl = zsm + slot * L::SL;
         slot = slot + 1 == ZS_R ? 0 : slot + 1;
         float2 v[K][NV];
 #pragma unroll
         for (int oy = 0; oy < K; ++oy)
 #pragma unroll
             for (int i = 0; i < NV; ++i)
-                v[oy][i] = *reinterpret_cast<const float2 *>(sl + nb[oy] + i * Z3_CH);
+                v[oy][i] = CIO<E>::ld2(sl + nb[oy] + i * Z3_CH);
 #pragma unroll
         for (int u = 0; u < Z3_PX; ++u)
 #pragma unroll
@@ -836,7 +909,7 @@ __global__ void __launch_bounds__(Z3_THREADS, 1) k_conv3d_zring(ConvDev p) {
         const long zo = zof(s);
 #pragma unroll
         for (int u = 0; u < Z3_PX; ++u) {
-            if (t.on[u]) *reinterpret_cast<float2 *>(dst + t.base[u] + zo) = acc[u][0];
+            if (t.on[u]) CIO<E>::st2(dst + t.base[u] + zo, acc[u][0]);
 #pragma unroll
             for (int i = 0; i + 1 < K; ++i) acc[u][i] = acc[u][i + 1];
             acc[u][K - 1] = b2;
@@ -844,32 +917,36 @@ __global__ void __launch_bounds__(Z3_THREADS, 1) k_conv3d_zring(ConvDev p) {
     }
 }
 
-template <int K>
+template <int K, typename E>
 __global__ void __launch_bounds__(Z3_THREADS, 1) k_conv3d_zring_param(ConvDev p) {
-    using L = ZSLayout<K>;
+    using L = ZSLayout<K, E>;
     constexpr int KK = K * K, KV = K * KK, NV = L::NV;
     constexpr int SLOT = L::SL + L::SLD;
-    extern __shared__ __align__(16) float zsm[];
+    extern __shared__ __align__(16) float zsmf[];
+    E *zsm = reinterpret_cast<E *>(zsmf);
     __shared__ float2 red[Z3_THREADS / 32][32];
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const Tile3 t = tile3(p);
     const long c0 = (long)blockIdx.x * Z3_CH;
-    ZSJobs<K, -1> jobs;
+    ZSJobs<K, -1, E> jobs;
     jobs.init(p, t.y0, t.x0, c0, tid);
-    /* dy of the CTA's own columns: one 16-byte chunk a thread */
-    const int dcol = tid / (Z3_CH / 4), dch = tid % (Z3_CH / 4);
+    const E *in = reinterpret_cast<const E *>(p.in), *dy = reinterpret_cast<const E *>(p.dy);
+    /* dy of the CTA's own columns: at most one 16-byte chunk a thread */
+    const bool djob = tid < L::DYJ;
+    const int dcol = tid / L::UPC, dch = tid % L::UPC;
     const int dyy = t.y0 + dcol / Z3_TX, dxx = t.x0 + dcol % Z3_TX;
-    const bool dok = dyy < t.Y && dxx < t.X && c0 + dch * 4 < p.D;
+    const bool dok = djob && dyy < t.Y && dxx < t.X && c0 + dch * L::EPU < p.D;
     const long dsrc = dok ? (long)blockIdx.z * p.P * p.D + ((long)dyy * t.X + dxx) * p.D + c0 +
-                                dch * 4
+                                dch * L::EPU
                           : 0;
-    const int ddst = L::SL + dcol * Z3_CH + dch * 4;
+    const int ddst = L::SL + dcol * Z3_CH + dch * L::EPU;
     auto issue = [&](int s) { /* input slice s and dy slice s + K - 1 */
-        float *slot = zsm + (s % ZS_R) * SLOT;
-        jobs.issue(slot, p.in, (long)s * t.sz);
+        E *slot = zsm + (s % ZS_R) * SLOT;
+        jobs.issue(slot, in, (long)s * t.sz);
         const bool ok = dok && s + K - 1 < t.Z;
-        kmb_cp_async16(slot + ddst, p.dy + (ok ? dsrc + (long)(s + K - 1) * t.sz : 0),
-                       ok ? 16 : 0);
+        if (djob)
+            kmb_cp_async16(slot + ddst, dy + (ok ? dsrc + (long)(s + K - 1) * t.sz : 0),
+                           ok ? 16 : 0);
     };
 #pragma unroll 1
     for (int s = 0; s < ZS_R - 1; ++s) {
@@ -890,7 +967,7 @@ __global__ void __launch_bounds__(Z3_THREADS, 1) k_conv3d_zring_param(ConvDev p)
     for (int u = 0; u < Z3_PX; ++u)
 #pragma unroll
         for (int i = 0; i + 1 < K; ++i)
-            dyw[u][i] = t.on[u] && i < t.Z ? ld2(p.dy + t.base[u] + (long)i * t.sz)
+            dyw[u][i] = t.on[u] && i < t.Z ? CIO<E>::ldg2(dy + t.base[u] + (long)i * t.sz)
                                            : kmb_f2s(0.f);
 #pragma unroll 1
     for (int s = 0; s < t.Z; ++s) {
@@ -898,16 +975,14 @@ __global__ void __launch_bounds__(Z3_THREADS, 1) k_conv3d_zring_param(ConvDev p)
         __syncthreads();
         if (s + ZS_R - 1 < t.Z) issue(s + ZS_R - 1);
         kmb_cp_async_commit();
-        const float *sl = zsm + (s % ZS_R) * SLOT;
+        const E *sl = zsm + (s % ZS_R) * SLOT;
 #pragma unroll
-        for (int u = 0; u < Z3_PX; ++u)
-            dyw[u][K - 1] = *reinterpret_cast<const float2 *>(sl + dme + u * Z3_CH);
+        for (int u = 0; u < Z3_PX; ++u) dyw[u][K - 1] = CIO<E>::ld2(sl + dme + u * Z3_CH);
         float2 v[K][NV];
 #pragma unroll
         for (int oy = 0; oy < K; ++oy)
 #pragma unroll
-            for (int i = 0; i < NV; ++i)
-                v[oy][i] = *reinterpret_cast<const float2 *>(sl + nb[oy] + i * Z3_CH);
+            for (int i = 0; i < NV; ++i) v[oy][i] = CIO<E>::ld2(sl + nb[oy] + i * Z3_CH);
 #pragma unroll
         for (int u = 0; u < Z3_PX; ++u) {
 #pragma unroll
@@ -948,40 +1023,41 @@ __global__ void __launch_bounds__(Z3_THREADS, 1) k_conv3d_zring_param(ConvDev p)
     }
 }
 
-template <int K>
+template <int K, typename E>
 cudaError_t launch3d_zring(const ConvDev &p, bool bwd, cudaStream_t s) {
-    using L = ZSLayout<K>;
+    using L = ZSLayout<K, E>;
     const unsigned tiles = (unsigned)(((p.dims[1] + Z3_TY - 1) / Z3_TY) *
                                       ((p.dims[2] + Z3_TX - 1) / Z3_TX));
     dim3 grid((unsigned)((p.D + Z3_CH - 1) / Z3_CH), tiles, (unsigned)p.batch);
-    const size_t sm1 = sizeof(float) * ZS_R * L::SL;
-    const size_t sm2 = sizeof(float) * ZS_R * (L::SL + L::SLD);
+    const size_t sm1 = sizeof(E) * ZS_R * L::SL;
+    const size_t sm2 = sizeof(E) * ZS_R * (L::SL + L::SLD);
     cudaError_t e;
     if (!bwd) {
-        e = cudaFuncSetAttribute(k_conv3d_zring<K, -1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)sm1);
+        auto fk = k_conv3d_zring<K, -1, E>;
+        e = cudaFuncSetAttribute(fk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1);
         if (e != cudaSuccess) return e;
-        k_conv3d_zring<K, -1><<<grid, Z3_THREADS, sm1, s>>>(p);
+        fk<<<grid, Z3_THREADS, sm1, s>>>(p);
         return cudaGetLastError();
     }
-    e = cudaFuncSetAttribute(k_conv3d_zring<K, +1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)sm1);
+    auto bk = k_conv3d_zring<K, +1, E>;
+    e = cudaFuncSetAttribute(bk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1);
     if (e != cudaSuccess) return e;
-    k_conv3d_zring<K, +1><<<grid, Z3_THREADS, sm1, s>>>(p);
+    bk<<<grid, Z3_THREADS, sm1, s>>>(p);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(k_conv3d_zring_param<K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)sm2);
+    auto pk = k_conv3d_zring_param<K, E>;
+    e = cudaFuncSetAttribute(pk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2);
     if (e != cudaSuccess) return e;
-    k_conv3d_zring_param<K><<<grid, Z3_THREADS, sm2, s>>>(p);
+    pk<<<grid, Z3_THREADS, sm2, s>>>(p);
     return cudaGetLastError();
 }
 
+template <typename E>
 cudaError_t dispatch3d(const ConvDev &p, bool bwd, cudaStream_t s) {
     switch (p.K) {
-    case 1: return launch3d_zring<1>(p, bwd, s);
-    case 2: return launch3d_zring<2>(p, bwd, s);
-    case 3: return launch3d_zring<3>(p, bwd, s);
+    case 1: return launch3d_zring<1, E>(p, bwd, s);
+    case 2: return launch3d_zring<2, E>(p, bwd, s);
+    case 3: return launch3d_zring<3, E>(p, bwd, s);
     default: return cudaErrorNotSupported;
     }
 }
@@ -1177,11 +1253,11 @@ extern "C" int kmb_launch_convnd_fwd(const KmbConvND *a, cudaStream_t s) {
     cudaError_t e;
     if (use_2d(p)) {
         if (aligned4(a, false) && p.D % (4 * R2_CG) == 0 && p.K <= R2_KMAX)
-            e = dispatch2d_fwd_ring(p, s);
+            e = dispatch2d_fwd_ring<float>(p, s);
         else
             e = aligned4(a, false) ? dispatch2d<4>(p, false, s) : dispatch2d<1>(p, false, s);
     } else if (use_3d(p) && aligned4(a, false) && p.P * p.D < (1L << 31)) {
-        e = dispatch3d(p, false, s);
+        e = dispatch3d<float>(p, false, s);
     } else {
         k_convnd_fwd_generic<<<grid_for(p.batch * p.P * p.D, 256), 256, 0, s>>>(p);
         e = cudaGetLastError();
@@ -1198,10 +1274,10 @@ extern "C" int kmb_launch_convnd_bwd(const KmbConvND *a, cudaStream_t s) {
     if (e != cudaSuccess) return kmb_cuda_fail(e, "convnd backward memset");
     if (use_2d(p)) {
         if (aligned4(a, true) && p.D % (4 * R2_CG) == 0 && p.K <= R2_KMAX)
-            e = dispatch2d_bwd_ring(p, s);
+            e = dispatch2d_bwd_ring<float>(p, s);
         else e = aligned4(a, true) ? dispatch2d<4>(p, true, s) : dispatch2d<1>(p, true, s);
     } else if (use_3d(p) && aligned4(a, true) && p.P * p.D < (1L << 31)) {
-        e = dispatch3d(p, true, s);
+        e = dispatch3d<float>(p, true, s);
     } else {
         k_convnd_bwd_input_generic<<<grid_for(p.batch * p.P * p.D, 256), 256, 0, s>>>(p);
         e = cudaGetLastError();
@@ -1216,4 +1292,37 @@ extern "C" int kmb_launch_convnd_bwd(const KmbConvND *a, cudaStream_t s) {
     }
     if (e != cudaSuccess) return kmb_cuda_fail(e, "convnd backward launch");
     return KMB_OK;
+}
+
+/* bf16 activations (input, output, dy, dinput), fp32 taps, bias, dkernel
+ * and dbias: the streamed 2D kernels (D a multiple of 64) and the 3D
+ * kernels (D a multiple of 8), K <= 3, 16-byte aligned device tensors. */
+extern "C" int kmb_convnd_bf16_supported(const KmbConvND *a, int bwd) {
+    auto al = [](const void *q) { return q == nullptr || ((uintptr_t)q & 15u) == 0; };
+    if (a->K < 1 || a->K > 3 || !al(a->input) || !al(a->kernel) || !al(a->bias)) return 0;
+    if (bwd ? !(al(a->dy) && al(a->dinput)) : !al(a->output)) return 0;
+    long P = 1;
+    for (long i = 0; i < a->ndims; ++i) P *= a->dims[i];
+    if (a->ndims == 2) return a->D % 64 == 0; /* the streamed kernels' 64-channel tiles */
+    if (a->ndims == 3) return a->D % 8 == 0 && P * a->D < (1L << 31);
+    return 0;
+}
+
+extern "C" int kmb_launch_convnd_fwd_bf16(const KmbConvND *a, cudaStream_t s) {
+    ConvDev p;
+    make_dev(a, &p);
+    const cudaError_t e = p.nd == 2 ? dispatch2d_fwd_ring<__nv_bfloat16>(p, s)
+                                    : dispatch3d<__nv_bfloat16>(p, false, s);
+    return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "convnd bf16 forward launch");
+}
+
+extern "C" int kmb_launch_convnd_bwd_bf16(const KmbConvND *a, cudaStream_t s) {
+    ConvDev p;
+    make_dev(a, &p);
+    cudaError_t e = cudaMemsetAsync(a->dkernel, 0, sizeof(float) * p.KV * p.D, s);
+    if (e == cudaSuccess && a->dbias) e = cudaMemsetAsync(a->dbias, 0, sizeof(float) * p.D, s);
+    if (e != cudaSuccess) return kmb_cuda_fail(e, "convnd bf16 backward memset");
+    e = p.nd == 2 ? dispatch2d_bwd_ring<__nv_bfloat16>(p, s)
+                  : dispatch3d<__nv_bfloat16>(p, true, s);
+    return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "convnd bf16 backward launch");
 }

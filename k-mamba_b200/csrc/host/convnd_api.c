@@ -69,6 +69,30 @@ static int run(const KmbConvND *a, int bwd) {
 int kmb_convnd_fwd(const KmbConvND *a) { return run(a, 0); }
 int kmb_convnd_bwd(const KmbConvND *a) { return run(a, 1); }
 
+/* bf16 activations on device memory (include/kmamba_b200.h) */
+static int run_bf16(const KmbConvND *a, int bwd) {
+    KmbStage st;
+    int rc = validate(a, bwd);
+    if (rc) return rc;
+    if (!kmb_convnd_bf16_supported(a, bwd))
+        return kmb_fail(KMB_EUNSUPPORTED,
+                        "convnd bf16: needs 2D with D a multiple of 64 or 3D with D a multiple "
+                        "of 8, K <= 3 and 16-byte aligned tensors");
+    const void *fwd_ptrs[] = {a->input, a->kernel, a->bias, a->output};
+    const void *bwd_ptrs[] = {a->input, a->kernel, a->dy, a->dinput, a->dkernel, a->dbias};
+    const void *const *ptrs = bwd ? bwd_ptrs : fwd_ptrs;
+    const size_t n = bwd ? sizeof bwd_ptrs / sizeof *bwd_ptrs : sizeof fwd_ptrs / sizeof *fwd_ptrs;
+    for (size_t i = 0; i < n; ++i)
+        if (ptrs[i] && !kmb_is_device_ptr(ptrs[i]))
+            return kmb_fail(KMB_EINVAL, "convnd bf16: every tensor must be device memory");
+    kmb_stage_begin(&st);
+    rc = bwd ? kmb_launch_convnd_bwd_bf16(a, st.s) : kmb_launch_convnd_fwd_bf16(a, st.s);
+    return kmb_stage_finish(&st, rc);
+}
+
+int kmb_convnd_fwd_bf16(const KmbConvND *a) { return run_bf16(a, 0); }
+int kmb_convnd_bwd_bf16(const KmbConvND *a) { return run_bf16(a, 1); }
+
 /* Fills a one-item KmbConvND from the reference params. */
 static int from_params(const ConvNDParams *p, KmbConvND *a) {
     if (!p || !p->dims || p->ndims <= 0 || p->ndims > 8) return 0;

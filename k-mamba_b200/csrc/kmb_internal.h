@@ -48,6 +48,10 @@ int kmb_launch_scan1d_bwd_m1_shared(const float *x, const float *A,
 /* ConvND launchers (csrc/cuda/convnd.cu). */
 int kmb_launch_convnd_fwd(const KmbConvND *a, cudaStream_t s);
 int kmb_launch_convnd_bwd(const KmbConvND *a, cudaStream_t s);
+/* bf16 activations: shapes kmb_convnd_bf16_supported accepts */
+int kmb_convnd_bf16_supported(const KmbConvND *a, int bwd);
+int kmb_launch_convnd_fwd_bf16(const KmbConvND *a, cudaStream_t s);
+int kmb_launch_convnd_bwd_bf16(const KmbConvND *a, cudaStream_t s);
 
 /* ND scan launchers (csrc/cuda/scannd.cu).  Per-axis pointers so that
  * both the contiguous [ndims, P, D] delta of scan_nd.h and the separate

@@ -319,6 +319,8 @@ PROTOTYPES = {
     "om_convnd_backward": (C.c_int, [C.POINTER(ConvNDParams)]),
     "kmb_convnd_fwd": (C.c_int, [C.POINTER(KmbConvND)]),
     "kmb_convnd_bwd": (C.c_int, [C.POINTER(KmbConvND)]),
+    "kmb_convnd_fwd_bf16": (C.c_int, [C.POINTER(KmbConvND)]),
+    "kmb_convnd_bwd_bf16": (C.c_int, [C.POINTER(KmbConvND)]),
     # topology
     "wavefront_nd_validate_dims": (C.c_int, [fp, lg]),
     "wavefront_nd_total_points": (lg, [fp, lg]),
