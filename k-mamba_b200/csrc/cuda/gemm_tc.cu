@@ -14,6 +14,11 @@
  * bf16 (round to nearest even).
  *
  * CTA tile BM x BN x BK = 128 x BN x 64, STAGES shared-memory stages.
+ * Split-K: when the M x N tiles do not fill the GPU and K is long (the
+ * weight gradients: M x N = d x d, K = tokens), blockIdx.z takes a range of
+ * the k-blocks; every split adds its fp32 tile to C with vector atomics
+ * (split 0 also adds bias and residual; C is zeroed first unless the call
+ * accumulates).  Only fp32 C without activation splits.
  * Warp roles inside a CTA of 128 threads:
  *   warp 0, one elected lane: TMA producer (two 2D tensor-map loads per
  *                             stage, 128-byte swizzle, no multicast);
@@ -30,6 +35,7 @@
  * Tensor maps cover this GPU's own memory only (the caller's A and B).
  */
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <cuda.h>
@@ -128,6 +134,7 @@ struct GemmDev {
     const float *residual;
     long M, N, K, ldc, ldr;
     int c_bf16, act, accumulate;
+    int kb_per_split; /* k-blocks of one split (gridDim.z splits) */
 };
 
 __device__ __forceinline__ float silu(float v) { return v / (1.f + __expf(-v)); }
@@ -154,7 +161,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kBM;
-    const int nk = (int)((p.K + kBK - 1) / kBK);
+    const int nk_all = (int)((p.K + kBK - 1) / kBK);
+    const int kb0 = (int)blockIdx.z * p.kb_per_split; /* this split's first k-block */
+    const int nk = min(nk_all - kb0, p.kb_per_split);
+    const bool split = gridDim.z > 1;
+    const bool lead = blockIdx.z == 0; /* adds bias and residual */
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -187,7 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!mbar_wait(&empty[s], ph ^ 1u, abort)) break;
             issued = kb + 1;
             mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
-            const int k0 = kb * kBK;
+            const int k0 = (kb0 + kb) * kBK;
             if (AMN) {
                 tma_load_2d(sA + s * A_BYTES, &mapA, m0, k0, &full[s]);
                 tma_load_2d(sA + s * A_BYTES + kBK * 128, &mapA, m0 + 64, k0, &full[s]);
@@ -264,12 +275,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
             float t = __uint_as_float(r[j]);
-            if (p.bias && n + j < p.N) t += p.bias[n + j];
+            if (lead && p.bias && n + j < p.N) t += p.bias[n + j];
             if (p.act == 1) t = silu(t);
-            if (p.residual && n + j < p.N) t += p.residual[row * p.ldr + n + j];
+            if (lead && p.residual && n + j < p.N) t += p.residual[row * p.ldr + n + j];
             v[j] = t;
         }
         const bool full16 = n + 16 <= p.N;
+        if (split) { /* fp32 C: this split's share, added atomically */
+            float *c = reinterpret_cast<float *>(p.C) + row * p.ldc + n;
+            if (full16 && ((reinterpret_cast<uintptr_t>(c) & 15) == 0)) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    atomicAdd(reinterpret_cast<float4 *>(c) + j,
+                              make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
+            } else {
+                for (int j = 0; j < 16 && n + j < p.N; ++j) atomicAdd(c + j, v[j]);
+            }
+            continue;
+        }
         if (p.c_bf16) {
             __nv_bfloat16 *c = reinterpret_cast<__nv_bfloat16 *>(p.C) + row * p.ldc + n;
             if (full16 && !p.accumulate && ((reinterpret_cast<uintptr_t>(c) & 15) == 0)) {
@@ -363,6 +386,22 @@ int make_map(CUtensorMap *m, const void *base, long rows, long cols, long ld, in
     return KMB_OK;
 }
 
+/* Splits of K: enough CTAs for one wave of one per SM when the tiles alone
+ * leave SMs idle, at least 8 k-blocks (512 of K) a split; only fp32 C
+ * without activation (the splits are added atomically).  KMB_GEMM_SPLITK=0
+ * disables it. */
+int split_count(long tiles, long nk, const KmbGemm *g) {
+    static int enabled = -1;
+    if (enabled < 0) {
+        const char *e = getenv("KMB_GEMM_SPLITK");
+        enabled = !(e && e[0] == '0' && e[1] == 0);
+    }
+    if (!enabled || g->c_bf16 || g->act != 0 || tiles >= 148) return 1;
+    long sp = 148 / tiles;
+    if (sp > nk / 8) sp = nk / 8;
+    return sp > 1 ? (int)sp : 1;
+}
+
 template <int BN, int STAGES, bool AMN, bool BMN>
 int launch(const KmbGemm *g, cudaStream_t s) {
     CUtensorMap ma, mb;
@@ -385,7 +424,16 @@ int launch(const KmbGemm *g, cudaStream_t s) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return kmb_cuda_fail(e, "gemm: smem attribute");
-    dim3 grid((unsigned)((g->N + BN - 1) / BN), (unsigned)((g->M + kBM - 1) / kBM));
+    const long tiles = ((g->N + BN - 1) / BN) * ((g->M + kBM - 1) / kBM);
+    const long nk = (g->K + kBK - 1) / kBK;
+    const int splits = split_count(tiles, nk, g);
+    p.kb_per_split = (int)((nk + splits - 1) / splits);
+    const unsigned gz = (unsigned)((nk + p.kb_per_split - 1) / p.kb_per_split); /* no empty split */
+    if (gz > 1 && !g->accumulate) {
+        e = cudaMemset2DAsync(g->C, (size_t)g->ldc * 4, 0, (size_t)g->N * 4, (size_t)g->M, s);
+        if (e != cudaSuccess) return kmb_cuda_fail(e, "gemm: split-K zero fill");
+    }
+    dim3 grid((unsigned)((g->N + BN - 1) / BN), (unsigned)((g->M + kBM - 1) / kBM), gz);
     kern<<<grid, kThreads, smem, s>>>(ma, mb, p);
     e = cudaGetLastError();
     return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "gemm: launch");

@@ -127,3 +127,41 @@ def test_gemm_rejects_bad_layouts(lib, cuda):
     g.C = host.ctypes.data
     assert lib.kmb_gemm_bf16(C.byref(g)) == kb.KMB_EINVAL        # host C
     assert lib.kmb_gemm_check_error() == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 512, 16384), (136, 264, 8192), (128, 1024, 4096)])
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (True, True), (False, True)])
+def test_gemm_split_k(lib, cuda, M, N, K, a_mn, b_mn):
+    """Few M x N tiles and a long K (the weight-gradient shape d x d x
+    tokens): the k-blocks are split over CTAs whose fp32 tiles are added
+    atomically; bias and residual are added once, and an accumulating call
+    keeps C."""
+    A, B = problem(M + N + K, M, N, K)
+    exact = A.astype(np.float64) @ B.astype(np.float64).T
+    assert rel_err(run(lib, A, B, a_mn, b_mn), exact) <= TOL
+    rng = np.random.default_rng(K)
+    bias = rng.standard_normal(N).astype(np.float32)
+    res = rng.standard_normal((M, N)).astype(np.float32)
+    assert rel_err(run(lib, A, B, a_mn, b_mn, bias=bias, residual=res), exact + bias + res) <= TOL
+    c0 = rng.standard_normal((M, N)).astype(np.float32)
+    assert rel_err(run(lib, A, B, a_mn, b_mn, c_init=c0), exact + c0) <= TOL
+
+
+def test_gemm_split_k_padded_mn_major(lib, cuda):
+    """The dt-projection weight gradient of the ND model: A^T is [K, 40]
+    with 35 live columns (M = 35, lda = 40), B MN-major, K = tokens."""
+    import torch
+    M, N, K, lda = 35, 512, 8192, 40
+    A, B = problem(35, M, N, K)
+    at = np.zeros((K, lda), np.float32)
+    at[:, :M] = A.T
+    ta = torch.from_numpy(at).to(torch.bfloat16).cuda()
+    tb = torch.from_numpy(np.ascontiguousarray(B.T)).to(torch.bfloat16).cuda()
+    tc = torch.full((M, N), float("nan"), device="cuda")
+    g = kb.KmbGemm()
+    g.A, g.B, g.C = ta.data_ptr(), tb.data_ptr(), tc.data_ptr()
+    g.M, g.N, g.K, g.lda, g.ldb, g.ldc, g.ldr = M, N, K, lda, N, N, N
+    g.a_mn_major, g.b_mn_major = 1, 1
+    kb.check(lib, lib.kmb_gemm_bf16(C.byref(g)))
+    torch.cuda.synchronize()
+    assert rel_err(tc.cpu().numpy(), A.astype(np.float64) @ B.astype(np.float64).T) <= TOL
