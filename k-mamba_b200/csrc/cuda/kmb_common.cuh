@@ -78,6 +78,44 @@ __device__ __forceinline__ float2 kmb_exp2_decay2(float2 w) {
     return kmb_decay_fix2(w, kmb_ex2_2(w));
 }
 
+/*
+ * 2^w of both elements of a pair on the FMA pipe, without MUFU, so that a
+ * kernel can move part of its exponentials off the 16-per-clock MUFU unit.
+ *
+ * Range reduction (exact, base 2 needs no split constant): t = w + 1.5 * 2^23
+ * rounds w to the nearest integer n in t's low mantissa bits, n = t - 1.5 *
+ * 2^23 and f = w - n in [-1/2, 1/2] are both exact.  2^f is a degree-6
+ * polynomial with p(0) = 1 and p'(0) = ln 2 held fixed and the other
+ * coefficients fitted for minimax relative error on [-1/2, 1/2]
+ * (iteratively reweighted least squares on a dense grid): 3.0e-9 in real
+ * arithmetic, 6.7e-8 maximum and 1.5e-10 mean relative error in fp32
+ * Horner form, and a mean of -3e-11 on the weak-decay range |w| < 1/32,
+ * so a long-memory recurrence accumulates no bias (MUFU ex2: ~1.4e-7 with
+ * a negative mean).  2^n is then added to the exponent field: the low 9
+ * bits of 1.5 * 2^23's pattern are zero, so (bits(t) << 23) is n << 23.
+ *
+ * Valid for |w| <= 125 (a normal result); callers check that bound and
+ * redo the work with kmb_exp2_decay2 when it fails.  NaN inputs give a
+ * finite or NaN pattern, so callers must also reject non-finite w.
+ */
+__device__ __forceinline__ float2 kmb_exp2_fma2(float2 w) {
+    const float2 t = kmb_add2(w, kmb_f2s(12582912.0f));
+    const float2 n = kmb_add2(t, kmb_f2s(-12582912.0f));
+    const float2 f = kmb_fma2(n, kmb_f2s(-1.0f), w);
+    float2 p = kmb_fma2(kmb_f2s(1.532424212200567e-4f), f, kmb_f2s(1.339093898423016e-3f));
+    p = kmb_fma2(p, f, kmb_f2s(9.618517942726612e-3f));
+    p = kmb_fma2(p, f, kmb_f2s(5.550359562039375e-2f));
+    p = kmb_fma2(p, f, kmb_f2s(2.4022647738456726e-1f));
+    p = kmb_fma2(p, f, kmb_f2s(6.931471824645996e-1f));
+    p = kmb_fma2(p, f, kmb_f2s(1.0f));
+    return kmb_f2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                  __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
+}
+
+/* Largest |w| for which kmb_exp2_fma2 is used (its valid range, with a
+ * margin for the rounding of w = dt * A log2 e). */
+#define KMB_EXP2_FMA_MAX 125.0f
+
 /* Asynchronous global->shared copies (cp.async, sm_80+).  A source size
  * below the copy size zero-fills the remainder of the destination. */
 __device__ __forceinline__ void kmb_cp_async4(void *smem, const void *gmem,

@@ -51,6 +51,39 @@ constexpr int kCh = KMB_SCAN1D_CHUNK; /* backward chunk = checkpoint interval */
 constexpr int kBurnSteps = 256;
 constexpr float kBurnLog2 = -40.f;
 constexpr unsigned kFull = 0xffffffffu;
+/* State pairs per lane (of 2) whose decays the fast paths compute on the
+ * FMA pipe (kmb_exp2_fma2) instead of MUFU ex2.  Off: both kernels are
+ * bound by instruction issue, not by the 16-per-clock MUFU rate, and the
+ * FMA-pipe exponential issues more instructions (one pair of two per lane
+ * measured forward 0.503 -> 0.555 ms and backward 1.141 -> 1.206 ms at
+ * config 2).  Kept as a build option for issue-light variants. */
+#ifndef KMB_SEG_FMA_PAIRS_FWD
+#define KMB_SEG_FMA_PAIRS_FWD 0
+#endif
+#ifndef KMB_SEG_FMA_PAIRS_BWD
+#define KMB_SEG_FMA_PAIRS_BWD 0
+#endif
+constexpr int kFmaFwd = KMB_SEG_FMA_PAIRS_FWD, kFmaBwd = KMB_SEG_FMA_PAIRS_BWD;
+
+/* Largest |A log2 e| over the lane's FMA-pipe state pairs, or +inf when
+ * one of them is not finite (the range check then fails at once). */
+template <int NP>
+__device__ __forceinline__ float fma_pairs_amax(const float2 (&A2p)[2]) {
+    float m = 0.f;
+#pragma unroll
+    for (int jp = 2 - NP; jp < 2; ++jp) {
+        const float a = fabsf(A2p[jp].x), b = fabsf(A2p[jp].y);
+        m = (a <= 3.0e38f && b <= 3.0e38f) ? fmaxf(m, fmaxf(a, b)) : __int_as_float(0x7f800000);
+    }
+    return m;
+}
+
+/* The decays of pair jp: FMA pipe for the last NP pairs, else MUFU ex2 with
+ * the weak-decay polynomial. */
+template <int NP>
+__device__ __forceinline__ float2 decay_pair(float2 w, int jp) {
+    return jp >= 2 - NP ? kmb_exp2_fma2(w) : kmb_exp2_decay2(w);
+}
 
 template <typename T> struct IO;
 template <> struct IO<float> {
@@ -156,6 +189,7 @@ __device__ __forceinline__ int fwd_run(const SegArgs &p, unsigned char *smem, in
     const T *Cg = static_cast<const T *>(p.C) + b * L * kN;
     T *yg = static_cast<T *>(p.y);
     float *ck = p.ckpt ? p.ckpt + (b * p.nslots * D + d) * kN + n0 : nullptr;
+    const float amaxF = fma_pairs_amax<kFmaFwd>(A2p);
 
     auto stage = [&](int k) { return smem + (k % kST) * LY::STAGE; };
     auto load = [&](int k) {
@@ -273,6 +307,7 @@ __device__ __forceinline__ int fwd_run(const SegArgs &p, unsigned char *smem, in
             float hst[4] = {h[0], h[1], h[2], h[3]};
             const float2 wst[2] = {wsum[0], wsum[1]};
             float2 sq = kmb_f2s(0.f);
+            float dmax = 0.f; /* max |dt| of the tile: bounds |w| of the FMA-pipe pairs */
 #pragma unroll
             for (int i0 = 0; i0 < kTT; i0 += kP) {
                 float yq[kP];
@@ -280,6 +315,7 @@ __device__ __forceinline__ int fwd_run(const SegArgs &p, unsigned char *smem, in
                 for (int s4 = 0; s4 < kP; ++s4) {
                     const int i = i0 + s4;
                     const float dv = IO<T>::f(ds[i * kDT]);
+                    if (kFmaFwd > 0) dmax = fmaxf(dmax, fabsf(dv));
                     const float2 dv2 = kmb_f2s(dv), u2 = kmb_f2s(dv * IO<T>::f(xs[i * kDT]));
                     const float4 b4 = IO<T>::f4(bs + i * kN);
                     const float2 bp[2] = {kmb_f2(b4.x, b4.y), kmb_f2(b4.z, b4.w)};
@@ -287,7 +323,7 @@ __device__ __forceinline__ int fwd_run(const SegArgs &p, unsigned char *smem, in
 #pragma unroll
                     for (int jp = 0; jp < 2; ++jp) {
                         w[jp] = kmb_mul2(dv2, A2p[jp]);
-                        a[jp] = kmb_exp2_decay2(w[jp]);
+                        a[jp] = decay_pair<kFmaFwd>(w[jp], jp);
                     }
                     float2 hn[2];
 #pragma unroll
@@ -314,7 +350,13 @@ __device__ __forceinline__ int fwd_run(const SegArgs &p, unsigned char *smem, in
                 }
                 if (!warm) ys[(i0 + g) * kDT] = rs4(yq, lane);
             }
-            if (CLAMP && __any_sync(kFull, !(sq.x + sq.y < 1e6f))) {
+            /* replay the tile exactly (clamped, MUFU / polynomial decays)
+             * when a state may have reached the clamp or a FMA-pipe decay
+             * argument may have left its range */
+            bool bad = false;
+            if (CLAMP) bad = !(sq.x + sq.y < 1e6f);
+            if (kFmaFwd > 0) bad = bad || !(dmax * amaxF <= KMB_EXP2_FMA_MAX);
+            if ((CLAMP || kFmaFwd > 0) && __any_sync(kFull, bad)) {
                 if (seg) {
                     *sflag = 1; /* the CTA stops at the next tile boundary */
                 } else {
@@ -337,7 +379,7 @@ __device__ __forceinline__ int fwd_run(const SegArgs &p, unsigned char *smem, in
 }
 
 template <typename T, bool CLAMP>
-__global__ void __launch_bounds__(kNT, 3) k_scan1d_fwd_seg(SegArgs p) {
+__global__ void __launch_bounds__(kNT, 4) k_scan1d_fwd_seg(SegArgs p) {
     extern __shared__ __align__(16) unsigned char smem[];
     int *sflag = reinterpret_cast<int *>(smem + kST * FwdLayout<T>::STAGE);
     const int tid = threadIdx.x, n0 = (tid & 3) * 4;
@@ -453,6 +495,7 @@ __device__ __forceinline__ int bwd_run(const SegArgs &p, unsigned char *smem, lo
     };
 
     float2 wsum[2] = {kmb_f2s(0.f), kmb_f2s(0.f)};
+    const float amaxF = fma_pairs_amax<kFmaBwd>(A2p);
     load(ct, 0);
     kmb_cp_async_commit();
     int status = 0;
@@ -503,9 +546,11 @@ __device__ __forceinline__ int bwd_run(const SegArgs &p, unsigned char *smem, lo
             constexpr bool EXACT = decltype(exact_tag)::value;
             float2 hh[2] = {hsp[0], hsp[1]};
             float2 sq = kmb_f2s(0.f);
+            float dmax = 0.f;
 #pragma unroll
             for (int i = 0; i < kCh; ++i) {
                 const float dv = IO<T>::f(ds[i * kDT]);
+                if (!EXACT && kFmaBwd > 0) dmax = fmaxf(dmax, fabsf(dv));
                 const float2 dv2 = kmb_f2s(dv), u2 = kmb_f2s(dv * IO<T>::f(xs[i * kDT]));
                 const float4 b4 = IO<T>::f4(bs + i * kN);
                 const float2 bp[2] = {kmb_f2(b4.x, b4.y), kmb_f2(b4.z, b4.w)};
@@ -513,9 +558,9 @@ __device__ __forceinline__ int bwd_run(const SegArgs &p, unsigned char *smem, lo
                 for (int jp = 0; jp < 2; ++jp) {
                     const float2 w = kmb_mul2(dv2, A2p[jp]);
                     if (warm && !EXACT) wsum[jp] = kmb_add2(wsum[jp], w);
-                    const float2 a = kmb_exp2_decay2(w);
+                    const float2 a = EXACT ? kmb_exp2_decay2(w) : decay_pair<kFmaBwd>(w, jp);
                     float2 hn = kmb_fma2(a, hh[jp], kmb_mul2(bp[jp], u2));
-                    if (EXACT) {
+                    if (EXACT && CLAMP) {
                         hn.x = clamp1000(hn.x);
                         hn.y = clamp1000(hn.y);
                     } else if (CLAMP) {
@@ -526,7 +571,10 @@ __device__ __forceinline__ int bwd_run(const SegArgs &p, unsigned char *smem, lo
                     ar[i][jp] = a;
                 }
             }
-            return CLAMP && !EXACT && !(sq.x + sq.y < 1e6f);
+            if (EXACT) return false;
+            bool bad = CLAMP && !(sq.x + sq.y < 1e6f);
+            if (kFmaBwd > 0) bad = bad || !(dmax * amaxF <= KMB_EXP2_FMA_MAX);
+            return bad;
         };
         if (__any_sync(kFull, recompute(std::false_type{}))) recompute(std::true_type{});
 
@@ -672,6 +720,15 @@ __global__ void __launch_bounds__(kNT, 3) k_scan1d_bwd_seg(SegArgs p) {
     }
 }
 
+__global__ void k_exp2_fma_eval(const float *w, float *out, long n) {
+    for (long i = ((long)blockIdx.x * blockDim.x + threadIdx.x) * 2; i < n;
+         i += (long)gridDim.x * blockDim.x * 2) {
+        const float2 r = kmb_exp2_fma2(kmb_f2(w[i], i + 1 < n ? w[i + 1] : 0.f));
+        out[i] = r.x;
+        if (i + 1 < n) out[i + 1] = r.y;
+    }
+}
+
 __global__ void k_f32_to_bf16(const float *src, __nv_bfloat16 *dst, long n) {
     for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
         dst[i] = __float2bfloat16_rn(src[i]);
@@ -787,4 +844,15 @@ extern "C" int kmb_launch_scan1d_bwd_seg(const KmbScan1D *a, const float *ckpt_i
     k_f32_to_bf16<<<blocks, 256, 0, s>>>(dC32, static_cast<__nv_bfloat16 *>((void *)a->dC), n);
     e = cudaGetLastError();
     return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "scan1d seg dB/dC conversion");
+}
+
+extern "C" int kmb_exp2_fma_eval(const float *w, float *out, long n) {
+    if (!w || !out || n < 0) return kmb_fail(KMB_EINVAL, "exp2_fma_eval: bad arguments");
+    if (n == 0) return KMB_OK;
+    cudaStream_t s = kmb_stream();
+    const long blocks = (n / 2 + 255) / 256 < 1024 ? (n / 2 + 255) / 256 + 1 : 1024;
+    k_exp2_fma_eval<<<(unsigned)blocks, 256, 0, s>>>(w, out, n);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess && kmb_sync_enabled()) e = cudaStreamSynchronize(s);
+    return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "exp2_fma_eval");
 }

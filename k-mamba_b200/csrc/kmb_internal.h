@@ -32,6 +32,9 @@ int kmb_launch_scan1d_bwd(const KmbScan1D *a, const float *ckpt_in,
  * D * 16 floats, flag batch * (D / 32) * S ints. */
 int kmb_scan1d_seg_supported(const KmbScan1D *a, int elem_bytes);
 int kmb_scan1d_seg_plan(long batch, long L, long D, int *S, int *seg_len);
+/* Diagnostic (exported for the tests): out[i] = kmb_exp2_fma2(w[i]), the
+ * FMA-pipe 2^w of csrc/cuda/kmb_common.cuh, on device pointers. */
+int kmb_exp2_fma_eval(const float *w, float *out, long n);
 int kmb_launch_scan1d_fwd_seg(const KmbScan1D *a, int bf16, int S, int seg_len,
                               float *seg_state, int *flag, cudaStream_t s);
 int kmb_launch_scan1d_bwd_seg(const KmbScan1D *a, const float *ckpt_in, int bf16, int S,

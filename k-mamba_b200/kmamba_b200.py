@@ -293,6 +293,8 @@ PROTOTYPES = {
     "kmb_scan1d_ckpt_elems": (lg, [lg, lg, lg, lg]),
     # segments and steps per segment the 1D entry points split L into
     "kmb_scan1d_seg_plan": (C.c_int, [lg, lg, lg, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+    # diagnostic: the FMA-pipe 2^w of the scans on device pointers
+    "kmb_exp2_fma_eval": (C.c_int, [C.c_void_p, C.c_void_p, lg]),
     "kmb_scan1d_fwd": (C.c_int, [C.POINTER(KmbScan1D)]),
     "kmb_scan1d_bwd": (C.c_int, [C.POINTER(KmbScan1D)]),
     "kmb_scan1d_bwd_noalloc": (C.c_int, [C.POINTER(KmbScan1D)]),
