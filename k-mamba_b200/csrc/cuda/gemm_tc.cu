@@ -139,6 +139,92 @@ struct GemmDev {
 
 __device__ __forceinline__ float silu(float v) { return v / (1.f + __expf(-v)); }
 
+/*
+ * Epilogue of one tile for the calling warp: accumulator rows 32q..32q+31
+ * (q = the warp's TMEM lane quarter) at TMEM column `col0`, written to C
+ * rows m0 + 32q + lane, columns n0.. (bias, activation, residual; `split`:
+ * fp32 atomics of a split-K share).  All 32 lanes must call it.
+ */
+template <int BN>
+__device__ __forceinline__ void epilogue_rows(const GemmDev &p, uint32_t tmem, uint32_t col0,
+                                              int q, int lane, long m0, long n0, bool ok,
+                                              bool lead, bool split) {
+    const long row = m0 + q * 32 + lane;
+    const bool row_ok = ok && row < p.M;
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t r[16];
+        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + col0 + (uint32_t)c0;
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, "
+            "%10, %11, %12, %13, %14, %15}, [%16];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+              "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
+              "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+            : "r"(taddr));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (!row_ok) continue;
+        const long n = n0 + c0;
+        if (n >= p.N) continue;
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            float t = __uint_as_float(r[j]);
+            if (lead && p.bias && n + j < p.N) t += p.bias[n + j];
+            if (p.act == 1) t = silu(t);
+            if (lead && p.residual && n + j < p.N) t += p.residual[row * p.ldr + n + j];
+            v[j] = t;
+        }
+        const bool full16 = n + 16 <= p.N;
+        if (split) { /* fp32 C: this split's share, added atomically */
+            float *c = reinterpret_cast<float *>(p.C) + row * p.ldc + n;
+            if (full16 && ((reinterpret_cast<uintptr_t>(c) & 15) == 0)) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    atomicAdd(reinterpret_cast<float4 *>(c) + j,
+                              make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
+            } else {
+                for (int j = 0; j < 16 && n + j < p.N; ++j) atomicAdd(c + j, v[j]);
+            }
+            continue;
+        }
+        if (p.c_bf16) {
+            __nv_bfloat16 *c = reinterpret_cast<__nv_bfloat16 *>(p.C) + row * p.ldc + n;
+            if (full16 && !p.accumulate && ((reinterpret_cast<uintptr_t>(c) & 15) == 0)) {
+                uint32_t w[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+                    w[j] = *reinterpret_cast<const uint32_t *>(&h2);
+                }
+                reinterpret_cast<uint4 *>(c)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                reinterpret_cast<uint4 *>(c)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+            } else {
+                for (int j = 0; j < 16 && n + j < p.N; ++j) {
+                    float t = v[j];
+                    if (p.accumulate) t += __bfloat162float(c[j]);
+                    c[j] = __float2bfloat16_rn(t);
+                }
+            }
+        } else {
+            float *c = reinterpret_cast<float *>(p.C) + row * p.ldc + n;
+            if (full16 && ((reinterpret_cast<uintptr_t>(c) & 15) == 0)) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float4 t = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                    if (p.accumulate) {
+                        const float4 o = reinterpret_cast<const float4 *>(c)[j];
+                        t.x += o.x; t.y += o.y; t.z += o.z; t.w += o.w;
+                    }
+                    reinterpret_cast<float4 *>(c)[j] = t;
+                }
+            } else {
+                for (int j = 0; j < 16 && n + j < p.N; ++j) c[j] = p.accumulate ? c[j] + v[j] : v[j];
+            }
+        }
+    }
+}
+
 template <int BN, int STAGES, bool AMN, bool BMN>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
@@ -254,80 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     /* epilogue: all four warps */
     const bool ok = nk > 0 && mbar_wait(acc_full, 0, abort);
     asm volatile("tcgen05.fence::after_thread_sync;");
-    const long row = m0 + warp * 32 + lane;
-    const bool row_ok = ok && row < p.M;
-#pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 16) {
-        uint32_t r[16];
-        const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0;
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, "
-            "%10, %11, %12, %13, %14, %15}, [%16];"
-            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
-              "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
-              "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-            : "r"(taddr));
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if (!row_ok) continue;
-        const long n = n0 + c0;
-        if (n >= p.N) continue;
-        float v[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            float t = __uint_as_float(r[j]);
-            if (lead && p.bias && n + j < p.N) t += p.bias[n + j];
-            if (p.act == 1) t = silu(t);
-            if (lead && p.residual && n + j < p.N) t += p.residual[row * p.ldr + n + j];
-            v[j] = t;
-        }
-        const bool full16 = n + 16 <= p.N;
-        if (split) { /* fp32 C: this split's share, added atomically */
-            float *c = reinterpret_cast<float *>(p.C) + row * p.ldc + n;
-            if (full16 && ((reinterpret_cast<uintptr_t>(c) & 15) == 0)) {
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    atomicAdd(reinterpret_cast<float4 *>(c) + j,
-                              make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
-            } else {
-                for (int j = 0; j < 16 && n + j < p.N; ++j) atomicAdd(c + j, v[j]);
-            }
-            continue;
-        }
-        if (p.c_bf16) {
-            __nv_bfloat16 *c = reinterpret_cast<__nv_bfloat16 *>(p.C) + row * p.ldc + n;
-            if (full16 && !p.accumulate && ((reinterpret_cast<uintptr_t>(c) & 15) == 0)) {
-                uint32_t w[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
-                    w[j] = *reinterpret_cast<const uint32_t *>(&h2);
-                }
-                reinterpret_cast<uint4 *>(c)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-                reinterpret_cast<uint4 *>(c)[1] = make_uint4(w[4], w[5], w[6], w[7]);
-            } else {
-                for (int j = 0; j < 16 && n + j < p.N; ++j) {
-                    float t = v[j];
-                    if (p.accumulate) t += __bfloat162float(c[j]);
-                    c[j] = __float2bfloat16_rn(t);
-                }
-            }
-        } else {
-            float *c = reinterpret_cast<float *>(p.C) + row * p.ldc + n;
-            if (full16 && ((reinterpret_cast<uintptr_t>(c) & 15) == 0)) {
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    float4 t = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-                    if (p.accumulate) {
-                        const float4 o = reinterpret_cast<const float4 *>(c)[j];
-                        t.x += o.x; t.y += o.y; t.z += o.z; t.w += o.w;
-                    }
-                    reinterpret_cast<float4 *>(c)[j] = t;
-                }
-            } else {
-                for (int j = 0; j < 16 && n + j < p.N; ++j) c[j] = p.accumulate ? c[j] + v[j] : v[j];
-            }
-        }
-    }
+    epilogue_rows<BN>(p, tmem, 0, warp, lane, m0, n0, ok, lead, split);
 
     if (warp == 0 && lane == 0 && *abort) {
         /* after an abort, let the copies still in flight land before the
@@ -335,6 +348,318 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kb = issued > STAGES ? issued - STAGES : 0; kb < issued; ++kb) {
             const unsigned long long t0 = clock64();
             while (!mbar_test(&full[kb % STAGES], (uint32_t)(kb / STAGES) & 1u) &&
+                   clock64() - t0 < kWaitCycles) {
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(TMEM_COLS));
+    }
+}
+
+/* Row stride (floats) of an epilogue warp's staging tile [32 rows][64
+ * columns]: 4 floats of padding put the 16-byte row segments of 8
+ * consecutive lanes in disjoint banks. */
+constexpr int kStgLd = 64 + 4;
+constexpr int kStgBytes = 32 * kStgLd * 4;
+
+/* Loads 4 consecutive floats of a row (16-byte aligned, or element-wise
+ * when `vec` is false, up to `cnt` of them). */
+__device__ __forceinline__ float4 load4(const float *src, bool vec, int cnt) {
+    if (vec) return *reinterpret_cast<const float4 *>(src);
+    float t[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < cnt && j < 4; ++j) t[j] = src[j];
+    return make_float4(t[0], t[1], t[2], t[3]);
+}
+
+/*
+ * Epilogue of one tile for the calling warp, staged through shared memory
+ * so that C is written in whole row segments: for each group of 64
+ * columns, the warp reads its 32 accumulator rows (TMEM lane quarter q)
+ * with tcgen05.ld, applies bias and activation, and stores them to its
+ * padded [32][64] staging tile (one row per lane); it then reads the tile
+ * back row-wise (16 lanes x 16 B per fp32 row, 8 lanes x 16 B per bf16
+ * row), adds the residual and, when accumulating, the old C, and writes
+ * contiguous 256-byte (fp32) or 128-byte (bf16) row segments.
+ */
+template <int BN>
+__device__ __forceinline__ void epilogue_staged(const GemmDev &p, uint32_t tmem, uint32_t col0,
+                                                int q, int lane, long m0, long n0, float *stg) {
+#pragma unroll 1
+    for (int cg = 0; cg < BN; cg += 64) {
+        const long nb = n0 + cg; /* first column of the group */
+#pragma unroll
+        for (int c16 = 0; c16 < 64; c16 += 16) {
+            uint32_t r[16];
+            const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + col0 + (uint32_t)(cg + c16);
+            asm volatile(
+                "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, "
+                "%10, %11, %12, %13, %14, %15}, [%16];"
+                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                  "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
+                  "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+                : "r"(taddr));
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            float v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                float t = __uint_as_float(r[j]);
+                const long n = nb + c16 + j;
+                if (p.bias && n < p.N) t += p.bias[n];
+                if (p.act == 1) t = silu(t);
+                v[j] = t;
+            }
+            float4 *dst = reinterpret_cast<float4 *>(stg + lane * kStgLd + c16);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        }
+        __syncwarp();
+        if (p.c_bf16) {
+            const int rsub = lane >> 3, c8 = (lane & 7) * 8;
+#pragma unroll 1
+            for (int r0 = 0; r0 < 32; r0 += 4) {
+                const int rr = r0 + rsub;
+                const long row = m0 + q * 32 + rr, col = nb + c8;
+                if (row >= p.M || col >= p.N) continue;
+                const int cnt = (int)min((long)8, p.N - col);
+                const float4 a = *reinterpret_cast<const float4 *>(stg + rr * kStgLd + c8);
+                const float4 b = *reinterpret_cast<const float4 *>(stg + rr * kStgLd + c8 + 4);
+                float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+                if (p.residual) {
+                    const float *rs = p.residual + row * p.ldr + col;
+                    const bool rv = cnt == 8 && ((reinterpret_cast<uintptr_t>(rs) & 15) == 0);
+                    const float4 x0 = load4(rs, rv, cnt), x1 = load4(rs + 4, rv, cnt - 4);
+                    v[0] += x0.x; v[1] += x0.y; v[2] += x0.z; v[3] += x0.w;
+                    v[4] += x1.x; v[5] += x1.y; v[6] += x1.z; v[7] += x1.w;
+                }
+                __nv_bfloat16 *c = reinterpret_cast<__nv_bfloat16 *>(p.C) + row * p.ldc + col;
+                if (cnt == 8 && !p.accumulate && ((reinterpret_cast<uintptr_t>(c) & 15) == 0)) {
+                    uint32_t w[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+                        w[j] = *reinterpret_cast<const uint32_t *>(&h2);
+                    }
+                    *reinterpret_cast<uint4 *>(c) = make_uint4(w[0], w[1], w[2], w[3]);
+                } else {
+                    for (int j = 0; j < cnt; ++j) {
+                        float t = v[j];
+                        if (p.accumulate) t += __bfloat162float(c[j]);
+                        c[j] = __float2bfloat16_rn(t);
+                    }
+                }
+            }
+        } else {
+            const int rsub = lane >> 4, c4 = (lane & 15) * 4;
+#pragma unroll 1
+            for (int r0 = 0; r0 < 32; r0 += 2) {
+                const int rr = r0 + rsub;
+                const long row = m0 + q * 32 + rr, col = nb + c4;
+                if (row >= p.M || col >= p.N) continue;
+                const int cnt = (int)min((long)4, p.N - col);
+                float4 t = *reinterpret_cast<const float4 *>(stg + rr * kStgLd + c4);
+                if (p.residual) {
+                    const float *rs = p.residual + row * p.ldr + col;
+                    const float4 x = load4(rs, cnt == 4 && ((reinterpret_cast<uintptr_t>(rs) & 15) == 0), cnt);
+                    t.x += x.x; t.y += x.y; t.z += x.z; t.w += x.w;
+                }
+                float *c = reinterpret_cast<float *>(p.C) + row * p.ldc + col;
+                if (cnt == 4 && ((reinterpret_cast<uintptr_t>(c) & 15) == 0)) {
+                    if (p.accumulate) {
+                        const float4 o = *reinterpret_cast<const float4 *>(c);
+                        t.x += o.x; t.y += o.y; t.z += o.z; t.w += o.w;
+                    }
+                    *reinterpret_cast<float4 *>(c) = t;
+                } else {
+                    const float tv[4] = {t.x, t.y, t.z, t.w};
+                    for (int j = 0; j < cnt; ++j) c[j] = p.accumulate ? c[j] + tv[j] : tv[j];
+                }
+            }
+        }
+        __syncwarp();
+    }
+}
+
+/*
+ * Persistent variant for grids of many tiles (no split-K): one CTA per SM
+ * walks the tiles blockIdx.x, blockIdx.x + gridDim.x, ... (n tile fastest,
+ * so concurrent CTAs share the A row block in L2) with two accumulators in
+ * TMEM (2 x BN columns), so that the epilogue of tile i overlaps the MMAs
+ * of tile i + 1 and the TMA ring runs across tile boundaries.
+ * Warps (192 threads):
+ *   warp 0, one lane: TMA producer over every k-block of every tile;
+ *   warp 1, one lane: MMA issuer; tile i accumulates into buffer i & 1
+ *                     once the epilogue has drained it (acc_empty), and
+ *                     commits acc_full[i & 1] after its last k-block;
+ *   warps 2-5:        epilogue; warp w reads TMEM lane quarter w % 4 (rows
+ *                     32 (w % 4) ..) of the finished buffer, writes C in
+ *                     row segments through its shared staging tile
+ *                     (epilogue_staged), and arrives on acc_empty (one
+ *                     arrive per warp).
+ * The staging tiles take 34 KB of shared memory, so the ring has 3 stages
+ * at BN = 256 and 5 at BN = 128.
+ * Every wait is bounded as in k_gemm_tc.
+ */
+constexpr int kPThreads = 192;
+
+template <int BN, int STAGES, bool AMN, bool BMN>
+__global__ void __launch_bounds__(kPThreads, 1)
+    k_gemm_tc_persist(const __grid_constant__ CUtensorMap mapA,
+                      const __grid_constant__ CUtensorMap mapB, GemmDev p, int tiles_n,
+                      int tiles) {
+    constexpr int A_BYTES = kBM * kBK * 2;
+    constexpr int B_BYTES = BN * kBK * 2;
+    constexpr uint32_t TMEM_COLS = 2 * BN; /* two fp32 accumulators */
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sA = smem;
+    uint8_t *sB = smem + STAGES * A_BYTES;
+    float *stg_all = reinterpret_cast<float *>(sB + STAGES * B_BYTES); /* [4][32][kStgLd] */
+    uint64_t *full = reinterpret_cast<uint64_t *>(stg_all + 4 * 32 * kStgLd);
+    uint64_t *empty = full + STAGES;
+    uint64_t *acc_full = empty + STAGES;    /* [2] */
+    uint64_t *acc_empty = acc_full + 2;     /* [2] */
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+    volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nk = (int)((p.K + kBK - 1) / kBK);
+    const int my_tiles = blockIdx.x < (unsigned)tiles
+                             ? (tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 4);
+        }
+        *abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mapA)));
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mapB)));
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    const uint32_t tmem = *tmem_slot;
+
+    long issued = 0; /* k-blocks the producer has loaded, over all tiles */
+    if (warp == 0 && lane == 0) {
+        /* TMA producer */
+        long g = 0;
+        for (int i = 0; i < my_tiles && !*abort; ++i) {
+            const int t = (int)blockIdx.x + i * (int)gridDim.x;
+            const int n0 = (t % tiles_n) * BN, m0 = (t / tiles_n) * kBM;
+            for (int kb = 0; kb < nk; ++kb, ++g) {
+                const int s = (int)(g % STAGES);
+                const uint32_t ph = (uint32_t)(g / STAGES) & 1u;
+                if (!mbar_wait(&empty[s], ph ^ 1u, abort)) break;
+                issued = g + 1;
+                mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
+                const int k0 = kb * kBK;
+                if (AMN) {
+                    tma_load_2d(sA + s * A_BYTES, &mapA, m0, k0, &full[s]);
+                    tma_load_2d(sA + s * A_BYTES + kBK * 128, &mapA, m0 + 64, k0, &full[s]);
+                } else {
+                    tma_load_2d(sA + s * A_BYTES, &mapA, k0, m0, &full[s]);
+                }
+                if (BMN) {
+#pragma unroll
+                    for (int j = 0; j < BN / 64; ++j)
+                        tma_load_2d(sB + s * B_BYTES + j * kBK * 128, &mapB, n0 + 64 * j, k0,
+                                    &full[s]);
+                } else {
+                    tma_load_2d(sB + s * B_BYTES, &mapB, k0, n0, &full[s]);
+                }
+            }
+        }
+    } else if (warp == 1 && lane == 0) {
+        /* MMA issuer */
+        constexpr uint32_t idesc = instr_desc<BN, AMN, BMN>();
+        long g = 0;
+        for (int i = 0; i < my_tiles; ++i) {
+            const int buf = i & 1;
+            const uint32_t use = (uint32_t)(i >> 1) & 1u;
+            /* the epilogue has drained this buffer (tile i - 2) */
+            if (!mbar_wait(&acc_empty[buf], use ^ 1u, abort)) break;
+            asm volatile("tcgen05.fence::after_thread_sync;");
+            const uint32_t acc = tmem + (uint32_t)(buf * BN);
+            bool ok = true;
+            for (int kb = 0; kb < nk; ++kb, ++g) {
+                const int s = (int)(g % STAGES);
+                const uint32_t ph = (uint32_t)(g / STAGES) & 1u;
+                if (!mbar_wait(&full[s], ph, abort)) {
+                    ok = false;
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;");
+                const uint32_t a_addr = smem_u32(sA + s * A_BYTES);
+                const uint32_t b_addr = smem_u32(sB + s * B_BYTES);
+#pragma unroll
+                for (int k = 0; k < kBK / 16; ++k) {
+                    const uint64_t da = AMN ? smem_desc(a_addr + k * 2048, kBK * 128)
+                                            : smem_desc(a_addr + k * 32, 16);
+                    const uint64_t db = BMN ? smem_desc(b_addr + k * 2048, kBK * 128)
+                                            : smem_desc(b_addr + k * 32, 16);
+                    const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+                    asm volatile(
+                        "{\n\t.reg .pred p;\n\t"
+                        "setp.ne.b32 p, %4, 0;\n\t"
+                        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(acc),
+                        "l"(da), "l"(db), "r"(idesc), "r"(accum));
+                }
+                asm volatile(
+                    "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
+                    "[%0];" ::"r"(smem_u32(&empty[s]))
+                    : "memory");
+            }
+            if (!ok) break;
+            asm volatile(
+                "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                    smem_u32(&acc_full[buf]))
+                : "memory");
+        }
+    } else if (warp >= 2) {
+        /* epilogue warps */
+        const int q = warp & 3;
+        for (int i = 0; i < my_tiles; ++i) {
+            const int buf = i & 1;
+            const uint32_t ph = (uint32_t)(i >> 1) & 1u;
+            const int t = (int)blockIdx.x + i * (int)gridDim.x;
+            const long n0 = (long)(t % tiles_n) * BN, m0 = (long)(t / tiles_n) * kBM;
+            const bool ok = mbar_wait(&acc_full[buf], ph, abort);
+            asm volatile("tcgen05.fence::after_thread_sync;");
+            if (!ok) break;
+            epilogue_staged<BN>(p, tmem, (uint32_t)(buf * BN), q, lane, m0, n0,
+                                stg_all + (warp - 2) * 32 * kStgLd);
+            asm volatile("tcgen05.fence::before_thread_sync;");
+            __syncwarp();
+            if (lane == 0)
+                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(
+                                 smem_u32(&acc_empty[buf]))
+                             : "memory");
+        }
+    }
+    __syncwarp();
+
+    if (warp == 0 && lane == 0 && *abort) {
+        for (long g = issued > STAGES ? issued - STAGES : 0; g < issued; ++g) {
+            const unsigned long long t0 = clock64();
+            while (!mbar_test(&full[g % STAGES], (uint32_t)(g / STAGES) & 1u) &&
                    clock64() - t0 < kWaitCycles) {
             }
         }
@@ -402,6 +727,36 @@ int split_count(long tiles, long nk, const KmbGemm *g) {
     return sp > 1 ? (int)sp : 1;
 }
 
+/* SMs of the current device (the persistent grid: one CTA per SM). */
+int kmb_sm_count() {
+    static int cached[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        (void)cudaGetLastError();
+        return 148;
+    }
+    if (!cached[dev]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+            (void)cudaGetLastError();
+            n = 148;
+        }
+        cached[dev] = n;
+    }
+    return cached[dev];
+}
+
+/* The persistent kernel serves every call without split-K unless
+ * KMB_GEMM_PERSIST=0 (one CTA per tile, k_gemm_tc). */
+bool persist_enabled() {
+    static int enabled = -1;
+    if (enabled < 0) {
+        const char *e = getenv("KMB_GEMM_PERSIST");
+        enabled = !(e && e[0] == '0' && e[1] == 0);
+    }
+    return enabled != 0;
+}
+
 template <int BN, int STAGES, bool AMN, bool BMN>
 int launch(const KmbGemm *g, cudaStream_t s) {
     CUtensorMap ma, mb;
@@ -429,6 +784,20 @@ int launch(const KmbGemm *g, cudaStream_t s) {
     const int splits = split_count(tiles, nk, g);
     p.kb_per_split = (int)((nk + splits - 1) / splits);
     const unsigned gz = (unsigned)((nk + p.kb_per_split - 1) / p.kb_per_split); /* no empty split */
+    if (gz == 1 && persist_enabled()) {
+        constexpr int PST = BN == 256 ? 3 : 5;
+        const int tiles_n = (int)((g->N + BN - 1) / BN);
+        const int ntiles = (int)tiles;
+        const size_t psmem = 1024 + (size_t)PST * (kBM + BN) * kBK * 2 + 4 * (size_t)kStgBytes +
+                             (2 * PST + 4) * 8 + 16;
+        auto pk = k_gemm_tc_persist<BN, PST, AMN, BMN>;
+        e = cudaFuncSetAttribute(pk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psmem);
+        if (e != cudaSuccess) return kmb_cuda_fail(e, "gemm: smem attribute");
+        const int grid_p = ntiles < kmb_sm_count() ? ntiles : kmb_sm_count();
+        pk<<<(unsigned)grid_p, kPThreads, psmem, s>>>(ma, mb, p, tiles_n, ntiles);
+        e = cudaGetLastError();
+        return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "gemm: launch");
+    }
     if (gz > 1 && !g->accumulate) {
         e = cudaMemset2DAsync(g->C, (size_t)g->ldc * 4, 0, (size_t)g->N * 4, (size_t)g->M, s);
         if (e != cudaSuccess) return kmb_cuda_fail(e, "gemm: split-K zero fill");
