@@ -240,30 +240,74 @@ def run_reference_arm(args):
 # secondary workloads (configs 3 and 4), single GPU, device-resident
 # --------------------------------------------------------------------------
 
+def lib_comm(lib, kb, dist, world, rank, local):
+    """The library's own NCCL communicator (kmamba_distributed.h); its
+    unique id travels over torch.distributed.  None for one rank."""
+    if world <= 1:
+        return None
+    uid = C.create_string_buffer(128)
+    if rank == 0:
+        kb.check(lib, lib.kmb_dist_get_unique_id(uid))
+    box = [uid.raw if rank == 0 else None]
+    dist.broadcast_object_list(box, src=0)
+    ctx = lib.kmb_dist_init_with_id(world, rank, local, C.create_string_buffer(box[0], 128))
+    if not ctx:
+        raise RuntimeError(kb.last_error(lib))
+    return ctx
+
+
 def run_secondary(args):
     """Times one forward + backward of BASELINE config 3 (ConvND 512x512,
     D 64, K 3, batch 16) or config 4 (2D scan 256x256, batch 8, D 256,
     N 16, B/C shared, same dt on both axes) and prints one JSON line with
     the per-kernel roofline.  Algorithmic bytes: inputs read once plus
-    outputs written once."""
+    outputs written once.
+
+    Under torchrun every rank runs the same pass on its share of the
+    config's batch (--shard-batch: the batch split over the ranks, SURVEY
+    8(e)'s fixed-config series; otherwise a full batch per rank), and the
+    parameter gradients (dkernel / dbias, or dA) are summed over the ranks
+    by the library's NCCL communicator after every backward.  Time: max
+    over ranks; value: bytes of all ranks per second."""
     import torch
+    import torch.distributed as dist
     import kmamba_b200 as kb
+    import kmb_dist
+    rank, world = kmb_dist.env_rank()
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        kmb_dist.init("nccl", timeout_s=120, device_id=torch.device("cuda", local))
     lib = kb.load()
     stream = torch.cuda.current_stream()
-    lib.kmb_set_stream(C.c_void_p(stream.cuda_stream))
+    sp = C.c_void_p(stream.cuda_stream)
+    lib.kmb_set_stream(sp)
     lib.kmb_set_sync(0)
+    ctx = lib_comm(lib, kb, dist, world, rank, local)
+
+    def share(full):
+        """(items on this rank, items of the whole job)"""
+        if args.batch is not None:
+            return args.batch, args.batch * world
+        if args.shard_batch and world > 1:
+            n = full // world + (1 if rank < full % world else 0)
+            if n == 0:
+                raise SystemExit(f"--shard-batch: {world} ranks for a batch of {full}")
+            return n, full
+        return full, full * world
     f = np.float32
-    rng = np.random.default_rng(7)
+    rng = np.random.default_rng(kmb_dist.shard_seed(7, rank))
     dev = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=f)).cuda()  # noqa: E731
     dtype = "f32"
     if args.workload == "conv3":
-        bsz, H, W, Dc, K = (args.batch or 16), 512, 512, 64, 3
+        (bsz, gbatch), H, W, Dc, K = share(16), 512, 512, 64, 3
         Pn = H * W
         E3 = bsz * Pn * Dc
         # activations (input, output, dy, dinput) in fp32 or bf16; taps,
         # bias and their gradients fp32
         ab = 2 if args.io == "bf16" else 4
         fwd_b, bwd_b = ab * 2 * E3 + 4 * 640, ab * 3 * E3 + 4 * 1280
+        scale_job = gbatch / bsz
         act = (lambda a: dev(a).to(torch.bfloat16)) if ab == 2 else dev
         inp = act(rng.standard_normal((bsz, Pn, Dc), dtype=f))
         ker = dev(rng.standard_normal((9, Dc), dtype=f) / 3)
@@ -281,16 +325,18 @@ def run_secondary(args):
         fwd = lambda: kb.check(lib, ffn(C.byref(a)))  # noqa: E731
         bwd = lambda: kb.check(lib, bfn(C.byref(a)))  # noqa: E731
         names = ("k_conv2d_fwd_ring", "k_conv2d_bwd_ring")
+        grads = [(dk, 9 * Dc), (db, Dc)]
         dtype = "bf16 I/O, fp32 math" if ab == 2 else "f32"
-        workload = (f"config3: ConvND 2D 512x512, D 64, K 3, batch {bsz}, "
+        workload = (f"config3: ConvND 2D 512x512, D 64, K 3, batch {gbatch} ({bsz} per GPU), "
                     f"{'bf16 activations' if ab == 2 else 'fp32'}, fwd+bwd")
         metric = "ConvND HBM GB/s (algorithmic bytes / device time)"
     else:
-        bsz, H, W, Dc, Nn = (args.batch or 8), 256, 256, 256, 16
+        (bsz, gbatch), H, W, Dc, Nn = share(8), 256, 256, 256, 16
         Pn = H * W
         E4 = bsz * Pn * Dc
         fwd_b = 4 * (3 * E4 + 2 * bsz * Pn * Nn + 2 * Dc * Nn)
         bwd_b = 4 * (5 * E4 + 4 * bsz * Pn * Nn + 4 * Dc * Nn)
+        scale_job = gbatch / bsz
         x = dev(rng.standard_normal((bsz, Pn, Dc), dtype=f))
         dt1 = (np.log1p(np.exp(rng.standard_normal((bsz, 1, Pn, Dc), dtype=f) - 2)) +
                np.log(2)).astype(f)
@@ -319,40 +365,83 @@ def run_secondary(args):
         fwd = lambda: kb.check(lib, lib.kmb_scannd_fwd(C.byref(a)))  # noqa: E731
         bwd = lambda: kb.check(lib, lib.kmb_scannd_bwd(C.byref(a)))  # noqa: E731
         names = ("k_scan2d_fwd", "k_scan2d_bwd")
-        workload = (f"config4: 2D selective scan 256x256, batch {bsz}, D 256, N 16, fp32, "
+        grads = [(dA, 2 * Dc * Nn)]
+        workload = (f"config4: 2D selective scan 256x256, batch {gbatch} ({bsz} per GPU), D 256, "
+                    "N 16, fp32, "
                     "B/C shared, dt = softplus(N(0,1)-2) + ln 2 on both axes, fwd+bwd "
                     "(stored-state kernels of the reference API)")
         metric = "scan HBM GB/s (algorithmic bytes / device time), 2D selective scan fwd+bwd"
+    def exchange():
+        # sum of the parameter gradients over the ranks (side stream,
+        # ordered after the backward; the next step's backward waits)
+        if ctx:
+            for t, n in grads:
+                kb.check(lib, lib.kmb_dist_bucket_add(ctx, t.data_ptr(), n, 0, sp))
+            kb.check(lib, lib.kmb_dist_bucket_flush(ctx, sp))
+
     ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
     for _ in range(args.warmup):
         fwd()
+        if ctx:
+            kb.check(lib, lib.kmb_dist_wait(ctx, sp))
         bwd()
+        exchange()
+    if ctx:
+        kb.check(lib, lib.kmb_dist_wait(ctx, sp))
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
     torch.cuda.synchronize()
     marks = [[ev(), ev(), ev()] for _ in range(args.steps)]
-    with Clocks(0) as clk:
+    start, stop = ev(), ev()
+    with Clocks(local) as clk:
+        start.record(stream)
         for m in marks:
             m[0].record(stream)
             fwd()
+            if ctx:
+                kb.check(lib, lib.kmb_dist_wait(ctx, sp))
             m[1].record(stream)
             bwd()
             m[2].record(stream)
+            exchange()
+        if ctx:
+            kb.check(lib, lib.kmb_dist_wait(ctx, sp))
+        stop.record(stream)
         torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    elapsed = kmb_dist.max_over_ranks(start.elapsed_time(stop) / 1e3, world, device="cuda")
     fms = sum(m[0].elapsed_time(m[1]) for m in marks) / args.steps
     bms = sum(m[1].elapsed_time(m[2]) for m in marks) / args.steps
     pk, pk_kind = peaks()
     dom = (bms, bwd_b, names[1]) if bms >= fms else (fms, fwd_b, names[0])
     ach = dom[1] / (dom[0] / 1e3) / 1e9
+    job_bytes = (fwd_b + bwd_b) * scale_job
+    if ctx:
+        lib.kmamba_distributed_fini_nccl(ctx)
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
     print(json.dumps({
-        "metric": metric, "value": (fwd_b + bwd_b) / ((fms + bms) / 1e3) / 1e9, "unit": "GB/s",
-        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": fms + bms,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype,
+        "metric": metric, "value": job_bytes * args.steps / elapsed / 1e9, "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "strong" if (args.shard_batch and world > 1) else "weak",
+        "vs_baseline": None, "dtype": dtype,
         "data": "synthetic", "config": {"workload": workload, "fwd_ms": fms, "bwd_ms": bms,
+                                        "batch_per_gpu": bsz, "global_batch": gbatch,
+                                        "parallelism": f"dp{world} (parameter gradients summed by "
+                                                       "the library's NCCL communicator)",
                                         "fwd_GBps": fwd_b / fms / 1e6,
                                         "bwd_GBps": bwd_b / bms / 1e6},
         "roofline": {"bound": "hbm", "kernel": dom[2], "achieved": ach, "peak": pk["hbm_gbs"],
                      "unit": "GB/s", "frac": ach / pk["hbm_gbs"],
                      "peak_source": f"{pk_kind} hbm_gbs", "traffic": None},
         "gpu_launches": 2 * args.steps, "clocks": clk.summary()}), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
 
 
 # --------------------------------------------------------------------------
