@@ -407,18 +407,26 @@ __device__ __forceinline__ void epilogue_staged(const GemmDev &p, uint32_t tmem,
                 : "r"(taddr));
         }
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (!p.bias && p.act == 0) { /* the plain product: stored as loaded */
 #pragma unroll
-        for (int c4 = 0; c4 < 64; c4 += 4) {
-            float v[4];
+            for (int c4 = 0; c4 < 64; c4 += 4)
+                *reinterpret_cast<uint4 *>(stg + lane * kStgLd + c4) =
+                    make_uint4(r[c4], r[c4 + 1], r[c4 + 2], r[c4 + 3]);
+        } else {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                float t = __uint_as_float(r[c4 + j]);
-                const long n = nb + c4 + j;
-                if (p.bias && n < p.N) t += p.bias[n];
-                if (p.act == 1) t = silu(t);
-                v[j] = t;
+            for (int c4 = 0; c4 < 64; c4 += 4) {
+                float v[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float t = __uint_as_float(r[c4 + j]);
+                    const long n = nb + c4 + j;
+                    if (p.bias && n < p.N) t += p.bias[n];
+                    if (p.act == 1) t = silu(t);
+                    v[j] = t;
+                }
+                *reinterpret_cast<float4 *>(stg + lane * kStgLd + c4) =
+                    make_float4(v[0], v[1], v[2], v[3]);
             }
-            *reinterpret_cast<float4 *>(stg + lane * kStgLd + c4) = make_float4(v[0], v[1], v[2], v[3]);
         }
         __syncwarp();
         if (p.c_bf16) {
@@ -429,8 +437,12 @@ __device__ __forceinline__ void epilogue_staged(const GemmDev &p, uint32_t tmem,
                 const long row = m0 + q * 32 + rr, col = nb + c8;
                 if (row >= p.M || col >= p.N) continue;
                 const int cnt = (int)min((long)8, p.N - col);
-                const float4 a = *reinterpret_cast<const float4 *>(stg + rr * kStgLd + c8);
-                const float4 b = *reinterpret_cast<const float4 *>(stg + rr * kStgLd + c8 + 4);
+                /* lanes 4-7 of each row read their second half first, so
+                 * the 8 lanes of a row touch 8 distinct bank quads */
+                const bool sw = (lane & 4) != 0;
+                const float4 a0 = *reinterpret_cast<const float4 *>(stg + rr * kStgLd + c8 + (sw ? 4 : 0));
+                const float4 b0 = *reinterpret_cast<const float4 *>(stg + rr * kStgLd + c8 + (sw ? 0 : 4));
+                const float4 a = sw ? b0 : a0, b = sw ? a0 : b0;
                 float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
                 if (p.residual) {
                     const float *rs = p.residual + row * p.ldr + col;
