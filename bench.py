@@ -334,17 +334,20 @@ def run_secondary(args):
         (bsz, gbatch), H, W, Dc, Nn = share(8), 256, 256, 256, 16
         Pn = H * W
         E4 = bsz * Pn * Dc
-        fwd_b = 4 * (3 * E4 + 2 * bsz * Pn * Nn + 2 * Dc * Nn)
-        bwd_b = 4 * (5 * E4 + 4 * bsz * Pn * Nn + 4 * Dc * Nn)
+        # bf16 I/O: x, dt, B, C, y, dy, dx, ddelta, dB, dC in 2 bytes; A, dA fp32
+        ab = 2 if args.io == "bf16" else 4
+        fwd_b = ab * (3 * E4 + 2 * bsz * Pn * Nn) + 4 * 2 * Dc * Nn
+        bwd_b = ab * (5 * E4 + 4 * bsz * Pn * Nn) + 4 * 4 * Dc * Nn
         scale_job = gbatch / bsz
-        x = dev(rng.standard_normal((bsz, Pn, Dc), dtype=f))
+        act = (lambda a: dev(a).to(torch.bfloat16)) if ab == 2 else dev
+        x = act(rng.standard_normal((bsz, Pn, Dc), dtype=f))
         dt1 = (np.log1p(np.exp(rng.standard_normal((bsz, 1, Pn, Dc), dtype=f) - 2)) +
                np.log(2)).astype(f)
-        delta = dev(np.concatenate([dt1, dt1], axis=1))  # same dt on both axes
+        delta = act(np.concatenate([dt1, dt1], axis=1))  # same dt on both axes
         A = dev(-np.exp(rng.uniform(0, np.log(16), (2, Dc, Nn))))
-        B = dev(rng.standard_normal((bsz, Pn, Nn), dtype=f))
-        Cm = dev(rng.standard_normal((bsz, Pn, Nn), dtype=f))
-        dy = dev(rng.standard_normal((bsz, Pn, Dc), dtype=f))
+        B = act(rng.standard_normal((bsz, Pn, Nn), dtype=f))
+        Cm = act(rng.standard_normal((bsz, Pn, Nn), dtype=f))
+        dy = act(rng.standard_normal((bsz, Pn, Dc), dtype=f))
         h = torch.empty((bsz, Pn, Dc, Nn), device="cuda")
         y, dx = torch.empty_like(x), torch.empty_like(x)
         ddl, dA = torch.empty_like(delta), torch.empty_like(A)
@@ -360,15 +363,18 @@ def run_secondary(args):
         a.dy, a.dx, a.ddelta, a.dA, a.dB, a.dC = (t.data_ptr() for t in (dy, dx, ddl, dA, dB, dC))
         a.dims[0], a.dims[1] = H, W
         a.ndims, a.batch, a.D, a.M, a.bc_shared = 2, bsz, Dc, Nn, 1
-        lib.kmb_scannd_fwd.argtypes = [C.c_void_p]
-        lib.kmb_scannd_bwd.argtypes = [C.c_void_p]
-        fwd = lambda: kb.check(lib, lib.kmb_scannd_fwd(C.byref(a)))  # noqa: E731
-        bwd = lambda: kb.check(lib, lib.kmb_scannd_bwd(C.byref(a)))  # noqa: E731
+        ffn, bfn = ((lib.kmb_scannd_fwd_bf16, lib.kmb_scannd_bwd_bf16) if ab == 2
+                    else (lib.kmb_scannd_fwd, lib.kmb_scannd_bwd))
+        ffn.argtypes = [C.c_void_p]
+        bfn.argtypes = [C.c_void_p]
+        fwd = lambda: kb.check(lib, ffn(C.byref(a)))  # noqa: E731
+        bwd = lambda: kb.check(lib, bfn(C.byref(a)))  # noqa: E731
+        dtype = "bf16 I/O, fp32 math and states" if ab == 2 else "f32"
         names = ("k_scan2d_fwd", "k_scan2d_bwd")
         grads = [(dA, 2 * Dc * Nn)]
         workload = (f"config4: 2D selective scan 256x256, batch {gbatch} ({bsz} per GPU), D 256, "
-                    "N 16, fp32, "
-                    "B/C shared, dt = softplus(N(0,1)-2) + ln 2 on both axes, fwd+bwd "
+                    + ("N 16, bf16 tensors (fp32 A, dA, h), " if ab == 2 else "N 16, fp32, ")
+                    + "B/C shared, dt = softplus(N(0,1)-2) + ln 2 on both axes, fwd+bwd "
                     "(stored-state kernels of the reference API)")
         metric = "scan HBM GB/s (algorithmic bytes / device time), 2D selective scan fwd+bwd"
     def exchange():
@@ -856,7 +862,7 @@ def main():
     ap.add_argument("--dim", type=int, default=None,
                     help="nd5 only: channels (default 1024; smaller for profiling captures)")
     ap.add_argument("--io", choices=["f32", "bf16"], default="f32",
-                    help="conv3 only: activation element type of the ConvND calls")
+                    help="conv3 / scan2d4: element type of the activation / scan tensors")
     ap.add_argument("--layers", type=int, default=24, help="nd5model only: ND blocks")
     ap.add_argument("--nd-side", type=int, default=64, help="nd5model only: volume side")
     ap.add_argument("--shard-batch", action="store_true",

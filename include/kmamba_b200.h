@@ -223,6 +223,19 @@ typedef struct {
 int kmb_scannd_fwd(const KmbScanND *args);
 int kmb_scannd_bwd(const KmbScanND *args);
 
+/*
+ * bf16-I/O variants (no reference counterpart beyond the truncating host
+ * conversions of include/kmamba_mixed_precision.h:106-112): x, delta, B,
+ * C, y, dy, dx, ddelta, dB and dC point to bf16 (rounded to nearest even
+ * on output); A, dA and h stay fp32; arithmetic is fp32.  Device memory
+ * only.  Two axes with channel-shared B/C, M = 8 or 16 and D a multiple of
+ * 8 (the config-4 layout) run the 2D wavefront kernels on bf16 tensors
+ * directly (16-byte aligned inputs); other shapes convert the bf16
+ * tensors to pooled fp32 scratch around the fp32 kernels.
+ */
+int kmb_scannd_fwd_bf16(const KmbScanND *args);
+int kmb_scannd_bwd_bf16(const KmbScanND *args);
+
 /* ------------------------------------------------------------------ */
 /* bf16 GEMM on the tensor cores (block projections)                   */
 /* ------------------------------------------------------------------ */

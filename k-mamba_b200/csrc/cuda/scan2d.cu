@@ -38,6 +38,8 @@
 
 #include <type_traits>
 
+#include <cuda_bf16.h>
+
 #include "kmb_common.cuh"
 #include "../kmb_internal.h"
 
@@ -57,6 +59,41 @@ constexpr int kSlotX = kCPW * kCh;
 constexpr int kSlotB = kCPW * 16;
 constexpr int kSlotE = 128;
 constexpr int kSlot = 3 * kSlotX + 2 * kSlotB + kSlotE;
+
+/* The same slot with inputs of element type T (fp32, or bf16 for the
+ * bf16-I/O entry points), offsets in floats: x / delta_0 / delta_1 regions
+ * of X floats, B / C regions of Bn floats, then the fp32 edge column. */
+template <typename T> struct FL {
+    static constexpr int X = kSlotX * (int)sizeof(T) / 4;
+    static constexpr int Bn = kSlotB * (int)sizeof(T) / 4;
+    static constexpr int E0 = 3 * X + 2 * Bn;
+    static constexpr int SLOT = E0 + kSlotE;
+};
+static_assert(FL<float>::SLOT == kSlot, "fp32 forward slot layout");
+
+/* Element idx of a staged region of T, as float. */
+template <typename T> __device__ __forceinline__ float ldT(const float *region, int idx) {
+    if constexpr (sizeof(T) == 4) return region[idx];
+    else return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(region)[idx]);
+}
+
+/* Elements idx .. idx + 3 (idx a multiple of 4) of a staged region of T. */
+template <typename T> __device__ __forceinline__ float4 ld4T(const float *region, int idx) {
+    if constexpr (sizeof(T) == 4) {
+        return *reinterpret_cast<const float4 *>(region + idx);
+    } else {
+        const uint2 u = *reinterpret_cast<const uint2 *>(
+            reinterpret_cast<const __nv_bfloat16 *>(region) + idx);
+        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.x));
+        const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.y));
+        return make_float4(a.x, a.y, b.x, b.y);
+    }
+}
+
+template <typename T> __device__ __forceinline__ void stT(T *dst, float v) {
+    if constexpr (sizeof(T) == 4) *dst = v;
+    else *dst = __float2bfloat16_rn(v);
+}
 
 struct S2D {
     const float *x, *d0, *d1, *A0, *A1, *B, *C, *dy, *h;
@@ -101,37 +138,47 @@ __device__ __forceinline__ void exp2_decay_point(const float2 (&w)[4], float2 (&
  * so the source pointer at row 0, the row stride and the column validity
  * are fixed for a strip. */
 struct FwdCopies {
-    const float *src[4]; /* source of the next row staged */
-    long rs[4];          /* row stride (x / delta rows: W*D; B / C rows: W*M) */
-    int dst[4];
+    const char *src[4]; /* source of the next row staged */
+    long rs[4];         /* row stride in bytes (x / delta rows: W*D; B / C rows: W*M elements) */
+    int dst[4];         /* destination in floats from the slot start */
     bool ok[4];
 };
 
+/* fp32: x / delta_0 / delta_1 rows are 8 columns x 8 channels = 16 chunks
+ * of 16 bytes each, B / C rows 8 columns x 16 states = 32 chunks each (112
+ * in all); bf16: 8 and 16 chunks (56 in all).  Chunk e goes to lane e % 32. */
+template <typename T>
 __device__ __forceinline__ void fwd_copies(const S2D &p, long b, long j0, long dch0, int lane,
                                            FwdCopies &f) {
+    using L = FL<T>;
+    constexpr int ES = (int)sizeof(T), EPC = 16 / ES;       /* elements per chunk */
+    constexpr int XC = kCh / EPC;                            /* chunks per column of x */
+    constexpr int BC = 16 / EPC;                             /* chunks per column of B */
+    constexpr int NX = 3 * kCPW * XC, NB = 2 * kCPW * BC;
     const long W = p.W, D = p.D, M = p.M;
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
         const int e = lane + 32 * u;
-        if (e < 48) {
-            const int t = e / 16, r = e % 16, col = r / 2, half = r % 2;
+        if (e < NX) {
+            const int t = e / (kCPW * XC), r = e % (kCPW * XC), col = r / XC, part = r % XC;
             const long j = j0 + col;
-            const float *base = t == 0 ? p.x + b * p.H * W * D
-                                       : (t == 1 ? p.d0 : p.d1) + b * p.dl_bs;
-            f.src[u] = base + j * D + dch0 + half * 4;
-            f.rs[u] = W * D;
-            f.dst[u] = t * kSlotX + col * kCh + half * 4;
+            const T *base = t == 0 ? reinterpret_cast<const T *>(p.x) + b * p.H * W * D
+                                   : reinterpret_cast<const T *>(t == 1 ? p.d0 : p.d1) + b * p.dl_bs;
+            f.src[u] = reinterpret_cast<const char *>(base + j * D + dch0 + part * EPC);
+            f.rs[u] = W * D * ES;
+            f.dst[u] = t * L::X + (col * kCh + part * EPC) * ES / 4;
             f.ok[u] = j < W;
-        } else if (e < 112) {
-            const int e2 = e - 48, t = e2 / (kCPW * 4), r = e2 % (kCPW * 4);
-            const int col = r / 4, q = r % 4;
+        } else if (e < NX + NB) {
+            const int e2 = e - NX, t = e2 / (kCPW * BC), r = e2 % (kCPW * BC);
+            const int col = r / BC, q = r % BC;
             const long j = j0 + col;
-            f.src[u] = (t == 0 ? p.B : p.C) + b * p.H * W * M + j * M + q * 4;
-            f.rs[u] = W * M;
-            f.dst[u] = 3 * kSlotX + t * kSlotB + col * 16 + q * 4;
-            f.ok[u] = j < W && q * 4 < M;
+            const T *base = reinterpret_cast<const T *>(t == 0 ? p.B : p.C) + b * p.H * W * M;
+            f.src[u] = reinterpret_cast<const char *>(base + j * M + q * EPC);
+            f.rs[u] = W * M * ES;
+            f.dst[u] = 3 * L::X + t * L::Bn + (col * 16 + q * EPC) * ES / 4;
+            f.ok[u] = j < W && q * EPC < M;
         } else {
-            f.src[u] = p.x;
+            f.src[u] = reinterpret_cast<const char *>(p.x);
             f.rs[u] = 0;
             f.dst[u] = -1;
             f.ok[u] = false;
@@ -141,23 +188,27 @@ __device__ __forceinline__ void fwd_copies(const S2D &p, long b, long j0, long d
 
 /* stages row i (rows are staged in order 0, 1, 2, ... once each: the
  * sources then move one row down) */
+template <typename T>
 __device__ __forceinline__ void stage_row_fast(const S2D &p, FwdCopies &f, long i, float *s,
                                                int lane, const float *edge_row) {
     const bool rok = i >= 0 && i < p.H;
     if (edge_row)
-        kmb_cp_async16(s + 3 * kSlotX + 2 * kSlotB + lane * 4, rok ? edge_row + lane * 4 : p.x,
+        kmb_cp_async16(s + FL<T>::E0 + lane * 4, rok ? edge_row + lane * 4 : p.x,
                        rok ? 16 : 0);
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
         if (f.dst[u] >= 0) {
             const bool ok = rok && f.ok[u];
-            kmb_cp_async16(s + f.dst[u], ok ? f.src[u] : p.x, ok ? 16 : 0);
+            kmb_cp_async16(s + f.dst[u], ok ? (const void *)f.src[u] : (const void *)p.x,
+                           ok ? 16 : 0);
             f.src[u] += f.rs[u];
         }
     }
 }
 
+template <typename T>
 __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_fwd(S2D p) {
+    using L = FL<T>;
     extern __shared__ __align__(16) float sm[];
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const int c = lane >> 2, q = lane & 3;
@@ -166,8 +217,8 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_fwd(S2D p) {
     const long d = dch0 + c;
     const long H = p.H, W = p.W, D = p.D, M = p.M;
     const bool qok = q * 4 < M;
-    float *ring = sm + w * kRing * kSlot;                      /* this warp's rows */
-    float *xbuf = sm + kWarps * kRing * kSlot;                 /* [warp][2][32][4] */
+    float *ring = sm + w * kRing * L::SLOT;                    /* this warp's rows */
+    float *xbuf = sm + kWarps * kRing * L::SLOT;               /* [warp][2][32][4] */
     float *edge = p.edge + ((long)blockIdx.y * gridDim.x + blockIdx.x) * H * 128;
 
     float2 A0p[2], A1p[2];
@@ -183,7 +234,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_fwd(S2D p) {
     const long nstrips = (W + kStrip - 1) / kStrip;
     const long nsteps = H + kWarps - 1;
     float *hb = p.hout + b * H * W * D * M;
-    float *yb = p.y + b * H * W * D;
+    T *yb = reinterpret_cast<T *>(p.y) + b * H * W * D;
 
     for (long sidx = 0; sidx < nstrips; ++sidx) {
         const long j0 = sidx * kStrip + w * kCPW; /* this warp's first column */
@@ -195,11 +246,11 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_fwd(S2D p) {
         const bool use_edge = w == 0 && sidx > 0;
         auto edge_row = [&](long r) { return use_edge ? edge + r * 128 : nullptr; };
         FwdCopies fc;
-        fwd_copies(p, b, j0, dch0, lane, fc);
+        fwd_copies<T>(p, b, j0, dch0, lane, fc);
         /* h and y of this warp's first column at row 0; a row is W*D*M
          * (W*D) floats further */
         float *hcol = hb + (j0 * D + d) * M + q * 4;
-        float *ycol = yb + j0 * D + d;
+        T *ycol = yb + j0 * D + d;
         const long hrow = W * D * M, yrow = W * D;
         const int hcolst = (int)(D * M), ycolst = (int)D; /* one column further */
         /* every column of this warp inside the grid and every lane's states
@@ -208,7 +259,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_fwd(S2D p) {
         /* prologue: rows 0 .. kRing-2 of this warp */
 #pragma unroll
         for (int r = 0; r < kRing - 1; ++r) {
-            stage_row_fast(p, fc, r, ring + r * kSlot, lane, edge_row(r));
+            stage_row_fast<T>(p, fc, r, ring + r * L::SLOT, lane, edge_row(r));
             kmb_cp_async_commit();
         }
         int slot = 0; /* i % kRing once i >= 0 */
@@ -218,13 +269,14 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_fwd(S2D p) {
              * kRing - 1 came with the prologue.  One commit per step keeps
              * the group count uniform. */
             if (i >= 0)
-                stage_row_fast(p, fc, i + kRing - 1, ring + (slot == 0 ? kRing - 1 : slot - 1) * kSlot,
-                               lane, edge_row(i + kRing - 1));
+                stage_row_fast<T>(p, fc, i + kRing - 1,
+                                  ring + (slot == 0 ? kRing - 1 : slot - 1) * L::SLOT, lane,
+                                  edge_row(i + kRing - 1));
             kmb_cp_async_commit();
             kmb_cp_async_wait<kRing - 1>();
             __syncwarp();
             if (i >= 0 && i < H) {
-                const float *s = ring + slot * kSlot;
+                const float *s = ring + slot * L::SLOT;
                 /* left neighbour of column j0 at row i */
                 float2 hl[2];
                 if (w > 0) {
@@ -233,7 +285,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_fwd(S2D p) {
                     hl[0] = kmb_f2(v.x, v.y);
                     hl[1] = kmb_f2(v.z, v.w);
                 } else if (use_edge) {
-                    const float4 v = *reinterpret_cast<const float4 *>(s + 3 * kSlotX + 2 * kSlotB + lane * 4);
+                    const float4 v = *reinterpret_cast<const float4 *>(s + L::E0 + lane * 4);
                     hl[0] = kmb_f2(v.x, v.y);
                     hl[1] = kmb_f2(v.z, v.w);
                 } else {
@@ -241,18 +293,18 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_fwd(S2D p) {
                 }
                 /* this step's row of h / y (32-bit column offsets below) */
                 float *const hrowp = hcol + i * hrow;
-                float *const yrowp = ycol + i * yrow;
+                T *const yrowp = ycol + i * yrow;
                 auto points = [&](auto full_tag) {
                 constexpr bool FULL = decltype(full_tag)::value;
                 float yq[4];
 #pragma unroll
                 for (int k = 0; k < kCPW; ++k) {
                     const long j = j0 + k;
-                    const float xv = s[k * kCh + c];
-                    const float dv0 = s[kSlotX + k * kCh + c];
-                    const float dv1 = s[2 * kSlotX + k * kCh + c];
-                    const float4 B4 = *reinterpret_cast<const float4 *>(s + 3 * kSlotX + k * 16 + q * 4);
-                    const float4 C4 = *reinterpret_cast<const float4 *>(s + 3 * kSlotX + kSlotB + k * 16 + q * 4);
+                    const float xv = ldT<T>(s, k * kCh + c);
+                    const float dv0 = ldT<T>(s + L::X, k * kCh + c);
+                    const float dv1 = ldT<T>(s + 2 * L::X, k * kCh + c);
+                    const float4 B4 = ld4T<T>(s + 3 * L::X, k * 16 + q * 4);
+                    const float4 C4 = ld4T<T>(s + 3 * L::X + L::Bn, k * 16 + q * 4);
                     const float2 dtx2 = kmb_f2s((dv0 + dv1) / 2.0f * xv); /* dt_bar x */
                     const float2 dv02 = kmb_f2s(dv0), dv12 = kmb_f2s(dv1);
                     const float2 Bp[2] = {kmb_f2(B4.x, B4.y), kmb_f2(B4.z, B4.w)};
@@ -289,7 +341,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_fwd(S2D p) {
                             }
                         }
                         const long jy = j0 + (k - 3) + q;
-                        if (FULL || jy < W) yrowp[((k - 3) + q) * ycolst] = yq[0];
+                        if (FULL || jy < W) stT<T>(yrowp + ((k - 3) + q) * ycolst, yq[0]);
                     }
                 }
                 };
@@ -326,6 +378,19 @@ constexpr int kBL = kCh * 16;
 constexpr int kBE = 128;
 constexpr int kBSlot = 4 * kBX + 2 * kBB + kBH + kBL + kBE;
 
+/* The backward slot with inputs of element type T, offsets in floats:
+ * x / delta_0 / delta_1 / dy regions of X floats, B / C regions of Bn,
+ * then the fp32 h rows (H0), left h column (L0) and edge carry (E0). */
+template <typename T> struct BL {
+    static constexpr int X = kBX * (int)sizeof(T) / 4;
+    static constexpr int Bn = kBB * (int)sizeof(T) / 4;
+    static constexpr int H0 = 4 * X + 2 * Bn;
+    static constexpr int L0 = H0 + kBH;
+    static constexpr int E0 = L0 + kBL;
+    static constexpr int SLOT = E0 + kBE;
+};
+static_assert(BL<float>::SLOT == kBSlot, "fp32 backward slot layout");
+
 /* The backward's copies of one staged row, per lane, fixed for a strip:
  * one chunk of x / delta_0 / delta_1 / dy (lane / 8 picks the tensor), one
  * of B / C (lane / 16), and five of h: h(i-1, j0 + u) for u < 4 and
@@ -333,44 +398,57 @@ constexpr int kBSlot = 4 * kBX + 2 * kBB + kBH + kBL + kBE;
  * Sources are kept at row 0; a row further is W*D (inputs), W*M (B, C)
  * or W*D*M (h) floats. */
 struct BwdCopies {
-    const float *in, *bc, *h; /* sources at the next row staged */
-    int in_rs, bc_rs, h_rs;   /* row strides: W*D, W*M, W*D*M floats */
+    const char *in, *bc;      /* sources at the next row staged */
+    const float *h;
+    long in_rs, bc_rs;        /* row strides in bytes: W*D, W*M elements */
+    int h_rs;                 /* W*D*M floats */
     int h_col;                /* one column of h: D*M floats */
-    int in_dst, bc_dst;
+    int in_dst, bc_dst;       /* floats from the slot start; -1: no chunk */
     bool in_ok, bc_ok;
     unsigned h_ok; /* bit u: column of h chunk u inside the grid and q*4 < M */
 };
 
+/* Per lane one 16-byte chunk of the x / delta / dy rows (fp32: 4 tensors x
+ * 4 columns x 2 chunks; bf16: 4 x 4 x 1, lanes 0-15), one of the B / C rows
+ * (fp32: 2 x 4 columns x 4 chunks; bf16: 2 x 4 x 2, lanes 0-15) and five of
+ * h (fp32 always). */
+template <typename T>
 __device__ __forceinline__ void bwd_copies(const S2D &p, long b, long j0, long dch0, int lane,
                                            BwdCopies &f) {
+    using L = BL<T>;
+    constexpr int ES = (int)sizeof(T), EPC = 16 / ES;
+    constexpr int XC = kCh / EPC, BC = 16 / EPC;
     const long H = p.H, W = p.W, D = p.D, M = p.M;
     {
-        const int t = lane / 8, r = lane % 8, col = r / 2, half = r % 2;
+        const int t = lane / (kBCPW * XC), r = lane % (kBCPW * XC), col = r / XC, part = r % XC;
         const long j = j0 + col;
-        const float *base = t == 0   ? p.x + b * H * W * D
-                            : t == 1 ? p.d0 + b * p.dl_bs
-                            : t == 2 ? p.d1 + b * p.dl_bs
-                                     : p.dy + b * H * W * D;
-        f.in = base + j * D + dch0 + half * 4;
-        f.in_dst = t * kBX + col * kCh + half * 4;
-        f.in_ok = j < W;
+        const T *base = t == 0   ? reinterpret_cast<const T *>(p.x) + b * H * W * D
+                        : t == 1 ? reinterpret_cast<const T *>(p.d0) + b * p.dl_bs
+                        : t == 2 ? reinterpret_cast<const T *>(p.d1) + b * p.dl_bs
+                                 : reinterpret_cast<const T *>(p.dy) + b * H * W * D;
+        const bool live = lane < 4 * kBCPW * XC;
+        f.in = reinterpret_cast<const char *>(base + j * D + dch0 + part * EPC);
+        f.in_dst = live ? t * L::X + (col * kCh + part * EPC) * ES / 4 : -1;
+        f.in_ok = live && j < W;
     }
     {
-        const int t = lane / 16, r = lane % 16, col = r / 4, q = r % 4;
+        const int t = lane / (kBCPW * BC), r = lane % (kBCPW * BC), col = r / BC, q = r % BC;
         const long j = j0 + col;
-        f.bc = (t == 0 ? p.B : p.C) + b * H * W * M + j * M + q * 4;
-        f.bc_dst = 4 * kBX + t * kBB + col * 16 + q * 4;
-        f.bc_ok = j < W && q * 4 < M;
+        const bool live = lane < 2 * kBCPW * BC;
+        f.bc = reinterpret_cast<const char *>(reinterpret_cast<const T *>(t == 0 ? p.B : p.C) +
+                                              b * H * W * M + j * M + q * EPC);
+        f.bc_dst = live ? 4 * L::X + t * L::Bn + (col * 16 + q * EPC) * ES / 4 : -1;
+        f.bc_ok = live && j < W && q * EPC < M;
     }
     const int ch = lane / 4, q = lane % 4;
     f.h = p.h + b * H * W * D * M + (j0 * D + dch0 + ch) * M + q * 4;
-    f.in_rs = (int)(W * D);
-    f.bc_rs = (int)(W * M);
+    f.in_rs = W * D * ES;
+    f.bc_rs = W * M * ES;
     f.h_rs = (int)(W * D * M);
     f.h_col = (int)(D * M);
     /* rows are staged from the last one up */
-    f.in += (H - 1) * W * D;
-    f.bc += (H - 1) * W * M;
+    f.in += (H - 1) * f.in_rs;
+    f.bc += (H - 1) * f.bc_rs;
     f.h += (H - 1) * W * D * M;
     f.h_ok = 0;
 #pragma unroll
@@ -384,31 +462,32 @@ __device__ __forceinline__ void bwd_copies(const S2D &p, long b, long j0, long d
  * row i-1 for the same columns and h(i, j0-1); zero outside the grid.
  * Rows are staged in order H-1, H-2, ... once each: the sources then move
  * one row up. */
+template <typename T>
 __device__ __forceinline__ void stage_row_bwd_fast(const S2D &p, BwdCopies &f, long i, float *s,
                                                    int lane, const float *edge_row) {
+    using L = BL<T>;
     const bool rok = i >= 0 && i < p.H;
     if (edge_row)
-        kmb_cp_async16(s + 4 * kBX + 2 * kBB + kBH + kBL + lane * 4,
-                       rok ? edge_row + lane * 4 : p.x, rok ? 16 : 0);
-    {
+        kmb_cp_async16(s + L::E0 + lane * 4, rok ? edge_row + lane * 4 : p.x, rok ? 16 : 0);
+    if (sizeof(T) == 4 || f.in_dst >= 0) {
         const bool ok = rok && f.in_ok;
-        kmb_cp_async16(s + f.in_dst, ok ? f.in : p.x, ok ? 16 : 0);
+        kmb_cp_async16(s + f.in_dst, ok ? (const void *)f.in : (const void *)p.x, ok ? 16 : 0);
     }
-    {
+    if (sizeof(T) == 4 || f.bc_dst >= 0) {
         const bool ok = rok && f.bc_ok;
-        kmb_cp_async16(s + f.bc_dst, ok ? f.bc : p.x, ok ? 16 : 0);
+        kmb_cp_async16(s + f.bc_dst, ok ? (const void *)f.bc : (const void *)p.x, ok ? 16 : 0);
     }
     const int ch = lane / 4, q = lane % 4;
     const float *hup = f.h - f.h_rs;
 #pragma unroll
     for (int u = 0; u < kBCPW; ++u) {
         const bool ok = rok && i >= 1 && ((f.h_ok >> u) & 1);
-        kmb_cp_async16(s + 4 * kBX + 2 * kBB + (u * kCh + ch) * 16 + q * 4,
+        kmb_cp_async16(s + L::H0 + (u * kCh + ch) * 16 + q * 4,
                        ok ? hup + u * f.h_col : p.x, ok ? 16 : 0);
     }
     {
         const bool ok = rok && ((f.h_ok >> kBCPW) & 1);
-        kmb_cp_async16(s + 4 * kBX + 2 * kBB + kBH + ch * 16 + q * 4,
+        kmb_cp_async16(s + L::L0 + ch * 16 + q * 4,
                        ok ? f.h - f.h_col : p.x, ok ? 16 : 0);
     }
     f.in -= f.in_rs;
@@ -434,7 +513,9 @@ __device__ __forceinline__ float rs8_channels(float (&v)[8], int lane) {
     return v[0];
 }
 
+template <typename T>
 __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_bwd(S2D p) {
+    using L = BL<T>;
     extern __shared__ __align__(16) float sm[];
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const int c = lane >> 2, q = lane & 3;
@@ -443,8 +524,8 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_bwd(S2D p) {
     const long d = dch0 + c;
     const long H = p.H, W = p.W, D = p.D, M = p.M;
     const bool qok = q * 4 < M;
-    float *ring = sm + w * kBRing * kBSlot;
-    float *xbuf = sm + kWarps * kBRing * kBSlot; /* [warp][2][32][4] */
+    float *ring = sm + w * kBRing * L::SLOT;
+    float *xbuf = sm + kWarps * kBRing * L::SLOT; /* [warp][2][32][4] */
     float *edge = p.edge + ((long)blockIdx.y * gridDim.x + blockIdx.x) * H * 128;
 
     float2 A0p[2], A1p[2], dA0[2], dA1[2];
@@ -461,9 +542,9 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_bwd(S2D p) {
     const long nstrips = (W + kBStrip - 1) / kBStrip;
     const long nsteps = H + kWarps - 1;
     const float *hb = p.h + b * H * W * D * M;
-    float *dxb = p.dx + b * H * W * D;
-    float *dd0b = p.dd0 + b * p.dl_bs;
-    float *dd1b = p.dd1 + b * p.dl_bs;
+    T *dxb = reinterpret_cast<T *>(p.dx) + b * H * W * D;
+    T *dd0b = reinterpret_cast<T *>(p.dd0) + b * p.dl_bs;
+    T *dd1b = reinterpret_cast<T *>(p.dd1) + b * p.dl_bs;
     float *dBb = p.dB + b * H * W * M;
     float *dCb = p.dC + b * H * W * M;
     const int lead = kWarps - 1 - w; /* steps this warp runs behind the leader */
@@ -493,11 +574,11 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_bwd(S2D p) {
          * inside M: the per-point guards are all true */
         const bool full = j0 + kBCPW <= W && M == 16;
         BwdCopies bc;
-        bwd_copies(p, b, j0, dch0, lane, bc);
+        bwd_copies<T>(p, b, j0, dch0, lane, bc);
         /* prologue: the first kBRing-1 rows this warp will run (H-1, H-2, ..) */
 #pragma unroll
         for (int r = 0; r < kBRing - 1; ++r) {
-            stage_row_bwd_fast(p, bc, H - 1 - r, ring + r * kBSlot, lane, edge_row(H - 1 - r));
+            stage_row_bwd_fast<T>(p, bc, H - 1 - r, ring + r * L::SLOT, lane, edge_row(H - 1 - r));
             kmb_cp_async_commit();
         }
         int slot = 0; /* n % kBRing once n >= 0 */
@@ -505,16 +586,16 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_bwd(S2D p) {
             const long n = t - lead; /* rows this warp has done before this step */
             if (n >= 0) {
                 const long nr = n + kBRing - 1;
-                stage_row_bwd_fast(p, bc, H - 1 - nr,
-                                   ring + (slot == 0 ? kBRing - 1 : slot - 1) * kBSlot, lane,
-                                   edge_row(H - 1 - nr));
+                stage_row_bwd_fast<T>(p, bc, H - 1 - nr,
+                                      ring + (slot == 0 ? kBRing - 1 : slot - 1) * L::SLOT, lane,
+                                      edge_row(H - 1 - nr));
             }
             kmb_cp_async_commit();
             kmb_cp_async_wait<kBRing - 1>();
             __syncwarp();
             const long i = row_of(t);
             if (n >= 0 && i >= 0) {
-                const float *s = ring + slot * kBSlot;
+                const float *s = ring + slot * L::SLOT;
                 /* carry from the right neighbour column: e1(p+1) G(p+1) */
                 float2 qh[2];
                 if (w < kWarps - 1) {
@@ -523,8 +604,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_bwd(S2D p) {
                     qh[0] = kmb_f2(v.x, v.y);
                     qh[1] = kmb_f2(v.z, v.w);
                 } else if (use_edge) {
-                    const float4 v = *reinterpret_cast<const float4 *>(
-                        s + 4 * kBX + 2 * kBB + kBH + kBL + lane * 4);
+                    const float4 v = *reinterpret_cast<const float4 *>(s + L::E0 + lane * 4);
                     qh[0] = kmb_f2(v.x, v.y);
                     qh[1] = kmb_f2(v.z, v.w);
                 } else {
@@ -533,27 +613,27 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_bwd(S2D p) {
                 /* offsets of (i, j0): channel d in [P, D] tensors, states
                  * 4q.. in [P, M] ones */
                 const long ox = (i * W + j0) * D + d, obc = (i * W + j0) * M + q * 4;
-                float *const dxr = dxb + ox, *const dd0r = dd0b + ox, *const dd1r = dd1b + ox;
+                T *const dxr = dxb + ox, *const dd0r = dd0b + ox, *const dd1r = dd1b + ox;
                 auto points = [&](auto full_tag) {
                 constexpr bool FULL = decltype(full_tag)::value;
 #pragma unroll
                 for (int k = kBCPW - 1; k >= 0; --k) {
                     const long j = j0 + k;
-                    const float xv = s[k * kCh + c];
-                    const float dv0 = s[kBX + k * kCh + c];
-                    const float dv1 = s[2 * kBX + k * kCh + c];
-                    const float gy = s[3 * kBX + k * kCh + c];
-                    const float4 B4 = *reinterpret_cast<const float4 *>(s + 4 * kBX + k * 16 + q * 4);
-                    const float4 C4 = *reinterpret_cast<const float4 *>(s + 4 * kBX + kBB + k * 16 + q * 4);
+                    const float xv = ldT<T>(s, k * kCh + c);
+                    const float dv0 = ldT<T>(s + L::X, k * kCh + c);
+                    const float dv1 = ldT<T>(s + 2 * L::X, k * kCh + c);
+                    const float gy = ldT<T>(s + 3 * L::X, k * kCh + c);
+                    const float4 B4 = ld4T<T>(s + 4 * L::X, k * 16 + q * 4);
+                    const float4 C4 = ld4T<T>(s + 4 * L::X + L::Bn, k * 16 + q * 4);
                     const float4 H0 = *reinterpret_cast<const float4 *>(
-                        s + 4 * kBX + 2 * kBB + (k * kCh + c) * 16 + q * 4); /* h(i-1, j) */
+                        s + L::H0 + (k * kCh + c) * 16 + q * 4); /* h(i-1, j) */
                     float2 hl[2]; /* h(i, j-1) */
                     if (k > 0) {
                         hl[0] = hc[k > 0 ? k - 1 : 0][0];
                         hl[1] = hc[k > 0 ? k - 1 : 0][1];
                     } else {
                         const float4 v = *reinterpret_cast<const float4 *>(
-                            s + 4 * kBX + 2 * kBB + kBH + c * 16 + q * 4);
+                            s + L::L0 + c * 16 + q * 4);
                         hl[0] = kmb_f2(v.x, v.y);
                         hl[1] = kmb_f2(v.z, v.w);
                     }
@@ -615,9 +695,9 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_bwd(S2D p) {
                     const float r4 = __shfl_down_sync(kFull, r1, 12);
                     if (FULL || j < W) {
                         if (q == 0) {
-                            dxr[k * D] = sx;
-                            dd0r[k * D] = s0 * KMB_LN2 + sb / 2.0f;
-                            dd1r[k * D] = s1 * KMB_LN2 + sb / 2.0f;
+                            stT<T>(dxr + k * D, sx);
+                            stT<T>(dd0r + k * D, s0 * KMB_LN2 + sb / 2.0f);
+                            stT<T>(dd1r + k * D, s1 * KMB_LN2 + sb / 2.0f);
                         }
                         if ((c & 3) == 0 && (FULL || qok)) {
                             float *dst = ((c >> 2) ? dCb : dBb) + obc + k * M;
@@ -637,7 +717,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_bwd(S2D p) {
 #pragma unroll
                 for (int k = 0; k < kBCPW; ++k) {
                     const float4 v = *reinterpret_cast<const float4 *>(
-                        s + 4 * kBX + 2 * kBB + (k * kCh + c) * 16 + q * 4);
+                        s + L::H0 + (k * kCh + c) * 16 + q * 4);
                     hc[k][0] = kmb_f2(v.x, v.y);
                     hc[k][1] = kmb_f2(v.z, v.w);
                 }
@@ -690,7 +770,15 @@ extern "C" size_t kmb_scan2d_scratch_elems(const KmbNDLaunch *a) {
     return (size_t)a->batch * (a->D / kCh) * a->dims[0] * 128;
 }
 
-extern "C" int kmb_launch_scan2d_fwd(const KmbNDLaunch *a, cudaStream_t s) {
+namespace {
+
+__global__ void k_f32_to_bf16_2d(const float *src, __nv_bfloat16 *dst, long n) {
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+        dst[i] = __float2bfloat16_rn(src[i]);
+}
+
+template <typename T>
+int launch_fwd(const KmbNDLaunch *a, cudaStream_t s) {
     if (!kmb_scan2d_supported(a)) return kmb_fail(KMB_EUNSUPPORTED, "scan2d: unsupported shape");
     if (!a->scratch || a->scratch_elems < kmb_scan2d_scratch_elems(a))
         return kmb_fail(KMB_EINVAL, "scan2d: scratch too small");
@@ -698,18 +786,21 @@ extern "C" int kmb_launch_scan2d_fwd(const KmbNDLaunch *a, cudaStream_t s) {
     p.hout = a->h;
     p.y = a->y;
     p.edge = a->scratch;
-    const size_t smem = sizeof(float) * ((size_t)kWarps * kRing * kSlot + kWarps * 2 * 32 * 4);
-    cudaError_t e = cudaFuncSetAttribute(k_scan2d_fwd, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    const size_t smem = sizeof(float) * ((size_t)kWarps * kRing * FL<T>::SLOT + kWarps * 2 * 32 * 4);
+    cudaError_t e = cudaFuncSetAttribute(k_scan2d_fwd<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e == cudaSuccess) {
         dim3 grid((unsigned)(a->D / kCh), (unsigned)a->batch);
-        k_scan2d_fwd<<<grid, kWarps * 32, smem, s>>>(p);
+        k_scan2d_fwd<T><<<grid, kWarps * 32, smem, s>>>(p);
         e = cudaGetLastError();
     }
     return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "scan2d forward");
 }
 
-extern "C" int kmb_launch_scan2d_bwd(const KmbNDLaunch *a, cudaStream_t s) {
+/* dB32 / dC32: the fp32 buffers the channel sums are accumulated in (the
+ * outputs themselves for fp32). */
+template <typename T>
+int launch_bwd(const KmbNDLaunch *a, float *dB32, float *dC32, cudaStream_t s) {
     if (!kmb_scan2d_supported(a)) return kmb_fail(KMB_EUNSUPPORTED, "scan2d: unsupported shape");
     if (!a->scratch || a->scratch_elems < kmb_scan2d_scratch_elems(a))
         return kmb_fail(KMB_EINVAL, "scan2d: scratch too small");
@@ -721,21 +812,77 @@ extern "C" int kmb_launch_scan2d_bwd(const KmbNDLaunch *a, cudaStream_t s) {
     p.dd1 = a->ddelta[1];
     p.dA0 = a->dA[0];
     p.dA1 = a->dA[1];
-    p.dB = a->dB;
-    p.dC = a->dC;
+    p.dB = dB32;
+    p.dC = dC32;
     cudaError_t e = cudaMemsetAsync(a->dA[0], 0, sizeof(float) * a->D * a->M, s);
     if (e == cudaSuccess) e = cudaMemsetAsync(a->dA[1], 0, sizeof(float) * a->D * a->M, s);
     const size_t nb = sizeof(float) * a->batch * a->P * a->M;
-    if (e == cudaSuccess) e = cudaMemsetAsync(a->dB, 0, nb, s);
-    if (e == cudaSuccess) e = cudaMemsetAsync(a->dC, 0, nb, s);
-    const size_t smem = sizeof(float) * ((size_t)kWarps * kBRing * kBSlot + kWarps * 2 * 32 * 4);
+    if (e == cudaSuccess) e = cudaMemsetAsync(dB32, 0, nb, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(dC32, 0, nb, s);
+    const size_t smem = sizeof(float) * ((size_t)kWarps * kBRing * BL<T>::SLOT + kWarps * 2 * 32 * 4);
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(k_scan2d_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        e = cudaFuncSetAttribute(k_scan2d_bwd<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)smem);
     if (e == cudaSuccess) {
         dim3 grid((unsigned)(a->D / kCh), (unsigned)a->batch);
-        k_scan2d_bwd<<<grid, kWarps * 32, smem, s>>>(p);
+        k_scan2d_bwd<T><<<grid, kWarps * 32, smem, s>>>(p);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess && sizeof(T) == 2) {
+        const long n = a->batch * a->P * a->M;
+        const unsigned blocks = (unsigned)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+        k_f32_to_bf16_2d<<<blocks, 256, 0, s>>>(dB32, reinterpret_cast<__nv_bfloat16 *>(a->dB), n);
+        k_f32_to_bf16_2d<<<blocks, 256, 0, s>>>(dC32, reinterpret_cast<__nv_bfloat16 *>(a->dC), n);
         e = cudaGetLastError();
     }
     return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "scan2d backward");
+}
+
+} // namespace
+
+extern "C" int kmb_launch_scan2d_fwd(const KmbNDLaunch *a, cudaStream_t s) {
+    return launch_fwd<float>(a, s);
+}
+
+extern "C" int kmb_launch_scan2d_bwd(const KmbNDLaunch *a, cudaStream_t s) {
+    return launch_bwd<float>(a, a->dB, a->dC, s);
+}
+
+/* bf16 tensors: the 16-byte staging chunks hold 8 states, so M must be 8
+ * or 16. */
+extern "C" int kmb_scan2d_bf16_supported(const KmbNDLaunch *a) {
+    return kmb_scan2d_supported(a) && a->M % 8 == 0;
+}
+
+extern "C" int kmb_launch_scan2d_fwd_bf16(const KmbNDLaunch *a, cudaStream_t s) {
+    if (!kmb_scan2d_bf16_supported(a)) return kmb_fail(KMB_EUNSUPPORTED, "scan2d bf16: unsupported shape");
+    return launch_fwd<__nv_bfloat16>(a, s);
+}
+
+extern "C" int kmb_launch_scan2d_bwd_bf16(const KmbNDLaunch *a, float *dB32, float *dC32,
+                                          cudaStream_t s) {
+    if (!kmb_scan2d_bf16_supported(a)) return kmb_fail(KMB_EUNSUPPORTED, "scan2d bf16: unsupported shape");
+    return launch_bwd<__nv_bfloat16>(a, dB32, dC32, s);
+}
+
+namespace {
+__global__ void k_bf16_to_f32(const __nv_bfloat16 *src, float *dst, long n) {
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+        dst[i] = __bfloat162float(src[i]);
+}
+unsigned conv_blocks(long n) { return (unsigned)((n + 255) / 256 < 8192 ? (n + 255) / 256 : 8192); }
+} // namespace
+
+extern "C" int kmb_launch_bf16_to_f32(const void *src, float *dst, long n, cudaStream_t s) {
+    if (n <= 0) return KMB_OK;
+    k_bf16_to_f32<<<conv_blocks(n), 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(src), dst, n);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "bf16 -> fp32");
+}
+
+extern "C" int kmb_launch_f32_to_bf16(const float *src, void *dst, long n, cudaStream_t s) {
+    if (n <= 0) return KMB_OK;
+    k_f32_to_bf16_2d<<<conv_blocks(n), 256, 0, s>>>(src, static_cast<__nv_bfloat16 *>(dst), n);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "fp32 -> bf16");
 }

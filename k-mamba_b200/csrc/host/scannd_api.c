@@ -4,6 +4,7 @@
  * src/scan_nd.c:17-308, cuda/scan_nd.cu:337-400, cpu/scan2d.asm) and the
  * batched kmb_scannd_* extension, routed to csrc/cuda/scannd.cu.
  */
+#include <stdint.h>
 #include <stdio.h>
 #include <string.h>
 
@@ -37,7 +38,12 @@ static int validate(const KmbScanND *a, int bwd) {
     return KMB_OK;
 }
 
-static int run(const KmbScanND *a, int bwd) {
+/* bf16 I/O (bf16 = 1): x, delta, B, C, y, dy, dx, ddelta, dB, dC are bf16
+ * device tensors; A, dA and h stay fp32.  The 2D wavefront kernels read
+ * and write bf16 directly (channel-shared B/C, M 8 or 16, D a multiple of
+ * 8); other shapes are converted to fp32 scratch around the fp32 kernels
+ * (run_bf16_converted). */
+static int run(const KmbScanND *a, int bwd, int bf16) {
     KmbStage st;
     KmbNDLaunch L;
     KmbDevPlan plan;
@@ -78,12 +84,15 @@ static int run(const KmbScanND *a, int bwd) {
         L.dC = kmb_stage_out(&st, a->dC, bc, 0);
         L.G = kmb_scratch(&st, pdm);
         for (long i = 0; i < nd; ++i) {
-            L.ddelta[i] = ddelta_d ? ddelta_d + i * P * a->D : NULL;
+            /* bf16 tensors: the axes are P * D two-byte elements apart */
+            L.ddelta[i] = ddelta_d ? (float *)((char *)ddelta_d + i * P * a->D * (bf16 ? 2 : 4))
+                                   : NULL;
             L.dA[i] = dA_d ? dA_d + i * a->D * a->M : NULL;
         }
     }
     if (st.status) return kmb_stage_finish(&st, st.status);
-    for (long i = 0; i < nd; ++i) L.delta[i] = delta_d + i * P * a->D;
+    for (long i = 0; i < nd; ++i)
+        L.delta[i] = (const float *)((const char *)delta_d + i * P * a->D * (bf16 ? 2 : 4));
     L.delta_bstride = nd * P * a->D;
     L.lvl_start = plan.lvl_start;
     L.lvl_off = plan.lvl_off;
@@ -99,7 +108,17 @@ static int run(const KmbScanND *a, int bwd) {
     L.nlevels = plan.nlevels;
     L.bc_shared = a->bc_shared;
     for (long i = 0; i < nd; ++i) L.dims[i] = a->dims[i];
-    if (kmb_scan2d_supported(&L)) {
+    if (bf16) {
+        /* the caller checked kmb_scan2d_bf16_supported */
+        L.scratch_elems = kmb_scan2d_scratch_elems(&L);
+        L.scratch = (float *)kmb_scratch(&st, sizeof(float) * L.scratch_elems);
+        float *dB32 = bwd ? (float *)kmb_scratch(&st, bc) : NULL;
+        float *dC32 = bwd ? (float *)kmb_scratch(&st, bc) : NULL;
+        rc = st.status;
+        if (!rc)
+            rc = bwd ? kmb_launch_scan2d_bwd_bf16(&L, dB32, dC32, st.s)
+                     : kmb_launch_scan2d_fwd_bf16(&L, st.s);
+    } else if (kmb_scan2d_supported(&L)) {
         L.scratch_elems = kmb_scan2d_scratch_elems(&L);
         L.scratch = (float *)kmb_scratch(&st, sizeof(float) * L.scratch_elems);
         rc = st.status;
@@ -109,8 +128,96 @@ static int run(const KmbScanND *a, int bwd) {
     return kmb_stage_finish(&st, rc);
 }
 
-int kmb_scannd_fwd(const KmbScanND *a) { return run(a, 0); }
-int kmb_scannd_bwd(const KmbScanND *a) { return run(a, 1); }
+int kmb_scannd_fwd(const KmbScanND *a) { return run(a, 0, 0); }
+int kmb_scannd_bwd(const KmbScanND *a) { return run(a, 1, 0); }
+
+/* ---------------- bf16 I/O variants -------------------------------- */
+
+/* Shapes the 2D kernels take in bf16 directly. */
+static int bf16_direct(const KmbScanND *a) {
+    return a->ndims == 2 && a->bc_shared && a->M % 8 == 0 && a->M <= 16 && a->D % 8 == 0 &&
+           a->D * a->M < (1L << 24);
+}
+
+/* Other shapes: every bf16 input converted into pooled fp32 scratch, the
+ * fp32 kernels, the bf16 outputs converted back (round to nearest even). */
+static int run_bf16_converted(const KmbScanND *a, int bwd) {
+    const long nd = a->ndims, P = wavefront_nd_total_points(a->dims, nd);
+    const size_t pd = (size_t)a->batch * P * a->D;
+    const size_t bc = (size_t)a->batch * P * (a->bc_shared ? 1 : a->D) * a->M;
+    struct { const void *src; void *dst; size_t n; int out; } t[10];
+    int nt = 0, rc = KMB_OK;
+    KmbScanND f = *a;
+#define KMB_CONV(field, count, is_out) do { t[nt].src = a->field; t[nt].n = (count); \
+        t[nt].out = (is_out); t[nt].dst = kmb_pool_alloc(sizeof(float) * (count)); \
+        if (!t[nt].dst) { rc = kmb_fail(KMB_ENOMEM, "scannd bf16: scratch"); goto done; } \
+        f.field = (float *)t[nt].dst; ++nt; } while (0)
+    KMB_CONV(x, pd, 0);
+    KMB_CONV(delta, pd * nd, 0);
+    KMB_CONV(B, bc, 0);
+    KMB_CONV(C, bc, 0);
+    if (!bwd) {
+        KMB_CONV(y, pd, 1);
+    } else {
+        KMB_CONV(dy, pd, 0);
+        KMB_CONV(dx, pd, 1);
+        KMB_CONV(ddelta, pd * nd, 1);
+        KMB_CONV(dB, bc, 1);
+        KMB_CONV(dC, bc, 1);
+    }
+#undef KMB_CONV
+    for (int i = 0; i < nt && !rc; ++i)
+        if (!t[i].out) rc = kmb_launch_bf16_to_f32(t[i].src, (float *)t[i].dst, (long)t[i].n, kmb_stream());
+    if (!rc) {
+        const int sync = kmb_sync_enabled();
+        kmb_set_sync(0);
+        rc = run(&f, bwd, 0);
+        kmb_set_sync(sync);
+    }
+    for (int i = 0; i < nt && !rc; ++i)
+        if (t[i].out)
+            rc = kmb_launch_f32_to_bf16((const float *)t[i].dst, (void *)t[i].src, (long)t[i].n,
+                                        kmb_stream());
+    if (!rc && kmb_sync_enabled()) {
+        cudaError_t e = cudaStreamSynchronize(kmb_stream());
+        if (e != cudaSuccess) rc = kmb_cuda_fail(e, "scannd bf16: synchronize");
+    }
+done:
+    for (int i = 0; i < nt; ++i) kmb_pool_free(t[i].dst);
+    return rc;
+}
+
+static int run_bf16(const KmbScanND *a, int bwd) {
+    int rc = validate(a, bwd);
+    if (rc) return rc;
+    const void *ptrs[] = {a->x, a->delta, a->A, a->B, a->C, a->h, a->y, a->dy, a->dx,
+                          a->ddelta, a->dA, a->dB, a->dC};
+    for (size_t i = 0; i < sizeof ptrs / sizeof ptrs[0]; ++i)
+        if (ptrs[i] && !kmb_is_device_ptr(ptrs[i]))
+            return kmb_fail(KMB_EINVAL, "scannd bf16: every tensor must be device memory");
+    if (bf16_direct(a)) {
+        const void *al[] = {a->x, a->delta, a->B, a->C, a->dy};
+        for (size_t i = 0; i < sizeof al / sizeof al[0]; ++i)
+            if (al[i] && ((uintptr_t)al[i] & 15u))
+                return kmb_fail(KMB_EUNSUPPORTED, "scannd bf16: inputs must be 16-byte aligned");
+        return run(a, bwd, 1);
+    }
+    return run_bf16_converted(a, bwd);
+}
+
+int kmb_scannd_fwd_bf16(const KmbScanND *a) {
+    kmb_clear_error();
+    const int rc = run_bf16(a, 0);
+    report(rc);
+    return rc;
+}
+
+int kmb_scannd_bwd_bf16(const KmbScanND *a) {
+    kmb_clear_error();
+    const int rc = run_bf16(a, 1);
+    report(rc);
+    return rc;
+}
 
 /* ------------------------------------------------------------------ */
 /* reference API                                                       */

@@ -84,6 +84,15 @@ int kmb_launch_scannd_bwd(const KmbNDLaunch *a, cudaStream_t s);
 int kmb_launch_scan2d_fwd(const KmbNDLaunch *a, cudaStream_t s);
 int kmb_launch_scan2d_bwd(const KmbNDLaunch *a, cudaStream_t s);
 int kmb_scan2d_supported(const KmbNDLaunch *a);
+/* bf16 tensors in the 2D kernels (M 8 or 16); the backward accumulates the
+ * channel sums dB / dC in the fp32 buffers dB32 / dC32, then rounds them
+ * into the bf16 outputs. */
+int kmb_scan2d_bf16_supported(const KmbNDLaunch *a);
+int kmb_launch_scan2d_fwd_bf16(const KmbNDLaunch *a, cudaStream_t s);
+int kmb_launch_scan2d_bwd_bf16(const KmbNDLaunch *a, float *dB32, float *dC32, cudaStream_t s);
+/* Elementwise conversions (round to nearest even to bf16). */
+int kmb_launch_bf16_to_f32(const void *src, float *dst, long n, cudaStream_t s);
+int kmb_launch_f32_to_bf16(const float *src, void *dst, long n, cudaStream_t s);
 size_t kmb_scan2d_scratch_elems(const KmbNDLaunch *a);
 
 /* tcgen05 bf16 GEMM (csrc/cuda/gemm_tc.cu); operands already validated. */
