@@ -34,6 +34,7 @@
  * channels by shuffles and added to global memory with one atomic per
  * (point, state) and CTA.
  */
+#include <stdlib.h>
 #include <string.h>
 
 #include <type_traits>
@@ -101,7 +102,77 @@ struct S2D {
     float *dx, *dd0, *dd1, *dA0, *dA1, *dB, *dC;
     long H, W, D, M;
     long dl_bs; /* floats between batch items of each delta axis */
+    long batch;
+    /* strip split: every (item, channel group, strip) is a work item taken
+     * in order from *work by persistent CTAs; prog[(strip * batch + b) *
+     * groups + g] counts the rows whose edge column that strip has
+     * published */
+    int split;
+    int *work, *prog;
 };
+
+/* set when a wait on another CTA's progress gave up (kmb_scan2d_check_error) */
+__device__ int g_scan2d_error;
+
+/* Warp-wide wait until *prog >= need (lane 0 polls with acquire loads,
+ * bounded by about 2^31 clock cycles; on expiry the error word is set and
+ * later waits return at once). */
+__device__ __forceinline__ void wait_progress(const int *prog, int need, int lane) {
+    if (lane == 0) {
+        const long long t0 = clock64();
+        for (;;) {
+            int v;
+            asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(prog) : "memory");
+            if (v >= need) break;
+            if (*reinterpret_cast<volatile int *>(&g_scan2d_error)) break;
+            if (clock64() - t0 > (1ll << 31)) {
+                atomicExch(&g_scan2d_error, 1);
+                break;
+            }
+            __nanosleep(64);
+        }
+        asm volatile("fence.acq_rel.gpu;" ::: "memory");
+    }
+    __syncwarp();
+}
+
+/* Publishes `value` rows of this warp's edge writes (all lanes call it). */
+__device__ __forceinline__ void publish_progress(int *prog, int value, int lane) {
+    __threadfence();
+    __syncwarp();
+    if (lane == 0)
+        asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(prog), "r"(value) : "memory");
+}
+
+/* The next work item of a CTA: (b, g, first strip, end strip).  Strip-split
+ * items come strip by strip in the order `order` (forward: ascending,
+ * backward: descending), so the producer of an item's edge column was
+ * taken earlier by a CTA already running; without the split a CTA has one
+ * item, all strips of its (blockIdx.y, blockIdx.x). */
+__device__ __forceinline__ bool next_item(const S2D &p, long iter, long nstrips, bool descending,
+                                          long *sh, long &b, long &g, long &s0, long &s1) {
+    const long groups = p.D / kCh;
+    if (!p.split) {
+        if (iter > 0) return false;
+        b = blockIdx.y;
+        g = blockIdx.x;
+        s0 = 0;
+        s1 = nstrips;
+        return true;
+    }
+    if (threadIdx.x == 0) *sh = atomicAdd(p.work, 1);
+    __syncthreads();
+    const long it = *sh;
+    __syncthreads();
+    const long per = p.batch * groups;
+    if (it >= nstrips * per) return false;
+    const long s = descending ? nstrips - 1 - it / per : it / per, r = it % per;
+    b = r / groups;
+    g = r % groups;
+    s0 = s;
+    s1 = s + 1;
+    return true;
+}
 
 /* min over the lane's four states of |log2(e) A| */
 __device__ __forceinline__ float abs_min4(const float2 (&a)[2]) {
@@ -212,14 +283,20 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_fwd(S2D p) {
     extern __shared__ __align__(16) float sm[];
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const int c = lane >> 2, q = lane & 3;
-    const long b = blockIdx.y;
-    const long dch0 = (long)blockIdx.x * kCh;
-    const long d = dch0 + c;
     const long H = p.H, W = p.W, D = p.D, M = p.M;
     const bool qok = q * 4 < M;
     float *ring = sm + w * kRing * L::SLOT;                    /* this warp's rows */
     float *xbuf = sm + kWarps * kRing * L::SLOT;               /* [warp][2][32][4] */
-    float *edge = p.edge + ((long)blockIdx.y * gridDim.x + blockIdx.x) * H * 128;
+    const long nstrips = (W + kStrip - 1) / kStrip;
+    const long groups = D / kCh;
+    __shared__ long item_sh;
+    long b, g, s0, s1;
+    for (long iter = 0; next_item(p, iter, nstrips, false, &item_sh, b, g, s0, s1); ++iter) {
+    const long dch0 = g * kCh;
+    const long d = dch0 + c;
+    /* edge columns: one per (item, group), two alternating by strip
+     * parity when strips are split over CTAs */
+    float *const edge_base = p.edge + (b * groups + g) * (p.split ? 2 : 1) * H * 128;
 
     float2 A0p[2], A1p[2];
 #pragma unroll
@@ -231,12 +308,16 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_fwd(S2D p) {
         A1p[jp] = kmb_f2(e0 * KMB_LOG2E, e1 * KMB_LOG2E);
     }
     const float amin0 = abs_min4(A0p), amin1 = abs_min4(A1p);
-    const long nstrips = (W + kStrip - 1) / kStrip;
     const long nsteps = H + kWarps - 1;
     float *hb = p.hout + b * H * W * D * M;
     T *yb = reinterpret_cast<T *>(p.y) + b * H * W * D;
 
-    for (long sidx = 0; sidx < nstrips; ++sidx) {
+    for (long sidx = s0; sidx < s1; ++sidx) {
+        float *const edge_rd = edge_base + (p.split ? ((sidx - 1) & 1) * H * 128 : 0);
+        float *const edge_wr = edge_base + (p.split ? (sidx & 1) * H * 128 : 0);
+        const int *prog_rd = p.split && sidx > 0 ? p.prog + ((sidx - 1) * p.batch + b) * groups + g
+                                                 : nullptr;
+        int *prog_wr = p.split ? p.prog + (sidx * p.batch + b) * groups + g : nullptr;
         const long j0 = sidx * kStrip + w * kCPW; /* this warp's first column */
         float2 hv[kCPW][2];                       /* h(i-1, j0 + k) */
 #pragma unroll
@@ -244,7 +325,13 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_fwd(S2D p) {
         /* the first warp of a strip also stages the previous strip's last
          * column, written by that strip's last warp (CTA barriers since) */
         const bool use_edge = w == 0 && sidx > 0;
-        auto edge_row = [&](long r) { return use_edge ? edge + r * 128 : nullptr; };
+        /* the edge row r of the previous strip; with the split, once its
+         * CTA has published it */
+        auto edge_row = [&](long r) -> const float * {
+            if (!use_edge) return nullptr;
+            if (prog_rd && r < H) wait_progress(prog_rd, (int)r + 1, lane);
+            return edge_rd + r * 128;
+        };
         FwdCopies fc;
         fwd_copies<T>(p, b, j0, dch0, lane, fc);
         /* h and y of this warp's first column at row 0; a row is W*D*M
@@ -351,7 +438,10 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_fwd(S2D p) {
                  * the last warp, to the next strip) */
                 const float4 last = make_float4(hl[0].x, hl[0].y, hl[1].x, hl[1].y);
                 *reinterpret_cast<float4 *>(xbuf + ((w * 2 + (t & 1)) * 32 + lane) * 4) = last;
-                if (w == kWarps - 1) *reinterpret_cast<float4 *>(edge + i * 128 + lane * 4) = last;
+                if (w == kWarps - 1) {
+                    *reinterpret_cast<float4 *>(edge_wr + i * 128 + lane * 4) = last;
+                    if (prog_wr) publish_progress(prog_wr, (int)i + 1, lane);
+                }
             }
             if (i >= 0) slot = slot == kRing - 1 ? 0 : slot + 1;
             __syncthreads();
@@ -359,6 +449,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_fwd(S2D p) {
         kmb_cp_async_wait<0>();
         __syncthreads();
     }
+    } /* work items */
 }
 
 /* ------------------------------------------------------------------ */
@@ -519,14 +610,18 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_bwd(S2D p) {
     extern __shared__ __align__(16) float sm[];
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const int c = lane >> 2, q = lane & 3;
-    const long b = blockIdx.y;
-    const long dch0 = (long)blockIdx.x * kCh;
-    const long d = dch0 + c;
     const long H = p.H, W = p.W, D = p.D, M = p.M;
     const bool qok = q * 4 < M;
     float *ring = sm + w * kBRing * L::SLOT;
     float *xbuf = sm + kWarps * kBRing * L::SLOT; /* [warp][2][32][4] */
-    float *edge = p.edge + ((long)blockIdx.y * gridDim.x + blockIdx.x) * H * 128;
+    const long nstrips = (W + kBStrip - 1) / kBStrip;
+    const long groups = D / kCh;
+    __shared__ long item_sh;
+    long b, g, s0, s1;
+    for (long iter = 0; next_item(p, iter, nstrips, true, &item_sh, b, g, s0, s1); ++iter) {
+    const long dch0 = g * kCh;
+    const long d = dch0 + c;
+    float *const edge_base = p.edge + (b * groups + g) * (p.split ? 2 : 1) * H * 128;
 
     float2 A0p[2], A1p[2], dA0[2], dA1[2];
 #pragma unroll
@@ -539,7 +634,6 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_bwd(S2D p) {
         dA0[jp] = dA1[jp] = kmb_f2s(0.f);
     }
     const float amin0 = abs_min4(A0p), amin1 = abs_min4(A1p);
-    const long nstrips = (W + kBStrip - 1) / kBStrip;
     const long nsteps = H + kWarps - 1;
     const float *hb = p.h + b * H * W * D * M;
     T *dxb = reinterpret_cast<T *>(p.dx) + b * H * W * D;
@@ -549,7 +643,13 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_bwd(S2D p) {
     float *dCb = p.dC + b * H * W * M;
     const int lead = kWarps - 1 - w; /* steps this warp runs behind the leader */
 
-    for (long sidx = nstrips - 1; sidx >= 0; --sidx) {
+    for (long sidx = s1 - 1; sidx >= s0; --sidx) {
+        /* the carry column comes from strip sidx + 1 (to the right) */
+        float *const edge_rd = edge_base + (p.split ? ((sidx + 1) & 1) * H * 128 : 0);
+        float *const edge_wr = edge_base + (p.split ? (sidx & 1) * H * 128 : 0);
+        const int *prog_rd = p.split && sidx + 1 < nstrips
+                                 ? p.prog + ((sidx + 1) * p.batch + b) * groups + g : nullptr;
+        int *prog_wr = p.split ? p.prog + (sidx * p.batch + b) * groups + g : nullptr;
         const long j0 = sidx * kBStrip + w * kBCPW;
         /* step t handles row r(t) = H-1 - (t - lead) */
         auto row_of = [&](long t) { return H - 1 - (t - lead); };
@@ -569,7 +669,12 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_bwd(S2D p) {
             }
         }
         const bool use_edge = w == kWarps - 1 && sidx + 1 < nstrips;
-        auto edge_row = [&](long r) { return use_edge ? edge + r * 128 : nullptr; };
+        /* rows run bottom-up: row r is published once H - r rows are done */
+        auto edge_row = [&](long r) -> const float * {
+            if (!use_edge) return nullptr;
+            if (prog_rd && r >= 0 && r < H) wait_progress(prog_rd, (int)(H - r), lane);
+            return edge_rd + r * 128;
+        };
         /* every column of this warp inside the grid and every lane's states
          * inside M: the per-point guards are all true */
         const bool full = j0 + kBCPW <= W && M == 16;
@@ -712,7 +817,10 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_bwd(S2D p) {
                  * the next strip (its last warp) get e1 G of column j0 */
                 const float4 outq = make_float4(qh[0].x, qh[0].y, qh[1].x, qh[1].y);
                 *reinterpret_cast<float4 *>(xbuf + ((w * 2 + (t & 1)) * 32 + lane) * 4) = outq;
-                if (w == 0) *reinterpret_cast<float4 *>(edge + i * 128 + lane * 4) = outq;
+                if (w == 0) {
+                    *reinterpret_cast<float4 *>(edge_wr + i * 128 + lane * 4) = outq;
+                    if (prog_wr) publish_progress(prog_wr, (int)(H - i), lane);
+                }
                 /* h of row i-1 becomes the current row */
 #pragma unroll
                 for (int k = 0; k < kBCPW; ++k) {
@@ -737,6 +845,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_scan2d_bwd(S2D p) {
             atomicAdd(p.dA1 + d * M + q * 4 + u, dAs1[u]);
         }
     }
+    } /* work items */
 }
 
 } // namespace
@@ -765,12 +874,72 @@ static S2D make_s2d(const KmbNDLaunch *a) {
     return p;
 }
 
+/* Scratch layout (floats): two edge columns (H rows x 32 lanes x 4 states)
+ * per (item, channel group), then the strip-split progress counters (one
+ * int per (strip, item, group), backward strips being the narrower) and the
+ * work counter. */
+static size_t edge_elems(const KmbNDLaunch *a) {
+    return (size_t)a->batch * (a->D / kCh) * a->dims[0] * 128 * 2;
+}
+static size_t prog_ints(const KmbNDLaunch *a) {
+    return (size_t)a->batch * (a->D / kCh) * ((a->dims[1] + kBStrip - 1) / kBStrip) + 1;
+}
+
 extern "C" size_t kmb_scan2d_scratch_elems(const KmbNDLaunch *a) {
-    /* one edge column (H rows x 32 lanes x 4 states) per CTA */
-    return (size_t)a->batch * (a->D / kCh) * a->dims[0] * 128;
+    return edge_elems(a) + prog_ints(a) + 4;
 }
 
 namespace {
+
+/* Strips split over CTAs (persistent CTAs taking (item, group, strip) work
+ * items) when the items and channel groups alone leave SMs idle.  Config 4
+ * (256 x 256, 32 groups per item), forward / backward ms whole -> split:
+ * batch 1 1.95 / 5.23 -> 0.89 / 1.79, batch 2 1.94 / 5.33 -> 1.60 / 2.74,
+ * batch 4 1.95 / 5.40 -> 2.19 / 4.46, batch 8 2.76 / 7.26 -> 3.61 / 7.60;
+ * hence the forward splits up to half an SM's worth of groups, the
+ * backward up to one per SM (`max_per_sm` x SMs).  KMB_SCAN2D_SPLIT=0 / 1
+ * forces it off / on. */
+bool split_wanted(long item_groups, long nstrips, int sms, double max_per_sm) {
+    const char *e = getenv("KMB_SCAN2D_SPLIT");
+    if (e && e[0] == '0' && e[1] == 0) return false;
+    if (e && e[0] == '1' && e[1] == 0) return nstrips > 1;
+    return nstrips > 1 && (double)item_groups <= max_per_sm * sms;
+}
+
+int sm_count() {
+    int dev = 0, n = 148;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+        (void)cudaGetLastError();
+        n = 148;
+    }
+    return n;
+}
+
+/* Grid of a launch: (groups, batch) CTAs, or with the split as many
+ * persistent CTAs as fit (at most one per work item). */
+template <typename K>
+cudaError_t plan_grid(K kern, size_t smem, S2D &p, const KmbNDLaunch *a, long nstrips,
+                      double max_per_sm, dim3 &grid, cudaStream_t s) {
+    const long groups = a->D / kCh;
+    const int sms = sm_count();
+    p.batch = a->batch;
+    p.split = split_wanted(a->batch * groups, nstrips, sms, max_per_sm) ? 1 : 0;
+    p.prog = reinterpret_cast<int *>(a->scratch + edge_elems(a));
+    p.work = p.prog + prog_ints(a) - 1;
+    if (!p.split) {
+        grid = dim3((unsigned)groups, (unsigned)a->batch);
+        return cudaSuccess;
+    }
+    int per_sm = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kWarps * 32, smem);
+    if (e != cudaSuccess) return e;
+    const long items = nstrips * a->batch * groups;
+    long ctas = (long)(per_sm > 0 ? per_sm : 1) * sms;
+    if (ctas > items) ctas = items;
+    grid = dim3((unsigned)ctas, 1);
+    return cudaMemsetAsync(p.prog, 0, sizeof(int) * prog_ints(a), s);
+}
 
 __global__ void k_f32_to_bf16_2d(const float *src, __nv_bfloat16 *dst, long n) {
     for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
@@ -789,8 +958,10 @@ int launch_fwd(const KmbNDLaunch *a, cudaStream_t s) {
     const size_t smem = sizeof(float) * ((size_t)kWarps * kRing * FL<T>::SLOT + kWarps * 2 * 32 * 4);
     cudaError_t e = cudaFuncSetAttribute(k_scan2d_fwd<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
+    dim3 grid;
+    if (e == cudaSuccess)
+        e = plan_grid(k_scan2d_fwd<T>, smem, p, a, (a->dims[1] + kStrip - 1) / kStrip, 0.5, grid, s);
     if (e == cudaSuccess) {
-        dim3 grid((unsigned)(a->D / kCh), (unsigned)a->batch);
         k_scan2d_fwd<T><<<grid, kWarps * 32, smem, s>>>(p);
         e = cudaGetLastError();
     }
@@ -823,8 +994,11 @@ int launch_bwd(const KmbNDLaunch *a, float *dB32, float *dC32, cudaStream_t s) {
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(k_scan2d_bwd<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)smem);
+    dim3 grid;
+    if (e == cudaSuccess)
+        e = plan_grid(k_scan2d_bwd<T>, smem, p, a, (a->dims[1] + kBStrip - 1) / kBStrip, 1.0, grid,
+                      s);
     if (e == cudaSuccess) {
-        dim3 grid((unsigned)(a->D / kCh), (unsigned)a->batch);
         k_scan2d_bwd<T><<<grid, kWarps * 32, smem, s>>>(p);
         e = cudaGetLastError();
     }
@@ -885,4 +1059,18 @@ extern "C" int kmb_launch_f32_to_bf16(const float *src, void *dst, long n, cudaS
     k_f32_to_bf16_2d<<<conv_blocks(n), 256, 0, s>>>(src, static_cast<__nv_bfloat16 *>(dst), n);
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? KMB_OK : kmb_cuda_fail(e, "fp32 -> bf16");
+}
+
+/* KMB_ETIMEOUT (and the word cleared) when a strip-split wait gave up
+ * since the last check. */
+extern "C" int kmb_scan2d_check_error(void) {
+    int flag = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&flag, g_scan2d_error, sizeof flag);
+    if (e != cudaSuccess) return kmb_cuda_fail(e, "scan2d: error word");
+    if (flag) {
+        const int zero = 0;
+        (void)cudaMemcpyToSymbol(g_scan2d_error, &zero, sizeof zero);
+        return kmb_fail(KMB_ETIMEOUT, "scan2d: a wait on another strip's progress expired");
+    }
+    return KMB_OK;
 }

@@ -123,9 +123,15 @@ static int run(const KmbScanND *a, int bwd, int bf16) {
         L.scratch = (float *)kmb_scratch(&st, sizeof(float) * L.scratch_elems);
         rc = st.status;
         if (!rc) rc = bwd ? kmb_launch_scan2d_bwd(&L, st.s) : kmb_launch_scan2d_fwd(&L, st.s);
-    } else
+    } else {
         rc = bwd ? kmb_launch_scannd_bwd(&L, st.s) : kmb_launch_scannd_fwd(&L, st.s);
-    return kmb_stage_finish(&st, rc);
+        return kmb_stage_finish(&st, rc);
+    }
+    rc = kmb_stage_finish(&st, rc);
+    /* the 2D kernels' bounded waits (strip split) report through a device
+     * word, read when the call is synchronous */
+    if (!rc && kmb_sync_enabled()) rc = kmb_scan2d_check_error();
+    return rc;
 }
 
 int kmb_scannd_fwd(const KmbScanND *a) { return run(a, 0, 0); }

@@ -94,6 +94,8 @@ int kmb_launch_scan2d_bwd_bf16(const KmbNDLaunch *a, float *dB32, float *dC32, c
 int kmb_launch_bf16_to_f32(const void *src, float *dst, long n, cudaStream_t s);
 int kmb_launch_f32_to_bf16(const float *src, void *dst, long n, cudaStream_t s);
 size_t kmb_scan2d_scratch_elems(const KmbNDLaunch *a);
+/* KMB_ETIMEOUT once after a strip-split wait of the 2D kernels expired. */
+int kmb_scan2d_check_error(void);
 
 /* tcgen05 bf16 GEMM (csrc/cuda/gemm_tc.cu); operands already validated. */
 int kmb_launch_gemm_bf16(const KmbGemm *g, cudaStream_t s);
