@@ -29,6 +29,7 @@
 
 #include "../kmb_internal.h"
 #include "kmamba.h"
+#include "kmamba_resident.h"
 
 /* ------------------------------------------------------------------ */
 /* block tensor tables                                                 */
@@ -855,7 +856,10 @@ void mamba_zero_grads(MambaBlock *b) {
     if (!b || !b->opt_state) return;
     d = block_dims(b);
     optstate_grad_ptrs(b->opt_state, g);
-    for (int i = 0; i < P_COUNT; ++i) memset(g[i], 0, d.n[i] * sizeof(float));
+    for (int i = 0; i < P_COUNT; ++i) {
+        memset(g[i], 0, d.n[i] * sizeof(float));
+        (void)kmb_resident_update(g[i]);
+    }
 }
 
 float mamba_block_grad_sqnorm(const MambaBlock *b) {
@@ -1051,6 +1055,82 @@ void mb_compute_delta(float *delta_out, const MambaBlock *b, const float *delta_
 /* model                                                               */
 /* ------------------------------------------------------------------ */
 
+/* ------------------------------------------------------------------ */
+/* device-resident models                                              */
+/* ------------------------------------------------------------------ */
+
+typedef struct {
+    float *p;
+    size_t bytes;
+} HostArr;
+
+/* Every host array of m the calls stage (weights, gradients, moments),
+ * each once; returns the count (<= cap) or -1 when cap is too small. */
+static int model_host_arrays(const KMamba *m, HostArr *out, int cap) {
+    int n = 0;
+    const size_t VD = sizeof(float) * m->cfg.vocab_size * m->cfg.dim;
+#define KMB_ADD(ptr, nbytes) do { float *q_ = (ptr); int dup_ = 0; \
+        if (q_) { for (int k_ = 0; k_ < n; ++k_) dup_ |= out[k_].p == q_; \
+                  if (!dup_) { if (n >= cap) return -1; out[n].p = q_; out[n].bytes = (nbytes); ++n; } } \
+    } while (0)
+    KMB_ADD(m->embedding, VD);
+    KMB_ADD(m->head, VD);
+    KMB_ADD(m->m_embedding, VD);
+    KMB_ADD(m->v_embedding, VD);
+    KMB_ADD(m->m_head, VD);
+    KMB_ADD(m->v_head, VD);
+    for (size_t l = 0; l < m->cfg.n_layers; ++l) {
+        const MambaBlock *b = m->layers[l];
+        if (!b) continue;
+        const BlockDims d = block_dims(b);
+        float *hp[P_COUNT];
+        block_param_ptrs(b, hp);
+        for (int i = 0; i < P_COUNT; ++i) KMB_ADD(hp[i], d.n[i] * sizeof(float));
+        if (b->opt_state) {
+            float *g[P_COUNT], *hm[P_COUNT], *hv[P_COUNT];
+            optstate_grad_ptrs(b->opt_state, g);
+            optstate_moment_ptrs(b->opt_state, hm, hv);
+            for (int i = 0; i < P_COUNT; ++i) {
+                KMB_ADD(g[i], d.n[i] * sizeof(float));
+                KMB_ADD(hm[i], d.n[i] * sizeof(float));
+                KMB_ADD(hv[i], d.n[i] * sizeof(float));
+            }
+        }
+    }
+#undef KMB_ADD
+    return n;
+}
+
+/* Applies op (0 add, 1 sync, 2 remove with copy back, 3 remove, 4 update)
+ * to every host array of m. */
+static int model_resident_op(KMamba *m, int op) {
+    if (!m || !m->layers) return kmb_fail(KMB_EINVAL, "resident: NULL model");
+    const int cap = 6 + (int)m->cfg.n_layers * 4 * P_COUNT;
+    HostArr *a = (HostArr *)malloc(sizeof *a * (size_t)cap);
+    if (!a) return kmb_fail(KMB_ENOMEM, "resident: host allocation failed");
+    const int n = model_host_arrays(m, a, cap);
+    int rc = n < 0 ? kmb_fail(KMB_EINVAL, "resident: array table overflow") : KMB_OK;
+    for (int i = 0; i < n && rc == KMB_OK; ++i) {
+        if (op == 0) rc = kmb_resident_add(a[i].p, a[i].bytes);
+        else if (op == 1) rc = kmb_resident_sync(a[i].p);
+        else if (op == 4) rc = kmb_resident_update(a[i].p);
+        else rc = kmb_resident_remove(a[i].p, op == 2);
+    }
+    free(a);
+    return rc;
+}
+
+int kmamba_set_device_resident(KMamba *m, int on) {
+    kmb_clear_error();
+    return model_resident_op(m, on ? 0 : 2);
+}
+
+int kmamba_sync_to_host(KMamba *m) {
+    kmb_clear_error();
+    if (!kmb_resident_count()) return m ? KMB_OK : kmb_fail(KMB_EINVAL, "resident: NULL model");
+    return model_resident_op(m, 1);
+}
+
 KMamba *kmamba_create(const KMambaConfig *cfg) {
     KMamba *m;
     if (!cfg || !cfg->vocab_size || !cfg->dim || !cfg->seq_len || !cfg->n_layers) return NULL;
@@ -1098,6 +1178,9 @@ KMamba *kmamba_create(const KMambaConfig *cfg) {
 
 void kmamba_free(KMamba *m) {
     if (!m) return;
+    /* release device-resident copies first: a later host allocation at the
+     * same address must not find them */
+    if (m->layers && kmb_resident_count()) (void)model_resident_op(m, 3);
     if (m->layers) {
         for (size_t i = 0; i < m->cfg.n_layers; ++i) mamba_block_free(m->layers[i]);
         free(m->layers);
@@ -1124,6 +1207,8 @@ int kmamba_init(KMamba *m, uint32_t seed) {
     if (!m->cfg.weight_tying)
         xavier(m->head, m->cfg.dim, m->cfg.vocab_size, m->cfg.dim * m->cfg.vocab_size);
     for (size_t i = 0; i < m->cfg.n_layers; ++i) mamba_block_init(m->layers[i]);
+    /* a device-resident model takes the new values */
+    if (kmb_resident_count() && model_resident_op(m, 4) != KMB_OK) return -1;
     return 0;
 }
 
@@ -1207,6 +1292,8 @@ int kmamba_save(const KMamba *m, const char *path) {
     FILE *f;
     int rc;
     if (!m || !path) return -1;
+    /* a device-resident model's current values are on the device */
+    if (kmb_resident_count() && model_resident_op((KMamba *)m, 1) != KMB_OK) return -1;
     f = fopen(path, "wb");
     if (!f) return -1;
     memset(&h, 0, sizeof h);

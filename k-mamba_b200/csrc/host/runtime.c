@@ -202,6 +202,142 @@ size_t kmb_pool_bytes_held(void) {
 }
 
 /* ------------------------------------------------------------------ */
+/* device-resident host arrays                                         */
+/* ------------------------------------------------------------------ */
+
+/* A host array registered here has a device copy that staging uses in its
+ * place: no host->device copy on the way in and no copy back on the way
+ * out.  The device copy is then the array's current value until
+ * kmb_resident_sync copies it back. */
+typedef struct {
+    const void *host;
+    void *dev;
+    size_t bytes;
+    int device;
+} ResidentBuf;
+
+static ResidentBuf *g_res;
+static int g_nres, g_rescap;
+static pthread_mutex_t g_res_mu = PTHREAD_MUTEX_INITIALIZER;
+
+static int current_device(void) {
+    int d = -1;
+    if (cudaGetDevice(&d) != cudaSuccess) {
+        (void)cudaGetLastError();
+        d = -1;
+    }
+    return d;
+}
+
+/* index of `host` on `device`, or -1 (caller holds g_res_mu) */
+static int resident_index(const void *host, int device) {
+    for (int i = 0; i < g_nres; ++i)
+        if (g_res[i].host == host && g_res[i].device == device) return i;
+    return -1;
+}
+
+static void *resident_find(const void *host, size_t bytes) {
+    void *d = NULL;
+    if (!g_nres) return NULL;
+    const int dev = current_device();
+    pthread_mutex_lock(&g_res_mu);
+    const int i = resident_index(host, dev);
+    if (i >= 0 && bytes <= g_res[i].bytes) d = g_res[i].dev;
+    pthread_mutex_unlock(&g_res_mu);
+    return d;
+}
+
+int kmb_resident_add(const void *host, size_t bytes) {
+    cudaError_t e;
+    int rc = KMB_OK;
+    if (!host || !bytes) return kmb_fail(KMB_EINVAL, "resident: NULL or empty array");
+    if (kmb_is_device_ptr(host)) return KMB_OK; /* already device memory */
+    const int dev = current_device();
+    pthread_mutex_lock(&g_res_mu);
+    int i = resident_index(host, dev);
+    if (i >= 0 && bytes > g_res[i].bytes) {
+        pthread_mutex_unlock(&g_res_mu);
+        return kmb_fail(KMB_EINVAL, "resident: %p registered with %zu bytes, not %zu", host,
+                        g_res[i].bytes, bytes);
+    }
+    if (i < 0) {
+        void *d = NULL;
+        if (g_nres == g_rescap) {
+            const int cap = g_rescap ? 2 * g_rescap : 64;
+            ResidentBuf *t = (ResidentBuf *)realloc(g_res, sizeof *t * (size_t)cap);
+            if (!t) {
+                pthread_mutex_unlock(&g_res_mu);
+                return kmb_fail(KMB_ENOMEM, "resident: host allocation failed");
+            }
+            g_res = t;
+            g_rescap = cap;
+        }
+        e = cudaMalloc(&d, bytes);
+        if (e != cudaSuccess) {
+            pthread_mutex_unlock(&g_res_mu);
+            return kmb_cuda_fail(e, "resident: cudaMalloc");
+        }
+        i = g_nres++;
+        g_res[i].host = host;
+        g_res[i].dev = d;
+        g_res[i].bytes = bytes;
+        g_res[i].device = dev;
+    }
+    /* (re-)upload the host value; ordered after the library stream's work */
+    e = cudaStreamSynchronize(kmb_stream());
+    if (e == cudaSuccess) e = cudaMemcpy(g_res[i].dev, host, bytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) rc = kmb_cuda_fail(e, "resident: upload");
+    pthread_mutex_unlock(&g_res_mu);
+    return rc;
+}
+
+int kmb_resident_update(const void *host) {
+    if (!g_nres) return KMB_OK;
+    const int dev = current_device();
+    pthread_mutex_lock(&g_res_mu);
+    const int i = resident_index(host, dev);
+    size_t bytes = i >= 0 ? g_res[i].bytes : 0;
+    pthread_mutex_unlock(&g_res_mu);
+    return i >= 0 ? kmb_resident_add(host, bytes) : KMB_OK;
+}
+
+int kmb_resident_sync(void *host) {
+    cudaError_t e;
+    int rc = KMB_OK;
+    const int dev = current_device();
+    pthread_mutex_lock(&g_res_mu);
+    const int i = resident_index(host, dev);
+    if (i >= 0) {
+        e = cudaStreamSynchronize(kmb_stream());
+        if (e == cudaSuccess) e = cudaMemcpy(host, g_res[i].dev, g_res[i].bytes, cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) rc = kmb_cuda_fail(e, "resident: download");
+    }
+    pthread_mutex_unlock(&g_res_mu);
+    return rc;
+}
+
+int kmb_resident_remove(void *host, int copy_back) {
+    int rc = copy_back ? kmb_resident_sync(host) : KMB_OK;
+    const int dev = current_device();
+    pthread_mutex_lock(&g_res_mu);
+    const int i = resident_index(host, dev);
+    if (i >= 0) {
+        (void)cudaStreamSynchronize(kmb_stream());
+        cudaFree(g_res[i].dev);
+        g_res[i] = g_res[--g_nres];
+    }
+    pthread_mutex_unlock(&g_res_mu);
+    return rc;
+}
+
+int kmb_resident_count(void) {
+    pthread_mutex_lock(&g_res_mu);
+    const int n = g_nres;
+    pthread_mutex_unlock(&g_res_mu);
+    return n;
+}
+
+/* ------------------------------------------------------------------ */
 /* staging                                                             */
 /* ------------------------------------------------------------------ */
 
@@ -255,6 +391,14 @@ static void *stage_add(KmbStage *st, const void *p, size_t bytes, int out, int c
     b->user = p;
     b->bytes = bytes;
     b->out = out;
+    {
+        void *rd = resident_find(p, bytes);
+        if (rd) { /* a device-resident host array: its device copy, no copies */
+            b->dev = rd;
+            b->owned = 0;
+            return b->dev;
+        }
+    }
     if (kmb_is_device_ptr(p)) {
         b->dev = (void *)p;
         b->owned = 0;

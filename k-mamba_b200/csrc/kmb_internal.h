@@ -210,6 +210,16 @@ typedef struct {
     cudaStream_t s;
 } KmbStage;
 
+/* Device-resident host arrays (kmamba_set_device_resident): staging returns
+ * the registered device copy of such an array and copies nothing.  add
+ * (re-)uploads the host value; update re-uploads only registered arrays;
+ * sync copies the device value back; remove drops the registration (after
+ * a copy back when asked). */
+int kmb_resident_add(const void *host, size_t bytes);
+int kmb_resident_update(const void *host); /* re-upload when registered */
+int kmb_resident_sync(void *host);
+int kmb_resident_remove(void *host, int copy_back);
+int kmb_resident_count(void);
 void kmb_stage_begin(KmbStage *st);
 /* Grows the table to hold `cap` buffers (model calls that move every
  * parameter, gradient and moment of every layer).  Call right after

@@ -219,6 +219,9 @@ MODEL_PROTOTYPES = {
     "kmamba_enable_training_with_optimizer": (C.c_int, [_PK, C.c_int, _PO, C.c_float,
                                                         C.c_float]),
     "kmamba_save": (C.c_int, [_PK, C.c_char_p]),
+    # device-resident models (kmamba_resident.h)
+    "kmamba_set_device_resident": (C.c_int, [_PK, C.c_int]),
+    "kmamba_sync_to_host": (C.c_int, [_PK]),
     "kmamba_load": (_PK, [C.c_char_p, C.c_int, _PO, C.c_float, C.c_float]),
     "kmamba_forward": (C.c_int, [_PK, fp, fp]),
     "kmamba_train_step": (C.c_float, [_PK, fp]),
