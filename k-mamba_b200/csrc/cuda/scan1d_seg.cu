@@ -378,8 +378,13 @@ __device__ __forceinline__ int fwd_run(const SegArgs &p, unsigned char *smem, in
     return status;
 }
 
-template <typename T, bool CLAMP>
-__global__ void __launch_bounds__(kNT, 4) k_scan1d_fwd_seg(SegArgs p) {
+/* MINB CTAs per SM: 4 (128 registers) for grids of more than two waves of
+ * 3, where it measured faster (config 2 at batch 8, 1152 CTAs: 0.503 ->
+ * 0.489 ms); 3 (168 registers, more room for the tile's loads in flight)
+ * for the smaller grids of small batches, where fewer resident warps make
+ * the per-CTA latency count (batch 1, 384 CTAs: 0.130 ms with 3). */
+template <typename T, bool CLAMP, int MINB>
+__global__ void __launch_bounds__(kNT, MINB) k_scan1d_fwd_seg(SegArgs p) {
     extern __shared__ __align__(16) unsigned char smem[];
     int *sflag = reinterpret_cast<int *>(smem + kST * FwdLayout<T>::STAGE);
     const int tid = threadIdx.x, n0 = (tid & 3) * 4;
@@ -737,7 +742,10 @@ __global__ void k_f32_to_bf16(const float *src, __nv_bfloat16 *dst, long n) {
 template <typename T>
 int launch_fwd(const SegArgs &p, long batch, int clamp, cudaStream_t s) {
     const size_t smem = FwdLayout<T>::SMEM;
-    auto kern = clamp ? k_scan1d_fwd_seg<T, true> : k_scan1d_fwd_seg<T, false>;
+    const long ctas = (p.D / kDT) * batch * p.S;
+    const bool big = ctas > 2L * 3 * 148;
+    auto kern = big ? (clamp ? k_scan1d_fwd_seg<T, true, 4> : k_scan1d_fwd_seg<T, false, 4>)
+                    : (clamp ? k_scan1d_fwd_seg<T, true, 3> : k_scan1d_fwd_seg<T, false, 3>);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return kmb_cuda_fail(e, "scan1d seg forward smem");
     SegArgs q = p;
