@@ -264,8 +264,8 @@ def run_secondary(args):
     outputs written once.
 
     Under torchrun every rank runs the same pass on its share of the
-    config's batch (--shard-batch: the batch split over the ranks, SURVEY
-    8(e)'s fixed-config series; otherwise a full batch per rank), and the
+    config's batch (--shard-batch: the batch split over the ranks, the
+    fixed-batch series; otherwise a full batch per rank), and the
     parameter gradients (dkernel / dbias, or dA) are summed over the ranks
     by the library's NCCL communicator after every backward.  Time: max
     over ranks; value: bytes of all ranks per second."""
